@@ -1,0 +1,335 @@
+"""Benchmark: MoE decode tokens/s of the routed-expert path on B200 (FP8 experts).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mine|reference] [--lines 16]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU)
+
+A step is one decode pass of `lines` rows (16: lines decoded together) through 48 MoE layers of the BASELINE shape
+(hidden 2048, 128 experts, top-8, intermediate 768, SwiGLU), each layer with its own FP8 banks (e4m3 + 128x128
+block scales, the reference layout) and its own seeded routing: 29 GB of experts, far larger than L2, so every
+step streams its experts from HBM (no flush needed). Inputs are resident in HBM; the timed region replays one CUDA
+graph per step. Multi-GPU: independent replicas (each rank decodes its own lines with all experts resident; no
+collective), weak scaling. `value` = tokens/s of all ranks; timing = CUDA events, max over ranks.
+
+Also reported: the 1-line decode, the end-to-end rate through the Python API with host buffers, the reference's own
+kernels (compiled from drama3/kernels.py into oracle/_ref) on the same GPU, and the reference's CPU path on the host
+cores. `--impl reference` runs only that CPU path (rank 0) and prints its line.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "comfyui-drama3_b200"))
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+METRIC = "MoE decode tokens/s (1 & 16 lines), expert GEMV HBM GB/s vs ~8 TB/s, 1-8 B200"
+E, H, I, K_TOP = 128, 2048, 768, 8
+LAYERS = 48
+# algorithmic bytes of one FP8 expert (reference layout): gate_up 1536x2048 + down 2048x768 e4m3, block scales
+EXPERT_BYTES = 2 * I * H + H * I + (2 * I // 128) * (H // 128) * 4 + (H // 128) * (I // 128) * 4
+
+
+def peaks():
+    try:
+        data = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return float(data["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi samples of SM clock and throttle reasons while the timed region runs."""
+
+    def __init__(self, index):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 7:
+                self.rows.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            self.proc.wait(timeout=5)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[3 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": float(self.rows[0][1]),
+                "samples": len(self.rows), "reasons": reasons}
+
+
+def make_layers(device, lines, seed=4):
+    """48 layers of FP8 banks (random valid e4m3 bytes, positive block scales) and per-layer routing."""
+    gen = torch.Generator(device=device).manual_seed(seed)
+    layers = []
+    for _ in range(LAYERS):
+        bank = []
+        for n, k in ((2 * I, H), (H, I)):
+            w = torch.randint(0, 254, (E * n, k), generator=gen, device=device, dtype=torch.uint8)
+            w = torch.where(w >= 0x7F, w + 1, w)  # no 0x7F / 0xFF (NaN codes)
+            s = torch.rand((E * n // 128, k // 128), generator=gen, device=device) * 1e-4 + 5e-5
+            bank.append({"weight": w, "scale": s})
+        layers.append(tuple(bank))
+    cpu_gen = torch.Generator().manual_seed(seed + 1)
+    ids, weights = [], []
+    for _ in range(LAYERS):
+        w, i = torch.softmax(torch.randn((lines, E), generator=cpu_gen), dim=-1).topk(K_TOP, dim=-1)
+        ids.append(i)
+        weights.append((w / w.sum(-1, keepdim=True)).to(torch.bfloat16).float())
+    return layers, torch.stack(ids).to(device), torch.stack(weights).to(device)
+
+
+def unique_bytes(ids):
+    """Algorithmic bytes of one step: each layer's unique experts, plus its rows in and out (bf16)."""
+    total = 0
+    lines = ids.shape[1]
+    for layer in ids.cpu():
+        total += len(set(layer.reshape(-1).tolist())) * EXPERT_BYTES + 2 * lines * H * 2 + lines * K_TOP * 12
+    return total
+
+
+def time_graph(fn, steps, warmup, stream):
+    """(ms per step) of fn() captured as one CUDA graph and replayed; CUDA events on the capturing stream."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        fn()
+    graph.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    return graph, start, end
+
+
+def cpu_reference(lines, layers_sampled=2, seed=4):
+    """The reference's CPU decode (oracle/cpu_port.py) on the host cores: `lines` rows through `layers_sampled`
+    layers, scaled to 48 layers. Returns (tokens/s, seconds, threads, sample description)."""
+    from oracle import cpu_port
+    torch.set_num_threads(os.cpu_count() or 1)
+    gen = torch.Generator().manual_seed(seed)
+    x = torch.randn((lines, H), generator=gen).to(torch.bfloat16)
+    total = 0.0
+    for _ in range(layers_sampled):
+        gu = torch.randint(0, 126, (E, 2 * I, H), generator=gen, dtype=torch.uint8)
+        dn = torch.randint(0, 126, (E, H, I), generator=gen, dtype=torch.uint8)
+        gs = torch.rand((E, 2 * I // 128, H // 128), generator=gen) * 1e-4
+        ds = torch.rand((E, H // 128, I // 128), generator=gen) * 1e-4
+        w, ids = torch.softmax(torch.randn((lines, E), generator=gen), -1).topk(K_TOP, dim=-1)
+        w = (w / w.sum(-1, keepdim=True)).to(torch.bfloat16)
+        started = time.perf_counter()
+        cpu_port.fp8_decode_lines(x, ids, w, gu, gs, dn, ds)
+        total += time.perf_counter() - started
+    per_step = total / layers_sampled * LAYERS
+    sample = (f"{lines} rows x {layers_sampled} layers of the reference CPU path (bf16 dequant + matmuls, one row at "
+              f"a time), scaled to {LAYERS} layers")
+    return lines / per_step, total, torch.get_num_threads(), sample
+
+
+def run_reference_arm(args, rank):
+    if rank != 0:
+        return
+    tps, secs, threads, sample = cpu_reference(args.lines, layers_sampled=max(1, min(args.steps, 2)))
+    line = {"impl": "reference", "metric": METRIC, "value": tps, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * args.lines / tps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (CPU)",
+            "data": "synthetic", "config": config(args),
+            "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def config(args):
+    return {"workload": f"fp8 MoE decode, {args.lines} lines x {LAYERS} layers per step (BASELINE configs[1] layer "
+                        f"shape; 48 layers as configs[4])",
+            "layers": LAYERS, "lines": args.lines, "experts": E, "top_k": K_TOP, "hidden": H, "intermediate": I,
+            "format": "e4m3 + fp32 128x128 block scales (reference layout)",
+            "l2": "inputs larger than L2: 29 GB of expert banks streamed per step",
+            "parallelism": f"replicas x{args.gpus} (lines data-parallel)"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("mine", "reference"), default="mine")
+    ap.add_argument("--lines", type=int, default=16)
+    ap.add_argument("--no-extras", action="store_true", help="skip e2e / reference GPU / CPU legs")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference_arm(args, rank)
+        return
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+        pg = dist
+
+    from drama3_b200 import kernels
+
+    layers, ids, weights = make_layers(device, args.lines, seed=4 + rank)
+    x = torch.randn((args.lines, H), generator=torch.Generator().manual_seed(7 + rank)).to(torch.bfloat16).to(device)
+    ws = kernels.decode_workspace(args.lines, K_TOP, I, device)
+    outs = torch.empty((LAYERS, args.lines, H), dtype=torch.bfloat16, device=device)
+    stream = torch.cuda.Stream(device)
+
+    def step(lines=args.lines, xin=x, ids_=ids, w_=weights, ws_=ws, out_=outs):
+        for l_ in range(LAYERS):
+            kernels.moe_decode("fp8", xin, ids_[l_], w_[l_], layers[l_], workspace=ws_, out=out_[l_])
+
+    with torch.cuda.stream(stream):
+        graph, start, end = time_graph(step, 0, args.warmup, stream)
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+        if pg:
+            pg.barrier()
+        torch.cuda.synchronize()
+        with Clocks(local) as clocks:
+            start.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            end.record(stream)
+            torch.cuda.synchronize()
+        ms = start.elapsed_time(end) / args.steps
+    if pg:
+        t = torch.tensor([ms], device=device)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms = float(t.item())
+    step_bytes = unique_bytes(ids)
+    hbm_peak, peak_kind = peaks()
+    achieved = step_bytes / (ms * 1e-3) / 1e9
+    value = world * args.lines / (ms * 1e-3)
+
+    extras = {}
+    if not args.no_extras and rank == 0:
+        # one line decoded at a time (M = 1)
+        x1, ids1, w1 = x[:1].contiguous(), ids[:, :1].contiguous(), weights[:, :1].contiguous()
+        ws1 = kernels.decode_workspace(1, K_TOP, I, device)
+        out1 = torch.empty((LAYERS, 1, H), dtype=torch.bfloat16, device=device)
+        with torch.cuda.stream(stream):
+            g1, s1, e1 = time_graph(lambda: step(1, x1, ids1, w1, ws1, out1), 0, args.warmup, stream)
+            s1.record(stream)
+            for _ in range(args.steps):
+                g1.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+        ms1 = s1.elapsed_time(e1) / args.steps
+        b1 = unique_bytes(ids1)
+        extras["lines_1"] = {"tokens_per_s": 1 / (ms1 * 1e-3), "ms_per_step": ms1,
+                             "hbm_gbs": b1 / (ms1 * 1e-3) / 1e9, "frac": b1 / (ms1 * 1e-3) / 1e9 / hbm_peak,
+                             "bytes_per_step": b1, "us_per_layer": 1e3 * ms1 / LAYERS}
+        del g1
+        # end to end through the Python API: host inputs in, host output back, every step
+        xh = x.cpu().pin_memory()
+        idh, wh = ids.cpu().pin_memory(), weights.cpu().pin_memory()
+        outh = torch.empty((args.lines, H), dtype=torch.bfloat16).pin_memory()
+        xd, idd, wd = torch.empty_like(x), torch.empty_like(ids), torch.empty_like(weights)
+        n_e2e = max(3, min(args.steps, 20))
+        for it in range(n_e2e + 2):
+            if it == 2:
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                es.record()
+            xd.copy_(xh, non_blocking=True)
+            idd.copy_(idh, non_blocking=True)
+            wd.copy_(wh, non_blocking=True)
+            step(args.lines, xd, idd, wd, ws, outs)
+            outh.copy_(outs[-1], non_blocking=True)
+        ee.record()
+        torch.cuda.synchronize()
+        ms_e2e = es.elapsed_time(ee) / n_e2e
+        extras["e2e"] = {"value": args.lines / (ms_e2e * 1e-3), "unit": "tokens/s",
+                         "h2d_bytes_per_step": xh.nbytes + idh.nbytes + wh.nbytes, "d2h_bytes_per_step": outh.nbytes,
+                         "ms_per_step": ms_e2e, "wall_ms_per_step": 1e3 * (time.perf_counter() - t0) / n_e2e}
+        # the reference's own kernels on this GPU, one row at a time (drama3/model.py:111-113)
+        try:
+            from oracle import ref_gpu
+            if ref_gpu.available():
+                def ref_step():
+                    for l_ in range(LAYERS):
+                        ref_gpu.lines_decode(x, ids[l_], weights[l_], layers[l_], (2 * I, H), "fp8", (None, None))
+                with torch.cuda.stream(stream):
+                    gr, rs, re_ = time_graph(ref_step, 0, 2, stream)
+                    n_ref = max(3, min(args.steps, 10))
+                    rs.record(stream)
+                    for _ in range(n_ref):
+                        gr.replay()
+                    re_.record(stream)
+                    torch.cuda.synchronize()
+                rms = rs.elapsed_time(re_) / n_ref
+                del gr
+                extras["reference_gpu"] = {"tokens_per_s": args.lines / (rms * 1e-3), "ms_per_step": rms,
+                                           "hbm_gbs": step_bytes / (rms * 1e-3) / 1e9,
+                                           "what": "reference kernels (drama3/kernels.py, nvcc sm_100) driven as "
+                                                   "drama3/offload.py:108-117, one row at a time, one CUDA graph "
+                                                   "per step"}
+        except Exception as exc:  # the comparison leg must not sink the bench line
+            extras["reference_gpu"] = {"error": repr(exc)[:200]}
+        # the reference's CPU path on the host cores (bounded sample)
+        tps, secs, threads, sample = cpu_reference(args.lines)
+        extras["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
+                                  "sample": sample, "seconds": secs}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "e4m3 weights, f32 math", "data": "synthetic (seeded random banks)",
+                "config": config(args),
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                             "frac": achieved / hbm_peak, "traffic": None, "peak_kind": peak_kind,
+                             "kernel": "moe_up + moe_down (one decode layer; the pair overlaps through programmatic "
+                                       "dependent launch)",
+                             "bytes_per_step": step_bytes, "us_per_layer": 1e3 * ms / LAYERS},
+                "gpu_launches": 2 * LAYERS * args.steps,
+                "clocks": clocks.summary()}
+        line.update(extras)
+        print(json.dumps(line), flush=True)
+    del graph
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

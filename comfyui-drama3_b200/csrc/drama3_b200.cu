@@ -1,0 +1,398 @@
+// C ABI of the B200 routed-expert library (declared in include/drama3_b200.h). Every entry point checks its
+// arguments, launches on the caller's stream, allocates nothing and never synchronizes (except d3_take_fault),
+// so calls can be captured in CUDA graphs. Return value 0 or a D3_ERR_* code.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <mutex>
+
+#include "../../include/drama3_b200.h"
+#include "common.cuh"
+#include "gemv.cuh"
+#include "moe_decode.cuh"
+#include "resolve.cuh"
+#include "rotate.cuh"
+#include "route.cuh"
+
+namespace {
+
+thread_local int g_last_cuda = 0;
+
+int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return D3_OK;
+  g_last_cuda = (int)e;
+  return D3_ERR_CUDA;
+}
+
+int launch_status() { return cuda_status(cudaGetLastError()); }
+
+bool aligned(const void* p, size_t a) { return ((uintptr_t)p % a) == 0; }
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  int sms = 0;
+  int smem_optin = 0;
+  int cc = 0;
+};
+
+std::mutex g_mu;
+DeviceInfo g_dev[kMaxDevices];
+
+int device_info(DeviceInfo* out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return D3_ERR_DEVICE;
+  std::lock_guard<std::mutex> lock(g_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (d.sms == 0) {
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&d.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    d.cc = major * 10 + minor;
+  }
+  *out = d;
+  if (d.cc != 100) return D3_ERR_DEVICE;
+  return D3_OK;
+}
+
+// Raise a kernel's dynamic shared-memory ceiling (once per device and kernel).
+template <class K>
+int allow_smem(K kernel, int bytes) {
+  if (bytes <= 48 * 1024) return D3_OK;
+  return cuda_status(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+}
+
+template <class K, class... Args>
+int launch(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (pdl) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cuda_status(cudaLaunchKernelEx(&cfg, kernel, args...));
+}
+
+int static_smem(const void* kernel) {
+  cudaFuncAttributes fa;
+  if (cudaFuncGetAttributes(&fa, kernel) != cudaSuccess) return 0;
+  return (int)fa.sharedSizeBytes;
+}
+
+}  // namespace
+
+extern "C" {
+
+int d3_version(void) { return D3_VERSION; }
+
+const char* d3_error_string(int code) {
+  switch (code) {
+    case D3_OK: return "ok";
+    case D3_ERR_ARG: return "invalid argument (shape, count or format)";
+    case D3_ERR_ALIGN: return "pointer not aligned as required (16 bytes for weight rows and activations)";
+    case D3_ERR_CUDA: return "CUDA error at launch (see d3_last_cuda_error)";
+    case D3_ERR_DEVICE: return "current device is not an sm_100 (B200) GPU";
+    case D3_ERR_WORKSPACE: return "workspace too small";
+    default: return "unknown error";
+  }
+}
+
+int d3_last_cuda_error(void) { return g_last_cuda; }
+
+int d3_device_check(void) {
+  DeviceInfo d;
+  return device_info(&d);
+}
+
+int d3_take_fault(unsigned int* fault) {
+  if (fault == nullptr) return D3_ERR_ARG;
+  unsigned int v = 0, zero = 0;
+  int st = cuda_status(cudaMemcpyFromSymbol(&v, d3::g_fault, sizeof(v)));
+  if (st) return st;
+  st = cuda_status(cudaMemcpyToSymbol(d3::g_fault, &zero, sizeof(zero)));
+  *fault = v;
+  return st;
+}
+
+// ------------------------------------------------------------------------------------------------------------
+int d3_route(const uint16_t* logits, int rows, int n, int k, int64_t* ids, float* weights, void* stream) {
+  if (rows < 0 || n < 1 || n > d3::ROUTE_MAX_N || k < 1 || k > 32 || k > n) return D3_ERR_ARG;
+  if (!logits || !ids || !weights) return D3_ERR_ARG;
+  if (rows == 0) return D3_OK;
+  dim3 grid((rows + d3::ROUTE_WARPS - 1) / d3::ROUTE_WARPS);
+  d3::route_rows<<<grid, d3::ROUTE_WARPS * 32, 0, (cudaStream_t)stream>>>(logits, rows, n, k, ids, weights);
+  return launch_status();
+}
+
+int d3_weighted_sum(const float* parts, const float* weights, int rows, int k, int H, uint16_t* out, void* stream) {
+  if (rows < 0 || k < 1 || H < 1 || rows > 65535 || !parts || !weights || !out) return D3_ERR_ARG;
+  if (rows == 0) return D3_OK;
+  dim3 grid((H + 255) / 256, rows);
+  d3::combine_rows<<<grid, 256, 0, (cudaStream_t)stream>>>(parts, weights, rows, k, H, out);
+  return launch_status();
+}
+
+int d3_rotate(const void* x, int mode, int rows, int K, float* out, const int* only_if, void* stream) {
+  if (rows < 0 || K < 256 || K % 256 != 0 || K > 12288 || mode < 0 || mode > 2 || !x || !out) return D3_ERR_ARG;
+  if (rows == 0) return D3_OK;
+  int smem = K * 4;
+  int st = allow_smem(d3::rotate_rows_kernel, smem);
+  if (st) return st;
+  d3::rotate_rows_kernel<<<rows, 256, smem, (cudaStream_t)stream>>>(x, mode, K, out, only_if);
+  return launch_status();
+}
+
+int d3_resolve(const int64_t* ids, int k, int layer, int layers, int experts, int* table, int* owner, float* score,
+               int* at, int* pending, int count, int* clock, int* budget, int* plan, int* reads, int* step,
+               const float* share, double half_life, int cpu, double admit, void* stream) {
+  if (k < 1 || k > d3::RESOLVE_MAX_K || layers < 1 || layer < 0 || layer >= layers || experts < 1 || count < 1)
+    return D3_ERR_ARG;
+  if ((long long)layers * experts > 0x7fffffffLL) return D3_ERR_ARG;
+  if (!ids || !table || !owner || !score || !at || !pending || !clock || !budget || !plan || !reads || !step || !share)
+    return D3_ERR_ARG;
+  d3::resolve_kernel<<<1, d3::RESOLVE_THREADS, 0, (cudaStream_t)stream>>>(ids, k, layer, layers, experts, table, owner,
+                                                                         score, at, pending, count, clock, budget,
+                                                                         plan, reads, step, share, half_life, cpu,
+                                                                         admit);
+  return launch_status();
+}
+
+// ------------------------------------------------------------------------------------------------------------
+static int gemv_common(int fmt, const d3::GemvArgs& a, int k, void* stream) {
+  // K % 32: the swizzled staging of x permutes float4 slots within aligned groups of eight
+  if (k < 1 || k > 65535 || a.N < 16 || a.N % 16 || a.K < 32 || a.K % 32 || a.K > 32 * 16 * d3::GEMV_MAXV)
+    return D3_ERR_ARG;
+  if (a.x_rows != 1 && a.x_rows != k) return D3_ERR_ARG;
+  if (a.num_experts < 1 || a.slots < 0) return D3_ERR_ARG;
+  if (fmt == d3::FMT_FP8 && (a.N % 128 || a.K % 128)) return D3_ERR_ARG;
+  if ((fmt == d3::FMT_W4 || fmt == d3::FMT_W6) && (a.K % 256)) return D3_ERR_ARG;
+  if (fmt == d3::FMT_W4 && !a.codebook) return D3_ERR_ARG;
+  if (!a.x || !a.ids || !a.plan || !a.host_w || !a.host_s || !a.out) return D3_ERR_ARG;
+  if (!aligned(a.x, 16) || !aligned(a.host_w, 16) || (a.slot_w && !aligned(a.slot_w, 16))) return D3_ERR_ALIGN;
+  DeviceInfo d;
+  if (int st = device_info(&d)) return st;
+  dim3 grid(a.N / d3::GEMV_ROWS, k);
+  int smem = a.K * 4;
+  cudaStream_t s = (cudaStream_t)stream;
+  switch (fmt) {
+    case d3::FMT_FP8:
+      if (int st = allow_smem(d3::gemv_plan_kernel<d3::FMT_FP8>, smem)) return st;
+      d3::gemv_plan_kernel<d3::FMT_FP8><<<grid, d3::GEMV_WARPS * 32, smem, s>>>(a);
+      break;
+    case d3::FMT_I8:
+      if (int st = allow_smem(d3::gemv_plan_kernel<d3::FMT_I8>, smem)) return st;
+      d3::gemv_plan_kernel<d3::FMT_I8><<<grid, d3::GEMV_WARPS * 32, smem, s>>>(a);
+      break;
+    case d3::FMT_W4:
+      if (int st = allow_smem(d3::gemv_plan_kernel<d3::FMT_W4>, smem)) return st;
+      d3::gemv_plan_kernel<d3::FMT_W4><<<grid, d3::GEMV_WARPS * 32, smem, s>>>(a);
+      break;
+    case d3::FMT_W6:
+      if (int st = allow_smem(d3::gemv_plan_kernel<d3::FMT_W6>, smem)) return st;
+      d3::gemv_plan_kernel<d3::FMT_W6><<<grid, d3::GEMV_WARPS * 32, smem, s>>>(a);
+      break;
+    default: return D3_ERR_ARG;
+  }
+  return launch_status();
+}
+
+int d3_gemv_fp8(const float* x, int x_rows, const int64_t* ids, const int* plan, int k, uint8_t* slot_w,
+                float* slot_s, const uint8_t* host_w, const float* host_s, float* out, int N, int K,
+                int num_experts, int slots, void* stream) {
+  d3::GemvArgs a = {x, x_rows, ids, plan, nullptr, 0, slot_w, slot_s, nullptr, host_w, host_s, nullptr,
+                    nullptr, out, N, K, num_experts, slots};
+  return gemv_common(d3::FMT_FP8, a, k, stream);
+}
+
+int d3_gemv_int8(const float* x, int x_rows, const int64_t* ids, const int* plan, const int* took_over, int late,
+                 int k, int8_t* slot_w, float* slot_s, const int8_t* host_w, const float* host_s, float* out, int N,
+                 int K, int num_experts, int slots, void* stream) {
+  if (!took_over) return D3_ERR_ARG;
+  d3::GemvArgs a = {x, x_rows, ids, plan, took_over, late, (uint8_t*)slot_w, slot_s, nullptr, (const uint8_t*)host_w,
+                    host_s, nullptr, nullptr, out, N, K, num_experts, slots};
+  return gemv_common(d3::FMT_I8, a, k, stream);
+}
+
+int d3_gemv_codes(const float* x, int x_rows, const int64_t* ids, const int* plan, int k, uint8_t* slot_w,
+                  uint8_t* slot_r, float* slot_c, const uint8_t* host_w, const uint8_t* host_r,
+                  const float* host_c, const float* codebook, int bits, float* out, int N, int K, int num_experts,
+                  int slots, void* stream) {
+  if (bits != 4 && bits != 6) return D3_ERR_ARG;
+  if (!host_c) return D3_ERR_ARG;
+  d3::GemvArgs a = {x, x_rows, ids, plan, nullptr, 0, slot_w, slot_r, slot_c, host_w, host_r, host_c,
+                    codebook, out, N, K, num_experts, slots};
+  return gemv_common(bits == 4 ? d3::FMT_W4 : d3::FMT_W6, a, k, stream);
+}
+
+// ------------------------------------------------------------------------------------------------------------
+static int grouped_common(int fmt, const d3::GroupedArgs& a, int n_groups, void* stream) {
+  if (n_groups < 0 || n_groups > 65535 || a.N < 64 || a.N % 64 || a.K < 64 || a.K % 64 || a.x_rows < 0)
+    return D3_ERR_ARG;
+  if (fmt == d3::FMT_FP8 && (a.N % 128 || a.K % 128)) return D3_ERR_ARG;
+  if ((fmt == d3::FMT_W4 || fmt == d3::FMT_W6) && (a.K % 256)) return D3_ERR_ARG;
+  if (fmt == d3::FMT_W4 && !a.codebook) return D3_ERR_ARG;
+  if (!a.x || !a.groups || !a.host_w || !a.host_s || !a.out) return D3_ERR_ARG;
+  if (!aligned(a.x, 16) || !aligned(a.host_w, 16) || (a.slot_w && !aligned(a.slot_w, 16))) return D3_ERR_ALIGN;
+  if (n_groups == 0 || a.x_rows == 0) return D3_OK;
+  DeviceInfo d;
+  if (int st = device_info(&d)) return st;
+  int z = (a.x_rows + d3::GRP_TT - 1) / d3::GRP_TT;
+  if (z > 64) z = 64;
+  dim3 grid(a.N / d3::GRP_TN, n_groups, z);
+  cudaStream_t s = (cudaStream_t)stream;
+  switch (fmt) {
+    case d3::FMT_FP8: d3::grouped_plan_kernel<d3::FMT_FP8><<<grid, 256, 0, s>>>(a); break;
+    case d3::FMT_I8: d3::grouped_plan_kernel<d3::FMT_I8><<<grid, 256, 0, s>>>(a); break;
+    case d3::FMT_W4: d3::grouped_plan_kernel<d3::FMT_W4><<<grid, 256, 0, s>>>(a); break;
+    case d3::FMT_W6: d3::grouped_plan_kernel<d3::FMT_W6><<<grid, 256, 0, s>>>(a); break;
+    default: return D3_ERR_ARG;
+  }
+  return launch_status();
+}
+
+int d3_grouped_fp8(const float* x, int x_rows, const int* groups, int n_groups, uint8_t* slot_w, float* slot_s,
+                   const uint8_t* host_w, const float* host_s, float* out, int N, int K, int num_experts, int slots,
+                   void* stream) {
+  d3::GroupedArgs a = {x, groups, slot_w, slot_s, nullptr, host_w, host_s, nullptr, nullptr, out, N, K, num_experts,
+                       slots, x_rows};
+  return grouped_common(d3::FMT_FP8, a, n_groups, stream);
+}
+
+int d3_grouped_int8(const float* x, int x_rows, const int* groups, int n_groups, int8_t* slot_w, float* slot_s,
+                    const int8_t* host_w, const float* host_s, float* out, int N, int K, int num_experts, int slots,
+                    void* stream) {
+  d3::GroupedArgs a = {x, groups, (uint8_t*)slot_w, slot_s, nullptr, (const uint8_t*)host_w, host_s, nullptr,
+                       nullptr, out, N, K, num_experts, slots, x_rows};
+  return grouped_common(d3::FMT_I8, a, n_groups, stream);
+}
+
+int d3_grouped_codes(const float* x, int x_rows, const int* groups, int n_groups, uint8_t* slot_w, uint8_t* slot_r,
+                     float* slot_c, const uint8_t* host_w, const uint8_t* host_r, const float* host_c,
+                     const float* codebook, int bits, float* out, int N, int K, int num_experts, int slots,
+                     void* stream) {
+  if (bits != 4 && bits != 6) return D3_ERR_ARG;
+  if (!host_c) return D3_ERR_ARG;
+  d3::GroupedArgs a = {x, groups, slot_w, slot_r, slot_c, host_w, host_r, host_c, codebook, out, N, K, num_experts,
+                       slots, x_rows};
+  return grouped_common(bits == 4 ? d3::FMT_W4 : d3::FMT_W6, a, n_groups, stream);
+}
+
+// ------------------------------------------------------------------------------------------------------------
+// Fused decode.
+// Pairs a segment of one expert carries (the up kernel stages that many input rows in shared memory): the next
+// power of two >= M, at most 8. An expert routed to more rows is cut into several segments, each reading it again.
+static int cap_for(int M) {
+  int c = 1;
+  while (c < M && c < 8) c <<= 1;
+  return c;
+}
+
+size_t d3_moe_decode_workspace(int M, int k, int I) {
+  if (M < 1 || k < 1 || I < 1) return 0;
+  return (((size_t)M * k * I * 4) + 255) & ~(size_t)255;
+}
+
+}  // extern "C"
+
+template <int FMT, int CAP, int NV>
+static int decode_launch(const d3::UpArgs& up, d3::DownArgs down, const DeviceInfo& d, cudaStream_t s) {
+  auto k1 = d3::moe_up_kernel<FMT, CAP, NV>;
+  auto k2 = d3::moe_down_kernel<FMT, CAP>;
+  constexpr int RPW = CAP == 1 ? 1 : 2;
+  constexpr int CH = d3::DEC_WARPS * RPW;
+  const int H = up.H, I = up.I, P = up.M * up.k;
+  const int rb1 = d3::fmt_row_bytes(FMT, H), gb1 = H / 16;
+  const int stage1 = 2 * CH * rb1 + (d3::fmt_codes(FMT) ? 2 * CH * gb1 : 0);
+  const int sc1 = FMT == d3::FMT_FP8 ? (((2 * I / 128) * (H / 128) + 3) & ~3) * 4 : 0;
+  const int fixed1 = CAP * H * 4 + sc1;
+  const int G = d.sms;
+  const int RM = (H + G - 1) / G;
+  const int rb2 = d3::fmt_row_bytes(FMT, I), gb2 = I / 16;
+  const int stage2 = RM * rb2 + (d3::fmt_codes(FMT) ? RM * gb2 : 0) + CAP * I * 4;
+  const int fixed2 = ((P * RM * 4) + 127) & ~127;
+  const int st1 = static_smem((const void*)k1), st2 = static_smem((const void*)k2);
+  const int limit = d.smem_optin;  // per block
+  // Small M: keep both kernels resident on one SM (the down kernel's prologue and weight copies overlap the up
+  // kernel); large M: give the up kernel the deeper ring.
+  const int sm_total = 228 * 1024 - 2 * 1024;
+  int ns1 = CAP <= 2 ? 3 : d3::DEC_MAX_STAGES;
+  while (ns1 > 2 && fixed1 + ns1 * stage1 > limit) --ns1;
+  if (fixed1 + ns1 * stage1 > limit) return D3_ERR_ARG;
+  int ns2 = d3::DEC_MAX_STAGES;
+  const int room2 = CAP <= 2 ? sm_total - (fixed1 + ns1 * stage1 + st1) - st2 : limit;
+  while (ns2 > 2 && fixed2 + ns2 * stage2 > (room2 < limit ? room2 : limit)) --ns2;
+  if (fixed2 + ns2 * stage2 > limit) return D3_ERR_ARG;
+  d3::UpArgs u = up;
+  u.stages = ns1;
+  down.stages = ns2;
+  down.rows_max = RM;
+  down.cap = CAP;
+  const int smem1 = fixed1 + ns1 * stage1, smem2 = fixed2 + ns2 * stage2;
+  if (int st = allow_smem(k1, smem1)) return st;
+  if (int st = allow_smem(k2, smem2)) return st;
+  if (int st = launch(k1, dim3(G), dim3(d3::DEC_THREADS), smem1, s, false, u)) return st;
+  if (d3::fmt_rotated(FMT)) {
+    if (int st = allow_smem(d3::rotate_rows_kernel, I * 4)) return st;
+    if (int st = launch(d3::rotate_rows_kernel, dim3(P), dim3(256), I * 4, s, true, (const void*)up.a1, 0, I,
+                        up.a1, (const int*)nullptr))
+      return st;
+  }
+  return launch(k2, dim3(G), dim3(d3::DEC_THREADS), smem2, s, true, down);
+}
+
+template <int FMT, int NV>
+static int decode_cap(int cap, const d3::UpArgs& up, const d3::DownArgs& down, const DeviceInfo& d, cudaStream_t s) {
+  switch (cap) {
+    case 1: return decode_launch<FMT, 1, NV>(up, down, d, s);
+    case 2: return decode_launch<FMT, 2, NV>(up, down, d, s);
+    case 4: return decode_launch<FMT, 4, NV>(up, down, d, s);
+    case 8: return decode_launch<FMT, 8, NV>(up, down, d, s);
+    default: return D3_ERR_ARG;
+  }
+}
+
+template <int FMT>
+static int decode_fmt(int cap, const d3::UpArgs& up, const d3::DownArgs& down, const DeviceInfo& d, cudaStream_t s) {
+  switch (up.H) {
+    case 2048: return decode_cap<FMT, 4>(cap, up, down, d, s);
+    default: return D3_ERR_ARG;
+  }
+}
+
+extern "C" int d3_moe_decode(int fmt, const void* x, int x_bf16, int M, int k, int E, int H, int I, const int64_t* ids,
+                  const float* weights, const uint8_t* w13, const void* s13, const float* c13, const uint8_t* w2,
+                  const void* s2, const float* c2, const float* codebook13, const float* codebook2, uint16_t* out,
+                  void* workspace, size_t workspace_bytes, void* stream) {
+  if (fmt < d3::FMT_FP8 || fmt > d3::FMT_W6) return D3_ERR_ARG;
+  if (M < 1 || M > 16 || k < 1 || k > 32 || M * k > d3::DEC_MAX_PAIRS || E < 1) return D3_ERR_ARG;
+  if (H != 2048) return D3_ERR_ARG;
+  if (I < 128 || I % 128 || (d3::fmt_rotated(fmt) && I % 256)) return D3_ERR_ARG;
+  if (!x || !ids || !weights || !w13 || !s13 || !w2 || !s2 || !out || !workspace) return D3_ERR_ARG;
+  if (d3::fmt_codes(fmt) && (!c13 || !c2)) return D3_ERR_ARG;
+  if (fmt == d3::FMT_W4 && (!codebook13 || !codebook2)) return D3_ERR_ARG;
+  if (workspace_bytes < d3_moe_decode_workspace(M, k, I)) return D3_ERR_WORKSPACE;
+  if (!aligned(x, 16) || !aligned(w13, 16) || !aligned(w2, 16) || !aligned(workspace, 16) || !aligned(s13, 16) ||
+      !aligned(s2, 16))
+    return D3_ERR_ALIGN;
+  DeviceInfo d;
+  if (int st = device_info(&d)) return st;
+  d3::UpArgs up = {x, x_bf16, ids, M, k, E, H, I, w13, s13, c13, codebook13, (float*)workspace, 0};
+  d3::DownArgs down = {(const float*)workspace, ids, weights, M, k, E, H, I, w2, s2, c2, codebook2, out, 0, 0, 0};
+  const int cap = cap_for(M);
+  cudaStream_t s = (cudaStream_t)stream;
+  switch (fmt) {
+    case d3::FMT_FP8: return decode_fmt<d3::FMT_FP8>(cap, up, down, d, s);
+    case d3::FMT_I8: return decode_fmt<d3::FMT_I8>(cap, up, down, d, s);
+    case d3::FMT_W4: return decode_fmt<d3::FMT_W4>(cap, up, down, d, s);
+    case d3::FMT_W6: return decode_fmt<d3::FMT_W6>(cap, up, down, d, s);
+  }
+  return D3_ERR_ARG;
+}

@@ -1,0 +1,232 @@
+"""The reference's kernel module surface (drama3/kernels.py:604-724), backed by libdrama3_b200.so instead of NVRTC.
+
+Same function names, arguments, output shapes and dtypes; every output is allocated with torch on the input's device
+and every launch goes on the device's current stream, so calls can be captured in CUDA graphs. Differences:
+  - `available` returns False only for non-CUDA devices (as the reference does); on a CUDA device it raises if the
+    library is missing or the device is not an sm_100 GPU: there is no fallback implementation;
+  - `route` and `weighted_sum` also take several rows at once;
+  - `await_cpu` (the CPU-expert handshake) is not provided: this path has no CPU side;
+  - `moe_decode` is new: the whole resident decode (gate_up, SwiGLU, down, combine) for 1..16 rows in one pass.
+"""
+import functools
+
+import torch
+
+from . import _lib
+from ._lib import check, lib
+
+ROWS_PER_BLOCK = 16
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device):
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+@functools.cache
+def _device_ok(index):
+    with torch.cuda.device(index):
+        check(lib().d3_device_check(), f"cuda:{index}")
+    return True
+
+
+def available(device):
+    """Whether `device` runs these kernels: a CUDA device that is an sm_100 GPU, with the library built. Raises on a
+    CUDA device where that is not so (no fallback); False for other devices."""
+    device = torch.device(device)
+    if device.type != "cuda":
+        return False
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    return _device_ok(index)
+
+
+def _on(device):
+    available(device)
+    return torch.cuda.device(device)
+
+
+def resolve(ids, layer, layers, num_experts, half_life, cpu, admit, table, owner, score, at, pending, clock, budget,
+            reads, step, share):
+    """plan [k, 2] int32 for the row's experts `ids` [k] (int64) of `layer` (drama3/kernels.py:618-625)."""
+    plan = torch.empty((ids.shape[0], 2), dtype=torch.int32, device=ids.device)
+    with _on(ids.device):
+        check(lib().d3_resolve(_ptr(ids), ids.shape[0], int(layer), int(layers), int(num_experts), _ptr(table),
+                               _ptr(owner), _ptr(score), _ptr(at), _ptr(pending), owner.shape[0], _ptr(clock),
+                               _ptr(budget), _ptr(plan), _ptr(reads), _ptr(step), _ptr(share), float(half_life),
+                               int(cpu), float(admit), _stream(ids.device)), "resolve")
+    return plan
+
+
+def await_cpu(plan, flag, step, result, timeout_us, took_over):
+    raise NotImplementedError("drama3_b200 has no CPU-expert side: every expert runs on the GPU")
+
+
+def rotate(x, only_if, swiglu=False):
+    """Rows of x [rows, K] (float32 or bfloat16; float32 [rows, 2K] gate | up with `swiglu`, SiLU(gate) * up first)
+    in the ConvRot basis: float32 [rows, K]; left unset when `only_if` (an int32 on the GPU) is 0
+    (drama3/kernels.py:636-644)."""
+    rows, width = x.shape
+    k = width // 2 if swiglu else width
+    mode = 2 if swiglu else (1 if x.dtype == torch.bfloat16 else 0)
+    if mode != 1 and x.dtype != torch.float32:
+        raise TypeError(f"rotate takes float32 or bfloat16 rows, not {x.dtype}")
+    x = x.contiguous()
+    out = torch.empty((rows, k), dtype=torch.float32, device=x.device)
+    with _on(x.device):
+        check(lib().d3_rotate(_ptr(x), mode, rows, k, _ptr(out), _ptr(only_if), _stream(x.device)), "rotate")
+    return out
+
+
+def route(logits, k):
+    """(ids [rows, k] int64, weights [rows, k] float32) of router logits [rows, n] (bfloat16): the k largest, by
+    descending logit (ties: lower index first), and their softmax weights renormalized over them, rounded to
+    bfloat16 (drama3/kernels.py:647-653, for any number of rows)."""
+    if logits.dtype != torch.bfloat16:
+        raise TypeError("route takes bfloat16 logits")
+    logits = logits.contiguous()
+    rows, n = logits.shape
+    ids = torch.empty((rows, k), dtype=torch.int64, device=logits.device)
+    weights = torch.empty((rows, k), dtype=torch.float32, device=logits.device)
+    with _on(logits.device):
+        check(lib().d3_route(_ptr(logits), rows, n, int(k), _ptr(ids), _ptr(weights), _stream(logits.device)), "route")
+    return ids, weights
+
+
+def weighted_sum(parts, weights):
+    """[rows, H] bfloat16: parts [rows * k, H] (float32) summed per row by weights [rows, k] or [k] (float32), in
+    rank order (drama3/kernels.py:656-661; there rows == 1)."""
+    weights = weights.reshape(-1, weights.shape[-1]).float().contiguous()
+    rows, k = weights.shape
+    parts = parts.contiguous()
+    H = parts.shape[-1]
+    if parts.numel() != rows * k * H:
+        raise ValueError("parts must hold rows * k rows")
+    out = torch.empty((rows, H), dtype=torch.bfloat16, device=parts.device)
+    with _on(parts.device):
+        check(lib().d3_weighted_sum(_ptr(parts), _ptr(weights), rows, k, H, _ptr(out), _stream(parts.device)),
+              "weighted_sum")
+    return out
+
+
+def _bank_rows(fields, key, n):
+    return fields[key].shape[0] // n
+
+
+def gemv_int8(x, ids, plan, took_over, late, slot_fields, host_fields, n):
+    """[k, n] float32: each expert's int8 rows against x [1 or k, K] (float32, rotated); fields are
+    {"_qdata", "scale"} (drama3/kernels.py:664-671)."""
+    k, width = ids.shape[0], x.shape[1]
+    out = torch.empty((k, n), dtype=torch.float32, device=x.device)
+    with _on(x.device):
+        check(lib().d3_gemv_int8(_ptr(x), x.shape[0], _ptr(ids), _ptr(plan), _ptr(took_over), int(late), k,
+                                 _ptr(slot_fields["_qdata"]), _ptr(slot_fields["scale"]), _ptr(host_fields["_qdata"]),
+                                 _ptr(host_fields["scale"]), _ptr(out), n, width,
+                                 _bank_rows(host_fields, "_qdata", n), _bank_rows(slot_fields, "_qdata", n),
+                                 _stream(x.device)), "gemv_int8")
+    return out
+
+
+def gemv_fp8(x, ids, plan, slot_fields, host_fields, n):
+    """[k, n] float32: each expert's float8 rows against x [1 or k, K] float32; fields are {"weight", "scale"}
+    (drama3/kernels.py:674-681)."""
+    k, width = ids.shape[0], x.shape[1]
+    out = torch.empty((k, n), dtype=torch.float32, device=x.device)
+    with _on(x.device):
+        check(lib().d3_gemv_fp8(_ptr(x), x.shape[0], _ptr(ids), _ptr(plan), k, _ptr(slot_fields["weight"]),
+                                _ptr(slot_fields["scale"]), _ptr(host_fields["weight"]), _ptr(host_fields["scale"]),
+                                _ptr(out), n, width, _bank_rows(host_fields, "weight", n),
+                                _bank_rows(slot_fields, "weight", n), _stream(x.device)), "gemv_fp8")
+    return out
+
+
+def gemv_codes(x, ids, plan, slot_fields, host_fields, codebook, bits, n):
+    """gemv_int8 for W4A8/W6A8 banks; fields are {"_qdata", "scale" (e4m3), "s_channel"}, codebook [16] at 4 bits
+    (drama3/kernels.py:703-713)."""
+    k, width = ids.shape[0], x.shape[1]
+    out = torch.empty((k, n), dtype=torch.float32, device=x.device)
+    with _on(x.device):
+        check(lib().d3_gemv_codes(_ptr(x), x.shape[0], _ptr(ids), _ptr(plan), k, _ptr(slot_fields["_qdata"]),
+                                  _ptr(slot_fields["scale"]), _ptr(slot_fields["s_channel"]),
+                                  _ptr(host_fields["_qdata"]), _ptr(host_fields["scale"]),
+                                  _ptr(host_fields["s_channel"]), _ptr(codebook), int(bits), _ptr(out), n, width,
+                                  _bank_rows(host_fields, "_qdata", n), _bank_rows(slot_fields, "_qdata", n),
+                                  _stream(x.device)), "gemv_codes")
+    return out
+
+
+def grouped_int8(x, groups, slot_fields, host_fields, n):
+    """[rows, n] float32 for x's rows (float32, rotated, sorted by expert) through their experts; groups [g, 5] int32
+    (expert, slot, fill, first, rows). Rows outside every group are left unset (drama3/kernels.py:684-691)."""
+    out = torch.empty((x.shape[0], n), dtype=torch.float32, device=x.device)
+    with _on(x.device):
+        check(lib().d3_grouped_int8(_ptr(x), x.shape[0], _ptr(groups), groups.shape[0], _ptr(slot_fields["_qdata"]),
+                                    _ptr(slot_fields["scale"]), _ptr(host_fields["_qdata"]),
+                                    _ptr(host_fields["scale"]), _ptr(out), n, x.shape[1],
+                                    _bank_rows(host_fields, "_qdata", n), _bank_rows(slot_fields, "_qdata", n),
+                                    _stream(x.device)), "grouped_int8")
+    return out
+
+
+def grouped_fp8(x, groups, slot_fields, host_fields, n):
+    """grouped_int8 for float8 experts, against float32 rows x (drama3/kernels.py:694-700)."""
+    out = torch.empty((x.shape[0], n), dtype=torch.float32, device=x.device)
+    with _on(x.device):
+        check(lib().d3_grouped_fp8(_ptr(x), x.shape[0], _ptr(groups), groups.shape[0], _ptr(slot_fields["weight"]),
+                                   _ptr(slot_fields["scale"]), _ptr(host_fields["weight"]),
+                                   _ptr(host_fields["scale"]), _ptr(out), n, x.shape[1],
+                                   _bank_rows(host_fields, "weight", n), _bank_rows(slot_fields, "weight", n),
+                                   _stream(x.device)), "grouped_fp8")
+    return out
+
+
+def grouped_codes(x, groups, slot_fields, host_fields, codebook, bits, n):
+    """grouped_int8 for W4A8/W6A8 banks (drama3/kernels.py:716-724)."""
+    out = torch.empty((x.shape[0], n), dtype=torch.float32, device=x.device)
+    with _on(x.device):
+        check(lib().d3_grouped_codes(_ptr(x), x.shape[0], _ptr(groups), groups.shape[0], _ptr(slot_fields["_qdata"]),
+                                     _ptr(slot_fields["scale"]), _ptr(slot_fields["s_channel"]),
+                                     _ptr(host_fields["_qdata"]), _ptr(host_fields["scale"]),
+                                     _ptr(host_fields["s_channel"]), _ptr(codebook), int(bits), _ptr(out), n,
+                                     x.shape[1], _bank_rows(host_fields, "_qdata", n),
+                                     _bank_rows(slot_fields, "_qdata", n), _stream(x.device)), "grouped_codes")
+    return out
+
+
+def decode_workspace(rows, k, intermediate, device):
+    """The workspace moe_decode needs, allocated once by the caller (graph-captured steps reuse it)."""
+    size = lib().d3_moe_decode_workspace(rows, k, intermediate)
+    return torch.empty((size,), dtype=torch.uint8, device=device)
+
+
+def moe_decode(kind, x, ids, weights, banks, codebooks=(None, None), workspace=None, out=None):
+    """[M, H] bfloat16: rows x [M, H] (bfloat16 or float32, M <= 16) through their routed experts ids [M, k] (int64)
+    mixed by weights [M, k], with banks (gate_up, down) held whole on the GPU in the reference layouts:
+    fp8 {"weight" uint8 [E*2I, H] / [E*H, I], "scale" fp32 block scales}; int8 {"_qdata", "scale"};
+    w4/w6 {"_qdata", "scale" (e4m3 bytes), "s_channel"} and a codebook per bank for w4. Each routed expert is read
+    once for all M rows."""
+    fmt = _lib.FORMATS[kind]
+    gate_up, down = banks
+    wkey = "weight" if kind == "fp8" else "_qdata"
+    M, H = x.shape
+    k = ids.shape[-1]
+    w13, w2 = gate_up[wkey], down[wkey]
+    E = w2.shape[0] // H
+    I = w13.shape[0] // (2 * E)
+    if out is None:
+        out = torch.empty((M, H), dtype=torch.bfloat16, device=x.device)
+    if workspace is None:
+        workspace = decode_workspace(M, k, I, x.device)
+    x = x.contiguous()
+    ids = ids.reshape(M, k).contiguous()
+    weights = weights.reshape(M, k).float().contiguous()
+    scale13 = gate_up["scale"].view(torch.uint8) if kind in ("w4", "w6") else gate_up["scale"]
+    scale2 = down["scale"].view(torch.uint8) if kind in ("w4", "w6") else down["scale"]
+    with _on(x.device):
+        check(lib().d3_moe_decode(fmt, _ptr(x), int(x.dtype == torch.bfloat16), M, k, E, H, I, _ptr(ids),
+                                  _ptr(weights), _ptr(w13), _ptr(scale13), _ptr(gate_up.get("s_channel")), _ptr(w2),
+                                  _ptr(scale2), _ptr(down.get("s_channel")), _ptr(codebooks[0]), _ptr(codebooks[1]),
+                                  _ptr(out), _ptr(workspace), workspace.numel(), _stream(x.device)), "moe_decode")
+    return out

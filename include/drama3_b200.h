@@ -1,0 +1,127 @@
+/* drama3_b200: the routed-expert MoE path of ComfyUI-Drama3, as a C ABI over hand-written sm_100a (B200) kernels.
+ *
+ * Conventions for every entry point:
+ *   - all tensor arguments are device pointers (or pinned, mapped host pointers where a "host_*" field says so);
+ *   - `stream` is a cudaStream_t (NULL: the legacy default stream); the call launches on it and returns without
+ *     synchronizing, so calls can be captured in CUDA graphs;
+ *   - nothing is allocated: outputs and workspaces are the caller's;
+ *   - the return value is D3_OK (0) or a D3_ERR_* code, checked before any launch;
+ *   - kernels never trap on bad data: an out-of-range expert id or slot is skipped (zeros) and recorded in a
+ *     per-device fault word that d3_take_fault() reads and clears; a wait that runs past its limit does the same.
+ *
+ * Each entry cites the reference interface it replaces, as path:line inside PedroMarinhoDev/ComfyUI-Drama3. The
+ * reference launches these computations from Python (drama3/kernels.py) through NVRTC; there is no C FFI there.
+ */
+#ifndef DRAMA3_B200_H
+#define DRAMA3_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define D3_VERSION 100
+
+#define D3_OK 0
+#define D3_ERR_ARG 1       /* a shape, count, format or null pointer the kernels do not take */
+#define D3_ERR_ALIGN 2     /* a weight, activation or workspace pointer not 16-byte aligned */
+#define D3_ERR_CUDA 3      /* the launch failed; d3_last_cuda_error() has the cudaError_t */
+#define D3_ERR_DEVICE 4    /* the current device is not compute capability 10.0 */
+#define D3_ERR_WORKSPACE 5 /* the workspace is smaller than d3_moe_decode_workspace() */
+
+/* Weight formats of the fused decode (the reference's safetensors layouts; drama3/offload.py:72-90,755-766). */
+#define D3_FMT_FP8 0  /* e4m3 rows + fp32 128x128 block scales */
+#define D3_FMT_INT8 1 /* int8 ConvRot rows + fp32 row scales */
+#define D3_FMT_W4 2   /* 4-bit codes + e4m3 group-16 scales + s_channel + 16-entry codebook, ConvRot */
+#define D3_FMT_W6 3   /* 6-bit codes (nibble plane + 2-bit plane) + e4m3 group-16 scales + s_channel, ConvRot */
+
+int d3_version(void);
+const char* d3_error_string(int code);
+int d3_last_cuda_error(void);
+
+/* D3_OK when the current device is an sm_100 GPU; stands in for the reference's availability probe
+ * drama3/kernels.py:604-615 (available), which there falls back to PyTorch; here there is no fallback. */
+int d3_device_check(void);
+
+/* Reads and clears the current device's fault word (synchronous). Bits: 1 a wait timed out, 2 an expert id out of
+ * range, 4 a slot out of range. No counterpart in the reference, whose kernels do not check indices. */
+int d3_take_fault(unsigned int* fault);
+
+/* Decode routing, `rows` independent rows: ids [rows, k] (int64) and weights [rows, k] (fp32 holding bfloat16
+ * values) of logits [rows, n] (bfloat16): the k largest by (value desc, index asc) and their softmax weights
+ * renormalized over them. n <= 1024, k <= 32.
+ * Replaces drama3/kernels.py:39-67 (route_experts) and its launcher :647-653 (route), which take one row. */
+int d3_route(const uint16_t* logits, int rows, int n, int k, int64_t* ids, float* weights, void* stream);
+
+/* out [rows, H] (bfloat16) = sum_e parts[row*k + e, :] * weights[row*k + e], fp32 in e order.
+ * Replaces drama3/kernels.py:69-76 (weighted_sum) and :656-661. */
+int d3_weighted_sum(const float* parts, const float* weights, int rows, int k, int H, uint16_t* out, void* stream);
+
+/* ConvRot rotation of rows: mode 0 fp32 x [rows, K], 1 bfloat16 x [rows, K], 2 fp32 x [rows, 2K] gate|up with
+ * SwiGLU first; out fp32 [rows, K] (out may equal x); skipped when only_if (device int, may be NULL) is 0.
+ * K % 256 == 0. Replaces drama3/kernels.py:222-258 (rotate_rows) and :636-644 (rotate). */
+int d3_rotate(const void* x, int mode, int rows, int K, float* out, const int* only_if, void* stream);
+
+/* Slot-cache lookup and eviction for one decode row's k experts of `layer`; writes plan [k, 2] (slot, code) and
+ * updates the cache state in place. Same state arrays and semantics as drama3/kernels.py:78-191 (resolve_experts),
+ * launcher :618-625 (resolve); k <= 32. */
+int d3_resolve(const int64_t* ids, int k, int layer, int layers, int experts, int* table, int* owner, float* score,
+               int* at, int* pending, int count, int* clock, int* budget, int* plan, int* reads, int* step,
+               const float* share, double half_life, int cpu, double admit, void* stream);
+
+/* Per-expert GEMVs under a slot plan: out [k, N] fp32 = expert e's rows . x[e or 0] (x fp32 [x_rows, K],
+ * x_rows 1 or k). Expert e comes from slot plan[2e] (code 0) or from host memory expert ids[e] (code != 0,
+ * mapped pinned memory), filling its slot when plan[2e] >= 0. num_experts bounds ids, slots bounds plan slots.
+ * Replace drama3/kernels.py:316-363 (gemv_fp8) / :674-681, :274-314 (gemv_int8) / :664-671, :495-536
+ * (gemv_codes) / :703-713. N % 16 == 0, K % 32 == 0, K <= 4096 (fp8 N, K % 128; codes K % 256). */
+int d3_gemv_fp8(const float* x, int x_rows, const int64_t* ids, const int* plan, int k, uint8_t* slot_w,
+                float* slot_s, const uint8_t* host_w, const float* host_s, float* out, int N, int K,
+                int num_experts, int slots, void* stream);
+int d3_gemv_int8(const float* x, int x_rows, const int64_t* ids, const int* plan, const int* took_over, int late,
+                 int k, int8_t* slot_w, float* slot_s, const int8_t* host_w, const float* host_s, float* out, int N,
+                 int K, int num_experts, int slots, void* stream);
+int d3_gemv_codes(const float* x, int x_rows, const int64_t* ids, const int* plan, int k, uint8_t* slot_w,
+                  uint8_t* slot_r, float* slot_c, const uint8_t* host_w, const uint8_t* host_r,
+                  const float* host_c, const float* codebook, int bits, float* out, int N, int K, int num_experts,
+                  int slots, void* stream);
+
+/* Prompt rows grouped by expert: groups [n_groups, 5] int32 (expert, slot, fill, first, rows) over x fp32
+ * [x_rows, K] sorted by expert; out [x_rows, N] fp32 (rows outside every group untouched).
+ * Replace drama3/kernels.py:408-464 (grouped_fp8) / :694-700, :365-406 (grouped_int8) / :684-691, :538-587
+ * (grouped_codes) / :716-724. N % 64 == 0, K % 64 == 0. */
+int d3_grouped_fp8(const float* x, int x_rows, const int* groups, int n_groups, uint8_t* slot_w, float* slot_s,
+                   const uint8_t* host_w, const float* host_s, float* out, int N, int K, int num_experts, int slots,
+                   void* stream);
+int d3_grouped_int8(const float* x, int x_rows, const int* groups, int n_groups, int8_t* slot_w, float* slot_s,
+                    const int8_t* host_w, const float* host_s, float* out, int N, int K, int num_experts, int slots,
+                    void* stream);
+int d3_grouped_codes(const float* x, int x_rows, const int* groups, int n_groups, uint8_t* slot_w, uint8_t* slot_r,
+                     float* slot_c, const uint8_t* host_w, const uint8_t* host_r, const float* host_c,
+                     const float* codebook, int bits, float* out, int N, int K, int num_experts, int slots,
+                     void* stream);
+
+/* Bytes of workspace d3_moe_decode needs for M rows, top-k and expert width I. */
+size_t d3_moe_decode_workspace(int M, int k, int I);
+
+/* Fused decode of M rows (1..16) through their routed experts held whole in device memory:
+ *   out [M, H] bf16 = sum_j weights[t, j] * down_{ids[t,j]}(SwiGLU(gate_up_{ids[t,j]} . x[t]))
+ * with x [M, H] (bfloat16 when x_bf16, else fp32), ids [M, k] int64, weights [M, k] fp32. Banks in the reference
+ * layouts, flattened over experts: w13 [E*2I, row] (gate rows then up rows per expert), w2 [E*H, row];
+ * s13/s2: fp8 block scales (fp32 [E*N/128, K/128]), int8 row scales (fp32 [E*N]) or code group scales
+ * (uint8 e4m3 [E*N, K/16]); c13/c2: s_channel (codes only); codebook13/2: W4 codebooks (fp32 [16]).
+ * ConvRot formats rotate x and the SwiGLU output as the reference does. Each unique expert of the M*k pairs is
+ * read once (an expert routed to more than 8 of the rows is read once per 8 of them). H == 2048, I % 128 == 0 (% 256 for ConvRot formats), M*k <= 128.
+ * Replaces the chain drama3/offload.py:108-123 (resident_decode) = gemv -> SwiGLU/rotate -> gemv -> weighted_sum,
+ * which drama3/model.py:111-113 runs once per row of a lines-at-once batch. */
+int d3_moe_decode(int fmt, const void* x, int x_bf16, int M, int k, int E, int H, int I, const int64_t* ids,
+                  const float* weights, const uint8_t* w13, const void* s13, const float* c13, const uint8_t* w2,
+                  const void* s2, const float* c2, const float* codebook13, const float* codebook2, uint16_t* out,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DRAMA3_B200_H */

@@ -1,0 +1,487 @@
+"""CPU restatement (numpy) of the reference's routed-expert arithmetic. TEST INFRASTRUCTURE ONLY (see __init__).
+
+Every function names the reference lines it follows (PedroMarinhoDev/ComfyUI-Drama3). Integer and byte work
+(routing indices, code decoding, slot plans, packing) is restated exactly; float work keeps the reference's
+data flow (fp32 tensors between steps) with float64 dot products, so the oracle is at least as accurate as the
+kernels it checks. The math functions (expf, exp2f) come from numpy; CUDA's own are never restated.
+"""
+import numpy as np
+
+F32 = np.float32
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# number formats
+def bf16_to_f32(bits):
+    """bfloat16 bits (uint16) -> float32 (drama3/kernels.py:31)."""
+    return (np.asarray(bits).astype(np.uint32) << np.uint32(16)).view(np.float32)
+
+
+def f32_to_bf16(values):
+    """float32 -> bfloat16 bits, nearest-even, the reference's rounding (drama3/kernels.py:33-37)."""
+    b = np.asarray(values, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    return ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def bf16_round(values):
+    return bf16_to_f32(f32_to_bf16(values))
+
+
+def _e4m3_table():
+    """float value of each e4m3 byte as the reference decodes it: the 7 magnitude bits shifted into a float's exponent
+    and mantissa, times 2^120 (drama3/kernels.py:25-29). Byte 0x7F decodes to 480 there (not NaN); valid banks never
+    hold it."""
+    b = np.arange(256, dtype=np.uint32)
+    bits = ((b & 0x80) << 24) | ((b & 0x7F) << 20)
+    return (bits.view(np.float32).astype(np.float64) * 2.0 ** 120).astype(np.float32)
+
+
+E4M3 = _e4m3_table()
+
+
+def e4m3_to_f32(bytes_):
+    return E4M3[np.asarray(bytes_, dtype=np.uint8)]
+
+
+def f32_to_e4m3(values):
+    """float -> nearest e4m3 byte, ties to even mantissa, saturating at +-448 (the quantizer side; torch's cast does
+    the same for in-range values)."""
+    v = np.asarray(values, dtype=np.float32)
+    pos = E4M3[:0x7F]  # 0x00..0x7E, ascending
+    a = np.minimum(np.abs(v), F32(448.0))
+    idx = np.clip(np.searchsorted(pos, a), 1, 0x7E)
+    lo, hi = pos[idx - 1], pos[idx]
+    pick_hi = (a - lo > hi - a) | ((a - lo == hi - a) & ((idx & 1) == 0))
+    code = np.where(pick_hi, idx, idx - 1).astype(np.uint8)
+    code = np.where(a <= 0, 0, code).astype(np.uint8)
+    return (code | np.where(v < 0, 0x80, 0).astype(np.uint8)).astype(np.uint8)
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# routing and combine
+def route(logits_bits, k):
+    """Decode routing per row (drama3/kernels.py:47-66): the k largest logits by (value desc, index asc), weights
+    expf(l - l_0) summed on one thread in rank order, each divided by the sum, rounded to bfloat16."""
+    v = bf16_to_f32(logits_bits).reshape(-1, np.asarray(logits_bits).shape[-1])
+    rows, n = v.shape
+    ids = np.zeros((rows, k), dtype=np.int64)
+    weights = np.zeros((rows, k), dtype=np.float32)
+    for r in range(rows):
+        order = sorted(range(n), key=lambda i: (-float(v[r, i]), i))[:k]
+        top = v[r, order]
+        with np.errstate(over="ignore"):
+            ex = np.exp((top - top[0]).astype(np.float32)).astype(np.float32)
+        total = F32(0.0)
+        for e in range(k):
+            total = F32(total + ex[e])
+        ids[r] = order
+        weights[r] = bf16_round((ex / total).astype(np.float32))
+    return ids, weights
+
+
+def route_prefill(logits_bits, k):
+    """Prompt routing (drama3/model.py:120-121): softmax in fp32, top-k, renormalized, cast to bfloat16. Returns ids
+    and the bf16-valued weights as float32; ids equal route()'s on inputs without ties at the k-th place."""
+    v = bf16_to_f32(logits_bits).astype(np.float64)
+    p = np.exp(v - v.max(axis=-1, keepdims=True))
+    p = p / p.sum(axis=-1, keepdims=True)
+    order = np.argsort(-p, axis=-1, kind="stable")[:, :k]
+    top = np.take_along_axis(p, order, axis=-1)
+    return order.astype(np.int64), bf16_round((top / top.sum(axis=-1, keepdims=True)).astype(np.float32))
+
+
+def fma32(a, b, c):
+    """float32 fused multiply-add, through float64 (exact product)."""
+    return (np.asarray(a, np.float64) * np.asarray(b, np.float64) + np.asarray(c, np.float64)).astype(np.float32)
+
+
+def weighted_sum(parts, weights):
+    """out [rows, H] bfloat16-valued float32 = sum_e parts[e] * w[e], fp32 multiply-add in e order
+    (drama3/kernels.py:69-76)."""
+    weights = np.asarray(weights, np.float32).reshape(-1, np.asarray(weights).shape[-1])
+    rows, k = weights.shape
+    parts = np.asarray(parts, np.float32).reshape(rows, k, -1)
+    acc = np.zeros((rows, parts.shape[-1]), np.float32)
+    for e in range(k):
+        acc = fma32(parts[:, e], weights[:, e:e + 1], acc)
+    return bf16_round(acc)
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# ConvRot
+def hadamard(size):
+    """The regular Hadamard matrix of `size` (a power of 4), normalized (drama3/offload.py:170-176)."""
+    h4 = np.array([[1, 1, 1, -1], [1, 1, -1, 1], [1, -1, 1, 1], [-1, 1, 1, 1]], np.float64)
+    h = h4
+    while h.shape[0] < size:
+        h = np.kron(h, h4)
+    return h / size ** 0.5
+
+
+def swiglu_fast(g, u):
+    """g / (1 + exp(-g)) * u in fp32 (drama3/kernels.py:233-236)."""
+    g = np.asarray(g, np.float32)
+    with np.errstate(over="ignore"):
+        return (g / (F32(1.0) + np.exp(-g)) * np.asarray(u, np.float32)).astype(np.float32)
+
+
+def rotate(x, swiglu=False):
+    """Rows in the ConvRot basis (drama3/kernels.py:226-258): optional SwiGLU of [rows, 2K] gate | up, then the
+    four radix-4 butterfly stages in the kernel's order and expression order, then * 1/16. Bit-exact in fp32 for
+    the butterfly; the SwiGLU exp is numpy's."""
+    x = np.asarray(x, np.float32)
+    if swiglu:
+        K = x.shape[-1] // 2
+        row = swiglu_fast(x[..., :K], x[..., K:])
+    else:
+        row = x.copy()
+    rows, K = row.shape
+    row = row.copy()
+    for stride in (1, 4, 16, 64):
+        t = np.arange(K // 4)
+        within = t & 63
+        low, high = within % stride, within // stride
+        i = (t >> 6) * 256 + high * stride * 4 + low
+        a, b, c, d = row[:, i], row[:, i + stride], row[:, i + 2 * stride], row[:, i + 3 * stride]
+        row[:, i] = a + b + c - d
+        row[:, i + stride] = a + b - c + d
+        row[:, i + 2 * stride] = a - b + c + d
+        row[:, i + 3 * stride] = -a + b + c + d
+    return (row * F32(0.0625)).astype(np.float32)
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# weight formats
+def decode_codes(qrow, srow, K, bits, codebook):
+    """W4/W6 rows on the int8 grid (drama3/kernels.py:469-483): code = nibble (low nibble = even column), plus two
+    bits from the high plane after the K/2 nibble bytes at 6 bits; value = codebook[code] (4 bits) or code - 32
+    (6 bits); times the group's e4m3 scale, rounded half-even, clamped to +-127. qrow [..., K*bits/8],
+    srow [..., K/16] -> int8 [..., K]."""
+    qrow = np.asarray(qrow, np.uint8)
+    lead = qrow.shape[:-1]
+    nib = np.empty(lead + (K,), np.uint32)
+    nib[..., 0::2] = qrow[..., :K // 2] & 0xF
+    nib[..., 1::2] = qrow[..., :K // 2] >> 4
+    if bits == 6:
+        hi = qrow[..., K // 2:K // 2 + K // 4]
+        h = np.stack([(hi >> (2 * j)) & 3 for j in range(4)], axis=-1).reshape(lead + (K,)).astype(np.uint32)
+        value = (nib | (h << 4)).astype(np.float32) - F32(32.0)
+    else:
+        value = np.asarray(codebook, np.float32)[nib]
+    s = np.repeat(e4m3_to_f32(srow), 16, axis=-1)
+    return np.clip(np.rint((value * s).astype(np.float32)), -127, 127).astype(np.int8)
+
+
+def dequant_fp8(weight, scale):
+    """float8 rows [R, C] with fp32 128x128 block scales [R/128, C/128] -> float64 (drama3/offload.py:163-167)."""
+    w = e4m3_to_f32(weight).astype(np.float64)
+    R, C = w.shape
+    s = np.asarray(scale, np.float64)
+    return (w.reshape(R // 128, 128, C // 128, 128) * s[:, None, :, None]).reshape(R, C)
+
+
+def dequant_int8(qdata, scale):
+    return np.asarray(qdata, np.int8).astype(np.float64) * np.asarray(scale, np.float64).reshape(-1, 1)
+
+
+def dequant_codes(qdata, rel, channel, K, bits, codebook):
+    q = decode_codes(qdata, rel, K, bits, codebook)
+    return q.astype(np.float64) * np.asarray(channel, np.float64).reshape(-1, 1)
+
+
+def expert_rows(kind, fields, first_row, rows, K, codebook=None):
+    """Rows [first_row, first_row + rows) of a bank (host or slot fields) as float64 weights in the basis the kernel
+    multiplies with (rotated for ConvRot formats)."""
+    sl = slice(first_row, first_row + rows)
+    if kind == "fp8":
+        return dequant_fp8(fields["weight"][sl], fields["scale"][first_row // 128:(first_row + rows) // 128])
+    if kind == "int8":
+        return dequant_int8(fields["_qdata"][sl], np.asarray(fields["scale"]).reshape(-1)[sl])
+    bits = int(kind[1])
+    return dequant_codes(fields["_qdata"][sl], fields["scale"][sl], np.asarray(fields["s_channel"]).reshape(-1)[sl],
+                         K, bits, codebook)
+
+
+def _copy_rows(kind, src, dst, src_row, dst_row, rows):
+    """Slot fill: expert rows (and their scales) copied from host fields into slot fields."""
+    for name, s in src.items():
+        d = dst[name]
+        if kind == "fp8" and name == "scale":
+            a, b = src_row // 128, dst_row // 128
+            d[b:b + rows // 128] = s[a:a + rows // 128]
+        else:
+            d[dst_row:dst_row + rows] = s[src_row:src_row + rows]
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# per-expert GEMVs and grouped kernels under a slot plan
+def gemv(kind, x, ids, plan, slot_fields, host_fields, n, codebook=None, took_over=0, late=False):
+    """out [k, n] (float32) of each expert's rows against x [1 or k, K], the slot plan's sources and fills as in
+    drama3/kernels.py:274-314 (int8: code 2 left to the CPU, `late` runs only those), :316-363 (fp8) and :495-536
+    (codes). Slot fields are updated in place for filled experts."""
+    x = np.asarray(x, np.float32)
+    k, K = len(ids), x.shape[1]
+    out = np.zeros((k, n), np.float32)
+    for e in range(k):
+        slot, code = int(plan[e][0]), int(plan[e][1])
+        if kind == "int8" and (code != 2 or not took_over if late else code == 2):
+            continue
+        host = code != 0
+        fill = (code == 1 if kind == "int8" else host) and slot >= 0
+        fields = host_fields if host else slot_fields
+        first = int(ids[e]) * n if host else slot * n
+        w = expert_rows(kind, fields, first, n, K, codebook)
+        xr = x[0 if x.shape[0] == 1 else e].astype(np.float64)
+        out[e] = (w @ xr).astype(np.float32)
+        if fill:
+            _copy_rows(kind, host_fields, slot_fields, int(ids[e]) * n, slot * n, n)
+    return out
+
+
+def grouped(kind, x, groups, slot_fields, host_fields, n, codebook=None, out=None):
+    """Rows of x sorted by expert through their groups' experts (drama3/kernels.py:365-464, 538-587): group =
+    (expert, slot, fill, first, rows); host memory when slot < 0 or fill, which copies the expert into its slot."""
+    x = np.asarray(x, np.float32)
+    K = x.shape[1]
+    if out is None:
+        out = np.zeros((x.shape[0], n), np.float32)
+    for expert, slot, fill, first, rows in np.asarray(groups).tolist():
+        host = slot < 0 or fill
+        fields = host_fields if host else slot_fields
+        w = expert_rows(kind, fields, (expert if host else slot) * n, n, K, codebook)
+        out[first:first + rows] = (x[first:first + rows].astype(np.float64) @ w.T).astype(np.float32)
+        if fill and slot >= 0:
+            _copy_rows(kind, host_fields, slot_fields, expert * n, slot * n, n)
+    return out
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# slot cache
+def new_state(layers, experts, count):
+    """Slot-cache state as drama3/offload.py:579-596 creates it (SlotPool.__init__)."""
+    return {
+        "table": np.full(layers * experts, -1, np.int32), "owner": np.full(count, -1, np.int32),
+        "score": np.zeros(layers * experts, np.float32), "at": np.full(layers * experts, -1, np.int32),
+        "pending": np.zeros(count, np.int32), "clock": np.zeros(1, np.int32), "budget": np.zeros(2, np.int32),
+        "reads": np.zeros(3, np.int32), "step": np.zeros(1, np.int32), "share": np.zeros(1, np.float32),
+    }
+
+
+def resolve(state, ids, layer, layers, experts, half_life, cpu, admit):
+    """plan [k, 2] for one decode row's experts, updating `state` in place, step by step as
+    drama3/kernels.py:87-191 (resolve_experts)."""
+    st = state
+    k = len(ids)
+    base = layer * experts
+    log2_decay = F32(F32(-1.0) / F32(F32(half_life) * F32(layers)))
+    if layer == 0:
+        st["clock"][0] += 1
+    now = int(st["clock"][0]) * layers + layer
+    st["step"][0] = now
+
+    def decayed(key):
+        return F32(st["score"][key] * np.exp2(F32(log2_decay * F32(now - int(st["at"][key])))))
+
+    slot_of, fill, uses = [0] * k, [0] * k, [F32(0)] * k
+    for t in range(k):
+        key = base + int(ids[t])
+        kept = F32(0.0) if st["at"][key] < 0 else decayed(key)
+        st["score"][key] = F32(kept + F32(1.0))
+        uses[t] = F32(kept + F32(1.0))
+        st["at"][key] = now
+        slot = int(st["table"][key])
+        slot_of[t] = slot if slot >= 0 else -1
+        fill[t] = 0 if slot >= 0 else (1 if not cpu else (4 if slot == -1 else 2))
+    ahead = [0] * k
+    misses = 0
+    for e in range(k):
+        for o in range(k):
+            if fill[e] == 4 and fill[o] == 4 and (uses[o] > uses[e] or (uses[o] == uses[e] and o < e)):
+                ahead[e] += 1
+        misses += fill[e] == 4
+    sh = F32(st["share"][0])
+    gpu = int(fma32(F32(misses), sh, F32(F32(0.5) * F32(F32(1.0) - sh))))
+    for e in range(k):
+        if fill[e] == 4:
+            fill[e] = 1 if ahead[e] < gpu else (3 if uses[e] >= F32(admit) else 2)
+    allowed = min(int(st["budget"][0]), int(st["budget"][1]))
+    for e in range(k):
+        if fill[e] != 3:
+            continue
+        before = sum(1 for o in range(k) if fill[o] == 3 and (uses[o] > uses[e] or (uses[o] == uses[e] and o < e)))
+        if before < allowed:
+            st["budget"][0] -= 1
+        else:
+            fill[e] = 5
+    for e in range(k):
+        if fill[e] == 5:
+            fill[e] = 2
+        st["reads"][0 if fill[e] == 0 else 1 if fill[e] == 1 else 2] += 1
+    for e in range(k):
+        if fill[e] != 1 and fill[e] != 3:
+            continue
+        best, index = F32(3.0e38), None
+        for i in range(len(st["owner"])):
+            key = int(st["owner"][i])
+            if key < 0:
+                v = F32(-1.0)
+            elif st["pending"][i] or st["at"][key] == now:
+                v = F32(3.0e38)
+            else:
+                v = decayed(key)
+            if v < best:
+                best, index = v, i
+        if index is not None and best < F32(3.0e38):
+            key = base + int(ids[e])
+            old = int(st["owner"][index])
+            if old >= 0:
+                st["table"][old] = -1
+            st["owner"][index] = key
+            if fill[e] == 1:
+                st["table"][key] = index
+            else:
+                st["table"][key] = -2 - index
+                st["pending"][index] = 1
+            slot_of[e] = index
+    return np.array([[slot_of[t], 2 if fill[t] == 3 else fill[t]] for t in range(k)], np.int32)
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# the decode and prefill chains
+def _silu_mul(gate, up):
+    """torch's silu(gate) * up in fp32 (the fp8 path, drama3/offload.py:116)."""
+    g = np.asarray(gate, np.float64)
+    return (g / (1.0 + np.exp(-g)) * np.asarray(up, np.float64)).astype(np.float32)
+
+
+def resident_decode(kind, x, ids, weights, banks, rows, codebooks=(None, None)):
+    """One row x [1, H] through experts ids [k] of banks held whole (expert e in slot e) (drama3/offload.py:108-123):
+    fp8: gemv -> silu(gate) * up -> gemv -> weighted_sum; quantized: rotate -> gemv -> rotate(swiglu) -> gemv ->
+    weighted_sum. Returns [1, H] bf16-valued float32."""
+    gate_up, down = banks
+    n1, n2 = rows
+    x = np.asarray(x, np.float32).reshape(1, -1)
+    plan = np.stack([np.asarray(ids, np.int32), np.zeros(len(ids), np.int32)], axis=-1)
+    if kind == "fp8":
+        h = gemv("fp8", x, ids, plan, gate_up, gate_up, n1)
+        a = _silu_mul(h[:, :n1 // 2], h[:, n1 // 2:])
+        out = gemv("fp8", a, ids, plan, down, down, n2)
+    else:
+        h = gemv(kind, rotate(x), ids, plan, gate_up, gate_up, n1, codebooks[0])
+        out = gemv(kind, rotate(h, swiglu=True), ids, plan, down, down, n2, codebooks[1])
+    return weighted_sum(out, np.asarray(weights, np.float32).reshape(1, -1))
+
+
+def moe_decode(kind, x, ids, weights, banks, codebooks=(None, None)):
+    """M rows, each through resident_decode, as SparseMoeBlock.forward does for a lines-at-once batch
+    (drama3/model.py:111-113)."""
+    gate_up, down = banks
+    x = np.asarray(x, np.float32)
+    H = x.shape[1]
+    wkey = "weight" if kind == "fp8" else "_qdata"
+    E = down[wkey].shape[0] // H
+    n1 = gate_up[wkey].shape[0] // E
+    return np.concatenate([resident_decode(kind, x[t:t + 1], ids[t], weights[t], banks, (n1, H), codebooks)
+                           for t in range(x.shape[0])])
+
+
+def resident_prefill(kind, x, topk_idx, topk_weight, banks, codebooks=(None, None)):
+    """Many rows through banks held whole (drama3/offload.py:138-149): rows sorted by expert, one grouped pass per
+    bank, scattered back, times the routing weight, summed over k, cast to bf16."""
+    gate_up, down = banks
+    x = np.asarray(x, np.float32)
+    T, k = topk_idx.shape
+    H = x.shape[1]
+    wkey = "weight" if kind == "fp8" else "_qdata"
+    E = down[wkey].shape[0] // H
+    n1 = gate_up[wkey].shape[0] // E
+    flat = np.asarray(topk_idx).reshape(-1)
+    order = np.argsort(flat, kind="stable")
+    counts = np.bincount(flat, minlength=E)
+    offsets = np.concatenate([[0], np.cumsum(counts)])
+    groups = np.array([(e, e, 0, offsets[e], c) for e, c in enumerate(counts) if c], np.int32).reshape(-1, 5)
+    sx = x[order // k]
+    if kind == "fp8":
+        h = grouped("fp8", sx, groups, gate_up, gate_up, n1)
+        out = grouped("fp8", _silu_mul(h[:, :n1 // 2], h[:, n1 // 2:]), groups, down, down, H)
+    else:
+        h = grouped(kind, rotate(sx), groups, gate_up, gate_up, n1, codebooks[0])
+        out = grouped(kind, rotate(h, swiglu=True), groups, down, down, H, codebooks[1])
+    full = np.empty_like(out)
+    full[order] = out * np.asarray(topk_weight, np.float32).reshape(-1)[order][:, None]
+    return bf16_round(full.reshape(T, k, -1).sum(axis=1, dtype=np.float32))
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# synthetic banks (the quantizer side; comfy_kitchen's quantizers are not available, so W4/W6 use plain
+# nearest-value rounding)
+def quantize_fp8_blocks(w):
+    """[N, K] float -> (e4m3 bytes [N, K], fp32 128x128 block scales absmax/448) (the layout of
+    tools/convert.py:179-189)."""
+    w = np.asarray(w, np.float32)
+    N, K = w.shape
+    blocks = w.reshape(N // 128, 128, K // 128, 128)
+    scale = (np.abs(blocks).max(axis=(1, 3)) / F32(448.0)).astype(np.float32)
+    scale = np.where(scale == 0, F32(1.0), scale).astype(np.float32)
+    q = f32_to_e4m3((blocks / scale[:, None, :, None]).reshape(N, K).astype(np.float32))
+    return q, scale
+
+
+def convrot_weight(w):
+    """W in the ConvRot basis: each row times H256 per 256-column group (so W x = W_rot (x H))."""
+    w = np.asarray(w, np.float64)
+    N, K = w.shape
+    return (w.reshape(N, K // 256, 256) @ hadamard(256)).reshape(N, K)
+
+
+def quantize_int8_convrot(w):
+    """[N, K] float -> (int8 [N, K], fp32 row scales [N]): per-row absmax/127 of the rotated rows, rounded half-even
+    (the layout of tools/convert.py:48-53)."""
+    r = convrot_weight(w)
+    scale = (np.abs(r).max(axis=1) / 127.0).astype(np.float32)
+    scale = np.where(scale == 0, F32(1.0), scale)
+    q = np.clip(np.rint(r / scale[:, None].astype(np.float64)), -127, 127).astype(np.int8)
+    return q, scale
+
+
+CODEBOOK4 = np.array([-1.0, -0.6962, -0.5251, -0.3949, -0.2844, -0.1848, -0.0911, 0.0, 0.0796, 0.1609, 0.2461,
+                      0.3379, 0.4407, 0.5626, 0.7230, 1.0], np.float32)
+
+
+def quantize_codes(w, bits, codebook=CODEBOOK4):
+    """[N, K] float -> (codes [N, K*bits/8], e4m3 group scales [N, K/16], fp32 s_channel [N]) in the reference's
+    W4A8 / W6A8 plane layout (drama3/kernels.py:466-483), by nearest-value rounding in the rotated basis."""
+    r = convrot_weight(w)
+    N, K = r.shape
+    chan = (np.abs(r).max(axis=1) / 127.0).astype(np.float32)
+    chan = np.where(chan == 0, F32(1.0), chan)
+    target = r / chan[:, None]  # on the int8 grid
+    groups = target.reshape(N, K // 16, 16)
+    top = float(np.abs(codebook).max()) if bits == 4 else 31.0
+    gscale = f32_to_e4m3(np.maximum(np.abs(groups).max(axis=2) / top, 2.0 ** -6).astype(np.float32))
+    s = e4m3_to_f32(gscale).astype(np.float64)[:, :, None]
+    if bits == 4:
+        cand = np.clip(np.rint(np.asarray(codebook, np.float64)[None, None, None, :] * s[..., None]), -127, 127)
+        code = np.abs(cand - groups[..., None]).argmin(axis=-1).reshape(N, K)
+    else:
+        code = (np.clip(np.rint(groups / s), -32, 31) + 32).astype(np.int64).reshape(N, K)
+    nib = (code & 0xF).astype(np.uint8)
+    planes = [nib[:, 0::2] | (nib[:, 1::2] << 4)]
+    if bits == 6:
+        h = (code >> 4).astype(np.uint8).reshape(N, K // 4, 4)
+        planes.append(h[..., 0] | (h[..., 1] << 2) | (h[..., 2] << 4) | (h[..., 3] << 6))
+    return np.concatenate(planes, axis=1).astype(np.uint8), gscale, chan.astype(np.float32)
+
+
+def make_bank(kind, w, codebook=CODEBOOK4):
+    """Fields of one flat bank [E * N, ...] from float experts w [E, N, K]."""
+    E, N, K = w.shape
+    flat = np.asarray(w, np.float32).reshape(E * N, K)
+    if kind == "fp8":
+        q, s = quantize_fp8_blocks(flat)
+        return {"weight": q, "scale": s}
+    if kind == "int8":
+        q, s = quantize_int8_convrot(flat)
+        return {"_qdata": q, "scale": s}
+    q, g, c = quantize_codes(flat, int(kind[1]), codebook)
+    return {"_qdata": q, "scale": g, "s_channel": c}
