@@ -17,7 +17,7 @@ SOURCES = [HERE / "csrc" / "drama3_b200.cu"]
 DEPENDS = sorted((HERE / "csrc").glob("*.cu*")) + [ROOT / "include" / "drama3_b200.h"]
 OUTPUT = HERE / "drama3_b200" / "libdrama3_b200.so"
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
-              "-shared", "-Xptxas", "-warn-spills", "-diag-suppress", "177"]
+              "-shared", "-Xptxas", "-warn-spills", "-diag-suppress", "177,128"]
 
 
 def nvcc():

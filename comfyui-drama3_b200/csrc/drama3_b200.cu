@@ -112,6 +112,11 @@ int d3_device_check(void) {
   return device_info(&d);
 }
 
+#ifdef D3_TRACE
+// Trace builds only: copy the per-CTA phase timestamps (uint64 [1024][24]) to host memory.
+int d3_trace_read(void* dst) { return cuda_status(cudaMemcpyFromSymbol(dst, d3::g_trace, sizeof(d3::g_trace))); }
+#endif
+
 int d3_take_fault(unsigned int* fault) {
   if (fault == nullptr) return D3_ERR_ARG;
   unsigned int v = 0, zero = 0;
@@ -287,82 +292,41 @@ int d3_grouped_codes(const float* x, int x_rows, const int* groups, int n_groups
 
 // ------------------------------------------------------------------------------------------------------------
 // Fused decode.
-// Pairs a segment of one expert carries (the up kernel stages that many input rows in shared memory): the next
-// power of two >= M, at most 8. An expert routed to more rows is cut into several segments, each reading it again.
-static int cap_for(int M) {
-  int c = 1;
-  while (c < M && c < 8) c <<= 1;
-  return c;
-}
+// Pairs a segment of one expert carries (the MMA's 8 columns): at most 8. An expert routed to more of the rows is
+// cut into several segments, each reading it again.
+static int cap_for(int M) { return M < d3::DEC_MAX_CAP ? M : d3::DEC_MAX_CAP; }
+
+static size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
 
 size_t d3_moe_decode_workspace(int M, int k, int I) {
   if (M < 1 || k < 1 || I < 1) return 0;
-  return (((size_t)M * k * I * 4) + 255) & ~(size_t)255;
+  const size_t P = (size_t)M * k;
+  return align256(P * I * 4) + align256(P * d3::DEC_H * 4) + 256;
 }
 
 }  // extern "C"
 
-template <int FMT, int CAP, int NV>
-static int decode_launch(const d3::UpArgs& up, d3::DownArgs down, const DeviceInfo& d, cudaStream_t s) {
-  auto k1 = d3::moe_up_kernel<FMT, CAP, NV>;
-  auto k2 = d3::moe_down_kernel<FMT, CAP>;
-  constexpr int RPW = CAP == 1 ? 1 : 2;
-  constexpr int CH = d3::DEC_WARPS * RPW;
-  const int H = up.H, I = up.I, P = up.M * up.k;
-  const int rb1 = d3::fmt_row_bytes(FMT, H), gb1 = H / 16;
-  const int stage1 = 2 * CH * rb1 + (d3::fmt_codes(FMT) ? 2 * CH * gb1 : 0);
-  const int sc1 = FMT == d3::FMT_FP8 ? (((2 * I / 128) * (H / 128) + 3) & ~3) * 4 : 0;
-  const int fixed1 = CAP * H * 4 + sc1;
-  const int G = d.sms;
-  const int RM = (H + G - 1) / G;
-  const int rb2 = d3::fmt_row_bytes(FMT, I), gb2 = I / 16;
-  const int stage2 = RM * rb2 + (d3::fmt_codes(FMT) ? RM * gb2 : 0) + CAP * I * 4;
-  const int fixed2 = ((P * RM * 4) + 127) & ~127;
-  const int st1 = static_smem((const void*)k1), st2 = static_smem((const void*)k2);
-  const int limit = d.smem_optin;  // per block
-  // Small M: keep both kernels resident on one SM (the down kernel's prologue and weight copies overlap the up
-  // kernel); large M: give the up kernel the deeper ring.
-  const int sm_total = 228 * 1024 - 2 * 1024;
-  int ns1 = CAP <= 2 ? 3 : d3::DEC_MAX_STAGES;
-  while (ns1 > 2 && fixed1 + ns1 * stage1 > limit) --ns1;
-  if (fixed1 + ns1 * stage1 > limit) return D3_ERR_ARG;
-  int ns2 = d3::DEC_MAX_STAGES;
-  const int room2 = CAP <= 2 ? sm_total - (fixed1 + ns1 * stage1 + st1) - st2 : limit;
-  while (ns2 > 2 && fixed2 + ns2 * stage2 > (room2 < limit ? room2 : limit)) --ns2;
-  if (fixed2 + ns2 * stage2 > limit) return D3_ERR_ARG;
-  d3::UpArgs u = up;
-  u.stages = ns1;
-  down.stages = ns2;
-  down.rows_max = RM;
-  down.cap = CAP;
-  const int smem1 = fixed1 + ns1 * stage1, smem2 = fixed2 + ns2 * stage2;
-  if (int st = allow_smem(k1, smem1)) return st;
-  if (int st = allow_smem(k2, smem2)) return st;
-  if (int st = launch(k1, dim3(G), dim3(d3::DEC_THREADS), smem1, s, false, u)) return st;
-  if (d3::fmt_rotated(FMT)) {
-    if (int st = allow_smem(d3::rotate_rows_kernel, I * 4)) return st;
-    if (int st = launch(d3::rotate_rows_kernel, dim3(P), dim3(256), I * 4, s, true, (const void*)up.a1, 0, I,
-                        up.a1, (const int*)nullptr))
-      return st;
-  }
-  return launch(k2, dim3(G), dim3(d3::DEC_THREADS), smem2, s, true, down);
+template <int FMT, bool XBF, int NKC>
+static int decode_launch(const d3::DecodeArgs& a0, const DeviceInfo& d, cudaStream_t s) {
+  auto kern = d3::moe_decode_kernel<FMT, XBF, NKC>;
+  d3::DecodeArgs a = a0;
+  const int SB = d3::decode_stage_bytes<FMT>(d3::DEC_H, a.I);
+  const int limit = d.smem_optin - static_smem((const void*)kern);
+  int ns = d3::DEC_MAX_STAGES;
+  while (ns > 2 && d3::decode_smem<FMT, XBF>(d3::DEC_H, a.I, ns, SB).total > limit) --ns;
+  const int smem = d3::decode_smem<FMT, XBF>(d3::DEC_H, a.I, ns, SB).total;
+  if (smem > limit) return D3_ERR_ARG;
+  a.stages = ns;
+  a.stage_bytes = SB;
+  if (int st = allow_smem(kern, smem)) return st;
+  return launch(kern, dim3(d.sms), dim3(d3::DEC_ALL), smem, s, false, a);
 }
 
-template <int FMT, int NV>
-static int decode_cap(int cap, const d3::UpArgs& up, const d3::DownArgs& down, const DeviceInfo& d, cudaStream_t s) {
-  switch (cap) {
-    case 1: return decode_launch<FMT, 1, NV>(up, down, d, s);
-    case 2: return decode_launch<FMT, 2, NV>(up, down, d, s);
-    case 4: return decode_launch<FMT, 4, NV>(up, down, d, s);
-    case 8: return decode_launch<FMT, 8, NV>(up, down, d, s);
-    default: return D3_ERR_ARG;
-  }
-}
-
-template <int FMT>
-static int decode_fmt(int cap, const d3::UpArgs& up, const d3::DownArgs& down, const DeviceInfo& d, cudaStream_t s) {
-  switch (up.H) {
-    case 2048: return decode_cap<FMT, 4>(cap, up, down, d, s);
+template <int FMT, bool XBF>
+static int decode_nkc(const d3::DecodeArgs& a, const DeviceInfo& d, cudaStream_t s) {
+  switch (a.I) {
+    case 512: return decode_launch<FMT, XBF, 2>(a, d, s);
+    case 768: return decode_launch<FMT, XBF, 3>(a, d, s);
     default: return D3_ERR_ARG;
   }
 }
@@ -373,26 +337,31 @@ extern "C" int d3_moe_decode(int fmt, const void* x, int x_bf16, int M, int k, i
                   void* workspace, size_t workspace_bytes, void* stream) {
   if (fmt < d3::FMT_FP8 || fmt > d3::FMT_W6) return D3_ERR_ARG;
   if (M < 1 || M > 16 || k < 1 || k > 32 || M * k > d3::DEC_MAX_PAIRS || E < 1) return D3_ERR_ARG;
-  if (H != 2048) return D3_ERR_ARG;
-  if (I < 128 || I % 128 || (d3::fmt_rotated(fmt) && I % 256)) return D3_ERR_ARG;
+  if (H != d3::DEC_H || (I != 512 && I != 768)) return D3_ERR_ARG;
   if (!x || !ids || !weights || !w13 || !s13 || !w2 || !s2 || !out || !workspace) return D3_ERR_ARG;
   if (d3::fmt_codes(fmt) && (!c13 || !c2)) return D3_ERR_ARG;
   if (fmt == d3::FMT_W4 && (!codebook13 || !codebook2)) return D3_ERR_ARG;
   if (workspace_bytes < d3_moe_decode_workspace(M, k, I)) return D3_ERR_WORKSPACE;
-  if (!aligned(x, 16) || !aligned(w13, 16) || !aligned(w2, 16) || !aligned(workspace, 16) || !aligned(s13, 16) ||
+  if (!aligned(x, 16) || !aligned(w13, 16) || !aligned(w2, 16) || !aligned(workspace, 256) || !aligned(s13, 16) ||
       !aligned(s2, 16))
     return D3_ERR_ALIGN;
   DeviceInfo d;
   if (int st = device_info(&d)) return st;
-  d3::UpArgs up = {x, x_bf16, ids, M, k, E, H, I, w13, s13, c13, codebook13, (float*)workspace, 0};
-  d3::DownArgs down = {(const float*)workspace, ids, weights, M, k, E, H, I, w2, s2, c2, codebook2, out, 0, 0, 0};
+  const size_t P = (size_t)M * k;
+  uint8_t* ws = (uint8_t*)workspace;
+  float* a1 = (float*)ws;
+  float* parts = (float*)(ws + align256(P * I * 4));
+  auto* barrier = (unsigned long long*)(ws + align256(P * I * 4) + align256(P * d3::DEC_H * 4));
   const int cap = cap_for(M);
+  d3::DecodeArgs a = {x, x_bf16, ids, weights, M, k, E, H, I, w13, s13, c13, codebook13, w2, s2, c2, codebook2,
+                      out, a1, parts, barrier, 0, 0, cap};
   cudaStream_t s = (cudaStream_t)stream;
   switch (fmt) {
-    case d3::FMT_FP8: return decode_fmt<d3::FMT_FP8>(cap, up, down, d, s);
-    case d3::FMT_I8: return decode_fmt<d3::FMT_I8>(cap, up, down, d, s);
-    case d3::FMT_W4: return decode_fmt<d3::FMT_W4>(cap, up, down, d, s);
-    case d3::FMT_W6: return decode_fmt<d3::FMT_W6>(cap, up, down, d, s);
+    case d3::FMT_FP8:
+      return x_bf16 ? decode_nkc<d3::FMT_FP8, true>(a, d, s) : decode_nkc<d3::FMT_FP8, false>(a, d, s);
+    case d3::FMT_I8: return decode_nkc<d3::FMT_I8, true>(a, d, s);
+    case d3::FMT_W4: return decode_nkc<d3::FMT_W4, true>(a, d, s);
+    case d3::FMT_W6: return decode_nkc<d3::FMT_W6, true>(a, d, s);
   }
   return D3_ERR_ARG;
 }

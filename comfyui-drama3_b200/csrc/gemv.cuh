@@ -12,7 +12,7 @@
 #pragma once
 
 #include "common.cuh"
-#include "moe_decode.cuh"
+#include "formats.cuh"
 
 namespace d3 {
 

@@ -2,42 +2,65 @@
 //
 // Replaces, for banks resident in HBM, the chain of drama3/offload.py:108-123 (resident_decode): gemv(gate_up) ->
 // SwiGLU [-> ConvRot rotate] -> gemv(down) -> weighted_sum, which the reference runs once per row
-// (drama3/model.py:111-113). Here all M rows go through one pass that reads each routed expert once:
+// (drama3/model.py:111-113). Here all M rows go through one persistent kernel (one CTA per SM) that reads each
+// routed expert once:
 //
-//   up   (K1): the unique experts of the M*k (row, rank) pairs, gate and up rows streamed HBM -> shared memory by
-//              1-D bulk copies (cp.async.bulk) on an mbarrier ring filled by one producer warp; eight consumer warps
-//              dequantize in registers and write a1[pair, i] = SwiGLU(gate . x, up . x) (fp32).
-//   [rot]:     ConvRot formats only, the reference rotate of a1 (rotate_rows_kernel, in place).
-//   down (K2): each CTA owns a slice of output columns n0..n1 for every unique expert, so the routed combine
-//              out[t, n] = bf16(sum_j w[t, j] * down_{e(t,j)}[n] . a1[t*k+j]) happens inside the CTA, in rank order,
-//              deterministic and without atomics. Launched as a programmatic dependent of the kernel before it: it
-//              issues its weight copies before waiting for a1, so they overlap the previous kernel's tail.
+//   plan      every CTA sorts the M*k (row, rank) pairs by expert: segments of one expert and at most 8 pairs.
+//   phase 1   gate_up + SwiGLU: the segments' gate and up rows, split evenly over the CTAs as contiguous ranges of
+//             (segment, i) pair-rows; a1[pair, i] = SwiGLU(gate_i . x, up_i . x) to global scratch (fp32).
+//   barrier   (grid-wide, bounded wait)
+//   phase 2   down: the segments' down rows, split the same way; parts[pair, n] = down_n . a1[pair] (fp32 scratch).
+//   barrier
+//   phase 3   combine: out[t, n] = bf16(sum_j w[t, j] * parts[t*k + j, n]) in rank order (the reference's
+//             weighted_sum order), deterministic, no atomics.
 //
-// Formats (the reference's safetensors layouts, drama3/offload.py:72-90,755-766, tools/convert.py:48-82,179-215):
-//   FP8  e4m3 rows [E*N, K], fp32 128x128 block scales [E*N/128, K/128]; x used as is.
-//   I8   int8 rows [E*N, K], fp32 row scales [E*N]; ConvRot (x rotated per 256 columns).
-//   W4   4-bit codes [E*N, K/2] (low nibble = even column), e4m3 group scales [E*N, K/16], fp32 s_channel [E*N],
-//        a 16-entry float codebook; weight = clamp(rint(codebook[c] * scale), +-127) (drama3/kernels.py:469-483).
-//   W6   6-bit: nibble plane [K/2] then 2-bit high plane [K/4] per row; weight = clamp(rint((c - 32) * scale), +-127).
+// Data movement: weights reach shared memory through 1-D bulk copies (cp.async.bulk, the untiled TMA path) issued
+// by one producer warp on an mbarrier ring that runs through both phases, so the down rows stream in while phase 1
+// finishes and while the CTAs wait at the barrier.
+//
+// Arithmetic: tensor cores (mma.sync m16n8k16, f16 inputs, f32 accumulation). A = 16 weight rows converted in
+// registers to f16 exactly (e4m3 by cvt; int8 by byte placement; W4/W6 by the reference's int8-grid decode), B = the
+// segment's pairs (up to 8 columns) staged as f16: x * 2^e for bf16 rows (exact), or an f16 hi + lo pair for fp32
+// rows (~22 significant bits, two MMAs). A tile costs the same for 1 or 8 pairs, so the work per CTA is the bytes it
+// streams whatever the routing. The k index is permuted identically for A and B inside each 64-column chunk so that
+// a lane loads 16 contiguous weight columns and 16 contiguous activation halves; a dot product is order-free.
+// Each chunk's k range is split over the eight consumer warps and reduced through shared memory.
 #pragma once
 
+#include <cuda_fp16.h>
+
 #include "common.cuh"
+#include "formats.cuh"
 #include "rotate.cuh"
 
 namespace d3 {
 
-enum { FMT_FP8 = 0, FMT_I8 = 1, FMT_W4 = 2, FMT_W6 = 3 };
+#ifdef D3_TRACE
+// Compile-time phase timestamps (build with -DD3_TRACE): per CTA, globaltimer at the kernel's milestones and the
+// time the first consumer warp spent waiting for data and staging inputs. Off in normal builds.
+__device__ unsigned long long g_trace[1024][24];
+#define D3_STAMP(slot) \
+  if (threadIdx.x == 0 && blockIdx.x < 1024) g_trace[blockIdx.x][slot] = globaltimer()
+#define D3_ADD(slot, v) \
+  if (threadIdx.x == 0 && blockIdx.x < 1024) g_trace[blockIdx.x][slot] += (v)
+#define D3_ADD_EPI(slot, v) \
+  if (threadIdx.x == DEC_WARPS * 32 && blockIdx.x < 1024) g_trace[blockIdx.x][slot] += (v)
+#else
+#define D3_STAMP(slot)
+#define D3_ADD(slot, v)
+#define D3_ADD_EPI(slot, v)
+#endif
 
-constexpr int DEC_WARPS = 8;                      // consumer warps
-constexpr int DEC_THREADS = (DEC_WARPS + 1) * 32;  // + one producer warp
-constexpr int DEC_MAX_PAIRS = 128;                 // M * k (16 rows x top-8)
+constexpr int DEC_WARPS = 8;                       // consumer warps
+constexpr int DEC_THREADS = (DEC_WARPS + 2) * 32;  // + the epilogue warp and the producer warp
+constexpr int DEC_CONSUMERS = DEC_WARPS * 32;
+constexpr int DEC_MAX_PAIRS = 128;  // M * k
 constexpr int DEC_MAX_STAGES = 8;
-
-__host__ __device__ constexpr int fmt_row_bytes(int fmt, int K) {
-  return fmt == FMT_W4 ? K / 2 : fmt == FMT_W6 ? 3 * K / 4 : K;
-}
-__host__ __device__ constexpr bool fmt_rotated(int fmt) { return fmt != FMT_FP8; }
-__host__ __device__ constexpr bool fmt_codes(int fmt) { return fmt == FMT_W4 || fmt == FMT_W6; }
+constexpr int DEC_MAX_CAP = 8;  // pairs per segment = the MMA's N
+constexpr int DEC_H = 2048;     // hidden size the kernels are built for
+constexpr int DEC_CH1 = 8;      // phase-1 pair-rows per chunk: one 16-row tile (8 gate rows, 8 up rows)
+constexpr int DEC_CH2 = 32;     // phase-2 rows per chunk: two 16-row tiles
+constexpr int DEC_PAD = 8;      // halves of padding per staged row (conflict-free fragment loads)
 
 // ---------------------------------------------------------------------------------------------------------------
 // The pass plan: the M*k (row, rank) pairs sorted by (expert, pair), cut into segments of one expert and at most
@@ -101,167 +124,606 @@ D3_DEV void build_plan(DecodePlan& pl, const int64_t* __restrict__ ids, int P, i
   __syncthreads();
 }
 
-// Swizzled float4 slot of float4 index f in a staged activation row: conflict-free 16-byte loads when lane l reads
-// float4 4*(l + 32j) + q for fixed (j, q).
-D3_DEV int xswz(int f) { return f ^ ((f >> 2) & 7); }
-D3_DEV int xswz_elem(int i) { return (xswz(i >> 2) << 2) | (i & 3); }
-
 // ---------------------------------------------------------------------------------------------------------------
-// Weight decoding, 16 columns at a time (K1) or 4 / 8 columns (K2).
-D3_DEV void dec16_fp8(uint4 w, float (&f)[16]) {
-  e4m3x4(w.x, f[0], f[1], f[2], f[3]);
-  e4m3x4(w.y, f[4], f[5], f[6], f[7]);
-  e4m3x4(w.z, f[8], f[9], f[10], f[11]);
-  e4m3x4(w.w, f[12], f[13], f[14], f[15]);
+// Staged activation columns of the MMA (one per pair of the current segment): f16 [8][K + DEC_PAD], the hi term,
+// then for fp32 sources the lo term in a second such block. inv[j] = 2^-e (times 1/16 for ConvRot rows) undoes the
+// staging scale on the dot products.
+__host__ __device__ constexpr int stage_row_halves(int K) { return K + DEC_PAD; }
+
+// 2^e such that max * 2^e lies in [2^14, 2^15): f16 then holds every value of the row below 65504.
+D3_DEV int stage_exponent(float m) {
+  if (!(m > 0.0f) || !(m < 3.0e38f)) return 0;
+  const int ex = (int)((__float_as_uint(m) >> 23) & 0xFF) - 127;
+  return min(100, max(-100, 14 - ex));
 }
 
-D3_DEV void dec4_i8(uint32_t w, float& f0, float& f1, float& f2, float& f3) {
-  f0 = (float)(int)(signed char)(w & 0xFFu);
-  f1 = (float)(int)(signed char)((w >> 8) & 0xFFu);
-  f2 = (float)(int)(signed char)((w >> 16) & 0xFFu);
-  f3 = (float)((int)w >> 24);
-}
-
-D3_DEV void dec16_i8(uint4 w, float (&f)[16]) {
-  dec4_i8(w.x, f[0], f[1], f[2], f[3]);
-  dec4_i8(w.y, f[4], f[5], f[6], f[7]);
-  dec4_i8(w.z, f[8], f[9], f[10], f[11]);
-  dec4_i8(w.w, f[12], f[13], f[14], f[15]);
-}
-
-D3_DEV float grid_value(float v, float s) { return fmaxf(-127.0f, fminf(127.0f, rintf(v * s))); }
-
-// `n` codes starting at column c0 of a 16-column group (n = 16 or 8): W4 from 8 nibble bytes, W6 adding the 2-bit
-// high plane word `high` (2 bits per column of the group).
-template <int N>
-D3_DEV void dec_w4(uint2 low, float s, const float* __restrict__ lut, float (&f)[N]) {
+// The 8 values lane `lane` owns of item (row j, 256-column group q): columns 256q + 8 lane .. + 7 of source row
+// rows[j] (bf16, or fp32 read at L2).
+D3_DEV void stage_load(const void* src, bool bf16, size_t base, float (&v)[8]) {
+  if (bf16) {
+    const uint4 b = *(const uint4*)((const uint16_t*)src + base);
+    const uint32_t w[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
-  for (int j = 0; j < N; ++j) {
-    uint32_t code = ((j < 8 ? low.x : low.y) >> (4 * (j & 7))) & 0xFu;
-    f[j] = grid_value(lut[code], s);
-  }
-}
-template <int N>
-D3_DEV void dec_w6(uint2 low, uint32_t high, float s, float (&f)[N]) {
-#pragma unroll
-  for (int j = 0; j < N; ++j) {
-    uint32_t code = ((j < 8 ? low.x : low.y) >> (4 * (j & 7))) & 0xFu;
-    code |= ((high >> (2 * j)) & 3u) << 4;
-    f[j] = grid_value((float)((int)code - 32), s);
+    for (int u = 0; u < 4; ++u) {
+      v[2 * u] = bf16_to_f32(w[u] & 0xFFFFu);
+      v[2 * u + 1] = bf16_to_f32(w[u] >> 16);
+    }
+  } else {
+    const float4 f0 = __ldcg((const float4*)((const float*)src + base));
+    const float4 f1 = __ldcg((const float4*)((const float*)src + base) + 1);
+    v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w;
+    v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
   }
 }
 
-D3_DEV float dot16(const float (&w)[16], const float4* __restrict__ x0, const float4* __restrict__ x1,
-                   const float4* __restrict__ x2, const float4* __restrict__ x3) {
-  float4 a = *x0, b = *x1, c = *x2, d = *x3;
-  float acc = w[0] * a.x;
-  acc = fmaf(w[1], a.y, acc);
-  acc = fmaf(w[2], a.z, acc);
-  acc = fmaf(w[3], a.w, acc);
-  acc = fmaf(w[4], b.x, acc);
-  acc = fmaf(w[5], b.y, acc);
-  acc = fmaf(w[6], b.z, acc);
-  acc = fmaf(w[7], b.w, acc);
-  acc = fmaf(w[8], c.x, acc);
-  acc = fmaf(w[9], c.y, acc);
-  acc = fmaf(w[10], c.z, acc);
-  acc = fmaf(w[11], c.w, acc);
-  acc = fmaf(w[12], d.x, acc);
-  acc = fmaf(w[13], d.y, acc);
-  acc = fmaf(w[14], d.z, acc);
-  acc = fmaf(w[15], d.w, acc);
-  return acc;
-}
-
-D3_DEV float dot16r(const float (&w)[16], const float* __restrict__ x) {
-  float acc = w[0] * x[0];
+// Stage `cnt` rows of K columns (source row rows[j]) as the MMA's columns, by the eight MMA warps, in work items of
+// (row, 256-column group) spread over the warps. Pass A bounds each row's staged values: the exact max |x| of a
+// plain row; for a rotated row 16 * max over groups of the group's 2-norm (each output of the unscaled butterfly,
+// 16 times a normalized-Hadamard row dotted with the group, is within that). Pass B reloads the values (L2), rotates
+// each group with the reference's butterfly when `rotate` (in the warp's own 256-float scratch; the groups are
+// independent), scales by 2^e so the bound sits in [2^14, 2^15) and converts to f16 (hi, and lo when `two`).
+// Uses named barrier 1 (MMA warps); rowmax[] must be zero on entry.
+D3_DEV void stage_rows(__half* xin, float* inv, int* rowmax, float* wscratch, const void* src, bool bf16,
+                       const int* rows, int cnt, int K, bool rotate, bool two) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int groups = K / 256, items = cnt * groups;
+  for (int it = warp; it < items; it += DEC_WARPS) {
+    const int j = it / groups, q = it - j * groups;
+    float v[8];
+    stage_load(src, bf16, (size_t)rows[j] * K + 256 * q + 8 * lane, v);
+    float m = 0.0f;
+    if (rotate) {
 #pragma unroll
-  for (int j = 1; j < 16; ++j) acc = fmaf(w[j], x[j], acc);
-  return acc;
+      for (int u = 0; u < 8; ++u) m = fmaf(v[u], v[u], m);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m += __shfl_xor_sync(0xffffffffu, m, o);
+      m = 16.0f * sqrtf(m) * 1.001f;
+    } else {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) m = fmaxf(m, fabsf(v[u]));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    }
+    if (lane == 0) atomicMax(rowmax + j, __float_as_int(m));  // non-negative floats order as ints
+  }
+  named_sync(1, DEC_CONSUMERS);
+  const int RH = stage_row_halves(K);
+  for (int it = warp; it < items; it += DEC_WARPS) {
+    const int j = it / groups, q = it - j * groups;
+    float v[8];
+    stage_load(src, bf16, (size_t)rows[j] * K + 256 * q + 8 * lane, v);
+    if (rotate) {
+      float* row = wscratch + warp * 256;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) row[8 * lane + u] = v[u];
+      __syncwarp();
+#pragma unroll
+      for (int stride = 1; stride < 256; stride *= 4) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int tt = lane + 32 * h, low = tt % stride, high = tt / stride;
+          const int i = high * stride * 4 + low;
+          const float va = row[i], vb = row[i + stride], vc = row[i + 2 * stride], vd = row[i + 3 * stride];
+          row[i] = va + vb + vc - vd;
+          row[i + stride] = va + vb - vc + vd;
+          row[i + 2 * stride] = va - vb + vc + vd;
+          row[i + 3 * stride] = -va + vb + vc + vd;
+        }
+        __syncwarp();
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = row[8 * lane + u];
+      __syncwarp();
+    }
+    const int e = stage_exponent(__int_as_float(rowmax[j]));
+    const float scale = __uint_as_float((uint32_t)(e + 127) << 23);
+    __half* hi = xin + (size_t)j * RH + 256 * q + 8 * lane;
+    __half* lo = xin + (size_t)(DEC_MAX_CAP + j) * RH + 256 * q + 8 * lane;
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float s0 = v[2 * u] * scale, s1 = v[2 * u + 1] * scale;
+      const __half h0 = __float2half_rn(s0), h1 = __float2half_rn(s1);
+      hw[u] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+      const __half l0 = __float2half_rn(s0 - __half2float(h0)), l1 = __float2half_rn(s1 - __half2float(h1));
+      lw[u] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+    }
+    *(uint4*)hi = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    if (two) *(uint4*)lo = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    if (q == 0 && lane == 0) inv[j] = (rotate ? 0.0625f : 1.0f) * __uint_as_float((uint32_t)(127 - e) << 23);
+  }
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// K1: gate_up + SwiGLU.
-struct UpArgs {
+// MMA and the A-fragment builders. For a lane (g = lane / 4, c = lane % 4) and a 64-column chunk, the lane owns
+// columns 16c .. 16c + 15 of the chunk; k16-step j of the chunk uses columns 16c + 4j + {0, 1} (A register 0 / 1 of
+// the step: fragment slots 2c, 2c+1) and 16c + 4j + {2, 3} (registers 2 / 3: slots 2c+8, 2c+9). a[2j] holds the
+// first pair of f16 values, a[2j + 1] the second.
+D3_DEV void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+D3_DEV uint32_t pack_h2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// int8 x2 (low bytes of w) -> exact f16 x2: the unsigned byte as the mantissa of 1024 + u, minus 1152.
+D3_DEV uint32_t i8x2_h2(uint32_t w_xor80, uint32_t sel) {
+  const uint32_t m = __byte_perm(w_xor80, 0x64646464u, sel);
+  uint32_t r;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(m), "r"(0x64806480u));  // 1152.0 in both halves
+  return r;
+}
+
+// The 16 columns a lane owns in one weight row, as 8 f16x2 registers. `row` points at the row's bytes,
+// `col` is the first column (64 * kc + 16c); W4/W6 also read the row's group scales `srow` (one e4m3 byte per 16
+// columns) and the codebook `lut`.
+template <int FMT>
+D3_DEV void build_a(const uint8_t* row, const uint8_t* srow, int col, int K, const float* lut, uint32_t (&a)[8]) {
+  if (FMT == FMT_FP8 || FMT == FMT_I8) {
+    const uint4 q = *(const uint4*)(row + col);
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (FMT == FMT_FP8) {
+        a[2 * j] = e4m3x2_h2(w[j] & 0xFFFFu);
+        a[2 * j + 1] = e4m3x2_h2(w[j] >> 16);
+      } else {
+        const uint32_t t = w[j] ^ 0x80808080u;
+        a[2 * j] = i8x2_h2(t, 0x4140);
+        a[2 * j + 1] = i8x2_h2(t, 0x4342);
+      }
+    }
+  } else {
+    const uint2 low = *(const uint2*)(row + col / 2);
+    const uint32_t high = FMT == FMT_W6 ? *(const uint32_t*)(row + K / 2 + col / 4) : 0u;
+    const float s = e4m3_to_f32(srow[col / 16]);
+    float f[16];
+    if (FMT == FMT_W4)
+      dec_w4<16>(low, s, lut, f);
+    else
+      dec_w6<16>(low, high, s, f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a[j] = pack_h2(f[2 * j], f[2 * j + 1]);
+  }
+}
+
+// Activation fragment of column (pair) g for the lane's 16 columns: 8 b32 registers (pairs of halves).
+D3_DEV void load_b(const __half* xrow, int col, uint32_t (&b)[8]) {
+  const uint4 u0 = *(const uint4*)(xrow + col), u1 = *(const uint4*)(xrow + col + 8);
+  b[0] = u0.x;
+  b[1] = u0.y;
+  b[2] = u0.z;
+  b[3] = u0.w;
+  b[4] = u1.x;
+  b[5] = u1.y;
+  b[6] = u1.z;
+  b[7] = u1.w;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+struct DecodeArgs {
   const void* x;  // [M, H]: bf16 when x_bf16, else fp32
   int x_bf16;
-  const int64_t* ids;  // [M, k]
+  const int64_t* ids;    // [M, k]
+  const float* weights;  // [M, k]
   int M, k, E, H, I;
-  const uint8_t* w;      // gate_up rows [E * 2I, row_bytes(H)]
-  const void* scale;     // FP8: float [E*2I/128, H/128]; I8: float [E*2I]; W4/W6: uint8 e4m3 [E*2I, H/16]
-  const float* channel;  // W4/W6: s_channel [E*2I]
-  const float* codebook; // W4: [16]
-  float* a1;             // [M*k, I]
-  int stages;
+  const uint8_t* w13;  // gate_up rows [E * 2I, row_bytes(H)]
+  const void* s13;     // FP8: float [E*2I/128, H/128]; I8: float [E*2I]; W4/W6: uint8 e4m3 [E*2I, H/16]
+  const float* c13;    // W4/W6: s_channel [E*2I]
+  const float* cb13;   // W4: codebook [16]
+  const uint8_t* w2;   // down rows [E * H, row_bytes(I)]
+  const void* s2;
+  const float* c2;
+  const float* cb2;
+  uint16_t* out;                // [M, H] bf16
+  float* a1;                    // scratch [M*k, I]
+  float* parts;                 // scratch [M*k, H]
+  unsigned long long* barrier;  // scratch: zero before the first call; grows by 2 * gridDim.x per call
+  int stages, stage_bytes, cap;
 };
 
-// Rows of one K1 chunk: RPW pair-rows per consumer warp.
-template <int FMT, int RPW>
-struct UpGeom {
-  static constexpr int CH = DEC_WARPS * RPW;  // pair-rows per chunk
+// Warp roles: DEC_WARPS MMA warps, then the epilogue warp (reductions and stores), then the producer warp.
+constexpr int DEC_EPI = DEC_WARPS, DEC_PROD = DEC_WARPS + 1;
+constexpr int DEC_ALL = DEC_THREADS;
+constexpr int DEC_RED = 4;  // partial-sum slots between the MMA warps and the epilogue warp
+
+// One chunk's partial sums (per MMA warp and lane) and what the epilogue needs to finish it.
+struct RedSlot {
+  float4 part[DEC_WARPS * 32];
+  int pair[DEC_MAX_CAP];
+  float inv[DEC_MAX_CAP];
+  int r, cn, cnt, e;
 };
 
-template <int FMT, int CAP, int NV>
-__global__ void __launch_bounds__(DEC_THREADS, 1) moe_up_kernel(const UpArgs a) {
-  constexpr int RPW = CAP == 1 ? 1 : 2;
-  constexpr int CH = DEC_WARPS * RPW;
-  const int H = NV * 512, I = a.I, P = a.M * a.k;
-  const int rb = fmt_row_bytes(FMT, H);  // bytes per weight row
-  const int gb = H / 16;                  // group-scale bytes per row (codes)
-  const int stage_bytes = 2 * CH * rb + (fmt_codes(FMT) ? 2 * CH * gb : 0);
-  const int NS = a.stages;
+// Shared-memory layout of the decode kernel (dynamic part), shared with the host launcher.
+struct DecodeSmem {
+  int scratch, in, inv, rowmax, table, red, ring, total;
+};
+
+template <int FMT, bool XBF>
+__host__ __device__ inline DecodeSmem decode_smem(int H, int I, int stages, int stage_bytes) {
+  DecodeSmem s{};
+  s.scratch = 0;
+  const int scratch_bytes = fmt_rotated(FMT) ? DEC_WARPS * 256 * 4 : 0;
+  s.in = scratch_bytes;
+  // phase 1: hi (and lo unless bf16 rows of an fp8 bank) blocks of 8 rows of H; phase 2: hi and lo of I
+  const int terms1 = (FMT == FMT_FP8 && XBF) ? 1 : 2;
+  const int in1 = terms1 * DEC_MAX_CAP * stage_row_halves(H) * 2, in2 = 2 * DEC_MAX_CAP * stage_row_halves(I) * 2;
+  s.inv = s.in + (in1 > in2 ? in1 : in2);
+  s.rowmax = s.inv + 4 * DEC_MAX_CAP;
+  s.table = s.rowmax + 4 * DEC_MAX_CAP;
+  const int t = FMT == FMT_FP8 ? (2 * I / 128) * (H / 128) : 0;  // >= (H/128)(I/128)
+  s.red = s.table + ((4 * t + 15) / 16) * 16;
+  s.ring = s.red + DEC_RED * (int)sizeof(RedSlot);
+  s.ring = (s.ring + 127) / 128 * 128;
+  s.total = s.ring + stages * stage_bytes;
+  return s;
+}
+
+// Bytes of one ring stage: a phase-1 chunk (8 gate rows, 8 up rows, and their group scales) or a phase-2 chunk.
+template <int FMT>
+__host__ __device__ constexpr int decode_stage_bytes(int H, int I) {
+  return (2 * DEC_CH1 * (fmt_row_bytes(FMT, H) + (fmt_codes(FMT) ? H / 16 : 0))) >
+                 (DEC_CH2 * (fmt_row_bytes(FMT, I) + (fmt_codes(FMT) ? I / 16 : 0)))
+             ? 2 * DEC_CH1 * (fmt_row_bytes(FMT, H) + (fmt_codes(FMT) ? H / 16 : 0))
+             : DEC_CH2 * (fmt_row_bytes(FMT, I) + (fmt_codes(FMT) ? I / 16 : 0));
+}
+
+// The contiguous range [lo, hi) of `total` work items owned by CTA `b` of `g`.
+D3_DEV void split_range(int total, int b, int g, int& lo, int& hi) {
+  lo = (int)((long long)b * total / g);
+  hi = (int)((long long)(b + 1) * total / g);
+}
+
+// Grid-wide barrier of one CTA per SM, taken by the MMA warps and the epilogue warp (named barrier 2), by tickets on
+// a 64-bit counter that starts at zero and only grows: a round completes when the counter reaches the round's end.
+// Bounded: after WAIT_LIMIT_NS the fault word is set and false returned.
+D3_DEV bool grid_barrier(unsigned long long* counter, unsigned nblocks) {
+  __shared__ int passed;
+  named_sync(2, DEC_CONSUMERS + 32);
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned long long ticket = atomicAdd(counter, 1ull);
+    const unsigned long long target = (ticket / nblocks + 1) * nblocks;
+    int ok = 1;
+    unsigned long long seen;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(seen) : "l"(counter) : "memory");
+    if (seen < target) {
+      const unsigned long long start = globaltimer();
+      while (true) {
+        asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(seen) : "l"(counter) : "memory");
+        if (seen >= target) break;
+        if (globaltimer() - start > WAIT_LIMIT_NS) {
+          record_fault(FAULT_WAIT_TIMEOUT);
+          ok = 0;
+          break;
+        }
+      }
+    }
+    passed = ok;
+  }
+  named_sync(2, DEC_CONSUMERS + 32);
+  return passed != 0;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// The activation fragments a warp uses for every chunk of a segment (its k range is the same in each): phase 1 the
+// four 64-column chunks kc = warp + 8m, phase 2 the NKC chunks kc = warp % 4 + 4m. Loaded once per segment.
+constexpr int P1_KC = DEC_H / 64 / DEC_WARPS;
+
+template <bool TWO>
+D3_DEV void load_b1(const __half* xin, uint32_t (&bh)[P1_KC][8], uint32_t (&bl)[TWO ? P1_KC : 1][8]) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, c = lane & 3;
+  const __half* xh = xin + (size_t)g * stage_row_halves(DEC_H);
+  const __half* xl = xin + (size_t)(DEC_MAX_CAP + g) * stage_row_halves(DEC_H);
+#pragma unroll
+  for (int m = 0; m < P1_KC; ++m) {
+    const int col = 64 * (warp + DEC_WARPS * m) + 16 * c;
+    load_b(xh, col, bh[m]);
+    if (TWO) load_b(xl, col, bl[m]);
+  }
+}
+
+template <int NKC>
+D3_DEV void load_b2(const __half* xin, int I, uint32_t (&bh)[NKC][8], uint32_t (&bl)[NKC][8]) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, c = lane & 3;
+  const __half* xh = xin + (size_t)g * stage_row_halves(I);
+  const __half* xl = xin + (size_t)(DEC_MAX_CAP + g) * stage_row_halves(I);
+#pragma unroll
+  for (int m = 0; m < NKC; ++m) {
+    const int col = 64 * ((warp & 3) + 4 * m) + 16 * c;
+    load_b(xh, col, bh[m]);
+    load_b(xl, col, bl[m]);
+  }
+}
+
+// Phase 1, one chunk, one MMA warp: the warp's four 64-column chunks of the 16-row tile (rows 0-7: gate rows i0..,
+// rows 8-15: up rows i0..) against the segment's activation fragments.
+template <int FMT, bool TWO>
+D3_DEV float4 p1_chunk(const DecodeArgs& a, const uint8_t* stage, int i0, const uint32_t (&bh)[P1_KC][8],
+                       const uint32_t (&bl)[TWO ? P1_KC : 1][8], const float* table, const float* lut) {
+  constexpr int H = DEC_H;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, c = lane & 3;
+  const int I = a.I, rb = fmt_row_bytes(FMT, H), gb = H / 16;
+  const uint8_t* grow = stage + g * rb;
+  const uint8_t* urow = stage + (DEC_CH1 + g) * rb;
+  const uint8_t* gsrow = stage + 2 * DEC_CH1 * rb + g * gb;
+  const uint8_t* usrow = stage + 2 * DEC_CH1 * rb + (DEC_CH1 + g) * gb;
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+  for (int m = 0; m < P1_KC; ++m) {
+    const int kc = warp + DEC_WARPS * m, col = 64 * kc + 16 * c;
+    uint32_t ga[8], ua[8];
+    build_a<FMT>(grow, gsrow, col, H, lut, ga);
+    build_a<FMT>(urow, usrow, col, H, lut, ua);
+    float t0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, t1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float(&t)[4] = (j & 1) ? t1 : t0;  // two independent accumulation chains
+      mma16816(t, ga[2 * j], ua[2 * j], ga[2 * j + 1], ua[2 * j + 1], bh[m][2 * j], bh[m][2 * j + 1]);
+      if (TWO) mma16816(t, ga[2 * j], ua[2 * j], ga[2 * j + 1], ua[2 * j + 1], bl[m][2 * j], bl[m][2 * j + 1]);
+    }
+    if (FMT == FMT_FP8) {
+      // 128 x 128 block scales of rows (gate i0 + g, up I + i0 + g) and this chunk's columns (rows past a partial
+      // tile are stale and discarded; their block index is clamped into the table)
+      const float sg = table[min((i0 + g) / 128, 2 * I / 128 - 1) * (H / 128) + kc / 2];
+      const float su = table[min((I + i0 + g) / 128, 2 * I / 128 - 1) * (H / 128) + kc / 2];
+      acc[0] = fmaf(t0[0] + t1[0], sg, acc[0]);
+      acc[1] = fmaf(t0[1] + t1[1], sg, acc[1]);
+      acc[2] = fmaf(t0[2] + t1[2], su, acc[2]);
+      acc[3] = fmaf(t0[3] + t1[3], su, acc[3]);
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[q] += t0[q] + t1[q];
+    }
+  }
+  return make_float4(acc[0], acc[1], acc[2], acc[3]);
+}
+
+// Phase 2, one chunk, one MMA warp: tile warp / 4 (rows 16 * tile .. of the chunk), 64-column chunks kc = warp % 4 + 4m.
+template <int FMT, int NKC>
+D3_DEV float4 p2_chunk(const DecodeArgs& a, const uint8_t* stage, int n0, const uint32_t (&bh)[NKC][8],
+                       const uint32_t (&bl)[NKC][8], const float* table, const float* lut) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, c = lane & 3;
+  const int H = DEC_H, I = a.I, rb = fmt_row_bytes(FMT, I), gb = I / 16;
+  const int tile = warp >> 2, r_lo = 16 * tile + g, r_hi = r_lo + 8;
+  const uint8_t* lrow = stage + r_lo * rb;
+  const uint8_t* hrow = stage + r_hi * rb;
+  const uint8_t* lsrow = stage + DEC_CH2 * rb + r_lo * gb;
+  const uint8_t* hsrow = stage + DEC_CH2 * rb + r_hi * gb;
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+  for (int m = 0; m < NKC; ++m) {
+    const int kc = (warp & 3) + 4 * m, col = 64 * kc + 16 * c;
+    uint32_t la[8], ha[8];
+    build_a<FMT>(lrow, lsrow, col, I, lut, la);
+    build_a<FMT>(hrow, hsrow, col, I, lut, ha);
+    float t0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, t1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      mma16816(t0, la[2 * j], ha[2 * j], la[2 * j + 1], ha[2 * j + 1], bh[m][2 * j], bh[m][2 * j + 1]);
+      mma16816(t1, la[2 * j], ha[2 * j], la[2 * j + 1], ha[2 * j + 1], bl[m][2 * j], bl[m][2 * j + 1]);
+    }
+    if (FMT == FMT_FP8) {
+      const float sl = table[min((n0 + r_lo) / 128, H / 128 - 1) * (I / 128) + kc / 2];
+      const float sh = table[min((n0 + r_hi) / 128, H / 128 - 1) * (I / 128) + kc / 2];
+      acc[0] = fmaf(t0[0] + t1[0], sl, acc[0]);
+      acc[1] = fmaf(t0[1] + t1[1], sl, acc[1]);
+      acc[2] = fmaf(t0[2] + t1[2], sh, acc[2]);
+      acc[3] = fmaf(t0[3] + t1[3], sh, acc[3]);
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[q] += t0[q] + t1[q];
+    }
+  }
+  return make_float4(acc[0], acc[1], acc[2], acc[3]);
+}
+
+D3_DEV float f4get(const float4& v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
+
+// ---------------------------------------------------------------------------------------------------------------
+// The MMA warps' work for one phase: every chunk of the CTA's range [lo, hi) in order; the segment's activation
+// fragments are staged and loaded at each segment change; each chunk's partial sums go to the epilogue warp through
+// the RedSlot ring. `c` counts chunks across both phases (ring positions). Returns false after a failed wait.
+template <int FMT, bool XBF, int NKC, int PHASE>
+D3_DEV bool mma_phase(const DecodeArgs& a, const DecodePlan& pl, int lo, int hi, int& c, bool ok, uint8_t* ring,
+                      uint64_t* full_bar, uint64_t* empty_bar, uint64_t* rfull, uint64_t* rempty, RedSlot* red,
+                      __half* xin, float* inv, int* rowmax, float* wscratch, float* table, const float* lut,
+                      int* pair_in, int* rows_in) {
+  constexpr bool ROT = fmt_rotated(FMT);
+  constexpr bool TWO1 = !(FMT == FMT_FP8 && XBF);
+  constexpr int KC = PHASE == 1 ? P1_KC : NKC;
+  constexpr bool TWO = PHASE == 1 ? TWO1 : true;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int H = DEC_H, I = a.I, NS = a.stages, SB = a.stage_bytes;
+  const int per = PHASE == 1 ? I : H, ch = PHASE == 1 ? DEC_CH1 : DEC_CH2;
+  uint32_t bh[KC][8], bl[TWO ? KC : 1][8];
+  int cur = -1, cnt = 0, e = 0;
+  for (int q = lo; q < hi; ++c) {
+    const int s = q / per, r = q - s * per, cn = min(ch, min(per - r, hi - q));
+    if (s != cur) {
+      // a new segment: stage its pairs' rows (x in phase 1, a1 in phase 2) once all warps left the last one
+      named_sync(1, DEC_CONSUMERS);
+      cur = s;
+      cnt = pl.seg_count[s];
+      e = pl.seg_expert[s];
+      const int first = pl.seg_first[s];
+      if (tid < cnt) {
+        pair_in[tid] = pl.sorted[first + tid];
+        rows_in[tid] = PHASE == 1 ? pl.sorted[first + tid] / a.k : pl.sorted[first + tid];
+        rowmax[tid] = 0;
+      }
+      if (FMT == FMT_FP8) {
+        const int n = PHASE == 1 ? (2 * I / 128) * (H / 128) : (H / 128) * (I / 128);
+        const float* src = (const float*)(PHASE == 1 ? a.s13 : a.s2) + (size_t)e * n;
+        for (int t = tid; t < n; t += DEC_CONSUMERS) table[t] = src[t];
+      }
+      named_sync(1, DEC_CONSUMERS);
+#ifdef D3_TRACE
+      const unsigned long long ts0 = globaltimer();
+#endif
+      // a1 holds SwiGLU outputs; ConvRot formats rotate them, as the reference's rotate(swiglu=True) does
+      if (PHASE == 1)
+        stage_rows(xin, inv, rowmax, wscratch, a.x, a.x_bf16 != 0, rows_in, cnt, H, ROT, TWO1);
+      else
+        stage_rows(xin, inv, rowmax, wscratch, a.a1, false, rows_in, cnt, I, ROT, true);
+      named_sync(1, DEC_CONSUMERS);
+      if (PHASE == 1)
+        load_b1<TWO1>(xin, (uint32_t(&)[P1_KC][8])bh, (uint32_t(&)[TWO1 ? P1_KC : 1][8])bl);
+      else
+        load_b2<NKC>(xin, I, (uint32_t(&)[NKC][8])bh, (uint32_t(&)[NKC][8])bl);
+#ifdef D3_TRACE
+      D3_ADD(PHASE == 1 ? 8 : 10, globaltimer() - ts0);
+      D3_ADD(PHASE == 1 ? 12 : 14, 1);
+#endif
+    }
+    const int st = c % NS;
+#ifdef D3_TRACE
+    const unsigned long long tw0 = globaltimer();
+#endif
+    if (ok) ok = mbar_wait(&full_bar[st], (c / NS) & 1);
+#ifdef D3_TRACE
+    D3_ADD(PHASE == 1 ? 9 : 11, globaltimer() - tw0);
+    if (c == 0) D3_STAMP(13);
+    const unsigned long long tc0 = globaltimer();
+#endif
+    float4 part = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (ok) {
+      if (PHASE == 1)
+        part = p1_chunk<FMT, TWO1>(a, ring + (size_t)st * SB, r, (const uint32_t(&)[P1_KC][8])bh,
+                                   (const uint32_t(&)[TWO1 ? P1_KC : 1][8])bl, table, lut);
+      else
+        part = p2_chunk<FMT, NKC>(a, ring + (size_t)st * SB, r, (const uint32_t(&)[NKC][8])bh,
+                                  (const uint32_t(&)[NKC][8])bl, table, lut);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[st]);
+    const int slot = c % DEC_RED;
+#ifdef D3_TRACE
+    const unsigned long long tc1 = globaltimer();
+    D3_ADD(16, tc1 - tc0);
+#endif
+    if (c >= DEC_RED && ok) ok = mbar_wait(&rempty[slot], ((c / DEC_RED) - 1) & 1);
+#ifdef D3_TRACE
+    D3_ADD(15, globaltimer() - tc1);
+#endif
+    RedSlot& rs = red[slot];
+    rs.part[warp * 32 + lane] = part;
+    if (warp == 0) {
+      if (lane < DEC_MAX_CAP) {
+        rs.pair[lane] = pair_in[lane];
+        rs.inv[lane] = inv[lane];
+      }
+      if (lane == 0) {
+        rs.r = r;
+        rs.cn = cn;
+        rs.cnt = cnt;
+        rs.e = e;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&rfull[slot]);
+    q += cn;
+  }
+  return ok;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+template <int FMT, bool XBF, int NKC>
+__global__ void __launch_bounds__(DEC_ALL, 1) moe_decode_kernel(const DecodeArgs a) {
+  constexpr bool ROT = fmt_rotated(FMT);
+  constexpr bool TWO1 = !(FMT == FMT_FP8 && XBF);  // phase-1 activations need the lo term
+  const int H = DEC_H, I = a.I, P = a.M * a.k, NS = a.stages, SB = a.stage_bytes;
+  const int rb1 = fmt_row_bytes(FMT, H), gb1 = H / 16, rb2 = fmt_row_bytes(FMT, I), gb2 = I / 16;
 
   __shared__ DecodePlan pl;
   __shared__ __align__(8) uint64_t full_bar[DEC_MAX_STAGES], empty_bar[DEC_MAX_STAGES];
-  __shared__ float lut[16];
+  __shared__ __align__(8) uint64_t rfull[DEC_RED], rempty[DEC_RED];
+  __shared__ float lut1[16], lut2[16];
+  __shared__ int rows_in[DEC_MAX_CAP], pair_in[DEC_MAX_CAP];
   extern __shared__ __align__(128) uint8_t smem[];
-  float* xs = (float*)smem;                                   // CAP rows of H floats (swizzled)
-  float* sc = xs + CAP * H;                                   // FP8: the expert's gate_up block scales
-  const int sc_floats = FMT == FMT_FP8 ? ((2 * I / 128) * (H / 128) + 3) & ~3 : 0;
-  uint8_t* stages = (uint8_t*)(sc + sc_floats);
+  const DecodeSmem L = decode_smem<FMT, XBF>(H, I, NS, SB);
+  float* wscratch = (float*)(smem + L.scratch);
+  __half* xin = (__half*)(smem + L.in);
+  float* inv = (float*)(smem + L.inv);
+  int* rowmax = (int*)(smem + L.rowmax);
+  float* table = (float*)(smem + L.table);
+  RedSlot* red = (RedSlot*)(smem + L.red);
+  uint8_t* ring = smem + L.ring;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+#ifdef D3_TRACE
+  if (tid == 0 && blockIdx.x < 1024)
+    for (int t = 0; t < 24; ++t) g_trace[blockIdx.x][t] = 0;
+#endif
+  D3_STAMP(0);
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], DEC_WARPS);
     }
+    for (int s = 0; s < DEC_RED; ++s) {
+      mbar_init(&rfull[s], DEC_WARPS);
+      mbar_init(&rempty[s], 1);
+    }
     fence_mbar_init();
   }
-  if (FMT == FMT_W4 && tid < 16) lut[tid] = a.codebook[tid];
-  // the down kernel may start its prologue (and its weight copies) now
-  allow_dependents();
-  build_plan(pl, a.ids, P, a.E, CAP);
+  if (FMT == FMT_W4 && tid < 16) {
+    lut1[tid] = a.cb13[tid];
+    lut2[tid] = a.cb2[tid];
+  }
+  build_plan(pl, a.ids, P, a.E, a.cap);
+  D3_STAMP(1);
+  const int nseg = pl.nseg, G = gridDim.x;
+  int lo1, hi1, lo2, hi2;
+  split_range(nseg * I, blockIdx.x, G, lo1, hi1);
+  split_range(nseg * H, blockIdx.x, G, lo2, hi2);
 
-  const int total = pl.nseg * I;  // pair-rows in this pass
-  const int G = gridDim.x;
-  const int r0 = (int)((long long)blockIdx.x * total / G), r1 = (int)((long long)(blockIdx.x + 1) * total / G);
-
-  if (warp == DEC_WARPS) {
-    // ---------------- producer ----------------
+  if (warp == DEC_PROD) {
+    // ---------------- producer: phase-1 chunks, then phase-2 chunks, through one ring ----------------
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
       int c = 0;
-      for (int q = r0; q < r1; ++c) {
-        const int s = q / I, i0 = q - s * I, cn = min(CH, min(I - i0, r1 - q));
-        const int st = c % NS;
-        if (c >= NS && !mbar_wait(&empty_bar[st], ((c / NS) - 1) & 1)) break;
-        const int e = pl.seg_expert[s];
-        uint8_t* dst = stages + (size_t)st * stage_bytes;
-        const uint8_t* gate = a.w + ((size_t)e * 2 * I + i0) * rb;
-        const uint8_t* up = a.w + ((size_t)e * 2 * I + I + i0) * rb;
-        uint32_t bytes = 2u * cn * rb;
-        if (fmt_codes(FMT)) bytes += 2u * cn * gb;
-        mbar_arrive_expect_tx(&full_bar[st], bytes);
-        bulk_g2s(dst, gate, cn * rb, &full_bar[st], pol);
-        bulk_g2s(dst + CH * rb, up, cn * rb, &full_bar[st], pol);
-        if (fmt_codes(FMT)) {
-          const uint8_t* gs = (const uint8_t*)a.scale + ((size_t)e * 2 * I + i0) * gb;
-          const uint8_t* us = (const uint8_t*)a.scale + ((size_t)e * 2 * I + I + i0) * gb;
-          bulk_g2s(dst + 2 * CH * rb, gs, cn * gb, &full_bar[st], pol);
-          bulk_g2s(dst + 2 * CH * rb + CH * gb, us, cn * gb, &full_bar[st], pol);
+      bool ok = true;
+      for (int phase = 1; phase <= 2 && ok; ++phase) {
+        const int lo = phase == 1 ? lo1 : lo2, hi = phase == 1 ? hi1 : hi2, per = phase == 1 ? I : H;
+        const int ch = phase == 1 ? DEC_CH1 : DEC_CH2;
+        for (int q = lo; q < hi; ++c) {
+          const int s = q / per, r = q - s * per, cn = min(ch, min(per - r, hi - q));
+          const int st = c % NS;
+          if (c >= NS && !mbar_wait(&empty_bar[st], ((c / NS) - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          const int e = pl.seg_expert[s];
+          uint8_t* dst = ring + (size_t)st * SB;
+          if (phase == 1) {
+            const size_t g0 = (size_t)e * 2 * I + r, u0 = g0 + I;
+            const uint32_t bytes = 2u * cn * rb1 + (fmt_codes(FMT) ? 2u * cn * gb1 : 0u);
+            mbar_arrive_expect_tx(&full_bar[st], bytes);
+            bulk_g2s(dst, a.w13 + g0 * rb1, cn * rb1, &full_bar[st], pol);
+            bulk_g2s(dst + DEC_CH1 * rb1, a.w13 + u0 * rb1, cn * rb1, &full_bar[st], pol);
+            if (fmt_codes(FMT)) {
+              const uint8_t* sc = (const uint8_t*)a.s13;
+              bulk_g2s(dst + 2 * DEC_CH1 * rb1, sc + g0 * gb1, cn * gb1, &full_bar[st], pol);
+              bulk_g2s(dst + 2 * DEC_CH1 * rb1 + DEC_CH1 * gb1, sc + u0 * gb1, cn * gb1, &full_bar[st], pol);
+            }
+          } else {
+            const size_t n0 = (size_t)e * H + r;
+            const uint32_t bytes = cn * rb2 + (fmt_codes(FMT) ? cn * gb2 : 0);
+            mbar_arrive_expect_tx(&full_bar[st], bytes);
+            bulk_g2s(dst, a.w2 + n0 * rb2, cn * rb2, &full_bar[st], pol);
+            if (fmt_codes(FMT))
+              bulk_g2s(dst + DEC_CH2 * rb2, (const uint8_t*)a.s2 + n0 * gb2, cn * gb2, &full_bar[st], pol);
+          }
+          q += cn;
         }
-        q += cn;
       }
       // every issued copy lands before this thread leaves (bounded)
       for (int d = max(0, c - NS); d < c; ++d)
@@ -270,342 +732,124 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) moe_up_kernel(const UpArgs a) 
     return;
   }
 
-  // ---------------- consumers ----------------
-  // A failed (timed-out) wait clears `ok`: the warp then skips its work but still takes part in every named
-  // barrier, so no other warp is left waiting on it.
   bool ok = true;
-  float xr[CAP == 1 ? NV * 16 : 1];
-  int cur = -1, cnt = 0, first = 0, expert = 0;
-  int c = 0;
-  for (int q = r0; q < r1; ++c) {
-    const int s = q / I, i0 = q - s * I, cn = min(CH, min(I - i0, r1 - q));
-    if (s != cur) {
-      // stage this segment's input rows (and scales)
-      named_sync(1, DEC_WARPS * 32);
-      cur = s;
-      cnt = pl.seg_count[s];
-      first = pl.seg_first[s];
-      expert = pl.seg_expert[s];
-      for (int j = 0; j < cnt; ++j) {
-        const int t = pl.sorted[first + j] / a.k;
-        float4* dst = (float4*)(xs + j * H);
-        for (int f = tid; f < H / 4; f += DEC_WARPS * 32) {
-          float4 v;
-          if (a.x_bf16) {
-            uint2 b = ((const uint2*)((const uint16_t*)a.x + (size_t)t * H))[f];
-            v = make_float4(bf16_to_f32(b.x & 0xFFFFu), bf16_to_f32(b.x >> 16), bf16_to_f32(b.y & 0xFFFFu),
-                            bf16_to_f32(b.y >> 16));
-          } else {
-            v = ((const float4*)((const float*)a.x + (size_t)t * H))[f];
+  if (warp == DEC_EPI) {
+    // ---------------- epilogue: reduce each chunk's partial sums, scale, store ----------------
+    int c = 0;
+    for (int phase = 1; phase <= 2; ++phase) {
+      if (phase == 2) ok = grid_barrier(a.barrier, G) && ok;
+      const int lo = phase == 1 ? lo1 : lo2, hi = phase == 1 ? hi1 : hi2, per = phase == 1 ? I : H;
+      const int ch = phase == 1 ? DEC_CH1 : DEC_CH2;
+      for (int q = lo; q < hi; ++c) {
+        const int s = q / per, r = q - s * per, cn = min(ch, min(per - r, hi - q));
+        const int slot = c % DEC_RED;
+#ifdef D3_TRACE
+        const unsigned long long te0 = globaltimer();
+#endif
+        if (ok) ok = mbar_wait(&rfull[slot], (c / DEC_RED) & 1);
+#ifdef D3_TRACE
+        const unsigned long long te1 = globaltimer();
+        D3_ADD_EPI(17, te1 - te0);
+#endif
+        const RedSlot& rs = red[slot];
+        const int cnt = rs.cnt, e = rs.e;
+        // lane L finishes what lane L of the MMA warps holds: rows g, g + 8 of the tile x pairs 2c, 2c + 1
+        const int g = lane >> 2, n0 = 2 * (lane & 3), n1 = n0 + 1;
+        if (ok && phase == 1) {
+          float4 sum = rs.part[lane];
+#pragma unroll
+          for (int w = 1; w < DEC_WARPS; ++w) {
+            const float4 v = rs.part[w * 32 + lane];
+            sum.x += v.x;
+            sum.y += v.y;
+            sum.z += v.z;
+            sum.w += v.w;
           }
-          dst[xswz(f)] = v;
-        }
-      }
-      if (FMT == FMT_FP8) {
-        const int n = (2 * I / 128) * (H / 128);
-        const float* src = (const float*)a.scale + (size_t)expert * n;
-        for (int i = tid; i < n; i += DEC_WARPS * 32) sc[i] = src[i];
-      }
-      named_sync(1, DEC_WARPS * 32);
-      if (fmt_rotated(FMT)) {
-        for (int j = 0; j < cnt; ++j) {
-          float* row = xs + j * H;
-          for (int stride = 1; stride < 256; stride *= 4) {
-            for (int t = tid; t < H / 4; t += DEC_WARPS * 32) {
-              int within = t & 63, low = within % stride, high = within / stride;
-              int i = (t >> 6) * 256 + high * stride * 4 + low;
-              float* pa = row + xswz_elem(i);
-              float* pb = row + xswz_elem(i + stride);
-              float* pc = row + xswz_elem(i + 2 * stride);
-              float* pd = row + xswz_elem(i + 3 * stride);
-              float va = *pa, vb = *pb, vc = *pc, vd = *pd;
-              *pa = va + vb + vc - vd;
-              *pb = va + vb - vc + vd;
-              *pc = va - vb + vc + vd;
-              *pd = -va + vb + vc + vd;
+          // x, y: gate row g for pairs n0, n1; z, w: up row g
+          if (g < cn) {
+            const int i = r + g;
+            float gsc = 1.0f, usc = 1.0f;
+            if (FMT == FMT_I8) {
+              gsc = __ldg((const float*)a.s13 + (size_t)e * 2 * I + i);
+              usc = __ldg((const float*)a.s13 + (size_t)e * 2 * I + I + i);
+            } else if (fmt_codes(FMT)) {
+              gsc = __ldg(a.c13 + (size_t)e * 2 * I + i);
+              usc = __ldg(a.c13 + (size_t)e * 2 * I + I + i);
             }
-            named_sync(1, DEC_WARPS * 32);
-          }
-        }
-      }
-      if (CAP == 1) {
-#pragma unroll
-        for (int j = 0; j < NV; ++j) {
-          const int v = lane + 32 * j;
-          const float4* xrow = (const float4*)xs;
-#pragma unroll
-          for (int qq = 0; qq < 4; ++qq) {
-            float4 t = xrow[xswz(4 * v + qq)];
-            xr[16 * j + 4 * qq + 0] = t.x;
-            xr[16 * j + 4 * qq + 1] = t.y;
-            xr[16 * j + 4 * qq + 2] = t.z;
-            xr[16 * j + 4 * qq + 3] = t.w;
-          }
-        }
-      }
-    }
-    const int st = c % NS;
-    if (ok) ok = mbar_wait(&full_bar[st], (c / NS) & 1);
-    const uint8_t* stage = stages + (size_t)st * stage_bytes;
-#pragma unroll
-    for (int rr = 0; rr < RPW; ++rr) {
-      const int ws = warp * RPW + rr;
-      if (ok && ws < cn) {
-        const int i = i0 + ws;
-        const uint8_t* grow = stage + ws * rb;
-        const uint8_t* urow = stage + (CH + ws) * rb;
-        float ag[CAP], au[CAP];
-#pragma unroll
-        for (int j = 0; j < CAP; ++j) ag[j] = au[j] = 0.0f;
-#pragma unroll
-        for (int j = 0; j < NV; ++j) {
-          const int v = lane + 32 * j;  // 16-column group
-          float fg[16], fu[16];
-          float sg = 1.0f, su = 1.0f;
-          if (FMT == FMT_FP8) {
-            dec16_fp8(*(const uint4*)(grow + 16 * v), fg);
-            dec16_fp8(*(const uint4*)(urow + 16 * v), fu);
-            sg = sc[(i / 128) * (H / 128) + v / 8];
-            su = sc[((I + i) / 128) * (H / 128) + v / 8];
-          } else if (FMT == FMT_I8) {
-            dec16_i8(*(const uint4*)(grow + 16 * v), fg);
-            dec16_i8(*(const uint4*)(urow + 16 * v), fu);
-          } else {
-            const uint8_t* gsr = stage + 2 * CH * rb + ws * gb;
-            const uint8_t* usr = stage + 2 * CH * rb + (CH + ws) * gb;
-            const float gs = e4m3_to_f32(gsr[v]), us = e4m3_to_f32(usr[v]);
-            if (FMT == FMT_W4) {
-              dec_w4<16>(*(const uint2*)(grow + 8 * v), gs, lut, fg);
-              dec_w4<16>(*(const uint2*)(urow + 8 * v), us, lut, fu);
-            } else {
-              dec_w6<16>(*(const uint2*)(grow + 8 * v), *(const uint32_t*)(grow + H / 2 + 4 * v), gs, fg);
-              dec_w6<16>(*(const uint2*)(urow + 8 * v), *(const uint32_t*)(urow + H / 2 + 4 * v), us, fu);
+            if (n0 < cnt) {
+              const float s0 = rs.inv[n0];
+              a.a1[(size_t)rs.pair[n0] * I + i] = swiglu_fast(sum.x * (gsc * s0), sum.z * (usc * s0));
+            }
+            if (n1 < cnt) {
+              const float s1 = rs.inv[n1];
+              a.a1[(size_t)rs.pair[n1] * I + i] = swiglu_fast(sum.y * (gsc * s1), sum.w * (usc * s1));
             }
           }
+        } else if (ok) {
 #pragma unroll
-          for (int jj = 0; jj < CAP; ++jj) {
-            if (jj < cnt) {
-              float pg, pu;
-              if (CAP == 1) {
-                pg = dot16r(fg, xr + 16 * j);
-                pu = dot16r(fu, xr + 16 * j);
-              } else {
-                const float4* xrow = (const float4*)(xs + jj * H);
-                const float4 *x0 = xrow + xswz(4 * v), *x1 = xrow + xswz(4 * v + 1), *x2 = xrow + xswz(4 * v + 2),
-                             *x3 = xrow + xswz(4 * v + 3);
-                pg = dot16(fg, x0, x1, x2, x3);
-                pu = dot16(fu, x0, x1, x2, x3);
+          for (int t = 0; t < 2; ++t) {
+            float4 sum = rs.part[(4 * t) * 32 + lane];
+#pragma unroll
+            for (int w = 1; w < 4; ++w) {
+              const float4 v = rs.part[(4 * t + w) * 32 + lane];
+              sum.x += v.x;
+              sum.y += v.y;
+              sum.z += v.z;
+              sum.w += v.w;
+            }
+            // x, y: row 16t + g for pairs n0, n1; z, w: row 16t + g + 8
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+              const int row = 16 * t + g + 8 * half;
+              if (row < cn) {
+                const int nrow = r + row;
+                float sc = 1.0f;
+                if (FMT == FMT_I8) sc = __ldg((const float*)a.s2 + (size_t)e * H + nrow);
+                if (fmt_codes(FMT)) sc = __ldg(a.c2 + (size_t)e * H + nrow);
+                const float v0 = half ? sum.z : sum.x, v1 = half ? sum.w : sum.y;
+                if (n0 < cnt) a.parts[(size_t)rs.pair[n0] * H + nrow] = v0 * (sc * rs.inv[n0]);
+                if (n1 < cnt) a.parts[(size_t)rs.pair[n1] * H + nrow] = v1 * (sc * rs.inv[n1]);
               }
-              ag[jj] = fmaf(pg, sg, ag[jj]);
-              au[jj] = fmaf(pu, su, au[jj]);
             }
           }
         }
-        float gscale = 1.0f, uscale = 1.0f;
-        if (FMT == FMT_I8) {
-          // row scales, and the rotation's 1/16 folded in (exact: a power of two)
-          gscale = 0.0625f * __ldg((const float*)a.scale + (size_t)expert * 2 * I + i);
-          uscale = 0.0625f * __ldg((const float*)a.scale + (size_t)expert * 2 * I + I + i);
-        } else if (fmt_codes(FMT)) {
-          gscale = 0.0625f * __ldg(a.channel + (size_t)expert * 2 * I + i);
-          uscale = 0.0625f * __ldg(a.channel + (size_t)expert * 2 * I + I + i);
-        }
-#pragma unroll
-        for (int jj = 0; jj < CAP; ++jj) {
-          if (jj < cnt) {
-            float g = warp_sum(ag[jj]) * gscale, u = warp_sum(au[jj]) * uscale;
-            if (lane == 0) a.a1[(size_t)pl.sorted[first + jj] * I + i] = swiglu_fast(g, u);
-          }
-        }
+#ifdef D3_TRACE
+        D3_ADD_EPI(19, globaltimer() - te1);
+#endif
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&rempty[slot]);
+        q += cn;
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty_bar[st]);
-    q += cn;
+  } else {
+    // ---------------- MMA warps ----------------
+    int c = 0;
+    ok = mma_phase<FMT, XBF, NKC, 1>(a, pl, lo1, hi1, c, ok, ring, full_bar, empty_bar, rfull, rempty, red, xin, inv,
+                                     rowmax, wscratch, table, lut1, pair_in, rows_in);
+    D3_STAMP(2);
+    ok = grid_barrier(a.barrier, G) && ok;
+    D3_STAMP(3);
+    ok = mma_phase<FMT, XBF, NKC, 2>(a, pl, lo2, hi2, c, ok, ring, full_bar, empty_bar, rfull, rempty, red, xin, inv,
+                                     rowmax, wscratch, table, lut2, pair_in, rows_in);
+    D3_STAMP(4);
   }
-}
-
-// ---------------------------------------------------------------------------------------------------------------
-// K2: down projection + routed combine, split by output columns.
-struct DownArgs {
-  const float* a1;  // [M*k, I]: SwiGLU output (rotated for ConvRot formats)
-  const int64_t* ids;
-  const float* weights;  // [M, k] routing weights
-  int M, k, E, H, I;
-  const uint8_t* w;  // down rows [E * H, row_bytes(I)]
-  const void* scale;  // FP8: float [E*H/128, I/128]; I8: float [E*H]; W4/W6: uint8 [E*H, I/16]
-  const float* channel;
-  const float* codebook;
-  uint16_t* out;  // [M, H] bf16
-  int stages;
-  int rows_max;  // ceil(H / gridDim.x)
-  int cap;
-};
-
-template <int FMT, int CAP>
-__global__ void __launch_bounds__(DEC_THREADS, 1) moe_down_kernel(const DownArgs a) {
-  const int H = a.H, I = a.I, P = a.M * a.k, NS = a.stages, RM = a.rows_max;
-  const int rb = fmt_row_bytes(FMT, I);
-  const int gb = I / 16;
-  const int wbytes = RM * rb + (fmt_codes(FMT) ? RM * gb : 0);  // weight part of a stage, 16-byte multiple
-  const int stage_bytes = wbytes + CAP * I * 4;
-
-  __shared__ DecodePlan pl;
-  __shared__ __align__(8) uint64_t full_bar[DEC_MAX_STAGES], empty_bar[DEC_MAX_STAGES];
-  __shared__ float lut[16];
-  extern __shared__ __align__(128) uint8_t smem[];
-  float* dots = (float*)smem;  // [P][RM]
-  uint8_t* stages = smem + (((size_t)P * RM * 4 + 127) & ~(size_t)127);
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n0 = (int)((long long)blockIdx.x * H / gridDim.x), n1 = (int)((long long)(blockIdx.x + 1) * H / gridDim.x);
-  const int NR = n1 - n0;
-  if (tid == 0) {
-    for (int s = 0; s < NS; ++s) {
-      mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], DEC_WARPS);
-    }
-    fence_mbar_init();
-  }
-  if (FMT == FMT_W4 && tid < 16) lut[tid] = a.codebook[tid];
-  for (int i = tid; i < P * RM; i += DEC_THREADS) dots[i] = 0.0f;
-  build_plan(pl, a.ids, P, a.E, CAP);
-  const int nseg = pl.nseg;
-
-  if (warp == DEC_WARPS) {
-    if (lane == 0) {
-      const uint64_t pol = policy_evict_first();
-      // weights of the first stages: they do not depend on the previous kernel
-      const int pre = min(NS, nseg);
-      for (int c = 0; c < pre; ++c) {
-        const int e = pl.seg_expert[c], cnt = pl.seg_count[c];
-        uint8_t* dst = stages + (size_t)c * stage_bytes;
-        uint32_t bytes = NR * rb + (fmt_codes(FMT) ? NR * gb : 0) + cnt * I * 4;
-        mbar_arrive_expect_tx(&full_bar[c], bytes);
-        bulk_g2s(dst, a.w + ((size_t)e * H + n0) * rb, NR * rb, &full_bar[c], pol);
-        if (fmt_codes(FMT))
-          bulk_g2s(dst + RM * rb, (const uint8_t*)a.scale + ((size_t)e * H + n0) * gb, NR * gb, &full_bar[c], pol);
-      }
-      grid_dependency_wait();  // a1 is complete from here on
-      for (int c = 0; c < pre; ++c) {
-        const int first = pl.seg_first[c], cnt = pl.seg_count[c];
-        uint8_t* dst = stages + (size_t)c * stage_bytes + wbytes;
-        for (int j = 0; j < cnt; ++j)
-          bulk_g2s(dst + j * I * 4, a.a1 + (size_t)pl.sorted[first + j] * I, I * 4, &full_bar[c], pol);
-      }
-      for (int c = pre; c < nseg; ++c) {
-        const int st = c % NS;
-        if (!mbar_wait(&empty_bar[st], ((c / NS) - 1) & 1)) break;
-        const int e = pl.seg_expert[c], cnt = pl.seg_count[c], first = pl.seg_first[c];
-        uint8_t* dst = stages + (size_t)st * stage_bytes;
-        uint32_t bytes = NR * rb + (fmt_codes(FMT) ? NR * gb : 0) + cnt * I * 4;
-        mbar_arrive_expect_tx(&full_bar[st], bytes);
-        bulk_g2s(dst, a.w + ((size_t)e * H + n0) * rb, NR * rb, &full_bar[st], pol);
-        if (fmt_codes(FMT))
-          bulk_g2s(dst + RM * rb, (const uint8_t*)a.scale + ((size_t)e * H + n0) * gb, NR * gb, &full_bar[st], pol);
-        for (int j = 0; j < cnt; ++j)
-          bulk_g2s(dst + wbytes + j * I * 4, a.a1 + (size_t)pl.sorted[first + j] * I, I * 4, &full_bar[st], pol);
-      }
-      for (int d = max(0, nseg - NS); d < nseg; ++d)
-        if (!mbar_wait(&full_bar[d % NS], (d / NS) & 1)) break;
-    }
-    return;
-  }
-
-  // ---------------- consumers ----------------
-  bool ok = true;
-  for (int c = 0; c < nseg; ++c) {
-    const int st = c % NS;
-    const int e = pl.seg_expert[c], cnt = pl.seg_count[c], first = pl.seg_first[c];
-    if (ok) ok = mbar_wait(&full_bar[st], (c / NS) & 1);
-    if (!ok) continue;
-    const uint8_t* stage = stages + (size_t)st * stage_bytes;
-    const float* xa = (const float*)(stage + wbytes);
-    for (int r = warp; r < NR; r += DEC_WARPS) {
-      const int n = n0 + r;
-      const uint8_t* wrow = stage + r * rb;
-      float acc[CAP];
-#pragma unroll
-      for (int j = 0; j < CAP; ++j) acc[j] = 0.0f;
-      if (FMT == FMT_FP8 || FMT == FMT_I8) {
-        // lane covers columns 4f..4f+3, f = lane + 32m: block m of 128 columns
-        const float* srow = FMT == FMT_FP8 ? (const float*)a.scale + ((size_t)e * H + n) / 128 * (I / 128) : nullptr;
-        for (int m = 0; m < I / 128; ++m) {
-          const int f = lane + 32 * m;
-          const uint32_t wv = *(const uint32_t*)(wrow + 4 * f);
-          float w0, w1, w2, w3;
-          if (FMT == FMT_FP8)
-            e4m3x4(wv, w0, w1, w2, w3);
-          else
-            dec4_i8(wv, w0, w1, w2, w3);
-          const float s = FMT == FMT_FP8 ? __ldg(srow + m) : 1.0f;
-#pragma unroll
-          for (int j = 0; j < CAP; ++j) {
-            if (j < cnt) {
-              const float4 x = ((const float4*)(xa + j * I))[f];
-              float p = w0 * x.x;
-              p = fmaf(w1, x.y, p);
-              p = fmaf(w2, x.z, p);
-              p = fmaf(w3, x.w, p);
-              acc[j] = fmaf(p, s, acc[j]);
-            }
-          }
-        }
-      } else {
-        // lane covers 8 columns 8u..8u+7, u = lane + 32m (half a 16-column scale group)
-        const uint8_t* gsr = stage + RM * rb + r * gb;
-        for (int u = lane; u < I / 8; u += 32) {
-          const int g = u >> 1;
-          const float s = e4m3_to_f32(gsr[g]);
-          const uint32_t word = *(const uint32_t*)(wrow + 4 * u);  // nibbles of columns 8u..8u+7
-          float wf[8];
-          if (FMT == FMT_W4) {
-            uint2 l2 = make_uint2(word, 0u);
-            dec_w4<8>(l2, s, lut, wf);
-          } else {
-            const uint32_t hiw = *(const uint16_t*)(wrow + I / 2 + 2 * u);
-            dec_w6<8>(make_uint2(word, 0u), hiw, s, wf);
-          }
-#pragma unroll
-          for (int j = 0; j < CAP; ++j) {
-            if (j < cnt) {
-              const float4 x0 = ((const float4*)(xa + j * I))[2 * u];
-              const float4 x1 = ((const float4*)(xa + j * I))[2 * u + 1];
-              float p = wf[0] * x0.x;
-              p = fmaf(wf[1], x0.y, p);
-              p = fmaf(wf[2], x0.z, p);
-              p = fmaf(wf[3], x0.w, p);
-              p = fmaf(wf[4], x1.x, p);
-              p = fmaf(wf[5], x1.y, p);
-              p = fmaf(wf[6], x1.z, p);
-              p = fmaf(wf[7], x1.w, p);
-              acc[j] += p;
-            }
-          }
-        }
-      }
-      float rscale = 1.0f;
-      if (FMT == FMT_I8) rscale = 0.0625f * __ldg((const float*)a.scale + (size_t)e * H + n);
-      if (fmt_codes(FMT)) rscale = 0.0625f * __ldg(a.channel + (size_t)e * H + n);
-#pragma unroll
-      for (int j = 0; j < CAP; ++j) {
-        if (j < cnt) {
-          float v = warp_sum(acc[j]) * rscale;
-          if (lane == 0) dots[pl.sorted[first + j] * RM + r] = v;
-        }
-      }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty_bar[st]);
-  }
-  named_sync(1, DEC_WARPS * 32);
-  // routed combine in rank order, as the reference's weighted_sum
-  for (int idx = tid; idx < a.M * NR; idx += DEC_WARPS * 32) {
-    const int t = idx / NR, r = idx - t * NR;
+  ok = grid_barrier(a.barrier, G) && ok;
+  D3_STAMP(5);
+  // phase 3: routed combine in rank order, as the reference's weighted_sum
+  int n0, n1;
+  split_range(H, blockIdx.x, G, n0, n1);
+  const int NC = n1 - n0;
+  for (int idx = tid; idx < a.M * NC; idx += DEC_CONSUMERS + 32) {
+    const int t = idx / NC, n = n0 + idx - t * NC;
     float acc = 0.0f;
-    for (int j = 0; j < a.k; ++j) acc = __fmaf_rn(dots[(t * a.k + j) * RM + r], a.weights[t * a.k + j], acc);
-    a.out[(size_t)t * H + n0 + r] = f32_to_bf16(acc);
+    for (int j = 0; j < a.k; ++j) {
+      const long long id = a.ids[t * a.k + j];
+      const float part = (ok && id >= 0 && id < a.E) ? __ldcg(a.parts + (size_t)(t * a.k + j) * H + n) : 0.0f;
+      acc = __fmaf_rn(part, a.weights[t * a.k + j], acc);
+    }
+    a.out[(size_t)t * H + n] = f32_to_bf16(acc);
   }
+  D3_STAMP(6);
 }
 
 }  // namespace d3

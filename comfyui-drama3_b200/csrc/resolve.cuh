@@ -51,8 +51,8 @@ __global__ void __launch_bounds__(RESOLVE_THREADS)
       fill[tid] = 1;
     } else {
       int key = base + (int)id;
-      float kept = at[key] < 0 ? 0.0f : __fmul_rn(score[key], exp2f(log2_decay * (float)(now - at[key])));
-      float used = __fadd_rn(kept, 1.0f);
+      // score * decay + 1 as one fused multiply-add (what the reference kernel computes)
+      float used = at[key] < 0 ? 1.0f : __fmaf_rn(score[key], exp2f(log2_decay * (float)(now - at[key])), 1.0f);
       score[key] = used;
       uses[tid] = used;
       at[key] = now;

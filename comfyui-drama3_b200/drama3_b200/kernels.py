@@ -196,9 +196,11 @@ def grouped_codes(x, groups, slot_fields, host_fields, codebook, bits, n):
 
 
 def decode_workspace(rows, k, intermediate, device):
-    """The workspace moe_decode needs, allocated once by the caller (graph-captured steps reuse it)."""
+    """The workspace moe_decode needs, allocated once by the caller and reused by every call (graph-captured steps
+    included). It must start zeroed (its last bytes are the kernel's grid-barrier words, which every call leaves at
+    zero); calls that share one workspace must not overlap on the GPU."""
     size = lib().d3_moe_decode_workspace(rows, k, intermediate)
-    return torch.empty((size,), dtype=torch.uint8, device=device)
+    return torch.zeros((size,), dtype=torch.uint8, device=device)
 
 
 def moe_decode(kind, x, ids, weights, banks, codebooks=(None, None), workspace=None, out=None):
@@ -208,6 +210,8 @@ def moe_decode(kind, x, ids, weights, banks, codebooks=(None, None), workspace=N
     w4/w6 {"_qdata", "scale" (e4m3 bytes), "s_channel"} and a codebook per bank for w4. Each routed expert is read
     once for all M rows."""
     fmt = _lib.FORMATS[kind]
+    if x.dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError(f"moe_decode takes bfloat16 or float32 rows, not {x.dtype}")
     gate_up, down = banks
     wkey = "weight" if kind == "fp8" else "_qdata"
     M, H = x.shape

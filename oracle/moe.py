@@ -285,9 +285,13 @@ def resolve(state, ids, layer, layers, experts, half_life, cpu, admit):
     slot_of, fill, uses = [0] * k, [0] * k, [F32(0)] * k
     for t in range(k):
         key = base + int(ids[t])
-        kept = F32(0.0) if st["at"][key] < 0 else decayed(key)
-        st["score"][key] = F32(kept + F32(1.0))
-        uses[t] = F32(kept + F32(1.0))
+        if st["at"][key] < 0:
+            used = F32(1.0)
+        else:  # the kernel fuses score * decay + 1 into one multiply-add
+            decay = np.exp2(F32(log2_decay * F32(now - int(st["at"][key]))))
+            used = F32(fma32(st["score"][key], decay, F32(1.0)))
+        st["score"][key] = used
+        uses[t] = used
         st["at"][key] = now
         slot = int(st["table"][key])
         slot_of[t] = slot if slot >= 0 else -1
