@@ -101,6 +101,7 @@ const char* d3_error_string(int code) {
     case D3_ERR_CUDA: return "CUDA error at launch (see d3_last_cuda_error)";
     case D3_ERR_DEVICE: return "current device is not an sm_100 (B200) GPU";
     case D3_ERR_WORKSPACE: return "workspace too small";
+    case D3_ERR_TOO_LARGE: return "shape beyond the library-held scratch (at most 128 routed pairs, intermediate <= 768)";
     default: return "unknown error";
   }
 }
@@ -364,4 +365,51 @@ extern "C" int d3_moe_decode(int fmt, const void* x, int x_bf16, int M, int k, i
     case d3::FMT_W6: return decode_nkc<d3::FMT_W6, true>(a, d, s);
   }
   return D3_ERR_ARG;
+}
+
+// ------------------------------------------------------------------------------------------------------------
+// Fused decode without a caller-provided workspace, for callers that cannot allocate device memory themselves.
+// The scratch is this file-scope array, sized for the largest decode the kernel takes (16 rows x top-8 = 128 routed
+// pairs, intermediate 768, hidden 2048): 1,442,048 bytes that every GPU loading the library holds until exit.
+// Host code cannot use the array's name as a device address: set-up, once per device with that device current,
+// asks the runtime for the address (cudaGetSymbolAddress) and keeps it.
+namespace {
+
+constexpr size_t kStaticScratchBytes = 128u * 768u * 4u + 128u * 2048u * 4u + 256u;
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+void* g_static_ptr[kMaxDevices];
+
+// The device address of g_static_scratch on the current device (set up on first use: not inside a stream capture).
+int static_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return D3_ERR_DEVICE;
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (g_static_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (int st = cuda_status(cudaGetSymbolAddress(&p, g_static_scratch))) return st;
+    g_static_ptr[dev] = p;
+  }
+  *out = g_static_ptr[dev];
+  return D3_OK;
+}
+
+}  // namespace
+
+extern "C" int d3_moe_decode_static(int fmt, const void* x, int x_bf16, int M, int k, int E, int H, int I,
+                                    const int64_t* ids, const float* weights, const uint8_t* w13, const void* s13,
+                                    const float* c13, const uint8_t* w2, const void* s2, const float* c2,
+                                    const float* codebook13, const float* codebook2, uint16_t* out, void* stream) {
+  if (M < 1 || k < 1 || I < 1) return D3_ERR_ARG;
+  if ((long long)M * k > 128 || I > 768 || H != d3::DEC_H || d3_moe_decode_workspace(M, k, I) > kStaticScratchBytes)
+    return D3_ERR_TOO_LARGE;
+  void* ws = nullptr;
+  if (int st = static_scratch(&ws)) return st;
+  // The array keeps the last call's contents; of them only the grid-barrier counter must start at zero (its place
+  // depends on the shape). Cleared on the stream, ahead of the kernel.
+  const size_t P = (size_t)M * k;
+  unsigned char* barrier = (unsigned char*)ws + align256(P * I * 4) + align256(P * d3::DEC_H * 4);
+  if (int st = cuda_status(cudaMemsetAsync(barrier, 0, sizeof(unsigned long long), (cudaStream_t)stream))) return st;
+  return d3_moe_decode(fmt, x, x_bf16, M, k, E, H, I, ids, weights, w13, s13, c13, w2, s2, c2, codebook13, codebook2,
+                       out, ws, kStaticScratchBytes, stream);
 }

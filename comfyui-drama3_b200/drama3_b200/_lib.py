@@ -8,7 +8,7 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libdrama3_b200.so"
 
-D3_OK, D3_ERR_ARG, D3_ERR_ALIGN, D3_ERR_CUDA, D3_ERR_DEVICE, D3_ERR_WORKSPACE = range(6)
+D3_OK, D3_ERR_ARG, D3_ERR_ALIGN, D3_ERR_CUDA, D3_ERR_DEVICE, D3_ERR_WORKSPACE, D3_ERR_TOO_LARGE = range(7)
 FMT_FP8, FMT_INT8, FMT_W4, FMT_W6 = range(4)
 FORMATS = {"fp8": FMT_FP8, "int8": FMT_INT8, "w4": FMT_W4, "w6": FMT_W6}
 
@@ -36,6 +36,7 @@ SIGNATURES = {
     "d3_grouped_codes": (_i, [_p, _i, _p, _i, _p, _p, _p, _p, _p, _p, _p, _i, _p, _i, _i, _i, _i, _p]),
     "d3_moe_decode_workspace": (_sz, [_i, _i, _i]),
     "d3_moe_decode": (_i, [_i, _p, _i, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _sz, _p]),
+    "d3_moe_decode_static": (_i, [_i, _p, _i, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
 }
 
 

@@ -30,6 +30,7 @@ extern "C" {
 #define D3_ERR_CUDA 3      /* the launch failed; d3_last_cuda_error() has the cudaError_t */
 #define D3_ERR_DEVICE 4    /* the current device is not compute capability 10.0 */
 #define D3_ERR_WORKSPACE 5 /* the workspace is smaller than d3_moe_decode_workspace() */
+#define D3_ERR_TOO_LARGE 6 /* beyond the library-held scratch of d3_moe_decode_static() */
 
 /* Weight formats of the fused decode (the reference's safetensors layouts; drama3/offload.py:72-90,755-766). */
 #define D3_FMT_FP8 0  /* e4m3 rows + fp32 128x128 block scales */
@@ -119,6 +120,19 @@ int d3_moe_decode(int fmt, const void* x, int x_bf16, int M, int k, int E, int H
                   const float* weights, const uint8_t* w13, const void* s13, const float* c13, const uint8_t* w2,
                   const void* s2, const float* c2, const float* codebook13, const float* codebook2, uint16_t* out,
                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* d3_moe_decode without a workspace argument. No counterpart in the reference: it is for callers that cannot
+ * allocate device memory themselves, such as a plugin whose host application's memory manager owns every device
+ * allocation, or a C host that links this library without any device allocator. The scratch is an array inside the
+ * library (1,442,048 bytes, held on every GPU that loads it until the process exits), so the call allocates nothing
+ * and calls no allocating routine. Limits: at most 128 routed pairs (M * k), intermediate size <= 768; larger shapes
+ * return D3_ERR_TOO_LARGE. The first call on a device sets up the array's device address (synchronous); make it
+ * before any stream capture. All calls share the one array: calls that overlap on the GPU race, so issue them on
+ * one stream (or order them). Each call clears the array's barrier word on `stream` before its kernel. */
+int d3_moe_decode_static(int fmt, const void* x, int x_bf16, int M, int k, int E, int H, int I, const int64_t* ids,
+                         const float* weights, const uint8_t* w13, const void* s13, const float* c13,
+                         const uint8_t* w2, const void* s2, const float* c2, const float* codebook13,
+                         const float* codebook2, uint16_t* out, void* stream);
 
 #ifdef __cplusplus
 }
