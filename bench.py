@@ -1,6 +1,6 @@
 """Benchmark: MoE decode tokens/s of the routed-expert path on B200 (FP8 experts).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mine|reference] [--lines 16]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mine|reference] [--lines 16] [--layers 48]
     torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU)
 
 A step is one decode pass of `lines` rows (16: lines decoded together) through 48 MoE layers of the BASELINE shape
@@ -8,7 +8,9 @@ A step is one decode pass of `lines` rows (16: lines decoded together) through 4
 block scales, the reference layout) and its own seeded routing: 29 GB of experts, far larger than L2, so every
 step streams its experts from HBM (no flush needed). Inputs are resident in HBM; the timed region replays one CUDA
 graph per step. Multi-GPU: independent replicas (each rank decodes its own lines with all experts resident; no
-collective), weak scaling. `value` = tokens/s of all ranks; timing = CUDA events, max over ranks.
+collective), weak scaling. `value` = tokens/s of all ranks; timing = CUDA events, max over ranks. The timed region
+is bracketed by cudaProfilerStart/Stop, so `ncu --profile-from-start off` sees exactly its launches; `--layers 4` is
+the small case for multi-pass captures (same per-layer shapes and routing as the first 4 layers of the full run).
 
 Also reported: the 1-line decode, the end-to-end rate through the Python API with host buffers, the reference's own
 kernels (compiled from drama3/kernels.py into oracle/_ref) on the same GPU, and the reference's CPU path on the host
@@ -33,6 +35,9 @@ import torch  # noqa: E402
 METRIC = "MoE decode tokens/s (1 & 16 lines), expert GEMV HBM GB/s vs ~8 TB/s, 1-8 B200"
 E, H, I, K_TOP = 128, 2048, 768, 8
 LAYERS = 48
+# dram bytes (read + write) per launch over algorithmic bytes per launch, from the ncu capture of the small case
+# (bench.py --layers 4, all 4 launches of one timed step); the full run's traffic is this ratio x its own bytes
+TRAFFIC_RATIO = 1625.44 / 1609.96
 # algorithmic bytes of one FP8 expert (reference layout): gate_up 1536x2048 + down 2048x768 e4m3, block scales
 EXPERT_BYTES = 2 * I * H + H * I + (2 * I // 128) * (H // 128) * 4 + (H // 128) * (I // 128) * 4
 
@@ -87,11 +92,12 @@ class Clocks:
                 "samples": len(self.rows), "reasons": reasons}
 
 
-def make_layers(device, lines, seed=4):
-    """48 layers of FP8 banks (random valid e4m3 bytes, positive block scales) and per-layer routing."""
+def make_layers(device, lines, seed=4, n_layers=LAYERS):
+    """n_layers layers of FP8 banks (random valid e4m3 bytes, positive block scales) and per-layer routing; layer l's
+    routing does not depend on n_layers."""
     gen = torch.Generator(device=device).manual_seed(seed)
     layers = []
-    for _ in range(LAYERS):
+    for _ in range(n_layers):
         bank = []
         for n, k in ((2 * I, H), (H, I)):
             w = torch.randint(0, 254, (E * n, k), generator=gen, device=device, dtype=torch.uint8)
@@ -101,7 +107,7 @@ def make_layers(device, lines, seed=4):
         layers.append(tuple(bank))
     cpu_gen = torch.Generator().manual_seed(seed + 1)
     ids, weights = [], []
-    for _ in range(LAYERS):
+    for _ in range(n_layers):
         w, i = torch.softmax(torch.randn((lines, E), generator=cpu_gen), dim=-1).topk(K_TOP, dim=-1)
         ids.append(i)
         weights.append((w / w.sum(-1, keepdim=True)).to(torch.bfloat16).float())
@@ -131,34 +137,42 @@ def time_graph(fn, steps, warmup, stream):
     return graph, start, end
 
 
-def cpu_reference(lines, layers_sampled=2, seed=4):
+def cpu_reference(lines, layers_sampled=2, seed=4, n_layers=LAYERS, seconds=10.0):
     """The reference's CPU decode (oracle/cpu_port.py) on the host cores: `lines` rows through `layers_sampled`
-    layers, scaled to 48 layers. Returns (tokens/s, seconds, threads, sample description)."""
+    layers, scaled to n_layers layers. Returns (tokens/s, seconds, threads, sample description)."""
     from oracle import cpu_port
     torch.set_num_threads(os.cpu_count() or 1)
     gen = torch.Generator().manual_seed(seed)
     x = torch.randn((lines, H), generator=gen).to(torch.bfloat16)
-    total = 0.0
-    for _ in range(layers_sampled):
+    banks = []
+    for _ in range(2):
         gu = torch.randint(0, 126, (E, 2 * I, H), generator=gen, dtype=torch.uint8)
         dn = torch.randint(0, 126, (E, H, I), generator=gen, dtype=torch.uint8)
         gs = torch.rand((E, 2 * I // 128, H // 128), generator=gen) * 1e-4
         ds = torch.rand((E, H // 128, I // 128), generator=gen) * 1e-4
+        banks.append((gu, gs, dn, ds))
+    total, done = 0.0, 0
+    # at least `layers_sampled` layers, then more until about `seconds` of CPU work (two banks, alternating, each
+    # layer with its own routing)
+    while done < n_layers and (done < layers_sampled or total < seconds):
+        gu, gs, dn, ds = banks[done % 2]
         w, ids = torch.softmax(torch.randn((lines, E), generator=gen), -1).topk(K_TOP, dim=-1)
         w = (w / w.sum(-1, keepdim=True)).to(torch.bfloat16)
         started = time.perf_counter()
         cpu_port.fp8_decode_lines(x, ids, w, gu, gs, dn, ds)
         total += time.perf_counter() - started
-    per_step = total / layers_sampled * LAYERS
-    sample = (f"{lines} rows x {layers_sampled} layers of the reference CPU path (bf16 dequant + matmuls, one row at "
-              f"a time), scaled to {LAYERS} layers")
+        done += 1
+    per_step = total / done * n_layers
+    sample = (f"{lines} rows x {done} layers ({total:.1f} s) of the reference CPU path (bf16 dequant + matmuls, one "
+              f"row at a time), scaled to {n_layers} layers")
     return lines / per_step, total, torch.get_num_threads(), sample
 
 
 def run_reference_arm(args, rank):
     if rank != 0:
         return
-    tps, secs, threads, sample = cpu_reference(args.lines, layers_sampled=max(1, min(args.steps, 2)))
+    tps, secs, threads, sample = cpu_reference(args.lines, layers_sampled=max(1, min(args.steps, 2)),
+                                               n_layers=args.layers)
     line = {"impl": "reference", "metric": METRIC, "value": tps, "unit": "tokens/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * args.lines / tps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (CPU)",
@@ -169,11 +183,12 @@ def run_reference_arm(args, rank):
 
 
 def config(args):
-    return {"workload": f"fp8 MoE decode, {args.lines} lines x {LAYERS} layers per step (BASELINE configs[1] layer "
-                        f"shape; 48 layers as configs[4])",
-            "layers": LAYERS, "lines": args.lines, "experts": E, "top_k": K_TOP, "hidden": H, "intermediate": I,
+    return {"workload": f"fp8 MoE decode, {args.lines} lines x {args.layers} layers per step (BASELINE configs[1] "
+                        f"layer shape; 48 layers as configs[4])",
+            "layers": args.layers, "lines": args.lines, "experts": E, "top_k": K_TOP, "hidden": H, "intermediate": I,
             "format": "e4m3 + fp32 128x128 block scales (reference layout)",
-            "l2": "inputs larger than L2: 29 GB of expert banks streamed per step",
+            "l2": f"inputs larger than L2: {args.layers * E * EXPERT_BYTES / 1e9:.1f} GB of expert banks, each layer's "
+                  f"routed experts streamed per step",
             "parallelism": f"replicas x{args.gpus} (lines data-parallel)"}
 
 
@@ -184,6 +199,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("mine", "reference"), default="mine")
     ap.add_argument("--lines", type=int, default=16)
+    ap.add_argument("--layers", type=int, default=LAYERS, help="layers per step (48: the benchmark; 4: small case)")
     ap.add_argument("--no-extras", action="store_true", help="skip e2e / reference GPU / CPU legs")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -206,14 +222,15 @@ def main():
 
     from drama3_b200 import kernels
 
-    layers, ids, weights = make_layers(device, args.lines, seed=4 + rank)
+    n_layers = args.layers
+    layers, ids, weights = make_layers(device, args.lines, seed=4 + rank, n_layers=n_layers)
     x = torch.randn((args.lines, H), generator=torch.Generator().manual_seed(7 + rank)).to(torch.bfloat16).to(device)
     ws = kernels.decode_workspace(args.lines, K_TOP, I, device)
-    outs = torch.empty((LAYERS, args.lines, H), dtype=torch.bfloat16, device=device)
+    outs = torch.empty((n_layers, args.lines, H), dtype=torch.bfloat16, device=device)
     stream = torch.cuda.Stream(device)
 
     def step(lines=args.lines, xin=x, ids_=ids, w_=weights, ws_=ws, out_=outs):
-        for l_ in range(LAYERS):
+        for l_ in range(n_layers):
             kernels.moe_decode("fp8", xin, ids_[l_], w_[l_], layers[l_], workspace=ws_, out=out_[l_])
 
     with torch.cuda.stream(stream):
@@ -225,11 +242,13 @@ def main():
             pg.barrier()
         torch.cuda.synchronize()
         with Clocks(local) as clocks:
+            torch.cuda.profiler.start()
             start.record(stream)
             for _ in range(args.steps):
                 graph.replay()
             end.record(stream)
             torch.cuda.synchronize()
+            torch.cuda.profiler.stop()
         ms = start.elapsed_time(end) / args.steps
     if pg:
         t = torch.tensor([ms], device=device)
@@ -245,7 +264,7 @@ def main():
         # one line decoded at a time (M = 1)
         x1, ids1, w1 = x[:1].contiguous(), ids[:, :1].contiguous(), weights[:, :1].contiguous()
         ws1 = kernels.decode_workspace(1, K_TOP, I, device)
-        out1 = torch.empty((LAYERS, 1, H), dtype=torch.bfloat16, device=device)
+        out1 = torch.empty((n_layers, 1, H), dtype=torch.bfloat16, device=device)
         with torch.cuda.stream(stream):
             g1, s1, e1 = time_graph(lambda: step(1, x1, ids1, w1, ws1, out1), 0, args.warmup, stream)
             s1.record(stream)
@@ -257,7 +276,7 @@ def main():
         b1 = unique_bytes(ids1)
         extras["lines_1"] = {"tokens_per_s": 1 / (ms1 * 1e-3), "ms_per_step": ms1,
                              "hbm_gbs": b1 / (ms1 * 1e-3) / 1e9, "frac": b1 / (ms1 * 1e-3) / 1e9 / hbm_peak,
-                             "bytes_per_step": b1, "us_per_layer": 1e3 * ms1 / LAYERS}
+                             "bytes_per_step": b1, "us_per_layer": 1e3 * ms1 / n_layers}
         del g1
         # end to end through the Python API: host inputs in, host output back, every step
         xh = x.cpu().pin_memory()
@@ -287,7 +306,7 @@ def main():
             from oracle import ref_gpu
             if ref_gpu.available():
                 def ref_step():
-                    for l_ in range(LAYERS):
+                    for l_ in range(n_layers):
                         ref_gpu.lines_decode(x, ids[l_], weights[l_], layers[l_], (2 * I, H), "fp8", (None, None))
                 with torch.cuda.stream(stream):
                     gr, rs, re_ = time_graph(ref_step, 0, 2, stream)
@@ -307,7 +326,7 @@ def main():
         except Exception as exc:  # the comparison leg must not sink the bench line
             extras["reference_gpu"] = {"error": repr(exc)[:200]}
         # the reference's CPU path on the host cores (bounded sample)
-        tps, secs, threads, sample = cpu_reference(args.lines)
+        tps, secs, threads, sample = cpu_reference(args.lines, n_layers=n_layers)
         extras["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
                                   "sample": sample, "seconds": secs}
 
@@ -317,11 +336,15 @@ def main():
                 "vs_baseline": None, "dtype": "e4m3 weights, f32 math", "data": "synthetic (seeded random banks)",
                 "config": config(args),
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                             "frac": achieved / hbm_peak, "traffic": None, "peak_kind": peak_kind,
-                             "kernel": "moe_up + moe_down (one decode layer; the pair overlaps through programmatic "
-                                       "dependent launch)",
-                             "bytes_per_step": step_bytes, "us_per_layer": 1e3 * ms / LAYERS},
-                "gpu_launches": 2 * LAYERS * args.steps,
+                             "frac": achieved / hbm_peak, "peak_kind": peak_kind,
+                             "traffic": None if TRAFFIC_RATIO is None else TRAFFIC_RATIO * step_bytes / n_layers,
+                             "traffic_unit": "bytes per launch (ncu ratio of the --layers 4 capture x this run's "
+                                             "algorithmic bytes per launch)",
+                             "kernel": "moe_decode_kernel<fp8> (one persistent launch per layer: plan, gate_up + "
+                                       "SwiGLU, down, combine)",
+                             "bytes_per_launch": step_bytes / n_layers, "us_per_layer": 1e3 * ms / n_layers,
+                             "launch_time": "step time / layers: the launches run back to back in one graph"},
+                "gpu_launches": n_layers * args.steps,
                 "clocks": clocks.summary()}
         line.update(extras)
         print(json.dumps(line), flush=True)

@@ -197,8 +197,9 @@ def grouped_codes(x, groups, slot_fields, host_fields, codebook, bits, n):
 
 def decode_workspace(rows, k, intermediate, device):
     """The workspace moe_decode needs, allocated once by the caller and reused by every call (graph-captured steps
-    included). It must start zeroed (its last bytes are the kernel's grid-barrier words, which every call leaves at
-    zero); calls that share one workspace must not overlap on the GPU."""
+    included). It must start zeroed: its last bytes are the kernel's grid-barrier ticket counter, which each call
+    advances by a whole number of rounds, so it never needs resetting. Calls that share one workspace must not overlap
+    on the GPU."""
     size = lib().d3_moe_decode_workspace(rows, k, intermediate)
     return torch.zeros((size,), dtype=torch.uint8, device=device)
 
