@@ -6,9 +6,12 @@
 
 #include <mutex>
 
+#include <cudaTypedefs.h>
+
 #include "../../include/drama3_b200.h"
 #include "common.cuh"
 #include "gemv.cuh"
+#include "grouped_mma.cuh"
 #include "moe_decode.cuh"
 #include "resolve.cuh"
 #include "rotate.cuh"
@@ -79,6 +82,33 @@ int launch(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bo
     cfg.numAttrs = 1;
   }
   return cuda_status(cudaLaunchKernelEx(&cfg, kernel, args...));
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+  });
+  return fn;
+}
+
+// A 2-D byte tensor [rows, row_bytes] read in boxes of box_bytes x 128 rows, no swizzle.
+bool byte_tile_map(CUtensorMap* map, const void* base, uint64_t row_bytes, uint64_t rows, uint32_t box_bytes) {
+  PFN_cuTensorMapEncodeTiled_v12000 fn = tensor_map_encoder();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {row_bytes, rows};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_bytes, 128};
+  cuuint32_t elem[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, elem,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 int static_smem(const void* kernel) {
@@ -289,6 +319,62 @@ int d3_grouped_codes(const float* x, int x_rows, const int* groups, int n_groups
   d3::GroupedArgs a = {x, groups, slot_w, slot_r, slot_c, host_w, host_r, host_c, codebook, out, N, K, num_experts,
                        slots, x_rows};
   return grouped_common(bits == 4 ? d3::FMT_W4 : d3::FMT_W6, a, n_groups, stream);
+}
+
+// ------------------------------------------------------------------------------------------------------------
+// Grouped expert GEMM on the tensor cores (banks held whole on the GPU).
+
+size_t d3_grouped_mma_workspace(int tiles, int K) {
+  if (tiles < 0 || K < 256) return 0;
+  return d3::gm_workspace_bytes(tiles, K);
+}
+
+int d3_grouped_mma(int fmt, const float* x, const int* groups, int n_groups, int tiles, const void* weight,
+                   const void* scale, const float* s_channel, const float* codebook, int bank_rows, float* out, int N,
+                   int K, void* workspace, size_t workspace_bytes, void* stream) {
+  DeviceInfo d;
+  if (int st = device_info(&d)) return st;
+  if (fmt < d3::FMT_FP8 || fmt > d3::FMT_W6 || n_groups < 0 || tiles < 0) return D3_ERR_ARG;
+  if (N < d3::GM_M || N % d3::GM_M || K < 256 || K % 256 || bank_rows < N || bank_rows % d3::GM_M) return D3_ERR_ARG;
+  if (!x || !groups || !weight || !scale || !out || !workspace) return D3_ERR_ARG;
+  if ((fmt == d3::FMT_W4 || fmt == d3::FMT_W6) && !s_channel) return D3_ERR_ARG;
+  if (fmt == d3::FMT_W4 && !codebook) return D3_ERR_ARG;
+  if (!aligned(x, 16) || !aligned(out, 16) || !aligned(weight, 16) || !aligned(scale, 4) || !aligned(workspace, 256))
+    return D3_ERR_ALIGN;
+  if (workspace_bytes < d3::gm_workspace_bytes(tiles, K)) return D3_ERR_WORKSPACE;
+  if (tiles == 0 || n_groups == 0) return D3_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  uint8_t* ws = (uint8_t*)workspace;
+  uint8_t* staged = ws;
+  float* inv = (float*)(ws + d3::gm_staged_bytes(tiles, K));
+  d3::GroupedTile* table = (d3::GroupedTile*)(inv + (size_t)tiles * d3::GM_NT);
+  int* ntiles = (int*)(table + tiles);
+  CUtensorMap wmap, pmap;
+  const uint64_t row_bytes = (uint64_t)d3::fmt_row_bytes(fmt, K);
+  const uint32_t box = fmt == d3::FMT_FP8 || fmt == d3::FMT_I8 ? 64 : 32;
+  if (!byte_tile_map(&wmap, weight, row_bytes, (uint64_t)bank_rows, box)) return D3_ERR_ARG;
+  pmap = wmap;
+  if (fmt == d3::FMT_W6 && !byte_tile_map(&pmap, weight, row_bytes, (uint64_t)bank_rows, 16)) return D3_ERR_ARG;
+  if (int st = launch(d3::gm_stage_kernel, dim3(tiles), dim3(256), 0, s, false, x, groups, n_groups, K, tiles, staged,
+                      inv, table, ntiles))
+    return st;
+  const int units = tiles * (N / d3::GM_M);
+  d3::GmArgs a = {staged, inv, table, ntiles, groups, scale, s_channel, codebook, out, N, K, units, bank_rows};
+  const int smem = d3::GmSmem::launch;
+  const dim3 grid(units < d.sms ? units : d.sms);
+  switch (fmt) {
+#define D3_GM_CASE(F)                                                                    \
+  case F: {                                                                              \
+    if (int st = allow_smem(d3::grouped_mma_kernel<F>, smem)) return st;                 \
+    return launch(d3::grouped_mma_kernel<F>, grid, dim3(d3::GM_THREADS), smem, s, false, wmap, pmap, a); \
+  }
+    D3_GM_CASE(d3::FMT_FP8)
+    D3_GM_CASE(d3::FMT_I8)
+    D3_GM_CASE(d3::FMT_W4)
+    D3_GM_CASE(d3::FMT_W6)
+#undef D3_GM_CASE
+  }
+  return D3_ERR_ARG;
 }
 
 // ------------------------------------------------------------------------------------------------------------

@@ -1,0 +1,575 @@
+// Grouped expert GEMM for a prompt's rows on the 5th-generation tensor cores: out[row, n] = the rows of each group
+// (sorted by expert, fp32) against their expert's weight rows, as the reference's grouped kernels compute it
+// (drama3/kernels.py:365-464, 538-587: fp8 block-scaled, int8 ConvRot, W4A8 / W6A8 codes), for banks held whole on
+// the GPU.
+//
+// Work unit = (token tile of up to 128 rows of one group, block of 128 weight rows). Per unit, D[128 x 128] (weight
+// rows x tokens) accumulates in tensor memory (tcgen05.mma kind::f16, M = 128, N = 128, K = 16, f32 accumulate):
+//   A = 128 weight rows, converted exactly to f16 in shared memory (every e4m3 value, every int8 and every int8-grid
+//       code is an f16), K-major with the 128-byte swizzle;
+//   B = the tile's rows as two f16 terms, hi = f16(x * 2^e) and lo = f16(x * 2^e - hi) (e per row puts its max in
+//       [2^14, 2^15)), laid out by the staging kernel in global memory exactly as the MMA reads them from shared
+//       memory, so one 1-D bulk copy moves a 16 KB operand block. The products are exact; two MMAs per K step.
+// fp8 block scales vary every 128 columns: the accumulator is folded every 128 columns (two alternating regions of
+// 128 tensor-memory columns) by the fold warps, which add scale x partial into registers; the other formats fold
+// once per unit and apply the row scale (int8 scale, W4/W6 s_channel).
+//
+// Warps (352 threads, one CTA per SM, persistent over units):
+//   0     raw-weight producer: 2-D TMA tile loads (64 columns x 128 rows of bytes) into a 6-stage ring
+//   1     activation producer: two 16 KB bulk copies (hi, lo) per 64-column chunk into a 3-stage ring
+//   2     MMA issuer (one elected thread) and owner of the 256 tensor-memory columns
+//   3-6   converters: thread = weight row, raw bytes -> f16, written swizzled into the A stage
+//   7-10  fold + epilogue: tcgen05.ld of their 32-lane quarter, scale, accumulate, write fp32 rows
+// Every wait is bounded (2 s) and records FAULT_WAIT_TIMEOUT instead of hanging.
+#pragma once
+
+#include <cuda.h>
+
+#include "formats.cuh"
+#include "moe_decode.cuh"
+
+namespace d3 {
+
+constexpr int GM_M = 128;              // weight rows per unit (one fp8 scale block)
+constexpr int GM_NT = 128;             // token rows per tile
+constexpr int GM_KC = 64;              // columns per chunk: one 128-byte swizzle atom of f16
+constexpr int GM_RAW_ST = 6;           // raw weight ring depth
+constexpr int GM_MMA_ST = 3;           // operand ring depth (A f16 + B hi/lo)
+constexpr int GM_RAW_BYTES = 8192;     // one raw stage: up to 64 bytes x 128 rows
+constexpr int GM_A_BYTES = GM_M * GM_KC * 2;      // 16 KB
+constexpr int GM_B_BYTES = GM_NT * GM_KC * 2;     // 16 KB per term
+constexpr int GM_WARPS = 11;
+constexpr int GM_THREADS = GM_WARPS * 32;
+constexpr int GM_CONV0 = 3, GM_FOLD0 = 7;         // first converter / fold warp
+constexpr int GM_TMEM_COLS = 256;
+
+struct GroupedTile {
+  int group;  // index into groups[]
+  int row0;   // first sorted row of the tile
+  int rows;   // rows in the tile (1..128)
+  int pad;
+};
+
+// Byte offset of 16-byte chunk c (columns 8c..8c+7 of a 64-column chunk) of row r in a K-major, 128-byte-swizzled
+// operand block of 128 rows: 8-row atoms of 1024 bytes, chunk c of row r stored at position c ^ (r % 8).
+__host__ __device__ constexpr uint32_t sw128_offset(int r, int c) {
+  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+}
+
+// Bytes of the staged activations of `tiles` tiles with K columns, and of the whole workspace.
+__host__ __device__ constexpr size_t gm_staged_bytes(int tiles, int K) {
+  return (size_t)tiles * (size_t)(K / GM_KC) * 2u * GM_B_BYTES;
+}
+__host__ __device__ constexpr size_t gm_workspace_bytes(int tiles, int K) {
+  return gm_staged_bytes(tiles, K) + (size_t)tiles * GM_NT * 4u + (size_t)tiles * sizeof(GroupedTile) + 256u;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Staging: one block (8 warps) per tile slot. Block t finds its (group, tile of the group) from the groups' row
+// counts, writes the tile table entry, and converts the tile's rows (zeros past the group's end) to the hi / lo
+// f16 operand blocks plus inv[row] = 2^-e (0 for padding rows). Block 0 also writes the number of tiles.
+// Needs K % 256 == 0.
+__global__ void __launch_bounds__(256) gm_stage_kernel(const float* __restrict__ x, const int* __restrict__ groups,
+                                                       int G, int K, int max_tiles, uint8_t* __restrict__ staged,
+                                                       float* __restrict__ inv, GroupedTile* __restrict__ table,
+                                                       int* __restrict__ ntiles) {
+  __shared__ int s_group, s_local, s_total;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x;
+  if (warp == 0) {
+    int base = 0, found_g = -1, found_l = 0;
+    for (int c0 = 0; c0 < G; c0 += 32) {
+      const int g = c0 + lane;
+      const int n = g < G ? max(0, groups[5 * g + 4]) : 0;
+      const int tiles = (n + GM_NT - 1) / GM_NT;
+      int incl = tiles;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      const int excl = incl - tiles;
+      const unsigned hit = __ballot_sync(0xffffffffu, t >= base + excl && t < base + incl);
+      const int src = hit ? __ffs(hit) - 1 : 0;
+      const int src_excl = __shfl_sync(0xffffffffu, excl, src);
+      if (hit && found_g < 0) {
+        found_g = c0 + src;
+        found_l = t - base - src_excl;
+      }
+      base += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) {
+      s_group = found_g;
+      s_local = found_l;
+      s_total = base;
+      if (t == 0) *ntiles = min(base, max_tiles);
+    }
+  }
+  __syncthreads();
+  if (s_group < 0 || t >= s_total) return;
+  const int g = s_group;
+  const int first = groups[5 * g + 3], count = groups[5 * g + 4];
+  const int row0 = first + s_local * GM_NT, rows = min(GM_NT, count - s_local * GM_NT);
+  if (threadIdx.x == 0) table[t] = GroupedTile{g, row0, rows, 0};
+  const int nkc = K / GM_KC, nq = K / 256;
+  uint8_t* tile_base = staged + (size_t)t * nkc * 2 * GM_B_BYTES;
+  for (int j = warp; j < GM_NT; j += 8) {
+    const bool live = j < rows;
+    const float* src = x + (size_t)(row0 + (live ? j : 0)) * K;
+    float m = 0.0f;
+    if (live) {
+      for (int q = 0; q < nq; ++q) {
+        const float4 a = __ldg((const float4*)(src + 256 * q + 8 * lane));
+        const float4 b = __ldg((const float4*)(src + 256 * q + 8 * lane) + 1);
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(b.x), fabsf(b.y)), fmaxf(fabsf(b.z), fabsf(b.w))));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    }
+    const int e = stage_exponent(m);
+    const float scale = __uint_as_float((uint32_t)(e + 127) << 23);
+    for (int q = 0; q < nq; ++q) {
+      float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (live) {
+        const float4 a = __ldg((const float4*)(src + 256 * q + 8 * lane));
+        const float4 b = __ldg((const float4*)(src + 256 * q + 8 * lane) + 1);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      }
+      uint32_t hw[4], lw[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float s0 = v[2 * u] * scale, s1 = v[2 * u + 1] * scale;
+        const __half h0 = __float2half_rn(s0), h1 = __float2half_rn(s1);
+        hw[u] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+        const __half l0 = __float2half_rn(s0 - __half2float(h0)), l1 = __float2half_rn(s1 - __half2float(h1));
+        lw[u] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+      }
+      // columns 256q + 8 lane .. + 7: chunk kc = 4q + lane / 8, 16-byte piece c = lane % 8
+      const int kc = 4 * q + (lane >> 3), c = lane & 7;
+      uint8_t* blk = tile_base + (size_t)kc * 2 * GM_B_BYTES;
+      *(uint4*)(blk + sw128_offset(j, c)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *(uint4*)(blk + GM_B_BYTES + sw128_offset(j, c)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
+    if (lane == 0) inv[(size_t)t * GM_NT + j] = live ? __uint_as_float((uint32_t)(127 - e) << 23) : 0.0f;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// tcgen05 / TMA primitives (inline PTX, sm_100a)
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms 1024 bytes apart (SBO), version 1.
+D3_DEV uint64_t umma_desc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor, kind::f16: f32 accumulator, f16 A and B, both K-major, M = 128, N = 128.
+constexpr uint32_t GM_IDESC = (1u << 4) | ((uint32_t)(GM_NT >> 3) << 17) | ((uint32_t)(GM_M >> 4) << 24);
+
+D3_DEV void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` once every tcgen05.mma this thread issued so far has completed.
+D3_DEV void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+D3_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+D3_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Generic-proxy shared-memory writes made visible to the async proxy (the tensor cores' operand reads).
+D3_DEV void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+D3_DEV void tmem_alloc(uint32_t* dst_smem, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(cols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+D3_DEV void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+
+// 16 consecutive 32-bit columns of this warp's 32 lanes (lane = row): v[i] = column col + i of row (lane base + lane).
+D3_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 2-D tiled TMA load of box (x, y) of `map` into shared memory, completing on `bar`.
+D3_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"((uint64_t)map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+D3_DEV uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+struct GmArgs {
+  const uint8_t* staged;
+  const float* inv;
+  const GroupedTile* table;
+  const int* ntiles;
+  const int* groups;
+  const void* scale;       // fp8: fp32 blocks [E*N/128, K/128]; int8: fp32 [E*N]; W4/W6: e4m3 [E*N, K/16]
+  const float* s_channel;  // W4/W6
+  const float* codebook;   // W4
+  float* out;
+  int N, K, max_units;
+  int bank_rows;           // rows in the bank (E*N): slot indices beyond it are skipped
+};
+
+struct GmSmem {
+  static constexpr int a = 0;
+  static constexpr int b = a + GM_MMA_ST * GM_A_BYTES;
+  static constexpr int raw = b + GM_MMA_ST * 2 * GM_B_BYTES;
+  static constexpr int bars = raw + GM_RAW_ST * GM_RAW_BYTES;
+  // raw_full, raw_empty [GM_RAW_ST]; a_full, b_full, mma_empty [GM_MMA_ST]; acc_full, acc_empty [2]
+  static constexpr int nbars = 2 * GM_RAW_ST + 3 * GM_MMA_ST + 4;
+  static constexpr int tmem = bars + nbars * 8;
+  static constexpr int lut = tmem + 16;
+  static constexpr int total = lut + 64;
+  static constexpr int launch = total + 1024;  // slack to align the base to 1024 bytes
+};
+
+template <int FMT>
+__host__ __device__ constexpr int gm_raw_row_bytes() {
+  return FMT == FMT_FP8 || FMT == FMT_I8 ? 64 : FMT == FMT_W4 ? 32 : 48;
+}
+
+// The unit (tile, row block) a CTA takes k-th, or false past the end.
+D3_DEV bool gm_unit(const GmArgs& a, int ntiles, int u, int& tile, int& rb) {
+  const int RB = a.N / GM_M;
+  if (u >= ntiles * RB || u >= a.max_units) return false;
+  tile = u / RB;
+  rb = u - tile * RB;
+  return true;
+}
+
+// Convert one raw chunk (64 columns of weight row r) to f16 and store it swizzled into the A stage.
+template <int FMT>
+D3_DEV void gm_convert(const uint8_t* raw, uint8_t* astage, int r, uint32_t sbytes, const float* lut) {
+  if (FMT == FMT_FP8 || FMT == FMT_I8) {
+    const uint8_t* row = raw + r * 64;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int p = (i + (r >> 1)) & 3;  // rotation: four 16-byte reads per warp instruction hit distinct banks
+      const uint4 q = *(const uint4*)(row + 16 * p);
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+      uint32_t h[8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (FMT == FMT_FP8) {
+          h[2 * j] = e4m3x2_h2(w[j] & 0xFFFFu);
+          h[2 * j + 1] = e4m3x2_h2(w[j] >> 16);
+        } else {
+          const uint32_t t = w[j] ^ 0x80808080u;
+          h[2 * j] = i8x2_h2(t, 0x4140);
+          h[2 * j + 1] = i8x2_h2(t, 0x4342);
+        }
+      }
+      *(uint4*)(astage + sw128_offset(r, 2 * p)) = make_uint4(h[0], h[1], h[2], h[3]);
+      *(uint4*)(astage + sw128_offset(r, 2 * p + 1)) = make_uint4(h[4], h[5], h[6], h[7]);
+    }
+  } else {
+    // 64 columns = four 16-column groups: nibbles 8 bytes each (32 bytes per row), W6 high plane 4 bytes each
+    const uint8_t* low = raw + r * 32;
+    const uint8_t* high = raw + GM_M * 32 + r * 16;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int p = (i + (r >> 2)) & 3;
+      const uint2 lw = *(const uint2*)(low + 8 * p);
+      const uint32_t hb = FMT == FMT_W6 ? *(const uint32_t*)(high + 4 * p) : 0u;
+      const float s = e4m3_to_f32((sbytes >> (8 * p)) & 0xFFu);
+      float f[16];
+      if (FMT == FMT_W4)
+        dec_w4<16>(lw, s, lut, f);
+      else
+        dec_w6<16>(lw, hb, s, f);
+      uint32_t h[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) h[j] = pack_h2(f[2 * j], f[2 * j + 1]);
+      *(uint4*)(astage + sw128_offset(r, 2 * p)) = make_uint4(h[0], h[1], h[2], h[3]);
+      *(uint4*)(astage + sw128_offset(r, 2 * p + 1)) = make_uint4(h[4], h[5], h[6], h[7]);
+    }
+  }
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(GM_THREADS, 1)
+    grouped_mma_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap pmap, GmArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint64_t* bars = (uint64_t*)(smem + GmSmem::bars);
+  uint64_t* raw_full = bars;
+  uint64_t* raw_empty = bars + GM_RAW_ST;
+  uint64_t* a_full = bars + 2 * GM_RAW_ST;
+  uint64_t* b_full = a_full + GM_MMA_ST;
+  uint64_t* mma_empty = b_full + GM_MMA_ST;
+  uint64_t* acc_full = mma_empty + GM_MMA_ST;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = (uint32_t*)(smem + GmSmem::tmem);
+  float* lut = (float*)(smem + GmSmem::lut);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < GM_RAW_ST; ++i) {
+      mbar_init(raw_full + i, 1);
+      mbar_init(raw_empty + i, 4);
+    }
+    for (int i = 0; i < GM_MMA_ST; ++i) {
+      mbar_init(a_full + i, 4);
+      mbar_init(b_full + i, 1);
+      mbar_init(mma_empty + i, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(acc_full + i, 1);
+      mbar_init(acc_empty + i, 4);
+    }
+    fence_mbar_init();
+  }
+  if (FMT == FMT_W4 && threadIdx.x < 16) lut[threadIdx.x] = a.codebook[threadIdx.x];
+  if (warp == 2) tmem_alloc(tmem_slot, GM_TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int ntiles = *a.ntiles;
+  const int nkc = a.K / GM_KC;
+  const int G = gridDim.x;
+  bool ok = true;
+
+  if (warp == 0) {
+    // raw weights: TMA tiles of the unit's 128 rows, chunk by chunk
+    if (lane == 0) {
+      int rs = 0;
+      uint32_t rph = 0;
+      int tile, rb;
+      for (int u = blockIdx.x; ok && gm_unit(a, ntiles, u, tile, rb); u += G) {
+        const int slot = a.groups[5 * a.table[tile].group + 1];
+        const int wrow = slot * a.N + rb * GM_M;
+        if (slot < 0 || wrow + GM_M > a.bank_rows) continue;
+        for (int kc = 0; kc < nkc && ok; ++kc) {
+          ok = mbar_wait(raw_empty + rs, rph ^ 1);
+          if (!ok) break;
+          uint8_t* dst = smem + GmSmem::raw + rs * GM_RAW_BYTES;
+          if (FMT == FMT_FP8 || FMT == FMT_I8) {
+            mbar_arrive_expect_tx(raw_full + rs, GM_M * 64);
+            tma_load_2d(dst, &wmap, kc * 64, wrow, raw_full + rs);
+          } else if (FMT == FMT_W4) {
+            mbar_arrive_expect_tx(raw_full + rs, GM_M * 32);
+            tma_load_2d(dst, &wmap, kc * 32, wrow, raw_full + rs);
+          } else {
+            mbar_arrive_expect_tx(raw_full + rs, GM_M * 48);
+            tma_load_2d(dst, &wmap, kc * 32, wrow, raw_full + rs);
+            tma_load_2d(dst + GM_M * 32, &pmap, a.K / 2 + kc * 16, wrow, raw_full + rs);
+          }
+          if (++rs == GM_RAW_ST) {
+            rs = 0;
+            rph ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // staged activations: hi and lo operand blocks of each chunk
+    if (lane == 0) {
+      const uint64_t keep = policy_evict_last();
+      int ms = 0;
+      uint32_t mph = 0;
+      int tile, rb;
+      for (int u = blockIdx.x; ok && gm_unit(a, ntiles, u, tile, rb); u += G) {
+        const int slot = a.groups[5 * a.table[tile].group + 1];
+        if (slot < 0 || slot * a.N + rb * GM_M + GM_M > a.bank_rows) continue;
+        const uint8_t* src = a.staged + (size_t)tile * nkc * 2 * GM_B_BYTES;
+        for (int kc = 0; kc < nkc && ok; ++kc) {
+          ok = mbar_wait(mma_empty + ms, mph ^ 1);
+          if (!ok) break;
+          uint8_t* dst = smem + GmSmem::b + ms * 2 * GM_B_BYTES;
+          mbar_arrive_expect_tx(b_full + ms, 2 * GM_B_BYTES);
+          bulk_g2s(dst, src + (size_t)kc * 2 * GM_B_BYTES, 2 * GM_B_BYTES, b_full + ms, keep);
+          if (++ms == GM_MMA_ST) {
+            ms = 0;
+            mph ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 2) {
+    // MMA issuer
+    if (lane == 0) {
+      int ms = 0, folds = 0;
+      uint32_t mph = 0;
+      const int kbc = FMT == FMT_FP8 ? 128 / GM_KC : nkc;  // chunks per fold
+      int tile, rb;
+      for (int u = blockIdx.x; ok && gm_unit(a, ntiles, u, tile, rb); u += G) {
+        const int slot = a.groups[5 * a.table[tile].group + 1];
+        if (slot < 0 || slot * a.N + rb * GM_M + GM_M > a.bank_rows) continue;
+        uint32_t acc = 0;
+        for (int kc = 0; kc < nkc && ok; ++kc) {
+          if (kc % kbc == 0) {
+            const int region = folds & 1;
+            ok = mbar_wait(acc_empty + region, ((folds >> 1) & 1) ^ 1);
+            if (!ok) break;
+            tc_fence_after();
+            acc = tmem + region * GM_NT;
+          }
+          ok = mbar_wait(a_full + ms, mph) && mbar_wait(b_full + ms, mph);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t as = smem_u32(smem + GmSmem::a + ms * GM_A_BYTES);
+          const uint32_t bs = smem_u32(smem + GmSmem::b + ms * 2 * GM_B_BYTES);
+#pragma unroll
+          for (int ks = 0; ks < GM_KC / 16; ++ks) {
+            const uint64_t ad = umma_desc_sw128(as + 32 * ks);
+            umma_f16(acc, ad, umma_desc_sw128(bs + 32 * ks), GM_IDESC, (kc % kbc != 0 || ks != 0) ? 1u : 0u);
+            umma_f16(acc, ad, umma_desc_sw128(bs + GM_B_BYTES + 32 * ks), GM_IDESC, 1u);
+          }
+          umma_commit(mma_empty + ms);
+          if (kc % kbc == kbc - 1) {
+            umma_commit(acc_full + (folds & 1));
+            ++folds;
+          }
+          if (++ms == GM_MMA_ST) {
+            ms = 0;
+            mph ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp < GM_FOLD0) {
+    // converters: thread = weight row of the unit
+    const int r = threadIdx.x - GM_CONV0 * 32;
+    int rs = 0, ms = 0;
+    uint32_t rph = 0, mph = 0;
+    int tile, rb;
+    for (int u = blockIdx.x; ok && gm_unit(a, ntiles, u, tile, rb); u += G) {
+      const int slot = a.groups[5 * a.table[tile].group + 1];
+      const int wrow = slot * a.N + rb * GM_M;
+      if (slot < 0 || wrow + GM_M > a.bank_rows) continue;
+      const uint8_t* srow = FMT == FMT_W4 || FMT == FMT_W6
+                                ? (const uint8_t*)a.scale + (size_t)(wrow + r) * (a.K / 16)
+                                : nullptr;
+      for (int kc = 0; kc < nkc && ok; ++kc) {
+        const uint32_t sbytes = srow ? __ldg((const uint32_t*)(srow + 4 * kc)) : 0u;
+        ok = mbar_wait(raw_full + rs, rph) && mbar_wait(mma_empty + ms, mph ^ 1);
+        if (!ok) break;
+        gm_convert<FMT>(smem + GmSmem::raw + rs * GM_RAW_BYTES, smem + GmSmem::a + ms * GM_A_BYTES, r, sbytes, lut);
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(raw_empty + rs);
+          mbar_arrive(a_full + ms);
+        }
+        if (++rs == GM_RAW_ST) {
+          rs = 0;
+          rph ^= 1;
+        }
+        if (++ms == GM_MMA_ST) {
+          ms = 0;
+          mph ^= 1;
+        }
+      }
+    }
+  } else {
+    // fold + epilogue: this warp's quarter of the 128 accumulator lanes (weight rows)
+    const int quarter = warp & 3;
+    const int r = 32 * quarter + lane;
+    const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
+    const int kbc = FMT == FMT_FP8 ? 128 / GM_KC : nkc;
+    const int nfold = nkc / kbc;
+    int folds = 0;
+    int tile, rb;
+    for (int u = blockIdx.x; ok && gm_unit(a, ntiles, u, tile, rb); u += G) {
+      const GroupedTile tl = a.table[tile];
+      const int slot = a.groups[5 * tl.group + 1];
+      const int wrow = slot * a.N + rb * GM_M;
+      if (slot < 0 || wrow + GM_M > a.bank_rows) {
+        if (slot < 0 || wrow >= a.bank_rows) record_fault(FAULT_BAD_SLOT);
+        continue;
+      }
+      const float* inv = a.inv + (size_t)tile * GM_NT;
+      float* dst = a.out + (size_t)tl.row0 * a.N + rb * GM_M + r;
+      if (FMT == FMT_FP8) {
+        // one fold per 128 columns: acc += block scale x partial
+        float acc[GM_NT];
+#pragma unroll
+        for (int j = 0; j < GM_NT; ++j) acc[j] = 0.0f;
+        for (int f = 0; f < nfold && ok; ++f) {
+          const int region = folds & 1;
+          ok = mbar_wait(acc_full + region, (folds >> 1) & 1);
+          if (!ok) break;
+          tc_fence_after();
+          const float s = __ldg((const float*)a.scale + (size_t)(wrow / 128) * (a.K / 128) + f);
+#pragma unroll
+          for (int c = 0; c < GM_NT / 16; ++c) {
+            float v[16];
+            tmem_ld16(tmem + lane_base + region * GM_NT + 16 * c, v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) acc[16 * c + i] = fmaf(s, v[i], acc[16 * c + i]);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(acc_empty + region);
+          ++folds;
+        }
+        if (!ok) break;
+#pragma unroll
+        for (int j = 0; j < GM_NT; ++j)
+          if (j < tl.rows) dst[(size_t)j * a.N] = acc[j] * __ldg(inv + j);
+      } else {
+        // one fold per unit: the row scale (int8 scale, W4/W6 s_channel) and each row's 2^-e, straight to out
+        const int region = folds & 1;
+        ok = mbar_wait(acc_full + region, (folds >> 1) & 1);
+        if (!ok) break;
+        tc_fence_after();
+        const float rs = FMT == FMT_I8 ? __ldg((const float*)a.scale + wrow + r) : __ldg(a.s_channel + wrow + r);
+#pragma unroll 1
+        for (int c = 0; c < GM_NT / 16; ++c) {
+          float v[16];
+          tmem_ld16(tmem + lane_base + region * GM_NT + 16 * c, v);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int j = 16 * c + i;
+            if (j < tl.rows) dst[(size_t)j * a.N] = v[i] * __ldg(inv + j) * rs;
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty + region);
+        ++folds;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, GM_TMEM_COLS);
+  }
+}
+
+}  // namespace d3

@@ -6,7 +6,8 @@ and every launch goes on the device's current stream, so calls can be captured i
     library is missing or the device is not an sm_100 GPU: there is no fallback implementation;
   - `route` and `weighted_sum` also take several rows at once;
   - `await_cpu` (the CPU-expert handshake) is not provided: this path has no CPU side;
-  - `moe_decode` is new: the whole resident decode (gate_up, SwiGLU, down, combine) for 1..16 rows in one pass.
+  - `moe_decode` is new: the whole resident decode (gate_up, SwiGLU, down, combine) for 1..16 rows in one pass;
+  - `grouped_mma` is new: the grouped kernels on the tensor cores for banks held whole on the GPU.
 """
 import functools
 
@@ -192,6 +193,37 @@ def grouped_codes(x, groups, slot_fields, host_fields, codebook, bits, n):
                                      _ptr(host_fields["s_channel"]), _ptr(codebook), int(bits), _ptr(out), n,
                                      x.shape[1], _bank_rows(host_fields, "_qdata", n),
                                      _bank_rows(slot_fields, "_qdata", n), _stream(x.device)), "grouped_codes")
+    return out
+
+
+def grouped_tiles(counts):
+    """Tiles of 128 rows the tensor-core grouped kernel runs for groups of these row counts."""
+    return sum((int(n) + 127) // 128 for n in counts)
+
+
+def grouped_mma_fits(n, k):
+    """Whether an [n, k] bank runs on the tensor-core grouped kernel (n % 128 == 0, k % 256 == 0)."""
+    return n % 128 == 0 and k % 256 == 0 and k >= 256
+
+
+def grouped_mma(kind, x, groups, fields, codebook, n, tiles):
+    """[rows, n] float32 for x's rows (float32, sorted by expert; rotated for int8/W4/W6) through their experts, on
+    the tensor cores, for a bank held whole on the GPU: the grouped_fp8 / grouped_int8 / grouped_codes results with
+    every group's slot = its expert's index in `fields` (drama3/offload.py:126-149). groups [g, 5] int32 on the GPU;
+    tiles = grouped_tiles(row counts). Rows outside every group are left unset."""
+    fmt = _lib.FORMATS[kind]
+    wkey = "weight" if kind == "fp8" else "_qdata"
+    w = fields[wkey]
+    scale = fields["scale"].view(torch.uint8) if kind in ("w4", "w6") else fields["scale"]
+    x = x.contiguous()
+    K = x.shape[1]
+    out = torch.empty((x.shape[0], n), dtype=torch.float32, device=x.device)
+    size = lib().d3_grouped_mma_workspace(int(tiles), K)
+    ws = torch.empty((max(size, 256),), dtype=torch.uint8, device=x.device)
+    with _on(x.device):
+        check(lib().d3_grouped_mma(fmt, _ptr(x), _ptr(groups), groups.shape[0], int(tiles), _ptr(w), _ptr(scale),
+                                   _ptr(fields.get("s_channel")), _ptr(codebook), w.shape[0], _ptr(out), n, K,
+                                   _ptr(ws), ws.numel(), _stream(x.device)), "grouped_mma")
     return out
 
 

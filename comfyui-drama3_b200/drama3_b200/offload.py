@@ -197,16 +197,38 @@ def _scatter_sum(sorted_out, order, topk_weight, num_tokens, top_k):
     return out.view(num_tokens, top_k, -1).sum(dim=1)
 
 
+def _grouped_resident(kind, x, groups, tiles, bank, rows, codebook):
+    """One bank's grouped GEMM over banks held whole on the GPU: the tensor-core kernel where the shape allows it,
+    else the reference-API grouped kernel (slot = expert)."""
+    width = x.shape[1]
+    if kernels.grouped_mma_fits(rows, width):
+        return kernels.grouped_mma(kind, x, groups, bank, codebook, rows, tiles)
+    if kind == "fp8":
+        return kernels.grouped_fp8(x, groups, bank, bank, rows)
+    return quantized_grouped(kind, x, groups, bank, bank, rows, codebook)
+
+
 def resident_prefill(x, topk_idx, topk_weight, banks, rows, kind, codebooks, num_experts):
-    """Many rows x [T, H] through banks held whole on the GPU: one grouped kernel per bank
-    (drama3/offload.py:138-149). [T, H] in x's dtype."""
+    """Many rows x [T, H] through banks held whole on the GPU (drama3/offload.py:138-149): rows sorted by expert, one
+    grouped GEMM per bank on the tensor cores, SwiGLU between (with the ConvRot rotations for int8/W4/W6), scattered
+    back, weighted and summed. [T, H] in x's dtype."""
     num_tokens, top_k = topk_idx.shape
     order, counts = _sort_by_expert(topk_idx, num_experts)
     offsets = [0, *itertools.accumulate(counts)]
     groups = [(e, e, 0, offsets[e], n) for e, n in enumerate(counts) if n]
     groups = torch.tensor(groups, dtype=torch.int32).to(x.device)
+    tiles = kernels.grouped_tiles(counts)
     always = torch.ones((1,), dtype=torch.int32, device=x.device)
-    sorted_out = grouped_experts(x[order // top_k], groups, banks, banks, rows, kind, codebooks, always)
+    gate_up, down = banks
+    sorted_x = x[order // top_k].float()
+    if kind == "fp8":
+        gate, up = _grouped_resident(kind, sorted_x, groups, tiles, gate_up, rows[0], None).chunk(2, dim=-1)
+        sorted_out = _grouped_resident(kind, nn.functional.silu(gate) * up, groups, tiles, down, rows[1], None)
+    else:
+        hidden = _grouped_resident(kind, kernels.rotate(sorted_x, always), groups, tiles, gate_up, rows[0],
+                                   codebooks[0])
+        sorted_out = _grouped_resident(kind, kernels.rotate(hidden, always, swiglu=True), groups, tiles, down,
+                                       rows[1], codebooks[1])
     return _scatter_sum(sorted_out, order, topk_weight, num_tokens, top_k).to(x.dtype)
 
 
@@ -567,8 +589,9 @@ class ExpertStore:
         num_tokens, top_k = topk_idx.shape
         order, counts = _sort_by_expert(topk_idx, banks[0].num_experts)
         sorted_out = self.prefill_kernels(layer, banks, x[order // top_k], counts)
-        out = torch.empty_like(sorted_out)
-        out[order] = sorted_out * topk_weight.reshape(-1)[order].unsqueeze(1)
+        weighted = sorted_out * topk_weight.reshape(-1)[order].unsqueeze(1)
+        out = torch.empty_like(weighted)
+        out[order] = weighted
         return out.view(num_tokens, top_k, -1).sum(dim=1)
 
     def prefill_kernels(self, layer, banks, sorted_x, counts):

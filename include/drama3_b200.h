@@ -103,6 +103,18 @@ int d3_grouped_codes(const float* x, int x_rows, const int* groups, int n_groups
                      const float* codebook, int bits, float* out, int N, int K, int num_experts, int slots,
                      void* stream);
 
+/* The grouped kernels above on the tensor cores, for banks held whole on the GPU (every group's `slot` column is the
+ * expert's index in the bank; `fill` is ignored): the same outputs as d3_grouped_fp8 / _int8 / _codes for
+ * drama3/offload.py:126-149 (resident_prefill), up to summation order. fmt = D3_FMT_*; weight / scale / s_channel /
+ * codebook are the bank's fields (fp8: e4m3 rows + fp32 128x128 blocks; int8: rows + fp32 row scales; W4/W6: codes
+ * + e4m3 group-16 scales + fp32 s_channel, codebook float[16] for W4), bank_rows = rows in the bank (E * N).
+ * tiles = sum over groups of ceil(rows / 128) (an upper bound is allowed). N % 128 == 0, K % 256 == 0; x, out and
+ * weight 16-byte aligned, workspace 256-byte aligned, d3_grouped_mma_workspace(tiles, K) bytes (no initial state). */
+size_t d3_grouped_mma_workspace(int tiles, int K);
+int d3_grouped_mma(int fmt, const float* x, const int* groups, int n_groups, int tiles, const void* weight,
+                   const void* scale, const float* s_channel, const float* codebook, int bank_rows, float* out, int N,
+                   int K, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Bytes of workspace d3_moe_decode needs for M rows, top-k and expert width I. */
 size_t d3_moe_decode_workspace(int M, int k, int I);
 

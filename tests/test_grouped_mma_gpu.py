@@ -1,0 +1,91 @@
+"""The tensor-core grouped GEMM (tcgen05) against the reference-API grouped kernels (themselves matched to the
+reference's kernels) and the oracle: every format, both projections' shapes, ragged groups (empty, 1, 127, 128, 129,
+several tiles), rows outside every group left untouched, an upper-bound tile count."""
+import numpy as np
+import pytest
+import torch
+
+import gpu_data as gd
+from drama3_b200 import kernels
+from oracle import moe
+
+pytestmark = pytest.mark.gpu
+E = 16
+COUNTS = [0, 1, 127, 128, 129, 300, 5, 0, 64, 256, 17, 2, 0, 90, 33, 3]
+
+
+def grouped_case(kind, N, K, seed, device):
+    bank = gd.rand_bank(kind, E, N, K, seed, device)
+    offsets = np.concatenate([[0], np.cumsum(COUNTS)])
+    rows = int(offsets[-1]) + 7  # 7 rows past the last group stay untouched
+    gen = torch.Generator().manual_seed(seed + 1)
+    x = torch.randn((rows, K), generator=gen)
+    x[3] *= 1e-3  # rows of very different magnitudes
+    x[200] *= 50.0
+    x = x.to(device)
+    order = torch.randperm(E, generator=gen).tolist()  # groups listed out of expert order
+    groups = torch.tensor([(e, e, 0, int(offsets[e]), COUNTS[e]) for e in order if COUNTS[e]], dtype=torch.int32)
+    return bank, x, groups.to(device)
+
+
+def reference_grouped(kind, x, groups, bank, cb, N):
+    """The reference-API grouped kernel (slot = expert), over the same banks."""
+    if kind == "fp8":
+        return kernels.grouped_fp8(x, groups, bank, bank, N)
+    if kind == "int8":
+        return kernels.grouped_int8(x, groups, bank, bank, N)
+    return kernels.grouped_codes(x, groups, bank, bank, cb, int(kind[1]), N)
+
+
+@pytest.mark.parametrize("kind", gd.KINDS)
+@pytest.mark.parametrize("N,K", [(1536, 2048), (2048, 768)])
+def test_grouped_mma_matches_grouped_kernels(cuda, kind, N, K):
+    bank, x, groups = grouped_case(kind, N, K, 11 + N + K, cuda)
+    cb = gd.codebooks(kind, cuda)[0]
+    tiles = kernels.grouped_tiles(COUNTS)
+    got = kernels.grouped_mma(kind, x, groups, bank, cb, N, tiles)
+    want = reference_grouped(kind, x, groups, bank, cb, N)
+    live = int(sum(COUNTS))
+    assert gd.rel_l2(got[:live], want[:live]) <= 1e-5
+    # per row, not only overall
+    err = (got[:live] - want[:live]).norm(dim=1) / want[:live].norm(dim=1).clamp_min(1e-30)
+    assert float(err.max()) <= 1e-4
+
+
+@pytest.mark.parametrize("kind", ["fp8", "w6"])
+def test_grouped_mma_tile_bound_and_repeat(cuda, kind):
+    """An upper-bound tile count runs the same tiles; repeated calls give identical rows (no state kept)."""
+    N, K = 1536, 2048
+    bank, x, groups = grouped_case(kind, N, K, 5, cuda)
+    cb = gd.codebooks(kind, cuda)[0]
+    exact = kernels.grouped_tiles(COUNTS)
+    a = kernels.grouped_mma(kind, x, groups, bank, cb, N, exact)
+    b = kernels.grouped_mma(kind, x, groups, bank, cb, N, exact + 5)
+    c = kernels.grouped_mma(kind, x, groups, bank, cb, N, exact)
+    live = int(sum(COUNTS))
+    assert torch.isfinite(a[:live]).all()
+    assert torch.equal(a[:live], b[:live]) and torch.equal(a[:live], c[:live])
+
+
+@pytest.mark.parametrize("kind", gd.KINDS)
+def test_grouped_mma_matches_oracle(cuda, kind):
+    """A small case against the numpy restatement of the reference's grouped kernels."""
+    N, K = 256, 512
+    bank = gd.rand_bank(kind, 4, N, K, 21, cuda)
+    gen = torch.Generator().manual_seed(22)
+    x = torch.randn((200, K), generator=gen).to(cuda)
+    groups = torch.tensor([(2, 2, 0, 0, 150), (0, 0, 0, 150, 1), (3, 3, 0, 151, 49)], dtype=torch.int32).to(cuda)
+    cb = gd.codebooks(kind, cuda)[0]
+    got = kernels.grouped_mma(kind, x, groups, bank, cb, N, kernels.grouped_tiles([150, 1, 49]))
+    npb = gd.to_np_bank(bank)
+    want = moe.grouped(kind, x.cpu().numpy(), groups.cpu().numpy(), npb, npb, N,
+                       None if cb is None else cb.cpu().numpy())
+    assert gd.rel_l2(got, want) <= 1e-5
+
+
+def test_grouped_mma_rejects_bad_shapes(cuda):
+    bank = gd.rand_bank("fp8", 2, 256, 512, 1, cuda)
+    x = torch.zeros((4, 512), device=cuda)
+    groups = torch.tensor([(0, 0, 0, 0, 4)], dtype=torch.int32, device=cuda)
+    with pytest.raises(Exception):
+        kernels.grouped_mma("fp8", x[:, :384].contiguous(), groups, bank, None, 256, 1)  # K % 256 != 0

@@ -105,7 +105,7 @@ def device_state_consistent(pool):
 
 @pytest.mark.parametrize("kind", ["fp8", "int8", "w4"])
 def test_expert_store_matches_resident(cuda, kind):
-    """Two layers of experts in pinned host memory behind an 8-slot cache: 6 decode steps and a 40-row prompt pass,
+    """Two layers of 16 experts in pinned host memory behind a 24-slot cache: 6 decode steps and a 40-row prompt pass,
     bit for bit against the same experts held whole on the GPU (hits read a slot, misses read host memory and fill a
     slot, all through the same kernels); every slot then holds its owner's bytes."""
     store = offload.ExpertStore(cache_bytes=0, pin=True)
@@ -124,10 +124,10 @@ def test_expert_store_matches_resident(cuda, kind):
             banks = ({n: t.to(cuda) for n, t in gu_bank.items()}, {n: t.to(cuda) for n, t in dn_bank.items()})
             layers.append(store.add(type("X", (), {"gate_up_proj": gu, "down_proj": dn})()))
         device_banks.append(banks)
-    store.cache_bytes = 8 * sum(t[:b.rows(n)].nbytes for b in store.banks[0] for n, t in b.fields.items())
+    store.cache_bytes = 24 * sum(t[:b.rows(n)].nbytes for b in store.banks[0] for n, t in b.fields.items())
     cbs = gd.codebooks(kind, cuda)
     with store.session(cuda):
-        assert store.cache.count == 8 and all(m.sync_free(cuda) for m in layers)
+        assert store.cache.count == 24 and all(m.sync_free(cuda) for m in layers)
         for step in range(6):
             x = gd.rand_rows(1, H, 80 + step, cuda)
             for layer, module in enumerate(layers):
@@ -152,8 +152,9 @@ def test_expert_store_matches_resident(cuda, kind):
             always = torch.ones((1,), dtype=torch.int32, device=cuda)
             so = offload.grouped_experts(xt[order // 8], groups, device_banks[layer], device_banks[layer], (2 * I, H),
                                          kind, cbs, always).to(xt.dtype)
-            want = torch.empty_like(so)
-            want[order] = so * wt.reshape(-1)[order].unsqueeze(1)
+            weighted = so * wt.reshape(-1)[order].unsqueeze(1)
+            want = torch.empty_like(weighted)
+            want[order] = weighted
             assert torch.equal(got, want.view(40, 8, -1).sum(dim=1)), layer
         torch.cuda.synchronize()
         pool = store.cache
