@@ -114,6 +114,81 @@ def make_layers(device, lines, seed=4, n_layers=LAYERS):
     return layers, torch.stack(ids).to(device), torch.stack(weights).to(device)
 
 
+def rand_bank(kind, n, k, gen, device):
+    """A flat bank [E * n, ...] of random valid codes in the reference layout of `kind` (fp8 or w6)."""
+    if kind == "fp8":
+        w = torch.randint(0, 254, (E * n, k), generator=gen, device=device, dtype=torch.uint8)
+        w = torch.where(w >= 0x7F, w + 1, w)
+        s = torch.rand((E * n // 128, k // 128), generator=gen, device=device) * 1e-4 + 5e-5
+        return {"weight": w, "scale": s}
+    q = torch.randint(0, 256, (E * n, 3 * k // 4), generator=gen, device=device, dtype=torch.uint8)
+    g = torch.randint(0x30, 0x50, (E * n, k // 16), generator=gen, device=device, dtype=torch.uint8)
+    c = torch.rand((E * n,), generator=gen, device=device) * 2e-4 + 1e-4
+    return {"_qdata": q, "scale": g, "s_channel": c}
+
+
+def prefill_leg(device, steps, tokens=2048, seed=3):
+    """one MoE layer's prompt pass of `tokens` rows, router logits biased so expert load is
+    Zipf(1.1)-skewed (bias_e = -1.1 ln r_e, r a seeded permutation of ranks 1..128), W6 (reference layout) and fp8
+    experts. Times the whole resident_prefill (sort, grouped GEMMs on the tensor cores, combine) with CUDA events,
+    and the reference's own grouped kernels (oracle/_ref) on the same inputs."""
+    from drama3_b200 import offload
+    gen = torch.Generator().manual_seed(seed)
+    bias = -1.1 * torch.log(torch.randperm(E, generator=gen).float() + 1)
+    w, ids = torch.softmax(torch.randn((tokens, E), generator=gen) + bias, -1).topk(K_TOP, dim=-1)
+    w = (w / w.sum(-1, keepdim=True)).to(torch.bfloat16)
+    x = torch.randn((tokens, H), generator=gen).to(torch.bfloat16)
+    counts = torch.bincount(ids.reshape(-1), minlength=E)
+    x, ids, w = x.to(device), ids.to(device), w.to(device)
+    flops = 2.0 * tokens * K_TOP * (2 * I * H + H * I)
+    bf16_peak = 1590.0
+    try:
+        bf16_peak = float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"])
+    except (OSError, KeyError, ValueError):
+        pass
+    dgen = torch.Generator(device=device).manual_seed(seed)
+    out = {"tokens": tokens, "top_k": K_TOP, "largest_group": int(counts.max()), "median_group": int(counts.median()),
+           "flops_per_layer": flops, "peak_tflops": bf16_peak,
+           "note": "activations enter the MMA as two f16 terms (hi + lo), so the tensor pipe does twice the algorithmic "
+                   "flops; the frac is algorithmic flops / time / measured dense bf16 peak"}
+    for kind in ("w6", "fp8"):
+        banks = (rand_bank(kind, 2 * I, H, dgen, device), rand_bank(kind, H, I, dgen, device))
+
+        def run():
+            return offload.resident_prefill(x, ids, w, banks, (2 * I, H), kind, (None, None), E)
+
+        for _ in range(2):
+            run()
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = max(3, min(steps, 10))
+        s0.record()
+        for _ in range(n):
+            run()
+        s1.record()
+        torch.cuda.synchronize()
+        us = 1e3 * s0.elapsed_time(s1) / n
+        leg = {"us_per_layer": us, "tflops": flops / us / 1e6, "frac": flops / us / 1e6 / bf16_peak,
+               "tokens_per_s": tokens / us * 1e6}
+        try:
+            from oracle import ref_gpu
+            if ref_gpu.available():
+                ref_gpu.resident_prefill(x, ids, w, banks, (2 * I, H), kind, (None, None), E)
+                torch.cuda.synchronize()
+                s0.record()
+                ref_gpu.resident_prefill(x, ids, w, banks, (2 * I, H), kind, (None, None), E)
+                s1.record()
+                torch.cuda.synchronize()
+                rus = 1e3 * s0.elapsed_time(s1)
+                leg["reference_gpu_us_per_layer"] = rus
+                leg["speedup_vs_reference_gpu"] = rus / us
+        except Exception as exc:  # the comparison must not sink the bench line
+            leg["reference_gpu"] = {"error": repr(exc)[:200]}
+        out[kind] = leg
+        del banks
+    return out
+
+
 def unique_bytes(ids):
     """Algorithmic bytes of one step: each layer's unique experts, plus its rows in and out (bf16)."""
     total = 0
@@ -200,7 +275,8 @@ def main():
     ap.add_argument("--impl", choices=("mine", "reference"), default="mine")
     ap.add_argument("--lines", type=int, default=16)
     ap.add_argument("--layers", type=int, default=LAYERS, help="layers per step (48: the benchmark; 4: small case)")
-    ap.add_argument("--no-extras", action="store_true", help="skip e2e / reference GPU / CPU legs")
+    ap.add_argument("--no-extras", action="store_true", help="skip e2e / reference GPU / prefill / CPU legs")
+    ap.add_argument("--prefill-only", action="store_true", help="print only the prompt-pass leg (BASELINE configs[3])")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -222,6 +298,10 @@ def main():
 
     from drama3_b200 import kernels
 
+    if args.prefill_only:
+        if rank == 0:
+            print(json.dumps({"prefill": prefill_leg(device, args.steps)}), flush=True)
+        return
     n_layers = args.layers
     layers, ids, weights = make_layers(device, args.lines, seed=4 + rank, n_layers=n_layers)
     x = torch.randn((args.lines, H), generator=torch.Generator().manual_seed(7 + rank)).to(torch.bfloat16).to(device)
@@ -325,6 +405,11 @@ def main():
                                                    "per step"}
         except Exception as exc:  # the comparison leg must not sink the bench line
             extras["reference_gpu"] = {"error": repr(exc)[:200]}
+        # a prompt pass on the tensor cores (BASELINE configs[3] shape)
+        try:
+            extras["prefill"] = prefill_leg(device, args.steps)
+        except Exception as exc:
+            extras["prefill"] = {"error": repr(exc)[:200]}
         # the reference's CPU path on the host cores (bounded sample)
         tps, secs, threads, sample = cpu_reference(args.lines, n_layers=n_layers)
         extras["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",

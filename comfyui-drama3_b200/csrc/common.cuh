@@ -17,6 +17,7 @@ enum : unsigned {
   FAULT_WAIT_TIMEOUT = 1u,  // an mbarrier or flag wait ran past its time limit
   FAULT_BAD_EXPERT = 2u,    // an expert id outside [0, E): the pair was skipped
   FAULT_BAD_SLOT = 4u,      // a slot index outside [0, count): the expert was skipped
+  FAULT_TILES = 8u,         // the groups need more row tiles than the caller sized: the excess rows were skipped
 };
 __device__ unsigned int g_fault;
 

@@ -98,8 +98,13 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// A 2-D byte tensor [rows, row_bytes] read in boxes of box_bytes x 128 rows, no swizzle.
+// A 2-D byte tensor [rows, row_bytes] read in boxes of box_bytes x 128 rows, with the shared-memory swizzle of that
+// row width (128, 64 or 32 bytes).
 bool byte_tile_map(CUtensorMap* map, const void* base, uint64_t row_bytes, uint64_t rows, uint32_t box_bytes) {
+  const CUtensorMapSwizzle swizzle = box_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                     : box_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                     : box_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                                       : CU_TENSOR_MAP_SWIZZLE_NONE;
   PFN_cuTensorMapEncodeTiled_v12000 fn = tensor_map_encoder();
   if (!fn) return false;
   cuuint64_t dims[2] = {row_bytes, rows};
@@ -107,7 +112,7 @@ bool byte_tile_map(CUtensorMap* map, const void* base, uint64_t row_bytes, uint6
   cuuint32_t box[2] = {box_bytes, 128};
   cuuint32_t elem[2] = {1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, elem,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -324,18 +329,23 @@ int d3_grouped_codes(const float* x, int x_rows, const int* groups, int n_groups
 // ------------------------------------------------------------------------------------------------------------
 // Grouped expert GEMM on the tensor cores (banks held whole on the GPU).
 
+int d3_grouped_mma_tile_rows(void) { return d3::GM_NT; }
+
 size_t d3_grouped_mma_workspace(int tiles, int K) {
   if (tiles < 0 || K < 256) return 0;
   return d3::gm_workspace_bytes(tiles, K);
 }
 
-int d3_grouped_mma(int fmt, const float* x, const int* groups, int n_groups, int tiles, const void* weight,
-                   const void* scale, const float* s_channel, const float* codebook, int bank_rows, float* out, int N,
-                   int K, void* workspace, size_t workspace_bytes, void* stream) {
+int d3_grouped_mma(int fmt, const void* x, int x_bf16, const int64_t* row_index, int mode, const int* groups,
+                   int n_groups, int tiles, const void* weight, const void* scale, const float* s_channel,
+                   const float* codebook, int bank_rows, float* out, int N, int K, void* workspace,
+                   size_t workspace_bytes, void* stream) {
   DeviceInfo d;
   if (int st = device_info(&d)) return st;
   if (fmt < d3::FMT_FP8 || fmt > d3::FMT_W6 || n_groups < 0 || tiles < 0) return D3_ERR_ARG;
-  if (N < d3::GM_M || N % d3::GM_M || K < 256 || K % 256 || bank_rows < N || bank_rows % d3::GM_M) return D3_ERR_ARG;
+  if (mode < 0 || mode > (d3::GM_ROTATE | d3::GM_SWIGLU)) return D3_ERR_ARG;
+  if (N < d3::GM_M || N % d3::GM_M || K < 256 || K % 256 || K > 2048 || bank_rows < N || bank_rows % d3::GM_M)
+    return D3_ERR_ARG;
   if (!x || !groups || !weight || !scale || !out || !workspace) return D3_ERR_ARG;
   if ((fmt == d3::FMT_W4 || fmt == d3::FMT_W6) && !s_channel) return D3_ERR_ARG;
   if (fmt == d3::FMT_W4 && !codebook) return D3_ERR_ARG;
@@ -351,12 +361,13 @@ int d3_grouped_mma(int fmt, const float* x, const int* groups, int n_groups, int
   int* ntiles = (int*)(table + tiles);
   CUtensorMap wmap, pmap;
   const uint64_t row_bytes = (uint64_t)d3::fmt_row_bytes(fmt, K);
-  const uint32_t box = fmt == d3::FMT_FP8 || fmt == d3::FMT_I8 ? 64 : 32;
+  // one raw stage = 128 columns: fp8 / int8 128 bytes per row; W4 / W6 nibbles 64; the W6 high plane 32
+  const uint32_t box = fmt == d3::FMT_FP8 || fmt == d3::FMT_I8 ? 128 : 64;
   if (!byte_tile_map(&wmap, weight, row_bytes, (uint64_t)bank_rows, box)) return D3_ERR_ARG;
   pmap = wmap;
-  if (fmt == d3::FMT_W6 && !byte_tile_map(&pmap, weight, row_bytes, (uint64_t)bank_rows, 16)) return D3_ERR_ARG;
-  if (int st = launch(d3::gm_stage_kernel, dim3(tiles), dim3(256), 0, s, false, x, groups, n_groups, K, tiles, staged,
-                      inv, table, ntiles))
+  if (fmt == d3::FMT_W6 && !byte_tile_map(&pmap, weight, row_bytes, (uint64_t)bank_rows, 32)) return D3_ERR_ARG;
+  if (int st = launch(d3::gm_stage_kernel, dim3(tiles), dim3(256), 0, s, false, x, x_bf16, row_index, mode, groups,
+                      n_groups, K, tiles, staged, inv, table, ntiles))
     return st;
   const int units = tiles * (N / d3::GM_M);
   d3::GmArgs a = {staged, inv, table, ntiles, groups, scale, s_channel, codebook, out, N, K, units, bank_rows};
@@ -375,6 +386,17 @@ int d3_grouped_mma(int fmt, const float* x, const int* groups, int n_groups, int
 #undef D3_GM_CASE
   }
   return D3_ERR_ARG;
+}
+
+int d3_prefill_combine(const float* sorted, const int64_t* pos, const void* weights, int w_bf16, int T, int k, int H,
+                       void* out, int out_f32, void* stream) {
+  DeviceInfo d;
+  if (int st = device_info(&d)) return st;
+  if (T < 0 || k < 1 || k > 64 || H < 4 || H % 4 || !sorted || !pos || !weights || !out) return D3_ERR_ARG;
+  if (!aligned(sorted, 16) || !aligned(out, out_f32 ? 16 : 8)) return D3_ERR_ALIGN;
+  if (T == 0) return D3_OK;
+  return launch(d3::gm_combine_kernel, dim3(T), dim3(256), 0, (cudaStream_t)stream, false, sorted, pos, weights, w_bf16,
+                k, H, out, out_f32);
 }
 
 // ------------------------------------------------------------------------------------------------------------

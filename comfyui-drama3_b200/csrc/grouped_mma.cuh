@@ -4,7 +4,7 @@
 // the GPU.
 //
 // Work unit = (token tile of up to 128 rows of one group, block of 128 weight rows). Per unit, D[128 x 128] (weight
-// rows x tokens) accumulates in tensor memory (tcgen05.mma kind::f16, M = 128, N = 128, K = 16, f32 accumulate):
+// rows x tokens) accumulates in tensor memory (tcgen05.mma kind::f16, M = 128, N <= 128, K = 16, f32 accumulate):
 //   A = 128 weight rows, converted exactly to f16 in shared memory (every e4m3 value, every int8 and every int8-grid
 //       code is an f16), K-major with the 128-byte swizzle;
 //   B = the tile's rows as two f16 terms, hi = f16(x * 2^e) and lo = f16(x * 2^e - hi) (e per row puts its max in
@@ -15,8 +15,11 @@
 // once per unit and apply the row scale (int8 scale, W4/W6 s_channel).
 //
 // Warps (352 threads, one CTA per SM, persistent over units):
-//   0     raw-weight producer: 2-D TMA tile loads (64 columns x 128 rows of bytes) into a 6-stage ring
-//   1     activation producer: two 16 KB bulk copies (hi, lo) per 64-column chunk into a 3-stage ring
+//   0     raw-weight producer: 2-D TMA tile loads (128 columns x 128 rows, hardware-swizzled so the converters'
+//         row reads hit distinct banks) into a 4-stage ring of 16 KB
+//   1     activation producer: two bulk copies (hi, lo) per 64-column chunk into a 3-stage ring; a tile of R rows
+//         copies and multiplies only its first round_up(R, 16) rows (MMA N = that), which matters for the many
+//         small groups of a skewed routing
 //   2     MMA issuer (one elected thread) and owner of the 256 tensor-memory columns
 //   3-6   converters: thread = weight row, raw bytes -> f16, written swizzled into the A stage
 //   7-10  fold + epilogue: tcgen05.ld of their 32-lane quarter, scale, accumulate, write fp32 rows
@@ -27,21 +30,23 @@
 
 #include "formats.cuh"
 #include "moe_decode.cuh"
+#include "rotate.cuh"
 
 namespace d3 {
 
 constexpr int GM_M = 128;              // weight rows per unit (one fp8 scale block)
 constexpr int GM_NT = 128;             // token rows per tile
-constexpr int GM_KC = 64;              // columns per chunk: one 128-byte swizzle atom of f16
-constexpr int GM_RAW_ST = 6;           // raw weight ring depth
+constexpr int GM_KC = 64;              // columns per MMA chunk: one 128-byte swizzle atom of f16
+constexpr int GM_RKC = 128;            // columns per raw-weight stage (two MMA chunks)
+constexpr int GM_RAW_ST = 4;           // raw weight ring depth
 constexpr int GM_MMA_ST = 3;           // operand ring depth (A f16 + B hi/lo)
-constexpr int GM_RAW_BYTES = 8192;     // one raw stage: up to 64 bytes x 128 rows
+constexpr int GM_RAW_BYTES = 16384;    // one raw stage: up to 128 bytes x 128 rows
 constexpr int GM_A_BYTES = GM_M * GM_KC * 2;      // 16 KB
 constexpr int GM_B_BYTES = GM_NT * GM_KC * 2;     // 16 KB per term
 constexpr int GM_WARPS = 11;
 constexpr int GM_THREADS = GM_WARPS * 32;
 constexpr int GM_CONV0 = 3, GM_FOLD0 = 7;         // first converter / fold warp
-constexpr int GM_TMEM_COLS = 256;
+constexpr int GM_TMEM_COLS = 256;  // two accumulator regions of GM_NT columns
 
 struct GroupedTile {
   int group;  // index into groups[]
@@ -51,7 +56,8 @@ struct GroupedTile {
 };
 
 // Byte offset of 16-byte chunk c (columns 8c..8c+7 of a 64-column chunk) of row r in a K-major, 128-byte-swizzled
-// operand block of 128 rows: 8-row atoms of 1024 bytes, chunk c of row r stored at position c ^ (r % 8).
+// operand block: 8-row atoms of 1024 bytes, chunk c of row r stored at position c ^ (r % 8). TMA's 128-byte swizzle
+// writes the same pattern.
 __host__ __device__ constexpr uint32_t sw128_offset(int r, int c) {
   return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
 }
@@ -66,14 +72,46 @@ __host__ __device__ constexpr size_t gm_workspace_bytes(int tiles, int K) {
 
 // ---------------------------------------------------------------------------------------------------------------
 // Staging: one block (8 warps) per tile slot. Block t finds its (group, tile of the group) from the groups' row
-// counts, writes the tile table entry, and converts the tile's rows (zeros past the group's end) to the hi / lo
-// f16 operand blocks plus inv[row] = 2^-e (0 for padding rows). Block 0 also writes the number of tiles.
-// Needs K % 256 == 0.
-__global__ void __launch_bounds__(256) gm_stage_kernel(const float* __restrict__ x, const int* __restrict__ groups,
-                                                       int G, int K, int max_tiles, uint8_t* __restrict__ staged,
-                                                       float* __restrict__ inv, GroupedTile* __restrict__ table,
-                                                       int* __restrict__ ntiles) {
+// counts, writes the tile table entry, and converts the tile's rows (zeros past the group's end, up to the MMA width)
+// to the hi / lo f16 operand blocks plus inv[row] = 2^-e (times 1/16 after a rotation; 0 for padding rows). Block 0
+// also writes the number of tiles. A warp owns a row: its K values sit in registers (lane l holds columns
+// 256 q + 8 l .. + 7), so the row's bound is exact.
+//   source row of sorted row s: x[row_index ? row_index[s] : s], fp32 or bf16 (src_bf16)
+//   mode bit GM_SWIGLU: the source row holds 2K columns, gate then up; the staged value is SiLU(gate) * up in the
+//        fast-exp form of the reference's rotate kernel (drama3/kernels.py:233-236)
+//   mode bit GM_ROTATE: each 256-column group is rotated by the reference's radix-4 butterfly (ConvRot,
+//        drama3/kernels.py:240-256), the 1/16 folded into inv
+// Needs K % 256 == 0, K <= 2048.
+enum { GM_ROTATE = 1, GM_SWIGLU = 2 };
+
+D3_DEV float gm_load(const void* x, bool bf16, size_t i) {
+  return bf16 ? bf16_to_f32(((const uint16_t*)x)[i]) : ((const float*)x)[i];
+}
+
+D3_DEV void gm_load8(const void* x, bool bf16, size_t base, float (&v)[8]) {
+  if (bf16) {
+    const uint4 b = __ldg((const uint4*)((const uint16_t*)x + base));
+    const uint32_t w[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      v[2 * u] = bf16_to_f32(w[u] & 0xFFFFu);
+      v[2 * u + 1] = bf16_to_f32(w[u] >> 16);
+    }
+  } else {
+    const float4 a = __ldg((const float4*)((const float*)x + base));
+    const float4 b = __ldg((const float4*)((const float*)x + base) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+}
+
+__global__ void __launch_bounds__(256) gm_stage_kernel(const void* __restrict__ x, int src_bf16,
+                                                       const int64_t* __restrict__ row_index, int mode,
+                                                       const int* __restrict__ groups, int G, int K, int max_tiles,
+                                                       uint8_t* __restrict__ staged, float* __restrict__ inv,
+                                                       GroupedTile* __restrict__ table, int* __restrict__ ntiles) {
   __shared__ int s_group, s_local, s_total;
+  __shared__ float scratch[8][256];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x;
   if (warp == 0) {
@@ -102,7 +140,10 @@ __global__ void __launch_bounds__(256) gm_stage_kernel(const float* __restrict__
       s_group = found_g;
       s_local = found_l;
       s_total = base;
-      if (t == 0) *ntiles = min(base, max_tiles);
+      if (t == 0) {
+        *ntiles = min(base, max_tiles);
+        if (base > max_tiles) record_fault(FAULT_TILES);
+      }
     }
   }
   __syncthreads();
@@ -111,36 +152,68 @@ __global__ void __launch_bounds__(256) gm_stage_kernel(const float* __restrict__
   const int first = groups[5 * g + 3], count = groups[5 * g + 4];
   const int row0 = first + s_local * GM_NT, rows = min(GM_NT, count - s_local * GM_NT);
   if (threadIdx.x == 0) table[t] = GroupedTile{g, row0, rows, 0};
+  const bool bf16 = src_bf16 != 0, rotate = (mode & GM_ROTATE) != 0, swiglu = (mode & GM_SWIGLU) != 0;
   const int nkc = K / GM_KC, nq = K / 256;
+  const size_t pitch = swiglu ? 2 * (size_t)K : (size_t)K;
   uint8_t* tile_base = staged + (size_t)t * nkc * 2 * GM_B_BYTES;
-  for (int j = warp; j < GM_NT; j += 8) {
+  const int width = (rows + 15) & ~15;  // rows the GEMM reads (its MMA N)
+  float* row = scratch[warp];
+  for (int j = warp; j < width; j += 8) {
     const bool live = j < rows;
-    const float* src = x + (size_t)(row0 + (live ? j : 0)) * K;
+    const size_t src_row = live ? (size_t)(row_index ? row_index[row0 + j] : row0 + j) : 0;
+    float v[8][8];
     float m = 0.0f;
-    if (live) {
-      for (int q = 0; q < nq; ++q) {
-        const float4 a = __ldg((const float4*)(src + 256 * q + 8 * lane));
-        const float4 b = __ldg((const float4*)(src + 256 * q + 8 * lane) + 1);
-        m = fmaxf(m, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
-        m = fmaxf(m, fmaxf(fmaxf(fabsf(b.x), fabsf(b.y)), fmaxf(fabsf(b.z), fabsf(b.w))));
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      if (q >= nq) break;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[q][u] = 0.0f;
+      if (live) {
+        const size_t base = src_row * pitch + 256 * q + 8 * lane;
+        gm_load8(x, bf16, base, v[q]);
+        if (swiglu) {
+          float up[8];
+          gm_load8(x, bf16, base + K, up);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) v[q][u] = swiglu_fast(v[q][u], up[u]);
+        }
+      }
+      if (rotate) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) row[8 * lane + u] = v[q][u];
+        __syncwarp();
+#pragma unroll
+        for (int stride = 1; stride < 256; stride *= 4) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int tt = lane + 32 * h, low = tt % stride, high = tt / stride;
+            const int i = high * stride * 4 + low;
+            const float va = row[i], vb = row[i + stride], vc = row[i + 2 * stride], vd = row[i + 3 * stride];
+            row[i] = va + vb + vc - vd;
+            row[i + stride] = va + vb - vc + vd;
+            row[i + 2 * stride] = va - vb + vc + vd;
+            row[i + 3 * stride] = -va + vb + vc + vd;
+          }
+          __syncwarp();
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[q][u] = row[8 * lane + u];
+        __syncwarp();
       }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      for (int u = 0; u < 8; ++u) m = fmaxf(m, fabsf(v[q][u]));
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     const int e = stage_exponent(m);
     const float scale = __uint_as_float((uint32_t)(e + 127) << 23);
-    for (int q = 0; q < nq; ++q) {
-      float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      if (live) {
-        const float4 a = __ldg((const float4*)(src + 256 * q + 8 * lane));
-        const float4 b = __ldg((const float4*)(src + 256 * q + 8 * lane) + 1);
-        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-      }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      if (q >= nq) break;
       uint32_t hw[4], lw[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const float s0 = v[2 * u] * scale, s1 = v[2 * u + 1] * scale;
+        const float s0 = v[q][2 * u] * scale, s1 = v[q][2 * u + 1] * scale;
         const __half h0 = __float2half_rn(s0), h1 = __float2half_rn(s1);
         hw[u] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
         const __half l0 = __float2half_rn(s0 - __half2float(h0)), l1 = __float2half_rn(s1 - __half2float(h1));
@@ -152,7 +225,38 @@ __global__ void __launch_bounds__(256) gm_stage_kernel(const float* __restrict__
       *(uint4*)(blk + sw128_offset(j, c)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
       *(uint4*)(blk + GM_B_BYTES + sw128_offset(j, c)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
     }
-    if (lane == 0) inv[(size_t)t * GM_NT + j] = live ? __uint_as_float((uint32_t)(127 - e) << 23) : 0.0f;
+    if (lane == 0)
+      inv[(size_t)t * GM_NT + j] =
+          live ? (rotate ? 0.0625f : 1.0f) * __uint_as_float((uint32_t)(127 - e) << 23) : 0.0f;
+  }
+}
+
+// Combine of a prompt pass (drama3/offload.py:146-149): out[t, :] = sum over k of weight[t, k] * sorted[pos[t*k + k'], :]
+// in rank order (fmaf), rounded to bf16 (or kept fp32 with out_f32). pos = the sorted position of pair (t, k'). One
+// block per token.
+__global__ void __launch_bounds__(256) gm_combine_kernel(const float* __restrict__ sorted, const int64_t* __restrict__ pos,
+                                                         const void* __restrict__ weights, int w_bf16, int k, int H,
+                                                         void* __restrict__ out, int out_f32) {
+  const int t = blockIdx.x;
+  for (int n = 4 * threadIdx.x; n < H; n += 4 * blockDim.x) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r = 0; r < k; ++r) {
+      const float w = w_bf16 ? bf16_to_f32(((const uint16_t*)weights)[(size_t)t * k + r])
+                             : ((const float*)weights)[(size_t)t * k + r];
+      const float4 p = __ldg((const float4*)(sorted + (size_t)pos[(size_t)t * k + r] * H + n));
+      acc.x = __fmaf_rn(w, p.x, acc.x);
+      acc.y = __fmaf_rn(w, p.y, acc.y);
+      acc.z = __fmaf_rn(w, p.z, acc.z);
+      acc.w = __fmaf_rn(w, p.w, acc.w);
+    }
+    if (out_f32) {
+      *(float4*)((float*)out + (size_t)t * H + n) = acc;
+    } else {
+      uint2 o;
+      o.x = (uint32_t)f32_to_bf16(acc.x) | ((uint32_t)f32_to_bf16(acc.y) << 16);
+      o.y = (uint32_t)f32_to_bf16(acc.z) | ((uint32_t)f32_to_bf16(acc.w) << 16);
+      *(uint2*)((uint16_t*)out + (size_t)t * H + n) = o;
+    }
   }
 }
 
@@ -165,8 +269,11 @@ D3_DEV uint64_t umma_desc_sw128(uint32_t saddr) {
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-// Instruction descriptor, kind::f16: f32 accumulator, f16 A and B, both K-major, M = 128, N = 128.
-constexpr uint32_t GM_IDESC = (1u << 4) | ((uint32_t)(GM_NT >> 3) << 17) | ((uint32_t)(GM_M >> 4) << 24);
+// Instruction descriptor, kind::f16: f32 accumulator, f16 A and B, both K-major, M = 128, N = n (16..128, % 16).
+D3_DEV uint32_t gm_idesc(int n) { return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(GM_M >> 4) << 24); }
+
+// MMA width of a tile of `rows` rows.
+D3_DEV int gm_width(int rows) { return (rows + 15) & ~15; }
 
 D3_DEV void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
@@ -255,9 +362,10 @@ struct GmSmem {
   static constexpr int launch = total + 1024;  // slack to align the base to 1024 bytes
 };
 
+// Raw bytes per weight row in one raw stage (128 columns): fp8 / int8 128, W4 nibbles 64, W6 nibbles 64 + plane 32.
 template <int FMT>
 __host__ __device__ constexpr int gm_raw_row_bytes() {
-  return FMT == FMT_FP8 || FMT == FMT_I8 ? 64 : FMT == FMT_W4 ? 32 : 48;
+  return FMT == FMT_FP8 || FMT == FMT_I8 ? 128 : FMT == FMT_W4 ? 64 : 96;
 }
 
 // The unit (tile, row block) a CTA takes k-th, or false past the end.
@@ -269,51 +377,55 @@ D3_DEV bool gm_unit(const GmArgs& a, int ntiles, int u, int& tile, int& rb) {
   return true;
 }
 
-// Convert one raw chunk (64 columns of weight row r) to f16 and store it swizzled into the A stage.
+// Convert half h (64 columns) of a raw stage's weight row r to f16 and store it swizzled into the A stage. The raw
+// stage holds TMA tiles with the hardware swizzle of their row width: 128-byte rows (fp8, int8) put 16-byte chunk c of
+// row r at c ^ (r % 8); 64-byte rows (W4/W6 nibbles) at c ^ ((r / 2) % 4); 32-byte rows (the W6 high plane) at
+// c ^ ((r / 4) % 2).
 template <int FMT>
-D3_DEV void gm_convert(const uint8_t* raw, uint8_t* astage, int r, uint32_t sbytes, const float* lut) {
+D3_DEV void gm_convert(const uint8_t* raw, int h, uint8_t* astage, int r, uint32_t sbytes, const float* lut) {
   if (FMT == FMT_FP8 || FMT == FMT_I8) {
-    const uint8_t* row = raw + r * 64;
+    const uint8_t* row = raw + r * 128;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int p = (i + (r >> 1)) & 3;  // rotation: four 16-byte reads per warp instruction hit distinct banks
-      const uint4 q = *(const uint4*)(row + 16 * p);
+    for (int p = 0; p < 4; ++p) {
+      const int cc = 4 * h + p;
+      const uint4 q = *(const uint4*)(row + ((cc ^ (r & 7)) << 4));
       const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-      uint32_t h[8];
+      uint32_t o[8];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         if (FMT == FMT_FP8) {
-          h[2 * j] = e4m3x2_h2(w[j] & 0xFFFFu);
-          h[2 * j + 1] = e4m3x2_h2(w[j] >> 16);
+          o[2 * j] = e4m3x2_h2(w[j] & 0xFFFFu);
+          o[2 * j + 1] = e4m3x2_h2(w[j] >> 16);
         } else {
           const uint32_t t = w[j] ^ 0x80808080u;
-          h[2 * j] = i8x2_h2(t, 0x4140);
-          h[2 * j + 1] = i8x2_h2(t, 0x4342);
+          o[2 * j] = i8x2_h2(t, 0x4140);
+          o[2 * j + 1] = i8x2_h2(t, 0x4342);
         }
       }
-      *(uint4*)(astage + sw128_offset(r, 2 * p)) = make_uint4(h[0], h[1], h[2], h[3]);
-      *(uint4*)(astage + sw128_offset(r, 2 * p + 1)) = make_uint4(h[4], h[5], h[6], h[7]);
+      *(uint4*)(astage + sw128_offset(r, 2 * p)) = make_uint4(o[0], o[1], o[2], o[3]);
+      *(uint4*)(astage + sw128_offset(r, 2 * p + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
     }
   } else {
-    // 64 columns = four 16-column groups: nibbles 8 bytes each (32 bytes per row), W6 high plane 4 bytes each
-    const uint8_t* low = raw + r * 32;
-    const uint8_t* high = raw + GM_M * 32 + r * 16;
+    // four 16-column groups g = 4h + p: nibbles 8 bytes each, W6 high plane 4 bytes each
+    const uint8_t* low = raw + r * 64;
+    const uint8_t* high = raw + GM_M * 64 + r * 32;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int p = (i + (r >> 2)) & 3;
-      const uint2 lw = *(const uint2*)(low + 8 * p);
-      const uint32_t hb = FMT == FMT_W6 ? *(const uint32_t*)(high + 4 * p) : 0u;
+    for (int p = 0; p < 4; ++p) {
+      const int g = 4 * h + p;
+      const uint2 lw = *(const uint2*)(low + (((g >> 1) ^ ((r >> 1) & 3)) << 4) + 8 * (g & 1));
+      const uint32_t hb =
+          FMT == FMT_W6 ? *(const uint32_t*)(high + (((g >> 2) ^ ((r >> 2) & 1)) << 4) + 4 * (g & 3)) : 0u;
       const float s = e4m3_to_f32((sbytes >> (8 * p)) & 0xFFu);
       float f[16];
       if (FMT == FMT_W4)
         dec_w4<16>(lw, s, lut, f);
       else
         dec_w6<16>(lw, hb, s, f);
-      uint32_t h[8];
+      uint32_t o[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) h[j] = pack_h2(f[2 * j], f[2 * j + 1]);
-      *(uint4*)(astage + sw128_offset(r, 2 * p)) = make_uint4(h[0], h[1], h[2], h[3]);
-      *(uint4*)(astage + sw128_offset(r, 2 * p + 1)) = make_uint4(h[4], h[5], h[6], h[7]);
+      for (int j = 0; j < 8; ++j) o[j] = pack_h2(f[2 * j], f[2 * j + 1]);
+      *(uint4*)(astage + sw128_offset(r, 2 * p)) = make_uint4(o[0], o[1], o[2], o[3]);
+      *(uint4*)(astage + sw128_offset(r, 2 * p + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
     }
   }
 }
@@ -372,20 +484,16 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         const int slot = a.groups[5 * a.table[tile].group + 1];
         const int wrow = slot * a.N + rb * GM_M;
         if (slot < 0 || wrow + GM_M > a.bank_rows) continue;
-        for (int kc = 0; kc < nkc && ok; ++kc) {
+        for (int kr = 0; kr < a.K / GM_RKC && ok; ++kr) {
           ok = mbar_wait(raw_empty + rs, rph ^ 1);
           if (!ok) break;
           uint8_t* dst = smem + GmSmem::raw + rs * GM_RAW_BYTES;
+          mbar_arrive_expect_tx(raw_full + rs, GM_M * gm_raw_row_bytes<FMT>());
           if (FMT == FMT_FP8 || FMT == FMT_I8) {
-            mbar_arrive_expect_tx(raw_full + rs, GM_M * 64);
-            tma_load_2d(dst, &wmap, kc * 64, wrow, raw_full + rs);
-          } else if (FMT == FMT_W4) {
-            mbar_arrive_expect_tx(raw_full + rs, GM_M * 32);
-            tma_load_2d(dst, &wmap, kc * 32, wrow, raw_full + rs);
+            tma_load_2d(dst, &wmap, kr * 128, wrow, raw_full + rs);
           } else {
-            mbar_arrive_expect_tx(raw_full + rs, GM_M * 48);
-            tma_load_2d(dst, &wmap, kc * 32, wrow, raw_full + rs);
-            tma_load_2d(dst + GM_M * 32, &pmap, a.K / 2 + kc * 16, wrow, raw_full + rs);
+            tma_load_2d(dst, &wmap, kr * 64, wrow, raw_full + rs);
+            if (FMT == FMT_W6) tma_load_2d(dst + GM_M * 64, &pmap, a.K / 2 + kr * 32, wrow, raw_full + rs);
           }
           if (++rs == GM_RAW_ST) {
             rs = 0;
@@ -405,12 +513,15 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         const int slot = a.groups[5 * a.table[tile].group + 1];
         if (slot < 0 || slot * a.N + rb * GM_M + GM_M > a.bank_rows) continue;
         const uint8_t* src = a.staged + (size_t)tile * nkc * 2 * GM_B_BYTES;
+        const uint32_t bytes = (uint32_t)gm_width(a.table[tile].rows) * 128u;  // rows x 64 f16 per term
         for (int kc = 0; kc < nkc && ok; ++kc) {
           ok = mbar_wait(mma_empty + ms, mph ^ 1);
           if (!ok) break;
           uint8_t* dst = smem + GmSmem::b + ms * 2 * GM_B_BYTES;
-          mbar_arrive_expect_tx(b_full + ms, 2 * GM_B_BYTES);
-          bulk_g2s(dst, src + (size_t)kc * 2 * GM_B_BYTES, 2 * GM_B_BYTES, b_full + ms, keep);
+          const uint8_t* blk = src + (size_t)kc * 2 * GM_B_BYTES;
+          mbar_arrive_expect_tx(b_full + ms, 2 * bytes);
+          bulk_g2s(dst, blk, bytes, b_full + ms, keep);
+          bulk_g2s(dst + GM_B_BYTES, blk + GM_B_BYTES, bytes, b_full + ms, keep);
           if (++ms == GM_MMA_ST) {
             ms = 0;
             mph ^= 1;
@@ -429,6 +540,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         const int slot = a.groups[5 * a.table[tile].group + 1];
         if (slot < 0 || slot * a.N + rb * GM_M + GM_M > a.bank_rows) continue;
         uint32_t acc = 0;
+        const uint32_t idesc = gm_idesc(gm_width(a.table[tile].rows));
         for (int kc = 0; kc < nkc && ok; ++kc) {
           if (kc % kbc == 0) {
             const int region = folds & 1;
@@ -445,8 +557,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
 #pragma unroll
           for (int ks = 0; ks < GM_KC / 16; ++ks) {
             const uint64_t ad = umma_desc_sw128(as + 32 * ks);
-            umma_f16(acc, ad, umma_desc_sw128(bs + 32 * ks), GM_IDESC, (kc % kbc != 0 || ks != 0) ? 1u : 0u);
-            umma_f16(acc, ad, umma_desc_sw128(bs + GM_B_BYTES + 32 * ks), GM_IDESC, 1u);
+            umma_f16(acc, ad, umma_desc_sw128(bs + 32 * ks), idesc, (kc % kbc != 0 || ks != 0) ? 1u : 0u);
+            umma_f16(acc, ad, umma_desc_sw128(bs + GM_B_BYTES + 32 * ks), idesc, 1u);
           }
           umma_commit(mma_empty + ms);
           if (kc % kbc == kbc - 1) {
@@ -474,17 +586,19 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                                 ? (const uint8_t*)a.scale + (size_t)(wrow + r) * (a.K / 16)
                                 : nullptr;
       for (int kc = 0; kc < nkc && ok; ++kc) {
+        const int h = kc & 1;
         const uint32_t sbytes = srow ? __ldg((const uint32_t*)(srow + 4 * kc)) : 0u;
-        ok = mbar_wait(raw_full + rs, rph) && mbar_wait(mma_empty + ms, mph ^ 1);
+        ok = (h == 1 || mbar_wait(raw_full + rs, rph)) && mbar_wait(mma_empty + ms, mph ^ 1);
         if (!ok) break;
-        gm_convert<FMT>(smem + GmSmem::raw + rs * GM_RAW_BYTES, smem + GmSmem::a + ms * GM_A_BYTES, r, sbytes, lut);
+        gm_convert<FMT>(smem + GmSmem::raw + rs * GM_RAW_BYTES, h, smem + GmSmem::a + ms * GM_A_BYTES, r, sbytes,
+                        lut);
         fence_async_smem();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(raw_empty + rs);
+          if (h == 1) mbar_arrive(raw_empty + rs);
           mbar_arrive(a_full + ms);
         }
-        if (++rs == GM_RAW_ST) {
+        if (h == 1 && ++rs == GM_RAW_ST) {
           rs = 0;
           rph ^= 1;
         }
@@ -526,6 +640,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
           const float s = __ldg((const float*)a.scale + (size_t)(wrow / 128) * (a.K / 128) + f);
 #pragma unroll
           for (int c = 0; c < GM_NT / 16; ++c) {
+            if (16 * c >= tl.rows) break;
             float v[16];
             tmem_ld16(tmem + lane_base + region * GM_NT + 16 * c, v);
 #pragma unroll
@@ -548,7 +663,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         tc_fence_after();
         const float rs = FMT == FMT_I8 ? __ldg((const float*)a.scale + wrow + r) : __ldg(a.s_channel + wrow + r);
 #pragma unroll 1
-        for (int c = 0; c < GM_NT / 16; ++c) {
+        for (int c = 0; 16 * c < tl.rows; ++c) {
           float v[16];
           tmem_ld16(tmem + lane_base + region * GM_NT + 16 * c, v);
 #pragma unroll

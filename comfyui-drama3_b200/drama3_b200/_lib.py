@@ -34,8 +34,10 @@ SIGNATURES = {
     "d3_grouped_fp8": (_i, [_p, _i, _p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _i, _p]),
     "d3_grouped_int8": (_i, [_p, _i, _p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _i, _p]),
     "d3_grouped_codes": (_i, [_p, _i, _p, _i, _p, _p, _p, _p, _p, _p, _p, _i, _p, _i, _i, _i, _i, _p]),
+    "d3_grouped_mma_tile_rows": (_i, []),
     "d3_grouped_mma_workspace": (_sz, [_i, _i]),
-    "d3_grouped_mma": (_i, [_i, _p, _p, _i, _i, _p, _p, _p, _p, _i, _p, _i, _i, _p, _sz, _p]),
+    "d3_grouped_mma": (_i, [_i, _p, _i, _p, _i, _p, _i, _i, _p, _p, _p, _p, _i, _p, _i, _i, _p, _sz, _p]),
+    "d3_prefill_combine": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _i, _p]),
     "d3_moe_decode_workspace": (_sz, [_i, _i, _i]),
     "d3_moe_decode": (_i, [_i, _p, _i, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _sz, _p]),
     "d3_moe_decode_static": (_i, [_i, _p, _i, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]),

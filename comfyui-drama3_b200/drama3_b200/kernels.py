@@ -196,9 +196,16 @@ def grouped_codes(x, groups, slot_fields, host_fields, codebook, bits, n):
     return out
 
 
+@functools.cache
+def grouped_tile_rows():
+    """Rows per tile of the tensor-core grouped kernel (its MMA N at most)."""
+    return int(lib().d3_grouped_mma_tile_rows())
+
+
 def grouped_tiles(counts):
-    """Tiles of 128 rows the tensor-core grouped kernel runs for groups of these row counts."""
-    return sum((int(n) + 127) // 128 for n in counts)
+    """Row tiles the tensor-core grouped kernel runs for groups of these row counts."""
+    t = grouped_tile_rows()
+    return sum((int(n) + t - 1) // t for n in counts)
 
 
 def grouped_mma_fits(n, k):
@@ -206,24 +213,55 @@ def grouped_mma_fits(n, k):
     return n % 128 == 0 and k % 256 == 0 and k >= 256
 
 
-def grouped_mma(kind, x, groups, fields, codebook, n, tiles):
-    """[rows, n] float32 for x's rows (float32, sorted by expert; rotated for int8/W4/W6) through their experts, on
-    the tensor cores, for a bank held whole on the GPU: the grouped_fp8 / grouped_int8 / grouped_codes results with
-    every group's slot = its expert's index in `fields` (drama3/offload.py:126-149). groups [g, 5] int32 on the GPU;
-    tiles = grouped_tiles(row counts). Rows outside every group are left unset."""
+GM_ROTATE, GM_SWIGLU = 1, 2
+
+
+def grouped_mma(kind, x, groups, fields, codebook, n, tiles, row_index=None, rotate=False, swiglu=False):
+    """[rows, n] float32 for the sorted rows through their experts, on the tensor cores, for a bank held whole on the
+    GPU: the grouped_fp8 / grouped_int8 / grouped_codes results with every group's slot = its expert's index in
+    `fields` (drama3/offload.py:126-149). groups [g, 5] int32 on the GPU; tiles = grouped_tiles(row counts). Sorted
+    row s is x[row_index[s]] (x float32 or bfloat16; row_index int64, or None for x itself), optionally through
+    SwiGLU (x holds gate | up) and the ConvRot rotation first, as kernels.rotate would give it. Rows outside every
+    group are left unset."""
     fmt = _lib.FORMATS[kind]
     wkey = "weight" if kind == "fp8" else "_qdata"
     w = fields[wkey]
     scale = fields["scale"].view(torch.uint8) if kind in ("w4", "w6") else fields["scale"]
+    if x.dtype not in (torch.float32, torch.bfloat16):
+        raise TypeError(f"grouped_mma takes float32 or bfloat16 rows, not {x.dtype}")
     x = x.contiguous()
-    K = x.shape[1]
-    out = torch.empty((x.shape[0], n), dtype=torch.float32, device=x.device)
+    K = x.shape[1] // 2 if swiglu else x.shape[1]
+    rows = row_index.shape[0] if row_index is not None else x.shape[0]
+    mode = (GM_ROTATE if rotate else 0) | (GM_SWIGLU if swiglu else 0)
+    out = torch.empty((rows, n), dtype=torch.float32, device=x.device)
     size = lib().d3_grouped_mma_workspace(int(tiles), K)
     ws = torch.empty((max(size, 256),), dtype=torch.uint8, device=x.device)
+    if row_index is not None:
+        row_index = row_index.to(torch.int64).contiguous()
     with _on(x.device):
-        check(lib().d3_grouped_mma(fmt, _ptr(x), _ptr(groups), groups.shape[0], int(tiles), _ptr(w), _ptr(scale),
-                                   _ptr(fields.get("s_channel")), _ptr(codebook), w.shape[0], _ptr(out), n, K,
-                                   _ptr(ws), ws.numel(), _stream(x.device)), "grouped_mma")
+        check(lib().d3_grouped_mma(fmt, _ptr(x), int(x.dtype == torch.bfloat16), _ptr(row_index), mode, _ptr(groups),
+                                   groups.shape[0], int(tiles), _ptr(w), _ptr(scale), _ptr(fields.get("s_channel")),
+                                   _ptr(codebook), w.shape[0], _ptr(out), n, K, _ptr(ws), ws.numel(),
+                                   _stream(x.device)), "grouped_mma")
+    return out
+
+
+def prefill_combine(sorted_out, pos, weights, dtype=torch.bfloat16):
+    """[T, H] `dtype` (bfloat16 or float32): out[t] = sum over k' of weights[t, k'] * sorted_out[pos[t, k']] in rank
+    order (the scatter, weighting and sum of drama3/offload.py:146-149 in one launch); pos [T, k] int64, weights
+    [T, k] fp32 or bf16."""
+    T, k = pos.shape
+    H = sorted_out.shape[1]
+    if dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError(f"prefill_combine writes bfloat16 or float32, not {dtype}")
+    out = torch.empty((T, H), dtype=dtype, device=sorted_out.device)
+    weights = weights.contiguous()
+    if weights.dtype not in (torch.float32, torch.bfloat16):
+        weights = weights.float()
+    with _on(sorted_out.device):
+        check(lib().d3_prefill_combine(_ptr(sorted_out.contiguous()), _ptr(pos.to(torch.int64).contiguous()),
+                                       _ptr(weights), int(weights.dtype == torch.bfloat16), T, k, H, _ptr(out),
+                                       int(dtype == torch.float32), _stream(sorted_out.device)), "prefill_combine")
     return out
 
 

@@ -211,15 +211,30 @@ def _grouped_resident(kind, x, groups, tiles, bank, rows, codebook):
 def resident_prefill(x, topk_idx, topk_weight, banks, rows, kind, codebooks, num_experts):
     """Many rows x [T, H] through banks held whole on the GPU (drama3/offload.py:138-149): rows sorted by expert, one
     grouped GEMM per bank on the tensor cores, SwiGLU between (with the ConvRot rotations for int8/W4/W6), scattered
-    back, weighted and summed. [T, H] in x's dtype."""
+    back, weighted and summed. Where the shapes allow (N % 128, K % 256), the gather of the sorted rows, SwiGLU and
+    the rotations run inside the GEMMs' staging and the scatter / weight / sum is one combine launch. [T, H] in x's
+    dtype (bfloat16 or float32)."""
     num_tokens, top_k = topk_idx.shape
     order, counts = _sort_by_expert(topk_idx, num_experts)
     offsets = [0, *itertools.accumulate(counts)]
     groups = [(e, e, 0, offsets[e], n) for e, n in enumerate(counts) if n]
     groups = torch.tensor(groups, dtype=torch.int32).to(x.device)
     tiles = kernels.grouped_tiles(counts)
-    always = torch.ones((1,), dtype=torch.int32, device=x.device)
     gate_up, down = banks
+    quantized = kind != "fp8"
+    width = x.shape[1]
+    if (x.dtype in (torch.bfloat16, torch.float32) and kernels.grouped_mma_fits(rows[0], width)
+            and kernels.grouped_mma_fits(rows[1], rows[0] // 2)):
+        hidden = kernels.grouped_mma(kind, x, groups, gate_up, codebooks[0], rows[0], tiles, row_index=order // top_k,
+                                     rotate=quantized)
+        sorted_out = kernels.grouped_mma(kind, hidden, groups, down, codebooks[1], rows[1], tiles, rotate=quantized,
+                                         swiglu=True)
+        pos = torch.empty_like(order)
+        pos[order] = torch.arange(order.numel(), device=order.device)
+        out = kernels.prefill_combine(sorted_out, pos.view(num_tokens, top_k), topk_weight,
+                                      dtype=torch.float32 if x.dtype == torch.float32 else torch.bfloat16)
+        return out.to(x.dtype)
+    always = torch.ones((1,), dtype=torch.int32, device=x.device)
     sorted_x = x[order // top_k].float()
     if kind == "fp8":
         gate, up = _grouped_resident(kind, sorted_x, groups, tiles, gate_up, rows[0], None).chunk(2, dim=-1)

@@ -46,8 +46,14 @@ int d3_last_cuda_error(void);
  * drama3/kernels.py:604-615 (available), which there falls back to PyTorch; here there is no fallback. */
 int d3_device_check(void);
 
-/* Reads and clears the current device's fault word (synchronous). Bits: 1 a wait timed out, 2 an expert id out of
- * range, 4 a slot out of range. No counterpart in the reference, whose kernels do not check indices. */
+/* Reads and clears the current device's fault word (synchronous). Bits: D3_FAULT_WAIT (1) a wait timed out,
+ * D3_FAULT_EXPERT (2) an expert id out of range, D3_FAULT_SLOT (4) a slot out of range, D3_FAULT_TILES (8) a
+ * grouped GEMM given fewer row tiles than its groups need. No counterpart in the reference, whose kernels do not
+ * check indices. */
+#define D3_FAULT_WAIT 1u
+#define D3_FAULT_EXPERT 2u
+#define D3_FAULT_SLOT 4u
+#define D3_FAULT_TILES 8u
 int d3_take_fault(unsigned int* fault);
 
 /* Decode routing, `rows` independent rows: ids [rows, k] (int64) and weights [rows, k] (fp32 holding bfloat16
@@ -108,12 +114,28 @@ int d3_grouped_codes(const float* x, int x_rows, const int* groups, int n_groups
  * drama3/offload.py:126-149 (resident_prefill), up to summation order. fmt = D3_FMT_*; weight / scale / s_channel /
  * codebook are the bank's fields (fp8: e4m3 rows + fp32 128x128 blocks; int8: rows + fp32 row scales; W4/W6: codes
  * + e4m3 group-16 scales + fp32 s_channel, codebook float[16] for W4), bank_rows = rows in the bank (E * N).
- * tiles = sum over groups of ceil(rows / 128) (an upper bound is allowed). N % 128 == 0, K % 256 == 0; x, out and
- * weight 16-byte aligned, workspace 256-byte aligned, d3_grouped_mma_workspace(tiles, K) bytes (no initial state). */
+ * Sorted row s of the GEMM input is x[row_index ? row_index[s] : s] (fp32, or bf16 when x_bf16), transformed by
+ * `mode`: D3_GM_SWIGLU (x rows hold 2K columns, gate then up: SiLU(gate) * up, the reference rotate kernel's form),
+ * then D3_GM_ROTATE (ConvRot over each 256 columns, as kernels.rotate) - so a prompt pass needs no separate gather,
+ * SwiGLU or rotation launches. tiles = sum over groups of ceil(rows / d3_grouped_mma_tile_rows()) (an upper bound
+ * is allowed; fewer records D3_FAULT_TILES and skips the rows past them).
+ * N % 128 == 0, K % 256 == 0, K <= 2048; x, out and weight 16-byte aligned, workspace 256-byte aligned,
+ * d3_grouped_mma_workspace(tiles, K) bytes (no initial state). No counterpart in the reference's kernel set beyond
+ * the grouped kernels it replaces for resident banks. */
+#define D3_GM_ROTATE 1
+#define D3_GM_SWIGLU 2
+int d3_grouped_mma_tile_rows(void);
 size_t d3_grouped_mma_workspace(int tiles, int K);
-int d3_grouped_mma(int fmt, const float* x, const int* groups, int n_groups, int tiles, const void* weight,
-                   const void* scale, const float* s_channel, const float* codebook, int bank_rows, float* out, int N,
-                   int K, void* workspace, size_t workspace_bytes, void* stream);
+int d3_grouped_mma(int fmt, const void* x, int x_bf16, const int64_t* row_index, int mode, const int* groups,
+                   int n_groups, int tiles, const void* weight, const void* scale, const float* s_channel,
+                   const float* codebook, int bank_rows, float* out, int N, int K, void* workspace,
+                   size_t workspace_bytes, void* stream);
+
+/* The combine of a prompt pass (drama3/offload.py:146-149): out[t] = sum over k' of weights[t, k'] *
+ * sorted[pos[t * k + k']] (fp32 [rows, H]; pos = each pair's row in the sorted order), in rank order, into out
+ * [T, H]: bf16 (rounded to nearest even), or fp32 when out_f32. weights fp32 or bf16 (w_bf16). H % 4 == 0. */
+int d3_prefill_combine(const float* sorted, const int64_t* pos, const void* weights, int w_bf16, int T, int k, int H,
+                       void* out, int out_f32, void* stream);
 
 /* Bytes of workspace d3_moe_decode needs for M rows, top-k and expert width I. */
 size_t d3_moe_decode_workspace(int M, int k, int I);

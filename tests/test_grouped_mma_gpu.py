@@ -89,3 +89,85 @@ def test_grouped_mma_rejects_bad_shapes(cuda):
     groups = torch.tensor([(0, 0, 0, 0, 4)], dtype=torch.int32, device=cuda)
     with pytest.raises(Exception):
         kernels.grouped_mma("fp8", x[:, :384].contiguous(), groups, bank, None, 256, 1)  # K % 256 != 0
+
+
+@pytest.mark.parametrize("kind", ["fp8", "int8", "w4"])
+def test_grouped_mma_fused_staging(cuda, kind):
+    """Gather from bf16 rows by index, SwiGLU and ConvRot inside the staging give what the separate launches give."""
+    N, K = 1536, 2048
+    bank, x, groups = grouped_case(kind, N, K, 31, cuda)
+    cb = gd.codebooks(kind, cuda)[0]
+    tiles = kernels.grouped_tiles(COUNTS)
+    live = int(sum(COUNTS))
+    gen = torch.Generator().manual_seed(32)
+    src = torch.randn((900, K), generator=gen).to(torch.bfloat16).to(cuda)
+    index = torch.randint(0, 900, (x.shape[0],), generator=gen).to(cuda)
+    got = kernels.grouped_mma(kind, src, groups, bank, cb, N, tiles, row_index=index)
+    want = kernels.grouped_mma(kind, src[index].float(), groups, bank, cb, N, tiles)
+    assert gd.rel_l2(got[:live], want[:live]) <= 1e-6
+    always = torch.ones((1,), dtype=torch.int32, device=cuda)
+    got = kernels.grouped_mma(kind, x, groups, bank, cb, N, tiles, rotate=True)
+    want = kernels.grouped_mma(kind, kernels.rotate(x, always), groups, bank, cb, N, tiles)
+    assert gd.rel_l2(got[:live], want[:live]) <= 1e-5
+    # SwiGLU (+ rotation) of gate | up rows, for the down projection's K = 768
+    bank2 = gd.rand_bank(kind, E, 2048, 768, 33, cuda)
+    h = torch.randn((x.shape[0], 1536), generator=gen).to(cuda) * 3
+    got = kernels.grouped_mma(kind, h, groups, bank2, cb, 2048, tiles, swiglu=True, rotate=kind != "fp8")
+    if kind == "fp8":
+        g, u = h.chunk(2, dim=-1)
+        staged = g / (1 + torch.exp(-g)) * u
+    else:
+        staged = kernels.rotate(h, always, swiglu=True)
+    want = kernels.grouped_mma(kind, staged.contiguous(), groups, bank2, cb, 2048, tiles)
+    assert gd.rel_l2(got[:live], want[:live]) <= 1e-5
+
+
+@pytest.mark.parametrize("wdtype", [torch.float32, torch.bfloat16])
+def test_prefill_combine(cuda, wdtype):
+    T, k, H = 300, 8, 2048
+    gen = torch.Generator().manual_seed(40)
+    sorted_out = torch.randn((T * k, H), generator=gen).to(cuda)
+    order = torch.randperm(T * k, generator=gen).to(cuda)
+    pos = torch.empty_like(order)
+    pos[order] = torch.arange(T * k, device=cuda)
+    w = torch.softmax(torch.randn((T, k), generator=gen), -1).to(wdtype).to(cuda)
+    got = kernels.prefill_combine(sorted_out, pos.view(T, k), w)
+    full = torch.empty_like(sorted_out)
+    full[order] = sorted_out * w.reshape(-1)[order].unsqueeze(1).float()
+    ref = full.view(T, k, H).sum(dim=1)
+    assert got.dtype == torch.bfloat16 and gd.rel_l2(got.float(), ref.to(torch.bfloat16).float()) <= 1e-3
+    got32 = kernels.prefill_combine(sorted_out, pos.view(T, k), w, dtype=torch.float32)
+    assert gd.rel_l2(got32, ref) <= 1e-6
+
+
+@pytest.mark.parametrize("kind", gd.KINDS)
+def test_resident_prefill_fused_matches_oracle(cuda, kind):
+    """A 2048-token prompt through one MoE layer of the benchmark's shape (128 experts), skewed routing, fused path."""
+    from drama3_b200 import offload
+    Ex, H, I = 128, 2048, 768
+    gu = gd.rand_bank(kind, Ex, 2 * I, H, 50, cuda)
+    dn = gd.rand_bank(kind, Ex, H, I, 51, cuda)
+    cbs = gd.codebooks(kind, cuda)
+    skew = -1.1 * torch.log(torch.randperm(Ex, generator=torch.Generator().manual_seed(52)).float() + 1)
+    x = gd.rand_rows(2048, H, 53, cuda)
+    ids, w = gd.rand_routing(2048, Ex, 8, 54, cuda, skew=skew)
+    out = offload.resident_prefill(x, ids, w.to(torch.bfloat16), (gu, dn), (2 * I, H), kind, cbs, Ex)
+    # the oracle on a row subset (the full prompt takes minutes in numpy): rows through their own experts
+    rows = torch.arange(0, 2048, 64)
+    npb = (gd.to_np_bank(gu), gd.to_np_bank(dn))
+    cbn = tuple(None if c is None else c.cpu().numpy() for c in cbs)
+    ref = moe.resident_prefill(kind, x[rows].float().cpu().numpy(), ids[rows].cpu().numpy(),
+                               w[rows].to(torch.bfloat16).float().cpu().numpy(), npb, cbn)
+    assert out.dtype == torch.bfloat16 and gd.rel_l2(out[rows].float(), ref) <= 1e-3
+
+
+def test_grouped_mma_too_few_tiles_records_fault(cuda):
+    """A caller that sizes fewer row tiles than its groups need gets the fault bit, not a crash or a hang."""
+    from drama3_b200 import _lib
+    N, K = 1536, 2048
+    bank, x, groups = grouped_case("fp8", N, K, 7, cuda)
+    _lib.take_fault()
+    kernels.grouped_mma("fp8", x, groups, bank, None, N, 2)
+    assert _lib.take_fault() & 8
+    kernels.grouped_mma("fp8", x, groups, bank, None, N, kernels.grouped_tiles(COUNTS))
+    assert _lib.take_fault() == 0
