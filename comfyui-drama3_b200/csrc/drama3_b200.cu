@@ -410,7 +410,7 @@ static size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
 size_t d3_moe_decode_workspace(int M, int k, int I) {
   if (M < 1 || k < 1 || I < 1) return 0;
   const size_t P = (size_t)M * k;
-  return align256(P * I * 4) + align256(P * d3::DEC_H * 4) + 256;
+  return align256(P * I * 4) + align256(P * d3::DEC_H * 4) + d3::DEC_SYNC_BYTES;
 }
 
 }  // extern "C"
@@ -428,7 +428,7 @@ static int decode_launch(const d3::DecodeArgs& a0, const DeviceInfo& d, cudaStre
   a.stages = ns;
   a.stage_bytes = SB;
   if (int st = allow_smem(kern, smem)) return st;
-  return launch(kern, dim3(d.sms), dim3(d3::DEC_ALL), smem, s, false, a);
+  return launch(kern, dim3(d.sms), dim3(d3::DEC_ALL), smem, s, true, a);
 }
 
 template <int FMT, bool XBF>
@@ -460,10 +460,14 @@ extern "C" int d3_moe_decode(int fmt, const void* x, int x_bf16, int M, int k, i
   uint8_t* ws = (uint8_t*)workspace;
   float* a1 = (float*)ws;
   float* parts = (float*)(ws + align256(P * I * 4));
-  auto* barrier = (unsigned long long*)(ws + align256(P * I * 4) + align256(P * d3::DEC_H * 4));
+  // the synchronization words sit at the end of the caller's workspace, so a workspace reused for several shapes
+  // keeps them in one place
+  uint8_t* tail = ws + ((workspace_bytes - d3::DEC_SYNC_BYTES) & ~(size_t)255);
+  auto* barrier = (unsigned long long*)tail;
+  auto* words = (unsigned*)tail;
   const int cap = cap_for(M);
   d3::DecodeArgs a = {x, x_bf16, ids, weights, M, k, E, H, I, w13, s13, c13, codebook13, w2, s2, c2, codebook2,
-                      out, a1, parts, barrier, 0, 0, cap};
+                      out, a1, parts, barrier, words + 16, words + 128, words + 384, 0, 0, cap};
   cudaStream_t s = (cudaStream_t)stream;
   switch (fmt) {
     case d3::FMT_FP8:
@@ -478,12 +482,12 @@ extern "C" int d3_moe_decode(int fmt, const void* x, int x_bf16, int M, int k, i
 // ------------------------------------------------------------------------------------------------------------
 // Fused decode without a caller-provided workspace, for callers that cannot allocate device memory themselves.
 // The scratch is this file-scope array, sized for the largest decode the kernel takes (16 rows x top-8 = 128 routed
-// pairs, intermediate 768, hidden 2048): 1,442,048 bytes that every GPU loading the library holds until exit.
+// pairs, intermediate 768, hidden 2048): 1,445,888 bytes that every GPU loading the library holds until exit.
 // Host code cannot use the array's name as a device address: set-up, once per device with that device current,
 // asks the runtime for the address (cudaGetSymbolAddress) and keeps it.
 namespace {
 
-constexpr size_t kStaticScratchBytes = 128u * 768u * 4u + 128u * 2048u * 4u + 256u;
+constexpr size_t kStaticScratchBytes = 128u * 768u * 4u + 128u * 2048u * 4u + d3::DEC_SYNC_BYTES;
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
 void* g_static_ptr[kMaxDevices];
@@ -513,11 +517,11 @@ extern "C" int d3_moe_decode_static(int fmt, const void* x, int x_bf16, int M, i
     return D3_ERR_TOO_LARGE;
   void* ws = nullptr;
   if (int st = static_scratch(&ws)) return st;
-  // The array keeps the last call's contents; of them only the grid-barrier counter must start at zero (its place
-  // depends on the shape). Cleared on the stream, ahead of the kernel.
-  const size_t P = (size_t)M * k;
-  unsigned char* barrier = (unsigned char*)ws + align256(P * I * 4) + align256(P * d3::DEC_H * 4);
-  if (int st = cuda_status(cudaMemsetAsync(barrier, 0, sizeof(unsigned long long), (cudaStream_t)stream))) return st;
+  // The array keeps the last call's contents; of them only the synchronization words at its end must start at zero
+  // (every call leaves them so, but a call that recorded a fault may not). Cleared on the stream, ahead of the
+  // kernel.
+  unsigned char* tail = (unsigned char*)ws + kStaticScratchBytes - d3::DEC_SYNC_BYTES;
+  if (int st = cuda_status(cudaMemsetAsync(tail, 0, d3::DEC_SYNC_BYTES, (cudaStream_t)stream))) return st;
   return d3_moe_decode(fmt, x, x_bf16, M, k, E, H, I, ids, weights, w13, s13, c13, w2, s2, c2, codebook13, codebook2,
                        out, ws, kStaticScratchBytes, stream);
 }

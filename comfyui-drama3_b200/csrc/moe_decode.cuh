@@ -8,11 +8,14 @@
 //   plan      every CTA sorts the M*k (row, rank) pairs by expert: segments of one expert and at most 8 pairs.
 //   phase 1   gate_up + SwiGLU: the segments' gate and up rows, split evenly over the CTAs as contiguous ranges of
 //             (segment, i) pair-rows; a1[pair, i] = SwiGLU(gate_i . x, up_i . x) to global scratch (fp32).
-//   barrier   (grid-wide, bounded wait)
+//   barrier   grid-wide; or, with few segments (nseg * 8 <= CTAs, e.g. one or two rows), each segment owns a
+//             contiguous group of CTAs for both phases and only the group waits for its own a1
 //   phase 2   down: the segments' down rows, split the same way; parts[pair, n] = down_n . a1[pair] (fp32 scratch).
-//   barrier
-//   phase 3   combine: out[t, n] = bf16(sum_j w[t, j] * parts[t*k + j, n]) in rank order (the reference's
-//             weighted_sum order), deterministic, no atomics.
+//   combine   out[t, n] = bf16(sum_j w[t, j] * parts[t*k + j, n]) in rank order (the reference's weighted_sum
+//             order), one CTA per output: after a second grid-wide barrier each CTA sums an even share of the
+//             columns; in group mode each CTA instead adds the down rows it finished to a per-64-column-block
+//             counter, and the CTA that completes a block sums it and resets the counter (no second wait).
+//             Deterministic either way.
 //
 // Data movement: weights reach shared memory through 1-D bulk copies (cp.async.bulk, the untiled TMA path) issued
 // by one producer warp on an mbarrier ring that runs through both phases, so the down rows stream in while phase 1
@@ -324,9 +327,19 @@ struct DecodeArgs {
   uint16_t* out;                // [M, H] bf16
   float* a1;                    // scratch [M*k, I]
   float* parts;                 // scratch [M*k, H]
-  unsigned long long* barrier;  // scratch: zero before the first call; grows by 2 * gridDim.x per call
+  unsigned long long* barrier;  // scratch: zero before the first call; grows by gridDim.x per grid-wide barrier
+  unsigned* blocks;             // scratch [DEC_H / DEC_CB]: combine counters, zero between calls
+  unsigned* arrive;             // scratch [DEC_MAX_GRID]: group-barrier counters, zero between calls
+  unsigned* depart;             // scratch [DEC_MAX_GRID]
   int stages, stage_bytes, cap;
 };
+
+constexpr int DEC_CB = 64;          // columns per combine block
+constexpr int DEC_MAX_GRID = 256;   // CTAs the group counters cover
+// The workspace tail holding the synchronization words (at the end of the caller's workspace): the ticket
+// (8 bytes), the block counters at +64, arrive at +512, depart at +1536 (unsigned each). Zero before the first
+// call; every call leaves them zero (the ticket a multiple of the grid size), unless it recorded a fault.
+constexpr int DEC_SYNC_BYTES = 4096;
 
 // Warp roles: DEC_WARPS MMA warps, then the epilogue warp (reductions and stores), then the producer warp.
 constexpr int DEC_EPI = DEC_WARPS, DEC_PROD = DEC_WARPS + 1;
@@ -410,6 +423,64 @@ D3_DEV bool grid_barrier(unsigned long long* counter, unsigned nblocks) {
   }
   named_sync(2, DEC_CONSUMERS + 32);
   return passed != 0;
+}
+
+// Barrier of the `n` CTAs of one segment group (same participants as grid_barrier): arrive, wait for all n
+// arrivals, depart; the last to depart zeroes both counters for the next call (every member has passed the wait by
+// then). Bounded like grid_barrier.
+D3_DEV bool group_barrier(unsigned* arrive, unsigned* depart, unsigned n) {
+  __shared__ int passed;
+  named_sync(2, DEC_CONSUMERS + 32);
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(arrive, 1u);
+    int ok = 1;
+    unsigned seen;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(seen) : "l"(arrive) : "memory");
+    if (seen < n) {
+      const unsigned long long start = globaltimer();
+      while (true) {
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(seen) : "l"(arrive) : "memory");
+        if (seen >= n) break;
+        if (globaltimer() - start > WAIT_LIMIT_NS) {
+          record_fault(FAULT_WAIT_TIMEOUT);
+          ok = 0;
+          break;
+        }
+      }
+    }
+    passed = ok;
+    if (ok && atomicAdd(depart, 1u) == n - 1) {
+      atomicExch(arrive, 0u);
+      atomicExch(depart, 0u);
+    }
+  }
+  named_sync(2, DEC_CONSUMERS + 32);
+  return passed != 0;
+}
+
+// The phase-1 and phase-2 ranges of CTA b of G for nseg segments: contiguous even splits of the whole
+// (segment, row) space, or, in group mode, CTA b belongs to segment b * nseg / G and splits that segment's rows with
+// the other CTAs of its group. Returns the group (segment) or -1, and its size.
+D3_DEV int decode_ranges(int nseg, int I, int H, int b, int G, bool grouped, int& lo1, int& hi1, int& lo2, int& hi2,
+                         int& gsz) {
+  if (!grouped) {
+    split_range(nseg * I, b, G, lo1, hi1);
+    split_range(nseg * H, b, G, lo2, hi2);
+    gsz = G;
+    return -1;
+  }
+  const int s = (int)((long long)b * nseg / G);
+  const int b0 = (int)(((long long)s * G + nseg - 1) / nseg), b1 = (int)(((long long)(s + 1) * G + nseg - 1) / nseg);
+  gsz = b1 - b0;
+  int l, h;
+  split_range(I, b - b0, gsz, l, h);
+  lo1 = s * I + l;
+  hi1 = s * I + h;
+  split_range(H, b - b0, gsz, l, h);
+  lo2 = s * H + l;
+  hi2 = s * H + h;
+  return s;
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -634,6 +705,29 @@ D3_DEV bool mma_phase(const DecodeArgs& a, const DecodePlan& pl, int lo, int hi,
   return ok;
 }
 
+// The routed combine of columns [n0, n1) for every row, in rank order (the reference's weighted_sum order), by the
+// CTA's MMA and epilogue warps. valid[p] / w[p]: pair p's id is in range / its routing weight (shared memory). The
+// k parts of an output are loaded together (independent L2 loads), then summed in order.
+D3_DEV void combine_columns(const DecodeArgs& a, const unsigned char* valid, const float* w, int n0, int n1, bool ok) {
+  const int NC = n1 - n0, H = DEC_H;
+  for (int idx = threadIdx.x; idx < a.M * NC; idx += DEC_CONSUMERS + 32) {
+    const int t = idx / NC, n = n0 + idx - t * NC;
+    float acc = 0.0f;
+    for (int j0 = 0; j0 < a.k; j0 += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int p = t * a.k + j0 + u;
+        v[u] = (ok && j0 + u < a.k && valid[p]) ? __ldcg(a.parts + (size_t)p * H + n) : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (j0 + u < a.k) acc = __fmaf_rn(v[u], w[t * a.k + j0 + u], acc);
+    }
+    a.out[(size_t)t * H + n] = f32_to_bf16(acc);
+  }
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 template <int FMT, bool XBF, int NKC>
 __global__ void __launch_bounds__(DEC_ALL, 1) moe_decode_kernel(const DecodeArgs a) {
@@ -674,6 +768,10 @@ __global__ void __launch_bounds__(DEC_ALL, 1) moe_decode_kernel(const DecodeArgs
     }
     fence_mbar_init();
   }
+  // programmatic dependent launch: the next kernel in the stream may be scheduled onto SMs this grid frees; this one
+  // reads its inputs and touches the workspace only after the previous grid has completed
+  allow_dependents();
+  grid_dependency_wait();
   if (FMT == FMT_W4 && tid < 16) {
     lut1[tid] = a.cb13[tid];
     lut2[tid] = a.cb2[tid];
@@ -681,9 +779,10 @@ __global__ void __launch_bounds__(DEC_ALL, 1) moe_decode_kernel(const DecodeArgs
   build_plan(pl, a.ids, P, a.E, a.cap);
   D3_STAMP(1);
   const int nseg = pl.nseg, G = gridDim.x;
-  int lo1, hi1, lo2, hi2;
-  split_range(nseg * I, blockIdx.x, G, lo1, hi1);
-  split_range(nseg * H, blockIdx.x, G, lo2, hi2);
+  // group mode needs at least 8 CTAs per segment, so that a CTA's down rows (H / 8 = 256 at most) span <= 5 blocks
+  const bool grouped = nseg > 0 && nseg * 8 <= G && G <= DEC_MAX_GRID;
+  int lo1, hi1, lo2, hi2, gsz;
+  const int grp = decode_ranges(nseg, I, H, blockIdx.x, G, grouped, lo1, hi1, lo2, hi2, gsz);
 
   if (warp == DEC_PROD) {
     // ---------------- producer: phase-1 chunks, then phase-2 chunks, through one ring ----------------
@@ -737,7 +836,8 @@ __global__ void __launch_bounds__(DEC_ALL, 1) moe_decode_kernel(const DecodeArgs
     // ---------------- epilogue: reduce each chunk's partial sums, scale, store ----------------
     int c = 0;
     for (int phase = 1; phase <= 2; ++phase) {
-      if (phase == 2) ok = grid_barrier(a.barrier, G) && ok;
+      if (phase == 2)
+        ok = (grouped ? group_barrier(a.arrive + grp, a.depart + grp, gsz) : grid_barrier(a.barrier, G)) && ok;
       const int lo = phase == 1 ? lo1 : lo2, hi = phase == 1 ? hi1 : hi2, per = phase == 1 ? I : H;
       const int ch = phase == 1 ? DEC_CH1 : DEC_CH2;
       for (int q = lo; q < hi; ++c) {
@@ -807,8 +907,8 @@ __global__ void __launch_bounds__(DEC_ALL, 1) moe_decode_kernel(const DecodeArgs
                 if (FMT == FMT_I8) sc = __ldg((const float*)a.s2 + (size_t)e * H + nrow);
                 if (fmt_codes(FMT)) sc = __ldg(a.c2 + (size_t)e * H + nrow);
                 const float v0 = half ? sum.z : sum.x, v1 = half ? sum.w : sum.y;
-                if (n0 < cnt) a.parts[(size_t)rs.pair[n0] * H + nrow] = v0 * (sc * rs.inv[n0]);
-                if (n1 < cnt) a.parts[(size_t)rs.pair[n1] * H + nrow] = v1 * (sc * rs.inv[n1]);
+                if (n0 < cnt) __stcg(a.parts + (size_t)rs.pair[n0] * H + nrow, v0 * (sc * rs.inv[n0]));
+                if (n1 < cnt) __stcg(a.parts + (size_t)rs.pair[n1] * H + nrow, v1 * (sc * rs.inv[n1]));
               }
             }
           }
@@ -827,27 +927,59 @@ __global__ void __launch_bounds__(DEC_ALL, 1) moe_decode_kernel(const DecodeArgs
     ok = mma_phase<FMT, XBF, NKC, 1>(a, pl, lo1, hi1, c, ok, ring, full_bar, empty_bar, rfull, rempty, red, xin, inv,
                                      rowmax, wscratch, table, lut1, pair_in, rows_in);
     D3_STAMP(2);
-    ok = grid_barrier(a.barrier, G) && ok;
+    ok = (grouped ? group_barrier(a.arrive + grp, a.depart + grp, gsz) : grid_barrier(a.barrier, G)) && ok;
     D3_STAMP(3);
     ok = mma_phase<FMT, XBF, NKC, 2>(a, pl, lo2, hi2, c, ok, ring, full_bar, empty_bar, rfull, rempty, red, xin, inv,
                                      rowmax, wscratch, table, lut2, pair_in, rows_in);
     D3_STAMP(4);
   }
-  ok = grid_barrier(a.barrier, G) && ok;
   D3_STAMP(5);
-  // phase 3: routed combine in rank order, as the reference's weighted_sum
-  int n0, n1;
-  split_range(H, blockIdx.x, G, n0, n1);
-  const int NC = n1 - n0;
-  for (int idx = tid; idx < a.M * NC; idx += DEC_CONSUMERS + 32) {
-    const int t = idx / NC, n = n0 + idx - t * NC;
-    float acc = 0.0f;
-    for (int j = 0; j < a.k; ++j) {
-      const long long id = a.ids[t * a.k + j];
-      const float part = (ok && id >= 0 && id < a.E) ? __ldcg(a.parts + (size_t)(t * a.k + j) * H + n) : 0.0f;
-      acc = __fmaf_rn(part, a.weights[t * a.k + j], acc);
+  // ---------------- combine ----------------
+  __shared__ int s_nblk, s_blk[DEC_H / DEC_CB];
+  __shared__ float c_w[DEC_MAX_PAIRS];
+  __shared__ unsigned char c_ok[DEC_MAX_PAIRS];
+  if (tid < P) {
+    const long long id = a.ids[tid];
+    c_ok[tid] = nseg > 0 && id >= 0 && id < a.E;
+    c_w[tid] = a.weights[tid];
+  }
+  if (!grouped) {
+    // grid-wide: every CTA's parts are written; each CTA combines an even share of the columns
+    ok = grid_barrier(a.barrier, G) && ok;
+    int n0, n1;
+    split_range(H, blockIdx.x, G, n0, n1);
+    combine_columns(a, c_ok, c_w, n0, n1, ok);
+  } else {
+    // group mode: the CTA that completes a 64-column block (its counter reaching nseg * 64 finished down rows) sums
+    // that block; no second wait
+    named_sync(2, DEC_CONSUMERS + 32);  // the epilogue's parts stores are done
+    if (tid == 0) {
+      int nb = 0;
+      if (ok && hi2 > lo2) {
+        __threadfence();
+        // one segment's rows [r, end): at most 256 rows (G >= 8 nseg CTAs share H rows), so at most 5 blocks; the
+        // counter updates are issued together, then checked
+        const int r = lo2 % H, end = r + (hi2 - lo2), b0 = r / DEC_CB, nblk = min(8, (end - 1) / DEC_CB - b0 + 1);
+        unsigned old[8], cnt[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int lo = max(r, (b0 + i) * DEC_CB), hi = min(end, (b0 + i + 1) * DEC_CB);
+          cnt[i] = i < nblk ? (unsigned)(hi - lo) : 0u;
+          old[i] = i < nblk ? atomicAdd(a.blocks + b0 + i, cnt[i]) : 0u;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (i < nblk && old[i] + cnt[i] == (unsigned)(nseg * DEC_CB)) s_blk[nb++] = b0 + i;
+        __threadfence();
+      }
+      s_nblk = nb;
     }
-    a.out[(size_t)t * H + n] = f32_to_bf16(acc);
+    named_sync(2, DEC_CONSUMERS + 32);
+    for (int i = 0; i < s_nblk; ++i) {
+      const int b = s_blk[i];
+      combine_columns(a, c_ok, c_w, b * DEC_CB, (b + 1) * DEC_CB, ok);
+      if (tid == 0) a.blocks[b] = 0u;
+    }
   }
   D3_STAMP(6);
 }

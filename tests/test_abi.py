@@ -51,8 +51,8 @@ def test_argument_checks_return_before_launch(lib):
     assert lib.d3_moe_decode(0, 16, 1, 1, 8, 128, 2048, 700, *([16] * 12), 1 << 30, None) == 1   # I % 128
     assert lib.d3_moe_decode(0, 16, 1, 4, 8, 128, 2048, 768, *([16] * 12), 16, None) == 5        # workspace
     assert lib.d3_moe_decode(0, 17, 1, 1, 8, 128, 2048, 768, *([16] * 12), 1 << 30, None) == 2   # alignment
-    # a1 [M*k, I] + parts [M*k, 2048] fp32, each 256-aligned, + the grid-barrier words
-    assert lib.d3_moe_decode_workspace(16, 8, 768) == 16 * 8 * (768 + 2048) * 4 + 256
+    # a1 [M*k, I] + parts [M*k, 2048] fp32, each 256-aligned, + 4096 bytes of synchronization words
+    assert lib.d3_moe_decode_workspace(16, 8, 768) == 16 * 8 * (768 + 2048) * 4 + 4096
 
 
 def test_product_does_not_import_the_oracle():
