@@ -444,7 +444,7 @@ extern "C" int d3_moe_decode(int fmt, const void* x, int x_bf16, int M, int k, i
                   const float* weights, const uint8_t* w13, const void* s13, const float* c13, const uint8_t* w2,
                   const void* s2, const float* c2, const float* codebook13, const float* codebook2, uint16_t* out,
                   void* workspace, size_t workspace_bytes, void* stream) {
-  if (fmt < d3::FMT_FP8 || fmt > d3::FMT_W6) return D3_ERR_ARG;
+  if (fmt < 0 || fmt >= d3::FMT_COUNT) return D3_ERR_ARG;
   if (M < 1 || M > 16 || k < 1 || k > 32 || M * k > d3::DEC_MAX_PAIRS || E < 1) return D3_ERR_ARG;
   if (H != d3::DEC_H || (I != 512 && I != 768)) return D3_ERR_ARG;
   if (!x || !ids || !weights || !w13 || !s13 || !w2 || !s2 || !out || !workspace) return D3_ERR_ARG;
@@ -475,6 +475,10 @@ extern "C" int d3_moe_decode(int fmt, const void* x, int x_bf16, int M, int k, i
     case d3::FMT_I8: return decode_nkc<d3::FMT_I8, true>(a, d, s);
     case d3::FMT_W4: return decode_nkc<d3::FMT_W4, true>(a, d, s);
     case d3::FMT_W6: return decode_nkc<d3::FMT_W6, true>(a, d, s);
+    case d3::FMT_FP8C:
+      return x_bf16 ? decode_nkc<d3::FMT_FP8C, true>(a, d, s) : decode_nkc<d3::FMT_FP8C, false>(a, d, s);
+    case d3::FMT_W4A8: return decode_nkc<d3::FMT_W4A8, true>(a, d, s);
+    case d3::FMT_W6A8: return decode_nkc<d3::FMT_W6A8, true>(a, d, s);
   }
   return D3_ERR_ARG;
 }

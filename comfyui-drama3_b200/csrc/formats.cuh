@@ -5,6 +5,11 @@
 //   W4   4-bit codes [E*N, K/2] (low nibble = even column), e4m3 group-16 scales [E*N, K/16], fp32 s_channel,
 //        a 16-entry float codebook: weight = clamp(rint(codebook[c] * scale), +-127) (drama3/kernels.py:469-483)
 //   W6   nibble plane [K/2] then 2-bit high plane [K/4] per row: weight = clamp(rint((c - 32) * scale), +-127)
+// and the BASELINE layouts (BASELINE.json configs[1..3]; no reference implementation):
+//   FP8C e4m3 rows [E*N, K], fp32 per-output-channel scales [E*N]
+//   W4A8 int4 (-7..7) two per byte, low nibble = even column; bf16 group-128 scales [E*N, K/128]
+//   W6A8 int6 (-31..31) four per three bytes (24-bit little-endian words); bf16 group-128 scales
+//   (A8: the activations are quantized to int8 per row, absmax / 127, before every GEMV)
 //
 // Conversions avoid the slow converter paths measured on B200 (int8 -> float through I2F runs at about 16 per clock
 // per SM): e4m3 pairs go to f16 pairs with one cvt (every e4m3 value is an f16), int8 goes to f32 by placing the
@@ -15,13 +20,26 @@
 
 namespace d3 {
 
-enum { FMT_FP8 = 0, FMT_I8 = 1, FMT_W4 = 2, FMT_W6 = 3 };
+enum { FMT_FP8 = 0, FMT_I8 = 1, FMT_W4 = 2, FMT_W6 = 3, FMT_FP8C = 4, FMT_W4A8 = 5, FMT_W6A8 = 6 };
+constexpr int FMT_COUNT = 7;
+constexpr int A8_GROUP = 128;  // columns per bf16 group scale of W4A8 / W6A8
 
 __host__ __device__ constexpr int fmt_row_bytes(int fmt, int K) {
-  return fmt == FMT_W4 ? K / 2 : fmt == FMT_W6 ? 3 * K / 4 : K;
+  return fmt == FMT_W4 || fmt == FMT_W4A8 ? K / 2 : fmt == FMT_W6 || fmt == FMT_W6A8 ? 3 * K / 4 : K;
 }
-__host__ __device__ constexpr bool fmt_rotated(int fmt) { return fmt != FMT_FP8; }
+// ConvRot formats: the activations are rotated before the GEMVs
+__host__ __device__ constexpr bool fmt_rotated(int fmt) { return fmt == FMT_I8 || fmt == FMT_W4 || fmt == FMT_W6; }
+// the reference's codes with e4m3 group-16 scales and an s_channel
 __host__ __device__ constexpr bool fmt_codes(int fmt) { return fmt == FMT_W4 || fmt == FMT_W6; }
+__host__ __device__ constexpr bool fmt_e4m3(int fmt) { return fmt == FMT_FP8 || fmt == FMT_FP8C; }
+// int8 activations and bf16 group-128 scales
+__host__ __device__ constexpr bool fmt_a8(int fmt) { return fmt == FMT_W4A8 || fmt == FMT_W6A8; }
+// an fp32 scale per weight row (int8 ConvRot, per-channel fp8)
+__host__ __device__ constexpr bool fmt_row_scale(int fmt) { return fmt == FMT_I8 || fmt == FMT_FP8C; }
+// bytes of per-row group scales staged beside each weight row (e4m3 per 16 columns, or bf16 per 128)
+__host__ __device__ constexpr int fmt_gscale_bytes(int fmt, int K) {
+  return fmt_codes(fmt) ? K / 16 : fmt_a8(fmt) ? 2 * (K / A8_GROUP) : 0;
+}
 
 // Swizzled float4 slot of float4 index f in a staged activation row: conflict-free 16-byte loads when lane l reads
 // float4 4*(l + 32j) + q for fixed (j, q). Permutes within aligned groups of eight (rows of K % 32 == 0 floats).

@@ -164,10 +164,11 @@ D3_DEV void stage_load(const void* src, bool bf16, size_t base, float (&v)[8]) {
 // plain row; for a rotated row 16 * max over groups of the group's 2-norm (each output of the unscaled butterfly,
 // 16 times a normalized-Hadamard row dotted with the group, is within that). Pass B reloads the values (L2), rotates
 // each group with the reference's butterfly when `rotate` (in the warp's own 256-float scratch; the groups are
-// independent), scales by 2^e so the bound sits in [2^14, 2^15) and converts to f16 (hi, and lo when `two`).
+// independent), scales by 2^e so the bound sits in [2^14, 2^15) and converts to f16 (hi, and lo when `two`); with
+// `int8q` (W4A8 / W6A8) it instead quantizes the row to int8 by its exact max (inv = the int8 scale).
 // Uses named barrier 1 (MMA warps); rowmax[] must be zero on entry.
 D3_DEV void stage_rows(__half* xin, float* inv, int* rowmax, float* wscratch, const void* src, bool bf16,
-                       const int* rows, int cnt, int K, bool rotate, bool two) {
+                       const int* rows, int cnt, int K, bool rotate, bool two, bool int8q = false) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int groups = K / 256, items = cnt * groups;
   for (int it = warp; it < items; it += DEC_WARPS) {
@@ -218,10 +219,25 @@ D3_DEV void stage_rows(__half* xin, float* inv, int* rowmax, float* wscratch, co
       for (int u = 0; u < 8; ++u) v[u] = row[8 * lane + u];
       __syncwarp();
     }
-    const int e = stage_exponent(__int_as_float(rowmax[j]));
-    const float scale = __uint_as_float((uint32_t)(e + 127) << 23);
     __half* hi = xin + (size_t)j * RH + 256 * q + 8 * lane;
     __half* lo = xin + (size_t)(DEC_MAX_CAP + j) * RH + 256 * q + 8 * lane;
+    if (int8q) {
+      // per-row int8 quantization (W4A8 / W6A8): s = max|x| / 127, q = clamp(rint(x / s), +-127), IEEE division
+      const float s = __fdiv_rn(__int_as_float(rowmax[j]), 127.0f);
+      uint32_t hw[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float q0 = s > 0.0f ? fminf(127.0f, fmaxf(-127.0f, rintf(__fdiv_rn(v[2 * u], s)))) : 0.0f;
+        const float q1 = s > 0.0f ? fminf(127.0f, fmaxf(-127.0f, rintf(__fdiv_rn(v[2 * u + 1], s)))) : 0.0f;
+        hw[u] = (uint32_t)__half_as_ushort(__float2half_rn(q0)) |
+                ((uint32_t)__half_as_ushort(__float2half_rn(q1)) << 16);
+      }
+      *(uint4*)hi = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      if (q == 0 && lane == 0) inv[j] = s;
+      continue;
+    }
+    const int e = stage_exponent(__int_as_float(rowmax[j]));
+    const float scale = __uint_as_float((uint32_t)(e + 127) << 23);
     uint32_t hw[4], lw[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
@@ -266,14 +282,46 @@ D3_DEV uint32_t i8x2_h2(uint32_t w_xor80, uint32_t sel) {
 // The 16 columns a lane owns in one weight row, as 8 f16x2 registers. `row` points at the row's bytes,
 // `col` is the first column (64 * kc + 16c); W4/W6 also read the row's group scales `srow` (one e4m3 byte per 16
 // columns) and the codebook `lut`.
+// Signed 4-bit / 6-bit codes -> exact f16 pairs: the code, sign bit flipped, as the low mantissa bits of 1024, minus
+// 1024 + 8 (or + 32).
+D3_DEV uint32_t s4x2_h2(uint32_t byte) {
+  const uint32_t h = (((byte & 0xFu) | ((byte & 0xF0u) << 12)) ^ 0x00080008u) | 0x64006400u;
+  uint32_t r;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(0x64086408u));  // 1032.0 in both halves
+  return r;
+}
+D3_DEV uint32_t s6x2_h2(uint32_t c0, uint32_t c1) {
+  const uint32_t h = ((c0 | (c1 << 16)) ^ 0x00200020u) | 0x64006400u;
+  uint32_t r;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(0x64206420u));  // 1056.0 in both halves
+  return r;
+}
+
 template <int FMT>
 D3_DEV void build_a(const uint8_t* row, const uint8_t* srow, int col, int K, const float* lut, uint32_t (&a)[8]) {
-  if (FMT == FMT_FP8 || FMT == FMT_I8) {
+  if (FMT == FMT_W4A8) {
+    // 16 nibbles: byte i holds columns 2i (low) and 2i + 1
+    const uint2 p = *(const uint2*)(row + col / 2);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a[i] = s4x2_h2(((i < 4 ? p.x : p.y) >> (8 * (i & 3))) & 0xFFu);
+  } else if (FMT == FMT_W6A8) {
+    // 16 six-bit codes in 12 bytes: code i at bit 6i of the little-endian 96-bit word
+    const uint32_t* p = (const uint32_t*)(row + (col / 16) * 12);
+    const uint32_t w[3] = {p[0], p[1], p[2]};
+    uint32_t c[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int bit = 6 * i, k = bit >> 5, off = bit & 31;
+      c[i] = __funnelshift_r(w[k], k < 2 ? w[k + 1] : 0u, off) & 63u;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a[i] = s6x2_h2(c[2 * i], c[2 * i + 1]);
+  } else if (fmt_e4m3(FMT) || FMT == FMT_I8) {
     const uint4 q = *(const uint4*)(row + col);
     const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      if (FMT == FMT_FP8) {
+      if (fmt_e4m3(FMT)) {
         a[2 * j] = e4m3x2_h2(w[j] & 0xFFFFu);
         a[2 * j + 1] = e4m3x2_h2(w[j] >> 16);
       } else {
@@ -366,7 +414,7 @@ __host__ __device__ inline DecodeSmem decode_smem(int H, int I, int stages, int 
   const int scratch_bytes = fmt_rotated(FMT) ? DEC_WARPS * 256 * 4 : 0;
   s.in = scratch_bytes;
   // phase 1: hi (and lo unless bf16 rows of an fp8 bank) blocks of 8 rows of H; phase 2: hi and lo of I
-  const int terms1 = (FMT == FMT_FP8 && XBF) ? 1 : 2;
+  const int terms1 = ((fmt_e4m3(FMT) && XBF) || fmt_a8(FMT)) ? 1 : 2;
   const int in1 = terms1 * DEC_MAX_CAP * stage_row_halves(H) * 2, in2 = 2 * DEC_MAX_CAP * stage_row_halves(I) * 2;
   s.inv = s.in + (in1 > in2 ? in1 : in2);
   s.rowmax = s.inv + 4 * DEC_MAX_CAP;
@@ -380,12 +428,14 @@ __host__ __device__ inline DecodeSmem decode_smem(int H, int I, int stages, int 
 }
 
 // Bytes of one ring stage: a phase-1 chunk (8 gate rows, 8 up rows, and their group scales) or a phase-2 chunk.
+// A phase-2 chunk's group scales are copied from the 16-byte boundary below their first byte (W4A8 / W6A8 rows of
+// I = 768 hold 12 scale bytes), hence the 32 spare bytes.
 template <int FMT>
 __host__ __device__ constexpr int decode_stage_bytes(int H, int I) {
-  return (2 * DEC_CH1 * (fmt_row_bytes(FMT, H) + (fmt_codes(FMT) ? H / 16 : 0))) >
-                 (DEC_CH2 * (fmt_row_bytes(FMT, I) + (fmt_codes(FMT) ? I / 16 : 0)))
-             ? 2 * DEC_CH1 * (fmt_row_bytes(FMT, H) + (fmt_codes(FMT) ? H / 16 : 0))
-             : DEC_CH2 * (fmt_row_bytes(FMT, I) + (fmt_codes(FMT) ? I / 16 : 0));
+  return (2 * DEC_CH1 * (fmt_row_bytes(FMT, H) + fmt_gscale_bytes(FMT, H))) >
+                 (DEC_CH2 * (fmt_row_bytes(FMT, I) + fmt_gscale_bytes(FMT, I)) + 32)
+             ? 2 * DEC_CH1 * (fmt_row_bytes(FMT, H) + fmt_gscale_bytes(FMT, H))
+             : DEC_CH2 * (fmt_row_bytes(FMT, I) + fmt_gscale_bytes(FMT, I)) + 32;
 }
 
 // The contiguous range [lo, hi) of `total` work items owned by CTA `b` of `g`.
@@ -521,7 +571,7 @@ D3_DEV float4 p1_chunk(const DecodeArgs& a, const uint8_t* stage, int i0, const 
                        const uint32_t (&bl)[TWO ? P1_KC : 1][8], const float* table, const float* lut) {
   constexpr int H = DEC_H;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, c = lane & 3;
-  const int I = a.I, rb = fmt_row_bytes(FMT, H), gb = H / 16;
+  const int I = a.I, rb = fmt_row_bytes(FMT, H), gb = fmt_gscale_bytes(FMT, H);
   const uint8_t* grow = stage + g * rb;
   const uint8_t* urow = stage + (DEC_CH1 + g) * rb;
   const uint8_t* gsrow = stage + 2 * DEC_CH1 * rb + g * gb;
@@ -549,6 +599,14 @@ D3_DEV float4 p1_chunk(const DecodeArgs& a, const uint8_t* stage, int i0, const 
       acc[1] = fmaf(t0[1] + t1[1], sg, acc[1]);
       acc[2] = fmaf(t0[2] + t1[2], su, acc[2]);
       acc[3] = fmaf(t0[3] + t1[3], su, acc[3]);
+    } else if (fmt_a8(FMT)) {
+      // bf16 group-128 scales of the gate / up row (the chunk's 64 columns lie in group kc / 2)
+      const float sg = bf16_to_f32(*(const uint16_t*)(gsrow + 2 * (kc / 2)));
+      const float su = bf16_to_f32(*(const uint16_t*)(usrow + 2 * (kc / 2)));
+      acc[0] = fmaf(t0[0] + t1[0], sg, acc[0]);
+      acc[1] = fmaf(t0[1] + t1[1], sg, acc[1]);
+      acc[2] = fmaf(t0[2] + t1[2], su, acc[2]);
+      acc[3] = fmaf(t0[3] + t1[3], su, acc[3]);
     } else {
 #pragma unroll
       for (int q = 0; q < 4; ++q) acc[q] += t0[q] + t1[q];
@@ -558,16 +616,19 @@ D3_DEV float4 p1_chunk(const DecodeArgs& a, const uint8_t* stage, int i0, const 
 }
 
 // Phase 2, one chunk, one MMA warp: tile warp / 4 (rows 16 * tile .. of the chunk), 64-column chunks kc = warp % 4 + 4m.
+// soff: where the chunk's first group-scale byte sits past the stage's scale area (W4A8 / W6A8, see
+// decode_stage_bytes).
 template <int FMT, int NKC>
-D3_DEV float4 p2_chunk(const DecodeArgs& a, const uint8_t* stage, int n0, const uint32_t (&bh)[NKC][8],
+D3_DEV float4 p2_chunk(const DecodeArgs& a, const uint8_t* stage, int n0, int soff, const uint32_t (&bh)[NKC][8],
                        const uint32_t (&bl)[NKC][8], const float* table, const float* lut) {
+  constexpr bool TWO2 = !fmt_a8(FMT);  // int8-quantized a1 is one exact f16 term
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, c = lane & 3;
-  const int H = DEC_H, I = a.I, rb = fmt_row_bytes(FMT, I), gb = I / 16;
+  const int H = DEC_H, I = a.I, rb = fmt_row_bytes(FMT, I), gb = fmt_gscale_bytes(FMT, I);
   const int tile = warp >> 2, r_lo = 16 * tile + g, r_hi = r_lo + 8;
   const uint8_t* lrow = stage + r_lo * rb;
   const uint8_t* hrow = stage + r_hi * rb;
-  const uint8_t* lsrow = stage + DEC_CH2 * rb + r_lo * gb;
-  const uint8_t* hsrow = stage + DEC_CH2 * rb + r_hi * gb;
+  const uint8_t* lsrow = stage + DEC_CH2 * rb + soff + r_lo * gb;
+  const uint8_t* hsrow = stage + DEC_CH2 * rb + soff + r_hi * gb;
   float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
   for (int m = 0; m < NKC; ++m) {
@@ -579,11 +640,18 @@ D3_DEV float4 p2_chunk(const DecodeArgs& a, const uint8_t* stage, int n0, const 
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       mma16816(t0, la[2 * j], ha[2 * j], la[2 * j + 1], ha[2 * j + 1], bh[m][2 * j], bh[m][2 * j + 1]);
-      mma16816(t1, la[2 * j], ha[2 * j], la[2 * j + 1], ha[2 * j + 1], bl[m][2 * j], bl[m][2 * j + 1]);
+      if (TWO2) mma16816(t1, la[2 * j], ha[2 * j], la[2 * j + 1], ha[2 * j + 1], bl[m][2 * j], bl[m][2 * j + 1]);
     }
     if (FMT == FMT_FP8) {
       const float sl = table[min((n0 + r_lo) / 128, H / 128 - 1) * (I / 128) + kc / 2];
       const float sh = table[min((n0 + r_hi) / 128, H / 128 - 1) * (I / 128) + kc / 2];
+      acc[0] = fmaf(t0[0] + t1[0], sl, acc[0]);
+      acc[1] = fmaf(t0[1] + t1[1], sl, acc[1]);
+      acc[2] = fmaf(t0[2] + t1[2], sh, acc[2]);
+      acc[3] = fmaf(t0[3] + t1[3], sh, acc[3]);
+    } else if (fmt_a8(FMT)) {
+      const float sl = bf16_to_f32(*(const uint16_t*)(lsrow + 2 * (kc / 2)));
+      const float sh = bf16_to_f32(*(const uint16_t*)(hsrow + 2 * (kc / 2)));
       acc[0] = fmaf(t0[0] + t1[0], sl, acc[0]);
       acc[1] = fmaf(t0[1] + t1[1], sl, acc[1]);
       acc[2] = fmaf(t0[2] + t1[2], sh, acc[2]);
@@ -608,7 +676,8 @@ D3_DEV bool mma_phase(const DecodeArgs& a, const DecodePlan& pl, int lo, int hi,
                       __half* xin, float* inv, int* rowmax, float* wscratch, float* table, const float* lut,
                       int* pair_in, int* rows_in) {
   constexpr bool ROT = fmt_rotated(FMT);
-  constexpr bool TWO1 = !(FMT == FMT_FP8 && XBF);
+  constexpr bool A8 = fmt_a8(FMT);
+  constexpr bool TWO1 = !((fmt_e4m3(FMT) && XBF) || A8);
   constexpr int KC = PHASE == 1 ? P1_KC : NKC;
   constexpr bool TWO = PHASE == 1 ? TWO1 : true;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -641,9 +710,9 @@ D3_DEV bool mma_phase(const DecodeArgs& a, const DecodePlan& pl, int lo, int hi,
 #endif
       // a1 holds SwiGLU outputs; ConvRot formats rotate them, as the reference's rotate(swiglu=True) does
       if (PHASE == 1)
-        stage_rows(xin, inv, rowmax, wscratch, a.x, a.x_bf16 != 0, rows_in, cnt, H, ROT, TWO1);
+        stage_rows(xin, inv, rowmax, wscratch, a.x, a.x_bf16 != 0, rows_in, cnt, H, ROT, TWO1, A8);
       else
-        stage_rows(xin, inv, rowmax, wscratch, a.a1, false, rows_in, cnt, I, ROT, true);
+        stage_rows(xin, inv, rowmax, wscratch, a.a1, false, rows_in, cnt, I, ROT, !A8, A8);
       named_sync(1, DEC_CONSUMERS);
       if (PHASE == 1)
         load_b1<TWO1>(xin, (uint32_t(&)[P1_KC][8])bh, (uint32_t(&)[TWO1 ? P1_KC : 1][8])bl);
@@ -670,8 +739,9 @@ D3_DEV bool mma_phase(const DecodeArgs& a, const DecodePlan& pl, int lo, int hi,
         part = p1_chunk<FMT, TWO1>(a, ring + (size_t)st * SB, r, (const uint32_t(&)[P1_KC][8])bh,
                                    (const uint32_t(&)[TWO1 ? P1_KC : 1][8])bl, table, lut);
       else
-        part = p2_chunk<FMT, NKC>(a, ring + (size_t)st * SB, r, (const uint32_t(&)[NKC][8])bh,
-                                  (const uint32_t(&)[NKC][8])bl, table, lut);
+        part = p2_chunk<FMT, NKC>(a, ring + (size_t)st * SB, r,
+                                  A8 ? (int)((((size_t)e * H + r) * fmt_gscale_bytes(FMT, I)) & 15) : 0,
+                                  (const uint32_t(&)[NKC][8])bh, (const uint32_t(&)[NKC][8])bl, table, lut);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty_bar[st]);
@@ -732,9 +802,10 @@ D3_DEV void combine_columns(const DecodeArgs& a, const unsigned char* valid, con
 template <int FMT, bool XBF, int NKC>
 __global__ void __launch_bounds__(DEC_ALL, 1) moe_decode_kernel(const DecodeArgs a) {
   constexpr bool ROT = fmt_rotated(FMT);
-  constexpr bool TWO1 = !(FMT == FMT_FP8 && XBF);  // phase-1 activations need the lo term
+  constexpr bool TWO1 = !((fmt_e4m3(FMT) && XBF) || fmt_a8(FMT));  // phase-1 activations need the lo term
   const int H = DEC_H, I = a.I, P = a.M * a.k, NS = a.stages, SB = a.stage_bytes;
-  const int rb1 = fmt_row_bytes(FMT, H), gb1 = H / 16, rb2 = fmt_row_bytes(FMT, I), gb2 = I / 16;
+  const int rb1 = fmt_row_bytes(FMT, H), gb1 = fmt_gscale_bytes(FMT, H), rb2 = fmt_row_bytes(FMT, I),
+            gb2 = fmt_gscale_bytes(FMT, I);
 
   __shared__ DecodePlan pl;
   __shared__ __align__(8) uint64_t full_bar[DEC_MAX_STAGES], empty_bar[DEC_MAX_STAGES];
@@ -804,22 +875,23 @@ __global__ void __launch_bounds__(DEC_ALL, 1) moe_decode_kernel(const DecodeArgs
           uint8_t* dst = ring + (size_t)st * SB;
           if (phase == 1) {
             const size_t g0 = (size_t)e * 2 * I + r, u0 = g0 + I;
-            const uint32_t bytes = 2u * cn * rb1 + (fmt_codes(FMT) ? 2u * cn * gb1 : 0u);
+            const uint32_t bytes = 2u * cn * rb1 + 2u * cn * gb1;
             mbar_arrive_expect_tx(&full_bar[st], bytes);
             bulk_g2s(dst, a.w13 + g0 * rb1, cn * rb1, &full_bar[st], pol);
             bulk_g2s(dst + DEC_CH1 * rb1, a.w13 + u0 * rb1, cn * rb1, &full_bar[st], pol);
-            if (fmt_codes(FMT)) {
+            if (gb1 > 0) {
               const uint8_t* sc = (const uint8_t*)a.s13;
               bulk_g2s(dst + 2 * DEC_CH1 * rb1, sc + g0 * gb1, cn * gb1, &full_bar[st], pol);
               bulk_g2s(dst + 2 * DEC_CH1 * rb1 + DEC_CH1 * gb1, sc + u0 * gb1, cn * gb1, &full_bar[st], pol);
             }
           } else {
             const size_t n0 = (size_t)e * H + r;
-            const uint32_t bytes = cn * rb2 + (fmt_codes(FMT) ? cn * gb2 : 0);
-            mbar_arrive_expect_tx(&full_bar[st], bytes);
+            // group scales from the 16-byte boundary at or below their first byte, to one at or above their end
+            const size_t s0 = (n0 * gb2) & ~(size_t)15, s1 = ((n0 + cn) * gb2 + 15) & ~(size_t)15;
+            const uint32_t sbytes = gb2 > 0 ? (uint32_t)(s1 - s0) : 0u;
+            mbar_arrive_expect_tx(&full_bar[st], cn * rb2 + sbytes);
             bulk_g2s(dst, a.w2 + n0 * rb2, cn * rb2, &full_bar[st], pol);
-            if (fmt_codes(FMT))
-              bulk_g2s(dst + DEC_CH2 * rb2, (const uint8_t*)a.s2 + n0 * gb2, cn * gb2, &full_bar[st], pol);
+            if (gb2 > 0) bulk_g2s(dst + DEC_CH2 * rb2, (const uint8_t*)a.s2 + s0, sbytes, &full_bar[st], pol);
           }
           q += cn;
         }
@@ -869,7 +941,7 @@ __global__ void __launch_bounds__(DEC_ALL, 1) moe_decode_kernel(const DecodeArgs
           if (g < cn) {
             const int i = r + g;
             float gsc = 1.0f, usc = 1.0f;
-            if (FMT == FMT_I8) {
+            if (fmt_row_scale(FMT)) {
               gsc = __ldg((const float*)a.s13 + (size_t)e * 2 * I + i);
               usc = __ldg((const float*)a.s13 + (size_t)e * 2 * I + I + i);
             } else if (fmt_codes(FMT)) {
@@ -904,7 +976,7 @@ __global__ void __launch_bounds__(DEC_ALL, 1) moe_decode_kernel(const DecodeArgs
               if (row < cn) {
                 const int nrow = r + row;
                 float sc = 1.0f;
-                if (FMT == FMT_I8) sc = __ldg((const float*)a.s2 + (size_t)e * H + nrow);
+                if (fmt_row_scale(FMT)) sc = __ldg((const float*)a.s2 + (size_t)e * H + nrow);
                 if (fmt_codes(FMT)) sc = __ldg(a.c2 + (size_t)e * H + nrow);
                 const float v0 = half ? sum.z : sum.x, v1 = half ? sum.w : sum.y;
                 if (n0 < cnt) __stcg(a.parts + (size_t)rs.pair[n0] * H + nrow, v0 * (sc * rs.inv[n0]));

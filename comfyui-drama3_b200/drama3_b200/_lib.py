@@ -9,8 +9,13 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "libdrama3_b200.so"
 
 D3_OK, D3_ERR_ARG, D3_ERR_ALIGN, D3_ERR_CUDA, D3_ERR_DEVICE, D3_ERR_WORKSPACE, D3_ERR_TOO_LARGE = range(7)
-FMT_FP8, FMT_INT8, FMT_W4, FMT_W6 = range(4)
-FORMATS = {"fp8": FMT_FP8, "int8": FMT_INT8, "w4": FMT_W4, "w6": FMT_W6}
+FMT_FP8, FMT_INT8, FMT_W4, FMT_W6, FMT_FP8C, FMT_W4A8, FMT_W6A8 = range(7)
+# the reference's layouts, then the BASELINE ones (per-channel fp8; W4A8 / W6A8 with int8 activations)
+FORMATS = {"fp8": FMT_FP8, "int8": FMT_INT8, "w4": FMT_W4, "w6": FMT_W6, "fp8c": FMT_FP8C, "w4a8": FMT_W4A8,
+           "w6a8": FMT_W6A8}
+# field holding each format's weight rows
+WEIGHT_KEY = {"fp8": "weight", "fp8c": "weight", "int8": "_qdata", "w4": "_qdata", "w6": "_qdata", "w4a8": "_qdata",
+              "w6a8": "_qdata"}
 
 _p = ctypes.c_void_p
 _i = ctypes.c_int

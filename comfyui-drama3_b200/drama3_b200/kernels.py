@@ -224,9 +224,8 @@ def grouped_mma(kind, x, groups, fields, codebook, n, tiles, row_index=None, rot
     SwiGLU (x holds gate | up) and the ConvRot rotation first, as kernels.rotate would give it. Rows outside every
     group are left unset."""
     fmt = _lib.FORMATS[kind]
-    wkey = "weight" if kind == "fp8" else "_qdata"
-    w = fields[wkey]
-    scale = fields["scale"].view(torch.uint8) if kind in ("w4", "w6") else fields["scale"]
+    w = fields[_lib.WEIGHT_KEY[kind]]
+    scale = fields["scale"]
     if x.dtype not in (torch.float32, torch.bfloat16):
         raise TypeError(f"grouped_mma takes float32 or bfloat16 rows, not {x.dtype}")
     x = x.contiguous()
@@ -278,13 +277,14 @@ def moe_decode(kind, x, ids, weights, banks, codebooks=(None, None), workspace=N
     """[M, H] bfloat16: rows x [M, H] (bfloat16 or float32, M <= 16) through their routed experts ids [M, k] (int64)
     mixed by weights [M, k], with banks (gate_up, down) held whole on the GPU in the reference layouts:
     fp8 {"weight" uint8 [E*2I, H] / [E*H, I], "scale" fp32 block scales}; int8 {"_qdata", "scale"};
-    w4/w6 {"_qdata", "scale" (e4m3 bytes), "s_channel"} and a codebook per bank for w4. Each routed expert is read
+    w4/w6 {"_qdata", "scale" (e4m3 bytes), "s_channel"} and a codebook per bank for w4; the BASELINE layouts fp8c
+    {"weight", "scale" fp32 [E*N]} and w4a8 / w6a8 {"_qdata", "scale" bf16 [E*N, K/128]}. Each routed expert is read
     once for all M rows."""
     fmt = _lib.FORMATS[kind]
     if x.dtype not in (torch.bfloat16, torch.float32):
         raise TypeError(f"moe_decode takes bfloat16 or float32 rows, not {x.dtype}")
     gate_up, down = banks
-    wkey = "weight" if kind == "fp8" else "_qdata"
+    wkey = _lib.WEIGHT_KEY[kind]
     M, H = x.shape
     k = ids.shape[-1]
     w13, w2 = gate_up[wkey], down[wkey]
@@ -297,8 +297,7 @@ def moe_decode(kind, x, ids, weights, banks, codebooks=(None, None), workspace=N
     x = x.contiguous()
     ids = ids.reshape(M, k).contiguous()
     weights = weights.reshape(M, k).float().contiguous()
-    scale13 = gate_up["scale"].view(torch.uint8) if kind in ("w4", "w6") else gate_up["scale"]
-    scale2 = down["scale"].view(torch.uint8) if kind in ("w4", "w6") else down["scale"]
+    scale13, scale2 = gate_up["scale"], down["scale"]
     with _on(x.device):
         check(lib().d3_moe_decode(fmt, _ptr(x), int(x.dtype == torch.bfloat16), M, k, E, H, I, _ptr(ids),
                                   _ptr(weights), _ptr(w13), _ptr(scale13), _ptr(gate_up.get("s_channel")), _ptr(w2),

@@ -37,6 +37,12 @@ extern "C" {
 #define D3_FMT_INT8 1 /* int8 ConvRot rows + fp32 row scales */
 #define D3_FMT_W4 2   /* 4-bit codes + e4m3 group-16 scales + s_channel + 16-entry codebook, ConvRot */
 #define D3_FMT_W6 3   /* 6-bit codes (nibble plane + 2-bit plane) + e4m3 group-16 scales + s_channel, ConvRot */
+/* The BASELINE layouts (no counterpart in the reference; d3_moe_decode and d3_grouped_mma): */
+#define D3_FMT_FP8C 4 /* e4m3 rows + fp32 per-output-channel scales [E*N] */
+#define D3_FMT_W4A8 5 /* int4 (-7..7) two per byte, low nibble = even column; bf16 group-128 scales [E*N, K/128];
+                       * activations quantized to int8 per row (absmax / 127) before each GEMV */
+#define D3_FMT_W6A8 6 /* int6 (-31..31), four per three bytes (24-bit little-endian words); bf16 group-128 scales;
+                       * int8 activations as W4A8 */
 
 int d3_version(void);
 const char* d3_error_string(int code);

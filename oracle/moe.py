@@ -489,3 +489,159 @@ def make_bank(kind, w, codebook=CODEBOOK4):
         return {"_qdata": q, "scale": s}
     q, g, c = quantize_codes(flat, int(kind[1]), codebook)
     return {"_qdata": q, "scale": g, "s_channel": c}
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# The BASELINE layouts (BASELINE.json configs[1..3]). The reference has no implementation of these three; they are
+# restated from the benchmark's description, with every unspecified choice named here:
+#   fp8c   e4m3 rows [E*N, K], fp32 per-output-channel scale [E*N] = absmax / 448 (configs[1])
+#   w4a8   int4 symmetric (-7..7), two per byte along K, low nibble = even column, two's complement nibbles;
+#          bf16 group scales [E*N, K/128] = absmax / 7 (configs[2])
+#   w6a8   int6 symmetric (-31..31), four per three bytes along K: the 24-bit little-endian word
+#          q0 | q1 << 6 | q2 << 12 | q3 << 18 (6-bit two's complement each); bf16 group scales = absmax / 31
+#          (configs[3])
+# A8: every GEMV / GEMM input row is quantized to int8 per row (token, or routed pair for the down projection):
+#   s = absmax(row) / 127 (fp32), q = clip(rint(row / s), -127, 127) (half-even), s = 0 -> q = 0.
+#   out[n] = s * sum over 128-column groups g of float(scale[n, g]) * sum_{k in g} q_w[n, k] * q[k].
+BASELINE_KINDS = ("fp8c", "w4a8", "w6a8")
+A8_GROUP = 128
+
+
+def quantize_fp8_channel(w):
+    """[N, K] float -> (e4m3 bytes [N, K], fp32 row scales [N] = absmax / 448)."""
+    w = np.asarray(w, np.float32)
+    scale = (np.abs(w).max(axis=1) / F32(448.0)).astype(np.float32)
+    scale = np.where(scale == 0, F32(1.0), scale).astype(np.float32)
+    return f32_to_e4m3((w / scale[:, None]).astype(np.float32)), scale
+
+
+def dequant_fp8_channel(weight, scale):
+    return e4m3_to_f32(weight).astype(np.float64) * np.asarray(scale, np.float64).reshape(-1, 1)
+
+
+def pack_int4(q):
+    """[N, K] ints in [-8, 7] -> [N, K/2] bytes, low nibble = even column."""
+    q = np.asarray(q, np.int64) & 0xF
+    return (q[:, 0::2] | (q[:, 1::2] << 4)).astype(np.uint8)
+
+
+def unpack_int4(p, K):
+    p = np.asarray(p, np.uint8).astype(np.int64)
+    q = np.empty((p.shape[0], K), np.int64)
+    q[:, 0::2] = p & 0xF
+    q[:, 1::2] = p >> 4
+    return np.where(q >= 8, q - 16, q).astype(np.int8)
+
+
+def pack_int6(q):
+    """[N, K] ints in [-32, 31] -> [N, 3K/4] bytes: each 4 values a little-endian 24-bit word."""
+    q = np.asarray(q, np.int64) & 0x3F
+    N, K = q.shape
+    g = q.reshape(N, K // 4, 4)
+    word = g[..., 0] | (g[..., 1] << 6) | (g[..., 2] << 12) | (g[..., 3] << 18)
+    out = np.stack([word & 0xFF, (word >> 8) & 0xFF, (word >> 16) & 0xFF], axis=-1)
+    return out.reshape(N, 3 * K // 4).astype(np.uint8)
+
+
+def unpack_int6(p, K):
+    p = np.asarray(p, np.uint8).astype(np.int64)
+    N = p.shape[0]
+    b = p.reshape(N, K // 4, 3)
+    word = b[..., 0] | (b[..., 1] << 8) | (b[..., 2] << 16)
+    q = np.stack([(word >> (6 * i)) & 0x3F for i in range(4)], axis=-1).reshape(N, K)
+    return np.where(q >= 32, q - 64, q).astype(np.int8)
+
+
+def quantize_wa8(w, bits):
+    """[N, K] float -> (packed codes, bf16 group scales as uint16 [N, K/128]) of w4a8 (bits 4) / w6a8 (bits 6)."""
+    w = np.asarray(w, np.float32)
+    N, K = w.shape
+    qmax = 7 if bits == 4 else 31
+    groups = w.reshape(N, K // A8_GROUP, A8_GROUP)
+    s = (np.abs(groups).max(axis=2) / F32(qmax)).astype(np.float32)
+    s_bits = f32_to_bf16(np.where(s == 0, F32(1.0), s).astype(np.float32))
+    sv = bf16_to_f32(s_bits).astype(np.float64)
+    q = np.clip(np.rint(groups / sv[:, :, None]), -qmax, qmax).astype(np.int64).reshape(N, K)
+    return (pack_int4(q) if bits == 4 else pack_int6(q)), s_bits
+
+
+def quantize_rows_int8(x):
+    """Rows [R, K] -> (int8 [R, K], fp32 scales [R]): per row absmax / 127, round half even, clip +-127."""
+    x = np.asarray(x, np.float32)
+    s = (np.abs(x).max(axis=1) / F32(127.0)).astype(np.float32)
+    safe = np.where(s == 0, F32(1.0), s).astype(np.float32)
+    q = np.clip(np.rint(x / safe[:, None]), -127, 127)
+    q = np.where(s[:, None] == 0, 0, q).astype(np.int8)
+    return q, s
+
+
+def wa8_codes(kind, fields, first_row, rows, K):
+    sl = slice(first_row, first_row + rows)
+    return unpack_int4(fields["_qdata"][sl], K) if kind == "w4a8" else unpack_int6(fields["_qdata"][sl], K)
+
+
+def gemm_wa8(kind, x, fields, first_row, rows):
+    """x [R, K] (float32) through weight rows [first_row, + rows) of a w4a8 / w6a8 bank: [R, rows] float32, with x
+    quantized to int8 per row."""
+    x = np.asarray(x, np.float32)
+    K = x.shape[1]
+    q, s = quantize_rows_int8(x)
+    w = wa8_codes(kind, fields, first_row, rows, K).astype(np.int64)
+    gs = bf16_to_f32(np.asarray(fields["scale"])[first_row:first_row + rows]).astype(np.float64)  # [rows, K/128]
+    G = K // A8_GROUP
+    dots = np.einsum("rgk,ngk->rng", q.astype(np.int64).reshape(-1, G, A8_GROUP), w.reshape(rows, G, A8_GROUP))
+    out = (dots.astype(np.float64) * gs[None, :, :]).sum(axis=2) * s.astype(np.float64)[:, None]
+    return out.astype(np.float32)
+
+
+def baseline_rows(kind, x, fields, first_row, rows):
+    """x [R, K] through weight rows [first_row, + rows) of a BASELINE-layout bank: [R, rows] float32."""
+    if kind == "fp8c":
+        sl = slice(first_row, first_row + rows)
+        w = dequant_fp8_channel(fields["weight"][sl], np.asarray(fields["scale"]).reshape(-1)[sl])
+        return (np.asarray(x, np.float64) @ w.T).astype(np.float32)
+    return gemm_wa8(kind, x, fields, first_row, rows)
+
+
+def baseline_decode(kind, x, ids, weights, banks):
+    """Rows x [M, H] through their routed experts of BASELINE-layout banks held whole: per pair gate_up, SiLU(gate) *
+    up, down (input quantized per pair for w4a8 / w6a8), then the routing-weighted sum in rank order, bf16."""
+    gate_up, down = banks
+    x = np.asarray(x, np.float32)
+    M, H = x.shape
+    key = "weight" if kind == "fp8c" else "_qdata"
+    E = down[key].shape[0] // H
+    n1 = gate_up[key].shape[0] // E
+    I = n1 // 2
+    ids = np.asarray(ids)
+    parts = np.zeros((M, ids.shape[1], H), np.float32)
+    for t in range(M):
+        for j, e in enumerate(ids[t]):
+            h = baseline_rows(kind, x[t:t + 1], gate_up, int(e) * n1, n1)
+            a = _silu_mul(h[:, :I], h[:, I:])
+            parts[t, j] = baseline_rows(kind, a, down, int(e) * H, H)[0]
+    w = np.asarray(weights, np.float32)
+    out = np.zeros((M, H), np.float32)
+    for t in range(M):
+        acc = np.zeros(H, np.float32)
+        for j in range(ids.shape[1]):
+            acc = fma32(parts[t, j], np.full(H, w[t, j], np.float32), acc)
+        out[t] = acc
+    return bf16_round(out)
+
+
+def baseline_prefill(kind, x, topk_idx, topk_weight, banks):
+    """Many rows of a prompt through BASELINE-layout banks: the same per-pair arithmetic as baseline_decode, summed
+    in rank order; bf16."""
+    return baseline_decode(kind, x, topk_idx, topk_weight, banks)
+
+
+def make_baseline_bank(kind, w):
+    """Fields of one flat BASELINE-layout bank [E * N, ...] from float experts w [E, N, K]."""
+    E, N, K = w.shape
+    flat = np.asarray(w, np.float32).reshape(E * N, K)
+    if kind == "fp8c":
+        q, s = quantize_fp8_channel(flat)
+        return {"weight": q, "scale": s}
+    q, s = quantize_wa8(flat, 4 if kind == "w4a8" else 6)
+    return {"_qdata": q, "scale": s}

@@ -5,7 +5,9 @@ import torch
 from oracle import moe
 
 KINDS = ("fp8", "int8", "w4", "w6")
-WKEY = {"fp8": "weight", "int8": "_qdata", "w4": "_qdata", "w6": "_qdata"}
+BASELINE_KINDS = ("fp8c", "w4a8", "w6a8")
+WKEY = {"fp8": "weight", "int8": "_qdata", "w4": "_qdata", "w6": "_qdata", "fp8c": "weight", "w4a8": "_qdata",
+        "w6a8": "_qdata"}
 
 
 def _rand_e4m3(gen, shape, lo, hi, device):
@@ -24,6 +26,15 @@ def rand_bank(kind, E, N, K, seed, device):
     if kind == "int8":
         q = torch.randint(-127, 128, (E * N, K), generator=gen, dtype=torch.int8)
         s = torch.rand((E * N,), generator=gen) * 2e-4 + 1e-4
+        return {"_qdata": q.to(device), "scale": s.to(device)}
+    if kind == "fp8c":
+        w = torch.randint(0, 254, (E * N, K), generator=gen, dtype=torch.int32)
+        w = torch.where(w >= 0x7F, w + 1, w).to(torch.uint8)
+        s = torch.rand((E * N,), generator=gen) * 1e-4 + 5e-5
+        return {"weight": w.to(device), "scale": s.to(device)}
+    if kind in ("w4a8", "w6a8"):
+        q = torch.randint(0, 256, (E * N, K * int(kind[1]) // 8), generator=gen, dtype=torch.int32).to(torch.uint8)
+        s = (torch.rand((E * N, K // 128), generator=gen) * 2e-3 + 1e-3).to(torch.bfloat16)
         return {"_qdata": q.to(device), "scale": s.to(device)}
     bits = int(kind[1])
     q = torch.randint(0, 256, (E * N, K * bits // 8), generator=gen, dtype=torch.int32).to(torch.uint8)
@@ -56,8 +67,19 @@ def rand_routing(M, E, k, seed, device, skew=None):
     return ids.to(device), w.to(device)
 
 
+def to_np(t):
+    t = t.cpu()
+    return t.view(torch.int16).numpy().view(np.uint16) if t.dtype == torch.bfloat16 else t.numpy()
+
+
 def to_np_bank(bank):
-    return {n: t.cpu().numpy() for n, t in bank.items()}
+    return {n: to_np(t) for n, t in bank.items()}
+
+
+def baseline_oracle_decode(kind, x, ids, weights, banks):
+    """oracle.baseline_decode on the whole (small) banks."""
+    return moe.baseline_decode(kind, x.float().cpu().numpy(), ids.cpu().numpy(), weights.cpu().numpy(),
+                               tuple(to_np_bank(b) for b in banks))
 
 
 def subset(kind, bank, experts, rows):
