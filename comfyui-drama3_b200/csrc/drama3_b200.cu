@@ -342,8 +342,9 @@ int d3_grouped_mma(int fmt, const void* x, int x_bf16, const int64_t* row_index,
                    size_t workspace_bytes, void* stream) {
   DeviceInfo d;
   if (int st = device_info(&d)) return st;
-  if (fmt < d3::FMT_FP8 || fmt > d3::FMT_W6 || n_groups < 0 || tiles < 0) return D3_ERR_ARG;
+  if (fmt < 0 || fmt >= d3::FMT_COUNT || n_groups < 0 || tiles < 0) return D3_ERR_ARG;
   if (mode < 0 || mode > (d3::GM_ROTATE | d3::GM_SWIGLU)) return D3_ERR_ARG;
+  if (d3::fmt_a8(fmt)) mode |= d3::GM_INT8;  // A8 formats always quantize their inputs to int8
   if (N < d3::GM_M || N % d3::GM_M || K < 256 || K % 256 || K > 2048 || bank_rows < N || bank_rows % d3::GM_M)
     return D3_ERR_ARG;
   if (!x || !groups || !weight || !scale || !out || !workspace) return D3_ERR_ARG;
@@ -361,8 +362,9 @@ int d3_grouped_mma(int fmt, const void* x, int x_bf16, const int64_t* row_index,
   int* ntiles = (int*)(table + tiles);
   CUtensorMap wmap, pmap;
   const uint64_t row_bytes = (uint64_t)d3::fmt_row_bytes(fmt, K);
-  // one raw stage = 128 columns: fp8 / int8 128 bytes per row; W4 / W6 nibbles 64; the W6 high plane 32
-  const uint32_t box = fmt == d3::FMT_FP8 || fmt == d3::FMT_I8 ? 128 : 64;
+  // one raw stage = 128 columns: fp8 / fp8c / int8 128 bytes per row; W4 / W6 nibbles and W4A8 64; W6A8 96; the W6
+  // high plane 32
+  const uint32_t box = d3::fmt_e4m3(fmt) || fmt == d3::FMT_I8 ? 128 : fmt == d3::FMT_W6A8 ? 96 : 64;
   if (!byte_tile_map(&wmap, weight, row_bytes, (uint64_t)bank_rows, box)) return D3_ERR_ARG;
   pmap = wmap;
   if (fmt == d3::FMT_W6 && !byte_tile_map(&pmap, weight, row_bytes, (uint64_t)bank_rows, 32)) return D3_ERR_ARG;
@@ -383,6 +385,9 @@ int d3_grouped_mma(int fmt, const void* x, int x_bf16, const int64_t* row_index,
     D3_GM_CASE(d3::FMT_I8)
     D3_GM_CASE(d3::FMT_W4)
     D3_GM_CASE(d3::FMT_W6)
+    D3_GM_CASE(d3::FMT_FP8C)
+    D3_GM_CASE(d3::FMT_W4A8)
+    D3_GM_CASE(d3::FMT_W6A8)
 #undef D3_GM_CASE
   }
   return D3_ERR_ARG;

@@ -82,7 +82,9 @@ __host__ __device__ constexpr size_t gm_workspace_bytes(int tiles, int K) {
 //   mode bit GM_ROTATE: each 256-column group is rotated by the reference's radix-4 butterfly (ConvRot,
 //        drama3/kernels.py:240-256), the 1/16 folded into inv
 // Needs K % 256 == 0, K <= 2048.
-enum { GM_ROTATE = 1, GM_SWIGLU = 2 };
+//   mode bit GM_INT8 (W4A8 / W6A8): the row is quantized to int8 by its exact max (s = max / 127, q = rint(x / s)
+//        clamped, IEEE division) and staged as one exact f16 term; inv = s
+enum { GM_ROTATE = 1, GM_SWIGLU = 2, GM_INT8 = 4 };
 
 D3_DEV float gm_load(const void* x, bool bf16, size_t i) {
   return bf16 ? bf16_to_f32(((const uint16_t*)x)[i]) : ((const float*)x)[i];
@@ -153,6 +155,7 @@ __global__ void __launch_bounds__(256) gm_stage_kernel(const void* __restrict__ 
   const int row0 = first + s_local * GM_NT, rows = min(GM_NT, count - s_local * GM_NT);
   if (threadIdx.x == 0) table[t] = GroupedTile{g, row0, rows, 0};
   const bool bf16 = src_bf16 != 0, rotate = (mode & GM_ROTATE) != 0, swiglu = (mode & GM_SWIGLU) != 0;
+  const bool int8q = (mode & GM_INT8) != 0;
   const int nkc = K / GM_KC, nq = K / 256;
   const size_t pitch = swiglu ? 2 * (size_t)K : (size_t)K;
   uint8_t* tile_base = staged + (size_t)t * nkc * 2 * GM_B_BYTES;
@@ -207,10 +210,21 @@ __global__ void __launch_bounds__(256) gm_stage_kernel(const void* __restrict__ 
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     const int e = stage_exponent(m);
     const float scale = __uint_as_float((uint32_t)(e + 127) << 23);
+    const float qs = __fdiv_rn(m, 127.0f);  // int8 scale (GM_INT8)
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       if (q >= nq) break;
       uint32_t hw[4], lw[4];
+      if (int8q) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float q0 = qs > 0.0f ? fminf(127.0f, fmaxf(-127.0f, rintf(__fdiv_rn(v[q][2 * u], qs)))) : 0.0f;
+          const float q1 = qs > 0.0f ? fminf(127.0f, fmaxf(-127.0f, rintf(__fdiv_rn(v[q][2 * u + 1], qs)))) : 0.0f;
+          hw[u] = (uint32_t)__half_as_ushort(__float2half_rn(q0)) |
+                  ((uint32_t)__half_as_ushort(__float2half_rn(q1)) << 16);
+          lw[u] = 0u;
+        }
+      } else {
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const float s0 = v[q][2 * u] * scale, s1 = v[q][2 * u + 1] * scale;
@@ -218,6 +232,7 @@ __global__ void __launch_bounds__(256) gm_stage_kernel(const void* __restrict__ 
         hw[u] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
         const __half l0 = __float2half_rn(s0 - __half2float(h0)), l1 = __float2half_rn(s1 - __half2float(h1));
         lw[u] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+      }
       }
       // columns 256q + 8 lane .. + 7: chunk kc = 4q + lane / 8, 16-byte piece c = lane % 8
       const int kc = 4 * q + (lane >> 3), c = lane & 7;
@@ -227,7 +242,7 @@ __global__ void __launch_bounds__(256) gm_stage_kernel(const void* __restrict__ 
     }
     if (lane == 0)
       inv[(size_t)t * GM_NT + j] =
-          live ? (rotate ? 0.0625f : 1.0f) * __uint_as_float((uint32_t)(127 - e) << 23) : 0.0f;
+          !live ? 0.0f : int8q ? qs : (rotate ? 0.0625f : 1.0f) * __uint_as_float((uint32_t)(127 - e) << 23);
   }
 }
 
@@ -362,10 +377,16 @@ struct GmSmem {
   static constexpr int launch = total + 1024;  // slack to align the base to 1024 bytes
 };
 
-// Raw bytes per weight row in one raw stage (128 columns): fp8 / int8 128, W4 nibbles 64, W6 nibbles 64 + plane 32.
+// Raw bytes per weight row in one raw stage (128 columns): fp8 / fp8c / int8 128, W4 nibbles 64, W6 nibbles 64 +
+// plane 32, W4A8 64, W6A8 96.
 template <int FMT>
 __host__ __device__ constexpr int gm_raw_row_bytes() {
-  return FMT == FMT_FP8 || FMT == FMT_I8 ? 128 : FMT == FMT_W4 ? 64 : 96;
+  return fmt_e4m3(FMT) || FMT == FMT_I8 ? 128 : FMT == FMT_W4 || FMT == FMT_W4A8 ? 64 : 96;
+}
+// Formats folded every 128 columns (a scale per 128-column block of each row): fp8 blocks, W4A8 / W6A8 groups.
+template <int FMT>
+__host__ __device__ constexpr bool gm_folds() {
+  return FMT == FMT_FP8 || fmt_a8(FMT);
 }
 
 // The unit (tile, row block) a CTA takes k-th, or false past the end.
@@ -383,7 +404,38 @@ D3_DEV bool gm_unit(const GmArgs& a, int ntiles, int u, int& tile, int& rb) {
 // c ^ ((r / 4) % 2).
 template <int FMT>
 D3_DEV void gm_convert(const uint8_t* raw, int h, uint8_t* astage, int r, uint32_t sbytes, const float* lut) {
-  if (FMT == FMT_FP8 || FMT == FMT_I8) {
+  if (FMT == FMT_W4A8) {
+    // 64-byte rows (swizzled like the W4 nibbles): 16-column group g = 4h + p is 8 bytes
+    const uint8_t* low = raw + r * 64;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const int g = 4 * h + p;
+      const uint2 lw = *(const uint2*)(low + (((g >> 1) ^ ((r >> 1) & 3)) << 4) + 8 * (g & 1));
+      uint32_t o[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = s4x2_h2(((i < 4 ? lw.x : lw.y) >> (8 * (i & 3))) & 0xFFu);
+      *(uint4*)(astage + sw128_offset(r, 2 * p)) = make_uint4(o[0], o[1], o[2], o[3]);
+      *(uint4*)(astage + sw128_offset(r, 2 * p + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+    }
+  } else if (FMT == FMT_W6A8) {
+    // 96-byte rows, no swizzle: 16-column group g = 4h + p is 12 bytes at 12 g
+    const uint8_t* row = raw + r * 96;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const uint32_t* q = (const uint32_t*)(row + 12 * (4 * h + p));
+      const uint32_t w[3] = {q[0], q[1], q[2]};
+      uint32_t c[16], o[8];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int bit = 6 * i, k = bit >> 5, off = bit & 31;
+        c[i] = __funnelshift_r(w[k], k < 2 ? w[k + 1] : 0u, off) & 63u;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = s6x2_h2(c[2 * i], c[2 * i + 1]);
+      *(uint4*)(astage + sw128_offset(r, 2 * p)) = make_uint4(o[0], o[1], o[2], o[3]);
+      *(uint4*)(astage + sw128_offset(r, 2 * p + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+    }
+  } else if (fmt_e4m3(FMT) || FMT == FMT_I8) {
     const uint8_t* row = raw + r * 128;
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
@@ -393,7 +445,7 @@ D3_DEV void gm_convert(const uint8_t* raw, int h, uint8_t* astage, int r, uint32
       uint32_t o[8];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        if (FMT == FMT_FP8) {
+        if (fmt_e4m3(FMT)) {
           o[2 * j] = e4m3x2_h2(w[j] & 0xFFFFu);
           o[2 * j + 1] = e4m3x2_h2(w[j] >> 16);
         } else {
@@ -489,8 +541,12 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
           if (!ok) break;
           uint8_t* dst = smem + GmSmem::raw + rs * GM_RAW_BYTES;
           mbar_arrive_expect_tx(raw_full + rs, GM_M * gm_raw_row_bytes<FMT>());
-          if (FMT == FMT_FP8 || FMT == FMT_I8) {
+          if (fmt_e4m3(FMT) || FMT == FMT_I8) {
             tma_load_2d(dst, &wmap, kr * 128, wrow, raw_full + rs);
+          } else if (FMT == FMT_W4A8) {
+            tma_load_2d(dst, &wmap, kr * 64, wrow, raw_full + rs);
+          } else if (FMT == FMT_W6A8) {
+            tma_load_2d(dst, &wmap, kr * 96, wrow, raw_full + rs);
           } else {
             tma_load_2d(dst, &wmap, kr * 64, wrow, raw_full + rs);
             if (FMT == FMT_W6) tma_load_2d(dst + GM_M * 64, &pmap, a.K / 2 + kr * 32, wrow, raw_full + rs);
@@ -519,9 +575,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
           if (!ok) break;
           uint8_t* dst = smem + GmSmem::b + ms * 2 * GM_B_BYTES;
           const uint8_t* blk = src + (size_t)kc * 2 * GM_B_BYTES;
-          mbar_arrive_expect_tx(b_full + ms, 2 * bytes);
+          mbar_arrive_expect_tx(b_full + ms, fmt_a8(FMT) ? bytes : 2 * bytes);
           bulk_g2s(dst, blk, bytes, b_full + ms, keep);
-          bulk_g2s(dst + GM_B_BYTES, blk + GM_B_BYTES, bytes, b_full + ms, keep);
+          if (!fmt_a8(FMT)) bulk_g2s(dst + GM_B_BYTES, blk + GM_B_BYTES, bytes, b_full + ms, keep);
           if (++ms == GM_MMA_ST) {
             ms = 0;
             mph ^= 1;
@@ -534,7 +590,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     if (lane == 0) {
       int ms = 0, folds = 0;
       uint32_t mph = 0;
-      const int kbc = FMT == FMT_FP8 ? 128 / GM_KC : nkc;  // chunks per fold
+      const int kbc = gm_folds<FMT>() ? 128 / GM_KC : nkc;  // chunks per fold
       int tile, rb;
       for (int u = blockIdx.x; ok && gm_unit(a, ntiles, u, tile, rb); u += G) {
         const int slot = a.groups[5 * a.table[tile].group + 1];
@@ -558,7 +614,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
           for (int ks = 0; ks < GM_KC / 16; ++ks) {
             const uint64_t ad = umma_desc_sw128(as + 32 * ks);
             umma_f16(acc, ad, umma_desc_sw128(bs + 32 * ks), idesc, (kc % kbc != 0 || ks != 0) ? 1u : 0u);
-            umma_f16(acc, ad, umma_desc_sw128(bs + GM_B_BYTES + 32 * ks), idesc, 1u);
+            if (!fmt_a8(FMT)) umma_f16(acc, ad, umma_desc_sw128(bs + GM_B_BYTES + 32 * ks), idesc, 1u);
           }
           umma_commit(mma_empty + ms);
           if (kc % kbc == kbc - 1) {
@@ -613,7 +669,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     const int quarter = warp & 3;
     const int r = 32 * quarter + lane;
     const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
-    const int kbc = FMT == FMT_FP8 ? 128 / GM_KC : nkc;
+    const int kbc = gm_folds<FMT>() ? 128 / GM_KC : nkc;
     const int nfold = nkc / kbc;
     int folds = 0;
     int tile, rb;
@@ -627,8 +683,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       }
       const float* inv = a.inv + (size_t)tile * GM_NT;
       float* dst = a.out + (size_t)tl.row0 * a.N + rb * GM_M + r;
-      if (FMT == FMT_FP8) {
-        // one fold per 128 columns: acc += block scale x partial
+      if (gm_folds<FMT>()) {
+        // one fold per 128 columns: acc += scale x partial (fp8: the 128 x 128 block's; W4A8 / W6A8: the row's
+        // bf16 group scale)
         float acc[GM_NT];
 #pragma unroll
         for (int j = 0; j < GM_NT; ++j) acc[j] = 0.0f;
@@ -637,7 +694,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
           ok = mbar_wait(acc_full + region, (folds >> 1) & 1);
           if (!ok) break;
           tc_fence_after();
-          const float s = __ldg((const float*)a.scale + (size_t)(wrow / 128) * (a.K / 128) + f);
+          const float s = FMT == FMT_FP8
+                              ? __ldg((const float*)a.scale + (size_t)(wrow / 128) * (a.K / 128) + f)
+                              : bf16_to_f32(__ldg((const uint16_t*)a.scale + (size_t)(wrow + r) * (a.K / 128) + f));
 #pragma unroll
           for (int c = 0; c < GM_NT / 16; ++c) {
             if (16 * c >= tl.rows) break;
@@ -661,7 +720,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         ok = mbar_wait(acc_full + region, (folds >> 1) & 1);
         if (!ok) break;
         tc_fence_after();
-        const float rs = FMT == FMT_I8 ? __ldg((const float*)a.scale + wrow + r) : __ldg(a.s_channel + wrow + r);
+        const float rs = fmt_row_scale(FMT) ? __ldg((const float*)a.scale + wrow + r) : __ldg(a.s_channel + wrow + r);
 #pragma unroll 1
         for (int c = 0; 16 * c < tl.rows; ++c) {
           float v[16];

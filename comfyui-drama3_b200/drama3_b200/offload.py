@@ -38,6 +38,9 @@ RESERVE_START, RESERVE_MIN, RESERVE_MAX = 32, 8, 256
 ADMIT = 6.0
 # the fused decode's limit on rows per call
 MAX_DECODE_ROWS = 16
+# formats whose activations are ConvRot-rotated; the BASELINE layouts (no reference kernels, fused paths only)
+ROTATED_KINDS = ("int8", "w4", "w6")
+BASELINE_KINDS = ("fp8c", "w4a8", "w6a8")
 
 
 def pinned(tensor, pin):
@@ -120,7 +123,7 @@ FUSED_HIDDEN, FUSED_INTERMEDIATE, FUSED_MAX_PAIRS = 2048, (512, 768), 128
 def _decode_banks(banks, rows, kind):
     """(gate_up, down) field dicts checked against the per-expert row counts, and (E, H, I)."""
     gate_up, down = banks
-    key = "weight" if kind == "fp8" else "_qdata"
+    key = "weight" if kind in ("fp8", "fp8c") else "_qdata"
     if gate_up[key].shape[0] % rows[0] or down[key].shape[0] % rows[1]:
         raise ValueError("bank rows are not a whole number of experts")
     experts = gate_up[key].shape[0] // rows[0]
@@ -139,6 +142,8 @@ def _decode_sequence(x, ids, weights, banks, rows, kind, codebooks):
     """One row through the reference's kernel sequence (drama3/offload.py:112-123): gemv, SwiGLU [+ rotation], gemv,
     weighted sum; used for shapes the fused kernel is not built for."""
     gate_up, down = banks
+    if kind in BASELINE_KINDS:
+        raise ValueError(f"{kind} banks decode through the fused kernel only (hidden 2048, intermediate 512 / 768)")
     plan = torch.stack((ids.to(torch.int32), torch.zeros_like(ids, dtype=torch.int32)), dim=-1)
     if kind == "fp8":
         gate, up = kernels.gemv_fp8(x.float(), ids, plan, gate_up, gate_up, rows[0]).chunk(2, dim=-1)
@@ -221,19 +226,21 @@ def resident_prefill(x, topk_idx, topk_weight, banks, rows, kind, codebooks, num
     groups = torch.tensor(groups, dtype=torch.int32).to(x.device)
     tiles = kernels.grouped_tiles(counts)
     gate_up, down = banks
-    quantized = kind != "fp8"
+    rotated = kind in ROTATED_KINDS
     width = x.shape[1]
     if (x.dtype in (torch.bfloat16, torch.float32) and kernels.grouped_mma_fits(rows[0], width)
             and kernels.grouped_mma_fits(rows[1], rows[0] // 2)):
         hidden = kernels.grouped_mma(kind, x, groups, gate_up, codebooks[0], rows[0], tiles, row_index=order // top_k,
-                                     rotate=quantized)
-        sorted_out = kernels.grouped_mma(kind, hidden, groups, down, codebooks[1], rows[1], tiles, rotate=quantized,
+                                     rotate=rotated)
+        sorted_out = kernels.grouped_mma(kind, hidden, groups, down, codebooks[1], rows[1], tiles, rotate=rotated,
                                          swiglu=True)
         pos = torch.empty_like(order)
         pos[order] = torch.arange(order.numel(), device=order.device)
         out = kernels.prefill_combine(sorted_out, pos.view(num_tokens, top_k), topk_weight,
                                       dtype=torch.float32 if x.dtype == torch.float32 else torch.bfloat16)
         return out.to(x.dtype)
+    if kind in BASELINE_KINDS:
+        raise ValueError(f"{kind} banks run on the tensor-core kernel only (N % 128, K % 256)")
     always = torch.ones((1,), dtype=torch.int32, device=x.device)
     sorted_x = x[order // top_k].float()
     if kind == "fp8":
