@@ -1,20 +1,25 @@
-"""Benchmark: MoE decode tokens/s of the routed-expert path on B200 (FP8 experts).
+"""Benchmark: MoE decode tokens/s of the routed-expert path on B200 (FP8 experts with
+per-output-channel scales).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mine|reference] [--lines 16] [--layers 48]
+                    [--kind fp8c] [--no-extras] [--prefill-only]
     torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU)
 
 A step is one decode pass of `lines` rows (16: lines decoded together) through 48 MoE layers of the BASELINE shape
-(hidden 2048, 128 experts, top-8, intermediate 768, SwiGLU), each layer with its own FP8 banks (e4m3 + 128x128
-block scales, the reference layout) and its own seeded routing: 29 GB of experts, far larger than L2, so every
-step streams its experts from HBM (no flush needed). Inputs are resident in HBM; the timed region replays one CUDA
-graph per step. Multi-GPU: independent replicas (each rank decodes its own lines with all experts resident; no
-collective), weak scaling. `value` = tokens/s of all ranks; timing = CUDA events, max over ranks. The timed region
-is bracketed by cudaProfilerStart/Stop, so `ncu --profile-from-start off` sees exactly its launches; `--layers 4` is
-the small case for multi-pass captures (same per-layer shapes and routing as the first 4 layers of the full run).
+(hidden 2048, 128 experts, top-8, intermediate 768, SwiGLU), each layer with its own expert banks (default fp8c:
+e4m3 rows + fp32 per-output-channel scales) and its own seeded routing: 29 GB of experts, far
+larger than L2, so every step streams its experts from HBM (no flush needed). Inputs are resident in HBM; the timed
+region replays one CUDA graph per step and is bracketed by cudaProfilerStart/Stop, so `ncu --profile-from-start off`
+sees exactly its launches; `--layers 4` is the small case for multi-pass captures (the same banks and routing as the
+first 4 layers of the full run). Multi-GPU: independent replicas (each rank decodes its own lines with all experts
+resident; no collective), weak scaling. `value` = tokens/s of all ranks; timing = CUDA events, max over ranks.
 
-Also reported: the 1-line decode, the end-to-end rate through the Python API with host buffers, the reference's own
-kernels (compiled from drama3/kernels.py into oracle/_ref) on the same GPU, and the reference's CPU path on the host
-cores. `--impl reference` runs only that CPU path (rank 0) and prints its line.
+Also reported (rank 0): the 1-line decode; W4A8 at 16 and 1 lines; the reference's fp8 layout
+(128 x 128 block scales) at 16 lines beside the reference's own kernels (compiled from drama3/kernels.py into
+oracle/_ref) on the same GPU; the end-to-end rate through the Python API with host buffers; a prompt-pass leg
+(2048 tokens, Zipf-skewed routing; W6A8, and the reference's W6 and fp8 layouts beside the
+reference's kernels); the reference's CPU path on the host cores. `--impl reference` runs only that CPU path
+(rank 0) and prints its line.
 """
 import argparse
 import json
@@ -35,11 +40,60 @@ import torch  # noqa: E402
 METRIC = "MoE decode tokens/s (1 & 16 lines), expert GEMV HBM GB/s vs ~8 TB/s, 1-8 B200"
 E, H, I, K_TOP = 128, 2048, 768, 8
 LAYERS = 48
+KINDS = ("fp8c", "fp8", "w4a8", "w6a8", "w6")
+FORMAT_NAMES = {
+    "fp8c": "e4m3 rows + fp32 per-output-channel scales (BASELINE configs[1])",
+    "fp8": "e4m3 rows + fp32 128x128 block scales (the reference's layout)",
+    "w4a8": "int4 two per byte + bf16 group-128 scales, int8 per-row activations (BASELINE configs[2])",
+    "w6a8": "int6 four per three bytes + bf16 group-128 scales, int8 per-row activations (BASELINE configs[3])",
+    "w6": "6-bit codes + e4m3 group-16 scales + s_channel, ConvRot (the reference's W6A8 layout)",
+}
 # dram bytes (read + write) per launch over algorithmic bytes per launch, from the ncu capture of the small case
 # (bench.py --layers 4, all 4 launches of one timed step); the full run's traffic is this ratio x its own bytes
 TRAFFIC_RATIO = 1625.44 / 1609.96
-# algorithmic bytes of one FP8 expert (reference layout): gate_up 1536x2048 + down 2048x768 e4m3, block scales
-EXPERT_BYTES = 2 * I * H + H * I + (2 * I // 128) * (H // 128) * 4 + (H // 128) * (I // 128) * 4
+TRAFFIC_SOURCE = ("ncu capture of the 4-layer small case (bench.py --layers 4 --kind fp8): DRAM read + write / "
+                  "algorithmic bytes of the same launches")
+
+
+def rand_bank(kind, n, k, gen, device):
+    """A flat bank [E * n, ...] of random valid codes in the layout of `kind`."""
+    if kind in ("fp8", "fp8c"):
+        w = torch.randint(0, 254, (E * n, k), generator=gen, device=device, dtype=torch.uint8)
+        w = torch.where(w >= 0x7F, w + 1, w)  # no 0x7F / 0xFF (NaN codes)
+        shape = (E * n // 128, k // 128) if kind == "fp8" else (E * n,)
+        return {"weight": w, "scale": torch.rand(shape, generator=gen, device=device) * 1e-4 + 5e-5}
+    if kind in ("w4a8", "w6a8"):
+        q = torch.randint(0, 256, (E * n, k * int(kind[1]) // 8), generator=gen, device=device, dtype=torch.uint8)
+        s = (torch.rand((E * n, k // 128), generator=gen, device=device) * 2e-3 + 1e-3).to(torch.bfloat16)
+        return {"_qdata": q, "scale": s}
+    q = torch.randint(0, 256, (E * n, 3 * k // 4), generator=gen, device=device, dtype=torch.uint8)
+    g = torch.randint(0x30, 0x50, (E * n, k // 16), generator=gen, device=device, dtype=torch.uint8)
+    c = torch.rand((E * n,), generator=gen, device=device) * 2e-4 + 1e-4
+    return {"_qdata": q, "scale": g, "s_channel": c}
+
+
+def expert_bytes(kind):
+    """Algorithmic bytes of one expert of the BASELINE shape in `kind`'s layout (weight and scale bytes)."""
+    total = 0
+    for n, k in ((2 * I, H), (H, I)):
+        total += n * {"fp8": k, "fp8c": k, "w4a8": k // 2, "w6a8": 3 * k // 4, "w6": 3 * k // 4}[kind]
+        total += {"fp8": (n // 128) * (k // 128) * 4, "fp8c": n * 4, "w4a8": n * (k // 128) * 2,
+                  "w6a8": n * (k // 128) * 2, "w6": n * (k // 16 + 4)}[kind]
+    return total
+
+
+def make_layers(device, lines, kind="fp8c", seed=4, n_layers=LAYERS):
+    """n_layers layers of banks (random valid codes, positive scales) and per-layer routing; layer l's routing does
+    not depend on n_layers or the format."""
+    gen = torch.Generator(device=device).manual_seed(seed)
+    layers = [tuple(rand_bank(kind, n, k, gen, device) for n, k in ((2 * I, H), (H, I))) for _ in range(n_layers)]
+    cpu_gen = torch.Generator().manual_seed(seed + 1)
+    ids, weights = [], []
+    for _ in range(n_layers):
+        w, i = torch.softmax(torch.randn((lines, E), generator=cpu_gen), dim=-1).topk(K_TOP, dim=-1)
+        ids.append(i)
+        weights.append((w / w.sum(-1, keepdim=True)).to(torch.bfloat16).float())
+    return layers, torch.stack(ids).to(device), torch.stack(weights).to(device)
 
 
 def peaks():
@@ -92,46 +146,69 @@ class Clocks:
                 "samples": len(self.rows), "reasons": reasons}
 
 
-def make_layers(device, lines, seed=4, n_layers=LAYERS):
-    """n_layers layers of FP8 banks (random valid e4m3 bytes, positive block scales) and per-layer routing; layer l's
-    routing does not depend on n_layers."""
-    gen = torch.Generator(device=device).manual_seed(seed)
-    layers = []
-    for _ in range(n_layers):
-        bank = []
-        for n, k in ((2 * I, H), (H, I)):
-            w = torch.randint(0, 254, (E * n, k), generator=gen, device=device, dtype=torch.uint8)
-            w = torch.where(w >= 0x7F, w + 1, w)  # no 0x7F / 0xFF (NaN codes)
-            s = torch.rand((E * n // 128, k // 128), generator=gen, device=device) * 1e-4 + 5e-5
-            bank.append({"weight": w, "scale": s})
-        layers.append(tuple(bank))
-    cpu_gen = torch.Generator().manual_seed(seed + 1)
-    ids, weights = [], []
-    for _ in range(n_layers):
-        w, i = torch.softmax(torch.randn((lines, E), generator=cpu_gen), dim=-1).topk(K_TOP, dim=-1)
-        ids.append(i)
-        weights.append((w / w.sum(-1, keepdim=True)).to(torch.bfloat16).float())
-    return layers, torch.stack(ids).to(device), torch.stack(weights).to(device)
+def unique_bytes(ids, kind):
+    """Algorithmic bytes of one step: each layer's unique experts, plus its rows in and out (bf16)."""
+    per, total = expert_bytes(kind), 0
+    lines = ids.shape[1]
+    for layer in ids.cpu():
+        total += len(set(layer.reshape(-1).tolist())) * per + 2 * lines * H * 2 + lines * K_TOP * 12
+    return total
 
 
-def rand_bank(kind, n, k, gen, device):
-    """A flat bank [E * n, ...] of random valid codes in the reference layout of `kind` (fp8 or w6)."""
-    if kind == "fp8":
-        w = torch.randint(0, 254, (E * n, k), generator=gen, device=device, dtype=torch.uint8)
-        w = torch.where(w >= 0x7F, w + 1, w)
-        s = torch.rand((E * n // 128, k // 128), generator=gen, device=device) * 1e-4 + 5e-5
-        return {"weight": w, "scale": s}
-    q = torch.randint(0, 256, (E * n, 3 * k // 4), generator=gen, device=device, dtype=torch.uint8)
-    g = torch.randint(0x30, 0x50, (E * n, k // 16), generator=gen, device=device, dtype=torch.uint8)
-    c = torch.rand((E * n,), generator=gen, device=device) * 2e-4 + 1e-4
-    return {"_qdata": q, "scale": g, "s_channel": c}
+def capture(fn, warmup, stream):
+    """fn() run `warmup` times, then captured as one CUDA graph (replayed once)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        fn()
+    graph.replay()
+    torch.cuda.synchronize()
+    return graph
+
+
+def time_replays(graph, steps, stream):
+    """ms per replay of `graph`, CUDA events on `stream`."""
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        graph.replay()
+    end.record(stream)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / steps
+
+
+def decode_leg(kernels, device, kind, lines, steps, warmup, stream, n_layers, layers):
+    """{tokens_per_s, ms_per_step, hbm_gbs, frac, ...} of the fused decode of `lines` rows through n_layers layers;
+    layers = (banks, ids, weights)."""
+    hbm_peak, _ = peaks()
+    banks, ids, weights = layers
+    x = torch.randn((lines, H), generator=torch.Generator().manual_seed(7)).to(torch.bfloat16).to(device)
+    ws = kernels.decode_workspace(lines, K_TOP, I, device)
+    outs = torch.empty((n_layers, lines, H), dtype=torch.bfloat16, device=device)
+
+    def step():
+        for l_ in range(n_layers):
+            kernels.moe_decode(kind, x, ids[l_], weights[l_], banks[l_], workspace=ws, out=outs[l_])
+
+    with torch.cuda.stream(stream):
+        graph = capture(step, warmup, stream)
+        ms = time_replays(graph, steps, stream)
+    del graph
+    b = unique_bytes(ids, kind)
+    gbs = b / (ms * 1e-3) / 1e9
+    return {"tokens_per_s": lines / (ms * 1e-3), "ms_per_step": ms, "us_per_layer": 1e3 * ms / n_layers,
+            "hbm_gbs": gbs, "frac": gbs / hbm_peak, "bytes_per_step": b, "format": FORMAT_NAMES[kind],
+            "lines": lines}
 
 
 def prefill_leg(device, steps, tokens=2048, seed=3):
     """one MoE layer's prompt pass of `tokens` rows, router logits biased so expert load is
-    Zipf(1.1)-skewed (bias_e = -1.1 ln r_e, r a seeded permutation of ranks 1..128), W6 (reference layout) and fp8
-    experts. Times the whole resident_prefill (sort, grouped GEMMs on the tensor cores, combine) with CUDA events,
-    and the reference's own grouped kernels (oracle/_ref) on the same inputs."""
+    Zipf(1.1)-skewed (bias_e = -1.1 ln r_e, r a seeded permutation of ranks 1..128): W6A8 (the BASELINE layout),
+    then the reference's W6 and fp8 layouts. Times the whole resident_prefill (sort, grouped GEMMs on the tensor
+    cores, combine) with CUDA events, and for the reference layouts the reference's own grouped kernels
+    (oracle/_ref) on the same inputs."""
     from drama3_b200 import offload
     gen = torch.Generator().manual_seed(seed)
     bias = -1.1 * torch.log(torch.randperm(E, generator=gen).float() + 1)
@@ -149,9 +226,9 @@ def prefill_leg(device, steps, tokens=2048, seed=3):
     dgen = torch.Generator(device=device).manual_seed(seed)
     out = {"tokens": tokens, "top_k": K_TOP, "largest_group": int(counts.max()), "median_group": int(counts.median()),
            "flops_per_layer": flops, "peak_tflops": bf16_peak,
-           "note": "activations enter the MMA as two f16 terms (hi + lo), so the tensor pipe does twice the algorithmic "
-                   "flops; the frac is algorithmic flops / time / measured dense bf16 peak"}
-    for kind in ("w6", "fp8"):
+           "note": "f16 MMAs with f32 accumulation; fp32 activations enter as two f16 terms (hi + lo), int8-quantized "
+                   "ones (W6A8) as one exact term; frac = algorithmic flops / time / measured dense bf16 peak"}
+    for kind in ("w6a8", "w6", "fp8"):
         banks = (rand_bank(kind, 2 * I, H, dgen, device), rand_bank(kind, H, I, dgen, device))
 
         def run():
@@ -169,52 +246,31 @@ def prefill_leg(device, steps, tokens=2048, seed=3):
         torch.cuda.synchronize()
         us = 1e3 * s0.elapsed_time(s1) / n
         leg = {"us_per_layer": us, "tflops": flops / us / 1e6, "frac": flops / us / 1e6 / bf16_peak,
-               "tokens_per_s": tokens / us * 1e6}
-        try:
-            from oracle import ref_gpu
-            if ref_gpu.available():
-                ref_gpu.resident_prefill(x, ids, w, banks, (2 * I, H), kind, (None, None), E)
-                torch.cuda.synchronize()
-                s0.record()
-                ref_gpu.resident_prefill(x, ids, w, banks, (2 * I, H), kind, (None, None), E)
-                s1.record()
-                torch.cuda.synchronize()
-                rus = 1e3 * s0.elapsed_time(s1)
-                leg["reference_gpu_us_per_layer"] = rus
-                leg["speedup_vs_reference_gpu"] = rus / us
-        except Exception as exc:  # the comparison must not sink the bench line
-            leg["reference_gpu"] = {"error": repr(exc)[:200]}
+               "tokens_per_s": tokens / us * 1e6, "format": FORMAT_NAMES[kind]}
+        if kind in ("w6", "fp8"):
+            try:
+                from oracle import ref_gpu
+                if ref_gpu.available():
+                    ref_gpu.resident_prefill(x, ids, w, banks, (2 * I, H), kind, (None, None), E)
+                    torch.cuda.synchronize()
+                    s0.record()
+                    ref_gpu.resident_prefill(x, ids, w, banks, (2 * I, H), kind, (None, None), E)
+                    s1.record()
+                    torch.cuda.synchronize()
+                    rus = 1e3 * s0.elapsed_time(s1)
+                    leg["reference_gpu_us_per_layer"] = rus
+                    leg["speedup_vs_reference_gpu"] = rus / us
+            except Exception as exc:  # the comparison must not sink the bench line
+                leg["reference_gpu"] = {"error": repr(exc)[:200]}
         out[kind] = leg
         del banks
     return out
 
 
-def unique_bytes(ids):
-    """Algorithmic bytes of one step: each layer's unique experts, plus its rows in and out (bf16)."""
-    total = 0
-    lines = ids.shape[1]
-    for layer in ids.cpu():
-        total += len(set(layer.reshape(-1).tolist())) * EXPERT_BYTES + 2 * lines * H * 2 + lines * K_TOP * 12
-    return total
-
-
-def time_graph(fn, steps, warmup, stream):
-    """(ms per step) of fn() captured as one CUDA graph and replayed; CUDA events on the capturing stream."""
-    for _ in range(warmup):
-        fn()
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        fn()
-    graph.replay()
-    torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    return graph, start, end
-
-
 def cpu_reference(lines, layers_sampled=2, seed=4, n_layers=LAYERS, seconds=10.0):
-    """The reference's CPU decode (oracle/cpu_port.py) on the host cores: `lines` rows through `layers_sampled`
-    layers, scaled to n_layers layers. Returns (tokens/s, seconds, threads, sample description)."""
+    """The reference's CPU decode (oracle/cpu_port.py, the FP8Experts CPU forward with its block-scaled layout) on
+    the host cores: `lines` rows through at least `layers_sampled` layers and about `seconds` of work, scaled to
+    n_layers layers. Returns (tokens/s, seconds, threads, sample description)."""
     from oracle import cpu_port
     torch.set_num_threads(os.cpu_count() or 1)
     gen = torch.Generator().manual_seed(seed)
@@ -227,8 +283,6 @@ def cpu_reference(lines, layers_sampled=2, seed=4, n_layers=LAYERS, seconds=10.0
         ds = torch.rand((E, H // 128, I // 128), generator=gen) * 1e-4
         banks.append((gu, gs, dn, ds))
     total, done = 0.0, 0
-    # at least `layers_sampled` layers, then more until about `seconds` of CPU work (two banks, alternating, each
-    # layer with its own routing)
     while done < n_layers and (done < layers_sampled or total < seconds):
         gu, gs, dn, ds = banks[done % 2]
         w, ids = torch.softmax(torch.randn((lines, E), generator=gen), -1).topk(K_TOP, dim=-1)
@@ -241,6 +295,16 @@ def cpu_reference(lines, layers_sampled=2, seed=4, n_layers=LAYERS, seconds=10.0
     sample = (f"{lines} rows x {done} layers ({total:.1f} s) of the reference CPU path (bf16 dequant + matmuls, one "
               f"row at a time), scaled to {n_layers} layers")
     return lines / per_step, total, torch.get_num_threads(), sample
+
+
+def config(args):
+    return {"workload": f"MoE decode, {args.lines} lines x {args.layers} layers per step, {args.kind} experts "
+                        f"(BASELINE configs[1] layer shape; 48 layers as configs[4])",
+            "layers": args.layers, "lines": args.lines, "experts": E, "top_k": K_TOP, "hidden": H, "intermediate": I,
+            "format": FORMAT_NAMES[args.kind],
+            "l2": f"inputs larger than L2: {args.layers * E * expert_bytes(args.kind) / 1e9:.1f} GB of expert banks, "
+                  f"each layer's routed experts streamed per step",
+            "parallelism": f"replicas x{args.gpus} (lines data-parallel)"}
 
 
 def run_reference_arm(args, rank):
@@ -257,16 +321,6 @@ def run_reference_arm(args, rank):
     print(json.dumps(line), flush=True)
 
 
-def config(args):
-    return {"workload": f"fp8 MoE decode, {args.lines} lines x {args.layers} layers per step (BASELINE configs[1] "
-                        f"layer shape; 48 layers as configs[4])",
-            "layers": args.layers, "lines": args.lines, "experts": E, "top_k": K_TOP, "hidden": H, "intermediate": I,
-            "format": "e4m3 + fp32 128x128 block scales (reference layout)",
-            "l2": f"inputs larger than L2: {args.layers * E * EXPERT_BYTES / 1e9:.1f} GB of expert banks, each layer's "
-                  f"routed experts streamed per step",
-            "parallelism": f"replicas x{args.gpus} (lines data-parallel)"}
-
-
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -275,7 +329,8 @@ def main():
     ap.add_argument("--impl", choices=("mine", "reference"), default="mine")
     ap.add_argument("--lines", type=int, default=16)
     ap.add_argument("--layers", type=int, default=LAYERS, help="layers per step (48: the benchmark; 4: small case)")
-    ap.add_argument("--no-extras", action="store_true", help="skip e2e / reference GPU / prefill / CPU legs")
+    ap.add_argument("--kind", choices=KINDS[:4], default="fp8c", help="expert layout of the headline decode")
+    ap.add_argument("--no-extras", action="store_true", help="skip every leg but the headline")
     ap.add_argument("--prefill-only", action="store_true", help="print only the prompt-pass leg (BASELINE configs[3])")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -302,19 +357,19 @@ def main():
         if rank == 0:
             print(json.dumps({"prefill": prefill_leg(device, args.steps)}), flush=True)
         return
-    n_layers = args.layers
-    layers, ids, weights = make_layers(device, args.lines, seed=4 + rank, n_layers=n_layers)
+    n_layers, kind = args.layers, args.kind
+    layers, ids, weights = make_layers(device, args.lines, kind, seed=4 + rank, n_layers=n_layers)
     x = torch.randn((args.lines, H), generator=torch.Generator().manual_seed(7 + rank)).to(torch.bfloat16).to(device)
     ws = kernels.decode_workspace(args.lines, K_TOP, I, device)
     outs = torch.empty((n_layers, args.lines, H), dtype=torch.bfloat16, device=device)
     stream = torch.cuda.Stream(device)
 
-    def step(lines=args.lines, xin=x, ids_=ids, w_=weights, ws_=ws, out_=outs):
+    def step(xin=x, ids_=ids, w_=weights, out_=outs):
         for l_ in range(n_layers):
-            kernels.moe_decode("fp8", xin, ids_[l_], w_[l_], layers[l_], workspace=ws_, out=out_[l_])
+            kernels.moe_decode(kind, xin, ids_[l_], w_[l_], layers[l_], workspace=ws, out=out_[l_])
 
     with torch.cuda.stream(stream):
-        graph, start, end = time_graph(step, 0, args.warmup, stream)
+        graph = capture(step, args.warmup, stream)
         for _ in range(args.warmup):
             graph.replay()
         torch.cuda.synchronize()
@@ -323,41 +378,23 @@ def main():
         torch.cuda.synchronize()
         with Clocks(local) as clocks:
             torch.cuda.profiler.start()
-            start.record(stream)
-            for _ in range(args.steps):
-                graph.replay()
-            end.record(stream)
-            torch.cuda.synchronize()
+            ms = time_replays(graph, args.steps, stream)
             torch.cuda.profiler.stop()
-        ms = start.elapsed_time(end) / args.steps
     if pg:
         t = torch.tensor([ms], device=device)
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         ms = float(t.item())
-    step_bytes = unique_bytes(ids)
+    step_bytes = unique_bytes(ids, kind)
     hbm_peak, peak_kind = peaks()
     achieved = step_bytes / (ms * 1e-3) / 1e9
     value = world * args.lines / (ms * 1e-3)
+    del graph
 
     extras = {}
     if not args.no_extras and rank == 0:
-        # one line decoded at a time (M = 1)
-        x1, ids1, w1 = x[:1].contiguous(), ids[:, :1].contiguous(), weights[:, :1].contiguous()
-        ws1 = kernels.decode_workspace(1, K_TOP, I, device)
-        out1 = torch.empty((n_layers, 1, H), dtype=torch.bfloat16, device=device)
-        with torch.cuda.stream(stream):
-            g1, s1, e1 = time_graph(lambda: step(1, x1, ids1, w1, ws1, out1), 0, args.warmup, stream)
-            s1.record(stream)
-            for _ in range(args.steps):
-                g1.replay()
-            e1.record(stream)
-            torch.cuda.synchronize()
-        ms1 = s1.elapsed_time(e1) / args.steps
-        b1 = unique_bytes(ids1)
-        extras["lines_1"] = {"tokens_per_s": 1 / (ms1 * 1e-3), "ms_per_step": ms1,
-                             "hbm_gbs": b1 / (ms1 * 1e-3) / 1e9, "frac": b1 / (ms1 * 1e-3) / 1e9 / hbm_peak,
-                             "bytes_per_step": b1, "us_per_layer": 1e3 * ms1 / n_layers}
-        del g1
+        # one line decoded at a time (M = 1), same banks
+        extras["lines_1"] = decode_leg(kernels, device, kind, 1, args.steps, args.warmup, stream, n_layers,
+                                       (layers, ids[:, :1].contiguous(), weights[:, :1].contiguous()))
         # end to end through the Python API: host inputs in, host output back, every step
         xh = x.cpu().pin_memory()
         idh, wh = ids.cpu().pin_memory(), weights.cpu().pin_memory()
@@ -373,7 +410,7 @@ def main():
             xd.copy_(xh, non_blocking=True)
             idd.copy_(idh, non_blocking=True)
             wd.copy_(wh, non_blocking=True)
-            step(args.lines, xd, idd, wd, ws, outs)
+            step(xd, idd, wd, outs)
             outh.copy_(outs[-1], non_blocking=True)
         ee.record()
         torch.cuda.synchronize()
@@ -381,30 +418,42 @@ def main():
         extras["e2e"] = {"value": args.lines / (ms_e2e * 1e-3), "unit": "tokens/s",
                          "h2d_bytes_per_step": xh.nbytes + idh.nbytes + wh.nbytes, "d2h_bytes_per_step": outh.nbytes,
                          "ms_per_step": ms_e2e, "wall_ms_per_step": 1e3 * (time.perf_counter() - t0) / n_e2e}
-        # the reference's own kernels on this GPU, one row at a time (drama3/model.py:111-113)
+        del layers
+        torch.cuda.empty_cache()
+        # W4A8 at 16 and 1 lines
+        w4 = make_layers(device, args.lines, "w4a8", 5, n_layers)
+        extras["w4a8"] = {
+            "lines_16": decode_leg(kernels, device, "w4a8", args.lines, args.steps, args.warmup, stream, n_layers, w4),
+            "lines_1": decode_leg(kernels, device, "w4a8", 1, args.steps, args.warmup, stream, n_layers,
+                                  (w4[0], w4[1][:, :1].contiguous(), w4[2][:, :1].contiguous()))}
+        del w4
+        torch.cuda.empty_cache()
+        # the reference's fp8 layout, and the reference's own kernels on it, one row at a time
+        # (drama3/model.py:111-113), one CUDA graph per step
+        ref_layers = make_layers(device, args.lines, "fp8", 4, n_layers)
+        leg = decode_leg(kernels, device, "fp8", args.lines, args.steps, args.warmup, stream, n_layers, ref_layers)
         try:
             from oracle import ref_gpu
             if ref_gpu.available():
+                banks_r, ids_r, w_r = ref_layers
+
                 def ref_step():
                     for l_ in range(n_layers):
-                        ref_gpu.lines_decode(x, ids[l_], weights[l_], layers[l_], (2 * I, H), "fp8", (None, None))
+                        ref_gpu.lines_decode(x, ids_r[l_], w_r[l_], banks_r[l_], (2 * I, H), "fp8", (None, None))
+
                 with torch.cuda.stream(stream):
-                    gr, rs, re_ = time_graph(ref_step, 0, 2, stream)
-                    n_ref = max(3, min(args.steps, 10))
-                    rs.record(stream)
-                    for _ in range(n_ref):
-                        gr.replay()
-                    re_.record(stream)
-                    torch.cuda.synchronize()
-                rms = rs.elapsed_time(re_) / n_ref
+                    gr = capture(ref_step, 2, stream)
+                    rms = time_replays(gr, max(3, min(args.steps, 10)), stream)
                 del gr
-                extras["reference_gpu"] = {"tokens_per_s": args.lines / (rms * 1e-3), "ms_per_step": rms,
-                                           "hbm_gbs": step_bytes / (rms * 1e-3) / 1e9,
-                                           "what": "reference kernels (drama3/kernels.py, nvcc sm_100) driven as "
-                                                   "drama3/offload.py:108-117, one row at a time, one CUDA graph "
-                                                   "per step"}
+                leg["reference_gpu"] = {"tokens_per_s": args.lines / (rms * 1e-3), "ms_per_step": rms,
+                                        "what": "reference kernels (drama3/kernels.py, nvcc sm_100) driven as "
+                                                "drama3/offload.py:108-117, one row at a time"}
+                leg["speedup_vs_reference_gpu"] = rms / leg["ms_per_step"]
         except Exception as exc:  # the comparison leg must not sink the bench line
-            extras["reference_gpu"] = {"error": repr(exc)[:200]}
+            leg["reference_gpu"] = {"error": repr(exc)[:200]}
+        extras["fp8_reference_layout"] = leg
+        del ref_layers
+        torch.cuda.empty_cache()
         # a prompt pass on the tensor cores (BASELINE configs[3] shape)
         try:
             extras["prefill"] = prefill_leg(device, args.steps)
@@ -418,22 +467,20 @@ def main():
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "e4m3 weights, f32 math", "data": "synthetic (seeded random banks)",
-                "config": config(args),
+                "vs_baseline": None, "dtype": "f16 MMA inputs (exact e4m3 weights), f32 accumulation",
+                "data": "synthetic (seeded random banks)", "config": config(args),
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                              "frac": achieved / hbm_peak, "peak_kind": peak_kind,
-                             "traffic": None if TRAFFIC_RATIO is None else TRAFFIC_RATIO * step_bytes / n_layers,
-                             "traffic_unit": "bytes per launch (ncu ratio of the --layers 4 capture x this run's "
-                                             "algorithmic bytes per launch)",
-                             "kernel": "moe_decode_kernel<fp8> (one persistent launch per layer: plan, gate_up + "
-                                       "SwiGLU, down, combine)",
+                             "traffic": TRAFFIC_RATIO * step_bytes / n_layers,
+                             "traffic_unit": "bytes per launch", "traffic_source": TRAFFIC_SOURCE,
+                             "kernel": f"moe_decode_kernel<{kind}> (one persistent launch per layer: plan, gate_up + "
+                                       f"SwiGLU, down, combine)",
                              "bytes_per_launch": step_bytes / n_layers, "us_per_layer": 1e3 * ms / n_layers,
                              "launch_time": "step time / layers: the launches run back to back in one graph"},
                 "gpu_launches": n_layers * args.steps,
                 "clocks": clocks.summary()}
         line.update(extras)
         print(json.dumps(line), flush=True)
-    del graph
     if pg:
         pg.barrier()
         pg.destroy_process_group()

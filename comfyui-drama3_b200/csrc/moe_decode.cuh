@@ -300,10 +300,17 @@ D3_DEV uint32_t s6x2_h2(uint32_t c0, uint32_t c1) {
 template <int FMT>
 D3_DEV void build_a(const uint8_t* row, const uint8_t* srow, int col, int K, const float* lut, uint32_t (&a)[8]) {
   if (FMT == FMT_W4A8) {
-    // 16 nibbles: byte i holds columns 2i (low) and 2i + 1
+    // 16 nibbles: byte i holds columns 2i (low) and 2i + 1. Sign bits flipped once per word; byte i copied into both
+    // halves (prmt), low nibble and high nibble (times 16) into the mantissas of 1024 (lop3), then one f16x2 FMA:
+    // lo * 1 - 1032, hi * 1/16 - 72 (both exact).
     const uint2 p = *(const uint2*)(row + col / 2);
+    const uint32_t w[2] = {p.x ^ 0x88888888u, p.y ^ 0x88888888u};
 #pragma unroll
-    for (int i = 0; i < 8; ++i) a[i] = s4x2_h2(((i < 4 ? p.x : p.y) >> (8 * (i & 3))) & 0xFFu);
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t t = __byte_perm(w[i >> 2], 0u, (uint32_t)((i & 3) | 0x40 | ((i & 3) << 8) | 0x4000));
+      const uint32_t h = (t & 0x00F0000Fu) | 0x64006400u;
+      asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(a[i]) : "r"(h), "r"(0x2C003C00u), "r"(0xD480E408u));
+    }
   } else if (FMT == FMT_W6A8) {
     // 16 six-bit codes in 12 bytes: code i at bit 6i of the little-endian 96-bit word
     const uint32_t* p = (const uint32_t*)(row + (col / 16) * 12);
@@ -399,8 +406,13 @@ struct RedSlot {
   float4 part[DEC_WARPS * 32];
   int pair[DEC_MAX_CAP];
   float inv[DEC_MAX_CAP];
+  float rsc[DEC_CH2];  // fp8c / int8: the chunk's row scales (phase 1: gate rows, then up rows at +8)
   int r, cn, cnt, e;
 };
+
+// Row scales (fp8c / int8) ride with their chunk: each span is copied from the 16-byte boundary at or below its first
+// scale, into a 64-byte (phase 1: gate, then up) or 160-byte (phase 2) area after the chunk's rows.
+constexpr int DEC_RS1 = 64, DEC_RS2 = 160;
 
 // Shared-memory layout of the decode kernel (dynamic part), shared with the host launcher.
 struct DecodeSmem {
@@ -432,10 +444,11 @@ __host__ __device__ inline DecodeSmem decode_smem(int H, int I, int stages, int 
 // I = 768 hold 12 scale bytes), hence the 32 spare bytes.
 template <int FMT>
 __host__ __device__ constexpr int decode_stage_bytes(int H, int I) {
-  return (2 * DEC_CH1 * (fmt_row_bytes(FMT, H) + fmt_gscale_bytes(FMT, H))) >
-                 (DEC_CH2 * (fmt_row_bytes(FMT, I) + fmt_gscale_bytes(FMT, I)) + 32)
-             ? 2 * DEC_CH1 * (fmt_row_bytes(FMT, H) + fmt_gscale_bytes(FMT, H))
-             : DEC_CH2 * (fmt_row_bytes(FMT, I) + fmt_gscale_bytes(FMT, I)) + 32;
+  return (2 * DEC_CH1 * (fmt_row_bytes(FMT, H) + fmt_gscale_bytes(FMT, H)) + (fmt_row_scale(FMT) ? 2 * DEC_RS1 : 0)) >
+                 (DEC_CH2 * (fmt_row_bytes(FMT, I) + fmt_gscale_bytes(FMT, I)) + 32 +
+                  (fmt_row_scale(FMT) ? DEC_RS2 : 0))
+             ? 2 * DEC_CH1 * (fmt_row_bytes(FMT, H) + fmt_gscale_bytes(FMT, H)) + (fmt_row_scale(FMT) ? 2 * DEC_RS1 : 0)
+             : DEC_CH2 * (fmt_row_bytes(FMT, I) + fmt_gscale_bytes(FMT, I)) + 32 + (fmt_row_scale(FMT) ? DEC_RS2 : 0);
 }
 
 // The contiguous range [lo, hi) of `total` work items owned by CTA `b` of `g`.
@@ -743,6 +756,20 @@ D3_DEV bool mma_phase(const DecodeArgs& a, const DecodePlan& pl, int lo, int hi,
                                   A8 ? (int)((((size_t)e * H + r) * fmt_gscale_bytes(FMT, I)) & 15) : 0,
                                   (const uint32_t(&)[NKC][8])bh, (const uint32_t(&)[NKC][8])bl, table, lut);
     }
+    // fp8c / int8: warp 0 takes the chunk's row scales out of the stage before it is released
+    float rsv = 0.0f;
+    if (fmt_row_scale(FMT) && warp == 0 && ok) {
+      const uint8_t* stg = ring + (size_t)st * SB;
+      if (PHASE == 1) {
+        const size_t base = (size_t)e * 2 * I + r + (lane < 8 ? 0 : I);
+        if (lane < 16 && (lane & 7) < cn)
+          rsv = *(const float*)(stg + 2 * DEC_CH1 * fmt_row_bytes(FMT, H) + (lane < 8 ? 0 : DEC_RS1) +
+                                ((base * 4) & 15) + (lane & 7) * 4);
+      } else {
+        const size_t base = (size_t)e * H + r;
+        if (lane < cn) rsv = *(const float*)(stg + DEC_CH2 * fmt_row_bytes(FMT, I) + ((base * 4) & 15) + lane * 4);
+      }
+    }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty_bar[st]);
     const int slot = c % DEC_RED;
@@ -756,6 +783,7 @@ D3_DEV bool mma_phase(const DecodeArgs& a, const DecodePlan& pl, int lo, int hi,
 #endif
     RedSlot& rs = red[slot];
     rs.part[warp * 32 + lane] = part;
+    if (fmt_row_scale(FMT) && warp == 0) rs.rsc[lane] = rsv;
     if (warp == 0) {
       if (lane < DEC_MAX_CAP) {
         rs.pair[lane] = pair_in[lane];
@@ -875,10 +903,20 @@ __global__ void __launch_bounds__(DEC_ALL, 1) moe_decode_kernel(const DecodeArgs
           uint8_t* dst = ring + (size_t)st * SB;
           if (phase == 1) {
             const size_t g0 = (size_t)e * 2 * I + r, u0 = g0 + I;
-            const uint32_t bytes = 2u * cn * rb1 + 2u * cn * gb1;
+            // row scales (fp8c / int8): 16-byte-aligned spans around each set of cn scales
+            const size_t a0 = (g0 * 4) & ~(size_t)15, a1 = ((g0 + cn) * 4 + 15) & ~(size_t)15;
+            const size_t b0 = (u0 * 4) & ~(size_t)15, b1 = ((u0 + cn) * 4 + 15) & ~(size_t)15;
+            const uint32_t rsb = fmt_row_scale(FMT) ? (uint32_t)(a1 - a0 + b1 - b0) : 0u;
+            const uint32_t bytes = 2u * cn * rb1 + 2u * cn * gb1 + rsb;
             mbar_arrive_expect_tx(&full_bar[st], bytes);
             bulk_g2s(dst, a.w13 + g0 * rb1, cn * rb1, &full_bar[st], pol);
             bulk_g2s(dst + DEC_CH1 * rb1, a.w13 + u0 * rb1, cn * rb1, &full_bar[st], pol);
+            if (fmt_row_scale(FMT)) {
+              const uint8_t* sc = (const uint8_t*)a.s13;
+              uint8_t* rs = dst + 2 * DEC_CH1 * rb1;
+              bulk_g2s(rs, sc + a0, (uint32_t)(a1 - a0), &full_bar[st], pol);
+              bulk_g2s(rs + DEC_RS1, sc + b0, (uint32_t)(b1 - b0), &full_bar[st], pol);
+            }
             if (gb1 > 0) {
               const uint8_t* sc = (const uint8_t*)a.s13;
               bulk_g2s(dst + 2 * DEC_CH1 * rb1, sc + g0 * gb1, cn * gb1, &full_bar[st], pol);
@@ -886,12 +924,15 @@ __global__ void __launch_bounds__(DEC_ALL, 1) moe_decode_kernel(const DecodeArgs
             }
           } else {
             const size_t n0 = (size_t)e * H + r;
-            // group scales from the 16-byte boundary at or below their first byte, to one at or above their end
-            const size_t s0 = (n0 * gb2) & ~(size_t)15, s1 = ((n0 + cn) * gb2 + 15) & ~(size_t)15;
-            const uint32_t sbytes = gb2 > 0 ? (uint32_t)(s1 - s0) : 0u;
+            // group scales (W4/W6/A8) or row scales (fp8c / int8), from the 16-byte boundary at or below their
+            // first byte to one at or above their end
+            const int sb = gb2 > 0 ? gb2 : (fmt_row_scale(FMT) ? 4 : 0);
+            const size_t s0 = (n0 * sb) & ~(size_t)15, s1 = ((n0 + cn) * sb + 15) & ~(size_t)15;
+            const uint32_t sbytes = sb > 0 ? (uint32_t)(s1 - s0) : 0u;
+            const uint8_t* ssrc = (const uint8_t*)a.s2;
             mbar_arrive_expect_tx(&full_bar[st], cn * rb2 + sbytes);
             bulk_g2s(dst, a.w2 + n0 * rb2, cn * rb2, &full_bar[st], pol);
-            if (gb2 > 0) bulk_g2s(dst + DEC_CH2 * rb2, (const uint8_t*)a.s2 + s0, sbytes, &full_bar[st], pol);
+            if (sb > 0) bulk_g2s(dst + DEC_CH2 * rb2, ssrc + s0, sbytes, &full_bar[st], pol);
           }
           q += cn;
         }
@@ -942,8 +983,8 @@ __global__ void __launch_bounds__(DEC_ALL, 1) moe_decode_kernel(const DecodeArgs
             const int i = r + g;
             float gsc = 1.0f, usc = 1.0f;
             if (fmt_row_scale(FMT)) {
-              gsc = __ldg((const float*)a.s13 + (size_t)e * 2 * I + i);
-              usc = __ldg((const float*)a.s13 + (size_t)e * 2 * I + I + i);
+              gsc = rs.rsc[g];
+              usc = rs.rsc[DEC_CH1 + g];
             } else if (fmt_codes(FMT)) {
               gsc = __ldg(a.c13 + (size_t)e * 2 * I + i);
               usc = __ldg(a.c13 + (size_t)e * 2 * I + I + i);
@@ -976,7 +1017,7 @@ __global__ void __launch_bounds__(DEC_ALL, 1) moe_decode_kernel(const DecodeArgs
               if (row < cn) {
                 const int nrow = r + row;
                 float sc = 1.0f;
-                if (fmt_row_scale(FMT)) sc = __ldg((const float*)a.s2 + (size_t)e * H + nrow);
+                if (fmt_row_scale(FMT)) sc = rs.rsc[row];
                 if (fmt_codes(FMT)) sc = __ldg(a.c2 + (size_t)e * H + nrow);
                 const float v0 = half ? sum.z : sum.x, v1 = half ? sum.w : sum.y;
                 if (n0 < cnt) __stcg(a.parts + (size_t)rs.pair[n0] * H + nrow, v0 * (sc * rs.inv[n0]));
