@@ -14,12 +14,13 @@ sees exactly its launches; `--layers 4` is the small case for multi-pass capture
 first 4 layers of the full run). Multi-GPU: independent replicas (each rank decodes its own lines with all experts
 resident; no collective), weak scaling. `value` = tokens/s of all ranks; timing = CUDA events, max over ranks.
 
-Also reported (rank 0): the 1-line decode; W4A8 at 16 and 1 lines; the reference's fp8 layout
+Also reported at N = 1: the 1-line decode; W4A8 at 16 and 1 lines; the reference's fp8 layout
 (128 x 128 block scales) at 16 lines beside the reference's own kernels (compiled from drama3/kernels.py into
 oracle/_ref) on the same GPU; the end-to-end rate through the Python API with host buffers; a prompt-pass leg
 (2048 tokens, Zipf-skewed routing; W6A8, and the reference's W6 and fp8 layouts beside the
-reference's kernels); the reference's CPU path on the host cores. `--impl reference` runs only that CPU path
-(rank 0) and prints its line.
+reference's kernels); the reference's CPU path on the host cores. At N > 1: expert parallelism over the N GPUs
+(each holds 128 / N experts of every layer, all decode the same 16 lines, fp32 partials all-gathered and summed in
+rank order per layer). `--impl reference` runs only that CPU path (rank 0) and prints its line.
 """
 import argparse
 import json
@@ -297,6 +298,52 @@ def cpu_reference(lines, layers_sampled=2, seed=4, n_layers=LAYERS, seconds=10.0
     return lines / per_step, total, torch.get_num_threads(), sample
 
 
+def ep_leg(kernels, device, kind, args, stream, pg):
+    """Expert-parallel decode of `lines` rows through n_layers layers: rank r holds experts expert_range(E, r, N) of
+    every layer (seeded whole banks, sliced), all ranks see the same rows and routing; per layer one fused decode of
+    the local experts (fp32 partial) and one all-gather + rank-order sum, captured as one CUDA graph per step. Timed
+    with CUDA events, max over ranks."""
+    from drama3_b200 import ep
+    rank, world = pg.get_rank(), pg.get_world_size()
+    n_layers = args.layers
+    gen = torch.Generator(device=device).manual_seed(4)
+    layers = []
+    for _ in range(n_layers):
+        full = tuple(rand_bank(kind, n, k, gen, device) for n, k in ((2 * I, H), (H, I)))
+        layers.append(ep.ExpertParallelDecode(kind, tuple({n: t.clone() for n, t in b.items()}
+                                                          for b in ep.local_banks(full, E, rank, world)), E))
+        del full
+    torch.cuda.empty_cache()
+    cpu_gen = torch.Generator().manual_seed(5)
+    ids, weights = [], []
+    for _ in range(n_layers):
+        w, i = torch.softmax(torch.randn((args.lines, E), generator=cpu_gen), dim=-1).topk(K_TOP, dim=-1)
+        ids.append(i.to(device))
+        weights.append((w / w.sum(-1, keepdim=True)).to(torch.bfloat16).float().to(device))
+    x = torch.randn((args.lines, H), generator=torch.Generator().manual_seed(7)).to(torch.bfloat16).to(device)
+
+    outs = [None] * n_layers
+
+    def step():
+        for l_ in range(n_layers):
+            outs[l_] = layers[l_](x, ids[l_], weights[l_])
+
+    with torch.cuda.stream(stream):
+        graph = capture(step, args.warmup, stream)  # the all-gathers are captured with the kernels
+        torch.cuda.synchronize()
+        pg.barrier()
+        ms = time_replays(graph, max(3, min(args.steps, 20)), stream)
+    del graph  # released before the process group is destroyed
+    t = torch.tensor([ms], device=device)
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    ms = float(t.item())
+    first, count = ep.expert_range(E, rank, world)
+    return {"tokens_per_s": args.lines / (ms * 1e-3), "ms_per_step": ms, "us_per_layer": 1e3 * ms / n_layers,
+            "experts_per_rank": count, "scaling": "strong (one job of `lines` rows over all ranks)",
+            "exchange": "NCCL all-gather of fp32 partials [lines, 2048] + rank-order sum, per layer",
+            "resident_bytes_per_rank": sum(t.nbytes for lay in layers for b in lay.banks for t in b.values())}
+
+
 def config(args):
     return {"workload": f"MoE decode, {args.lines} lines x {args.layers} layers per step, {args.kind} experts "
                         f"(BASELINE configs[1] layer shape; 48 layers as configs[4])",
@@ -391,7 +438,12 @@ def main():
     del graph
 
     extras = {}
-    if not args.no_extras and rank == 0:
+    if world > 1 and not args.no_extras:
+        # expert parallelism (every rank): each rank holds 128 / N experts of one bank set, all ranks decode the same
+        # 16 lines, partials gathered and summed in rank order (ep.py); strong scaling of one job
+        extras["expert_parallel"] = ep_leg(kernels, device, kind, args, stream, pg)
+    if not args.no_extras and world == 1:
+        # the single-GPU legs (at N > 1 the other ranks would wait on them at the final barrier)
         # one line decoded at a time (M = 1), same banks
         extras["lines_1"] = decode_leg(kernels, device, kind, 1, args.steps, args.warmup, stream, n_layers,
                                        (layers, ids[:, :1].contiguous(), weights[:, :1].contiguous()))

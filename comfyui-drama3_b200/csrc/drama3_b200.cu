@@ -445,14 +445,16 @@ static int decode_nkc(const d3::DecodeArgs& a, const DeviceInfo& d, cudaStream_t
   }
 }
 
-extern "C" int d3_moe_decode(int fmt, const void* x, int x_bf16, int M, int k, int E, int H, int I, const int64_t* ids,
-                  const float* weights, const uint8_t* w13, const void* s13, const float* c13, const uint8_t* w2,
-                  const void* s2, const float* c2, const float* codebook13, const float* codebook2, uint16_t* out,
-                  void* workspace, size_t workspace_bytes, void* stream) {
+static int decode_common(int fmt, const void* x, int x_bf16, int M, int k, int E, int e_first, int e_count, int H,
+                         int I, const int64_t* ids, const float* weights, const uint8_t* w13, const void* s13,
+                         const float* c13, const uint8_t* w2, const void* s2, const float* c2,
+                         const float* codebook13, const float* codebook2, uint16_t* out, float* out_f32,
+                         void* workspace, size_t workspace_bytes, void* stream) {
   if (fmt < 0 || fmt >= d3::FMT_COUNT) return D3_ERR_ARG;
   if (M < 1 || M > 16 || k < 1 || k > 32 || M * k > d3::DEC_MAX_PAIRS || E < 1) return D3_ERR_ARG;
+  if (e_first < 0 || e_count < 1 || e_first + e_count > E) return D3_ERR_ARG;
   if (H != d3::DEC_H || (I != 512 && I != 768)) return D3_ERR_ARG;
-  if (!x || !ids || !weights || !w13 || !s13 || !w2 || !s2 || !out || !workspace) return D3_ERR_ARG;
+  if (!x || !ids || !weights || !w13 || !s13 || !w2 || !s2 || (!out && !out_f32) || !workspace) return D3_ERR_ARG;
   if (d3::fmt_codes(fmt) && (!c13 || !c2)) return D3_ERR_ARG;
   if (fmt == d3::FMT_W4 && (!codebook13 || !codebook2)) return D3_ERR_ARG;
   if (workspace_bytes < d3_moe_decode_workspace(M, k, I)) return D3_ERR_WORKSPACE;
@@ -472,7 +474,8 @@ extern "C" int d3_moe_decode(int fmt, const void* x, int x_bf16, int M, int k, i
   auto* words = (unsigned*)tail;
   const int cap = cap_for(M);
   d3::DecodeArgs a = {x, x_bf16, ids, weights, M, k, E, H, I, w13, s13, c13, codebook13, w2, s2, c2, codebook2,
-                      out, a1, parts, barrier, words + 16, words + 128, words + 384, 0, 0, cap};
+                      out, out_f32, e_first, e_count, a1, parts, barrier, words + 16, words + 128, words + 384,
+                      0, 0, cap};
   cudaStream_t s = (cudaStream_t)stream;
   switch (fmt) {
     case d3::FMT_FP8:
@@ -486,6 +489,27 @@ extern "C" int d3_moe_decode(int fmt, const void* x, int x_bf16, int M, int k, i
     case d3::FMT_W6A8: return decode_nkc<d3::FMT_W6A8, true>(a, d, s);
   }
   return D3_ERR_ARG;
+}
+
+extern "C" int d3_moe_decode(int fmt, const void* x, int x_bf16, int M, int k, int E, int H, int I, const int64_t* ids,
+                             const float* weights, const uint8_t* w13, const void* s13, const float* c13,
+                             const uint8_t* w2, const void* s2, const float* c2, const float* codebook13,
+                             const float* codebook2, uint16_t* out, void* workspace, size_t workspace_bytes,
+                             void* stream) {
+  if (!out) return D3_ERR_ARG;
+  return decode_common(fmt, x, x_bf16, M, k, E, 0, E, H, I, ids, weights, w13, s13, c13, w2, s2, c2, codebook13,
+                       codebook2, out, nullptr, workspace, workspace_bytes, stream);
+}
+
+extern "C" int d3_moe_decode_ep(int fmt, const void* x, int x_bf16, int M, int k, int E, int e_first, int e_count,
+                                int H, int I, const int64_t* ids, const float* weights, const uint8_t* w13,
+                                const void* s13, const float* c13, const uint8_t* w2, const void* s2, const float* c2,
+                                const float* codebook13, const float* codebook2, float* partial, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  if (!partial) return D3_ERR_ARG;
+  if (!aligned(partial, 16)) return D3_ERR_ALIGN;
+  return decode_common(fmt, x, x_bf16, M, k, E, e_first, e_count, H, I, ids, weights, w13, s13, c13, w2, s2, c2,
+                       codebook13, codebook2, nullptr, partial, workspace, workspace_bytes, stream);
 }
 
 // ------------------------------------------------------------------------------------------------------------

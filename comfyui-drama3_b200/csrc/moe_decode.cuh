@@ -80,15 +80,18 @@ struct DecodePlan {
   int warp_total[DEC_THREADS / 32];
 };
 
-// All DEC_THREADS threads call this; P <= DEC_MAX_PAIRS <= DEC_THREADS.
-D3_DEV void build_plan(DecodePlan& pl, const int64_t* __restrict__ ids, int P, int E, int cap) {
+// All DEC_THREADS threads call this; P <= DEC_MAX_PAIRS <= DEC_THREADS. Expert parallelism: only ids in
+// [e_first, e_first + e_count) are this rank's (local expert id - e_first); the others are skipped, and only ids
+// outside [0, E) are faults.
+D3_DEV void build_plan(DecodePlan& pl, const int64_t* __restrict__ ids, int P, int E, int cap, int e_first,
+                       int e_count) {
   __shared__ int key[DEC_MAX_PAIRS];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (tid < P) {
-    long long e = ids[tid];
-    bool ok = e >= 0 && e < E;
-    if (!ok) record_fault(FAULT_BAD_EXPERT);
-    key[tid] = ok ? (int)e : 0x7fffffff;
+    const long long e = ids[tid];
+    if (e < 0 || e >= E) record_fault(FAULT_BAD_EXPERT);
+    const bool mine = e >= e_first && e < (long long)e_first + e_count && e < E;
+    key[tid] = mine ? (int)(e - e_first) : 0x7fffffff;
   }
   __syncthreads();
   if (tid < P) {
@@ -379,7 +382,9 @@ struct DecodeArgs {
   const void* s2;
   const float* c2;
   const float* cb2;
-  uint16_t* out;                // [M, H] bf16
+  uint16_t* out;                // [M, H] bf16 (or null, with out_f32)
+  float* out_f32;               // [M, H] fp32 partial sums of this rank's experts (expert parallelism), or null
+  int e_first, e_count;         // this rank's experts: ids in [e_first, e_first + e_count); the banks hold them
   float* a1;                    // scratch [M*k, I]
   float* parts;                 // scratch [M*k, H]
   unsigned long long* barrier;  // scratch: zero before the first call; grows by gridDim.x per grid-wide barrier
@@ -822,7 +827,10 @@ D3_DEV void combine_columns(const DecodeArgs& a, const unsigned char* valid, con
       for (int u = 0; u < 8; ++u)
         if (j0 + u < a.k) acc = __fmaf_rn(v[u], w[t * a.k + j0 + u], acc);
     }
-    a.out[(size_t)t * H + n] = f32_to_bf16(acc);
+    if (a.out_f32)
+      a.out_f32[(size_t)t * H + n] = acc;
+    else
+      a.out[(size_t)t * H + n] = f32_to_bf16(acc);
   }
 }
 
@@ -875,7 +883,7 @@ __global__ void __launch_bounds__(DEC_ALL, 1) moe_decode_kernel(const DecodeArgs
     lut1[tid] = a.cb13[tid];
     lut2[tid] = a.cb2[tid];
   }
-  build_plan(pl, a.ids, P, a.E, a.cap);
+  build_plan(pl, a.ids, P, a.E, a.cap, a.e_first, a.e_count);
   D3_STAMP(1);
   const int nseg = pl.nseg, G = gridDim.x;
   // group mode needs at least 8 CTAs per segment, so that a CTA's down rows (H / 8 = 256 at most) span <= 5 blocks
@@ -1053,7 +1061,7 @@ __global__ void __launch_bounds__(DEC_ALL, 1) moe_decode_kernel(const DecodeArgs
   __shared__ unsigned char c_ok[DEC_MAX_PAIRS];
   if (tid < P) {
     const long long id = a.ids[tid];
-    c_ok[tid] = nseg > 0 && id >= 0 && id < a.E;
+    c_ok[tid] = nseg > 0 && id >= a.e_first && id < (long long)a.e_first + a.e_count && id < a.E;
     c_w[tid] = a.weights[tid];
   }
   if (!grouped) {

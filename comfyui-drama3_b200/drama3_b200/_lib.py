@@ -46,6 +46,8 @@ SIGNATURES = {
     "d3_moe_decode_workspace": (_sz, [_i, _i, _i]),
     "d3_moe_decode": (_i, [_i, _p, _i, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _sz, _p]),
     "d3_moe_decode_static": (_i, [_i, _p, _i, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
+    "d3_moe_decode_ep": (_i, [_i, _p, _i, _i, _i, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
+                              _sz, _p]),
 }
 
 

@@ -264,6 +264,39 @@ def prefill_combine(sorted_out, pos, weights, dtype=torch.bfloat16):
     return out
 
 
+def moe_decode_ep(kind, x, ids, weights, banks, e_first, num_experts, codebooks=(None, None), workspace=None,
+                  partial=None):
+    """[M, H] float32: moe_decode over this rank's experts only (expert parallelism). `banks` hold experts
+    [e_first, e_first + E_local) of the num_experts routed ones (bank expert 0 = expert e_first); pairs routed to other
+    ranks' experts are skipped. The result is the routing-weighted sum over this rank's pairs, in rank order;
+    summing the ranks' results and rounding to bf16 gives moe_decode's output."""
+    fmt = _lib.FORMATS[kind]
+    if x.dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError(f"moe_decode_ep takes bfloat16 or float32 rows, not {x.dtype}")
+    gate_up, down = banks
+    wkey = _lib.WEIGHT_KEY[kind]
+    M, H = x.shape
+    k = ids.shape[-1]
+    w13, w2 = gate_up[wkey], down[wkey]
+    e_local = w2.shape[0] // H
+    I = w13.shape[0] // (2 * e_local)
+    if partial is None:
+        partial = torch.empty((M, H), dtype=torch.float32, device=x.device)
+    if workspace is None:
+        workspace = decode_workspace(M, k, I, x.device)
+    x = x.contiguous()
+    ids = ids.reshape(M, k).contiguous()
+    weights = weights.reshape(M, k).float().contiguous()
+    with _on(x.device):
+        check(lib().d3_moe_decode_ep(fmt, _ptr(x), int(x.dtype == torch.bfloat16), M, k, int(num_experts),
+                                     int(e_first), e_local, H, I, _ptr(ids), _ptr(weights), _ptr(w13),
+                                     _ptr(gate_up["scale"]), _ptr(gate_up.get("s_channel")), _ptr(w2),
+                                     _ptr(down["scale"]), _ptr(down.get("s_channel")), _ptr(codebooks[0]),
+                                     _ptr(codebooks[1]), _ptr(partial), _ptr(workspace), workspace.numel(),
+                                     _stream(x.device)), "moe_decode_ep")
+    return partial
+
+
 def decode_workspace(rows, k, intermediate, device):
     """The workspace moe_decode needs, allocated once by the caller and reused by every call (graph-captured steps
     included). It must start zeroed: its last bytes are the kernel's grid-barrier ticket counter, which each call

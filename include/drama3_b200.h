@@ -161,6 +161,15 @@ int d3_moe_decode(int fmt, const void* x, int x_bf16, int M, int k, int E, int H
                   const void* s2, const float* c2, const float* codebook13, const float* codebook2, uint16_t* out,
                   void* workspace, size_t workspace_bytes, void* stream);
 
+/* Expert parallelism: d3_moe_decode of this rank's experts only. The banks hold experts [e_first, e_first +
+ * e_count) of the E routed ones (bank expert 0 = expert e_first); pairs routed elsewhere are skipped (not faults);
+ * partial [M, H] fp32 receives the routing-weighted sum over this rank's pairs, in rank order. Summing the ranks'
+ * partials (in rank order) and rounding to bf16 gives the whole decode. No counterpart in the reference (one GPU). */
+int d3_moe_decode_ep(int fmt, const void* x, int x_bf16, int M, int k, int E, int e_first, int e_count, int H, int I,
+                     const int64_t* ids, const float* weights, const uint8_t* w13, const void* s13, const float* c13,
+                     const uint8_t* w2, const void* s2, const float* c2, const float* codebook13,
+                     const float* codebook2, float* partial, void* workspace, size_t workspace_bytes, void* stream);
+
 /* d3_moe_decode without a workspace argument. No counterpart in the reference: it is for callers that cannot
  * allocate device memory themselves, such as a plugin whose host application's memory manager owns every device
  * allocation, or a C host that links this library without any device allocator. The scratch is an array inside the

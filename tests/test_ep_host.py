@@ -1,0 +1,86 @@
+"""Expert parallelism on CPU ranks (gloo, world size 2): the expert partition, the bank slicing and the exchange
+(all-gather + rank-order sum) of drama3_b200.ep, with the oracle standing in for each rank's GPU kernel."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from drama3_b200 import ep
+from oracle import moe
+
+E, H, I, K = 8, 256, 128, 4
+
+
+def test_expert_range_covers_all_in_order():
+    for E_, world in ((128, 8), (128, 3), (7, 4), (16, 16)):
+        ranges = [ep.expert_range(E_, r, world) for r in range(world)]
+        assert ranges[0][0] == 0 and sum(c for _, c in ranges) == E_
+        for (f0, c0), (f1, _) in zip(ranges, ranges[1:]):
+            assert f1 == f0 + c0
+        assert max(c for _, c in ranges) - min(c for _, c in ranges) <= 1
+
+
+def _banks():
+    rng = np.random.default_rng(11)
+    w13 = rng.normal(0, 0.02, size=(E, 2 * I, H)).astype(np.float32)
+    w2 = rng.normal(0, 0.02, size=(E, H, I)).astype(np.float32)
+    return moe.make_baseline_bank("fp8c", w13), moe.make_baseline_bank("fp8c", w2)
+
+
+def _inputs():
+    rng = np.random.default_rng(12)
+    x = moe.bf16_round(rng.normal(size=(3, H)).astype(np.float32))
+    ids = np.stack([rng.permutation(E)[:K] for _ in range(3)])
+    w = moe.bf16_round(rng.dirichlet(np.ones(K), size=3).astype(np.float32))
+    return x, ids, w
+
+
+def _oracle_partial(banks, x, ids, w, first, count):
+    """The routing-weighted sum over the pairs of experts [first, first + count), in rank order (fp32)."""
+    gate_up, down = banks
+    out = np.zeros((x.shape[0], H), np.float32)
+    for t in range(x.shape[0]):
+        for j, e in enumerate(ids[t]):
+            if not first <= e < first + count:
+                continue
+            h = moe.baseline_rows("fp8c", x[t:t + 1], gate_up, int(e) * 2 * I, 2 * I)
+            a = moe._silu_mul(h[:, :I], h[:, I:])
+            part = moe.baseline_rows("fp8c", a, down, int(e) * H, H)[0]
+            out[t] = moe.fma32(part, np.full(H, w[t, j], np.float32), out[t])
+    return out
+
+
+def _worker(rank, world, port, result):
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        banks = _banks()
+        x, ids, w = _inputs()
+        first, count = ep.expert_range(E, rank, world)
+        local = ep.local_banks(tuple({n: torch.from_numpy(v) for n, v in b.items()} for b in banks), E, rank, world)
+        assert local[0]["weight"].shape[0] == count * 2 * I and local[1]["scale"].shape[0] == count * H
+
+        def decode_fn(xt, idt, wt):
+            return torch.from_numpy(_oracle_partial(banks, xt.numpy(), idt.numpy(), wt.numpy(), first, count))
+
+        layer = ep.ExpertParallelDecode("fp8c", local, E, decode_fn=decode_fn)
+        out = layer(torch.from_numpy(x), torch.from_numpy(ids), torch.from_numpy(w))
+        full = moe.baseline_decode("fp8c", x, ids, w, banks)
+        err = float(np.linalg.norm(out.float().numpy() - full) / np.linalg.norm(full))
+        result[rank] = err
+    finally:
+        dist.destroy_process_group()
+
+
+def test_expert_parallel_exchange_two_cpu_ranks():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    result = ctx.Manager().dict()
+    mp.start_processes(_worker, args=(2, port, result), nprocs=2, join=True, start_method="spawn")
+    assert sorted(result.keys()) == [0, 1]
+    assert all(err <= 1e-3 for err in result.values()), dict(result)
