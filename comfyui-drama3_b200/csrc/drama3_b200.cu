@@ -151,6 +151,10 @@ int d3_device_check(void) {
 #ifdef D3_TRACE
 // Trace builds only: copy the per-CTA phase timestamps (uint64 [1024][24]) to host memory.
 int d3_trace_read(void* dst) { return cuda_status(cudaMemcpyFromSymbol(dst, d3::g_trace, sizeof(d3::g_trace))); }
+// Trace builds only: the grouped GEMM's per-CTA wait counters (uint64 [1024][12]).
+int d3_gm_trace_read(void* dst) {
+  return cuda_status(cudaMemcpyFromSymbol(dst, d3::g_gm_trace, sizeof(d3::g_gm_trace)));
+}
 #endif
 
 int d3_take_fault(unsigned int* fault) {

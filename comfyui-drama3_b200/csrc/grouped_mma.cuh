@@ -34,6 +34,20 @@
 
 namespace d3 {
 
+#ifdef D3_TRACE
+// Trace builds only: per CTA, cycles each role spent waiting at each barrier (clock64), and counters.
+//   0 raw producer / raw_empty   1 B producer / mma_empty   2 MMA / acc_empty   3 MMA / a_full   4 MMA / b_full
+//   5 converters / raw_full      6 converters / mma_empty   7 fold / acc_full   8 units   9 total cycles
+//   10 converter busy cycles     11 fold busy cycles
+__device__ unsigned long long g_gm_trace[1024][12];
+#define GM_T0() const long long _t0 = clock64()
+#define GM_TADD(slot) \
+  if (blockIdx.x < 1024) atomicAdd(&g_gm_trace[blockIdx.x][slot], (unsigned long long)(clock64() - _t0))
+#else
+#define GM_T0()
+#define GM_TADD(slot)
+#endif
+
 constexpr int GM_M = 128;              // weight rows per unit (one fp8 scale block)
 constexpr int GM_NT = 128;             // token rows per tile
 constexpr int GM_KC = 64;              // columns per MMA chunk: one 128-byte swizzle atom of f16
@@ -499,6 +513,11 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
   float* lut = (float*)(smem + GmSmem::lut);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#ifdef D3_TRACE
+  const long long t_kernel = clock64();
+  if (threadIdx.x == 0 && blockIdx.x < 1024)
+    for (int i = 0; i < 12; ++i) g_gm_trace[blockIdx.x][i] = 0;
+#endif
   if (threadIdx.x == 0) {
     for (int i = 0; i < GM_RAW_ST; ++i) {
       mbar_init(raw_full + i, 1);
@@ -537,7 +556,11 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         const int wrow = slot * a.N + rb * GM_M;
         if (slot < 0 || wrow + GM_M > a.bank_rows) continue;
         for (int kr = 0; kr < a.K / GM_RKC && ok; ++kr) {
-          ok = mbar_wait(raw_empty + rs, rph ^ 1);
+          {
+            GM_T0();
+            ok = mbar_wait(raw_empty + rs, rph ^ 1);
+            GM_TADD(0);
+          }
           if (!ok) break;
           uint8_t* dst = smem + GmSmem::raw + rs * GM_RAW_BYTES;
           mbar_arrive_expect_tx(raw_full + rs, GM_M * gm_raw_row_bytes<FMT>());
@@ -571,7 +594,11 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         const uint8_t* src = a.staged + (size_t)tile * nkc * 2 * GM_B_BYTES;
         const uint32_t bytes = (uint32_t)gm_width(a.table[tile].rows) * 128u;  // rows x 64 f16 per term
         for (int kc = 0; kc < nkc && ok; ++kc) {
-          ok = mbar_wait(mma_empty + ms, mph ^ 1);
+          {
+            GM_T0();
+            ok = mbar_wait(mma_empty + ms, mph ^ 1);
+            GM_TADD(1);
+          }
           if (!ok) break;
           uint8_t* dst = smem + GmSmem::b + ms * 2 * GM_B_BYTES;
           const uint8_t* blk = src + (size_t)kc * 2 * GM_B_BYTES;
@@ -600,12 +627,25 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         for (int kc = 0; kc < nkc && ok; ++kc) {
           if (kc % kbc == 0) {
             const int region = folds & 1;
-            ok = mbar_wait(acc_empty + region, ((folds >> 1) & 1) ^ 1);
+            {
+              GM_T0();
+              ok = mbar_wait(acc_empty + region, ((folds >> 1) & 1) ^ 1);
+              GM_TADD(2);
+            }
             if (!ok) break;
             tc_fence_after();
             acc = tmem + region * GM_NT;
           }
-          ok = mbar_wait(a_full + ms, mph) && mbar_wait(b_full + ms, mph);
+          {
+            GM_T0();
+            ok = mbar_wait(a_full + ms, mph);
+            GM_TADD(3);
+          }
+          {
+            GM_T0();
+            ok = ok && mbar_wait(b_full + ms, mph);
+            GM_TADD(4);
+          }
           if (!ok) break;
           tc_fence_after();
           const uint32_t as = smem_u32(smem + GmSmem::a + ms * GM_A_BYTES);
@@ -644,10 +684,23 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       for (int kc = 0; kc < nkc && ok; ++kc) {
         const int h = kc & 1;
         const uint32_t sbytes = srow ? __ldg((const uint32_t*)(srow + 4 * kc)) : 0u;
-        ok = (h == 1 || mbar_wait(raw_full + rs, rph)) && mbar_wait(mma_empty + ms, mph ^ 1);
+        {
+          GM_T0();
+          ok = (h == 1 || mbar_wait(raw_full + rs, rph));
+          if (r == 0) GM_TADD(5);
+        }
+        {
+          GM_T0();
+          ok = ok && mbar_wait(mma_empty + ms, mph ^ 1);
+          if (r == 0) GM_TADD(6);
+        }
         if (!ok) break;
-        gm_convert<FMT>(smem + GmSmem::raw + rs * GM_RAW_BYTES, h, smem + GmSmem::a + ms * GM_A_BYTES, r, sbytes,
-                        lut);
+        {
+          GM_T0();
+          gm_convert<FMT>(smem + GmSmem::raw + rs * GM_RAW_BYTES, h, smem + GmSmem::a + ms * GM_A_BYTES, r, sbytes,
+                          lut);
+          if (r == 0) GM_TADD(10);
+        }
         fence_async_smem();
         __syncwarp();
         if (lane == 0) {
@@ -691,7 +744,11 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         for (int j = 0; j < GM_NT; ++j) acc[j] = 0.0f;
         for (int f = 0; f < nfold && ok; ++f) {
           const int region = folds & 1;
-          ok = mbar_wait(acc_full + region, (folds >> 1) & 1);
+          {
+            GM_T0();
+            ok = mbar_wait(acc_full + region, (folds >> 1) & 1);
+            if (r == 0) GM_TADD(7);
+          }
           if (!ok) break;
           tc_fence_after();
           const float s = FMT == FMT_FP8
@@ -717,7 +774,11 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       } else {
         // one fold per unit: the row scale (int8 scale, W4/W6 s_channel) and each row's 2^-e, straight to out
         const int region = folds & 1;
-        ok = mbar_wait(acc_full + region, (folds >> 1) & 1);
+        {
+          GM_T0();
+          ok = mbar_wait(acc_full + region, (folds >> 1) & 1);
+          if (r == 0) GM_TADD(7);
+        }
         if (!ok) break;
         tc_fence_after();
         const float rs = fmt_row_scale(FMT) ? __ldg((const float*)a.scale + wrow + r) : __ldg(a.s_channel + wrow + r);
@@ -740,6 +801,14 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
+#ifdef D3_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < 1024) {
+    g_gm_trace[blockIdx.x][9] = clock64() - t_kernel;
+    int n = 0, tile, rb;
+    for (int u = blockIdx.x; gm_unit(a, ntiles, u, tile, rb); u += G) ++n;
+    g_gm_trace[blockIdx.x][8] = n;
+  }
+#endif
   if (warp == 2) {
     tc_fence_after();
     tmem_dealloc(tmem, GM_TMEM_COLS);
