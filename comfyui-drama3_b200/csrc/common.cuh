@@ -18,6 +18,7 @@ enum : unsigned {
   FAULT_BAD_EXPERT = 2u,    // an expert id outside [0, E): the pair was skipped
   FAULT_BAD_SLOT = 4u,      // a slot index outside [0, count): the expert was skipped
   FAULT_TILES = 8u,         // the groups need more row tiles than the caller sized: the excess rows were skipped
+  FAULT_EXCHANGE = 16u,     // an expert-parallel exchange area that does not fit the call: nothing was exchanged
 };
 __device__ unsigned int g_fault;
 

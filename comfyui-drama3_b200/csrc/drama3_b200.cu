@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstring>
 #include <mutex>
 
 #include <cudaTypedefs.h>
@@ -453,17 +454,18 @@ static int decode_common(int fmt, const void* x, int x_bf16, int M, int k, int E
                          int I, const int64_t* ids, const float* weights, const uint8_t* w13, const void* s13,
                          const float* c13, const uint8_t* w2, const void* s2, const float* c2,
                          const float* codebook13, const float* codebook2, uint16_t* out, float* out_f32,
-                         void* workspace, size_t workspace_bytes, void* stream) {
+                         const void* exchange, void* workspace, size_t workspace_bytes, void* stream) {
   if (fmt < 0 || fmt >= d3::FMT_COUNT) return D3_ERR_ARG;
   if (M < 1 || M > 16 || k < 1 || k > 32 || M * k > d3::DEC_MAX_PAIRS || E < 1) return D3_ERR_ARG;
   if (e_first < 0 || e_count < 1 || e_first + e_count > E) return D3_ERR_ARG;
   if (H != d3::DEC_H || (I != 512 && I != 768)) return D3_ERR_ARG;
-  if (!x || !ids || !weights || !w13 || !s13 || !w2 || !s2 || (!out && !out_f32) || !workspace) return D3_ERR_ARG;
+  if (!x || !ids || !weights || !w13 || !s13 || !w2 || !s2 || (!out && !out_f32 && !exchange) || !workspace)
+    return D3_ERR_ARG;
   if (d3::fmt_codes(fmt) && (!c13 || !c2)) return D3_ERR_ARG;
   if (fmt == d3::FMT_W4 && (!codebook13 || !codebook2)) return D3_ERR_ARG;
   if (workspace_bytes < d3_moe_decode_workspace(M, k, I)) return D3_ERR_WORKSPACE;
   if (!aligned(x, 16) || !aligned(w13, 16) || !aligned(w2, 16) || !aligned(workspace, 256) || !aligned(s13, 16) ||
-      !aligned(s2, 16))
+      !aligned(s2, 16) || !aligned(exchange, 8))
     return D3_ERR_ALIGN;
   DeviceInfo d;
   if (int st = device_info(&d)) return st;
@@ -478,8 +480,8 @@ static int decode_common(int fmt, const void* x, int x_bf16, int M, int k, int E
   auto* words = (unsigned*)tail;
   const int cap = cap_for(M);
   d3::DecodeArgs a = {x, x_bf16, ids, weights, M, k, E, H, I, w13, s13, c13, codebook13, w2, s2, c2, codebook2,
-                      out, out_f32, e_first, e_count, a1, parts, barrier, words + 16, words + 128, words + 384,
-                      0, 0, cap};
+                      out, out_f32, e_first, e_count, (const d3::EpExchange*)exchange, words + 4, a1, parts, barrier,
+                      words + 16, words + 128, words + 384, 0, 0, cap};
   cudaStream_t s = (cudaStream_t)stream;
   switch (fmt) {
     case d3::FMT_FP8:
@@ -502,18 +504,83 @@ extern "C" int d3_moe_decode(int fmt, const void* x, int x_bf16, int M, int k, i
                              void* stream) {
   if (!out) return D3_ERR_ARG;
   return decode_common(fmt, x, x_bf16, M, k, E, 0, E, H, I, ids, weights, w13, s13, c13, w2, s2, c2, codebook13,
-                       codebook2, out, nullptr, workspace, workspace_bytes, stream);
+                       codebook2, out, nullptr, nullptr, workspace, workspace_bytes, stream);
 }
 
 extern "C" int d3_moe_decode_ep(int fmt, const void* x, int x_bf16, int M, int k, int E, int e_first, int e_count,
                                 int H, int I, const int64_t* ids, const float* weights, const uint8_t* w13,
                                 const void* s13, const float* c13, const uint8_t* w2, const void* s2, const float* c2,
-                                const float* codebook13, const float* codebook2, float* partial, void* workspace,
-                                size_t workspace_bytes, void* stream) {
-  if (!partial) return D3_ERR_ARG;
-  if (!aligned(partial, 16)) return D3_ERR_ALIGN;
+                                const float* codebook13, const float* codebook2, float* partial,
+                                const void* exchange, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!partial && !exchange) return D3_ERR_ARG;
+  if (partial && !aligned(partial, 16)) return D3_ERR_ALIGN;
   return decode_common(fmt, x, x_bf16, M, k, E, e_first, e_count, H, I, ids, weights, w13, s13, c13, w2, s2, c2,
-                       codebook13, codebook2, nullptr, partial, workspace, workspace_bytes, stream);
+                       codebook13, codebook2, nullptr, exchange ? nullptr : partial, exchange, workspace,
+                       workspace_bytes, stream);
+}
+
+// ------------------------------------------------------------------------------------------------------------
+// Expert-parallel exchange over peer memory.
+
+extern "C" size_t d3_ep_exchange_bytes(int world, int m_max, int H) {
+  if (world < 1 || world > d3::EP_MAX_RANKS || m_max < 1 || H < 1) return 0;
+  return align256((size_t)2 * world * m_max * H * 4) + 256;
+}
+
+extern "C" int d3_ep_reduce(const void* exchange, int M, int H, void* out, void* stream) {
+  DeviceInfo d;
+  if (int st = device_info(&d)) return st;
+  if (!exchange || !out || M < 1 || H < 1) return D3_ERR_ARG;
+  if (H % 4) return D3_ERR_ARG;
+  if (!aligned(exchange, 8) || !aligned(out, 8)) return D3_ERR_ALIGN;
+  const int blocks = (int)(((size_t)M * H / 4 + d3::EP_REDUCE_THREADS - 1) / d3::EP_REDUCE_THREADS);
+  return launch(d3::ep_reduce_kernel, dim3(blocks), dim3(d3::EP_REDUCE_THREADS), 0, (cudaStream_t)stream, true,
+                (const d3::EpExchange*)exchange, M, H, (uint16_t*)out);
+}
+
+namespace {
+PFN_cuMemGetAddressRange_v3020 address_range_fn() {
+  static PFN_cuMemGetAddressRange_v3020 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuMemGetAddressRange_v3020)p;
+  });
+  return fn;
+}
+}  // namespace
+
+extern "C" int d3_ipc_handle(const void* ptr, void* handle, size_t* offset) {
+  if (!ptr || !handle || !offset) return D3_ERR_ARG;
+  PFN_cuMemGetAddressRange_v3020 fn = address_range_fn();
+  if (!fn) return D3_ERR_DEVICE;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (fn(&base, &size, (CUdeviceptr)ptr) != CUDA_SUCCESS) return D3_ERR_ARG;
+  cudaIpcMemHandle_t h;
+  if (int st = cuda_status(cudaIpcGetMemHandle(&h, (void*)base))) return st;
+  memcpy(handle, &h, sizeof(h));
+  *offset = (size_t)((uintptr_t)ptr - (uintptr_t)base);
+  return D3_OK;
+}
+
+extern "C" int d3_ipc_open(const void* handle, size_t offset, void** ptr, void** base) {
+  if (!handle || !ptr || !base) return D3_ERR_ARG;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* b = nullptr;
+  if (int st = cuda_status(cudaIpcOpenMemHandle(&b, h, cudaIpcMemLazyEnablePeerAccess))) return st;
+  *base = b;
+  *ptr = (void*)((uintptr_t)b + offset);
+  return D3_OK;
+}
+
+extern "C" int d3_ipc_close(void* base) {
+  if (!base) return D3_ERR_ARG;
+  return cuda_status(cudaIpcCloseMemHandle(base));
 }
 
 // ------------------------------------------------------------------------------------------------------------

@@ -368,6 +368,26 @@ D3_DEV void load_b(const __half* xrow, int col, uint32_t (&b)[8]) {
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// Expert-parallel exchange over peer memory (one node, up to 8 ranks). Every rank holds an exchange area: fp32
+// slots [2][world][M_max * H] (two sets, alternating by call parity), flags [2][8] and its call counter `epoch`. A
+// decode pushes this rank's fp32 partial into its slot of every rank's area (P2P stores over NVLink for peers) and
+// then, once all its CTAs have, raises flag[parity][rank] = epoch + 1 on every rank (system-scope release); the
+// reduce kernel waits for all ranks' flags, sums the slots in rank order and advances the counter (the word after the
+// counter counts the reduce's finished CTAs). A rank can run at
+// most one call ahead of a peer's reduce (its next reduce needs the peer's next push), so two slot sets suffice.
+constexpr int EP_MAX_RANKS = 8;
+struct EpExchange {
+  float* slots[EP_MAX_RANKS];     // rank r's area (this rank's own pointer, or the IPC mapping of a peer's)
+  unsigned* flags[EP_MAX_RANKS];  // rank r's flags [2][EP_MAX_RANKS]
+  unsigned* epoch;                // this rank's call counter
+  int world, rank, m_max, h;      // the area's geometry: slots [2][world][m_max * h]
+};
+
+__device__ __forceinline__ bool ep_geometry_ok(const EpExchange& ex, int M, int H) {
+  return ex.world >= 1 && ex.world <= EP_MAX_RANKS && ex.rank >= 0 && ex.rank < ex.world && M <= ex.m_max &&
+         H == ex.h;
+}
+
 struct DecodeArgs {
   const void* x;  // [M, H]: bf16 when x_bf16, else fp32
   int x_bf16;
@@ -385,6 +405,8 @@ struct DecodeArgs {
   uint16_t* out;                // [M, H] bf16 (or null, with out_f32)
   float* out_f32;               // [M, H] fp32 partial sums of this rank's experts (expert parallelism), or null
   int e_first, e_count;         // this rank's experts: ids in [e_first, e_first + e_count); the banks hold them
+  const EpExchange* ex;         // expert parallelism over peer memory: push the partial to every rank, or null
+  unsigned* ep_done;            // scratch: combine-completion counter for the exchange, zero between calls
   float* a1;                    // scratch [M*k, I]
   float* parts;                 // scratch [M*k, H]
   unsigned long long* barrier;  // scratch: zero before the first call; grows by gridDim.x per grid-wide barrier
@@ -827,10 +849,21 @@ D3_DEV void combine_columns(const DecodeArgs& a, const unsigned char* valid, con
       for (int u = 0; u < 8; ++u)
         if (j0 + u < a.k) acc = __fmaf_rn(v[u], w[t * a.k + j0 + u], acc);
     }
-    if (a.out_f32)
+    if (a.ex) {
+      // this rank's slot in every rank's area (call parity set)
+      const EpExchange& ex = *a.ex;
+      if (ep_geometry_ok(ex, a.M, H)) {
+        const unsigned ep = *(volatile const unsigned*)ex.epoch + 1u;
+        const size_t off = ((size_t)((ep & 1u) * ex.world + ex.rank) * ex.m_max + t) * H + n;
+        for (int r = 0; r < ex.world; ++r) ex.slots[r][off] = acc;
+      } else if (t == 0 && n == n0) {
+        record_fault(FAULT_EXCHANGE);
+      }
+    } else if (a.out_f32) {
       a.out_f32[(size_t)t * H + n] = acc;
-    else
+    } else {
       a.out[(size_t)t * H + n] = f32_to_bf16(acc);
+    }
   }
 }
 
@@ -1102,7 +1135,95 @@ __global__ void __launch_bounds__(DEC_ALL, 1) moe_decode_kernel(const DecodeArgs
       if (tid == 0) a.blocks[b] = 0u;
     }
   }
+  if (a.ex) {
+    // exchange: once every column block of this rank's partial has been pushed, raise this rank's flag on every rank
+    // (grid mode: every CTA pushed its share of the columns; group mode: the CTAs that completed blocks pushed them)
+    __threadfence_system();  // this thread's pushes, before the count that releases them
+    named_sync(2, DEC_CONSUMERS + 32);
+    if (tid == 0 && ep_geometry_ok(*a.ex, a.M, H)) {
+      const unsigned share = grouped ? (unsigned)s_nblk : 1u, total = grouped ? (unsigned)(H / DEC_CB) : (unsigned)G;
+      if (share > 0) {
+        __threadfence_system();
+        if (atomicAdd(a.ep_done, share) + share == total) {
+          const EpExchange& ex = *a.ex;
+          const unsigned ep = *(volatile const unsigned*)ex.epoch + 1u;
+          __threadfence_system();
+          for (int r = 0; r < ex.world; ++r) {
+            unsigned* f = ex.flags[r] + (ep & 1u) * EP_MAX_RANKS + ex.rank;
+            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(ep) : "memory");
+          }
+          *a.ep_done = 0u;
+        }
+      }
+    }
+  }
   D3_STAMP(6);
+}
+
+// The exchange's reduce on one rank: every CTA waits (bounded) until each rank has raised its flag for this call,
+// then sums 4 columns a thread, out[t, n..n+3] = bf16(sum over ranks r in order of slot r); the last CTA to finish
+// advances this rank's call counter (the counter word after it counts finished CTAs). Launched with programmatic
+// dependent launch: it may be scheduled while the decode still runs, and reads nothing before that grid completes.
+constexpr int EP_REDUCE_THREADS = 256;
+__global__ void __launch_bounds__(EP_REDUCE_THREADS) ep_reduce_kernel(const EpExchange* __restrict__ exp, int M, int H,
+                                                                      uint16_t* __restrict__ out) {
+  __shared__ int s_ok;
+  __shared__ unsigned s_ep;
+  allow_dependents();
+  grid_dependency_wait();
+  const EpExchange& ex = *exp;
+  if (threadIdx.x == 0) {
+    const unsigned ep = *(volatile const unsigned*)ex.epoch + 1u;
+    int ok = ep_geometry_ok(ex, M, H) && H % 4 == 0;
+    if (!ok) record_fault(FAULT_EXCHANGE);
+    const unsigned* flags = ok ? ex.flags[ex.rank] + (ep & 1u) * EP_MAX_RANKS : nullptr;
+    const unsigned long long start = globaltimer();
+    for (int r = 0; r < ex.world && ok; ++r) {
+      while (true) {
+        unsigned v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + r) : "memory");
+        if ((int)(v - ep) >= 0) break;
+        if (globaltimer() - start > WAIT_LIMIT_NS) {
+          record_fault(FAULT_WAIT_TIMEOUT);
+          ok = 0;
+          break;
+        }
+      }
+    }
+    s_ok = ok;
+    s_ep = ep;
+  }
+  __syncthreads();
+  const int ok = s_ok;
+  const unsigned ep = s_ep;
+  const int q = blockIdx.x * EP_REDUCE_THREADS + threadIdx.x;  // a group of 4 columns
+  if (q * 4 < M * H) {
+    const int t = (q * 4) / H, n = q * 4 - t * H;
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (ok) {
+      const float* base = ex.slots[ex.rank] + (size_t)(ep & 1u) * ex.world * ex.m_max * H;
+      for (int r = 0; r < ex.world; ++r) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(base + ((size_t)r * ex.m_max + t) * H + n));
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+    }
+    uint2 packed;
+    packed.x = (uint32_t)f32_to_bf16(acc.x) | ((uint32_t)f32_to_bf16(acc.y) << 16);
+    packed.y = (uint32_t)f32_to_bf16(acc.z) | ((uint32_t)f32_to_bf16(acc.w) << 16);
+    *reinterpret_cast<uint2*>(out + (size_t)t * H + n) = packed;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned* done = ex.epoch + 1;
+    __threadfence();
+    if (atomicAdd(done, 1u) + 1u == gridDim.x) {
+      *done = 0u;
+      *(volatile unsigned*)ex.epoch = ep;
+    }
+  }
 }
 
 }  // namespace d3

@@ -47,7 +47,12 @@ SIGNATURES = {
     "d3_moe_decode": (_i, [_i, _p, _i, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _sz, _p]),
     "d3_moe_decode_static": (_i, [_i, _p, _i, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
     "d3_moe_decode_ep": (_i, [_i, _p, _i, _i, _i, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
-                              _sz, _p]),
+                              _p, _sz, _p]),
+    "d3_ep_exchange_bytes": (_sz, [_i, _i, _i]),
+    "d3_ep_reduce": (_i, [_p, _i, _i, _p, _p]),
+    "d3_ipc_handle": (_i, [_p, _p, ctypes.POINTER(ctypes.c_size_t)]),
+    "d3_ipc_open": (_i, [_p, _sz, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p)]),
+    "d3_ipc_close": (_i, [_p]),
 }
 
 

@@ -4,12 +4,94 @@ replicated), runs the fused decode over its own experts only and produces an fp3
 gathered and summed in rank order, then rounded to bf16 once, so every rank ends with the same output.
 
 The reference runs on one GPU; this is the multi-GPU layout of its decode step (experts split, tokens replicated,
-partial combines reduced). The exchange is a 128 KB all-gather per layer at 16 lines over NCCL (NVLink).
+partial combines reduced). Two exchanges: an all-gather over NCCL (128 KB per layer at 16 lines), or PeerExchange,
+where the decode kernel's combine stores its partial straight into every rank's exchange area over NVLink (P2P
+stores through CUDA IPC mappings) and a small reduce kernel sums them once all ranks' flags are up - no collective
+launch, the transfer overlapping the combine.
 """
+import ctypes
+
 import torch
 import torch.distributed as dist
 
-from . import kernels
+from . import _lib, kernels
+
+EP_MAX_RANKS = 8
+
+
+class ExchangeStruct(ctypes.Structure):
+    """The device struct the decode and reduce kernels read (d3::EpExchange)."""
+    _fields_ = [("slots", ctypes.c_uint64 * EP_MAX_RANKS), ("flags", ctypes.c_uint64 * EP_MAX_RANKS),
+                ("epoch", ctypes.c_uint64), ("world", ctypes.c_int32), ("rank", ctypes.c_int32),
+                ("m_max", ctypes.c_int32), ("h", ctypes.c_int32)]
+
+
+def exchange_layout(world, m_max, hidden):
+    """(area bytes, flags offset): fp32 slots [2][world][m_max][hidden], then at the next 256-byte boundary the
+    flags [2][8] (uint32) and this rank's call counter."""
+    size = _lib.lib().d3_ep_exchange_bytes(world, m_max, hidden)
+    if size == 0:
+        raise ValueError(f"no exchange for world {world}, m_max {m_max}, hidden {hidden}")
+    slots = 2 * world * m_max * hidden * 4
+    return size, (slots + 255) // 256 * 256
+
+
+def exchange_struct(slot_ptrs, flags_offset, rank, m_max, hidden):
+    """The struct for this rank, from the base addresses of every rank's area as mapped here."""
+    st = ExchangeStruct()
+    for r, base in enumerate(slot_ptrs):
+        st.slots[r] = base
+        st.flags[r] = base + flags_offset
+    st.epoch = slot_ptrs[rank] + flags_offset + 2 * EP_MAX_RANKS * 4
+    st.world, st.rank, st.m_max, st.h = len(slot_ptrs), rank, m_max, hidden
+    return bytes(st)
+
+
+class PeerExchange:
+    """Exchange areas for up to m_max lines of `hidden` columns, one per rank of `group` (one process per GPU of one
+    node), each mapped into every other rank with CUDA IPC. Collective to create and to close. One exchange serves
+    every layer: calls go through it one at a time, in the same order on every rank."""
+
+    def __init__(self, m_max, hidden, device, group=None):
+        self.group, self.m_max, self.hidden = group, m_max, hidden
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        if self.world > EP_MAX_RANKS:
+            raise ValueError(f"a peer exchange spans at most {EP_MAX_RANKS} ranks, not {self.world}")
+        size, flags_offset = exchange_layout(self.world, m_max, hidden)
+        self.area = torch.zeros((size,), dtype=torch.uint8, device=device)
+        torch.cuda.synchronize(device)
+        handle = (ctypes.c_char * 64)()
+        offset = ctypes.c_size_t()
+        with torch.cuda.device(self.area.device):
+            _lib.check(_lib.lib().d3_ipc_handle(ctypes.c_void_p(self.area.data_ptr()), handle,
+                                                ctypes.byref(offset)), "ipc_handle")
+        handles = [None] * self.world
+        dist.all_gather_object(handles, (bytes(handle), offset.value), group=group)
+        self.bases, ptrs = [], []
+        with torch.cuda.device(self.area.device):
+            for r, (h, off) in enumerate(handles):
+                if r == self.rank:
+                    ptrs.append(self.area.data_ptr())
+                    continue
+                ptr, base = ctypes.c_void_p(), ctypes.c_void_p()
+                _lib.check(_lib.lib().d3_ipc_open(h, off, ctypes.byref(ptr), ctypes.byref(base)), "ipc_open")
+                self.bases.append(base.value)
+                ptrs.append(ptr.value)
+        raw = exchange_struct(ptrs, flags_offset, self.rank, m_max, hidden)
+        self.device_struct = torch.frombuffer(bytearray(raw), dtype=torch.uint8).to(self.area.device)
+        dist.barrier(group=group)
+
+    def close(self):
+        """Collective: unmap the peers' areas once every rank is done with them."""
+        if self.bases is None:
+            return
+        torch.cuda.synchronize(self.area.device)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.area.device):
+            for base in self.bases:
+                _lib.check(_lib.lib().d3_ipc_close(ctypes.c_void_p(base)), "ipc_close")
+        self.bases = None
+        dist.barrier(group=self.group)
 
 
 def expert_range(num_experts, rank, world):
@@ -44,30 +126,42 @@ def sum_in_rank_order(gathered):
 
 class ExpertParallelDecode:
     """The decode of one MoE layer with this rank's experts. `decode_fn(x, ids, weights) -> fp32 [M, H]` replaces
-    the GPU kernel (kernels.moe_decode_ep over `banks`) when given, so the exchange can be exercised on CPU ranks."""
+    the GPU kernel (kernels.moe_decode_ep over `banks`) when given, so the exchange can be exercised on CPU ranks.
+    With `peer` (a PeerExchange) the partials cross NVLink inside the decode kernel instead of an NCCL all-gather."""
 
-    def __init__(self, kind, banks, num_experts, group=None, codebooks=(None, None), decode_fn=None):
+    def __init__(self, kind, banks, num_experts, group=None, codebooks=(None, None), decode_fn=None, peer=None):
         self.kind, self.banks, self.num_experts, self.group = kind, banks, num_experts, group
-        self.codebooks, self.decode_fn = codebooks, decode_fn
+        self.codebooks, self.decode_fn, self.peer = codebooks, decode_fn, peer
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         self.e_first, self.e_count = expert_range(num_experts, self.rank, self.world)
         self.workspace = {}
 
-    def partial(self, x, ids, weights):
-        if self.decode_fn is not None:
-            return self.decode_fn(x, ids, weights)
+    def _workspace(self, x, ids):
         key = (x.device, x.shape[0], ids.shape[-1])
         if key not in self.workspace:
             wkey = kernels._lib.WEIGHT_KEY[self.kind]
             e_local = self.banks[1][wkey].shape[0] // x.shape[1]
             inter = self.banks[0][wkey].shape[0] // (2 * e_local)
             self.workspace[key] = kernels.decode_workspace(x.shape[0], ids.shape[-1], inter, x.device)
+        return self.workspace[key]
+
+    def partial(self, x, ids, weights):
+        if self.decode_fn is not None:
+            return self.decode_fn(x, ids, weights)
         return kernels.moe_decode_ep(self.kind, x, ids, weights, self.banks, self.e_first, self.num_experts,
-                                     self.codebooks, workspace=self.workspace[key])
+                                     self.codebooks, workspace=self._workspace(x, ids))
 
     def __call__(self, x, ids, weights):
         """[M, H] bfloat16, the same on every rank: the whole layer's decode of rows x [M, H] routed to ids [M, k]."""
+        if self.peer is not None:
+            M, H = x.shape
+            if M > self.peer.m_max or H != self.peer.hidden:
+                raise ValueError(f"[{M}, {H}] rows do not fit the peer exchange ({self.peer.m_max}, {self.peer.hidden})")
+            kernels.moe_decode_ep(self.kind, x, ids, weights, self.banks, self.e_first, self.num_experts,
+                                  self.codebooks, workspace=self._workspace(x, ids),
+                                  exchange=self.peer.device_struct)
+            return kernels.ep_reduce(self.peer.device_struct, M, H)
         part = self.partial(x, ids, weights).float().contiguous()
         gathered = torch.empty((self.world * part.shape[0], part.shape[1]), dtype=part.dtype, device=part.device)
         dist.all_gather_into_tensor(gathered, part, group=self.group)

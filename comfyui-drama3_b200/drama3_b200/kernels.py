@@ -265,11 +265,13 @@ def prefill_combine(sorted_out, pos, weights, dtype=torch.bfloat16):
 
 
 def moe_decode_ep(kind, x, ids, weights, banks, e_first, num_experts, codebooks=(None, None), workspace=None,
-                  partial=None):
+                  partial=None, exchange=None):
     """[M, H] float32: moe_decode over this rank's experts only (expert parallelism). `banks` hold experts
     [e_first, e_first + E_local) of the num_experts routed ones (bank expert 0 = expert e_first); pairs routed to other
     ranks' experts are skipped. The result is the routing-weighted sum over this rank's pairs, in rank order;
-    summing the ranks' results and rounding to bf16 gives moe_decode's output."""
+    summing the ranks' results and rounding to bf16 gives moe_decode's output. With `exchange` (the device struct
+    of an ep.PeerExchange) the partial is pushed into every rank's exchange area instead and None is returned;
+    ep_reduce then finishes the layer."""
     fmt = _lib.FORMATS[kind]
     if x.dtype not in (torch.bfloat16, torch.float32):
         raise TypeError(f"moe_decode_ep takes bfloat16 or float32 rows, not {x.dtype}")
@@ -280,7 +282,7 @@ def moe_decode_ep(kind, x, ids, weights, banks, e_first, num_experts, codebooks=
     w13, w2 = gate_up[wkey], down[wkey]
     e_local = w2.shape[0] // H
     I = w13.shape[0] // (2 * e_local)
-    if partial is None:
+    if partial is None and exchange is None:
         partial = torch.empty((M, H), dtype=torch.float32, device=x.device)
     if workspace is None:
         workspace = decode_workspace(M, k, I, x.device)
@@ -292,9 +294,19 @@ def moe_decode_ep(kind, x, ids, weights, banks, e_first, num_experts, codebooks=
                                      int(e_first), e_local, H, I, _ptr(ids), _ptr(weights), _ptr(w13),
                                      _ptr(gate_up["scale"]), _ptr(gate_up.get("s_channel")), _ptr(w2),
                                      _ptr(down["scale"]), _ptr(down.get("s_channel")), _ptr(codebooks[0]),
-                                     _ptr(codebooks[1]), _ptr(partial), _ptr(workspace), workspace.numel(),
-                                     _stream(x.device)), "moe_decode_ep")
+                                     _ptr(codebooks[1]), _ptr(partial), _ptr(exchange), _ptr(workspace),
+                                     workspace.numel(), _stream(x.device)), "moe_decode_ep")
     return partial
+
+
+def ep_reduce(exchange, M, H, out=None):
+    """[M, H] bfloat16: waits (bounded) until every rank has pushed its partial for this call into this rank's
+    exchange area, then sums them in rank order. `exchange` is the device struct of an ep.PeerExchange."""
+    if out is None:
+        out = torch.empty((M, H), dtype=torch.bfloat16, device=exchange.device)
+    with _on(exchange.device):
+        check(lib().d3_ep_reduce(_ptr(exchange), M, H, _ptr(out), _stream(exchange.device)), "ep_reduce")
+    return out
 
 
 def decode_workspace(rows, k, intermediate, device):

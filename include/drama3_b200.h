@@ -54,12 +54,13 @@ int d3_device_check(void);
 
 /* Reads and clears the current device's fault word (synchronous). Bits: D3_FAULT_WAIT (1) a wait timed out,
  * D3_FAULT_EXPERT (2) an expert id out of range, D3_FAULT_SLOT (4) a slot out of range, D3_FAULT_TILES (8) a
- * grouped GEMM given fewer row tiles than its groups need. No counterpart in the reference, whose kernels do not
- * check indices. */
+ * grouped GEMM given fewer row tiles than its groups need, D3_FAULT_EXCHANGE (16) an expert-parallel exchange area
+ * whose geometry does not fit the call. No counterpart in the reference, whose kernels do not check indices. */
 #define D3_FAULT_WAIT 1u
 #define D3_FAULT_EXPERT 2u
 #define D3_FAULT_SLOT 4u
 #define D3_FAULT_TILES 8u
+#define D3_FAULT_EXCHANGE 16u
 int d3_take_fault(unsigned int* fault);
 
 /* Decode routing, `rows` independent rows: ids [rows, k] (int64) and weights [rows, k] (fp32 holding bfloat16
@@ -168,7 +169,24 @@ int d3_moe_decode(int fmt, const void* x, int x_bf16, int M, int k, int E, int H
 int d3_moe_decode_ep(int fmt, const void* x, int x_bf16, int M, int k, int E, int e_first, int e_count, int H, int I,
                      const int64_t* ids, const float* weights, const uint8_t* w13, const void* s13, const float* c13,
                      const uint8_t* w2, const void* s2, const float* c2, const float* codebook13,
-                     const float* codebook2, float* partial, void* workspace, size_t workspace_bytes, void* stream);
+                     const float* codebook2, float* partial, const void* exchange, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/* Expert parallelism over peer memory (NVLink P2P stores, one node, up to 8 ranks): `exchange` (device memory) is
+ * the struct { float* slots[8]; unsigned* flags[8]; unsigned* epoch; int world, rank, m_max, h; } where slots[r] /
+ * flags[r] address rank r's exchange area (d3_ep_exchange_bytes(world, m_max, H) bytes, zeroed: fp32 slots
+ * [2][world][m_max][H], then at the next 256-byte boundary flags [2][8], this rank's call counter and one scratch
+ * word) - the caller's own area for r == rank, the IPC mapping (d3_ipc_open) of the peers' - and epoch the counter
+ * in the caller's area. With it, d3_moe_decode_ep pushes the partial into every rank's area instead of `partial` and
+ * raises this rank's flag there; d3_ep_reduce then waits (bounded; fault bit 1 on timeout) for every rank's flag,
+ * writes out [M, H] bf16 (8-byte aligned, H a multiple of 4) = the partials summed in rank order, and advances the
+ * counter. Every rank makes the same calls in the same order; M <= m_max and H == h, else nothing is exchanged and
+ * D3_FAULT_EXCHANGE is set. No counterpart in the reference (one GPU). */
+size_t d3_ep_exchange_bytes(int world, int m_max, int H);
+int d3_ep_reduce(const void* exchange, int M, int H, void* out, void* stream);
+int d3_ipc_handle(const void* ptr, void* handle /* 64 bytes */, size_t* offset);
+int d3_ipc_open(const void* handle, size_t offset, void** ptr, void** base);
+int d3_ipc_close(void* base);
 
 /* d3_moe_decode without a workspace argument. No counterpart in the reference: it is for callers that cannot
  * allocate device memory themselves, such as a plugin whose host application's memory manager owns every device

@@ -27,3 +27,87 @@ def test_expert_parallel_decode_matches_one_gpu():
     proc = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=400)
     assert proc.returncode == 0, proc.stdout[-2000:] + proc.stderr[-3000:]
     assert "ok=True" in proc.stdout
+
+
+# ---- the peer exchange's kernels on one GPU: ranks emulated by areas in this GPU's memory, their calls issued one
+# after another on one stream (no kernel waits on one still running)
+
+import gpu_data as gd  # noqa: E402
+from drama3_b200 import _lib, ep, kernels  # noqa: E402
+
+E, H, I = 16, 2048, 768
+
+
+def local_exchanges(world, m_max, device):
+    """world exchange areas in this GPU's memory and each emulated rank's device struct over all of them."""
+    size, flags_offset = ep.exchange_layout(world, m_max, H)
+    areas = [torch.zeros((size,), dtype=torch.uint8, device=device) for _ in range(world)]
+    ptrs = [a.data_ptr() for a in areas]
+    structs = [torch.frombuffer(bytearray(ep.exchange_struct(ptrs, flags_offset, r, m_max, H)),
+                                dtype=torch.uint8).to(device) for r in range(world)]
+    return areas, structs
+
+
+@pytest.mark.parametrize("kind", ["fp8c", "w4a8"])
+def test_exchange_one_rank_equals_moe_decode(cuda, kind):
+    """World 1: the partial pushed into the area and reduced is moe_decode's output bit for bit, over calls of both
+    parities and fewer lines than the area holds."""
+    banks = (gd.rand_bank(kind, E, 2 * I, H, 200, cuda), gd.rand_bank(kind, E, H, I, 201, cuda))
+    _, (st,) = local_exchanges(1, 16, cuda)
+    _lib.take_fault()
+    for call, M in enumerate((16, 1, 5, 16)):
+        x = gd.rand_rows(M, H, 210 + call, cuda)
+        ids, w = gd.rand_routing(M, E, 8, 220 + call, cuda)
+        assert kernels.moe_decode_ep(kind, x, ids, w, banks, 0, E, exchange=st) is None
+        got = kernels.ep_reduce(st, M, H)
+        assert torch.equal(got, kernels.moe_decode(kind, x, ids, w, banks)), call
+    assert _lib.take_fault() == 0
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_exchange_ranks_on_one_gpu(cuda, world):
+    """world emulated ranks, each with its block of the experts: every rank's reduce returns the rank-order sum of
+    the partials (the all-gather exchange's result) bit for bit, and the single-GPU decode within 1e-3."""
+    kind = "fp8c"
+    full = (gd.rand_bank(kind, E, 2 * I, H, 230, cuda), gd.rand_bank(kind, E, H, I, 231, cuda))
+    _, structs = local_exchanges(world, 16, cuda)
+    _lib.take_fault()
+    for call, M in enumerate((16, 3, 16)):
+        x = gd.rand_rows(M, H, 240 + call, cuda)
+        ids, w = gd.rand_routing(M, E, 8, 250 + call, cuda)
+        partials = []
+        for r in range(world):
+            first, _ = ep.expert_range(E, r, world)
+            banks = ep.local_banks(full, E, r, world)
+            partials.append(kernels.moe_decode_ep(kind, x, ids, w, banks, first, E))
+            kernels.moe_decode_ep(kind, x, ids, w, banks, first, E, exchange=structs[r])
+        want = ep.sum_in_rank_order(torch.stack(partials)).to(torch.bfloat16)
+        for r in range(world):
+            assert torch.equal(kernels.ep_reduce(structs[r], M, H), want), (call, r)
+        assert gd.rel_l2(want.float(), kernels.moe_decode(kind, x, ids, w, full).float()) <= 1e-3
+    assert _lib.take_fault() == 0
+
+
+def test_exchange_reduce_times_out_without_peer(cuda):
+    """A reduce whose peer never pushes gives up after its wait limit: fault bit 1, zeros out, the context usable."""
+    _, structs = local_exchanges(2, 1, cuda)
+    _lib.take_fault()
+    out = kernels.ep_reduce(structs[0], 1, H, out=torch.full((1, H), 7.0, dtype=torch.bfloat16, device=cuda))
+    torch.cuda.synchronize()
+    assert _lib.take_fault() == 1 and not out.any()
+    assert torch.ones(4, device=cuda).sum().item() == 4
+
+
+def test_exchange_geometry_checked(cuda):
+    """More lines than the area holds: nothing is pushed or awaited, fault bit 16, zeros out."""
+    kind = "fp8c"
+    banks = (gd.rand_bank(kind, E, 2 * I, H, 260, cuda), gd.rand_bank(kind, E, H, I, 261, cuda))
+    areas, (st,) = local_exchanges(1, 2, cuda)
+    x = gd.rand_rows(4, H, 262, cuda)
+    ids, w = gd.rand_routing(4, E, 8, 263, cuda)
+    _lib.take_fault()
+    kernels.moe_decode_ep(kind, x, ids, w, banks, 0, E, exchange=st)
+    out = kernels.ep_reduce(st, 4, H)
+    torch.cuda.synchronize()
+    assert _lib.take_fault() == 16 and not out.any()
+    assert not areas[0][:-256].any()

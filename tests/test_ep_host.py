@@ -24,6 +24,23 @@ def test_expert_range_covers_all_in_order():
         assert max(c for _, c in ranges) - min(c for _, c in ranges) <= 1
 
 
+def test_exchange_struct_layout():
+    """The ctypes mirror of the kernels' exchange struct: its offsets, and the area layout (slots, then the flags and
+    the call counter at the next 256-byte boundary)."""
+    import ctypes
+    S = ep.ExchangeStruct
+    assert ctypes.sizeof(S) == 152 and S.flags.offset == 64 and S.epoch.offset == 128 and S.world.offset == 136
+    assert S.rank.offset == 140 and S.m_max.offset == 144 and S.h.offset == 148
+    size, flags = ep.exchange_layout(2, 3, 2048)
+    assert flags == 2 * 2 * 3 * 2048 * 4 and size == flags + 256
+    raw = ep.exchange_struct([0x1000, 0x200000], flags, 1, 3, 2048)
+    st = S.from_buffer_copy(raw)
+    assert list(st.slots[:2]) == [0x1000, 0x200000] and list(st.flags[:2]) == [0x1000 + flags, 0x200000 + flags]
+    assert st.epoch == 0x200000 + flags + 64 and (st.world, st.rank, st.m_max, st.h) == (2, 1, 3, 2048)
+    with pytest.raises(ValueError):
+        ep.exchange_layout(9, 1, 2048)
+
+
 def _banks():
     rng = np.random.default_rng(11)
     w13 = rng.normal(0, 0.02, size=(E, 2 * I, H)).astype(np.float32)
