@@ -326,10 +326,11 @@ def ep_leg(kernels, device, kind, args, stream, pg):
     peer_layers = [ep.ExpertParallelDecode(kind, lay.banks, E, peer=peer) for lay in layers]
     outs = [None] * n_layers
     timed = {}
-    for name, mods in (("nccl", layers), ("peer", peer_layers)):
-        def step(mods=mods):
+    for name, mods in (("local", layers), ("nccl", layers), ("peer", peer_layers)):
+        def step(mods=mods, local=name == "local"):
             for l_ in range(n_layers):
-                outs[l_] = mods[l_](x, ids[l_], weights[l_])
+                # "local": each rank's decode alone (its fp32 partial, no exchange), the floor of both exchanges
+                outs[l_] = (mods[l_].partial if local else mods[l_])(x, ids[l_], weights[l_])
 
         with torch.cuda.stream(stream):
             graph = capture(step, args.warmup, stream)  # the exchanges are captured with the kernels
@@ -347,10 +348,11 @@ def ep_leg(kernels, device, kind, args, stream, pg):
     return {"tokens_per_s": args.lines / (ms * 1e-3), "ms_per_step": ms, "us_per_layer": 1e3 * ms / n_layers,
             "experts_per_rank": count, "scaling": "strong (one job of `lines` rows over all ranks)",
             "exchange": "fused: each rank's decode kernel stores its fp32 partial into every rank's exchange area "
-                        "over NVLink (P2P), flags with system-scope release, a one-CTA reduce sums in rank order",
+                        "over NVLink (P2P), flags with system-scope release, a small reduce kernel sums in rank order",
             "fault_bits": fault,
             "nccl_all_gather": {"tokens_per_s": args.lines / (timed["nccl"] * 1e-3), "ms_per_step": timed["nccl"],
                                 "us_per_layer": 1e3 * timed["nccl"] / n_layers},
+            "decode_only_us_per_layer": 1e3 * timed["local"] / n_layers,
             "resident_bytes_per_rank": sum(t.nbytes for lay in layers for b in lay.banks for t in b.values())}
 
 

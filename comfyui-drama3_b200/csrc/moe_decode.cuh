@@ -834,35 +834,63 @@ D3_DEV bool mma_phase(const DecodeArgs& a, const DecodePlan& pl, int lo, int hi,
 // CTA's MMA and epilogue warps. valid[p] / w[p]: pair p's id is in range / its routing weight (shared memory). The
 // k parts of an output are loaded together (independent L2 loads), then summed in order.
 D3_DEV void combine_columns(const DecodeArgs& a, const unsigned char* valid, const float* w, int n0, int n1, bool ok) {
-  const int NC = n1 - n0, H = DEC_H;
-  for (int idx = threadIdx.x; idx < a.M * NC; idx += DEC_CONSUMERS + 32) {
-    const int t = idx / NC, n = n0 + idx - t * NC;
-    float acc = 0.0f;
+  // four adjacent columns a thread (n0, n1 multiples of 4): 16-byte loads of the parts and 16-byte stores (peer
+  // stores included)
+  const int NQ = (n1 - n0) >> 2, H = DEC_H;
+  float* dst32 = a.out_f32;
+  size_t slot = 0;
+  int world = 0;
+  if (a.ex) {
+    // this rank's slot in every rank's area (call parity set)
+    const EpExchange& ex = *a.ex;
+    if (ep_geometry_ok(ex, a.M, H)) {
+      const unsigned ep = *(volatile const unsigned*)ex.epoch + 1u;
+      slot = (size_t)((ep & 1u) * ex.world + ex.rank) * ex.m_max * H;
+      world = ex.world;
+    } else if (threadIdx.x == 0) {
+      record_fault(FAULT_EXCHANGE);
+    }
+    dst32 = nullptr;
+  }
+  const bool out8 = ((uintptr_t)a.out & 7u) == 0;
+  for (int idx = threadIdx.x; idx < a.M * NQ; idx += DEC_CONSUMERS + 32) {
+    const int t = idx / NQ, n = n0 + 4 * (idx - t * NQ);
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     for (int j0 = 0; j0 < a.k; j0 += 8) {
-      float v[8];
+      float4 v[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         const int p = t * a.k + j0 + u;
-        v[u] = (ok && j0 + u < a.k && valid[p]) ? __ldcg(a.parts + (size_t)p * H + n) : 0.0f;
+        v[u] = (ok && j0 + u < a.k && valid[p]) ? __ldcg(reinterpret_cast<const float4*>(a.parts + (size_t)p * H + n))
+                                                 : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       }
 #pragma unroll
       for (int u = 0; u < 8; ++u)
-        if (j0 + u < a.k) acc = __fmaf_rn(v[u], w[t * a.k + j0 + u], acc);
+        if (j0 + u < a.k) {
+          const float wt = w[t * a.k + j0 + u];
+          acc.x = __fmaf_rn(v[u].x, wt, acc.x);
+          acc.y = __fmaf_rn(v[u].y, wt, acc.y);
+          acc.z = __fmaf_rn(v[u].z, wt, acc.z);
+          acc.w = __fmaf_rn(v[u].w, wt, acc.w);
+        }
     }
     if (a.ex) {
-      // this rank's slot in every rank's area (call parity set)
-      const EpExchange& ex = *a.ex;
-      if (ep_geometry_ok(ex, a.M, H)) {
-        const unsigned ep = *(volatile const unsigned*)ex.epoch + 1u;
-        const size_t off = ((size_t)((ep & 1u) * ex.world + ex.rank) * ex.m_max + t) * H + n;
-        for (int r = 0; r < ex.world; ++r) ex.slots[r][off] = acc;
-      } else if (t == 0 && n == n0) {
-        record_fault(FAULT_EXCHANGE);
-      }
-    } else if (a.out_f32) {
-      a.out_f32[(size_t)t * H + n] = acc;
+      for (int r = 0; r < world; ++r)
+        *reinterpret_cast<float4*>(a.ex->slots[r] + slot + (size_t)t * H + n) = acc;
+    } else if (dst32) {
+      *reinterpret_cast<float4*>(dst32 + (size_t)t * H + n) = acc;
     } else {
-      a.out[(size_t)t * H + n] = f32_to_bf16(acc);
+      uint16_t* o = a.out + (size_t)t * H + n;
+      const uint16_t b0 = f32_to_bf16(acc.x), b1 = f32_to_bf16(acc.y), b2 = f32_to_bf16(acc.z),
+                     b3 = f32_to_bf16(acc.w);
+      if (out8) {
+        *reinterpret_cast<uint2*>(o) = make_uint2((uint32_t)b0 | ((uint32_t)b1 << 16), (uint32_t)b2 | ((uint32_t)b3 << 16));
+      } else {
+        o[0] = b0;
+        o[1] = b1;
+        o[2] = b2;
+        o[3] = b3;
+      }
     }
   }
 }
@@ -1100,9 +1128,9 @@ __global__ void __launch_bounds__(DEC_ALL, 1) moe_decode_kernel(const DecodeArgs
   if (!grouped) {
     // grid-wide: every CTA's parts are written; each CTA combines an even share of the columns
     ok = grid_barrier(a.barrier, G) && ok;
-    int n0, n1;
-    split_range(H, blockIdx.x, G, n0, n1);
-    combine_columns(a, c_ok, c_w, n0, n1, ok);
+    int q0, q1;
+    split_range(H / 4, blockIdx.x, G, q0, q1);
+    combine_columns(a, c_ok, c_w, 4 * q0, 4 * q1, ok);
   } else {
     // group mode: the CTA that completes a 64-column block (its counter reaching nseg * 64 finished down rows) sums
     // that block; no second wait
@@ -1138,11 +1166,12 @@ __global__ void __launch_bounds__(DEC_ALL, 1) moe_decode_kernel(const DecodeArgs
   if (a.ex) {
     // exchange: once every column block of this rank's partial has been pushed, raise this rank's flag on every rank
     // (grid mode: every CTA pushed its share of the columns; group mode: the CTAs that completed blocks pushed them)
-    __threadfence_system();  // this thread's pushes, before the count that releases them
-    named_sync(2, DEC_CONSUMERS + 32);
+    named_sync(2, DEC_CONSUMERS + 32);  // this CTA's pushes are issued
     if (tid == 0 && ep_geometry_ok(*a.ex, a.M, H)) {
       const unsigned share = grouped ? (unsigned)s_nblk : 1u, total = grouped ? (unsigned)(H / DEC_CB) : (unsigned)G;
       if (share > 0) {
+        // one system-scope fence for the CTA: the barrier orders its threads' pushes before it, and it orders them
+        // before the count that releases them (the pattern of a grid barrier, at system scope)
         __threadfence_system();
         if (atomicAdd(a.ep_done, share) + share == total) {
           const EpExchange& ex = *a.ex;

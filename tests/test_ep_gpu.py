@@ -53,7 +53,7 @@ def test_exchange_one_rank_equals_moe_decode(cuda, kind):
     """World 1: the partial pushed into the area and reduced is moe_decode's output bit for bit, over calls of both
     parities and fewer lines than the area holds."""
     banks = (gd.rand_bank(kind, E, 2 * I, H, 200, cuda), gd.rand_bank(kind, E, H, I, 201, cuda))
-    _, (st,) = local_exchanges(1, 16, cuda)
+    areas, (st,) = local_exchanges(1, 16, cuda)  # the areas stay referenced while the structs point at them
     _lib.take_fault()
     for call, M in enumerate((16, 1, 5, 16)):
         x = gd.rand_rows(M, H, 210 + call, cuda)
@@ -70,14 +70,14 @@ def test_exchange_ranks_on_one_gpu(cuda, world):
     the partials (the all-gather exchange's result) bit for bit, and the single-GPU decode within 1e-3."""
     kind = "fp8c"
     full = (gd.rand_bank(kind, E, 2 * I, H, 230, cuda), gd.rand_bank(kind, E, H, I, 231, cuda))
-    _, structs = local_exchanges(world, 16, cuda)
+    areas, structs = local_exchanges(world, 16, cuda)  # kept referenced while the structs point at them
     _lib.take_fault()
     for call, M in enumerate((16, 3, 16)):
         x = gd.rand_rows(M, H, 240 + call, cuda)
         ids, w = gd.rand_routing(M, E, 8, 250 + call, cuda)
         partials = []
         for r in range(world):
-            first, _ = ep.expert_range(E, r, world)
+            first = ep.expert_range(E, r, world)[0]
             banks = ep.local_banks(full, E, r, world)
             partials.append(kernels.moe_decode_ep(kind, x, ids, w, banks, first, E))
             kernels.moe_decode_ep(kind, x, ids, w, banks, first, E, exchange=structs[r])
@@ -90,7 +90,7 @@ def test_exchange_ranks_on_one_gpu(cuda, world):
 
 def test_exchange_reduce_times_out_without_peer(cuda):
     """A reduce whose peer never pushes gives up after its wait limit: fault bit 1, zeros out, the context usable."""
-    _, structs = local_exchanges(2, 1, cuda)
+    areas, structs = local_exchanges(2, 1, cuda)
     _lib.take_fault()
     out = kernels.ep_reduce(structs[0], 1, H, out=torch.full((1, H), 7.0, dtype=torch.bfloat16, device=cuda))
     torch.cuda.synchronize()
