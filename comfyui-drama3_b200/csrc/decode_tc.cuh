@@ -1,0 +1,509 @@
+// The routed-expert decode of M <= 16 lines on the 5th-generation tensor cores, for e4m3 rows with per-output-channel
+// fp32 scales (the fp8c layout). Same plan, phases, scratch and combine as moe_decode_kernel; what changes is how a
+// weight byte meets the activations:
+//
+//   * the e4m3 weight tiles go from HBM to shared memory by TMA and straight into tcgen05.mma kind::f8f6f4 as the A
+//     operand - no conversion, no register fragments;
+//   * the activations become the B operand as a sum of e4m3 terms: y = x * 2^e (e per row, so that max|y| lies in
+//     [128, 256)), t1 = e4m3(y), t2 = e4m3(y - t1), ... Each term is exact in fp32 and every product of two e4m3
+//     numbers is exact, so D = W t1 + W t2 + ... is the fp32 dot product with y rounded to the terms' precision:
+//     2 terms hold a bf16 value exactly (8 significant bits, 4 per term) and 3 / 4 terms keep 12 / 16 bits of an
+//     fp32 one. The terms sit side by side along N, so one MMA computes all of them;
+//   * the accumulators live in TMEM (two buffers, so a tile's epilogue overlaps the next tile's MMAs).
+//
+// Phase 1 (gate_up + SwiGLU): a tile is 64 gate rows and the matching 64 up rows of one expert (M = 128) over all H
+// columns; B holds every line's terms (N = 16 lines x terms), staged once per call, so a segment needs no staging of
+// its own - the epilogue picks the columns of the segment's lines. Phase 2 (down): a tile is 128 down rows over all I
+// columns; B holds the segment's pairs' a1 rows (N = 16 pairs x 4 terms), two segments' worth, staged after the grid
+// barrier. The work of each phase is split across the grid by whole tiles.
+//
+// Roles (8 warps): warp 0 lane 0 issues the TMA loads, warp 1 owns TMEM and lane 0 issues the MMAs, warps 2-5 are
+// the TMEM epilogue (one warp per lane quarter), warps 2-7 stage the B operands and run the combine.
+#pragma once
+#include "grouped_mma.cuh"
+#include "moe_decode.cuh"
+
+namespace d3 {
+
+constexpr int TC_WARPS = 8;
+constexpr int TC_THREADS = TC_WARPS * 32;
+constexpr int TC_HELP0 = 64;          // first helper thread (warp 2)
+constexpr int TC_HELPERS = 192;       // warps 2-7
+constexpr int TC_EPI = 128;           // warps 2-5
+constexpr int TC_STAGES = 6;          // A ring depth
+constexpr int TC_ABYTES = 16384;      // one A stage: 128 rows x 128 bytes
+constexpr int TC_U1 = 64;             // phase-1 units (a gate row and its up row) per tile
+constexpr int TC_R2 = 128;            // phase-2 rows per tile
+constexpr int TC_LINES = 16;          // phase-1 B rows per term: the (at most 16) lines
+constexpr int TC_CAP = 16;            // pairs per segment
+constexpr int TC_TERMS2 = 4;          // phase-2 terms (a1 is fp32)
+constexpr int TC_N2 = TC_CAP * TC_TERMS2;
+constexpr int TC_BREGION = 98304;     // phase-1 B (<= 48 rows x 2048) or two phase-2 B buffers (64 rows x <= 768)
+constexpr int TC_XPITCH = 17;         // exchange row pitch (floats)
+constexpr int TC_TMEM_COLS = 128;     // two accumulators of <= 64 columns
+
+struct TcSmem {
+  static constexpr int ring = 0;
+  static constexpr int breg = ring + TC_STAGES * TC_ABYTES;
+  static constexpr int xchg = breg + TC_BREGION;                       // float [128][17]
+  static constexpr int bars = xchg + 128 * TC_XPITCH * 4;              // 19 mbarriers
+  static constexpr int tmem = bars + 24 * 8;
+  static constexpr int linv = tmem + 16;                               // float [16]: phase-1 line scales
+  static constexpr int lmax = linv + 64;                               // int [16]
+  static constexpr int spair = lmax + 64;                              // int [2][16]: phase-2 B rows' pairs
+  static constexpr int sinv = spair + 128;                             // float [2][16]
+  static constexpr int smax = sinv + 128;                              // int [2][16]
+  static constexpr int end = smax + 128;
+  static constexpr int launch = end + 1024;                            // + alignment slack
+};
+
+// Instruction descriptor, kind::f8f6f4: f32 accumulator, e4m3 A and B, both K-major, M = 128, N = n.
+D3_DEV uint32_t tc_idesc(int n) { return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24); }
+
+D3_DEV void umma_f8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 2-D tiled TMA load with an L2 cache hint.
+D3_DEV void tma_load_2d_hint(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
+      "%3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"((uint64_t)map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// Two fp32 -> packed e4m3 x2 (round to nearest even, saturating): `lo` in the low byte.
+D3_DEV uint32_t f32x2_e4m3(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// Packed e4m3 x2 -> the two values as fp32 (exact).
+D3_DEV float2 e4m3x2_f32(uint32_t v) {
+  uint32_t h;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"((uint16_t)v));
+  return __half22float2(*reinterpret_cast<const __half2*>(&h));
+}
+
+// Byte offset of (row n, 16-byte chunk q of the K bytes) in a K-major, 128-byte-swizzled operand of `rows` rows:
+// 128-column blocks of rows x 128 bytes, 8-row atoms of 1024 bytes, chunk index XOR (row % 8).
+D3_DEV uint32_t tc_b_offset(int rows, int n, int q) {
+  return (uint32_t)((q >> 3) * rows * 128 + (n >> 3) * 1024 + (n & 7) * 128 + (((q & 7) ^ (n & 7)) << 4));
+}
+
+// Power-of-two scale for a row of maximum magnitude m: m * 2^e in [128, 256) (1 for an all-zero row).
+D3_DEV int tc_exponent(float m) {
+  if (!(m > 0.0f) || !(m < 3.0e38f)) return 0;
+  const int ex = (int)((__float_as_uint(m) >> 23) & 0xFF) - 127;
+  return min(100, max(-100, 7 - ex));
+}
+
+// 16 consecutive values of a row as `terms` e4m3 terms of y = v * scale, written as 16-byte chunks: term t of the
+// row goes to B row t * tstride + n.
+template <int TERMS>
+D3_DEV void tc_write_terms(uint8_t* b, int rows, int n, int tstride, int q, const float (&v)[16], float scale) {
+  float y[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) y[i] = v[i] * scale;
+#pragma unroll
+  for (int t = 0; t < TERMS; ++t) {
+    uint32_t w[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const uint32_t lo = f32x2_e4m3(y[4 * p], y[4 * p + 1]), hi = f32x2_e4m3(y[4 * p + 2], y[4 * p + 3]);
+      w[p] = lo | (hi << 16);
+      if (t + 1 < TERMS) {
+        const float2 a = e4m3x2_f32(lo), c = e4m3x2_f32(hi);
+        y[4 * p] -= a.x;
+        y[4 * p + 1] -= a.y;
+        y[4 * p + 2] -= c.x;
+        y[4 * p + 3] -= c.y;
+      }
+    }
+    *reinterpret_cast<uint4*>(b + tc_b_offset(rows, t * tstride + n, q)) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+D3_DEV void tc_load16(const void* src, bool bf16, size_t i, float (&v)[16]) {
+  if (bf16) {
+    const uint4* p = reinterpret_cast<const uint4*>((const uint16_t*)src + i);
+    const uint4 a = __ldcg(p), b = __ldcg(p + 1);
+    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      v[2 * u] = bf16_to_f32(w[u] & 0xFFFFu);
+      v[2 * u + 1] = bf16_to_f32(w[u] >> 16);
+    }
+  } else {
+    const float4* p = reinterpret_cast<const float4*>((const float*)src + i);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float4 f = __ldcg(p + u);
+      v[4 * u] = f.x;
+      v[4 * u + 1] = f.y;
+      v[4 * u + 2] = f.z;
+      v[4 * u + 3] = f.w;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+template <bool XBF, int NKB2>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    moe_decode_tc_kernel(const __grid_constant__ CUtensorMap map13, const __grid_constant__ CUtensorMap map2,
+                         const DecodeArgs a) {
+  constexpr int T1 = XBF ? 2 : 3;           // phase-1 terms
+  constexpr int N1 = TC_LINES * T1;         // 32 / 48
+  constexpr int H = DEC_H, NKB1 = H / 128;  // 16 column blocks in phase 1
+  constexpr int I = NKB2 * 128;
+  constexpr int TPS1 = I / TC_U1, TPS2 = H / TC_R2;
+  constexpr int B2BYTES = TC_N2 * I;        // one phase-2 B buffer
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint8_t* ring = smem + TcSmem::ring;
+  uint8_t* breg = smem + TcSmem::breg;
+  float* xchg = (float*)(smem + TcSmem::xchg);
+  uint64_t* bars = (uint64_t*)(smem + TcSmem::bars);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + TC_STAGES;
+  uint64_t* acc_full = bars + 2 * TC_STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* b1_full = acc_empty + 2;
+  uint64_t* b2_full = b1_full + 1;
+  uint32_t* tmem_slot = (uint32_t*)(smem + TcSmem::tmem);
+  float* linv = (float*)(smem + TcSmem::linv);
+  int* lmax = (int*)(smem + TcSmem::lmax);
+  int* spair = (int*)(smem + TcSmem::spair);
+  float* sinv = (float*)(smem + TcSmem::sinv);
+  int* smax = (int*)(smem + TcSmem::smax);
+  __shared__ DecodePlan pl;
+  __shared__ float c_w[DEC_MAX_PAIRS];
+  __shared__ unsigned char c_ok[DEC_MAX_PAIRS];
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int P = a.M * a.k, G = gridDim.x;
+  if (tid == 0) {
+    for (int s = 0; s < TC_STAGES; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(acc_full + s, 1);
+      mbar_init(acc_empty + s, 4);
+      mbar_init(b2_full + s, 1);
+    }
+    mbar_init(b1_full, 1);
+    fence_mbar_init();
+  }
+  if (tid < 16) lmax[tid] = 0;
+  if (tid < 32) smax[tid] = 0;
+  if (warp == 1) tmem_alloc(tmem_slot, TC_TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // programmatic dependent launch: inputs and the workspace are touched only after the previous grid has completed
+  allow_dependents();
+  grid_dependency_wait();
+  build_plan<TC_THREADS>(pl, a.ids, P, a.E, TC_CAP, a.e_first, a.e_count);
+  if (tid < P) {
+    const long long id = a.ids[tid];
+    c_ok[tid] = id >= a.e_first && id < (long long)a.e_first + a.e_count && id < a.E;
+    c_w[tid] = a.weights[tid];
+  }
+  const int nseg = pl.nseg;
+  const int t1_lo = (int)((long long)blockIdx.x * nseg * TPS1 / G);
+  const int t1_hi = (int)((long long)(blockIdx.x + 1) * nseg * TPS1 / G);
+  const int t2_lo = (int)((long long)blockIdx.x * nseg * TPS2 / G);
+  const int t2_hi = (int)((long long)(blockIdx.x + 1) * nseg * TPS2 / G);
+  // phase-2 segments of this CTA: at most two (its range is at most TPS2 tiles when nseg <= G, which the host checks)
+  const int s2a = t2_lo / TPS2, s2n = t2_hi > t2_lo ? (t2_hi - 1) / TPS2 - s2a + 1 : 0;
+  bool ok = true;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      int c = 0;
+      for (int t = t1_lo; t < t1_hi && ok; ++t) {
+        const int s = t / TPS1, ub = t - s * TPS1, e = pl.seg_expert[s];
+        const int grow = e * 2 * I + ub * TC_U1;
+        for (int kb = 0; kb < NKB1; ++kb, ++c) {
+          const int st = c % TC_STAGES;
+          ok = mbar_wait(empty + st, ((c / TC_STAGES) & 1) ^ 1);
+          if (!ok) break;
+          mbar_arrive_expect_tx(full + st, TC_ABYTES);
+          tma_load_2d_hint(ring + st * TC_ABYTES, &map13, kb * 128, grow, full + st, pol);
+          tma_load_2d_hint(ring + st * TC_ABYTES + TC_ABYTES / 2, &map13, kb * 128, grow + I, full + st, pol);
+        }
+      }
+      for (int t = t2_lo; t < t2_hi && ok; ++t) {
+        const int s = t / TPS2, rb = t - s * TPS2, e = pl.seg_expert[s];
+        const int row = e * H + rb * TC_R2;
+        for (int kb = 0; kb < NKB2; ++kb, ++c) {
+          const int st = c % TC_STAGES;
+          ok = mbar_wait(empty + st, ((c / TC_STAGES) & 1) ^ 1);
+          if (!ok) break;
+          mbar_arrive_expect_tx(full + st, TC_ABYTES);
+          tma_load_2d_hint(ring + st * TC_ABYTES, &map2, kb * 128, row, full + st, pol);
+        }
+      }
+      // every issued copy lands before this thread leaves (bounded)
+      for (int d = max(0, c - TC_STAGES); d < c; ++d)
+        if (!mbar_wait(full + d % TC_STAGES, (d / TC_STAGES) & 1)) break;
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t ring_s = smem_u32(ring), b_s = smem_u32(breg);
+      const uint32_t id1 = tc_idesc(N1), id2 = tc_idesc(TC_N2);
+      int c = 0, tn = 0;
+      if (t1_hi > t1_lo) ok = mbar_wait(b1_full, 0);
+      tc_fence_after();
+      for (int t = t1_lo; t < t1_hi && ok; ++t, ++tn) {
+        const int buf = tn & 1;
+        ok = mbar_wait(acc_empty + buf, ((tn >> 1) & 1) ^ 1);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t d = tmem + buf * 64;
+        for (int kb = 0; kb < NKB1; ++kb, ++c) {
+          const int st = c % TC_STAGES;
+          ok = mbar_wait(full + st, (c / TC_STAGES) & 1);
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            umma_f8(d, umma_desc_sw128(ring_s + st * TC_ABYTES + 32 * ks),
+                    umma_desc_sw128(b_s + kb * N1 * 128 + 32 * ks), id1, (kb | ks) != 0 ? 1u : 0u);
+          umma_commit(empty + st);
+        }
+        umma_commit(acc_full + buf);
+      }
+      int cur = -1;
+      for (int t = t2_lo; t < t2_hi && ok; ++t, ++tn) {
+        const int s = t / TPS2, bb = s - s2a;
+        if (s != cur) {
+          if (bb > 1) {
+            record_fault(FAULT_WAIT_TIMEOUT);
+            ok = false;
+            break;
+          }
+          ok = mbar_wait(b2_full + bb, 0);
+          if (!ok) break;
+          tc_fence_after();
+          cur = s;
+        }
+        const int buf = tn & 1;
+        ok = mbar_wait(acc_empty + buf, ((tn >> 1) & 1) ^ 1);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t d = tmem + buf * 64;
+        for (int kb = 0; kb < NKB2; ++kb, ++c) {
+          const int st = c % TC_STAGES;
+          ok = mbar_wait(full + st, (c / TC_STAGES) & 1);
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            umma_f8(d, umma_desc_sw128(ring_s + st * TC_ABYTES + 32 * ks),
+                    umma_desc_sw128(b_s + bb * B2BYTES + kb * TC_N2 * 128 + 32 * ks), id2,
+                    (kb | ks) != 0 ? 1u : 0u);
+          umma_commit(empty + st);
+        }
+        umma_commit(acc_full + buf);
+      }
+    }
+  } else {
+    // ---------------- helpers: staging, epilogue, barriers ----------------
+    const int hid = tid - TC_HELP0;
+    // phase-1 B: every line's terms (rows >= M are zero)
+    if (t1_hi > t1_lo) {
+      for (int it = hid; it < TC_LINES * (H / 16); it += TC_HELPERS) {
+        const int n = it / (H / 16), q = it - n * (H / 16);
+        if (n < a.M) {
+          float v[16];
+          tc_load16(a.x, a.x_bf16 != 0, (size_t)n * H + 16 * q, v);
+          float m = 0.0f;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(v[i]));
+          atomicMax(lmax + n, __float_as_int(m));
+        }
+      }
+      named_sync(1, TC_HELPERS);
+      for (int it = hid; it < TC_LINES * (H / 16); it += TC_HELPERS) {
+        const int n = it / (H / 16), q = it - n * (H / 16);
+        float v[16];
+        if (n < a.M) {
+          tc_load16(a.x, a.x_bf16 != 0, (size_t)n * H + 16 * q, v);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] = 0.0f;
+        }
+        const int e = tc_exponent(__int_as_float(lmax[n]));
+        tc_write_terms<T1>(breg, N1, n, TC_LINES, q, v, __uint_as_float((uint32_t)(e + 127) << 23));
+        if (q == 0) linv[n] = __uint_as_float((uint32_t)(127 - e) << 23);
+      }
+      fence_async_smem();
+      named_sync(1, TC_HELPERS);
+      if (hid == 0) mbar_arrive(b1_full);
+    }
+    int tn = 0;
+    if (warp < 6) {
+      // phase-1 epilogue: per tile, every line's gate / up sums, then SwiGLU for the segment's pairs
+      const int quarter = warp & 3, row = 32 * quarter + lane;
+      const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
+      for (int t = t1_lo; t < t1_hi; ++t, ++tn) {
+        const int buf = tn & 1;
+        if (ok) ok = mbar_wait(acc_full + buf, (tn >> 1) & 1);
+        ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective: the warp agrees
+        tc_fence_after();
+        float v[N1];
+        if (ok) {
+#pragma unroll
+          for (int cb = 0; cb < N1 / 16; ++cb) tmem_ld16(tmem + lane_base + buf * 64 + 16 * cb, (float(&)[16])v[16 * cb]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty + buf);
+#pragma unroll
+        for (int l = 0; l < TC_LINES; ++l) {
+          float sum = v[l];
+#pragma unroll
+          for (int tt = 1; tt < T1; ++tt) sum += v[tt * TC_LINES + l];
+          xchg[row * TC_XPITCH + l] = ok ? sum : 0.0f;
+        }
+        named_sync(3, TC_EPI);
+        if (row < TC_U1) {
+          const int s = t / TPS1, ub = t - s * TPS1, e = pl.seg_expert[s];
+          const int i = ub * TC_U1 + row;
+          const float gsc = __ldg((const float*)a.s13 + (size_t)e * 2 * I + i);
+          const float usc = __ldg((const float*)a.s13 + (size_t)e * 2 * I + I + i);
+          const int first = pl.seg_first[s], cnt = pl.seg_count[s];
+          for (int j = 0; j < cnt; ++j) {
+            const int pair = pl.sorted[first + j], line = pair / a.k;
+            const float sl = linv[line];
+            a.a1[(size_t)pair * I + i] = swiglu_fast(xchg[row * TC_XPITCH + line] * (gsc * sl),
+                                                     xchg[(row + TC_U1) * TC_XPITCH + line] * (usc * sl));
+          }
+        }
+        named_sync(3, TC_EPI);
+      }
+    }
+    // every CTA's a1 is written
+    ok = grid_barrier<TC_HELPERS, TC_HELP0>(a.barrier, G) && ok;
+    // phase-2 B: the pairs of this CTA's (at most two) segments, 4 terms each
+    if (s2n > 0) {
+      const int items = 2 * TC_CAP * (I / 16);
+      for (int it = hid; it < items; it += TC_HELPERS) {
+        const int bj = it / (I / 16), q = it - bj * (I / 16), bb = bj / TC_CAP, j = bj - bb * TC_CAP;
+        if (bb < s2n && j < pl.seg_count[s2a + bb]) {
+          const int pair = pl.sorted[pl.seg_first[s2a + bb] + j];
+          float v[16];
+          tc_load16(a.a1, false, (size_t)pair * I + 16 * q, v);
+          float m = 0.0f;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(v[i]));
+          atomicMax(smax + bj, __float_as_int(m));
+        }
+      }
+      named_sync(1, TC_HELPERS);
+      for (int it = hid; it < items; it += TC_HELPERS) {
+        const int bj = it / (I / 16), q = it - bj * (I / 16), bb = bj / TC_CAP, j = bj - bb * TC_CAP;
+        if (bb >= s2n) continue;
+        const bool live = j < pl.seg_count[s2a + bb];
+        const int pair = live ? pl.sorted[pl.seg_first[s2a + bb] + j] : 0;
+        float v[16];
+        if (live) {
+          tc_load16(a.a1, false, (size_t)pair * I + 16 * q, v);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] = 0.0f;
+        }
+        const int e = tc_exponent(__int_as_float(smax[bj]));
+        tc_write_terms<TC_TERMS2>(breg + bb * B2BYTES, TC_N2, j, TC_CAP, q, v,
+                                  __uint_as_float((uint32_t)(e + 127) << 23));
+        if (q == 0) {
+          spair[bj] = pair;
+          sinv[bj] = __uint_as_float((uint32_t)(127 - e) << 23);
+        }
+      }
+      fence_async_smem();
+      named_sync(1, TC_HELPERS);
+      if (hid == 0)
+        for (int bb = 0; bb < s2n && bb < 2; ++bb) mbar_arrive(b2_full + bb);
+    }
+    if (warp < 6) {
+      // phase-2 epilogue: parts[pair, row] = the pair's terms summed x row scale x 2^-e
+      const int quarter = warp & 3;
+      const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
+      for (int t = t2_lo; t < t2_hi; ++t, ++tn) {
+        const int buf = tn & 1;
+        if (ok) ok = mbar_wait(acc_full + buf, (tn >> 1) & 1);
+        ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective: the warp agrees
+        tc_fence_after();
+        float v[TC_N2];
+        if (ok) {
+#pragma unroll
+          for (int cb = 0; cb < TC_N2 / 16; ++cb)
+            tmem_ld16(tmem + lane_base + buf * 64 + 16 * cb, (float(&)[16])v[16 * cb]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty + buf);
+        if (!ok) continue;
+        const int s = t / TPS2, rb = t - s * TPS2, bb = s - s2a, e = pl.seg_expert[s];
+        if (bb > 1) continue;
+        const int r = rb * TC_R2 + 32 * quarter + lane;
+        const float sc = __ldg((const float*)a.s2 + (size_t)e * H + r);
+        const int cnt = pl.seg_count[s];
+#pragma unroll
+        for (int j = 0; j < TC_CAP; ++j) {
+          if (j < cnt) {
+            float sum = v[j];
+#pragma unroll
+            for (int tt = 1; tt < TC_TERMS2; ++tt) sum += v[tt * TC_CAP + j];
+            __stcg(a.parts + (size_t)spair[bb * TC_CAP + j] * H + r, sum * (sc * sinv[bb * TC_CAP + j]));
+          }
+        }
+      }
+    }
+    // every CTA's parts are written; each CTA combines an even share of the columns
+    ok = grid_barrier<TC_HELPERS, TC_HELP0>(a.barrier, G) && ok;
+    int q0, q1;
+    split_range(H / 4, blockIdx.x, G, q0, q1);
+    combine_columns(a, c_ok, c_w, 4 * q0, 4 * q1, ok, TC_HELP0, TC_HELPERS);
+    if (a.ex) {
+      // exchange: once every CTA has pushed its columns, raise this rank's flag on every rank
+      named_sync(2, TC_HELPERS);
+      if (tid == TC_HELP0 && ep_geometry_ok(*a.ex, a.M, H)) {
+        __threadfence_system();
+        if (atomicAdd(a.ep_done, 1u) + 1u == (unsigned)G) {
+          const EpExchange& ex = *a.ex;
+          const unsigned ep = *(volatile const unsigned*)ex.epoch + 1u;
+          __threadfence_system();
+          for (int r = 0; r < ex.world; ++r) {
+            unsigned* f = ex.flags[r] + (ep & 1u) * EP_MAX_RANKS + ex.rank;
+            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(ep) : "memory");
+          }
+          *a.ep_done = 0u;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TC_TMEM_COLS);
+  }
+}
+
+}  // namespace d3

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -14,6 +15,7 @@
 #include "gemv.cuh"
 #include "grouped_mma.cuh"
 #include "moe_decode.cuh"
+#include "decode_tc.cuh"
 #include "resolve.cuh"
 #include "rotate.cuh"
 #include "route.cuh"
@@ -101,7 +103,8 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 
 // A 2-D byte tensor [rows, row_bytes] read in boxes of box_bytes x 128 rows, with the shared-memory swizzle of that
 // row width (128, 64 or 32 bytes).
-bool byte_tile_map(CUtensorMap* map, const void* base, uint64_t row_bytes, uint64_t rows, uint32_t box_bytes) {
+bool byte_tile_map(CUtensorMap* map, const void* base, uint64_t row_bytes, uint64_t rows, uint32_t box_bytes,
+                   uint32_t box_rows = 128) {
   const CUtensorMapSwizzle swizzle = box_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
                                      : box_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
                                      : box_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
@@ -110,7 +113,7 @@ bool byte_tile_map(CUtensorMap* map, const void* base, uint64_t row_bytes, uint6
   if (!fn) return false;
   cuuint64_t dims[2] = {row_bytes, rows};
   cuuint64_t strides[1] = {row_bytes};
-  cuuint32_t box[2] = {box_bytes, 128};
+  cuuint32_t box[2] = {box_bytes, box_rows};
   cuuint32_t elem[2] = {1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, elem,
             CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -450,6 +453,34 @@ static int decode_nkc(const d3::DecodeArgs& a, const DeviceInfo& d, cudaStream_t
   }
 }
 
+// The tensor-core decode (per-channel e4m3 rows, >= 8 lines): on unless D3_DECODE_TC=0 in the environment at the
+// call (kept for comparing the two kernels on the same inputs).
+static bool decode_tc_enabled() {
+  const char* v = getenv("D3_DECODE_TC");
+  return !(v && v[0] == '0');
+}
+
+template <bool XBF, int NKB2>
+static int decode_tc_launch(const d3::DecodeArgs& a, const CUtensorMap& m13, const CUtensorMap& m2,
+                            const DeviceInfo& d, cudaStream_t s) {
+  auto kern = d3::moe_decode_tc_kernel<XBF, NKB2>;
+  const int smem = d3::TcSmem::launch;
+  if (int st = allow_smem(kern, smem)) return st;
+  return launch(kern, dim3(d.sms), dim3(d3::TC_THREADS), smem, s, true, m13, m2, a);
+}
+
+static int decode_tc(const d3::DecodeArgs& a, const DeviceInfo& d, cudaStream_t s) {
+  CUtensorMap m13, m2;
+  // gate_up rows [e_count * 2I, H] in boxes of 64 rows x 128 bytes; down rows [e_count * H, I] in 128 x 128
+  if (!byte_tile_map(&m13, a.w13, (uint64_t)a.H, (uint64_t)a.e_count * 2 * a.I, 128, 64)) return D3_ERR_ARG;
+  if (!byte_tile_map(&m2, a.w2, (uint64_t)a.I, (uint64_t)a.e_count * a.H, 128, 128)) return D3_ERR_ARG;
+  switch (a.I) {
+    case 512: return a.x_bf16 ? decode_tc_launch<true, 4>(a, m13, m2, d, s) : decode_tc_launch<false, 4>(a, m13, m2, d, s);
+    case 768: return a.x_bf16 ? decode_tc_launch<true, 6>(a, m13, m2, d, s) : decode_tc_launch<false, 6>(a, m13, m2, d, s);
+    default: return D3_ERR_ARG;
+  }
+}
+
 static int decode_common(int fmt, const void* x, int x_bf16, int M, int k, int E, int e_first, int e_count, int H,
                          int I, const int64_t* ids, const float* weights, const uint8_t* w13, const void* s13,
                          const float* c13, const uint8_t* w2, const void* s2, const float* c2,
@@ -483,6 +514,9 @@ static int decode_common(int fmt, const void* x, int x_bf16, int M, int k, int E
                       out, out_f32, e_first, e_count, (const d3::EpExchange*)exchange, words + 4, a1, parts, barrier,
                       words + 16, words + 128, words + 384, 0, 0, cap};
   cudaStream_t s = (cudaStream_t)stream;
+  // per-channel e4m3 with enough lines to fill the grid: the tensor-core kernel (its phase-2 split needs one CTA per
+  // segment at least: at most M * k <= 128 segments)
+  if (fmt == d3::FMT_FP8C && M >= 8 && d.sms >= d3::DEC_MAX_PAIRS && decode_tc_enabled()) return decode_tc(a, d, s);
   switch (fmt) {
     case d3::FMT_FP8:
       return x_bf16 ? decode_nkc<d3::FMT_FP8, true>(a, d, s) : decode_nkc<d3::FMT_FP8, false>(a, d, s);

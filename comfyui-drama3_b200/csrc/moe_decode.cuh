@@ -39,15 +39,19 @@
 namespace d3 {
 
 #ifdef D3_TRACE
-// Compile-time phase timestamps (build with -DD3_TRACE): per CTA, globaltimer at the kernel's milestones and the
-// time the first consumer warp spent waiting for data and staging inputs. Off in normal builds.
-__device__ unsigned long long g_trace[1024][24];
+// Compile-time phase timestamps (build with -DD3_TRACE): per CTA, globaltimer at the kernel's milestones, and in SM
+// clock cycles (clock64, cheap to read) the time the first consumer warp and the epilogue warp spent waiting for
+// data, staging inputs, computing and handing off. Off in normal builds.
+// The counters live in shared memory while the kernel runs (a global read-modify-write per chunk would stall the
+// consumer warps and distort what is measured); the CTA's row is written out once at the end.
+__device__ unsigned long long g_trace[1024][32];
+__shared__ unsigned long long s_trace[32];
 #define D3_STAMP(slot) \
-  if (threadIdx.x == 0 && blockIdx.x < 1024) g_trace[blockIdx.x][slot] = globaltimer()
+  if (threadIdx.x == 0) s_trace[slot] = globaltimer()
 #define D3_ADD(slot, v) \
-  if (threadIdx.x == 0 && blockIdx.x < 1024) g_trace[blockIdx.x][slot] += (v)
+  if (threadIdx.x == 0) s_trace[slot] += (v)
 #define D3_ADD_EPI(slot, v) \
-  if (threadIdx.x == DEC_WARPS * 32 && blockIdx.x < 1024) g_trace[blockIdx.x][slot] += (v)
+  if (threadIdx.x == DEC_WARPS * 32) s_trace[slot] += (v)
 #else
 #define D3_STAMP(slot)
 #define D3_ADD(slot, v)
@@ -83,6 +87,7 @@ struct DecodePlan {
 // All DEC_THREADS threads call this; P <= DEC_MAX_PAIRS <= DEC_THREADS. Expert parallelism: only ids in
 // [e_first, e_first + e_count) are this rank's (local expert id - e_first); the others are skipped, and only ids
 // outside [0, E) are faults.
+template <int NT = DEC_THREADS>
 D3_DEV void build_plan(DecodePlan& pl, const int64_t* __restrict__ ids, int P, int E, int cap, int e_first,
                        int e_count) {
   __shared__ int key[DEC_MAX_PAIRS];
@@ -115,7 +120,7 @@ D3_DEV void build_plan(DecodePlan& pl, const int64_t* __restrict__ ids, int P, i
   if (lane == 0) pl.warp_total[warp] = __popc(mask);
   __syncthreads();
   int offset = 0, total = 0;
-  for (int w = 0; w < DEC_THREADS / 32; ++w) {
+  for (int w = 0; w < NT / 32; ++w) {
     int t = pl.warp_total[w];
     offset += w < warp ? t : 0;
     total += t;
@@ -487,10 +492,12 @@ D3_DEV void split_range(int total, int b, int g, int& lo, int& hi) {
 // Grid-wide barrier of one CTA per SM, taken by the MMA warps and the epilogue warp (named barrier 2), by tickets on
 // a 64-bit counter that starts at zero and only grows: a round completes when the counter reaches the round's end.
 // Bounded: after WAIT_LIMIT_NS the fault word is set and false returned.
+// Participants: the NT threads from LEADER on, on named barrier 2.
+template <int NT = DEC_CONSUMERS + 32, int LEADER = 0>
 D3_DEV bool grid_barrier(unsigned long long* counter, unsigned nblocks) {
   __shared__ int passed;
-  named_sync(2, DEC_CONSUMERS + 32);
-  if (threadIdx.x == 0) {
+  named_sync(2, NT);
+  if (threadIdx.x == LEADER) {
     __threadfence();
     const unsigned long long ticket = atomicAdd(counter, 1ull);
     const unsigned long long target = (ticket / nblocks + 1) * nblocks;
@@ -511,7 +518,7 @@ D3_DEV bool grid_barrier(unsigned long long* counter, unsigned nblocks) {
     }
     passed = ok;
   }
-  named_sync(2, DEC_CONSUMERS + 32);
+  named_sync(2, NT);
   return passed != 0;
 }
 
@@ -725,11 +732,62 @@ D3_DEV bool mma_phase(const DecodeArgs& a, const DecodePlan& pl, int lo, int hi,
   const int per = PHASE == 1 ? I : H, ch = PHASE == 1 ? DEC_CH1 : DEC_CH2;
   uint32_t bh[KC][8], bl[TWO ? KC : 1][8];
   int cur = -1, cnt = 0, e = 0;
+  // Each chunk's sums are handed to the epilogue one chunk late, after the next chunk's work has been issued: the
+  // hand-off store waits for the MMA results, and by then they are long complete, so their latency overlaps the
+  // next chunk instead of stalling the warp. Pending sums are handed off before a segment change restages pair_in /
+  // inv, and at the end of the phase.
+  int pv_c = -1, pv_r = 0, pv_cn = 0;
+  float4 pv_part = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  float pv_rsv = 0.0f;
+  auto handoff = [&]() {
+    const int slot = pv_c % DEC_RED;
+#ifdef D3_TRACE
+    const unsigned long long th0 = (unsigned long long)clock64();
+#endif
+    if (pv_c >= DEC_RED && ok) ok = mbar_wait(&rempty[slot], ((pv_c / DEC_RED) - 1) & 1);
+#ifdef D3_TRACE
+    D3_ADD(PHASE == 1 ? 15 : 21, (unsigned long long)clock64() - th0);
+#endif
+#ifdef D3_TRACE
+    const unsigned long long th1 = (unsigned long long)clock64();
+#endif
+    RedSlot& rs = red[slot];
+    rs.part[warp * 32 + lane] = pv_part;
+    if (fmt_row_scale(FMT) && warp == 0) rs.rsc[lane] = pv_rsv;
+    if (warp == 0) {
+      if (lane < DEC_MAX_CAP) {
+        rs.pair[lane] = pair_in[lane];
+        rs.inv[lane] = inv[lane];
+      }
+      if (lane == 0) {
+        rs.r = pv_r;
+        rs.cn = pv_cn;
+        rs.cnt = cnt;
+        rs.e = e;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&rfull[slot]);
+    pv_c = -1;
+#ifdef D3_TRACE
+    D3_ADD(24, (unsigned long long)clock64() - th1);
+#endif
+  };
+#ifdef D3_TRACE
+  unsigned long long t_it = (unsigned long long)clock64();
+#endif
   for (int q = lo; q < hi; ++c) {
     const int s = q / per, r = q - s * per, cn = min(ch, min(per - r, hi - q));
     if (s != cur) {
       // a new segment: stage its pairs' rows (x in phase 1, a1 in phase 2) once all warps left the last one
+      if (pv_c >= 0) handoff();
+#ifdef D3_TRACE
+      const unsigned long long tn0 = (unsigned long long)clock64();
+#endif
       named_sync(1, DEC_CONSUMERS);
+#ifdef D3_TRACE
+      D3_ADD(7, (unsigned long long)clock64() - tn0);
+#endif
       cur = s;
       cnt = pl.seg_count[s];
       e = pl.seg_expert[s];
@@ -746,7 +804,7 @@ D3_DEV bool mma_phase(const DecodeArgs& a, const DecodePlan& pl, int lo, int hi,
       }
       named_sync(1, DEC_CONSUMERS);
 #ifdef D3_TRACE
-      const unsigned long long ts0 = globaltimer();
+      const unsigned long long ts0 = (unsigned long long)clock64();
 #endif
       // a1 holds SwiGLU outputs; ConvRot formats rotate them, as the reference's rotate(swiglu=True) does
       if (PHASE == 1)
@@ -759,19 +817,20 @@ D3_DEV bool mma_phase(const DecodeArgs& a, const DecodePlan& pl, int lo, int hi,
       else
         load_b2<NKC>(xin, I, (uint32_t(&)[NKC][8])bh, (uint32_t(&)[NKC][8])bl);
 #ifdef D3_TRACE
-      D3_ADD(PHASE == 1 ? 8 : 10, globaltimer() - ts0);
-      D3_ADD(PHASE == 1 ? 12 : 14, 1);
+      D3_ADD(PHASE == 1 ? 8 : 10, (unsigned long long)clock64() - ts0);
+      D3_ADD(12, 1);
 #endif
     }
     const int st = c % NS;
 #ifdef D3_TRACE
-    const unsigned long long tw0 = globaltimer();
+    const unsigned long long tw0 = (unsigned long long)clock64();
+    D3_ADD(25, tw0 - t_it);
 #endif
     if (ok) ok = mbar_wait(&full_bar[st], (c / NS) & 1);
 #ifdef D3_TRACE
-    D3_ADD(PHASE == 1 ? 9 : 11, globaltimer() - tw0);
+    D3_ADD(PHASE == 1 ? 9 : 11, (unsigned long long)clock64() - tw0);
     if (c == 0) D3_STAMP(13);
-    const unsigned long long tc0 = globaltimer();
+    const unsigned long long tc0 = (unsigned long long)clock64();
 #endif
     float4 part = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     if (ok) {
@@ -799,41 +858,33 @@ D3_DEV bool mma_phase(const DecodeArgs& a, const DecodePlan& pl, int lo, int hi,
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty_bar[st]);
-    const int slot = c % DEC_RED;
 #ifdef D3_TRACE
-    const unsigned long long tc1 = globaltimer();
-    D3_ADD(16, tc1 - tc0);
+    D3_ADD(PHASE == 1 ? 16 : 20, (unsigned long long)clock64() - tc0);
+    D3_ADD(PHASE == 1 ? 18 : 22, 1);
 #endif
-    if (c >= DEC_RED && ok) ok = mbar_wait(&rempty[slot], ((c / DEC_RED) - 1) & 1);
-#ifdef D3_TRACE
-    D3_ADD(15, globaltimer() - tc1);
-#endif
-    RedSlot& rs = red[slot];
-    rs.part[warp * 32 + lane] = part;
-    if (fmt_row_scale(FMT) && warp == 0) rs.rsc[lane] = rsv;
-    if (warp == 0) {
-      if (lane < DEC_MAX_CAP) {
-        rs.pair[lane] = pair_in[lane];
-        rs.inv[lane] = inv[lane];
-      }
-      if (lane == 0) {
-        rs.r = r;
-        rs.cn = cn;
-        rs.cnt = cnt;
-        rs.e = e;
-      }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&rfull[slot]);
+    if (pv_c >= 0) handoff();
+    pv_c = c;
+    pv_r = r;
+    pv_cn = cn;
+    pv_part = part;
+    pv_rsv = rsv;
     q += cn;
+#ifdef D3_TRACE
+    const unsigned long long t_now = (unsigned long long)clock64();
+    D3_ADD(PHASE == 1 ? 23 : 14, t_now - t_it);
+    t_it = t_now;
+#endif
   }
+  if (pv_c >= 0) handoff();
   return ok;
 }
 
 // The routed combine of columns [n0, n1) for every row, in rank order (the reference's weighted_sum order), by the
 // CTA's MMA and epilogue warps. valid[p] / w[p]: pair p's id is in range / its routing weight (shared memory). The
 // k parts of an output are loaded together (independent L2 loads), then summed in order.
-D3_DEV void combine_columns(const DecodeArgs& a, const unsigned char* valid, const float* w, int n0, int n1, bool ok) {
+// Run by the nt threads from t0 on.
+D3_DEV void combine_columns(const DecodeArgs& a, const unsigned char* valid, const float* w, int n0, int n1, bool ok,
+                            int t0 = 0, int nt = DEC_CONSUMERS + 32) {
   // four adjacent columns a thread (n0, n1 multiples of 4): 16-byte loads of the parts and 16-byte stores (peer
   // stores included)
   const int NQ = (n1 - n0) >> 2, H = DEC_H;
@@ -847,13 +898,13 @@ D3_DEV void combine_columns(const DecodeArgs& a, const unsigned char* valid, con
       const unsigned ep = *(volatile const unsigned*)ex.epoch + 1u;
       slot = (size_t)((ep & 1u) * ex.world + ex.rank) * ex.m_max * H;
       world = ex.world;
-    } else if (threadIdx.x == 0) {
+    } else if (threadIdx.x == t0) {
       record_fault(FAULT_EXCHANGE);
     }
     dst32 = nullptr;
   }
   const bool out8 = ((uintptr_t)a.out & 7u) == 0;
-  for (int idx = threadIdx.x; idx < a.M * NQ; idx += DEC_CONSUMERS + 32) {
+  for (int idx = threadIdx.x - t0; idx < a.M * NQ; idx += nt) {
     const int t = idx / NQ, n = n0 + 4 * (idx - t * NQ);
     float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     for (int j0 = 0; j0 < a.k; j0 += 8) {
@@ -921,8 +972,8 @@ __global__ void __launch_bounds__(DEC_ALL, 1) moe_decode_kernel(const DecodeArgs
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 #ifdef D3_TRACE
-  if (tid == 0 && blockIdx.x < 1024)
-    for (int t = 0; t < 24; ++t) g_trace[blockIdx.x][t] = 0;
+  if (tid == 0)
+    for (int t = 0; t < 32; ++t) s_trace[t] = 0;
 #endif
   D3_STAMP(0);
   if (tid == 0) {
@@ -1026,11 +1077,11 @@ __global__ void __launch_bounds__(DEC_ALL, 1) moe_decode_kernel(const DecodeArgs
         const int s = q / per, r = q - s * per, cn = min(ch, min(per - r, hi - q));
         const int slot = c % DEC_RED;
 #ifdef D3_TRACE
-        const unsigned long long te0 = globaltimer();
+        const unsigned long long te0 = (unsigned long long)clock64();
 #endif
         if (ok) ok = mbar_wait(&rfull[slot], (c / DEC_RED) & 1);
 #ifdef D3_TRACE
-        const unsigned long long te1 = globaltimer();
+        const unsigned long long te1 = (unsigned long long)clock64();
         D3_ADD_EPI(17, te1 - te0);
 #endif
         const RedSlot& rs = red[slot];
@@ -1096,7 +1147,7 @@ __global__ void __launch_bounds__(DEC_ALL, 1) moe_decode_kernel(const DecodeArgs
           }
         }
 #ifdef D3_TRACE
-        D3_ADD_EPI(19, globaltimer() - te1);
+        D3_ADD_EPI(19, (unsigned long long)clock64() - te1);
 #endif
         __syncwarp();
         if (lane == 0) mbar_arrive(&rempty[slot]);
@@ -1187,6 +1238,10 @@ __global__ void __launch_bounds__(DEC_ALL, 1) moe_decode_kernel(const DecodeArgs
     }
   }
   D3_STAMP(6);
+#ifdef D3_TRACE
+  if (tid == 0 && blockIdx.x < 1024)
+    for (int t = 0; t < 32; ++t) g_trace[blockIdx.x][t] = s_trace[t];
+#endif
 }
 
 // The exchange's reduce on one rank: every CTA waits (bounded) until each rank has raised its flag for this call,
