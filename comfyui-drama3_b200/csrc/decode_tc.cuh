@@ -14,8 +14,10 @@
 // Phase 1 (gate_up + SwiGLU): a tile is 64 gate rows and the matching 64 up rows of one expert (M = 128) over all H
 // columns; B holds every line's terms (N = 16 lines x terms), staged once per call, so a segment needs no staging of
 // its own - the epilogue picks the columns of the segment's lines. Phase 2 (down): a tile is 128 down rows over all I
-// columns; B holds the segment's pairs' a1 rows (N = 16 pairs x 4 terms), two segments' worth, staged after the grid
-// barrier. The work of each phase is split across the grid by whole tiles.
+// columns; B holds the segment's pairs' a1 rows (N = 16 pairs x 4 terms), two segments' worth. The work of each phase
+// is split across the grid by whole tiles, in proportion, so a CTA's phase-2 segments are mostly its own phase-1 ones.
+// Between the phases no grid-wide wait: a segment's phase-2 staging waits (bounded) for the count of its finished
+// phase-1 tiles. The combine follows a grid barrier, each CTA taking an even share of the columns.
 //
 // Roles (8 warps): warp 0 lane 0 issues the TMA loads, warp 1 owns TMEM and lane 0 issues the MMAs, warps 2-5 are
 // the TMEM epilogue (one warp per lane quarter), warps 2-7 stage the B operands and run the combine.
@@ -24,6 +26,15 @@
 #include "moe_decode.cuh"
 
 namespace d3 {
+
+#ifdef D3_TRACE
+// Trace builds: globaltimer at milestones and clock64 wait totals, kept in shared memory, one row per CTA.
+#define TC_STAMP(slot) s_trace[slot] = globaltimer()
+#define TC_ADD(slot, v) s_trace[slot] += (v)
+#else
+#define TC_STAMP(slot)
+#define TC_ADD(slot, v)
+#endif
 
 constexpr int TC_WARPS = 8;
 constexpr int TC_THREADS = TC_WARPS * 32;
@@ -205,19 +216,44 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   }
   if (tid < 16) lmax[tid] = 0;
   if (tid < 32) smax[tid] = 0;
+#ifdef D3_TRACE
+  if (tid < 32) s_trace[tid] = 0;
+#endif
   if (warp == 1) tmem_alloc(tmem_slot, TC_TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (tid == 0) TC_STAMP(0);
   // programmatic dependent launch: inputs and the workspace are touched only after the previous grid has completed
   allow_dependents();
   grid_dependency_wait();
+  // phase-1 B rows (lines) of this helper warp: hw, hw + 6, hw + 12; their loads are issued before the plan is built
+  // (bf16: all three rows; fp32: the first), so they land while it is
+  constexpr int XW = XBF ? 2 : 4;  // 16-byte words per 16-column chunk
+  constexpr int PRE = XBF ? 3 : 1;
+  const int hw = warp - 2;
+  uint4 xr[PRE][4][XW];
+  if (warp >= 2) {
+#pragma unroll
+    for (int r = 0; r < PRE; ++r) {
+      const int n = hw + 6 * r;
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int w = 0; w < XW; ++w)
+          xr[r][u][w] = (n < TC_LINES && n < a.M)
+                            ? __ldcg(reinterpret_cast<const uint4*>((const uint8_t*)a.x +
+                                                                     ((size_t)n * H + 16 * (lane + 32 * u)) * (XBF ? 2 : 4)) + w)
+                            : make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  const long long my_id = tid < P ? a.ids[tid] : 0;
+  const float my_w = tid < P ? a.weights[tid] : 0.0f;
   build_plan<TC_THREADS>(pl, a.ids, P, a.E, TC_CAP, a.e_first, a.e_count);
   if (tid < P) {
-    const long long id = a.ids[tid];
-    c_ok[tid] = id >= a.e_first && id < (long long)a.e_first + a.e_count && id < a.E;
-    c_w[tid] = a.weights[tid];
+    c_ok[tid] = my_id >= a.e_first && my_id < (long long)a.e_first + a.e_count && my_id < a.E;
+    c_w[tid] = my_w;
   }
   const int nseg = pl.nseg;
   const int t1_lo = (int)((long long)blockIdx.x * nseg * TPS1 / G);
@@ -227,6 +263,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   // phase-2 segments of this CTA: at most two (its range is at most TPS2 tiles when nseg <= G, which the host checks)
   const int s2a = t2_lo / TPS2, s2n = t2_hi > t2_lo ? (t2_hi - 1) / TPS2 - s2a + 1 : 0;
   bool ok = true;
+  if (tid == 0) TC_STAMP(1);
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -238,7 +275,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int grow = e * 2 * I + ub * TC_U1;
         for (int kb = 0; kb < NKB1; ++kb, ++c) {
           const int st = c % TC_STAGES;
+#ifdef D3_TRACE
+          const long long w0 = clock64();
+#endif
           ok = mbar_wait(empty + st, ((c / TC_STAGES) & 1) ^ 1);
+          TC_ADD(20, clock64() - w0);
           if (!ok) break;
           mbar_arrive_expect_tx(full + st, TC_ABYTES);
           tma_load_2d_hint(ring + st * TC_ABYTES, &map13, kb * 128, grow, full + st, pol);
@@ -250,7 +291,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int row = e * H + rb * TC_R2;
         for (int kb = 0; kb < NKB2; ++kb, ++c) {
           const int st = c % TC_STAGES;
+#ifdef D3_TRACE
+          const long long w0 = clock64();
+#endif
           ok = mbar_wait(empty + st, ((c / TC_STAGES) & 1) ^ 1);
+          TC_ADD(21, clock64() - w0);
           if (!ok) break;
           mbar_arrive_expect_tx(full + st, TC_ABYTES);
           tma_load_2d_hint(ring + st * TC_ABYTES, &map2, kb * 128, row, full + st, pol);
@@ -267,6 +312,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const uint32_t id1 = tc_idesc(N1), id2 = tc_idesc(TC_N2);
       int c = 0, tn = 0;
       if (t1_hi > t1_lo) ok = mbar_wait(b1_full, 0);
+      TC_STAMP(3);
       tc_fence_after();
       for (int t = t1_lo; t < t1_hi && ok; ++t, ++tn) {
         const int buf = tn & 1;
@@ -276,7 +322,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const uint32_t d = tmem + buf * 64;
         for (int kb = 0; kb < NKB1; ++kb, ++c) {
           const int st = c % TC_STAGES;
+#ifdef D3_TRACE
+          const long long w0 = clock64();
+#endif
           ok = mbar_wait(full + st, (c / TC_STAGES) & 1);
+          TC_ADD(22, clock64() - w0);
           if (!ok) break;
           tc_fence_after();
 #pragma unroll
@@ -287,6 +337,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         umma_commit(acc_full + buf);
       }
+      TC_STAMP(4);
       int cur = -1;
       for (int t = t2_lo; t < t2_hi && ok; ++t, ++tn) {
         const int s = t / TPS2, bb = s - s2a;
@@ -297,6 +348,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             break;
           }
           ok = mbar_wait(b2_full + bb, 0);
+          if (bb == 0) TC_STAMP(7);
           if (!ok) break;
           tc_fence_after();
           cur = s;
@@ -308,7 +360,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const uint32_t d = tmem + buf * 64;
         for (int kb = 0; kb < NKB2; ++kb, ++c) {
           const int st = c % TC_STAGES;
+#ifdef D3_TRACE
+          const long long w0 = clock64();
+#endif
           ok = mbar_wait(full + st, (c / TC_STAGES) & 1);
+          TC_ADD(23, clock64() - w0);
           if (!ok) break;
           tc_fence_after();
 #pragma unroll
@@ -320,41 +376,69 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         umma_commit(acc_full + buf);
       }
+      TC_STAMP(8);
     }
   } else {
-    // ---------------- helpers: staging, epilogue, barriers ----------------
-    const int hid = tid - TC_HELP0;
-    // phase-1 B: every line's terms (rows >= M are zero)
+    // ---------------- helpers: staging, epilogue, combine ----------------
+    const int hid = tid - TC_HELP0;  // helper thread 0..191
+    // phase-1 B: every line's terms, one warp per line (rows >= M are zero); the warp holds the whole row, so the
+    // row maximum is a warp reduction
     if (t1_hi > t1_lo) {
-      for (int it = hid; it < TC_LINES * (H / 16); it += TC_HELPERS) {
-        const int n = it / (H / 16), q = it - n * (H / 16);
-        if (n < a.M) {
-          float v[16];
-          tc_load16(a.x, a.x_bf16 != 0, (size_t)n * H + 16 * q, v);
-          float m = 0.0f;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(v[i]));
-          atomicMax(lmax + n, __float_as_int(m));
-        }
-      }
-      named_sync(1, TC_HELPERS);
-      for (int it = hid; it < TC_LINES * (H / 16); it += TC_HELPERS) {
-        const int n = it / (H / 16), q = it - n * (H / 16);
-        float v[16];
-        if (n < a.M) {
-          tc_load16(a.x, a.x_bf16 != 0, (size_t)n * H + 16 * q, v);
-        } else {
+      for (int r = 0; r < 3; ++r) {
+        const int n = hw + 6 * r;
+        if (n >= TC_LINES) break;
+        uint4 cur[4][XW];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) v[i] = 0.0f;
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int w = 0; w < XW; ++w)
+            cur[u][w] = r < PRE ? xr[r < PRE ? r : 0][u][w]
+                        : (n < a.M ? __ldcg(reinterpret_cast<const uint4*>((const uint8_t*)a.x +
+                                                                           ((size_t)n * H + 16 * (lane + 32 * u)) * 4) + w)
+                                   : make_uint4(0u, 0u, 0u, 0u));
+        float v[4][16];
+        float m = 0.0f;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (XBF) {
+#pragma unroll
+            for (int w = 0; w < 2; ++w) {
+              const uint32_t ww[4] = {cur[u][w].x, cur[u][w].y, cur[u][w].z, cur[u][w].w};
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                v[u][8 * w + 2 * h] = bf16_to_f32(ww[h] & 0xFFFFu);
+                v[u][8 * w + 2 * h + 1] = bf16_to_f32(ww[h] >> 16);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int w = 0; w < XW; ++w) {
+              v[u][4 * w] = __uint_as_float(cur[u][w].x);
+              v[u][4 * w + 1] = __uint_as_float(cur[u][w].y);
+              v[u][4 * w + 2] = __uint_as_float(cur[u][w].z);
+              v[u][4 * w + 3] = __uint_as_float(cur[u][w].w);
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(v[u][i]));
         }
-        const int e = tc_exponent(__int_as_float(lmax[n]));
-        tc_write_terms<T1>(breg, N1, n, TC_LINES, q, v, __uint_as_float((uint32_t)(e + 127) << 23));
-        if (q == 0) linv[n] = __uint_as_float((uint32_t)(127 - e) << 23);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        const int e = tc_exponent(m);
+        const float scale = __uint_as_float((uint32_t)(e + 127) << 23);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) tc_write_terms<T1>(breg, N1, n, TC_LINES, lane + 32 * u, v[u], scale);
+        if (lane == 0) linv[n] = __uint_as_float((uint32_t)(127 - e) << 23);
       }
       fence_async_smem();
       named_sync(1, TC_HELPERS);
-      if (hid == 0) mbar_arrive(b1_full);
+      if (hid == 0) {
+        mbar_arrive(b1_full);
+        TC_STAMP(2);
+      }
     }
+    unsigned* seg_done = a.arrive;  // per segment: phase-1 tiles finished (all CTAs), zero between calls
     int tn = 0;
     if (warp < 6) {
       // phase-1 epilogue: per tile, every line's gate / up sums, then SwiGLU for the segment's pairs
@@ -381,8 +465,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           xchg[row * TC_XPITCH + l] = ok ? sum : 0.0f;
         }
         named_sync(3, TC_EPI);
+        const int s = t / TPS1;
         if (row < TC_U1) {
-          const int s = t / TPS1, ub = t - s * TPS1, e = pl.seg_expert[s];
+          const int ub = t - s * TPS1, e = pl.seg_expert[s];
           const int i = ub * TC_U1 + row;
           const float gsc = __ldg((const float*)a.s13 + (size_t)e * 2 * I + i);
           const float usc = __ldg((const float*)a.s13 + (size_t)e * 2 * I + I + i);
@@ -395,59 +480,82 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
         }
         named_sync(3, TC_EPI);
+        if (tid == TC_HELP0) {
+          // the tile's a1 columns are written (the barrier orders the epilogue's stores before this fence)
+          __threadfence();
+          atomicAdd(seg_done + s, 1u);
+        }
       }
     }
-    // every CTA's a1 is written
-    ok = grid_barrier<TC_HELPERS, TC_HELP0>(a.barrier, G) && ok;
-    // phase-2 B: the pairs of this CTA's (at most two) segments, 4 terms each
-    if (s2n > 0) {
-      const int items = 2 * TC_CAP * (I / 16);
-      for (int it = hid; it < items; it += TC_HELPERS) {
-        const int bj = it / (I / 16), q = it - bj * (I / 16), bb = bj / TC_CAP, j = bj - bb * TC_CAP;
-        if (bb < s2n && j < pl.seg_count[s2a + bb]) {
-          const int pair = pl.sorted[pl.seg_first[s2a + bb] + j];
-          float v[16];
-          tc_load16(a.a1, false, (size_t)pair * I + 16 * q, v);
-          float m = 0.0f;
-#pragma unroll
-          for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(v[i]));
-          atomicMax(smax + bj, __float_as_int(m));
+    if (tid == TC_HELP0) TC_STAMP(5);
+    // phase-2 B, segment by segment (at most two): once every phase-1 tile of the segment is done (bounded wait),
+    // its pairs' a1 rows as 4 terms, two rows per warp (16 lanes a row)
+    __shared__ int s_ready;
+    for (int bb = 0; bb < s2n; ++bb) {
+      const int s = s2a + bb, cnt = pl.seg_count[s], first = pl.seg_first[s];
+      if (tid == TC_HELP0) {
+        int okw = 1;
+        unsigned seen;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(seen) : "l"(seg_done + s) : "memory");
+        if (seen < (unsigned)TPS1) {
+          const unsigned long long start = globaltimer();
+          while (true) {
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(seen) : "l"(seg_done + s) : "memory");
+            if (seen >= (unsigned)TPS1) break;
+            if (globaltimer() - start > WAIT_LIMIT_NS) {
+              record_fault(FAULT_WAIT_TIMEOUT);
+              okw = 0;
+              break;
+            }
+          }
         }
+        s_ready = okw;
+        if (bb == 0) TC_STAMP(6);
       }
       named_sync(1, TC_HELPERS);
-      for (int it = hid; it < items; it += TC_HELPERS) {
-        const int bj = it / (I / 16), q = it - bj * (I / 16), bb = bj / TC_CAP, j = bj - bb * TC_CAP;
-        if (bb >= s2n) continue;
-        const bool live = j < pl.seg_count[s2a + bb];
-        const int pair = live ? pl.sorted[pl.seg_first[s2a + bb] + j] : 0;
-        float v[16];
-        if (live) {
-          tc_load16(a.a1, false, (size_t)pair * I + 16 * q, v);
-        } else {
+      ok = ok && s_ready;
+      constexpr int CPL = I / 16 / 16;  // chunks per lane (16 lanes a row)
+      for (int jp = hw; jp < TC_CAP / 2; jp += TC_HELPERS / 32) {
+        const int j = 2 * jp + (lane >> 4), sub = lane & 15;
+        const bool live = j < cnt;
+        const int pair = live ? pl.sorted[first + j] : 0;
+        float v[CPL][16];
+        float m = 0.0f;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) v[i] = 0.0f;
+        for (int u = 0; u < CPL; ++u) {
+          if (live) {
+            tc_load16(a.a1, false, (size_t)pair * I + 16 * (sub + 16 * u), v[u]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[u][i] = 0.0f;
+          }
+#pragma unroll
+          for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(v[u][i]));
         }
-        const int e = tc_exponent(__int_as_float(smax[bj]));
-        tc_write_terms<TC_TERMS2>(breg + bb * B2BYTES, TC_N2, j, TC_CAP, q, v,
-                                  __uint_as_float((uint32_t)(e + 127) << 23));
-        if (q == 0) {
-          spair[bj] = pair;
-          sinv[bj] = __uint_as_float((uint32_t)(127 - e) << 23);
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        const int e = tc_exponent(m);
+        const float scale = __uint_as_float((uint32_t)(e + 127) << 23);
+#pragma unroll
+        for (int u = 0; u < CPL; ++u)
+          tc_write_terms<TC_TERMS2>(breg + bb * B2BYTES, TC_N2, j, TC_CAP, sub + 16 * u, v[u], scale);
+        if (sub == 0) {
+          spair[bb * TC_CAP + j] = pair;
+          sinv[bb * TC_CAP + j] = __uint_as_float((uint32_t)(127 - e) << 23);
         }
       }
       fence_async_smem();
       named_sync(1, TC_HELPERS);
-      if (hid == 0)
-        for (int bb = 0; bb < s2n && bb < 2; ++bb) mbar_arrive(b2_full + bb);
+      if (hid == 0) mbar_arrive(b2_full + bb);
     }
+    // phase-2 epilogue: parts[pair, row] = the pair's terms summed x row scale x 2^-e
     if (warp < 6) {
-      // phase-2 epilogue: parts[pair, row] = the pair's terms summed x row scale x 2^-e
       const int quarter = warp & 3;
       const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
       for (int t = t2_lo; t < t2_hi; ++t, ++tn) {
         const int buf = tn & 1;
         if (ok) ok = mbar_wait(acc_full + buf, (tn >> 1) & 1);
-        ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective: the warp agrees
+        ok = __all_sync(0xffffffffu, ok);
         tc_fence_after();
         float v[TC_N2];
         if (ok) {
@@ -458,25 +566,30 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(acc_empty + buf);
-        if (!ok) continue;
         const int s = t / TPS2, rb = t - s * TPS2, bb = s - s2a, e = pl.seg_expert[s];
-        if (bb > 1) continue;
-        const int r = rb * TC_R2 + 32 * quarter + lane;
-        const float sc = __ldg((const float*)a.s2 + (size_t)e * H + r);
-        const int cnt = pl.seg_count[s];
+        if (ok && bb <= 1) {
+          const int r = rb * TC_R2 + 32 * quarter + lane;
+          const float sc = __ldg((const float*)a.s2 + (size_t)e * H + r);
+          const int cnt = pl.seg_count[s];
 #pragma unroll
-        for (int j = 0; j < TC_CAP; ++j) {
-          if (j < cnt) {
-            float sum = v[j];
+          for (int j = 0; j < TC_CAP; ++j) {
+            if (j < cnt) {
+              float sum = v[j];
 #pragma unroll
-            for (int tt = 1; tt < TC_TERMS2; ++tt) sum += v[tt * TC_CAP + j];
-            __stcg(a.parts + (size_t)spair[bb * TC_CAP + j] * H + r, sum * (sc * sinv[bb * TC_CAP + j]));
+              for (int tt = 1; tt < TC_TERMS2; ++tt) sum += v[tt * TC_CAP + j];
+              __stcg(a.parts + (size_t)spair[bb * TC_CAP + j] * H + r, sum * (sc * sinv[bb * TC_CAP + j]));
+            }
           }
         }
       }
     }
     // every CTA's parts are written; each CTA combines an even share of the columns
+    if (tid == TC_HELP0) TC_STAMP(9);
     ok = grid_barrier<TC_HELPERS, TC_HELP0>(a.barrier, G) && ok;
+    if (tid == TC_HELP0) TC_STAMP(10);
+    // every CTA is past its phase-2 staging: CTA 0 clears the segment counters for the next call
+    if (blockIdx.x == 0)
+      for (int s = hid; s < nseg; s += TC_HELPERS) seg_done[s] = 0u;
     int q0, q1;
     split_range(H / 4, blockIdx.x, G, q0, q1);
     combine_columns(a, c_ok, c_w, 4 * q0, 4 * q1, ok, TC_HELP0, TC_HELPERS);
@@ -500,6 +613,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
+#ifdef D3_TRACE
+  if (tid == 0) {
+    TC_STAMP(11);
+    if (blockIdx.x < 1024)
+      for (int t = 0; t < 32; ++t) g_trace[blockIdx.x][t] = s_trace[t];
+  }
+#endif
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, TC_TMEM_COLS);

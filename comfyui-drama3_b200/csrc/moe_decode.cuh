@@ -90,23 +90,33 @@ struct DecodePlan {
 template <int NT = DEC_THREADS>
 D3_DEV void build_plan(DecodePlan& pl, const int64_t* __restrict__ ids, int P, int E, int cap, int e_first,
                        int e_count) {
-  __shared__ int key[DEC_MAX_PAIRS];
+  __shared__ __align__(16) int key[DEC_MAX_PAIRS];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid < P) {
-    const long long e = ids[tid];
-    if (e < 0 || e >= E) record_fault(FAULT_BAD_EXPERT);
-    const bool mine = e >= e_first && e < (long long)e_first + e_count && e < E;
-    key[tid] = mine ? (int)(e - e_first) : 0x7fffffff;
+  if (tid < DEC_MAX_PAIRS) {
+    int kv = 0x7fffffff;  // positions past P: no expert, ranked after every pair
+    if (tid < P) {
+      const long long e = ids[tid];
+      if (e < 0 || e >= E) record_fault(FAULT_BAD_EXPERT);
+      const bool mine = e >= e_first && e < (long long)e_first + e_count && e < E;
+      if (mine) kv = (int)(e - e_first);
+    }
+    key[tid] = kv;
   }
   __syncthreads();
   if (tid < P) {
     const int kp = key[tid];
     int rank = 0, lower = 0, same = 0;
-    for (int q = 0; q < P; ++q) {
-      int kq = key[q];
-      lower += kq < kp;
-      same += kq == kp;
-      rank += (kq < kp) | ((kq == kp) & (q < tid));
+    // all DEC_MAX_PAIRS keys, four per load (the padding never ranks below a pair or ties with a valid one)
+#pragma unroll 8
+    for (int q0 = 0; q0 < DEC_MAX_PAIRS; q0 += 4) {
+      const int4 k4 = *reinterpret_cast<const int4*>(key + q0);
+      const int kq[4] = {k4.x, k4.y, k4.z, k4.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        lower += kq[u] < kp;
+        same += kq[u] == kp;
+        rank += (kq[u] < kp) | ((kq[u] == kp) & (q0 + u < tid));
+      }
     }
     pl.sorted[rank] = tid;
     pl.rkey[rank] = kp;
