@@ -50,10 +50,22 @@ FORMAT_NAMES = {
     "w6": "6-bit codes + e4m3 group-16 scales + s_channel, ConvRot (the reference's W6A8 layout)",
 }
 # dram bytes (read + write) per launch over algorithmic bytes per launch, from the ncu capture of the small case
-# (bench.py --layers 4, all 4 launches of one timed step); the full run's traffic is this ratio x its own bytes
-TRAFFIC_RATIO = 1625.44 / 1609.96
-TRAFFIC_SOURCE = ("ncu capture of the 4-layer small case (bench.py --layers 4 --kind fp8): DRAM read + write / "
-                  "algorithmic bytes of the same launches")
+# (bench.py --layers 4, the first 2 launches of the timed step: 86 and 87 routed experts); the full run's traffic is
+# this ratio x its own bytes
+TRAFFIC_RATIO = (407.196928 + 5.279488 + 411.930368 + 4.855552) / (407.164416 + 411.897344)
+TRAFFIC_SOURCE = ("ncu capture of the 4-layer small case (bench.py --layers 4, moe_decode_tc_kernel, 2 launches): "
+                  "DRAM read + write / algorithmic bytes of the same launches")
+
+
+def kernel_of(kind, lines):
+    """(kernel name, arithmetic) of the fused decode for `kind` banks and `lines` rows."""
+    if kind == "fp8c" and lines >= 8:
+        return ("moe_decode_tc_kernel (tcgen05 kind::f8f6f4; one persistent launch per layer: plan, gate_up + "
+                "SwiGLU, down, combine)",
+                "e4m3 x e4m3 tensor-core MMA: e4m3 weights as stored, bf16 activations as two exact e4m3 terms, "
+                "f32 accumulation")
+    return (f"moe_decode_kernel<{kind}> (mma.sync; one persistent launch per layer: plan, gate_up + SwiGLU, down, "
+            f"combine)", "f16 MMA inputs (exact weight codes), f32 accumulation")
 
 
 def rand_bank(kind, n, k, gen, device):
@@ -531,14 +543,13 @@ def main():
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "f16 MMA inputs (exact e4m3 weights), f32 accumulation",
+                "vs_baseline": None, "dtype": kernel_of(kind, args.lines)[1],
                 "data": "synthetic (seeded random banks)", "config": config(args),
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                              "frac": achieved / hbm_peak, "peak_kind": peak_kind,
                              "traffic": TRAFFIC_RATIO * step_bytes / n_layers,
                              "traffic_unit": "bytes per launch", "traffic_source": TRAFFIC_SOURCE,
-                             "kernel": f"moe_decode_kernel<{kind}> (one persistent launch per layer: plan, gate_up + "
-                                       f"SwiGLU, down, combine)",
+                             "kernel": kernel_of(kind, args.lines)[0],
                              "bytes_per_launch": step_bytes / n_layers, "us_per_layer": 1e3 * ms / n_layers,
                              "launch_time": "step time / layers: the launches run back to back in one graph"},
                 "gpu_launches": n_layers * args.steps,

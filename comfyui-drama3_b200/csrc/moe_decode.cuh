@@ -106,9 +106,9 @@ D3_DEV void build_plan(DecodePlan& pl, const int64_t* __restrict__ ids, int P, i
   if (tid < P) {
     const int kp = key[tid];
     int rank = 0, lower = 0, same = 0;
-    // all DEC_MAX_PAIRS keys, four per load (the padding never ranks below a pair or ties with a valid one)
+    // the keys four per load, through the padding after P (which never ranks below a pair or ties with a valid one)
 #pragma unroll 8
-    for (int q0 = 0; q0 < DEC_MAX_PAIRS; q0 += 4) {
+    for (int q0 = 0; q0 < P; q0 += 4) {
       const int4 k4 = *reinterpret_cast<const int4*>(key + q0);
       const int kq[4] = {k4.x, k4.y, k4.z, k4.w};
 #pragma unroll
@@ -742,10 +742,8 @@ D3_DEV bool mma_phase(const DecodeArgs& a, const DecodePlan& pl, int lo, int hi,
   const int per = PHASE == 1 ? I : H, ch = PHASE == 1 ? DEC_CH1 : DEC_CH2;
   uint32_t bh[KC][8], bl[TWO ? KC : 1][8];
   int cur = -1, cnt = 0, e = 0;
-  // Each chunk's sums are handed to the epilogue one chunk late, after the next chunk's work has been issued: the
-  // hand-off store waits for the MMA results, and by then they are long complete, so their latency overlaps the
-  // next chunk instead of stalling the warp. Pending sums are handed off before a segment change restages pair_in /
-  // inv, and at the end of the phase.
+  // Each chunk's sums go to the epilogue as soon as they are computed (handing them off one chunk later, after the
+  // next chunk's MMAs were issued, measured slower).
   int pv_c = -1, pv_r = 0, pv_cn = 0;
   float4 pv_part = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   float pv_rsv = 0.0f;
@@ -790,7 +788,6 @@ D3_DEV bool mma_phase(const DecodeArgs& a, const DecodePlan& pl, int lo, int hi,
     const int s = q / per, r = q - s * per, cn = min(ch, min(per - r, hi - q));
     if (s != cur) {
       // a new segment: stage its pairs' rows (x in phase 1, a1 in phase 2) once all warps left the last one
-      if (pv_c >= 0) handoff();
 #ifdef D3_TRACE
       const unsigned long long tn0 = (unsigned long long)clock64();
 #endif
@@ -872,12 +869,12 @@ D3_DEV bool mma_phase(const DecodeArgs& a, const DecodePlan& pl, int lo, int hi,
     D3_ADD(PHASE == 1 ? 16 : 20, (unsigned long long)clock64() - tc0);
     D3_ADD(PHASE == 1 ? 18 : 22, 1);
 #endif
-    if (pv_c >= 0) handoff();
     pv_c = c;
     pv_r = r;
     pv_cn = cn;
     pv_part = part;
     pv_rsv = rsv;
+    handoff();
     q += cn;
 #ifdef D3_TRACE
     const unsigned long long t_now = (unsigned long long)clock64();
@@ -885,7 +882,6 @@ D3_DEV bool mma_phase(const DecodeArgs& a, const DecodePlan& pl, int lo, int hi,
     t_it = t_now;
 #endif
   }
-  if (pv_c >= 0) handoff();
   return ok;
 }
 
