@@ -59,7 +59,7 @@ TRAFFIC_SOURCE = ("ncu capture of the 4-layer small case (bench.py --layers 4, m
 
 def kernel_of(kind, lines):
     """(kernel name, arithmetic) of the fused decode for `kind` banks and `lines` rows."""
-    if kind == "fp8c" and lines >= 8:
+    if kind == "fp8c":
         return ("moe_decode_tc_kernel (tcgen05 kind::f8f6f4; one persistent launch per layer: plan, gate_up + "
                 "SwiGLU, down, combine)",
                 "e4m3 x e4m3 tensor-core MMA: e4m3 weights as stored, bf16 activations as two exact e4m3 terms, "

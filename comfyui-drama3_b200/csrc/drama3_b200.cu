@@ -453,11 +453,17 @@ static int decode_nkc(const d3::DecodeArgs& a, const DeviceInfo& d, cudaStream_t
   }
 }
 
-// The tensor-core decode (per-channel e4m3 rows, >= 8 lines): on unless D3_DECODE_TC=0 in the environment at the
-// call (kept for comparing the two kernels on the same inputs).
+// The tensor-core decode (per-channel e4m3 rows; faster than the mma.sync decode at every line count measured, 1-16):
+// on unless D3_DECODE_TC=0 in the environment at the call, from D3_DECODE_TC_MIN lines (default 1) on (both kept for
+// comparing the two kernels on the same inputs).
 static bool decode_tc_enabled() {
   const char* v = getenv("D3_DECODE_TC");
   return !(v && v[0] == '0');
+}
+
+static int decode_tc_min_lines() {
+  const char* v = getenv("D3_DECODE_TC_MIN");
+  return v ? atoi(v) : 1;
 }
 
 template <bool XBF, int NKB2>
@@ -514,9 +520,10 @@ static int decode_common(int fmt, const void* x, int x_bf16, int M, int k, int E
                       out, out_f32, e_first, e_count, (const d3::EpExchange*)exchange, words + 4, a1, parts, barrier,
                       words + 16, words + 128, words + 384, 0, 0, cap};
   cudaStream_t s = (cudaStream_t)stream;
-  // per-channel e4m3 with enough lines to fill the grid: the tensor-core kernel (its phase-2 split needs one CTA per
-  // segment at least: at most M * k <= 128 segments)
-  if (fmt == d3::FMT_FP8C && M >= 8 && d.sms >= d3::DEC_MAX_PAIRS && decode_tc_enabled()) return decode_tc(a, d, s);
+  // per-channel e4m3: the tensor-core kernel (its phase-2 split needs one CTA per segment at least: at most
+  // M * k <= 128 segments)
+  if (fmt == d3::FMT_FP8C && M >= decode_tc_min_lines() && d.sms >= d3::DEC_MAX_PAIRS && decode_tc_enabled())
+    return decode_tc(a, d, s);
   switch (fmt) {
     case d3::FMT_FP8:
       return x_bf16 ? decode_nkc<d3::FMT_FP8, true>(a, d, s) : decode_nkc<d3::FMT_FP8, false>(a, d, s);

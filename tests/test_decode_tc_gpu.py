@@ -1,4 +1,4 @@
-"""The tensor-core decode (per-channel e4m3 rows, 8-16 lines: tcgen05 kind::f8f6f4 with the activations as exact
+"""The tensor-core decode (per-channel e4m3 rows, 1-16 lines: tcgen05 kind::f8f6f4 with the activations as exact
 e4m3 terms) against the oracle and against the mma.sync decode on the same inputs (D3_DECODE_TC=0 selects it)."""
 import numpy as np
 import pytest
@@ -22,7 +22,7 @@ def both(monkeypatch, kind, x, ids, w, banks, **kw):
 
 
 @pytest.mark.parametrize("I", [768, 512])
-@pytest.mark.parametrize("M", [8, 12, 16])
+@pytest.mark.parametrize("M", [1, 2, 4, 8, 12, 16])
 @pytest.mark.parametrize("bf16", [True, False])
 def test_tc_decode_matches_oracle(cuda, monkeypatch, I, M, bf16):
     E = 32
