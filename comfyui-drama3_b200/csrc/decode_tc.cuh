@@ -248,6 +248,63 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                             : make_uint4(0u, 0u, 0u, 0u);
     }
   }
+  // phase-1 B (warps 2-7, after the plan): every line's terms, one warp per line; the warp holds the whole row, so
+  // the row maximum is a warp reduction
+  auto stage_b1 = [&]() {
+#pragma unroll
+      for (int r = 0; r < 3; ++r) {
+        const int n = hw + 6 * r;
+        if (n >= TC_LINES || n >= a.M) break;  // rows past M stay unwritten: the epilogue never reads their columns
+        uint4 cur[4][XW];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int w = 0; w < XW; ++w)
+            cur[u][w] = r < PRE ? xr[r < PRE ? r : 0][u][w]
+                        : (n < a.M ? __ldcg(reinterpret_cast<const uint4*>((const uint8_t*)a.x +
+                                                                           ((size_t)n * H + 16 * (lane + 32 * u)) * 4) + w)
+                                   : make_uint4(0u, 0u, 0u, 0u));
+        float v[4][16];
+        float m = 0.0f;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (XBF) {
+#pragma unroll
+            for (int w = 0; w < 2; ++w) {
+              const uint32_t ww[4] = {cur[u][w].x, cur[u][w].y, cur[u][w].z, cur[u][w].w};
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                v[u][8 * w + 2 * h] = bf16_to_f32(ww[h] & 0xFFFFu);
+                v[u][8 * w + 2 * h + 1] = bf16_to_f32(ww[h] >> 16);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int w = 0; w < XW; ++w) {
+              v[u][4 * w] = __uint_as_float(cur[u][w].x);
+              v[u][4 * w + 1] = __uint_as_float(cur[u][w].y);
+              v[u][4 * w + 2] = __uint_as_float(cur[u][w].z);
+              v[u][4 * w + 3] = __uint_as_float(cur[u][w].w);
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(v[u][i]));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        const int e = tc_exponent(m);
+        const float scale = __uint_as_float((uint32_t)(e + 127) << 23);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) tc_write_terms<T1>(breg, N1, n, TC_LINES, lane + 32 * u, v[u], scale);
+        if (lane == 0) linv[n] = __uint_as_float((uint32_t)(127 - e) << 23);
+      }
+      fence_async_smem();
+      named_sync(1, TC_HELPERS);
+      if (tid == TC_HELP0) {
+        mbar_arrive(b1_full);
+        TC_STAMP(2);
+      }
+  };
   const long long my_id = tid < P ? a.ids[tid] : 0;
   const float my_w = tid < P ? a.weights[tid] : 0.0f;
   build_plan<TC_THREADS>(pl, a.ids, P, a.E, TC_CAP, a.e_first, a.e_count);
@@ -255,6 +312,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     c_ok[tid] = my_id >= a.e_first && my_id < (long long)a.e_first + a.e_count && my_id < a.E;
     c_w[tid] = my_w;
   }
+  if (warp >= 2) stage_b1();
   const int nseg = pl.nseg;
   const int t1_lo = (int)((long long)blockIdx.x * nseg * TPS1 / G);
   const int t1_hi = (int)((long long)(blockIdx.x + 1) * nseg * TPS1 / G);
@@ -381,63 +439,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   } else {
     // ---------------- helpers: staging, epilogue, combine ----------------
     const int hid = tid - TC_HELP0;  // helper thread 0..191
-    // phase-1 B: every line's terms, one warp per line (rows >= M are zero); the warp holds the whole row, so the
-    // row maximum is a warp reduction
-    if (t1_hi > t1_lo) {
-#pragma unroll
-      for (int r = 0; r < 3; ++r) {
-        const int n = hw + 6 * r;
-        if (n >= TC_LINES) break;
-        uint4 cur[4][XW];
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-#pragma unroll
-          for (int w = 0; w < XW; ++w)
-            cur[u][w] = r < PRE ? xr[r < PRE ? r : 0][u][w]
-                        : (n < a.M ? __ldcg(reinterpret_cast<const uint4*>((const uint8_t*)a.x +
-                                                                           ((size_t)n * H + 16 * (lane + 32 * u)) * 4) + w)
-                                   : make_uint4(0u, 0u, 0u, 0u));
-        float v[4][16];
-        float m = 0.0f;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          if (XBF) {
-#pragma unroll
-            for (int w = 0; w < 2; ++w) {
-              const uint32_t ww[4] = {cur[u][w].x, cur[u][w].y, cur[u][w].z, cur[u][w].w};
-#pragma unroll
-              for (int h = 0; h < 4; ++h) {
-                v[u][8 * w + 2 * h] = bf16_to_f32(ww[h] & 0xFFFFu);
-                v[u][8 * w + 2 * h + 1] = bf16_to_f32(ww[h] >> 16);
-              }
-            }
-          } else {
-#pragma unroll
-            for (int w = 0; w < XW; ++w) {
-              v[u][4 * w] = __uint_as_float(cur[u][w].x);
-              v[u][4 * w + 1] = __uint_as_float(cur[u][w].y);
-              v[u][4 * w + 2] = __uint_as_float(cur[u][w].z);
-              v[u][4 * w + 3] = __uint_as_float(cur[u][w].w);
-            }
-          }
-#pragma unroll
-          for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(v[u][i]));
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        const int e = tc_exponent(m);
-        const float scale = __uint_as_float((uint32_t)(e + 127) << 23);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) tc_write_terms<T1>(breg, N1, n, TC_LINES, lane + 32 * u, v[u], scale);
-        if (lane == 0) linv[n] = __uint_as_float((uint32_t)(127 - e) << 23);
-      }
-      fence_async_smem();
-      named_sync(1, TC_HELPERS);
-      if (hid == 0) {
-        mbar_arrive(b1_full);
-        TC_STAMP(2);
-      }
-    }
     unsigned* seg_done = a.arrive;  // per segment: phase-1 tiles finished (all CTAs), zero between calls
     int tn = 0;
     if (warp < 6) {
@@ -515,7 +516,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       named_sync(1, TC_HELPERS);
       ok = ok && s_ready;
       constexpr int CPL = I / 16 / 16;  // chunks per lane (16 lanes a row)
-      for (int jp = hw; jp < TC_CAP / 2; jp += TC_HELPERS / 32) {
+      for (int jp = hw; 2 * jp < cnt; jp += TC_HELPERS / 32) {  // rows past cnt stay unwritten (never read)
         const int j = 2 * jp + (lane >> 4), sub = lane & 15;
         const bool live = j < cnt;
         const int pair = live ? pl.sorted[first + j] : 0;
@@ -536,10 +537,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         const int e = tc_exponent(m);
         const float scale = __uint_as_float((uint32_t)(e + 127) << 23);
+        if (live)
 #pragma unroll
-        for (int u = 0; u < CPL; ++u)
-          tc_write_terms<TC_TERMS2>(breg + bb * B2BYTES, TC_N2, j, TC_CAP, sub + 16 * u, v[u], scale);
-        if (sub == 0) {
+          for (int u = 0; u < CPL; ++u)
+            tc_write_terms<TC_TERMS2>(breg + bb * B2BYTES, TC_N2, j, TC_CAP, sub + 16 * u, v[u], scale);
+        if (live && sub == 0) {
           spair[bb * TC_CAP + j] = pair;
           sinv[bb * TC_CAP + j] = __uint_as_float((uint32_t)(127 - e) << 23);
         }
