@@ -52,6 +52,7 @@ constexpr int TC_N2 = TC_CAP * TC_TERMS2;
 constexpr int TC_BREGION = 98304;     // phase-1 B (<= 48 rows x 2048) or two phase-2 B buffers (64 rows x <= 768)
 constexpr int TC_XPITCH = 17;         // exchange row pitch (floats)
 constexpr int TC_TMEM_COLS = 128;     // two accumulators of <= 64 columns
+constexpr int TC_MAX_E = 512;         // experts per rank the plan's counting sort holds
 
 struct TcSmem {
   static constexpr int ring = 0;
@@ -165,6 +166,71 @@ D3_DEV void tc_load16(const void* src, bool bf16, size_t i, float (&v)[16]) {
   }
 }
 
+// The plan by counting sort (all TC_THREADS threads; `id` is pair tid's expert id, loaded by the caller): pairs
+// grouped by expert in expert order, segments of one expert and at most `cap` pairs. Within an expert the pairs
+// keep the order their atomic slots came in - every MMA column is computed on its own, so the order changes no
+// result. ecnt / ebase / esegb: shared scratch of TC_MAX_E ints each (e_count <= TC_MAX_E, checked by the host).
+D3_DEV void tc_plan(DecodePlan& pl, int* ecnt, int* ebase, int* esegb, long long id, int P, int E, int cap,
+                    int e_first, int e_count) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  for (int e = tid; e < e_count; e += TC_THREADS) ecnt[e] = 0;
+  int key = -1;
+  if (tid < P) {
+    if (id < 0 || id >= E) record_fault(FAULT_BAD_EXPERT);
+    if (id >= e_first && id < (long long)e_first + e_count && id < E) key = (int)(id - e_first);
+  }
+  __syncthreads();
+  const int slot = key >= 0 ? atomicAdd(ecnt + key, 1) : 0;
+  __syncthreads();
+  if (tid < 32) {
+    // exclusive scans of the pair counts and the segment counts: lane L takes experts 16L .. 16L + 15
+    int pc[TC_MAX_E / 32], sc[TC_MAX_E / 32];
+    int ps = 0, ss = 0;
+#pragma unroll
+    for (int i = 0; i < TC_MAX_E / 32; ++i) {
+      const int e = (TC_MAX_E / 32) * lane + i;
+      const int n = e < e_count ? ecnt[e] : 0;
+      pc[i] = n;
+      sc[i] = (n + cap - 1) / cap;
+      ps += pc[i];
+      ss += sc[i];
+    }
+    int pi = ps, si = ss;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int a = __shfl_up_sync(0xffffffffu, pi, o), b = __shfl_up_sync(0xffffffffu, si, o);
+      if (lane >= o) {
+        pi += a;
+        si += b;
+      }
+    }
+    int pb = pi - ps, sb = si - ss;
+#pragma unroll
+    for (int i = 0; i < TC_MAX_E / 32; ++i) {
+      const int e = (TC_MAX_E / 32) * lane + i;
+      if (e < e_count) {
+        ebase[e] = pb;
+        esegb[e] = sb;
+      }
+      pb += pc[i];
+      sb += sc[i];
+    }
+    if (lane == 31) pl.nseg = si;
+  }
+  __syncthreads();
+  if (key >= 0) pl.sorted[ebase[key] + slot] = tid;
+  for (int e = tid; e < e_count; e += TC_THREADS) {
+    const int n = ecnt[e];
+    for (int j = 0; j * cap < n; ++j) {
+      const int s = esegb[e] + j;
+      pl.seg_expert[s] = e;
+      pl.seg_first[s] = ebase[e] + j * cap;
+      pl.seg_count[s] = min(cap, n - j * cap);
+    }
+  }
+  __syncthreads();
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 template <bool XBF, int NKB2>
 __global__ void __launch_bounds__(TC_THREADS, 1)
@@ -196,6 +262,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   float* sinv = (float*)(smem + TcSmem::sinv);
   int* smax = (int*)(smem + TcSmem::smax);
   __shared__ DecodePlan pl;
+  __shared__ int ecnt[TC_MAX_E], ebase[TC_MAX_E], esegb[TC_MAX_E];
   __shared__ float c_w[DEC_MAX_PAIRS];
   __shared__ unsigned char c_ok[DEC_MAX_PAIRS];
 
@@ -228,6 +295,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   // programmatic dependent launch: inputs and the workspace are touched only after the previous grid has completed
   allow_dependents();
   grid_dependency_wait();
+  if (tid == 0) TC_STAMP(12);
   // phase-1 B rows (lines) of this helper warp: hw, hw + 6, hw + 12; their loads are issued before the plan is built
   // (bf16: all three rows; fp32: the first), so they land while it is
   constexpr int XW = XBF ? 2 : 4;  // 16-byte words per 16-column chunk
@@ -307,7 +375,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   };
   const long long my_id = tid < P ? a.ids[tid] : 0;
   const float my_w = tid < P ? a.weights[tid] : 0.0f;
-  build_plan<TC_THREADS>(pl, a.ids, P, a.E, TC_CAP, a.e_first, a.e_count);
+  if (tid == 0) TC_STAMP(13);
+  tc_plan(pl, ecnt, ebase, esegb, my_id, P, a.E, TC_CAP, a.e_first, a.e_count);
+  if (tid == 0) TC_STAMP(14);
   if (tid < P) {
     c_ok[tid] = my_id >= a.e_first && my_id < (long long)a.e_first + a.e_count && my_id < a.E;
     c_w[tid] = my_w;

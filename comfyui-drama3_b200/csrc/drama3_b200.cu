@@ -522,7 +522,8 @@ static int decode_common(int fmt, const void* x, int x_bf16, int M, int k, int E
   cudaStream_t s = (cudaStream_t)stream;
   // per-channel e4m3: the tensor-core kernel (its phase-2 split needs one CTA per segment at least: at most
   // M * k <= 128 segments)
-  if (fmt == d3::FMT_FP8C && M >= decode_tc_min_lines() && d.sms >= d3::DEC_MAX_PAIRS && decode_tc_enabled())
+  if (fmt == d3::FMT_FP8C && M >= decode_tc_min_lines() && d.sms >= d3::DEC_MAX_PAIRS && e_count <= d3::TC_MAX_E &&
+      decode_tc_enabled())
     return decode_tc(a, d, s);
   switch (fmt) {
     case d3::FMT_FP8:
