@@ -16,6 +16,7 @@
 #include "grouped_mma.cuh"
 #include "moe_decode.cuh"
 #include "decode_tc.cuh"
+#include "decode_tc8.cuh"
 #include "resolve.cuh"
 #include "rotate.cuh"
 #include "route.cuh"
@@ -104,11 +105,12 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 // A 2-D byte tensor [rows, row_bytes] read in boxes of box_bytes x 128 rows, with the shared-memory swizzle of that
 // row width (128, 64 or 32 bytes).
 bool byte_tile_map(CUtensorMap* map, const void* base, uint64_t row_bytes, uint64_t rows, uint32_t box_bytes,
-                   uint32_t box_rows = 128) {
-  const CUtensorMapSwizzle swizzle = box_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
-                                     : box_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
-                                     : box_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
-                                                       : CU_TENSOR_MAP_SWIZZLE_NONE;
+                   uint32_t box_rows = 128, bool swizzled = true) {
+  const CUtensorMapSwizzle swizzle = !swizzled           ? CU_TENSOR_MAP_SWIZZLE_NONE
+                                     : box_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                     : box_bytes == 64  ? CU_TENSOR_MAP_SWIZZLE_64B
+                                     : box_bytes == 32  ? CU_TENSOR_MAP_SWIZZLE_32B
+                                                        : CU_TENSOR_MAP_SWIZZLE_NONE;
   PFN_cuTensorMapEncodeTiled_v12000 fn = tensor_map_encoder();
   if (!fn) return false;
   cuuint64_t dims[2] = {row_bytes, rows};
@@ -487,6 +489,28 @@ static int decode_tc(const d3::DecodeArgs& a, const DeviceInfo& d, cudaStream_t 
   }
 }
 
+template <bool XBF, int NKB2>
+static int decode_tc8_launch(const d3::DecodeArgs& a, const CUtensorMap& m13, const CUtensorMap& m2,
+                             const DeviceInfo& d, cudaStream_t s) {
+  auto kern = d3::moe_decode_tc8_kernel<XBF, NKB2>;
+  const int smem = d3::T8Smem::launch;
+  if (int st = allow_smem(kern, smem)) return st;
+  return launch(kern, dim3(d.sms), dim3(d3::TC_THREADS), smem, s, true, m13, m2, a);
+}
+
+// W4A8 on the tensor cores: packed rows in boxes of 64 bytes (128 int4 columns), unswizzled (the converter warps
+// read them row by row)
+static int decode_tc8(const d3::DecodeArgs& a, const DeviceInfo& d, cudaStream_t s) {
+  CUtensorMap m13, m2;
+  if (!byte_tile_map(&m13, a.w13, (uint64_t)a.H / 2, (uint64_t)a.e_count * 2 * a.I, 64, 64, false)) return D3_ERR_ARG;
+  if (!byte_tile_map(&m2, a.w2, (uint64_t)a.I / 2, (uint64_t)a.e_count * a.H, 64, 128, false)) return D3_ERR_ARG;
+  switch (a.I) {
+    case 512: return a.x_bf16 ? decode_tc8_launch<true, 4>(a, m13, m2, d, s) : decode_tc8_launch<false, 4>(a, m13, m2, d, s);
+    case 768: return a.x_bf16 ? decode_tc8_launch<true, 6>(a, m13, m2, d, s) : decode_tc8_launch<false, 6>(a, m13, m2, d, s);
+    default: return D3_ERR_ARG;
+  }
+}
+
 static int decode_common(int fmt, const void* x, int x_bf16, int M, int k, int E, int e_first, int e_count, int H,
                          int I, const int64_t* ids, const float* weights, const uint8_t* w13, const void* s13,
                          const float* c13, const uint8_t* w2, const void* s2, const float* c2,
@@ -525,6 +549,9 @@ static int decode_common(int fmt, const void* x, int x_bf16, int M, int k, int E
   if (fmt == d3::FMT_FP8C && M >= decode_tc_min_lines() && d.sms >= d3::DEC_MAX_PAIRS && e_count <= d3::TC_MAX_E &&
       decode_tc_enabled())
     return decode_tc(a, d, s);
+  if (fmt == d3::FMT_W4A8 && M >= decode_tc_min_lines() && d.sms >= d3::DEC_MAX_PAIRS && e_count <= d3::TC_MAX_E &&
+      decode_tc_enabled())
+    return decode_tc8(a, d, s);
   switch (fmt) {
     case d3::FMT_FP8:
       return x_bf16 ? decode_nkc<d3::FMT_FP8, true>(a, d, s) : decode_nkc<d3::FMT_FP8, false>(a, d, s);
