@@ -124,6 +124,22 @@ D3_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// The int8 activation quantization of N values: rint(x / s) clipped to +-127 (s = max|x| / 127; 0 when s == 0), with
+// the quotient rounded correctly but without a division: r = __frcp_rn(s), y = x * r, then one correction step
+// y' = y + r (x - y s) with fused multiply-adds (Markstein, "Computation of elementary functions on the IBM RISC
+// System/6000 processor", IBM J. Res. Dev. 34(1), 1990), which gives the correctly rounded quotient from a correctly
+// rounded reciprocal. Rounding x * r alone flips ties: with bf16 rows, x = max / 2 (x / s = 63.5) is common. A
+// division, or an exact fix-up branch, in these loops made them several times slower.
+template <int N>
+D3_DEV void quant_i8_n(const float* v, float s, float r, float* q) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    const float y = v[i] * r;
+    const float yq = fmaf(fmaf(-y, s, v[i]), r, y);
+    q[i] = s > 0.0f ? fminf(127.0f, fmaxf(-127.0f, rintf(yq))) : 0.0f;
+  }
+}
+
 D3_DEV uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));

@@ -9,22 +9,24 @@
 //     columns go first and the odd ones after; the B rows are staged with the same order, and a dot product does
 //     not depend on it. No shift back is needed: the epilogue folds the 1/16 into the scales.
 //   * B: the lines' rows (phase 1) or the segment's pairs' a1 rows (phase 2), each quantized to int8 per row
-//     (s = max|x| / 127, q = rint(x / s), IEEE division, clip +-127) - one exact term.
+//     (s = max|x| / 127, q = rint(x * (1 / s)) clipped to +-127: quant_i8_n) - one exact term.
 //   * Every 128-column group has its own bf16 scale per row, so each group's MMAs (4 of K = 32) go to a TMEM region
-//     of their own (16 columns: the lines or pairs) and the epilogue warps fold region after region into fp32
-//     registers, acc += group scale x int32 sum, four regions in flight.
+//     of their own (16 columns: the lines or pairs); a tile's groups fill 16 regions (256 columns), two tiles in
+//     flight, and the epilogue warps fold a finished tile's regions into fp32 registers, acc += group scale x int32
+//     sum (a fold per group, handing each region back at once, measured slower: the round trip paced the MMAs).
 #pragma once
 #include "decode_tc.cuh"
 
 namespace d3 {
 
-constexpr int T8_RAW_ST = 8;         // raw ring: 128 rows x 64 packed bytes = 128 int4 columns a stage
+constexpr int T8_RAW_ST = 6;         // raw ring: 128 rows x 64 packed bytes = 128 int4 columns a stage
 constexpr int T8_RAW_BYTES = 8192;
-constexpr int T8_A_ST = 4;           // int8 A ring: 128 rows x 128 bytes
-constexpr int T8_REGIONS = 4;        // TMEM accumulators of 16 columns, one per 128-column group in flight
+constexpr int T8_A_ST = 8;           // int8 A ring: 128 rows x 128 bytes (deep: a stage comes back only once its
+                                     // MMAs have completed)
+constexpr int T8_BUF_COLS = 256;     // TMEM columns of one tile: 16 groups x 16 columns
 constexpr int T8_CONV0 = 192;        // converter threads: warps 6-7
 constexpr int T8_BREGION = 32768;    // phase-1 B (16 lines x 2048) or two phase-2 B buffers (16 pairs x <= 768)
-constexpr int T8_TMEM_COLS = 64;
+constexpr int T8_TMEM_COLS = 512;   // two tiles
 
 struct T8Smem {
   static constexpr int raw = 0;
@@ -60,32 +62,74 @@ D3_DEV void t8_load32(const void* src, bool bf16, size_t i, float (&v)[32]) {
   tc_load16(src, bf16, i + 16, (float(&)[16])v[16]);
 }
 
-// int8 of v / s (IEEE division, round half even, clip +-127; 0 when s == 0) for 4 values, packed little-endian.
-D3_DEV uint32_t t8_q4(float v0, float v1, float v2, float v3, float s) {
-  const float q[4] = {v0, v1, v2, v3};
-  uint32_t r = 0;
+// The bytes of one 32-column chunk of int8 codes in the A stages' column order: the 16 even columns, then the 16
+// odd ones (byte i of word p: column 8p + 2i, then 8p + 2i + 1).
+D3_DEV void t8_store_chunk(uint8_t* b, int rows, int n, int c, const float (&q)[32]) {
+  uint32_t w[8];
 #pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const float t = s > 0.0f ? fminf(127.0f, fmaxf(-127.0f, rintf(__fdiv_rn(q[u], s)))) : 0.0f;
-    r |= ((uint32_t)(int)t & 0xFFu) << (8 * u);
-  }
-  return r;
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      uint32_t r = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) r |= ((uint32_t)(int)q[8 * p + 2 * i + h] & 0xFFu) << (8 * i);
+      w[4 * h + p] = r;
+    }
+  *reinterpret_cast<uint4*>(b + tc_b_offset(rows, n, 2 * c)) = make_uint4(w[0], w[1], w[2], w[3]);
+  *reinterpret_cast<uint4*>(b + tc_b_offset(rows, n, 2 * c + 1)) = make_uint4(w[4], w[5], w[6], w[7]);
 }
 
-// One 32-column chunk c of a B row n, quantized by s, in the A stages' column order (the 16 even columns, then the
-// 16 odd ones), into a K-major 128-byte-swizzled operand of `rows` rows.
+// One 32-column chunk c of a B row n quantized to int8 by s (quant_i8_n), into a K-major 128-byte-swizzled operand
+// of `rows` rows in the A stages' column order.
 D3_DEV void t8_write_chunk(uint8_t* b, int rows, int n, int c, const float (&v)[32], float s) {
-  uint4 ev, od;
-  ev.x = t8_q4(v[0], v[2], v[4], v[6], s);
-  ev.y = t8_q4(v[8], v[10], v[12], v[14], s);
-  ev.z = t8_q4(v[16], v[18], v[20], v[22], s);
-  ev.w = t8_q4(v[24], v[26], v[28], v[30], s);
-  od.x = t8_q4(v[1], v[3], v[5], v[7], s);
-  od.y = t8_q4(v[9], v[11], v[13], v[15], s);
-  od.z = t8_q4(v[17], v[19], v[21], v[23], s);
-  od.w = t8_q4(v[25], v[27], v[29], v[31], s);
-  *reinterpret_cast<uint4*>(b + tc_b_offset(rows, n, 2 * c)) = ev;
-  *reinterpret_cast<uint4*>(b + tc_b_offset(rows, n, 2 * c + 1)) = od;
+  float q[32];
+  quant_i8_n<32>(v, s, __frcp_rn(s), q);
+  t8_store_chunk(b, rows, n, c, q);
+}
+
+// 16 consecutive TMEM columns of this warp's lanes, without waiting (tcgen05.wait::ld before the registers are read).
+D3_DEV void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+// The epilogue's fold of tile tn (TMEM buffer tn & 1, NK groups of 16 int32 columns at `taddr` = this warp's lanes):
+// acc[j] = sum over groups g of scale[g] x column 16g + j, the bf16 group scales packed two per word in gw. Waits
+// (bounded) for the tile, then hands the buffer back. Four groups are loaded per wait.
+template <int NK>
+D3_DEV void t8_fold(float (&acc)[16], const uint32_t* gw, uint32_t taddr, int tn, uint64_t* acc_full,
+                    uint64_t* acc_empty, bool& ok, int lane) {
+  const int buf = tn & 1;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
+  if (ok) ok = mbar_wait(acc_full + buf, (tn >> 1) & 1);
+  ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective: the warp agrees
+  tc_fence_after();
+  if (ok) {
+#pragma unroll
+    for (int k0 = 0; k0 < NK; k0 += 4) {
+      uint32_t v[4][16];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (k0 + u < NK) tmem_ld16_async(taddr + buf * T8_BUF_COLS + (k0 + u) * 16, v[u]);
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (k0 + u < NK) {
+          const int kb = k0 + u;
+          const float gs = bf16_to_f32((kb & 1) ? gw[kb >> 1] >> 16 : gw[kb >> 1] & 0xFFFFu);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[j] = fmaf((float)(int)v[u][j], gs, acc[j]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(acc_empty + buf);
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -110,15 +154,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t* a_full = raw_empty + T8_RAW_ST;
   uint64_t* a_empty = a_full + T8_A_ST;
   uint64_t* acc_full = a_empty + T8_A_ST;
-  uint64_t* acc_empty = acc_full + T8_REGIONS;
-  uint64_t* b1_full = acc_empty + T8_REGIONS;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* b1_full = acc_empty + 2;
   uint64_t* b2_full = b1_full + 1;
   uint32_t* tmem_slot = (uint32_t*)(smem + T8Smem::tmem);
   float* linv = (float*)(smem + T8Smem::linv);
   int* spair = (int*)(smem + T8Smem::spair);
   float* sinv = (float*)(smem + T8Smem::sinv);
   __shared__ DecodePlan pl;
-  __shared__ int ecnt[TC_MAX_E], ebase[TC_MAX_E], esegb[TC_MAX_E];
+  // the plan's counting-sort scratch lives in the raw ring, which no copy touches before the plan is built
+  int* ecnt = (int*)raw;
+  int* ebase = ecnt + TC_MAX_E;
+  int* esegb = ebase + TC_MAX_E;
   __shared__ float c_w[DEC_MAX_PAIRS];
   __shared__ unsigned char c_ok[DEC_MAX_PAIRS];
 
@@ -133,7 +180,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       mbar_init(a_full + s, 2);
       mbar_init(a_empty + s, 1);
     }
-    for (int s = 0; s < T8_REGIONS; ++s) {
+    for (int s = 0; s < 2; ++s) {
       mbar_init(acc_full + s, 1);
       mbar_init(acc_empty + s, 4);
     }
@@ -199,30 +246,32 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (!mbar_wait(raw_full + d % T8_RAW_ST, (d / T8_RAW_ST) & 1)) break;
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer: one group of 4 MMAs (K = 128) per TMEM region ----------------
+    // ---------------- MMA issuer: a tile's groups (4 MMAs of K = 32 each) into its 16-column TMEM regions ----------
     if (lane == 0) {
       const uint32_t a_s = smem_u32(astage), b_s = smem_u32(breg);
       const uint32_t idesc = t8_idesc(TC_CAP);
-      int c = 0;
+      int c = 0, tn = 0;
       if (t1_hi > t1_lo) ok = mbar_wait(b1_full, 0);
       tc_fence_after();
-      // the 4 MMAs (K = 128) of one 128-column group into the next TMEM region
-      auto group = [&](uint32_t bbase, int kb) {
-        const int st = c % T8_A_ST, reg = c % T8_REGIONS;
-        ok = mbar_wait(a_full + st, (c / T8_A_ST) & 1);
-        ok = ok && mbar_wait(acc_empty + reg, ((c / T8_REGIONS) & 1) ^ 1);
-        if (!ok) return;
+      auto tile = [&](uint32_t bbase, int nk) {
+        const int buf = tn & 1;
+        ok = mbar_wait(acc_empty + buf, ((tn >> 1) & 1) ^ 1);
         tc_fence_after();
+        for (int kb = 0; kb < nk && ok; ++kb, ++c) {
+          const int st = c % T8_A_ST;
+          ok = mbar_wait(a_full + st, (c / T8_A_ST) & 1);
+          if (!ok) break;
+          tc_fence_after();
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks)
-          umma_i8(tmem + reg * 16, umma_desc_sw128(a_s + st * TC_ABYTES + 32 * ks),
-                  umma_desc_sw128(bbase + kb * TC_CAP * 128 + 32 * ks), idesc, ks != 0 ? 1u : 0u);
-        umma_commit(a_empty + st);
-        umma_commit(acc_full + reg);
-        ++c;
+          for (int ks = 0; ks < 4; ++ks)
+            umma_i8(tmem + buf * T8_BUF_COLS + kb * 16, umma_desc_sw128(a_s + st * TC_ABYTES + 32 * ks),
+                    umma_desc_sw128(bbase + kb * TC_CAP * 128 + 32 * ks), idesc, ks != 0 ? 1u : 0u);
+          umma_commit(a_empty + st);
+        }
+        umma_commit(acc_full + buf);
+        ++tn;
       };
-      for (int t = t1_lo; t < t1_hi && ok; ++t)
-        for (int kb = 0; kb < NKB1 && ok; ++kb) group(b_s, kb);
+      for (int t = t1_lo; t < t1_hi && ok; ++t) tile(b_s, NKB1);
       int cur = -1;
       for (int t = t2_lo; t < t2_hi && ok; ++t) {
         const int s = t / TPS2, bb = s - s2a;
@@ -236,7 +285,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           tc_fence_after();
           cur = s;
         }
-        for (int kb = 0; kb < NKB2 && ok; ++kb) group(b_s + bb * B2BYTES, kb);
+        tile(b_s + bb * B2BYTES, NKB2);
       }
     }
   } else if (warp >= 6) {
@@ -249,13 +298,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const uint8_t* src = raw + rs * T8_RAW_BYTES;
       uint8_t* dst = astage + st * TC_ABYTES;
       if (ok) {
+        // all 8 loads first: stores to the A stage could alias them for all the compiler knows
+        uint4 w[8];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) w[m] = *reinterpret_cast<const uint4*>(src + 16 * (ct + 64 * m));
 #pragma unroll
         for (int m = 0; m < 8; ++m) {
           const int u = ct + 64 * m, row = u >> 2, ch = u & 3;  // 16 packed bytes: 32 columns of one row
-          const uint4 w = *reinterpret_cast<const uint4*>(src + 16 * u);
-          const uint4 lo = make_uint4((w.x << 4) & 0xF0F0F0F0u, (w.y << 4) & 0xF0F0F0F0u, (w.z << 4) & 0xF0F0F0F0u,
-                                      (w.w << 4) & 0xF0F0F0F0u);
-          const uint4 hi = make_uint4(w.x & 0xF0F0F0F0u, w.y & 0xF0F0F0F0u, w.z & 0xF0F0F0F0u, w.w & 0xF0F0F0F0u);
+          const uint4 lo = make_uint4((w[m].x << 4) & 0xF0F0F0F0u, (w[m].y << 4) & 0xF0F0F0F0u,
+                                      (w[m].z << 4) & 0xF0F0F0F0u, (w[m].w << 4) & 0xF0F0F0F0u);
+          const uint4 hi = make_uint4(w[m].x & 0xF0F0F0F0u, w[m].y & 0xF0F0F0F0u, w[m].z & 0xF0F0F0F0u,
+                                      w[m].w & 0xF0F0F0F0u);
           *reinterpret_cast<uint4*>(dst + tc_b_offset(128, row, 2 * ch)) = lo;
           *reinterpret_cast<uint4*>(dst + tc_b_offset(128, row, 2 * ch + 1)) = hi;
         }
@@ -271,27 +324,59 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   if (warp >= 2) {
     // ---------------- helpers (warps 2-5: staging and epilogue; 2-7: barriers and combine) ----------------
     const int hid = tid - TC_HELP0;
-    int g = 0;  // TMEM region sequence
+    int tn = 0;  // tile sequence (TMEM buffer tn & 1)
     if (warp < 6) {
       const int hw = warp - 2, quarter = warp & 3, row = 32 * quarter + lane;
       const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
       // phase-1 B: every line quantized to int8, one warp per line (lines past M stay unwritten: never read)
       if (t1_hi > t1_lo) {
-        for (int n = hw; n < a.M; n += 4) {
-          float v[2][32];
-          float m = 0.0f;
+        // the warp's lines hw, hw + 4, ...; a lane holds columns 32 lane .. + 31 and 1024 + 32 lane .. + 31 of a
+        // line. The loads of NB lines are issued together, then the lines are quantized one by one.
+        constexpr int EB = XBF ? 2 : 4, XW = 64 * EB / 16, NB = XBF ? 4 : 1;
+        for (int n0 = hw; n0 < a.M; n0 += 4 * NB) {
+          uint4 xr[NB][XW];
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            t8_load32(a.x, a.x_bf16 != 0, (size_t)n * H + 32 * (lane + 32 * u), v[u]);
+          for (int b = 0; b < NB; ++b) {
+            const int n = n0 + 4 * b;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) m = fmaxf(m, fabsf(v[u][i]));
+            for (int w = 0; w < XW; ++w) {
+              const int u = w / (XW / 2), k = w % (XW / 2);
+              xr[b][w] = n < a.M ? __ldcg(reinterpret_cast<const uint4*>(
+                                       (const uint8_t*)a.x + ((size_t)n * H + 32 * (lane + 32 * u)) * EB + 16 * k))
+                                 : make_uint4(0u, 0u, 0u, 0u);
+            }
           }
 #pragma unroll
-          for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-          const float s = __fdiv_rn(m, 127.0f);
+          for (int b = 0; b < NB; ++b) {
+            const int n = n0 + 4 * b;
+            if (n >= a.M) break;
+            float v[2][32];
+            float m = 0.0f;
 #pragma unroll
-          for (int u = 0; u < 2; ++u) t8_write_chunk(breg, TC_LINES, n, lane + 32 * u, v[u], s);
-          if (lane == 0) linv[n] = s;
+            for (int w = 0; w < XW; ++w) {
+              const int u = w / (XW / 2), k = w % (XW / 2);
+              const uint32_t ww[4] = {xr[b][w].x, xr[b][w].y, xr[b][w].z, xr[b][w].w};
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                if (XBF) {
+                  v[u][8 * k + 2 * h] = bf16_to_f32(ww[h] & 0xFFFFu);
+                  v[u][8 * k + 2 * h + 1] = bf16_to_f32(ww[h] >> 16);
+                } else {
+                  v[u][4 * k + h] = __uint_as_float(ww[h]);
+                }
+              }
+            }
+#pragma unroll
+            for (int u = 0; u < 2; ++u)
+#pragma unroll
+              for (int i = 0; i < 32; ++i) m = fmaxf(m, fabsf(v[u][i]));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            const float s = __fdiv_rn(m, 127.0f);
+#pragma unroll
+            for (int u = 0; u < 2; ++u) t8_write_chunk(breg, TC_LINES, n, lane + 32 * u, v[u], s);
+            if (lane == 0) linv[n] = s;
+          }
         }
         fence_async_smem();
         named_sync(3, TC_EPI);
@@ -307,23 +392,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const uint4 g0 = __ldg(gp), g1 = __ldg(gp + 1);
         const uint32_t gw[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
         float acc[TC_LINES];
-#pragma unroll
-        for (int j = 0; j < TC_LINES; ++j) acc[j] = 0.0f;
-#pragma unroll
-        for (int kb = 0; kb < NKB1; ++kb, ++g) {
-          const int reg = g % T8_REGIONS;
-          if (ok) ok = mbar_wait(acc_full + reg, (g / T8_REGIONS) & 1);
-          ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective: the warp agrees
-          tc_fence_after();
-          float v[16];
-          if (ok) tmem_ld16(tmem + lane_base + reg * 16, v);
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(acc_empty + reg);
-          const float gs = bf16_to_f32((kb & 1) ? gw[kb >> 1] >> 16 : gw[kb >> 1] & 0xFFFFu);
-#pragma unroll
-          for (int j = 0; j < TC_LINES; ++j) acc[j] = fmaf((float)__float_as_int(v[j]), gs, acc[j]);
-        }
+        t8_fold<NKB1>(acc, gw, tmem + lane_base, tn, acc_full, acc_empty, ok, lane);
+        ++tn;
 #pragma unroll
         for (int l = 0; l < TC_LINES; ++l) xchg[row * TC_XPITCH + l] = ok ? acc[l] : 0.0f;
         named_sync(3, TC_EPI);
@@ -399,23 +469,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
         for (int q = 0; q < NKB2 / 2; ++q) gw[q] = __ldg(gp + q);
         float acc[TC_CAP];
-#pragma unroll
-        for (int j = 0; j < TC_CAP; ++j) acc[j] = 0.0f;
-#pragma unroll
-        for (int kb = 0; kb < NKB2; ++kb, ++g) {
-          const int reg = g % T8_REGIONS;
-          if (ok) ok = mbar_wait(acc_full + reg, (g / T8_REGIONS) & 1);
-          ok = __all_sync(0xffffffffu, ok);
-          tc_fence_after();
-          float v[16];
-          if (ok) tmem_ld16(tmem + lane_base + reg * 16, v);
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(acc_empty + reg);
-          const float gs = bf16_to_f32((kb & 1) ? gw[kb >> 1] >> 16 : gw[kb >> 1] & 0xFFFFu);
-#pragma unroll
-          for (int j = 0; j < TC_CAP; ++j) acc[j] = fmaf((float)__float_as_int(v[j]), gs, acc[j]);
-        }
+        t8_fold<NKB2>(acc, gw, tmem + lane_base, tn, acc_full, acc_empty, ok, lane);
+        ++tn;
         if (ok && bb <= 1) {
           const int cnt = pl.seg_count[s];
 #pragma unroll

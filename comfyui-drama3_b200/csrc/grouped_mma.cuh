@@ -230,10 +230,12 @@ __global__ void __launch_bounds__(256) gm_stage_kernel(const void* __restrict__ 
       if (q >= nq) break;
       uint32_t hw[4], lw[4];
       if (int8q) {
+        float qv[8];
+        quant_i8_n<8>(v[q], qs, __frcp_rn(qs), qv);
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const float q0 = qs > 0.0f ? fminf(127.0f, fmaxf(-127.0f, rintf(__fdiv_rn(v[q][2 * u], qs)))) : 0.0f;
-          const float q1 = qs > 0.0f ? fminf(127.0f, fmaxf(-127.0f, rintf(__fdiv_rn(v[q][2 * u + 1], qs)))) : 0.0f;
+          const float q0 = qv[2 * u];
+          const float q1 = qv[2 * u + 1];
           hw[u] = (uint32_t)__half_as_ushort(__float2half_rn(q0)) |
                   ((uint32_t)__half_as_ushort(__float2half_rn(q1)) << 16);
           lw[u] = 0u;

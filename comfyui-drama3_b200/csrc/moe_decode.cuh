@@ -242,11 +242,13 @@ D3_DEV void stage_rows(__half* xin, float* inv, int* rowmax, float* wscratch, co
     if (int8q) {
       // per-row int8 quantization (W4A8 / W6A8): s = max|x| / 127, q = clamp(rint(x / s), +-127), IEEE division
       const float s = __fdiv_rn(__int_as_float(rowmax[j]), 127.0f);
+      float qv[8];
+      quant_i8_n<8>(v, s, __frcp_rn(s), qv);
       uint32_t hw[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const float q0 = s > 0.0f ? fminf(127.0f, fmaxf(-127.0f, rintf(__fdiv_rn(v[2 * u], s)))) : 0.0f;
-        const float q1 = s > 0.0f ? fminf(127.0f, fmaxf(-127.0f, rintf(__fdiv_rn(v[2 * u + 1], s)))) : 0.0f;
+        const float q0 = qv[2 * u];
+        const float q1 = qv[2 * u + 1];
         hw[u] = (uint32_t)__half_as_ushort(__float2half_rn(q0)) |
                 ((uint32_t)__half_as_ushort(__float2half_rn(q1)) << 16);
       }
