@@ -13,8 +13,8 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent
-SOURCES = [HERE / "csrc" / "drama3_b200.cu"]
-DEPENDS = sorted((HERE / "csrc").glob("*.cu*")) + [ROOT / "include" / "drama3_b200.h"]
+SOURCES = [HERE / "csrc" / "drama3_b200.cu", HERE / "csrc" / "pack.cpp"]
+DEPENDS = sorted((HERE / "csrc").glob("*.c*")) + [ROOT / "include" / "drama3_b200.h"]
 OUTPUT = HERE / "drama3_b200" / "libdrama3_b200.so"
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
               "-shared", "-Xptxas", "-warn-spills", "-diag-suppress", "177,128"]

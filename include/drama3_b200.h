@@ -182,6 +182,19 @@ int d3_moe_decode_ep(int fmt, const void* x, int x_bf16, int M, int k, int E, in
  * writes out [M, H] bf16 (8-byte aligned, H a multiple of 4) = the partials summed in rank order, and advances the
  * counter. Every rank makes the same calls in the same order; M <= m_max and H == h, else nothing is exchanged and
  * D3_FAULT_EXCHANGE is set. No counterpart in the reference (one GPU). */
+/* Host-side packers for the BASELINE layouts (CPU, no device work): float32 rows [rows, K] ->
+ *   d3_pack_fp8c: e4m3 bytes [rows, K] (nearest, ties to even, saturating at +-448) and fp32 row scales
+ *                 [rows] = absmax / 448 (1 for an all-zero row), the per-channel fp8 layout;
+ *   d3_pack_wa8:  bits 4: two codes per byte along K (low nibble first); bits 6: four codes per three bytes
+ *                 (little-endian 24-bit words), and bf16 scales [rows, K / 128] = absmax / qmax per 128 columns
+ *                 (qmax 7 / 31; 1 for an all-zero group), codes rint(x / scale) clipped to +-qmax (BASELINE
+ *                 configs[2], [3]). K % 128 == 0.
+ * Rows are split across `threads` host threads (<= 0: all hardware threads). Plain rounding: the repository's
+ * reference packers' arithmetic byte for byte. No counterpart in the reference, whose converter
+ * (tools/convert.py:48-82) quantizes through comfy_kitchen into its own layouts. */
+int d3_pack_fp8c(const float* w, int64_t rows, int K, uint8_t* codes, float* scales, int threads);
+int d3_pack_wa8(const float* w, int64_t rows, int K, int bits, uint8_t* packed, uint16_t* scales, int threads);
+
 size_t d3_ep_exchange_bytes(int world, int m_max, int H);
 int d3_ep_reduce(const void* exchange, int M, int H, void* out, void* stream);
 int d3_ipc_handle(const void* ptr, void* handle /* 64 bytes */, size_t* offset);
