@@ -48,6 +48,9 @@ SIGNATURES = {
     "d3_moe_decode_static": (_i, [_i, _p, _i, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
     "d3_moe_decode_ep": (_i, [_i, _p, _i, _i, _i, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
                               _p, _sz, _p]),
+    "d3_pack_fp8_blocks": (_i, [_p, ctypes.c_int64, _i, _p, _p, _i]),
+    "d3_pack_int8_convrot": (_i, [_p, ctypes.c_int64, _i, _p, _p, _i]),
+    "d3_pack_codes": (_i, [_p, ctypes.c_int64, _i, _i, _p, _p, _p, _p, _i]),
     "d3_pack_fp8c": (_i, [_p, ctypes.c_int64, _i, _p, _p, _i]),
     "d3_pack_wa8": (_i, [_p, ctypes.c_int64, _i, _i, _p, _p, _i]),
     "d3_ep_exchange_bytes": (_sz, [_i, _i, _i]),

@@ -182,16 +182,32 @@ int d3_moe_decode_ep(int fmt, const void* x, int x_bf16, int M, int k, int E, in
  * writes out [M, H] bf16 (8-byte aligned, H a multiple of 4) = the partials summed in rank order, and advances the
  * counter. Every rank makes the same calls in the same order; M <= m_max and H == h, else nothing is exchanged and
  * D3_FAULT_EXCHANGE is set. No counterpart in the reference (one GPU). */
-/* Host-side packers for the BASELINE layouts (CPU, no device work): float32 rows [rows, K] ->
- *   d3_pack_fp8c: e4m3 bytes [rows, K] (nearest, ties to even, saturating at +-448) and fp32 row scales
- *                 [rows] = absmax / 448 (1 for an all-zero row), the per-channel fp8 layout;
- *   d3_pack_wa8:  bits 4: two codes per byte along K (low nibble first); bits 6: four codes per three bytes
- *                 (little-endian 24-bit words), and bf16 scales [rows, K / 128] = absmax / qmax per 128 columns
- *                 (qmax 7 / 31; 1 for an all-zero group), codes rint(x / scale) clipped to +-qmax (BASELINE
- *                 configs[2], [3]). K % 128 == 0.
- * Rows are split across `threads` host threads (<= 0: all hardware threads). Plain rounding: the repository's
- * reference packers' arithmetic byte for byte. No counterpart in the reference, whose converter
- * (tools/convert.py:48-82) quantizes through comfy_kitchen into its own layouts. */
+/* Host-side packers (CPU, no device work), float32 rows w [rows, K] -> the expert layouts the kernels read, by plain
+ * nearest rounding (round half to even throughout). Rows are split across `threads` host threads (<= 0: all
+ * hardware threads). Inputs are finite. They replace the converter step tools/convert.py:48-82,179-215, whose own
+ * quantizers (comfy_kitchen, absent) are not reproduced: the codes here are the nearest ones, not GPTQ's.
+ *   d3_pack_fp8_blocks:   (fp8, tools/convert.py:179-189) e4m3 [rows, K] and fp32 128x128 block scales
+ *                         [rows / 128, K / 128] = block absmax / 448 (1 for an all-zero block); rows, K % 128 == 0.
+ *   d3_pack_int8_convrot: (int8, tools/convert.py:48-53) each 256-column group times the normalized 256-point
+ *                         Hadamard matrix (drama3/offload.py:170-176), then int8 [rows, K] = rint(r / s) clipped to
+ *                         +-127 with fp32 row scales s = absmax(r) / 127; K % 256 == 0.
+ *   d3_pack_codes:        (w4 / w6, tools/convert.py:61-82; the layout drama3/kernels.py:466-483 decodes) rotated
+ *                         as int8, t = r / s_channel (s_channel = absmax(r) / 127), e4m3 group scales per 16 columns
+ *                         g = max(absmax(t) / top, 2^-6) (top = max |codebook| for bits 4, 31 for bits 6); bits 4:
+ *                         the code c (first of equal distances) whose clip(rint(codebook[c] g), +-127) is nearest to
+ *                         t, nibbles two per byte (low nibble first) [rows, K / 2]; bits 6: c = clip(rint(t / g),
+ *                         -32, 31) + 32 as the same nibble plane followed by a 2-bit plane of c >> 4, four per byte
+ *                         [rows, K / 4]. codebook: 16 floats (bits 4 only). K % 256 == 0.
+ *   d3_pack_fp8c:         (BASELINE configs[1]) e4m3 [rows, K] (saturating at +-448) and fp32 row scales [rows] =
+ *                         absmax / 448 (1 for an all-zero row).
+ *   d3_pack_wa8:          ([3]) bits 4: two codes per byte along K (low nibble first); bits 6:
+ *                         four codes per three bytes (little-endian 24-bit words); bf16 scales [rows, K / 128] =
+ *                         absmax / qmax per 128 columns (qmax 7 / 31; 1 for an all-zero group), codes rint(x / scale)
+ *                         clipped to +-qmax. K % 128 == 0. */
+int d3_pack_fp8_blocks(const float* w, int64_t rows, int K, uint8_t* codes, float* scales, int threads);
+int d3_pack_int8_convrot(const float* w, int64_t rows, int K, int8_t* q, float* scales, int threads);
+int d3_pack_codes(const float* w, int64_t rows, int K, int bits, const float* codebook, uint8_t* codes,
+                  uint8_t* group_scales, float* s_channel, int threads);
 int d3_pack_fp8c(const float* w, int64_t rows, int K, uint8_t* codes, float* scales, int threads);
 int d3_pack_wa8(const float* w, int64_t rows, int K, int bits, uint8_t* packed, uint16_t* scales, int threads);
 

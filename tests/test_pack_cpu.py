@@ -1,6 +1,8 @@
-"""The native packers (d3_pack_fp8c, d3_pack_wa8 in csrc/pack.cpp, host code) byte for byte against the oracle's
-quantizers (oracle.moe.quantize_fp8_channel, quantize_wa8): random experts, all-zero rows and groups, exact ties of
-the rounding, saturation, tiny negatives, and several thread splits."""
+"""The native packers (csrc/pack.cpp, host code) byte for byte against the oracle's quantizers: the reference's
+layouts (oracle.moe.make_bank: fp8 block scales, int8 ConvRot, w4 / w6 codes) and the BASELINE ones
+(quantize_fp8_channel, quantize_wa8), on random experts, all-zero rows, blocks and groups, exact ties of the rounding,
+saturation, tiny negatives, and several thread splits; plus the relative error of what they pack, the check the
+reference's converter prints (tools/convert.py:102-109)."""
 import numpy as np
 import pytest
 import torch
@@ -102,4 +104,86 @@ def test_bad_arguments_raise():
     with pytest.raises(_lib.D3Error):
         pack.pack_wa8(torch.zeros((4, 256)), 5)
     with pytest.raises(ValueError):
-        pack.pack_bank("fp8", w)
+        pack.pack_bank("nf4", w)
+
+
+def same(got, want):
+    got, want = np.asarray(got), np.asarray(want)
+    return (got.shape == want.shape and got.dtype == want.dtype
+            and np.array_equal(got.view(np.uint8), want.view(np.uint8)))
+
+
+@pytest.mark.parametrize("kind", ["fp8", "int8", "w4", "w6"])
+@pytest.mark.parametrize("threads", [1, 3, 0])
+def test_reference_layouts_random_experts(kind, threads):
+    w = rows((3, 256, 768), 20)
+    got = pack.pack_bank(kind, torch.from_numpy(w), threads)
+    want = moe.make_bank(kind, w)
+    assert sorted(got) == sorted(want)
+    for name in want:
+        assert same(got[name].numpy(), want[name]), name
+
+
+@pytest.mark.parametrize("kind", ["fp8", "int8", "w4", "w6"])
+def test_reference_layouts_edge_rows(kind):
+    """All-zero rows and blocks (scale 1; fp8 code 0, int8 0, w4 the first code of the all-zero candidates, w6 32),
+    large and tiny magnitudes in one row, and sign-flipped copies."""
+    w = rows((1, 384, 512), 21)
+    w[0, :128, :128] = 0.0  # a zero fp8 block
+    w[0, 130] = 0.0  # a zero row
+    w[0, 131] *= np.float32(1e4)
+    w[0, 132, ::7] *= np.float32(1e-6)
+    w[0, 200:300] = -w[0, 100:200]
+    got = pack.pack_bank(kind, torch.from_numpy(w), 2)
+    want = moe.make_bank(kind, w)
+    for name in want:
+        assert same(got[name].numpy(), want[name]), name
+    if kind in ("int8", "w4"):
+        assert got["s_channel" if kind == "w4" else "scale"][130] == 1.0 and not got["_qdata"][130].any()
+    if kind == "w6":  # code 32 everywhere: nibble plane 0, 2-bit plane 0b10101010
+        assert got["s_channel"][130] == 1.0
+        assert not got["_qdata"][130, :256].any() and (got["_qdata"][130, 256:] == 0xAA).all()
+        assert not moe.decode_codes(got["_qdata"][130].numpy(), got["scale"][130].numpy(), 512, 6, None).any()
+
+
+def test_w4_custom_codebook_with_equal_candidates():
+    """A codebook with repeated and near values: several codes give the same rounded candidate, and the first of equal
+    distances wins, as numpy's argmin picks it."""
+    book = np.array([-1.0, -1.0, -0.5, -0.25, -0.25, -0.125, 0.0, 0.0, 0.01, 0.125, 0.25, 0.25, 0.5, 0.75, 1.0, 1.0],
+                    np.float32)
+    w = rows((2, 128, 512), 22)
+    got = pack.pack_codes(torch.from_numpy(w), 4, book)
+    q, g, c = moe.quantize_codes(w.reshape(-1, 512), 4, book)
+    assert same(got["_qdata"].numpy(), q) and same(got["scale"].numpy(), g) and same(got["s_channel"].numpy(), c)
+
+
+@pytest.mark.parametrize("kind, bound", [("fp8", 0.035), ("int8", 0.01), ("w4", 0.1), ("w6", 0.03), ("fp8c", 0.035),
+                                         ("w4a8", 0.15), ("w6a8", 0.035)])
+def test_packed_relative_error(kind, bound):
+    """What the packers write, decoded by the oracle, against the float rows (in the ConvRot basis where the layout
+    has it): the relative Frobenius error the reference's converter reports per layer."""
+    K = 512
+    w = rows((2, 256, K), 23)
+    flat = w.reshape(-1, K)
+    fields = {n: v.view(torch.int16).numpy().view(np.uint16) if v.dtype == torch.bfloat16 else v.numpy()
+              for n, v in pack.pack_bank(kind, torch.from_numpy(w)).items()}
+    if kind in ("fp8", "int8", "w4", "w6"):
+        back = moe.expert_rows(kind, fields, 0, flat.shape[0], K, moe.CODEBOOK4)
+        ref = flat.astype(np.float64) if kind == "fp8" else moe.convrot_weight(flat)
+    elif kind == "fp8c":
+        back, ref = moe.dequant_fp8_channel(fields["weight"], fields["scale"]), flat.astype(np.float64)
+    else:
+        codes = moe.wa8_codes(kind, fields, 0, flat.shape[0], K).astype(np.float64)
+        scale = np.repeat(moe.bf16_to_f32(fields["scale"]).astype(np.float64), 128, axis=1)
+        back, ref = codes * scale, flat.astype(np.float64)
+    err = np.linalg.norm(back - ref) / np.linalg.norm(ref)
+    assert 0 < err < bound
+
+
+def test_reference_layout_bad_arguments_raise():
+    with pytest.raises(_lib.D3Error):
+        pack.pack_fp8_blocks(torch.zeros((100, 256)))  # rows not a multiple of 128
+    with pytest.raises(_lib.D3Error):
+        pack.pack_int8_convrot(torch.zeros((4, 384)))  # K not a multiple of 256
+    with pytest.raises(ValueError):
+        pack.pack_codes(torch.zeros((4, 256)), 4, codebook=[0.0] * 8)
