@@ -3,6 +3,8 @@ the converter step of the reference (tools/convert.py:48-82,179-215) with plain 
 layouts (fp8 block-scaled, int8 ConvRot, w4 / w6 codes) and the BASELINE ones (fp8c, w4a8, w6a8). Banks come back as
 host torch tensors in the fields moe_decode / grouped_mma / resident_prefill and the offload store take, flat over
 experts ([E * N, ...], expert e's rows contiguous)."""
+import json
+
 import torch
 
 from ._lib import check, lib
@@ -98,3 +100,89 @@ def pack_bank(kind, w, threads=0, codebook=CODEBOOK4):
     if kind in ("w4a8", "w6a8"):
         return pack_wa8(w, int(kind[1]), threads)
     raise ValueError(f"no packer for {kind}")
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# The converter's on-disk expert layout (tools/convert.py:179-215): state-dict entries per layer, and back to banks.
+# The file's "drama3_format" metadata value of each reference layout (tools/convert.py:287).
+DRAMA3_FORMAT = {"fp8": "fp8", "int8": "int8_convrot", "w4": "w4a8", "w6": "w6a8"}
+CONVROT_GROUP = 256
+CODES_GROUP = 16
+
+
+def _comfy_quant(conf):
+    """The layout's config as the uint8 tensor of its JSON text (tools/convert.py:56-58,74-75)."""
+    return torch.tensor(list(json.dumps(conf).encode()), dtype=torch.uint8)
+
+
+def expert_state(kind, layer, gate_up, down, threads=0, codebook=CODEBOOK4):
+    """One layer's float experts, gate_up [E, 2I, H] (gate rows then up rows, tools/convert.py:195) and down [E, H, I],
+    packed into the converter's state-dict entries for `kind` ("fp8", "int8", "w4", "w6"):
+      fp8:  model.layers.{layer}.mlp.experts.{gate_up,down}_{weight [E, N, K] float8_e4m3fn, scale [E, N/128, K/128]
+            fp32} (tools/convert.py:181-189);
+      int8: model.layers.{layer}.mlp.experts.{gate_up,down}_proj.{weight [E, N, K] int8, weight_scale [E, N, 1] fp32,
+            comfy_quant} (:207-213);
+      w4 / w6: ....{gate_up,down}_proj.{weight [E, N, K*bits/8] uint8, weight_s_rel [E, N, K/16] uint8 (e4m3),
+            weight_s_channel [E, N] fp32, comfy_quant, weight_codebook fp32 [16] (w4 only)} (:61-82, :199-205).
+    The rounding is this module's plain nearest rounding, so the codes are not comfy_kitchen's; the layout is."""
+    out = {}
+    for bank, w in (("gate_up", gate_up), ("down", down)):
+        w = torch.as_tensor(w)
+        E, N, K = w.shape
+        fields = pack_bank(kind, w, threads, codebook)
+        if kind == "fp8":
+            prefix = f"model.layers.{layer}.mlp.experts.{bank}"
+            out[f"{prefix}_weight"] = fields["weight"].view(E, N, K).view(torch.float8_e4m3fn)
+            out[f"{prefix}_scale"] = fields["scale"].view(E, N // 128, K // 128)
+            continue
+        module = f"model.layers.{layer}.mlp.experts.{bank}_proj"
+        if kind == "int8":
+            out[f"{module}.weight"] = fields["_qdata"].view(E, N, K)
+            out[f"{module}.weight_scale"] = fields["scale"].view(E, N, 1)
+            out[f"{module}.comfy_quant"] = _comfy_quant({"format": "int8_tensorwise", "convrot": True,
+                                                         "convrot_groupsize": CONVROT_GROUP, "num_experts": E})
+            continue
+        bits = int(kind[1])
+        out[f"{module}.weight"] = fields["_qdata"].view(E, N, K * bits // 8)
+        out[f"{module}.weight_s_rel"] = fields["scale"].view(E, N, K // CODES_GROUP)
+        out[f"{module}.weight_s_channel"] = fields["s_channel"].view(E, N)
+        out[f"{module}.comfy_quant"] = _comfy_quant({"format": "asym_w4a8_int8" if bits == 4 else "w6a8_int8",
+                                                     "group_size": CODES_GROUP, "convrot_groupsize": CONVROT_GROUP,
+                                                     "num_experts": E})
+        if bits == 4:
+            out[f"{module}.weight_codebook"] = torch.as_tensor(codebook, dtype=torch.float32).clone()
+    return out
+
+
+def banks_from_state(kind, state, layer):
+    """The converter's entries of one layer (expert_state's keys) -> (gate_up fields, down fields, codebooks): flat
+    banks [E * N, ...] in the fields the kernels and the offload store take (drama3/offload.py:72-90,755-766), and
+    each bank's fp32 codebook for w4 (a bank holds one table, tools/convert.py:62-63), else (None, None)."""
+    banks = []
+    for bank in ("gate_up", "down"):
+        if kind == "fp8":
+            prefix = f"model.layers.{layer}.mlp.experts.{bank}"
+            w, s = state[f"{prefix}_weight"], state[f"{prefix}_scale"]
+            E, N, K = w.shape
+            banks.append({"weight": w.view(torch.uint8).reshape(E * N, K), "scale": s.reshape(E * N // 128, K // 128)})
+            continue
+        module = f"model.layers.{layer}.mlp.experts.{bank}_proj"
+        conf = json.loads(bytes(state[f"{module}.comfy_quant"].tolist()).decode())
+        q = state[f"{module}.weight"]
+        E, N = q.shape[:2]
+        if kind == "int8":
+            if conf.get("format") != "int8_tensorwise" or conf.get("convrot_groupsize") != CONVROT_GROUP:
+                raise ValueError(f"{module}: not an int8 ConvRot bank ({conf})")
+            banks.append({"_qdata": q.reshape(E * N, -1), "scale": state[f"{module}.weight_scale"].reshape(E * N)})
+            continue
+        want = "asym_w4a8_int8" if kind == "w4" else "w6a8_int8"
+        if conf.get("format") != want or conf.get("group_size") != CODES_GROUP:
+            raise ValueError(f"{module}: not a {kind} bank ({conf})")
+        banks.append({"_qdata": q.reshape(E * N, -1),
+                      "scale": state[f"{module}.weight_s_rel"].reshape(E * N, -1),
+                      "s_channel": state[f"{module}.weight_s_channel"].reshape(E * N)})
+    codebooks = (None, None)
+    if kind == "w4":
+        codebooks = tuple(state[f"model.layers.{layer}.mlp.experts.{bank}_proj.weight_codebook"].float()
+                          for bank in ("gate_up", "down"))
+    return banks[0], banks[1], codebooks

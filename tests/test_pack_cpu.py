@@ -2,7 +2,10 @@
 layouts (oracle.moe.make_bank: fp8 block scales, int8 ConvRot, w4 / w6 codes) and the BASELINE ones
 (quantize_fp8_channel, quantize_wa8), on random experts, all-zero rows, blocks and groups, exact ties of the rounding,
 saturation, tiny negatives, and several thread splits; plus the relative error of what they pack, the check the
-reference's converter prints (tools/convert.py:102-109)."""
+reference's converter prints (tools/convert.py:102-109); and the converter's on-disk expert layout (state-dict keys,
+comfy_quant configs, a safetensors round trip)."""
+import json
+
 import numpy as np
 import pytest
 import torch
@@ -187,3 +190,52 @@ def test_reference_layout_bad_arguments_raise():
         pack.pack_int8_convrot(torch.zeros((4, 384)))  # K not a multiple of 256
     with pytest.raises(ValueError):
         pack.pack_codes(torch.zeros((4, 256)), 4, codebook=[0.0] * 8)
+
+
+@pytest.mark.parametrize("kind", ["fp8", "int8", "w4", "w6"])
+def test_expert_state_layout_and_round_trip(kind, tmp_path):
+    """One layer through the converter's state-dict layout (keys, shapes, dtypes, comfy_quant JSON), a safetensors
+    file and back to flat banks equal to pack_bank's."""
+    from safetensors.torch import load_file, save_file
+    E, H, I = 4, 512, 256
+    gu = torch.from_numpy(rows((E, 2 * I, H), 30))
+    dn = torch.from_numpy(rows((E, H, I), 31))
+    state = pack.expert_state(kind, 7, gu, dn, threads=2)
+    if kind == "fp8":
+        assert state["model.layers.7.mlp.experts.gate_up_weight"].dtype == torch.float8_e4m3fn
+        assert state["model.layers.7.mlp.experts.gate_up_weight"].shape == (E, 2 * I, H)
+        assert state["model.layers.7.mlp.experts.down_scale"].shape == (E, H // 128, I // 128)
+    else:
+        mod = "model.layers.7.mlp.experts.down_proj"
+        conf = json.loads(bytes(state[f"{mod}.comfy_quant"].tolist()).decode())
+        assert conf["num_experts"] == E and conf["convrot_groupsize"] == 256
+        if kind == "int8":
+            assert conf["format"] == "int8_tensorwise" and conf["convrot"] is True
+            assert state[f"{mod}.weight"].shape == (E, H, I) and state[f"{mod}.weight_scale"].shape == (E, H, 1)
+        else:
+            bits = int(kind[1])
+            assert conf == {"format": "asym_w4a8_int8" if bits == 4 else "w6a8_int8", "group_size": 16,
+                            "convrot_groupsize": 256, "num_experts": E}
+            assert state[f"{mod}.weight"].shape == (E, H, I * bits // 8)
+            assert state[f"{mod}.weight_s_rel"].shape == (E, H, I // 16)
+            assert state[f"{mod}.weight_s_channel"].shape == (E, H)
+            assert (f"{mod}.weight_codebook" in state) == (bits == 4)
+    path = tmp_path / "experts.safetensors"
+    save_file(state, str(path), metadata={"drama3_format": pack.DRAMA3_FORMAT[kind]})
+    back = load_file(str(path))
+    gu_f, dn_f, books = pack.banks_from_state(kind, back, 7)
+    for fields, w in ((gu_f, gu), (dn_f, dn)):
+        want = pack.pack_bank(kind, w)
+        assert sorted(fields) == sorted(want)
+        for name in want:
+            assert torch.equal(fields[name], want[name]), name
+    if kind == "w4":
+        assert all(torch.equal(b, torch.tensor(pack.CODEBOOK4)) for b in books)
+    else:
+        assert books == (None, None)
+
+
+def test_banks_from_state_rejects_another_layout():
+    state = pack.expert_state("w6", 0, torch.zeros((1, 256, 256)), torch.zeros((1, 256, 256)))
+    with pytest.raises(ValueError):
+        pack.banks_from_state("w4", state, 0)
