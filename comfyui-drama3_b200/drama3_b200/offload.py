@@ -195,6 +195,31 @@ def _sort_by_expert(topk_idx, num_experts):
     return order, counts
 
 
+def prefill_plan(topk_idx, num_experts):
+    """The prompt's (token, rank) pairs sorted by expert on the device, with no host sync, so that a prompt pass can
+    be captured in a CUDA graph (the host-side sort of drama3/offload.py:141-145 reads the counts back): a counting
+    sort by per-expert prefix sums of the pairs' one-hot rows. Returns (order, pos, groups, tiles):
+      order [P] int64: the pairs in expert order, in (token, rank) order within an expert; pos [P] its inverse;
+      groups [E + 1, 5] int32 (expert, slot, 0, first, rows): every expert's group, empty ones included (they get no
+        tile), then one group for the pairs whose id is outside [0, E), which sort last (slot E: the grouped kernels
+        skip its rows and record the bad-slot fault, as they do for such a group of the host-side plan);
+      tiles: a host int from the shapes alone that bounds the row tiles of any routing, (P + (t - 1)(E + 1)) // t for
+        t rows per tile (the kernels run the number of tiles the groups need, counted on the device)."""
+    flat = topk_idx.reshape(-1)
+    E, P = num_experts, flat.numel()
+    key = torch.where((flat >= 0) & (flat < E), flat, torch.full_like(flat, E))
+    onehot = (key.unsqueeze(1) == torch.arange(E + 1, device=flat.device)).to(torch.int32)
+    ranks = torch.cumsum(onehot, dim=0, dtype=torch.int32)
+    counts = ranks[-1] if P else torch.zeros((E + 1,), dtype=torch.int32, device=flat.device)
+    first = torch.cumsum(counts, dim=0, dtype=torch.int32) - counts
+    pos = (first.gather(0, key) + ranks.gather(1, key.unsqueeze(1)).squeeze(1) - 1).to(torch.int64)
+    order = torch.empty_like(pos).scatter_(0, pos, torch.arange(P, device=flat.device))
+    experts = torch.arange(E + 1, dtype=torch.int32, device=flat.device)
+    groups = torch.stack([experts, experts, torch.zeros_like(experts), first, counts], dim=1).contiguous()
+    t = kernels.grouped_tile_rows()
+    return order, pos, groups, (P + (t - 1) * (E + 1)) // t
+
+
 def _scatter_sum(sorted_out, order, topk_weight, num_tokens, top_k):
     """Undo the sort, weight every pair, and sum each token's k pairs (drama3/offload.py:146-149)."""
     out = torch.empty_like(sorted_out)
@@ -213,29 +238,40 @@ def _grouped_resident(kind, x, groups, tiles, bank, rows, codebook):
     return quantized_grouped(kind, x, groups, bank, bank, rows, codebook)
 
 
-def resident_prefill(x, topk_idx, topk_weight, banks, rows, kind, codebooks, num_experts):
+def resident_prefill(x, topk_idx, topk_weight, banks, rows, kind, codebooks, num_experts, sync_free=False):
     """Many rows x [T, H] through banks held whole on the GPU (drama3/offload.py:138-149): rows sorted by expert, one
     grouped GEMM per bank on the tensor cores, SwiGLU between (with the ConvRot rotations for int8/W4/W6), scattered
     back, weighted and summed. Where the shapes allow (N % 128, K % 256), the gather of the sorted rows, SwiGLU and
     the rotations run inside the GEMMs' staging and the scatter / weight / sum is one combine launch. [T, H] in x's
-    dtype (bfloat16 or float32)."""
+    dtype (bfloat16 or float32).
+    sync_free: sort on the device (prefill_plan) instead of reading the expert counts back to the host, so the call
+    can be captured in a CUDA graph and replayed with new routing; same results bit for bit (every row's GEMMs and
+    its combine are computed alone, whatever tile it shares). Tensor-core shapes only."""
     num_tokens, top_k = topk_idx.shape
-    order, counts = _sort_by_expert(topk_idx, num_experts)
-    offsets = [0, *itertools.accumulate(counts)]
-    groups = [(e, e, 0, offsets[e], n) for e, n in enumerate(counts) if n]
-    groups = torch.tensor(groups, dtype=torch.int32).to(x.device)
-    tiles = kernels.grouped_tiles(counts)
     gate_up, down = banks
     rotated = kind in ROTATED_KINDS
     width = x.shape[1]
-    if (x.dtype in (torch.bfloat16, torch.float32) and kernels.grouped_mma_fits(rows[0], width)
-            and kernels.grouped_mma_fits(rows[1], rows[0] // 2)):
+    fused = (x.dtype in (torch.bfloat16, torch.float32) and kernels.grouped_mma_fits(rows[0], width)
+             and kernels.grouped_mma_fits(rows[1], rows[0] // 2))
+    if sync_free:
+        if not fused:
+            raise ValueError("a prompt pass without host syncs runs on the tensor-core kernels only (bfloat16 or "
+                             "float32 rows, N % 128 == 0, K % 256 == 0)")
+        order, pos, groups, tiles = prefill_plan(topk_idx, num_experts)
+    else:
+        order, counts = _sort_by_expert(topk_idx, num_experts)
+        offsets = [0, *itertools.accumulate(counts)]
+        groups = [(e, e, 0, offsets[e], n) for e, n in enumerate(counts) if n]
+        groups = torch.tensor(groups, dtype=torch.int32).to(x.device)
+        tiles = kernels.grouped_tiles(counts)
+    if fused:
         hidden = kernels.grouped_mma(kind, x, groups, gate_up, codebooks[0], rows[0], tiles, row_index=order // top_k,
                                      rotate=rotated)
         sorted_out = kernels.grouped_mma(kind, hidden, groups, down, codebooks[1], rows[1], tiles, rotate=rotated,
                                          swiglu=True)
-        pos = torch.empty_like(order)
-        pos[order] = torch.arange(order.numel(), device=order.device)
+        if not sync_free:
+            pos = torch.empty_like(order)
+            pos[order] = torch.arange(order.numel(), device=order.device)
         out = kernels.prefill_combine(sorted_out, pos.view(num_tokens, top_k), topk_weight,
                                       dtype=torch.float32 if x.dtype == torch.float32 else torch.bfloat16)
         return out.to(x.dtype)

@@ -1,0 +1,73 @@
+"""The device-side sort of a prompt's pairs by expert (offload.prefill_plan), run here on CPU tensors: the same torch
+ops the GPU runs, checked against the host-side plan of the reference's prompt pass (argsort + bincount,
+drama3/offload.py:141-145): a stable order by expert, its inverse, every expert's group with exclusive-sum offsets,
+out-of-range ids in one last group, and a tile bound no routing exceeds."""
+import numpy as np
+import pytest
+import torch
+
+from drama3_b200 import kernels, offload
+
+
+def check_plan(ids, E):
+    order, pos, groups, tiles = offload.prefill_plan(ids, E)
+    flat = ids.reshape(-1).numpy()
+    P = flat.size
+    key = np.where((flat >= 0) & (flat < E), flat, E)
+    want_order = np.argsort(key, kind="stable")
+    assert order.dtype == torch.int64 and pos.dtype == torch.int64 and groups.dtype == torch.int32
+    assert np.array_equal(order.numpy(), want_order)
+    assert np.array_equal(pos.numpy()[want_order], np.arange(P))
+    counts = np.bincount(key, minlength=E + 1)
+    first = np.concatenate([[0], np.cumsum(counts)[:-1]])
+    g = groups.numpy()
+    assert g.shape == (E + 1, 5)
+    assert np.array_equal(g[:, 0], np.arange(E + 1)) and np.array_equal(g[:, 1], np.arange(E + 1))
+    assert not g[:, 2].any()
+    assert np.array_equal(g[:, 3], first) and np.array_equal(g[:, 4], counts)
+    assert tiles >= kernels.grouped_tiles(counts)
+    # the host-side plan's non-empty groups over the valid ids are the same groups
+    valid = flat[(flat >= 0) & (flat < E)]
+    host_order, host_counts = offload._sort_by_expert(torch.from_numpy(valid), E)
+    assert host_counts == counts[:E].tolist()
+    assert sorted(valid[host_order.numpy()].tolist()) == valid[host_order.numpy()].tolist()
+    return order, pos, groups, tiles
+
+
+@pytest.mark.parametrize("T, k, E", [(2048, 8, 128), (37, 8, 16), (1, 8, 128), (300, 2, 4)])
+def test_plan_matches_host_sort(T, k, E):
+    gen = torch.Generator().manual_seed(T + E)
+    skew = -1.1 * torch.log(torch.randperm(E, generator=gen).float() + 1)
+    ids = (torch.rand((T, E), generator=gen).log().neg().reciprocal() * skew.exp()).topk(k, dim=-1).indices
+    check_plan(ids, E)
+
+
+def test_plan_all_pairs_on_one_expert_and_empty_experts():
+    ids = torch.full((513, 8), 5, dtype=torch.int64)
+    _, _, groups, tiles = check_plan(ids, 128)
+    assert groups[5, 4] == 513 * 8 and int(groups[:, 4].sum()) == 513 * 8
+    assert tiles >= (513 * 8 + 127) // 128
+
+
+def test_plan_out_of_range_ids_sort_last():
+    ids = torch.randint(0, 16, (40, 8), generator=torch.Generator().manual_seed(3))
+    ids[3, 2], ids[5, 0], ids[9, 7] = 16, -1, 99
+    order, _, groups, _ = check_plan(ids, 16)
+    assert groups[16].tolist() == [16, 16, 0, 40 * 8 - 3, 3]
+    assert sorted(order[-3:].tolist()) == [3 * 8 + 2, 5 * 8 + 0, 9 * 8 + 7]
+
+
+def test_plan_of_no_rows():
+    order, pos, groups, tiles = offload.prefill_plan(torch.zeros((0, 8), dtype=torch.int64), 128)
+    assert order.numel() == 0 and pos.numel() == 0 and not groups[:, 4].any()
+    assert tiles >= 0
+
+
+def test_tile_bound_is_tight_for_the_worst_routing():
+    """Every expert holding one row more than a whole number of tiles is the worst case: the bound equals it."""
+    E, t = 8, kernels.grouped_tile_rows()
+    counts = [t + 1] * E
+    ids = torch.repeat_interleave(torch.arange(E), torch.tensor(counts)).view(-1, 1)
+    _, _, groups, tiles = offload.prefill_plan(ids, E)
+    need = kernels.grouped_tiles(groups[:, 4].tolist())
+    assert need == 2 * E and tiles == need
