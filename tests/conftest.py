@@ -1,5 +1,4 @@
 """Shared test setup: import paths, the `gpu` marker, seeded helpers."""
-import os
 import sys
 from pathlib import Path
 

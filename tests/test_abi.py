@@ -1,6 +1,5 @@
 """The C ABI library: it loads, exports every symbol include/drama3_b200.h declares, and rejects bad arguments
 before launching anything. CPU only (no compute call reaches a GPU)."""
-import ctypes
 import re
 from pathlib import Path
 

@@ -1,7 +1,6 @@
 """The CPU oracle pinned against golden vectors from the reference's own CPU functions (tests/golden/make_golden.py).
 CPU only."""
 import numpy as np
-import pytest
 
 from oracle import moe
 
