@@ -239,3 +239,56 @@ def test_banks_from_state_rejects_another_layout():
     state = pack.expert_state("w6", 0, torch.zeros((1, 256, 256)), torch.zeros((1, 256, 256)))
     with pytest.raises(ValueError):
         pack.banks_from_state("w4", state, 0)
+
+
+def _draw_rows(data, rows, K):
+    """Rows with a drawn distribution: a scale of 1e-20 .. 1e20, normal / uniform / heavy-tailed values, some rows and
+    columns zeroed, and integer-valued entries (which land on rounding ties)."""
+    from hypothesis import strategies as st
+    seed = data.draw(st.integers(0, 2 ** 32 - 1))
+    rng = np.random.default_rng(seed)
+    scale = 10.0 ** data.draw(st.integers(-20, 20))
+    shape = data.draw(st.sampled_from(["normal", "uniform", "cauchy", "ints"]))
+    if shape == "normal":
+        w = rng.normal(size=(rows, K))
+    elif shape == "uniform":
+        w = rng.uniform(-1, 1, size=(rows, K))
+    elif shape == "cauchy":
+        w = np.clip(rng.standard_cauchy(size=(rows, K)), -1e6, 1e6)
+    else:
+        w = rng.integers(-64, 65, size=(rows, K)).astype(np.float64) / 2
+        scale = 1.0
+    w = (w * scale).astype(np.float32)
+    w[rng.random(rows) < 0.1] = 0.0
+    w[:, rng.random(K) < 0.05] = 0.0
+    return w
+
+
+def test_packers_property_against_oracle():
+    """Drawn rows through every packer, byte for byte against the oracle (hypothesis, 40 draws)."""
+    from hypothesis import HealthCheck, given, settings
+    from hypothesis import strategies as st
+
+    @settings(max_examples=40, deadline=None, suppress_health_check=[HealthCheck.too_slow])
+    @given(st.data())
+    def check(data):
+        kind = data.draw(st.sampled_from(["fp8", "int8", "w4", "w6", "fp8c", "w4a8", "w6a8"]))
+        K = data.draw(st.sampled_from([256, 512]))
+        rows_ = 128 * data.draw(st.integers(1, 2))
+        w = _draw_rows(data, rows_, K)
+        got = pack.pack_bank(kind, torch.from_numpy(w), threads=data.draw(st.integers(0, 3)))
+        with np.errstate(over="ignore", invalid="ignore"):
+            if kind in ("fp8", "int8", "w4", "w6"):
+                want = moe.make_bank(kind, w[None])
+            elif kind == "fp8c":
+                c, s = moe.quantize_fp8_channel(w)
+                want = {"weight": c, "scale": s}
+            else:
+                q, s = moe.quantize_wa8(w, int(kind[1]))
+                want = {"_qdata": q, "scale": s}
+        for name in want:
+            g = got[name]
+            g = g.view(torch.int16).numpy().view(np.uint16) if g.dtype == torch.bfloat16 else g.numpy()
+            assert same(g, want[name]), (kind, name)
+
+    check()
