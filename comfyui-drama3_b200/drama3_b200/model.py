@@ -13,7 +13,7 @@ import torch
 import torch.nn as nn
 
 from . import kernels
-from .offload import FP8Experts, MAX_DECODE_ROWS, kernel_bank, resident_decode_lines, resident_prefill, \
+from .offload import FP8Experts, MAX_DECODE_ROWS, capturing, kernel_bank, resident_decode_lines, resident_prefill, \
     fused_decode_fits
 
 
@@ -69,7 +69,8 @@ class Experts(nn.Module):
                     self._workspace[key] = kernels.decode_workspace(M, k, intermediate, x.device)
                 ws = self._workspace[key]
             return resident_decode_lines(x, topk_idx, topk_weight, banks, rows, kind, codebooks, workspace=ws)
-        return resident_prefill(x, topk_idx, topk_weight, banks, rows, kind, codebooks, self.num_experts)
+        return resident_prefill(x, topk_idx, topk_weight, banks, rows, kind, codebooks, self.num_experts,
+                                sync_free=capturing(x))
 
 
 class SparseMoeBlock(nn.Module):

@@ -195,6 +195,12 @@ def _sort_by_expert(topk_idx, num_experts):
     return order, counts
 
 
+def capturing(x):
+    """Whether the current stream of x's device is capturing a CUDA graph: prompt passes then sort on the device
+    (resident_prefill(sync_free=True)), since the host-side sort reads the counts back, which a capture forbids."""
+    return x.is_cuda and torch.cuda.is_current_stream_capturing()
+
+
 def prefill_plan(topk_idx, num_experts):
     """The prompt's (token, rank) pairs sorted by expert on the device, with no host sync, so that a prompt pass can
     be captured in a CUDA graph (the host-side sort of drama3/offload.py:141-145 reads the counts back): a counting
@@ -725,7 +731,8 @@ class FP8Experts(nn.Module):
         if M == 1 or fused_decode_fits(hidden, intermediate, M, k):
             ws = self.workspace(M, k, x.device) if fused_decode_fits(hidden, intermediate, M, k) else None
             return resident_decode_lines(x, topk_idx, topk_weight, banks, rows, "fp8", (None, None), workspace=ws)
-        return resident_prefill(x, topk_idx, topk_weight, banks, rows, "fp8", (None, None), self.num_experts)
+        return resident_prefill(x, topk_idx, topk_weight, banks, rows, "fp8", (None, None), self.num_experts,
+                                sync_free=capturing(x))
 
 
 class OffloadedExperts(nn.Module):

@@ -153,3 +153,21 @@ def test_prompt_routing_matches_reference(golden):
     ids, weights = block.route(logits, decode=False)
     np.testing.assert_array_equal(ids.numpy(), golden["route_ids"])
     np.testing.assert_array_equal(weights.float().numpy(), golden["route_w"])
+
+
+def test_prompt_pass_sorts_on_the_device_under_graph_capture(monkeypatch):
+    """A prompt pass reached while a CUDA graph is being captured asks resident_prefill for the device-side sort (the
+    host-side one reads counts back, which a capture forbids); outside a capture it keeps the host-side plan."""
+    from drama3_b200 import offload
+    calls = []
+    monkeypatch.setattr(offload.kernels, "available", lambda device: True)
+    monkeypatch.setattr(offload, "resident_prefill", lambda *args, **kw: calls.append(kw.get("sync_free")))
+    ex = offload.FP8Experts(4, 256, 128, dtype=torch.float32)
+    x = torch.zeros((40, 256))
+    ids = torch.zeros((40, 8), dtype=torch.int64)
+    w = torch.full((40, 8), 0.125)
+    assert offload.capturing(x) is False
+    ex(x, ids, w)
+    monkeypatch.setattr(offload, "capturing", lambda t: True)
+    ex(x, ids, w)
+    assert calls == [False, True]

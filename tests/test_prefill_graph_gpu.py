@@ -74,3 +74,27 @@ def test_sync_free_needs_the_tensor_core_shapes(cuda):
     x, ids, w = prompt(102, cuda)
     with pytest.raises(ValueError):
         offload.resident_prefill(x.to(torch.float16), ids, w, banks, (2 * I, H), "fp8", cbs, E, sync_free=True)
+
+
+def test_fp8_experts_prompt_pass_captured(cuda):
+    """FP8Experts reached inside a CUDA-graph capture takes the device-side sort by itself: the captured prompt pass
+    replays to the eager (host-planned) result bit for bit."""
+    from test_offload_gpu import fp8_module
+    ex, _ = fp8_module(16, H, I, 110, cuda)
+    x, ids, w = prompt(112, cuda)
+    ids = ids % 16
+    eager = ex(x, ids, w)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        ex(x, ids, w)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = ex(x, ids, w)
+    try:
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, eager)
+    finally:
+        del graph
