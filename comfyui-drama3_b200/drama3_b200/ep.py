@@ -1,7 +1,12 @@
-"""Expert parallelism for the routed-expert decode over the GPUs of one node (one process per GPU,
-torch.distributed): rank r holds a contiguous block of the experts, every rank sees all rows (lines are
-replicated), runs the fused decode over its own experts only and produces an fp32 partial [M, H]; the partials are
-gathered and summed in rank order, then rounded to bf16 once, so every rank ends with the same output.
+"""Expert parallelism for the routed experts over the GPUs of one node (one process per GPU, torch.distributed):
+rank r holds a contiguous block of the experts.
+
+Decode (ExpertParallelDecode): every rank sees all rows (lines are replicated), runs the fused decode over its own
+experts only and produces an fp32 partial [M, H]; the partials are gathered and summed in rank order, then rounded
+to bf16 once, so every rank ends with the same output.
+
+Prompt pass (ExpertParallelPrefill): every rank brings its own rows; each (row, rank) pair travels to the rank that
+holds its expert and its output travels back (two all-to-alls), then each rank weights and sums its rows' pairs.
 
 The reference runs on one GPU; this is the multi-GPU layout of its decode step (experts split, tokens replicated,
 partial combines reduced). Two exchanges: an all-gather over NCCL (128 KB per layer at 16 lines), or PeerExchange,
@@ -166,3 +171,98 @@ class ExpertParallelDecode:
         gathered = torch.empty((self.world * part.shape[0], part.shape[1]), dtype=part.dtype, device=part.device)
         dist.all_gather_into_tensor(gathered, part, group=self.group)
         return sum_in_rank_order(gathered.view(self.world, *part.shape)).to(torch.bfloat16)
+
+
+def expert_owner(ids, num_experts, world):
+    """The rank holding each expert id under expert_range's blocks; -1 for ids outside [0, num_experts)."""
+    base, extra = divmod(num_experts, world)
+    big = extra * (base + 1)
+    owner = torch.where(ids < big, ids // (base + 1), extra + (ids - big) // max(base, 1))
+    return torch.where((ids >= 0) & (ids < num_experts), owner, torch.full_like(owner, -1))
+
+
+def local_pairs(kind, banks, e_count, rows, codebooks, x, local_ids):
+    """fp32 [R, rows[1]]: rows x [R, H] (bfloat16 or float32) each through its expert local_ids [R] (0-based in this
+    rank's block of e_count experts, banks = local_banks), unweighted, in the given order: the two grouped GEMMs of
+    the prompt pass over the rows sorted by expert on the device (offload.prefill_plan), then put back in order."""
+    from . import offload
+    if x.shape[0] == 0:
+        return torch.zeros((0, rows[1]), dtype=torch.float32, device=x.device)
+    if not (x.dtype in (torch.bfloat16, torch.float32) and kernels.grouped_mma_fits(rows[0], x.shape[1])
+            and kernels.grouped_mma_fits(rows[1], rows[0] // 2)):
+        raise ValueError("an expert-parallel prompt pass runs on the tensor-core kernels only (bfloat16 or float32 "
+                         "rows, N % 128 == 0, K % 256 == 0)")
+    order, pos, groups, tiles = offload.prefill_plan(local_ids.view(-1, 1), e_count)
+    rotated = kind in offload.ROTATED_KINDS
+    hidden = kernels.grouped_mma(kind, x, groups, banks[0], codebooks[0], rows[0], tiles, row_index=order,
+                                 rotate=rotated)
+    out = kernels.grouped_mma(kind, hidden, groups, banks[1], codebooks[1], rows[1], tiles, rotate=rotated,
+                              swiglu=True)
+    return out[pos]
+
+
+def _wire(t):
+    """Rows as 32-bit words for the all-to-all (bfloat16 rows bit for bit, two values a word)."""
+    return t.view(torch.int32) if t.dtype == torch.bfloat16 else t
+
+
+class ExpertParallelPrefill:
+    """One MoE layer's prompt pass with this rank's experts (banks = local_banks(..., rank, world); rows = (2I, H),
+    the rows per expert of gate_up and down). Called on every rank with that rank's own rows x [T_r, H] and their
+    routing topk_idx / topk_weight [T_r, k]: each (row, rank) pair is sent to the rank holding its expert (all-to-all
+    of the rows and of their experts' indices within the receiver's block), runs there through the grouped GEMMs on
+    the tensor cores, and its fp32 output is sent back (all-to-all); the rank then weights and sums its rows' pairs in
+    rank order (kernels.prefill_combine). Every pair's output is computed alone and crosses exactly, so the result is
+    bit for bit the one-GPU prompt pass of the same rows (offload.resident_prefill). Pairs whose id is outside
+    [0, num_experts) add nothing. The split sizes are read back to the host once per call (the collectives need them).
+    `pairs_fn(x, ids) -> fp32 [R, H]` (global expert ids) and `combine_fn(pair_out [T_r * k, H], weights) -> [T_r, H]`
+    replace the kernels when given, so that the exchange runs on CPU ranks."""
+
+    def __init__(self, kind, banks, num_experts, rows, group=None, codebooks=(None, None), pairs_fn=None,
+                 combine_fn=None):
+        self.kind, self.banks, self.num_experts, self.rows, self.group = kind, banks, num_experts, rows, group
+        self.codebooks, self.pairs_fn, self.combine_fn = codebooks, pairs_fn, combine_fn
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self.e_first, self.e_count = expert_range(num_experts, self.rank, self.world)
+        self.firsts = [expert_range(num_experts, r, self.world)[0] for r in range(self.world)]
+
+    def pairs(self, x, local_ids):
+        if self.pairs_fn is not None:
+            return self.pairs_fn(x, local_ids.to(torch.int64) + self.e_first)
+        return local_pairs(self.kind, self.banks, self.e_count, self.rows, self.codebooks, x, local_ids)
+
+    def __call__(self, x, topk_idx, topk_weight):
+        """[T_r, H] in x's dtype: this rank's rows through the whole layer's experts."""
+        T, k = topk_idx.shape
+        device = x.device
+        flat = topk_idx.reshape(-1)
+        owner = expert_owner(flat, self.num_experts, self.world)
+        dest = torch.where(owner >= 0, owner, torch.full_like(owner, self.world))
+        order = torch.sort(dest, stable=True).indices
+        counts = torch.bincount(dest, minlength=self.world + 1)[:self.world].contiguous()
+        recv = torch.empty_like(counts)
+        dist.all_to_all_single(recv, counts, group=self.group)
+        send_counts, recv_counts = counts.tolist(), recv.tolist()
+        n_send, n_recv = sum(send_counts), sum(recv_counts)
+        sel = order[:n_send]
+        firsts = torch.tensor(self.firsts, dtype=torch.int64, device=device)
+        send_ids = (flat[sel] - firsts[owner[sel]]).to(torch.int32)
+        send_x = _wire(x[sel // k].contiguous())
+        recv_x = torch.empty((n_recv, send_x.shape[1]), dtype=send_x.dtype, device=device)
+        dist.all_to_all_single(recv_x, send_x, recv_counts, send_counts, group=self.group)
+        recv_ids = torch.empty((n_recv,), dtype=torch.int32, device=device)
+        dist.all_to_all_single(recv_ids, send_ids, recv_counts, send_counts, group=self.group)
+        if x.dtype == torch.bfloat16:
+            recv_x = recv_x.view(torch.bfloat16)
+        y = self.pairs(recv_x, recv_ids).to(torch.float32).contiguous()
+        back = torch.empty((n_send, self.rows[1]), dtype=torch.float32, device=device)
+        dist.all_to_all_single(back, y, send_counts, recv_counts, group=self.group)
+        pair_out = torch.zeros((T * k, self.rows[1]), dtype=torch.float32, device=device)
+        pair_out[sel] = back
+        if self.combine_fn is not None:
+            return self.combine_fn(pair_out, topk_weight)
+        if T == 0:
+            return torch.empty((0, self.rows[1]), dtype=x.dtype, device=device)
+        pos = torch.arange(T * k, device=device).view(T, k)
+        dtype = torch.float32 if x.dtype == torch.float32 else torch.bfloat16
+        return kernels.prefill_combine(pair_out, pos, topk_weight, dtype=dtype).to(x.dtype)

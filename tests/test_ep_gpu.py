@@ -13,7 +13,8 @@ pytestmark = pytest.mark.gpu
 ROOT = Path(__file__).resolve().parents[1]
 
 
-def test_expert_parallel_decode_matches_one_gpu():
+def run_workers(script):
+    """stdout of `script` run on every GPU of this node under torchrun (skipped with fewer than 2)."""
     n = torch.cuda.device_count() if torch.cuda.is_available() else 0
     if n < 2:
         pytest.skip("needs 2 or more GPUs")
@@ -23,17 +24,25 @@ def test_expert_parallel_decode_matches_one_gpu():
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={min(n, 8)}", "--master-addr", "127.0.0.1", "--master-port", str(port),
-           str(ROOT / "tests" / "ep_worker.py")]
+           str(ROOT / "tests" / script)]
     proc = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=400)
     assert proc.returncode == 0, proc.stdout[-2000:] + proc.stderr[-3000:]
-    assert "ok=True" in proc.stdout
+    return proc.stdout
+
+
+def test_expert_parallel_decode_matches_one_gpu():
+    assert "ok=True" in run_workers("ep_worker.py")
+
+
+def test_expert_parallel_prefill_matches_one_gpu():
+    assert "ok=True" in run_workers("ep_prefill_worker.py")
 
 
 # ---- the peer exchange's kernels on one GPU: ranks emulated by areas in this GPU's memory, their calls issued one
 # after another on one stream (no kernel waits on one still running)
 
 import gpu_data as gd  # noqa: E402
-from drama3_b200 import _lib, ep, kernels  # noqa: E402
+from drama3_b200 import _lib, ep, kernels, offload  # noqa: E402
 
 E, H, I = 16, 2048, 768
 
@@ -111,3 +120,30 @@ def test_exchange_geometry_checked(cuda):
     torch.cuda.synchronize()
     assert _lib.take_fault() == 16 and not out.any()
     assert not areas[0][:-256].any()
+
+
+@pytest.mark.parametrize("kind", ["fp8c", "w6a8", "fp8", "w4"])
+def test_prefill_pairs_of_emulated_ranks_equal_one_gpu(cuda, kind):
+    """The expert-parallel prompt pass's local step on one GPU: the pairs of each of 3 emulated ranks through that
+    rank's block of the experts (ep.local_pairs), put together and combined, equal the one-GPU prompt pass bit for
+    bit."""
+    T, k, world = 512, 8, 3
+    full = (gd.rand_bank(kind, E * 2, 2 * I, H, 130, cuda), gd.rand_bank(kind, E * 2, H, I, 131, cuda))
+    cbs = gd.codebooks(kind, cuda)
+    x = gd.rand_rows(T, H, 132, cuda)
+    ids, w = gd.rand_routing(T, E * 2, k, 133, cuda)
+    w = w.to(torch.bfloat16)
+    _lib.take_fault()
+    want = offload.resident_prefill(x, ids, w, full, (2 * I, H), kind, cbs, E * 2)
+    flat = ids.reshape(-1)
+    owner = ep.expert_owner(flat, E * 2, world)
+    pair_out = torch.zeros((T * k, H), dtype=torch.float32, device=cuda)
+    for r in range(world):
+        first, count = ep.expert_range(E * 2, r, world)
+        sel = (owner == r).nonzero().squeeze(1)
+        pair_out[sel] = ep.local_pairs(kind, ep.local_banks(full, E * 2, r, world), count, (2 * I, H), cbs,
+                                       x[sel // k], (flat[sel] - first).to(torch.int32))
+    got = kernels.prefill_combine(pair_out, torch.arange(T * k, device=cuda).view(T, k), w)
+    torch.cuda.synchronize()
+    assert _lib.take_fault() == 0
+    assert torch.equal(got, want)

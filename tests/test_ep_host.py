@@ -101,3 +101,80 @@ def test_expert_parallel_exchange_two_cpu_ranks():
     mp.start_processes(_worker, args=(2, port, result), nprocs=2, join=True, start_method="spawn")
     assert sorted(result.keys()) == [0, 1]
     assert all(err <= 1e-3 for err in result.values()), dict(result)
+
+
+# ---- the expert-parallel prompt pass: rows split by rank, pairs sent to their experts' ranks and back
+
+PF_T, PF_E, PF_H, PF_K = 50, 10, 64, 4
+PF_SHARDS = {2: [(0, 23), (23, 50)], 3: [(0, 20), (20, 20), (20, 50)]}
+
+
+def _pf_inputs():
+    gen = torch.Generator().manual_seed(21)
+    x = torch.randn((PF_T, PF_H), generator=gen).to(torch.bfloat16)
+    ids = torch.stack([torch.randperm(PF_E, generator=gen)[:PF_K] for _ in range(PF_T)])
+    ids[3, 1], ids[7, 0] = PF_E + 2, -1  # out of range: add nothing
+    w = torch.softmax(torch.randn((PF_T, PF_K), generator=gen), -1)
+    return x, ids, w
+
+
+def _pf_pair(x, ids):
+    """A stand-in for an expert on a row, exact and different per expert: fp32 x (e + 1) + e."""
+    e = ids.to(torch.float32).unsqueeze(1)
+    return x.float() * (e + 1) + e
+
+
+def _pf_combine(pair_out, w):
+    """Rank-order weighted sum of each row's pairs, fp32."""
+    T, k = w.shape
+    p = pair_out.view(T, k, pair_out.shape[1])
+    out = torch.zeros((T, pair_out.shape[1]))
+    for j in range(k):
+        out = out + w[:, j:j + 1] * p[:, j]
+    return out
+
+
+def _pf_worker(rank, world, port, result):
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        x, ids, w = _pf_inputs()
+        lo, hi = PF_SHARDS[world][rank]
+        first, count = ep.expert_range(PF_E, rank, world)
+        seen = []
+
+        def pairs_fn(xr, gid):
+            seen.append(bool(((gid >= first) & (gid < first + count)).all()))
+            return _pf_pair(xr, gid)
+
+        layer = ep.ExpertParallelPrefill("fp8c", None, PF_E, (2 * PF_H, PF_H), pairs_fn=pairs_fn,
+                                         combine_fn=_pf_combine)
+        out = layer(x[lo:hi], ids[lo:hi], w[lo:hi])
+        flat = ids[lo:hi].reshape(-1)
+        valid = ((flat >= 0) & (flat < PF_E)).unsqueeze(1)
+        ref_pairs = torch.where(valid, _pf_pair(x[lo:hi].repeat_interleave(PF_K, 0), flat), torch.zeros(()))
+        want = _pf_combine(ref_pairs, w[lo:hi])
+        result[rank] = (tuple(out.shape) == (hi - lo, PF_H) and torch.equal(out, want) and all(seen))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_expert_parallel_prefill_exchange_cpu_ranks(world):
+    """Each rank's rows come back equal to the one-process pass over the same rows, bit for bit; every rank receives
+    only pairs of its own experts; one rank with no rows at all (world 3) still takes part in the exchanges."""
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    result = mp.get_context("spawn").Manager().dict()
+    mp.start_processes(_pf_worker, args=(world, port, result), nprocs=world, join=True, start_method="spawn")
+    assert dict(result) == {r: True for r in range(world)}
+
+
+def test_expert_owner_matches_expert_range():
+    for E_, world in ((128, 8), (128, 3), (10, 4), (3, 8)):
+        ids = torch.arange(-2, E_ + 3)
+        owner = ep.expert_owner(ids, E_, world)
+        for i, o in zip(ids.tolist(), owner.tolist()):
+            blocks = [r for r in range(world) if 0 <= i - ep.expert_range(E_, r, world)[0] <
+                      ep.expert_range(E_, r, world)[1]]
+            assert o == (blocks[0] if blocks else -1)
