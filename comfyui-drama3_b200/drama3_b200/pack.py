@@ -3,6 +3,7 @@ the converter step of the reference (tools/convert.py:48-82,179-215) with plain 
 layouts (fp8 block-scaled, int8 ConvRot, w4 / w6 codes) and the BASELINE ones (fp8c, w4a8, w6a8). Banks come back as
 host torch tensors in the fields moe_decode / grouped_mma / resident_prefill and the offload store take, flat over
 experts ([E * N, ...], expert e's rows contiguous)."""
+import dataclasses
 import json
 
 import torch
@@ -186,3 +187,51 @@ def banks_from_state(kind, state, layer):
         codebooks = tuple(state[f"model.layers.{layer}.mlp.experts.{bank}_proj.weight_codebook"].float()
                           for bank in ("gate_up", "down"))
     return banks[0], banks[1], codebooks
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# Packed banks dressed as comfy's quantized tensors, for the modules that recognize those (offload.kernel_bank).
+@dataclasses.dataclass
+class PackedParams:
+    """The parameter fields of comfy's TensorWiseINT8Layout / AsymW4A8Int8Layout that the expert path reads."""
+    orig_shape: tuple
+    scale: torch.Tensor
+    s_channel: torch.Tensor = None
+    codebook: torch.Tensor = None
+    convrot: bool = True
+    convrot_groupsize: int = CONVROT_GROUP
+    group_size: int = CODES_GROUP
+    correction: object = None
+    transposed: bool = False
+
+
+class PackedWeight:
+    """A flat packed bank [E * N, ...] with the attributes of comfy's QuantizedTensor (`_qdata`, `_params`,
+    `_layout_cls`), so that offload.kernel_bank, model.Experts and offload.ExpertStore take it as they take a
+    converted checkpoint's expert weight."""
+
+    def __init__(self, layout, qdata, params):
+        self._layout_cls, self._qdata, self._params = layout, qdata, params
+
+    def to(self, device):
+        """The same bank with every tensor on `device`."""
+        moved = {f.name: (v.to(device) if torch.is_tensor(v) else v)
+                 for f in dataclasses.fields(self._params) for v in [getattr(self._params, f.name)]}
+        return PackedWeight(self._layout_cls, self._qdata.to(device), PackedParams(**moved))
+
+
+def packed_weight(kind, w, threads=0, codebook=CODEBOOK4):
+    """Float experts w [E, N, K] -> a PackedWeight of layout `kind` ("int8", "w4", "w6") on the host."""
+    if kind not in ("int8", "w4", "w6"):
+        raise ValueError(f"no quantized-tensor form for {kind}: fp8 banks are FP8Experts parameters, the BASELINE "
+                         "layouts are plain fields")
+    w = torch.as_tensor(w)
+    K = w.shape[-1]
+    fields = pack_bank(kind, w, threads, codebook)
+    rows = fields["_qdata"].shape[0]
+    if kind == "int8":
+        return PackedWeight("TensorWiseINT8Layout", fields["_qdata"],
+                            PackedParams((rows, K), scale=fields["scale"].view(rows, 1)))
+    book = torch.as_tensor(codebook, dtype=torch.float32).clone() if kind == "w4" else None
+    return PackedWeight("AsymW4A8Int8Layout", fields["_qdata"],
+                        PackedParams((rows, K), scale=fields["scale"], s_channel=fields["s_channel"], codebook=book))

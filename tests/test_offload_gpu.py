@@ -190,3 +190,32 @@ def test_moe_block_batched_lines(cuda):
         ids_r, _ = kernels.route(logits[r:r + 1], 8)
         assert torch.equal(ids[r], ids_r[0])
     assert together.shape == x.shape and gd.rel_l2(together.float(), alone.float()) <= 1e-3
+
+
+@pytest.mark.parametrize("kind, bound", [("int8", 0.03), ("w6", 0.07), ("w4", 0.25)])
+def test_packed_float_experts_through_the_module(cuda, kind, bound):
+    """Float experts N(0, 0.02) packed on the host (pack.packed_weight), moved to the GPU and run by Experts for 4
+    lines: against the oracle on the packed fields (rel-L2 1e-3) and against the float experts themselves (the
+    packing's own error, layout by layout)."""
+    from drama3_b200 import pack
+    Ef = 8
+    gen = torch.Generator().manual_seed(150)
+    gu_f = torch.randn((Ef, 2 * I, H), generator=gen) * 0.02
+    dn_f = torch.randn((Ef, H, I), generator=gen) * 0.02
+    mods = [type("Bank", (), {"weight": pack.packed_weight(kind, t).to(cuda), "num_experts": Ef})()
+            for t in (gu_f, dn_f)]
+    ex = Experts(Ef, *mods)
+    x = gd.rand_rows(4, H, 151, cuda)
+    ids, w = gd.rand_routing(4, Ef, 8, 152, cuda)
+    out = ex(x, ids, w).float()
+    banks = tuple(offload.kernel_bank(m.weight)[1] for m in mods)
+    cbs = tuple(m.weight._params.codebook for m in mods)
+    assert gd.rel_l2(out, gd.oracle_decode(kind, x, ids, w, banks, cbs, H)) <= 1e-3
+    xf, idc, wc = x.double().cpu(), ids.cpu(), w.double().cpu()
+    ref = torch.zeros((4, H), dtype=torch.float64)
+    for t in range(4):
+        for j in range(8):
+            e = int(idc[t, j])
+            h = gu_f[e].double() @ xf[t]
+            ref[t] += wc[t, j] * (dn_f[e].double() @ (torch.nn.functional.silu(h[:I]) * h[I:]))
+    assert gd.rel_l2(out, ref) <= bound

@@ -292,3 +292,23 @@ def test_packers_property_against_oracle():
             assert same(g, want[name]), (kind, name)
 
     check()
+
+
+@pytest.mark.parametrize("kind", ["int8", "w4", "w6"])
+def test_packed_weight_is_recognized_as_a_kernel_bank(kind):
+    """A packed bank dressed as a quantized tensor is what offload.kernel_bank recognizes, with pack_bank's fields;
+    the host bank of the slot cache takes it as well."""
+    from drama3_b200 import offload
+    w = torch.from_numpy(rows((4, 64, 512), 40))
+    weight = pack.packed_weight(kind, w, threads=2)
+    found = offload.kernel_bank(weight)
+    assert found is not None and found[0] == kind
+    want = pack.pack_bank(kind, w)
+    assert set(found[1]) == set(want)
+    for name in want:
+        assert torch.equal(found[1][name].reshape(want[name].shape), want[name]), name
+    bank = offload.QuantHostBank(type("M", (), {"weight": weight, "num_experts": 4})(), pin=False)
+    assert bank.kernel == kind and bank.rows("_qdata") == 64
+    assert weight.to("cpu")._qdata.data_ptr() != 0
+    with pytest.raises(ValueError):
+        pack.packed_weight("fp8c", w)
