@@ -211,7 +211,7 @@ def prefill_plan(topk_idx, num_experts):
         skip its rows and record the bad-slot fault, as they do for such a group of the host-side plan);
       tiles: a host int from the shapes alone that bounds the row tiles of any routing, (P + (t - 1)(E + 1)) // t for
         t rows per tile (the kernels run the number of tiles the groups need, counted on the device)."""
-    flat = topk_idx.reshape(-1)
+    flat = topk_idx.reshape(-1).to(torch.int64)
     E, P = num_experts, flat.numel()
     key = torch.where((flat >= 0) & (flat < E), flat, torch.full_like(flat, E))
     onehot = (key.unsqueeze(1) == torch.arange(E + 1, device=flat.device)).to(torch.int32)

@@ -71,3 +71,10 @@ def test_tile_bound_is_tight_for_the_worst_routing():
     _, _, groups, tiles = offload.prefill_plan(ids, E)
     need = kernels.grouped_tiles(groups[:, 4].tolist())
     assert need == 2 * E and tiles == need
+
+
+def test_plan_of_int32_ids_equals_int64():
+    ids = torch.randint(0, 32, (100, 8), generator=torch.Generator().manual_seed(9))
+    a = offload.prefill_plan(ids, 32)
+    b = offload.prefill_plan(ids.to(torch.int32), 32)
+    assert all(torch.equal(u, v) for u, v in zip(a[:3], b[:3])) and a[3] == b[3]
