@@ -184,7 +184,8 @@ def expert_owner(ids, num_experts, world):
 def local_pairs(kind, banks, e_count, rows, codebooks, x, local_ids):
     """fp32 [R, rows[1]]: rows x [R, H] (bfloat16 or float32) each through its expert local_ids [R] (0-based in this
     rank's block of e_count experts, banks = local_banks), unweighted, in the given order: the two grouped GEMMs of
-    the prompt pass over the rows sorted by expert on the device (offload.prefill_plan), then put back in order."""
+    the prompt pass over the rows sorted by expert on the device (offload.prefill_plan), then put back in order. Rows
+    whose id is outside [0, e_count) (padding) are not computed: their output rows are unspecified."""
     from . import offload
     if x.shape[0] == 0:
         return torch.zeros((0, rows[1]), dtype=torch.float32, device=x.device)
@@ -192,7 +193,7 @@ def local_pairs(kind, banks, e_count, rows, codebooks, x, local_ids):
             and kernels.grouped_mma_fits(rows[1], rows[0] // 2)):
         raise ValueError("an expert-parallel prompt pass runs on the tensor-core kernels only (bfloat16 or float32 "
                          "rows, N % 128 == 0, K % 256 == 0)")
-    order, pos, groups, tiles = offload.prefill_plan(local_ids.view(-1, 1), e_count)
+    order, pos, groups, tiles = offload.prefill_plan(local_ids.view(-1, 1), e_count, drop_invalid=True)
     rotated = kind in offload.ROTATED_KINDS
     hidden = kernels.grouped_mma(kind, x, groups, banks[0], codebooks[0], rows[0], tiles, row_index=order,
                                  rotate=rotated)
@@ -214,25 +215,83 @@ class ExpertParallelPrefill:
     the tensor cores, and its fp32 output is sent back (all-to-all); the rank then weights and sums its rows' pairs in
     rank order (kernels.prefill_combine). Every pair's output is computed alone and crosses exactly, so the result is
     bit for bit the one-GPU prompt pass of the same rows (offload.resident_prefill). Pairs whose id is outside
-    [0, num_experts) add nothing. The split sizes are read back to the host once per call (the collectives need them).
+    [0, num_experts) add nothing.
+    The split sizes of the all-to-alls are read back to the host once per call. With `capacity` (pairs a rank sends
+    to each rank, at most; T_r * k always suffices) the exchanges move fixed blocks of that many rows instead, padded,
+    and nothing is read back, so that the call can be captured in a CUDA graph; pairs beyond the capacity add nothing
+    and are counted in `self.dropped` (a device tensor).
     `pairs_fn(x, ids) -> fp32 [R, H]` (global expert ids) and `combine_fn(pair_out [T_r * k, H], weights) -> [T_r, H]`
     replace the kernels when given, so that the exchange runs on CPU ranks."""
 
     def __init__(self, kind, banks, num_experts, rows, group=None, codebooks=(None, None), pairs_fn=None,
-                 combine_fn=None):
+                 combine_fn=None, capacity=None):
         self.kind, self.banks, self.num_experts, self.rows, self.group = kind, banks, num_experts, rows, group
         self.codebooks, self.pairs_fn, self.combine_fn = codebooks, pairs_fn, combine_fn
         self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
         self.e_first, self.e_count = expert_range(num_experts, self.rank, self.world)
         self.firsts = [expert_range(num_experts, r, self.world)[0] for r in range(self.world)]
+        self.capacity = capacity
+        self.dropped = None
 
     def pairs(self, x, local_ids):
         if self.pairs_fn is not None:
-            return self.pairs_fn(x, local_ids.to(torch.int64) + self.e_first)
+            valid = local_ids >= 0
+            if bool(valid.all()):
+                return self.pairs_fn(x, local_ids.to(torch.int64) + self.e_first)
+            out = torch.zeros((x.shape[0], self.rows[1]), dtype=torch.float32, device=x.device)
+            if bool(valid.any()):
+                out[valid] = self.pairs_fn(x[valid], local_ids[valid].to(torch.int64) + self.e_first)
+            return out
         return local_pairs(self.kind, self.banks, self.e_count, self.rows, self.codebooks, x, local_ids)
+
+    def _combine(self, x, pair_out, topk_weight):
+        T, k = topk_weight.shape
+        if self.combine_fn is not None:
+            return self.combine_fn(pair_out, topk_weight)
+        if T == 0:
+            return torch.empty((0, self.rows[1]), dtype=x.dtype, device=x.device)
+        pos = torch.arange(T * k, device=x.device).view(T, k)
+        dtype = torch.float32 if x.dtype == torch.float32 else torch.bfloat16
+        return kernels.prefill_combine(pair_out, pos, topk_weight, dtype=dtype).to(x.dtype)
+
+    def _fixed(self, x, topk_idx, topk_weight):
+        """The exchange in fixed blocks of `capacity` rows per rank pair: no host sync."""
+        from . import offload
+        T, k = topk_idx.shape
+        W, C, device = self.world, self.capacity, x.device
+        flat = topk_idx.reshape(-1).to(torch.int64)
+        owner = expert_owner(flat, self.num_experts, W)
+        # each pair's rank among the pairs going to the same rank, by the device-side counting sort
+        _, pos, groups, _ = offload.prefill_plan(owner.view(-1, 1), W)
+        dest = torch.where(owner >= 0, owner, torch.full_like(owner, W))
+        slot = pos - groups[:, 3].to(torch.int64)[dest]
+        sent = (owner >= 0) & (slot < C)
+        spill = W * C  # one extra row that pairs not sent write to, never sent
+        index = torch.where(sent, owner * C + slot, torch.full_like(slot, spill))
+        lost = ((owner >= 0) & (slot >= C)).sum()
+        self.dropped = lost if self.dropped is None else self.dropped + lost
+        firsts = torch.tensor(self.firsts, dtype=torch.int64, device=device)
+        send_x = torch.zeros((spill + 1, x.shape[1]), dtype=x.dtype, device=device)
+        send_x[index] = x[torch.arange(T * k, device=device) // k]
+        send_ids = torch.full((spill + 1,), -1, dtype=torch.int32, device=device)
+        send_ids[index] = (flat - firsts[owner.clamp(min=0)]).to(torch.int32)
+        wire = _wire(send_x[:spill])
+        recv_x = torch.empty_like(wire)
+        dist.all_to_all_single(recv_x, wire, group=self.group)
+        recv_ids = torch.empty((spill,), dtype=torch.int32, device=device)
+        dist.all_to_all_single(recv_ids, send_ids[:spill].contiguous(), group=self.group)
+        if x.dtype == torch.bfloat16:
+            recv_x = recv_x.view(torch.bfloat16)
+        y = self.pairs(recv_x, recv_ids).to(torch.float32).contiguous()
+        back = torch.empty((spill + 1, self.rows[1]), dtype=torch.float32, device=device)
+        back[spill] = 0.0
+        dist.all_to_all_single(back[:spill], y, group=self.group)
+        return self._combine(x, back[index], topk_weight)
 
     def __call__(self, x, topk_idx, topk_weight):
         """[T_r, H] in x's dtype: this rank's rows through the whole layer's experts."""
+        if self.capacity is not None:
+            return self._fixed(x, topk_idx, topk_weight)
         T, k = topk_idx.shape
         device = x.device
         flat = topk_idx.reshape(-1)
@@ -259,10 +318,4 @@ class ExpertParallelPrefill:
         dist.all_to_all_single(back, y, send_counts, recv_counts, group=self.group)
         pair_out = torch.zeros((T * k, self.rows[1]), dtype=torch.float32, device=device)
         pair_out[sel] = back
-        if self.combine_fn is not None:
-            return self.combine_fn(pair_out, topk_weight)
-        if T == 0:
-            return torch.empty((0, self.rows[1]), dtype=x.dtype, device=device)
-        pos = torch.arange(T * k, device=device).view(T, k)
-        dtype = torch.float32 if x.dtype == torch.float32 else torch.bfloat16
-        return kernels.prefill_combine(pair_out, pos, topk_weight, dtype=dtype).to(x.dtype)
+        return self._combine(x, pair_out, topk_weight)

@@ -201,7 +201,7 @@ def capturing(x):
     return x.is_cuda and torch.cuda.is_current_stream_capturing()
 
 
-def prefill_plan(topk_idx, num_experts):
+def prefill_plan(topk_idx, num_experts, drop_invalid=False):
     """The prompt's (token, rank) pairs sorted by expert on the device, with no host sync, so that a prompt pass can
     be captured in a CUDA graph (the host-side sort of drama3/offload.py:141-145 reads the counts back): a counting
     sort by per-expert prefix sums of the pairs' one-hot rows. Returns (order, pos, groups, tiles):
@@ -210,7 +210,9 @@ def prefill_plan(topk_idx, num_experts):
         tile), then one group for the pairs whose id is outside [0, E), which sort last (slot E: the grouped kernels
         skip its rows and record the bad-slot fault, as they do for such a group of the host-side plan);
       tiles: a host int from the shapes alone that bounds the row tiles of any routing, (P + (t - 1)(E + 1)) // t for
-        t rows per tile (the kernels run the number of tiles the groups need, counted on the device)."""
+        t rows per tile (the kernels run the number of tiles the groups need, counted on the device).
+    drop_invalid: the last group gets no rows, so the pairs of out-of-range ids are left out (not computed, no fault):
+    for padding rows."""
     flat = topk_idx.reshape(-1).to(torch.int64)
     E, P = num_experts, flat.numel()
     key = torch.where((flat >= 0) & (flat < E), flat, torch.full_like(flat, E))
@@ -221,7 +223,8 @@ def prefill_plan(topk_idx, num_experts):
     pos = (first.gather(0, key) + ranks.gather(1, key.unsqueeze(1)).squeeze(1) - 1).to(torch.int64)
     order = torch.empty_like(pos).scatter_(0, pos, torch.arange(P, device=flat.device))
     experts = torch.arange(E + 1, dtype=torch.int32, device=flat.device)
-    groups = torch.stack([experts, experts, torch.zeros_like(experts), first, counts], dim=1).contiguous()
+    rows = torch.cat([counts[:E], torch.zeros_like(counts[E:])]) if drop_invalid else counts
+    groups = torch.stack([experts, experts, torch.zeros_like(experts), first, rows], dim=1).contiguous()
     t = kernels.grouped_tile_rows()
     return order, pos, groups, (P + (t - 1) * (E + 1)) // t
 

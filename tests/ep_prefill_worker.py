@@ -34,6 +34,22 @@ def main():
         got = layer(x[lo:hi], ids[lo:hi], w[lo:hi])
         want = offload.resident_prefill(x[lo:hi], ids[lo:hi], w[lo:hi], full, (2 * I, H), kind, (None, None), E)
         same = same and torch.equal(got, want)
+        # fixed blocks (no split sizes read back), eagerly and captured in a CUDA graph
+        fixed = ep.ExpertParallelPrefill(kind, ep.local_banks(full, E, rank, world), E, (2 * I, H),
+                                         capacity=(T // world + 1) * 8)
+        same = same and torch.equal(fixed(x[lo:hi], ids[lo:hi], w[lo:hi]), want)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            fixed(x[lo:hi], ids[lo:hi], w[lo:hi])
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            captured = fixed(x[lo:hi], ids[lo:hi], w[lo:hi])
+        graph.replay()
+        torch.cuda.synchronize()
+        same = same and torch.equal(captured, want) and int(fixed.dropped) == 0
+        del graph
     torch.cuda.synchronize()
     fault = kernels._lib.take_fault()
     ok = torch.tensor([1.0 if same and fault == 0 else 0.0], device=device)

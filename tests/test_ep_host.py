@@ -158,6 +158,47 @@ def _pf_worker(rank, world, port, result):
         dist.destroy_process_group()
 
 
+def _pf_fixed_worker(rank, world, port, result, capacity):
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        x, ids, w = _pf_inputs()
+        lo, hi = PF_SHARDS[world][rank]
+        layer = ep.ExpertParallelPrefill("fp8c", None, PF_E, (2 * PF_H, PF_H), pairs_fn=_pf_pair,
+                                         combine_fn=_pf_combine, capacity=capacity)
+        out = layer(x[lo:hi], ids[lo:hi], w[lo:hi])
+        flat = ids[lo:hi].reshape(-1)
+        owner = ep.expert_owner(flat, PF_E, world)
+        # the pairs sent: per destination rank, the first `capacity` in (row, rank) order
+        kept = torch.zeros_like(flat, dtype=torch.bool)
+        for r in range(world):
+            kept[(owner == r).nonzero().squeeze(1)[:capacity]] = True
+        ref_pairs = torch.where(kept.unsqueeze(1), _pf_pair(x[lo:hi].repeat_interleave(PF_K, 0), flat),
+                                torch.zeros(()))
+        want = _pf_combine(ref_pairs, w[lo:hi])
+        dropped = int(((owner >= 0) & ~kept).sum())
+        result[rank] = (torch.equal(out, want), int(layer.dropped), dropped)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world, capacity", [(2, 27 * PF_K), (3, 30 * PF_K), (2, 3), (3, 5)])
+def test_expert_parallel_prefill_fixed_blocks_cpu_ranks(world, capacity):
+    """The exchange in fixed blocks (no split sizes read back): with room for every pair it equals the pass over the
+    same rows; with less, each destination takes the first `capacity` pairs and the rest add nothing and are
+    counted."""
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    result = mp.get_context("spawn").Manager().dict()
+    mp.start_processes(_pf_fixed_worker, args=(world, port, result, capacity), nprocs=world, join=True,
+                       start_method="spawn")
+    assert sorted(result) == list(range(world))
+    for same, counted, expected in result.values():
+        assert same and counted == expected
+    if capacity >= 27 * PF_K:
+        assert all(v[2] == 0 for v in result.values())
+
+
 @pytest.mark.parametrize("world", [2, 3])
 def test_expert_parallel_prefill_exchange_cpu_ranks(world):
     """Each rank's rows come back equal to the one-process pass over the same rows, bit for bit; every rank receives

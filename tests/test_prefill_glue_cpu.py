@@ -95,7 +95,7 @@ def test_local_pairs_glue_keeps_the_given_order(fakes):
         assert torch.allclose(got[j], want, rtol=1e-5, atol=1e-6)
 
 
-def _worker(rank, world, port, result):
+def _worker(rank, world, port, result, capacity=None):
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
     try:
         kernels.grouped_mma, kernels.prefill_combine = fake_grouped_mma, fake_combine
@@ -103,19 +103,20 @@ def _worker(rank, world, port, result):
         lo, hi = 90 * rank // world, 90 * (rank + 1) // world
         first, count = ep.expert_range(E, rank, world)
         local = ({"count": count, "first": first},) * 2
-        layer = ep.ExpertParallelPrefill("fp8c", local, E, (2 * I, H))
+        layer = ep.ExpertParallelPrefill("fp8c", local, E, (2 * I, H), capacity=capacity)
         got = layer(x[lo:hi], ids[lo:hi], w[lo:hi])
         want = offload.resident_prefill(x[lo:hi], ids[lo:hi], w[lo:hi], BANKS, (2 * I, H), "fp8c", (None, None), E)
-        result[rank] = bool(torch.equal(got, want))
+        result[rank] = bool(torch.equal(got, want)) and (capacity is None or int(layer.dropped) == 0)
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_expert_parallel_prefill_default_path_on_cpu_ranks(world):
+@pytest.mark.parametrize("world, capacity", [(2, None), (3, None), (2, 45 * K_TOP), (3, 30 * K_TOP)])
+def test_expert_parallel_prefill_default_path_on_cpu_ranks(world, capacity):
+    """Split sizes read back, or fixed blocks of `capacity` rows (padding rows left out of the GEMMs' groups)."""
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     result = mp.get_context("spawn").Manager().dict()
-    mp.start_processes(_worker, args=(world, port, result), nprocs=world, join=True, start_method="spawn")
+    mp.start_processes(_worker, args=(world, port, result, capacity), nprocs=world, join=True, start_method="spawn")
     assert dict(result) == {r: True for r in range(world)}
