@@ -147,3 +147,24 @@ def test_prefill_pairs_of_emulated_ranks_equal_one_gpu(cuda, kind):
     torch.cuda.synchronize()
     assert _lib.take_fault() == 0
     assert torch.equal(got, want)
+
+
+def test_local_pairs_leave_padding_rows_out(cuda):
+    """Rows marked -1 (the padding of the fixed-block exchange) are left out of the grouped GEMMs without a fault;
+    the other rows equal the same call without the padding, bit for bit."""
+    kind, R, count = "fp8c", 300, 11
+    full = (gd.rand_bank(kind, E * 2, 2 * I, H, 140, cuda), gd.rand_bank(kind, E * 2, H, I, 141, cuda))
+    local = ep.local_banks(full, E * 2, 0, 3)
+    x = gd.rand_rows(R, H, 142, cuda)
+    ids = torch.randint(0, count, (R,), generator=torch.Generator().manual_seed(143)).to(torch.int32).to(cuda)
+    pad = torch.zeros(R, dtype=torch.bool)
+    pad[::3] = True
+    pad = pad.to(cuda)
+    _lib.take_fault()
+    padded = ep.local_pairs(kind, local, count, (2 * I, H), (None, None), x,
+                            torch.where(pad, torch.full_like(ids, -1), ids))
+    keep = (~pad).nonzero().squeeze(1)
+    plain = ep.local_pairs(kind, local, count, (2 * I, H), (None, None), x[keep], ids[keep])
+    torch.cuda.synchronize()
+    assert _lib.take_fault() == 0
+    assert torch.equal(padded[keep], plain)
