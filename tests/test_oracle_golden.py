@@ -114,3 +114,15 @@ def test_resolve_invariants():
         if key >= 0:
             assert st["table"][key] == slot
     assert int(st["reads"].sum()) == 40 * 4 * 4
+
+
+def test_cpu_baseline_port_equals_reference_cpu_forward(golden):
+    """The CPU baseline's torch port (oracle/cpu_port.py) on the golden decode row: bit for bit the reference's own
+    FP8Experts CPU forward (drama3/offload.py:771-784) in fp32."""
+    import torch
+    from oracle import cpu_port
+    t = {k: torch.from_numpy(golden[k]) for k in ("fp8_decode_x", "fp8_decode_ids", "fp8_decode_w", "fp8_gu_w",
+                                                   "fp8_gu_s", "fp8_dn_w", "fp8_dn_s")}
+    out = cpu_port.fp8_decode_lines(t["fp8_decode_x"], t["fp8_decode_ids"], t["fp8_decode_w"], t["fp8_gu_w"],
+                                    t["fp8_gu_s"], t["fp8_dn_w"], t["fp8_dn_s"], dtype=torch.float32)
+    np.testing.assert_array_equal(out.numpy(), golden["fp8_decode_out"])
