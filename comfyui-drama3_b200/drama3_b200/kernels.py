@@ -219,7 +219,8 @@ GM_ROTATE, GM_SWIGLU = 1, 2
 def grouped_mma(kind, x, groups, fields, codebook, n, tiles, row_index=None, rotate=False, swiglu=False):
     """[rows, n] float32 for the sorted rows through their experts, on the tensor cores, for a bank held whole on the
     GPU: the grouped_fp8 / grouped_int8 / grouped_codes results with every group's slot = its expert's index in
-    `fields` (drama3/offload.py:126-149). groups [g, 5] int32 on the GPU; tiles = grouped_tiles(row counts). Sorted
+    `fields` (drama3/offload.py:126-149). groups [g, 5] int32 on the GPU; tiles = grouped_tiles(row counts), or any
+    bound on it (the kernels count the tiles the groups need on the device; offload.prefill_plan gives one). Sorted
     row s is x[row_index[s]] (x float32 or bfloat16; row_index int64, or None for x itself), optionally through
     SwiGLU (x holds gate | up) and the ConvRot rotation first, as kernels.rotate would give it. Rows outside every
     group are left unset."""
