@@ -125,7 +125,8 @@ int d3_grouped_codes(const float* x, int x_rows, const int* groups, int n_groups
  * `mode`: D3_GM_SWIGLU (x rows hold 2K columns, gate then up: SiLU(gate) * up, the reference rotate kernel's form),
  * then D3_GM_ROTATE (ConvRot over each 256 columns, as kernels.rotate) - so a prompt pass needs no separate gather,
  * SwiGLU or rotation launches. tiles = sum over groups of ceil(rows / d3_grouped_mma_tile_rows()) (an upper bound
- * is allowed; fewer records D3_FAULT_TILES and skips the rows past them).
+ * is allowed: the kernels count the tiles on the device; fewer records D3_FAULT_TILES and skips the rows past them).
+ * Groups of 0 rows get no tile, so a caller may list every expert and build the groups on the device.
  * N % 128 == 0, K % 256 == 0, K <= 2048; x, out and weight 16-byte aligned, workspace 256-byte aligned,
  * d3_grouped_mma_workspace(tiles, K) bytes (no initial state). No counterpart in the reference's kernel set beyond
  * the grouped kernels it replaces for resident banks. */
