@@ -192,6 +192,18 @@ def time_replays(graph, steps, stream):
     return start.elapsed_time(end) / steps
 
 
+def replay_spread(graph, steps, stream):
+    """{median, p90} ms of `steps` single replays of `graph`, each between its own CUDA events on `stream`."""
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for start, end in events:
+        start.record(stream)
+        graph.replay()
+        end.record(stream)
+    torch.cuda.synchronize()
+    t = sorted(start.elapsed_time(end) for start, end in events)
+    return {"steps": steps, "ms_median": t[len(t) // 2], "ms_p90": t[min(len(t) - 1, (9 * len(t)) // 10)]}
+
+
 def decode_leg(kernels, device, kind, lines, steps, warmup, stream, n_layers, layers):
     """{tokens_per_s, ms_per_step, hbm_gbs, frac, ...} of the fused decode of `lines` rows through n_layers layers;
     layers = (banks, ids, weights)."""
@@ -467,6 +479,11 @@ def main():
             torch.cuda.profiler.start()
             ms = time_replays(graph, args.steps, stream)
             torch.cuda.profiler.stop()
+        # the spread of single steps, after the timed region (this rank's)
+        try:
+            spread = replay_spread(graph, max(5, min(args.steps, 50)), stream)
+        except Exception as exc:  # the spread must not sink the bench line
+            spread = {"error": repr(exc)[:200]}
     if pg:
         t = torch.tensor([ms], device=device)
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
@@ -568,7 +585,7 @@ def main():
                              "kernel": kernel_of(kind, args.lines)[0],
                              "bytes_per_launch": step_bytes / n_layers, "us_per_layer": 1e3 * ms / n_layers,
                              "launch_time": "step time / layers: the launches run back to back in one graph"},
-                "gpu_launches": n_layers * args.steps,
+                "gpu_launches": n_layers * args.steps, "step_spread": spread,
                 "clocks": clocks.summary()}
         line.update(extras)
         print(json.dumps(line), flush=True)
