@@ -19,7 +19,7 @@ import ctypes
 import torch
 import torch.distributed as dist
 
-from . import _lib, kernels
+from . import _lib, kernels, offload
 
 EP_MAX_RANKS = 8
 
@@ -186,7 +186,6 @@ def local_pairs(kind, banks, e_count, rows, codebooks, x, local_ids):
     rank's block of e_count experts, banks = local_banks), unweighted, in the given order: the two grouped GEMMs of
     the prompt pass over the rows sorted by expert on the device (offload.prefill_plan), then put back in order. Rows
     whose id is outside [0, e_count) (padding) are not computed: their output rows are unspecified."""
-    from . import offload
     if x.shape[0] == 0:
         return torch.zeros((0, rows[1]), dtype=torch.float32, device=x.device)
     if not (x.dtype in (torch.bfloat16, torch.float32) and kernels.grouped_mma_fits(rows[0], x.shape[1])
@@ -256,7 +255,6 @@ class ExpertParallelPrefill:
 
     def _fixed(self, x, topk_idx, topk_weight):
         """The exchange in fixed blocks of `capacity` rows per rank pair: no host sync."""
-        from . import offload
         T, k = topk_idx.shape
         W, C, device = self.world, self.capacity, x.device
         flat = topk_idx.reshape(-1).to(torch.int64)
