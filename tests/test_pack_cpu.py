@@ -265,11 +265,11 @@ def _draw_rows(data, rows, K):
 
 
 def test_packers_property_against_oracle():
-    """Drawn rows through every packer, byte for byte against the oracle (hypothesis, 40 draws)."""
+    """Drawn rows through every packer, byte for byte against the oracle (hypothesis, 40 draws, the same every run)."""
     from hypothesis import HealthCheck, given, settings
     from hypothesis import strategies as st
 
-    @settings(max_examples=40, deadline=None, suppress_health_check=[HealthCheck.too_slow])
+    @settings(max_examples=40, deadline=None, derandomize=True, suppress_health_check=[HealthCheck.too_slow])
     @given(st.data())
     def check(data):
         kind = data.draw(st.sampled_from(["fp8", "int8", "w4", "w6", "fp8c", "w4a8", "w6a8"]))
