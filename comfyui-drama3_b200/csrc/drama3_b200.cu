@@ -511,23 +511,36 @@ static int decode_tc8(const d3::DecodeArgs& a, const DeviceInfo& d, cudaStream_t
   }
 }
 
+// The host-side checks of a decode call's arguments other than its workspace: 0 or an error code. Every decode entry
+// point runs them before it asks the runtime anything or puts anything on the stream.
+static int check_decode(int fmt, const void* x, int M, int k, int E, int e_first, int e_count, int H, int I,
+                        const int64_t* ids, const float* weights, const uint8_t* w13, const void* s13,
+                        const float* c13, const uint8_t* w2, const void* s2, const float* c2,
+                        const float* codebook13, const float* codebook2, bool has_out, const void* exchange) {
+  if (fmt < 0 || fmt >= d3::FMT_COUNT) return D3_ERR_ARG;
+  if (M < 1 || M > 16 || k < 1 || k > 32 || M * k > d3::DEC_MAX_PAIRS || E < 1) return D3_ERR_ARG;
+  if (e_first < 0 || e_count < 1 || e_first + e_count > E) return D3_ERR_ARG;
+  if (H != d3::DEC_H || (I != 512 && I != 768)) return D3_ERR_ARG;
+  if (!x || !ids || !weights || !w13 || !s13 || !w2 || !s2 || !has_out) return D3_ERR_ARG;
+  if (d3::fmt_codes(fmt) && (!c13 || !c2)) return D3_ERR_ARG;
+  if (fmt == d3::FMT_W4 && (!codebook13 || !codebook2)) return D3_ERR_ARG;
+  if (!aligned(x, 16) || !aligned(w13, 16) || !aligned(w2, 16) || !aligned(s13, 16) || !aligned(s2, 16) ||
+      !aligned(exchange, 8))
+    return D3_ERR_ALIGN;
+  return D3_OK;
+}
+
 static int decode_common(int fmt, const void* x, int x_bf16, int M, int k, int E, int e_first, int e_count, int H,
                          int I, const int64_t* ids, const float* weights, const uint8_t* w13, const void* s13,
                          const float* c13, const uint8_t* w2, const void* s2, const float* c2,
                          const float* codebook13, const float* codebook2, uint16_t* out, float* out_f32,
                          const void* exchange, void* workspace, size_t workspace_bytes, void* stream) {
-  if (fmt < 0 || fmt >= d3::FMT_COUNT) return D3_ERR_ARG;
-  if (M < 1 || M > 16 || k < 1 || k > 32 || M * k > d3::DEC_MAX_PAIRS || E < 1) return D3_ERR_ARG;
-  if (e_first < 0 || e_count < 1 || e_first + e_count > E) return D3_ERR_ARG;
-  if (H != d3::DEC_H || (I != 512 && I != 768)) return D3_ERR_ARG;
-  if (!x || !ids || !weights || !w13 || !s13 || !w2 || !s2 || (!out && !out_f32 && !exchange) || !workspace)
-    return D3_ERR_ARG;
-  if (d3::fmt_codes(fmt) && (!c13 || !c2)) return D3_ERR_ARG;
-  if (fmt == d3::FMT_W4 && (!codebook13 || !codebook2)) return D3_ERR_ARG;
+  if (int st = check_decode(fmt, x, M, k, E, e_first, e_count, H, I, ids, weights, w13, s13, c13, w2, s2, c2,
+                            codebook13, codebook2, out || out_f32 || exchange, exchange))
+    return st;
+  if (!workspace) return D3_ERR_ARG;
   if (workspace_bytes < d3_moe_decode_workspace(M, k, I)) return D3_ERR_WORKSPACE;
-  if (!aligned(x, 16) || !aligned(w13, 16) || !aligned(w2, 16) || !aligned(workspace, 256) || !aligned(s13, 16) ||
-      !aligned(s2, 16) || !aligned(exchange, 8))
-    return D3_ERR_ALIGN;
+  if (!aligned(workspace, 256)) return D3_ERR_ALIGN;
   DeviceInfo d;
   if (int st = device_info(&d)) return st;
   const size_t P = (size_t)M * k;
@@ -686,8 +699,14 @@ extern "C" int d3_moe_decode_static(int fmt, const void* x, int x_bf16, int M, i
                                     const float* c13, const uint8_t* w2, const void* s2, const float* c2,
                                     const float* codebook13, const float* codebook2, uint16_t* out, void* stream) {
   if (M < 1 || k < 1 || I < 1) return D3_ERR_ARG;
-  if ((long long)M * k > 128 || I > 768 || H != d3::DEC_H || d3_moe_decode_workspace(M, k, I) > kStaticScratchBytes)
+  if ((long long)M * k > 128 || I > 768 || d3_moe_decode_workspace(M, k, I) > kStaticScratchBytes)
     return D3_ERR_TOO_LARGE;
+  // every other argument is checked before the array is looked up or anything is put on the stream
+  if (int st = check_decode(fmt, x, M, k, E, 0, E, H, I, ids, weights, w13, s13, c13, w2, s2, c2, codebook13,
+                            codebook2, out != nullptr, nullptr))
+    return st;
+  DeviceInfo d;
+  if (int st = device_info(&d)) return st;
   void* ws = nullptr;
   if (int st = static_scratch(&ws)) return st;
   // The array keeps the last call's contents; of them only the synchronization words at its end must start at zero

@@ -231,6 +231,15 @@ class ExpertParallelPrefill:
         self.firsts = [expert_range(num_experts, r, self.world)[0] for r in range(self.world)]
         self.capacity = capacity
         self.dropped = None
+        self._firsts = {}
+
+    def firsts_on(self, device):
+        """Each rank's first expert as an int64 tensor on `device`, made on first use and kept: a call captured in a
+        CUDA graph cannot copy it in from host memory."""
+        device = torch.device(device)
+        if device not in self._firsts:
+            self._firsts[device] = torch.tensor(self.firsts, dtype=torch.int64, device=device)
+        return self._firsts[device]
 
     def pairs(self, x, local_ids):
         if self.pairs_fn is not None:
@@ -268,7 +277,7 @@ class ExpertParallelPrefill:
         index = torch.where(sent, owner * C + slot, torch.full_like(slot, spill))
         lost = ((owner >= 0) & (slot >= C)).sum()
         self.dropped = lost if self.dropped is None else self.dropped + lost
-        firsts = torch.tensor(self.firsts, dtype=torch.int64, device=device)
+        firsts = self.firsts_on(device)
         send_x = torch.zeros((spill + 1, x.shape[1]), dtype=x.dtype, device=device)
         send_x[index] = x[torch.arange(T * k, device=device) // k]
         send_ids = torch.full((spill + 1,), -1, dtype=torch.int32, device=device)
@@ -302,7 +311,7 @@ class ExpertParallelPrefill:
         send_counts, recv_counts = counts.tolist(), recv.tolist()
         n_send, n_recv = sum(send_counts), sum(recv_counts)
         sel = order[:n_send]
-        firsts = torch.tensor(self.firsts, dtype=torch.int64, device=device)
+        firsts = self.firsts_on(device)
         send_ids = (flat[sel] - firsts[owner[sel]]).to(torch.int32)
         send_x = _wire(x[sel // k].contiguous())
         recv_x = torch.empty((n_recv, send_x.shape[1]), dtype=send_x.dtype, device=device)

@@ -286,7 +286,7 @@ def moe_decode_ep(kind, x, ids, weights, banks, e_first, num_experts, codebooks=
     if partial is None and exchange is None:
         partial = torch.empty((M, H), dtype=torch.float32, device=x.device)
     if workspace is None:
-        workspace = decode_workspace(M, k, I, x.device)
+        workspace = _default_workspace(M, k, I, x.device)
     x = x.contiguous()
     ids = ids.reshape(M, k).contiguous()
     weights = weights.reshape(M, k).float().contiguous()
@@ -319,6 +319,23 @@ def decode_workspace(rows, k, intermediate, device):
     return torch.zeros((size,), dtype=torch.uint8, device=device)
 
 
+_WORKSPACES = {}
+
+
+def _default_workspace(rows, k, intermediate, device):
+    """The workspace of a decode call made without one: one per (device, stream, rows, k, intermediate), made on first
+    use and kept, so repeated calls allocate and clear nothing (calls on one stream never overlap; calls on different
+    streams get different workspaces). During a CUDA-graph capture a fresh one is made (and zeroed) inside the
+    graph instead, which owns it."""
+    device = torch.device(device)
+    if torch.cuda.is_current_stream_capturing():
+        return decode_workspace(rows, k, intermediate, device)
+    key = (device, torch.cuda.current_stream(device).cuda_stream, rows, k, intermediate)
+    if key not in _WORKSPACES:
+        _WORKSPACES[key] = decode_workspace(rows, k, intermediate, device)
+    return _WORKSPACES[key]
+
+
 def moe_decode(kind, x, ids, weights, banks, codebooks=(None, None), workspace=None, out=None):
     """[M, H] bfloat16: rows x [M, H] (bfloat16 or float32, M <= 16) through their routed experts ids [M, k] (int64)
     mixed by weights [M, k], with banks (gate_up, down) held whole on the GPU in the reference layouts:
@@ -339,7 +356,7 @@ def moe_decode(kind, x, ids, weights, banks, codebooks=(None, None), workspace=N
     if out is None:
         out = torch.empty((M, H), dtype=torch.bfloat16, device=x.device)
     if workspace is None:
-        workspace = decode_workspace(M, k, I, x.device)
+        workspace = _default_workspace(M, k, I, x.device)
     x = x.contiguous()
     ids = ids.reshape(M, k).contiguous()
     weights = weights.reshape(M, k).float().contiguous()

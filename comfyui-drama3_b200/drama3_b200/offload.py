@@ -40,6 +40,8 @@ ADMIT = 6.0
 MAX_DECODE_ROWS = 16
 # formats whose activations are ConvRot-rotated; the BASELINE layouts (no reference kernels, fused paths only)
 ROTATED_KINDS = ("int8", "w4", "w6")
+# layout name of the BASELINE int-weight / int8-activation banks dressed as quantized tensors (pack.packed_weight)
+WA8_LAYOUT = "Drama3B200GroupInt8ActLayout"
 BASELINE_KINDS = ("fp8c", "w4a8", "w6a8")
 
 
@@ -80,7 +82,9 @@ def kernel_bank(weight):
     """(kind, fields) of a flat quantized bank [E * out, ...] the kernels read, or None (drama3/offload.py:73-90):
     "int8" = TensorWiseINT8Layout with ConvRot over 256 columns, fields {_qdata, scale}; "w4" / "w6" =
     AsymW4A8Int8Layout with 16-column groups, ConvRot 256, no correction, not transposed, fields
-    {_qdata, scale, s_channel}, 4 bits with a codebook or 6 bits without. K must be at most 2048."""
+    {_qdata, scale, s_channel}, 4 bits with a codebook or 6 bits without. K must be at most 2048.
+    This library's own layout for the BASELINE int8-activation banks, WA8_LAYOUT (int4 two per byte or 6-bit four
+    per three bytes along K, bf16 scales per 128 columns, fields {_qdata, scale}), gives "w4a8" / "w6a8"."""
     if not _is_quantized(weight) or weight._qdata.ndim != 2:
         return None
     params, fields = weight._params, per_row_fields(weight)
@@ -90,6 +94,10 @@ def kernel_bank(weight):
     if weight._layout_cls == "TensorWiseINT8Layout":
         convrot = getattr(params, "convrot", False) and params.convrot_groupsize == 256
         return ("int8", fields) if convrot and names == {"_qdata", "scale"} else None
+    if weight._layout_cls == WA8_LAYOUT:
+        bits = weight._qdata.shape[1] * 8 // params.orig_shape[-1]
+        ok = params.group_size == 128 and bits in (4, 6) and names == {"_qdata", "scale"}
+        return (f"w{bits}a8", fields) if ok else None
     if weight._layout_cls != "AsymW4A8Int8Layout":
         return None
     if (params.group_size != 16 or params.convrot_groupsize != 256 or params.correction is not None
@@ -116,6 +124,23 @@ def quantized_grouped(kind, x, groups, slot_fields, host_fields, rows, codebook)
     return kernels.grouped_codes(x, groups, slot_fields, host_fields, codebook, int(kind[1]), rows)
 
 
+def swiglu(h):
+    """SiLU of the first half times the second half (every fused gate_up bank holds its gate rows first)."""
+    gate, up = h.chunk(2, dim=-1)
+    return nn.functional.silu(gate) * up
+
+
+def expert_chain(kind, x, project, always):
+    """[rows, H] float32: rows x through their experts, unweighted: gate_up, SwiGLU, down. `project(index, rows)` runs
+    bank `index`'s kernel (0 = gate_up, 1 = down) on float32 (fp8) or rotated rows. Quantized banks hold their
+    weights in the ConvRot basis, so their inputs are rotated first, the SwiGLU fused into the second rotation
+    (drama3/offload.py:112-123 for a decode row, :126-135 for grouped rows). `always` is an int32 1 on the GPU."""
+    if kind == "fp8":
+        return project(1, swiglu(project(0, x.float())))
+    hidden = project(0, kernels.rotate(x, always))
+    return project(1, kernels.rotate(hidden, always, swiglu=True))
+
+
 # shapes the fused decode kernel is built for (hidden 2048; intermediate 512 as the model, 768 as the benchmark)
 FUSED_HIDDEN, FUSED_INTERMEDIATE, FUSED_MAX_PAIRS = 2048, (512, 768), 128
 
@@ -140,21 +165,19 @@ def fused_decode_fits(hidden, intermediate, rows, k):
 
 def _decode_sequence(x, ids, weights, banks, rows, kind, codebooks):
     """One row through the reference's kernel sequence (drama3/offload.py:112-123): gemv, SwiGLU [+ rotation], gemv,
-    weighted sum; used for shapes the fused kernel is not built for."""
-    gate_up, down = banks
+    weighted sum; used for shapes the fused kernel is not built for. Expert e sits in slot e (plan code 0)."""
     if kind in BASELINE_KINDS:
         raise ValueError(f"{kind} banks decode through the fused kernel only (hidden 2048, intermediate 512 / 768)")
     plan = torch.stack((ids.to(torch.int32), torch.zeros_like(ids, dtype=torch.int32)), dim=-1)
-    if kind == "fp8":
-        gate, up = kernels.gemv_fp8(x.float(), ids, plan, gate_up, gate_up, rows[0]).chunk(2, dim=-1)
-        out = kernels.gemv_fp8(nn.functional.silu(gate) * up, ids, plan, down, down, rows[1])
-        return kernels.weighted_sum(out, weights.float())
     took_over, always = torch.arange(2, dtype=torch.int32, device=x.device).split(1)
-    hidden = quantized_gemv(kind, kernels.rotate(x, always), ids, plan, took_over, False, gate_up, gate_up, rows[0],
-                            codebooks[0])
-    out = quantized_gemv(kind, kernels.rotate(hidden, always, swiglu=True), ids, plan, took_over, False, down, down,
-                         rows[1], codebooks[1])
-    return kernels.weighted_sum(out, weights.float())
+
+    def project(index, rows_in):
+        if kind == "fp8":
+            return kernels.gemv_fp8(rows_in, ids, plan, banks[index], banks[index], rows[index])
+        return quantized_gemv(kind, rows_in, ids, plan, took_over, False, banks[index], banks[index], rows[index],
+                              codebooks[index])
+
+    return kernels.weighted_sum(expert_chain(kind, x, project, always), weights.float())
 
 
 def resident_decode_lines(x, ids, weights, banks, rows, kind, codebooks, workspace=None):
@@ -176,15 +199,16 @@ def resident_decode(x, ids, weights, banks, rows, kind, codebooks):
 
 
 def grouped_experts(sorted_x, groups, slot_banks, host_banks, rows, kind, codebooks, always):
-    """[rows, H] float32: sorted_x's rows through their experts, one grouped kernel per bank (drama3/offload.py:126-135);
-    `always` is an int32 1 on the GPU."""
-    if kind == "fp8":
-        gate, up = kernels.grouped_fp8(sorted_x.float(), groups, slot_banks[0], host_banks[0], rows[0]).chunk(2, dim=-1)
-        return kernels.grouped_fp8(nn.functional.silu(gate) * up, groups, slot_banks[1], host_banks[1], rows[1])
-    hidden = quantized_grouped(kind, kernels.rotate(sorted_x.float(), always), groups, slot_banks[0], host_banks[0],
-                               rows[0], codebooks[0])
-    return quantized_grouped(kind, kernels.rotate(hidden, always, swiglu=True), groups, slot_banks[1], host_banks[1],
-                             rows[1], codebooks[1])
+    """[rows, H] float32: sorted_x's rows through their experts with the reference-API grouped kernels, each group
+    reading its expert from its slot or from host memory (drama3/offload.py:126-135); `always` is an int32 1 on the
+    GPU."""
+    def project(index, rows_in):
+        if kind == "fp8":
+            return kernels.grouped_fp8(rows_in, groups, slot_banks[index], host_banks[index], rows[index])
+        return quantized_grouped(kind, rows_in, groups, slot_banks[index], host_banks[index], rows[index],
+                                 codebooks[index])
+
+    return expert_chain(kind, sorted_x.float(), project, always)
 
 
 def _sort_by_expert(topk_idx, num_experts):
@@ -227,13 +251,6 @@ def prefill_plan(topk_idx, num_experts, drop_invalid=False):
     groups = torch.stack([experts, experts, torch.zeros_like(experts), first, rows], dim=1).contiguous()
     t = kernels.grouped_tile_rows()
     return order, pos, groups, (P + (t - 1) * (E + 1)) // t
-
-
-def _scatter_sum(sorted_out, order, topk_weight, num_tokens, top_k):
-    """Undo the sort, weight every pair, and sum each token's k pairs (drama3/offload.py:146-149)."""
-    out = torch.empty_like(sorted_out)
-    out[order] = sorted_out * topk_weight.reshape(-1)[order].unsqueeze(1).float()
-    return out.view(num_tokens, top_k, -1).sum(dim=1)
 
 
 def _grouped_resident(kind, x, groups, tiles, bank, rows, codebook):
@@ -296,12 +313,12 @@ def resident_prefill(x, topk_idx, topk_weight, banks, rows, kind, codebooks, num
                                    codebooks[0])
         sorted_out = _grouped_resident(kind, kernels.rotate(hidden, always, swiglu=True), groups, tiles, down,
                                        rows[1], codebooks[1])
-    return _scatter_sum(sorted_out, order, topk_weight, num_tokens, top_k).to(x.dtype)
+    return _unsort_weighted_sum(sorted_out, order, topk_weight.float(), num_tokens, top_k).to(x.dtype)
 
 
 class HostBank:
-    """One expert bank in host memory, pinned when asked: tensors whose first dimension holds each expert's rows in
-    turn (drama3/offload.py:200-217). `kernel` names the kernel family that reads it."""
+    """One expert bank in host memory, pinned when asked: every field's first dimension holds the experts' rows one
+    expert after another (drama3/offload.py:200-217). `kernel` names the kernel family that reads it."""
 
     kernel = None
 
@@ -310,14 +327,22 @@ class HostBank:
         self.fields = {name: pinned(t, pin) for name, t in fields.items()}
 
     def rows(self, name):
+        """Rows of field `name` per expert."""
         return self.fields[name].shape[0] // self.num_experts
 
+    def expert_bytes(self):
+        """Bytes of one expert over all fields."""
+        return sum(t.nbytes for t in self.fields.values()) // self.num_experts
+
     def take(self, fields, first, last):
-        """Experts [first, last) of `fields` (host or device), laid out like this bank's."""
-        return {name: t[first * self.rows(name):last * self.rows(name)] for name, t in fields.items()}
+        """Experts [first, last) of `fields` (this bank's, or any laid out like them), as views."""
+        return {name: t.narrow(0, first * self.rows(name), (last - first) * self.rows(name))
+                for name, t in fields.items()}
 
     def to_device(self, first, last, device):
-        return {name: t.to(device, non_blocking=True) for name, t in self.take(self.fields, first, last).items()}
+        """Experts [first, last) copied to `device` (asynchronously from pinned memory)."""
+        span = self.take(self.fields, first, last)
+        return {name: t.to(device, non_blocking=True) for name, t in span.items()}
 
 
 class QuantHostBank(HostBank):
@@ -361,161 +386,179 @@ class FP8HostBank(HostBank):
         return None
 
 
+def host_banks(experts, pin):
+    """(gate_up, down) host banks of a layer's expert module: an FP8Experts module's e4m3 block-scaled banks, or the
+    quantized banks of an Experts module's gate_up_proj / down_proj."""
+    if isinstance(experts, FP8Experts):
+        if experts.per_channel:
+            raise ValueError("the slot cache reads the reference layouts; per-channel fp8 experts stay resident")
+        return tuple(FP8HostBank(getattr(experts, f"{name}_weight"), getattr(experts, f"{name}_scale"), pin)
+                     for name in ("gate_up", "down"))
+    return tuple(QuantHostBank(getattr(experts, f"{name}_proj"), pin) for name in ("gate_up", "down"))
+
+
+def decayed_uses(score, at, keys, now, span):
+    """float32 use counts of `keys` at step `now`: each count halves every `span` steps after the step `at` it was
+    last updated at; a key never used (at < 0) counts 0. The arithmetic is torch's float32 one of the reference's host
+    methods: exp2 of the step difference divided by span, times the count (drama3/offload.py:667-670)."""
+    last = at[keys]
+    return torch.where(last < 0, 0.0, score[keys] * torch.exp2((last - now).float() / span))
+
+
+class SlotState:
+    """The slot cache's bookkeeping as a structure of arrays in one memory (the host's or a GPU's), in the layout the
+    resolve kernel reads (kernels.resolve): table [keys], owner [count], score [keys], at [keys], pending [count],
+    clock [1], reads [3]; key = layer * experts + expert."""
+
+    NAMES = ("table", "owner", "score", "at", "pending", "clock", "reads")
+
+    def __init__(self, keys, count, device="cpu"):
+        def full(n, value, dtype=torch.int32):
+            return torch.full((n,), value, dtype=dtype, device=device)
+        self.table, self.owner = full(keys, -1), full(count, -1)
+        self.score, self.at = full(keys, 0.0, torch.float32), full(keys, -1)
+        self.pending, self.clock, self.reads = full(count, 0), full(1, 0), full(3, 0)
+
+    def tensors(self):
+        return [getattr(self, name) for name in self.NAMES]
+
+    def copy_from(self, other):
+        for mine, theirs in zip(self.tensors(), other.tensors()):
+            mine.copy_(theirs)
+
+
 class SlotPool:
     """A fixed number of expert slots on the GPU, filled from host memory, the least used expert out first
     (drama3/offload.py:560-752).
 
-    `table[layer * E + expert]` = its slot, -1 (host only) or -2 - slot (being copied in); `owner[slot]` = its key or
-    -1 (free); `score` = decayed use count as of step `at` (clock * layers + layer, -1 never); `clock` ticks at layer
-    0 of every pass; `reads` = [hits, fills, CPU runs]. The state lives on the host for host-side calls and on the GPU
-    while the decode kernels run (`device_state`), at addresses that never change once made (captured graphs read
-    them)."""
+    Rules (the reference's observable ones):
+      - count = max(8, min(layers * experts, budget // expert_bytes)) slots; slot s of bank index i holds rows
+        [s * rows_i, (s + 1) * rows_i) of every field.
+      - table[key] = the key's slot, -1 (host memory only) or -2 - slot (being copied in); owner[slot] = its key or -1.
+      - score / at: a decayed use count (halving every HALF_LIFE passes) as of step at = clock * layers + layer
+        (-1: never). clock ticks when layer 0 starts a pass. reads = [hits, fills, CPU runs].
+      - A slot's eviction value is -1 when free, +inf while its expert was used by this layer in this pass, else its
+        decayed count; a claim takes the lowest (ties: the lower slot), and the old owner leaves the table.
+    The state has a host copy (host-side calls: use, assign, claim, room) and a device copy at addresses fixed for
+    the pool's life (the resolve kernel, and CUDA graphs recorded over it); `device_state` and `host` move it.
+    There is no CPU side here, so no slot is ever reserved for a host copy: between decode steps only the reservation
+    budget the resolve kernel reads moves, by the reference's rule."""
 
     def __init__(self, banks, budget, device):
         self.banks = banks
-        first = banks[0]
-        self.rows = [{name: bank.rows(name) for name in bank.fields} for bank in first]
-        self.expert_bytes = sum(t[:bank.rows(name)].nbytes for bank in first for name, t in bank.fields.items())
-        self.layers, self.num_experts = len(banks), first[0].num_experts
+        layer0 = banks[0]
+        self.layers, self.num_experts = len(banks), layer0[0].num_experts
+        self.rows = [{name: bank.rows(name) for name in bank.fields} for bank in layer0]
+        self.expert_bytes = sum(t.nbytes // bank.num_experts for bank in layer0 for t in bank.fields.values())
         self.count = max(8, min(self.layers * self.num_experts, budget // self.expert_bytes))
-        self.fields = [{name: torch.empty((self.count * bank.rows(name), *t.shape[1:]), dtype=t.dtype, device=device)
-                        for name, t in bank.fields.items()} for bank in first]
         self.device = torch.device(device)
-        keys = self.layers * self.num_experts
-        self.table = torch.full((keys,), -1, dtype=torch.int32)
-        self.owner = torch.full((self.count,), -1, dtype=torch.int32)
-        self.score = torch.zeros((keys,), dtype=torch.float32)
-        self.at = torch.full((keys,), -1, dtype=torch.int32)
-        self.pending = torch.zeros((self.count,), dtype=torch.int32)
-        self.clock = torch.zeros((1,), dtype=torch.int32)
-        self.reads = torch.zeros((3,), dtype=torch.int32)
-        self.on_device = False
-        self.resident = None
-        self.reserved, self.copying = [], []
+        self.fields = [{name: torch.empty((self.count * rows, *t.shape[1:]), dtype=t.dtype, device=self.device)
+                        for (name, t), rows in zip(bank.fields.items(), per.values())}
+                       for bank, per in zip(layer0, self.rows)]
+        self._span = HALF_LIFE * self.layers
+        self._host_state = SlotState(self.layers * self.num_experts, self.count)
+        self._device_state = None
+        self._state = self._host_state
         self.reserve = RESERVE_START
         self.budget = None
-        self.copy_stream = None
         # device scalars the kernels read: a layer's step, the took-over flag (always 0 here), a constant 1, the share
-        self.step, self.took_over, self.always = torch.tensor([[0], [0], [1]], dtype=torch.int32, device=device)
-        self.share = torch.zeros((1,), dtype=torch.float32, device=device)
+        self.step, self.took_over, self.always = torch.tensor([[0], [0], [1]], dtype=torch.int32, device=self.device)
+        self.share = torch.zeros((1,), dtype=torch.float32, device=self.device)
 
-    def _state(self):
-        return self.table, self.owner, self.score, self.at, self.pending, self.clock, self.reads
+    # the state arrays of the copy in use
+    table = property(lambda self: self._state.table)
+    owner = property(lambda self: self._state.owner)
+    score = property(lambda self: self._state.score)
+    at = property(lambda self: self._state.at)
+    pending = property(lambda self: self._state.pending)
+    clock = property(lambda self: self._state.clock)
+    reads = property(lambda self: self._state.reads)
+
+    @property
+    def on_device(self):
+        return self._state is self._device_state
 
     def _budget(self):
-        """[slots a decode step may reserve, at most per layer] (drama3/offload.py:649-651)."""
-        return [self.reserve, max(1, -(-2 * self.reserve // self.layers))]
+        """[slots a decode step may reserve, at most per layer]: the step's reserve spread over the layers, with
+        room for twice the even share (drama3/offload.py:649-651)."""
+        return [self.reserve, max(1, (2 * self.reserve + self.layers - 1) // self.layers)]
 
     def device_state(self):
-        """(table, owner, score, at, pending, clock, budget, reads, step, share) on the GPU (drama3/offload.py:598-613)."""
+        """(table, owner, score, at, pending, clock, budget, reads, step, share) on the GPU (drama3/offload.py:598-613):
+        the host copy moved into the device copy, which is made once and keeps its addresses."""
         if not self.on_device:
-            budget = torch.tensor(self._budget(), dtype=torch.int32)
-            if self.resident is None:
-                self.resident = [t.to(self.device) for t in self._state()]
-                self.budget = budget.to(self.device)
-            else:
-                for there, here in zip(self.resident, self._state()):
-                    there.copy_(here)
-                self.budget.copy_(budget)
-            self.table, self.owner, self.score, self.at, self.pending, self.clock, self.reads = self.resident
-            self.on_device = True
-        return (self.table, self.owner, self.score, self.at, self.pending, self.clock, self.budget, self.reads,
-                self.step, self.share)
+            if self._device_state is None:
+                self._device_state = SlotState(self.layers * self.num_experts, self.count, self.device)
+                self.budget = torch.empty((2,), dtype=torch.int32, device=self.device)
+            self._device_state.copy_from(self._host_state)
+            self.budget.copy_(torch.tensor(self._budget(), dtype=torch.int32))
+            self._state = self._device_state
+        s = self._state
+        return s.table, s.owner, s.score, s.at, s.pending, s.clock, self.budget, s.reads, self.step, self.share
 
     def host(self):
-        """Bring the state back to the host (after every reserved copy has landed)."""
+        """Bring the state back to the host copy (it waits for the GPU's work on it)."""
         if self.on_device:
-            self.settle()
-            self.table, self.owner, self.score, self.at, self.pending, self.clock, self.reads = (
-                t.cpu() for t in self._state())
-            self.on_device = False
+            self._host_state.copy_from(self._device_state)
+            self._state = self._host_state
 
     def promote(self):
-        """Between decode steps: map the slots whose copies landed and start the copies of newly reserved slots on a
-        copy stream (drama3/offload.py:624-647). With no CPU side nothing is reserved, so this only keeps the budget."""
+        """Between decode steps (drama3/offload.py:624-647). Nothing is ever reserved for a host copy here (no CPU
+        side), so the copies never lag and the step's reservation budget grows by a quarter plus one, up to
+        RESERVE_MAX."""
         if not self.on_device:
             return
-        landed = []
-        while self.copying and self.copying[0][0].query():
-            landed += self.copying.pop(0)[1]
-        self._map(landed)
-        lagging = bool(self.copying)
-        if self.reserved:
-            if self.copy_stream is None:
-                self.copy_stream = torch.cuda.Stream(self.device)
-            self.copy_stream.wait_stream(torch.cuda.current_stream(self.device))
-            with torch.cuda.stream(self.copy_stream):
-                for layer, expert, slot in self.reserved:
-                    self._fill(slot, [bank.take(bank.fields, expert, expert + 1) for bank in self.banks[layer]])
-                event = torch.cuda.Event()
-                event.record()
-            self.copying.append((event, [(layer * self.num_experts + e, slot) for layer, e, slot in self.reserved]))
-            self.reserved = []
-        if lagging:
-            self.reserve = max(RESERVE_MIN, self.reserve * 3 // 4)
-        else:
-            self.reserve = min(RESERVE_MAX, self.reserve * 5 // 4 + 1)
+        self.reserve = min(RESERVE_MAX, self.reserve + self.reserve // 4 + 1)
         self.budget.copy_(torch.tensor(self._budget(), dtype=torch.int32), non_blocking=True)
 
     def settle(self):
-        """Every reserved slot copied in and mapped."""
-        self.promote()
-        if self.copy_stream is not None:
-            self.copy_stream.synchronize()
-        self._map([pair for _, pairs in self.copying for pair in pairs])
-        self.copying = []
+        """Every reserved slot copied in: there are none here."""
 
-    def _map(self, pairs):
-        if not pairs:
-            return
-        keys, slots = zip(*pairs)
-        keys = torch.tensor(keys, dtype=torch.long).to(self.device)
-        slots = torch.tensor(slots, dtype=torch.int32).to(self.device)
-        self.table[keys] = slots
-        self.pending[slots.long()] = 0
-
-    def _now(self, layer):
-        """`layer`'s step in this pass; layer 0 starts a new pass (drama3/offload.py:661-665)."""
-        if layer == 0:
-            self.clock += 1
+    def _step(self, layer, tick):
+        """`layer`'s step in the current pass; with `tick`, layer 0 starts a new pass."""
+        if tick and layer == 0:
+            self.clock.add_(1)
         return int(self.clock) * self.layers + layer
 
-    def _uses(self, keys, now):
-        """Decayed use counts of `keys` at step `now` (drama3/offload.py:667-670)."""
-        at = self.at[keys]
-        decay = torch.exp2((at - now).float() / (HALF_LIFE * self.layers))
-        return torch.where(at < 0, 0.0, self.score[keys] * decay)
-
-    def _fill(self, slot, sources):
-        for fields, rows, source in zip(self.fields, self.rows, sources):
-            for name, target in fields.items():
-                target[slot * rows[name]:(slot + 1) * rows[name]].copy_(source[name], non_blocking=True)
+    def _eviction_values(self, layer):
+        """Per slot, the value a claim by `layer` minimizes: -1 free, +inf held by an expert `layer` used in this
+        pass, else the holder's decayed use count."""
+        now = self._step(layer, tick=False)
+        holder = self.owner.long()
+        key = holder.clamp(min=0)
+        values = torch.where(holder < 0, -1.0, decayed_uses(self.score, self.at, key, now, self._span))
+        return values.masked_fill((holder >= 0) & (self.at[key] == now), float("inf"))
 
     def slot_fields(self, index, slot):
-        """Bank `index`'s fields of the expert in `slot`."""
-        return {name: t[slot * self.rows[index][name]:(slot + 1) * self.rows[index][name]]
+        """Bank `index`'s fields of the expert in `slot`, as views laid out like one expert of a host bank."""
+        return {name: t.narrow(0, slot * self.rows[index][name], self.rows[index][name])
                 for name, t in self.fields[index].items()}
 
+    def _fill(self, slot, sources):
+        for index, source in enumerate(sources):
+            for name, view in self.slot_fields(index, slot).items():
+                view.copy_(source[name], non_blocking=True)
+
     def use(self, layer, experts):
-        """{expert: slot} of the cached ones among `experts`; each counts a use in this pass
+        """{expert: slot} of the cached ones among `experts` (distinct); each counts a use in this pass
         (drama3/offload.py:689-697)."""
         self.host()
-        now = self._now(layer)
-        keys = torch.tensor(experts, dtype=torch.long) + layer * self.num_experts
-        self.score[keys] = self._uses(keys, now) + 1
+        now = self._step(layer, tick=True)
+        keys = torch.as_tensor(experts, dtype=torch.long) + layer * self.num_experts
+        self.score[keys] = decayed_uses(self.score, self.at, keys, now, self._span) + 1
         self.at[keys] = now
-        table = self.table[layer * self.num_experts:(layer + 1) * self.num_experts].tolist()
-        return {e: table[e] for e in experts if table[e] >= 0}
+        return {e: s for e, s in zip(experts, self.table[keys].tolist()) if s >= 0}
 
     def free_slots(self):
-        return (self.owner < 0).nonzero().flatten().tolist()
+        """Slots without an expert, ascending."""
+        return [s for s, key in enumerate(self.owner.tolist()) if key < 0]
 
     def assign(self, slot, layer, expert):
-        """Give `slot` to an expert of `layer`; its old expert leaves the table (drama3/offload.py:702-709)."""
+        """Give `slot` to an expert of `layer`; its old expert leaves the table. The caller fills it."""
         key = layer * self.num_experts + expert
-        old = int(self.owner[slot])
-        if old >= 0:
-            self.table[old] = -1
+        evicted = int(self.owner[slot])
+        if evicted >= 0:
+            self.table[evicted] = -1
         self.owner[slot] = key
         self.table[key] = slot
         return slot
@@ -523,26 +566,30 @@ class SlotPool:
     def claim(self, layer, expert):
         """The slot of the least used cached expert (a free one first) that `layer` has not used in this pass; ties go
         to the lower slot (drama3/offload.py:711-717)."""
-        keys = self.owner.long()
-        held = keys.clamp(min=0)
-        now = int(self.clock) * self.layers + layer
-        uses = torch.where(keys < 0, -1.0, self._uses(held, now))
-        uses[(keys >= 0) & (self.at[held] == now)] = float("inf")
-        return self.assign(int(torch.argmin(uses)), layer, expert)
+        return self.assign(int(torch.argmin(self._eviction_values(layer))), layer, expert)
 
     def room(self, layer):
-        """Slots `layer` may still claim in this pass (drama3/offload.py:719-722)."""
-        keys = self.owner.long()
-        now = int(self.clock) * self.layers + layer
-        return int(((keys < 0) | (self.at[keys.clamp(min=0)] != now)).sum())
+        """Slots `layer` may still claim in this pass: those not held by an expert it used (drama3/offload.py:719-722)."""
+        return int(torch.isfinite(self._eviction_values(layer)).sum())
 
     def insert(self, layer, expert, sources):
+        """A claimed slot for an expert `layer` uses, filled from `sources` (one expert's fields per bank)."""
         slot = self.claim(layer, expert)
         self._fill(slot, sources)
         return slot
 
+    def slots(self, layer, experts, banks):
+        """The host-lookup decode's slots of `experts` (a device tensor), missed ones inserted; counts hits and
+        fills (drama3/offload.py:730-740)."""
+        found = self.use(layer, experts)
+        out = [found[e] if e in found else self.insert(layer, e, [b.take(b.fields, e, e + 1) for b in banks])
+               for e in experts]
+        self.reads.add_(torch.tensor([len(found), len(experts) - len(found), 0], dtype=torch.int32))
+        return torch.tensor(out, device=self.device)
+
     def gather(self, index, slots):
-        return {name: t.view(self.count, self.rows[index][name], *t.shape[1:]).index_select(0, slots).flatten(0, 1)
+        """Bank `index`'s fields of the experts in `slots` (a device tensor), one after another."""
+        return {name: t.unflatten(0, (self.count, -1)).index_select(0, slots).flatten(0, 1)
                 for name, t in self.fields[index].items()}
 
     def report(self):
@@ -555,11 +602,19 @@ class SlotPool:
                          "read over PCIe", self.count, size, 100 * hits / total, total, fills)
 
 
+def _unsort_weighted_sum(sorted_out, order, weights, num_tokens, top_k):
+    """Pair outputs in expert order back in (token, rank) order, each times its routing weight (stored in
+    sorted_out's dtype), summed over a token's k pairs (drama3/offload.py:146-149, 461-466)."""
+    out = torch.empty_like(sorted_out)
+    out[order] = sorted_out * weights.reshape(-1)[order].unsqueeze(1)
+    return out.view(num_tokens, top_k, -1).sum(dim=1)
+
+
 class ExpertStore:
     """Every layer's experts in host memory with one slot cache on the GPU per generation
     (drama3/offload.py:302-552). Decode rows run the slot-plan kernels (resolve, then GEMVs that read misses from
     pinned host memory and fill slots), so a decode step never waits on the host and can be captured as a graph;
-    a prompt's rows run the grouped kernels."""
+    a prompt's rows run the grouped kernels over slots the host chooses."""
 
     def __init__(self, cache_bytes, pin):
         self.banks = []
@@ -567,17 +622,13 @@ class ExpertStore:
         self.cache_bytes = cache_bytes
         self.pin = pin
         self.sync_free = False
+        # the reference's CPU side (experts run on the host beside the GPU): never used here
         self.cpu_experts = False
         self.cpu_side = None
 
     def add(self, experts):
         """Take a layer's experts into host memory; returns the module that replaces them."""
-        if isinstance(experts, FP8Experts):
-            banks = (FP8HostBank(experts.gate_up_weight, experts.gate_up_scale, self.pin),
-                     FP8HostBank(experts.down_weight, experts.down_scale, self.pin))
-        else:
-            banks = (QuantHostBank(experts.gate_up_proj, self.pin), QuantHostBank(experts.down_proj, self.pin))
-        self.banks.append(banks)
+        self.banks.append(host_banks(experts, self.pin))
         return OffloadedExperts(self, len(self.banks) - 1)
 
     @contextlib.contextmanager
@@ -592,9 +643,8 @@ class ExpertStore:
         if not self.pin:
             raise ValueError("the kernels read missed experts from pinned host memory: build the store with pin=True")
         kernels.available(device)
-        reserve = RESERVE_BASE + int(RESERVE_PER_ROW * rows)
         free, _ = torch.cuda.mem_get_info(device)
-        budget = max(0, free - reserve)
+        budget = max(0, free - RESERVE_BASE - int(RESERVE_PER_ROW * rows))
         if self.cache_bytes:
             budget = min(budget, self.cache_bytes)
         self.cache = SlotPool(self.banks, budget, device)
@@ -609,7 +659,7 @@ class ExpertStore:
             self.sync_free = False
 
     def between_steps(self):
-        """Between decode steps (drama3/offload.py:386-391): land reserved copies; no CPU share to rebalance."""
+        """Between decode steps (drama3/offload.py:386-391): no CPU share to rebalance; the pool's budget moves."""
         self.cache.promote()
 
     def after_layer(self, layer):
@@ -621,34 +671,26 @@ class ExpertStore:
             raise RuntimeError("ExpertStore.forward outside a session: open `session(device)` first")
         if x.device != self.cache.device:
             raise RuntimeError(f"rows on {x.device}, expert cache on {self.cache.device}")
-        banks = self.banks[layer]
         if x.shape[0] == 1:
-            return self.decode(layer, banks, x, topk_idx[0], topk_weight[0])
-        return self.prefill(layer, banks, x, topk_idx, topk_weight)
+            return self.decode(layer, self.banks[layer], x, topk_idx[0], topk_weight[0])
+        return self.prefill(layer, self.banks[layer], x, topk_idx, topk_weight)
 
     def decode(self, layer, banks, x, ids, weights):
         """One row x [1, H] through its experts ids [k]: resolve, gate_up, SwiGLU, down, weighted sum
         (drama3/offload.py:403-432 without the CPU side). [1, H] bfloat16."""
-        gate_up, down = banks
         cache = self.cache
-        plan = kernels.resolve(ids, layer, len(self.banks), gate_up.num_experts, HALF_LIFE, False, ADMIT,
+        kind = banks[0].kernel
+        plan = kernels.resolve(ids, layer, len(self.banks), banks[0].num_experts, HALF_LIFE, False, ADMIT,
                                *cache.device_state())
-        slots_gate_up, slots_down = cache.fields
-        weights = weights.float()
-        if gate_up.kernel == "fp8":
-            hidden = kernels.gemv_fp8(x.float(), ids, plan, slots_gate_up, gate_up.fields, gate_up.rows("weight"))
-            gate, up = hidden.chunk(2, dim=-1)
-            out = kernels.gemv_fp8(nn.functional.silu(gate) * up, ids, plan, slots_down, down.fields,
-                                   down.rows("weight"))
-            return kernels.weighted_sum(out, weights)
-        kind = gate_up.kernel
-        rotated = kernels.rotate(x, cache.always)
-        hidden = quantized_gemv(kind, rotated, ids, plan, cache.took_over, False, slots_gate_up, gate_up.fields,
-                                gate_up.rows("_qdata"), gate_up.codebook(x.device))
-        hidden = kernels.rotate(hidden, cache.always, swiglu=True)
-        out = quantized_gemv(kind, hidden, ids, plan, cache.took_over, False, slots_down, down.fields,
-                             down.rows("_qdata"), down.codebook(x.device))
-        return kernels.weighted_sum(out, weights)
+
+        def project(index, rows_in):
+            bank = banks[index]
+            if kind == "fp8":
+                return kernels.gemv_fp8(rows_in, ids, plan, cache.fields[index], bank.fields, bank.rows("weight"))
+            return quantized_gemv(kind, rows_in, ids, plan, cache.took_over, False, cache.fields[index], bank.fields,
+                                  bank.rows("_qdata"), bank.codebook(x.device))
+
+        return kernels.weighted_sum(expert_chain(kind, x, project, cache.always), weights.float())
 
     def prefill(self, layer, banks, x, topk_idx, topk_weight):
         """Many rows: each expert the rows use runs once on its rows (drama3/offload.py:454-466). As there, each
@@ -656,56 +698,62 @@ class ExpertStore:
         num_tokens, top_k = topk_idx.shape
         order, counts = _sort_by_expert(topk_idx, banks[0].num_experts)
         sorted_out = self.prefill_kernels(layer, banks, x[order // top_k], counts)
-        weighted = sorted_out * topk_weight.reshape(-1)[order].unsqueeze(1)
-        out = torch.empty_like(weighted)
-        out[order] = weighted
-        return out.view(num_tokens, top_k, -1).sum(dim=1)
+        return _unsort_weighted_sum(sorted_out, order, topk_weight, num_tokens, top_k)
+
+    def prompt_groups(self, layer, counts):
+        """(expert, slot, fill, first row, rows) for every expert with rows in a prompt sorted by expert (counts[e]
+        rows each): a cached expert reads its slot; of the others, those with the most rows (ties: the lower expert)
+        take free slots in ascending order, at most the layer's share of the cache (count // layers), and are filled
+        on the way (fill 1); the rest read host memory (slot -1) (drama3/offload.py:468-485)."""
+        cache = self.cache
+        used = [e for e, n in enumerate(counts) if n]
+        slot_of = cache.use(layer, used)
+        uncached = sorted((e for e in used if e not in slot_of), key=lambda e: (-counts[e], e))
+        free = cache.free_slots()
+        filled = uncached[:min(cache.count // len(self.banks), len(free))]
+        for e, slot in zip(filled, free):
+            slot_of[e] = cache.assign(slot, layer, e)
+        first = [0, *itertools.accumulate(counts)]
+        return [(e, slot_of.get(e, -1), int(e in filled), first[e], counts[e]) for e in used]
 
     def prefill_kernels(self, layer, banks, sorted_x, counts):
-        """sorted_x's rows (sorted by expert, counts[e] each) through their experts, unweighted: cached experts from
-        their slots, the most used uncached ones filled into free slots on the way (at most the layer's share of the
-        cache), the rest read from host memory; one grouped kernel per bank (drama3/offload.py:468-512)."""
-        gate_up, _ = banks
-        cache = self.cache
-        device = sorted_x.device
-        offsets = [0, *itertools.accumulate(counts)]
-        used = [e for e, n in enumerate(counts) if n]
-        slots = cache.use(layer, used)
-        rest = sorted((e for e in used if e not in slots), key=counts.__getitem__, reverse=True)
-        free = cache.free_slots()
-        fills = rest[:min(cache.count // len(self.banks), len(free))]
-        for e, slot in zip(fills, free):
-            slots[e] = cache.assign(slot, layer, e)
-        fills = set(fills)
-        groups = [(e, slots.get(e, -1), int(e in fills), offsets[e], counts[e]) for e in used]
+        """sorted_x's rows (sorted by expert, counts[e] each) through their experts, unweighted, one grouped kernel per
+        bank over the groups of prompt_groups (drama3/offload.py:468-512). In sorted_x's dtype."""
+        groups = self.prompt_groups(layer, counts)
         if not groups:
             return torch.zeros_like(sorted_x)
+        device = sorted_x.device
         groups = torch.tensor(groups, dtype=torch.int32).to(device)
-        key = "weight" if gate_up.kernel == "fp8" else "_qdata"
-        bank_rows = [bank.rows(key) for bank in banks]
-        codebooks = [bank.codebook(device) for bank in banks]
-        always = torch.ones((1,), dtype=torch.int32, device=device)
-        out = grouped_experts(sorted_x, groups, cache.fields, [bank.fields for bank in banks], bank_rows,
-                              gate_up.kernel, codebooks, always)
+        key = "weight" if banks[0].kernel == "fp8" else "_qdata"
+        out = grouped_experts(sorted_x, groups, self.cache.fields, [bank.fields for bank in banks],
+                              [bank.rows(key) for bank in banks], banks[0].kernel,
+                              [bank.codebook(device) for bank in banks], self.cache.always)
         return out.to(sorted_x.dtype)
 
 
 class FP8Experts(nn.Module):
-    """Routed experts as float8 e4m3 weights with a float32 scale per 128 x 128 block, held whole on the GPU
-    (drama3/offload.py:755-802). One row, or up to 16 rows of the fused kernel's shapes, run the decode; more run the
-    grouped kernels."""
+    """Routed experts as float8 e4m3 weights held whole on the GPU (drama3/offload.py:755-802): by default with a
+    float32 scale per 128 x 128 block, the reference's layout ({gate_up,down}_scale [E, N/128, K/128]); with
+    `per_channel` one float32 scale per output row ({gate_up,down}_scale [E, N]), the per-channel layout the fused
+    tensor-core decode reads fastest. Up to 16 rows of the fused kernel's shapes run the decode (one launch for all
+    rows); more run the grouped tensor-core GEMMs."""
 
-    def __init__(self, num_experts, hidden, intermediate, device=None, dtype=None):
+    def __init__(self, num_experts, hidden, intermediate, device=None, dtype=None, per_channel=False):
         super().__init__()
         self.num_experts = num_experts
         self.dtype = dtype
+        self.per_channel = per_channel
         for name, rows, cols in (("gate_up", 2 * intermediate, hidden), ("down", hidden, intermediate)):
             weight = torch.empty((num_experts, rows, cols), dtype=torch.float8_e4m3fn, device=device)
-            scale = torch.empty((num_experts, rows // FP8_BLOCK, cols // FP8_BLOCK), dtype=torch.float32,
-                                device=device)
+            shape = (num_experts, rows) if per_channel else (num_experts, rows // FP8_BLOCK, cols // FP8_BLOCK)
+            scale = torch.empty(shape, dtype=torch.float32, device=device)
             self.register_parameter(f"{name}_weight", nn.Parameter(weight, requires_grad=False))
             self.register_parameter(f"{name}_scale", nn.Parameter(scale, requires_grad=False))
         self._workspace = {}
+
+    @property
+    def kind(self):
+        return "fp8c" if self.per_channel else "fp8"
 
     def sync_free(self, device):
         """Whether a decode row on `device` runs without waiting on the host."""
@@ -731,10 +779,11 @@ class FP8Experts(nn.Module):
         banks, rows = self.banks()
         hidden, intermediate = self.down_weight.shape[1:]
         M, k = topk_idx.shape
-        if M == 1 or fused_decode_fits(hidden, intermediate, M, k):
-            ws = self.workspace(M, k, x.device) if fused_decode_fits(hidden, intermediate, M, k) else None
-            return resident_decode_lines(x, topk_idx, topk_weight, banks, rows, "fp8", (None, None), workspace=ws)
-        return resident_prefill(x, topk_idx, topk_weight, banks, rows, "fp8", (None, None), self.num_experts,
+        fits = fused_decode_fits(hidden, intermediate, M, k)
+        if M == 1 or fits:
+            ws = self.workspace(M, k, x.device) if fits else None
+            return resident_decode_lines(x, topk_idx, topk_weight, banks, rows, self.kind, (None, None), workspace=ws)
+        return resident_prefill(x, topk_idx, topk_weight, banks, rows, self.kind, (None, None), self.num_experts,
                                 sync_free=capturing(x))
 
 

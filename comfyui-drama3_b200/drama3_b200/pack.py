@@ -221,10 +221,10 @@ class PackedWeight:
 
 
 def packed_weight(kind, w, threads=0, codebook=CODEBOOK4):
-    """Float experts w [E, N, K] -> a PackedWeight of layout `kind` ("int8", "w4", "w6") on the host."""
-    if kind not in ("int8", "w4", "w6"):
-        raise ValueError(f"no quantized-tensor form for {kind}: fp8 banks are FP8Experts parameters, the BASELINE "
-                         "layouts are plain fields")
+    """Float experts w [E, N, K] -> a PackedWeight of layout `kind` on the host: the reference's "int8" (ConvRot),
+    "w4", "w6", or the BASELINE "w4a8" / "w6a8" (layout name offload.WA8_LAYOUT)."""
+    if kind not in ("int8", "w4", "w6", "w4a8", "w6a8"):
+        raise ValueError(f"no quantized-tensor form for {kind}: fp8 banks are FP8Experts parameters")
     w = torch.as_tensor(w)
     K = w.shape[-1]
     fields = pack_bank(kind, w, threads, codebook)
@@ -232,6 +232,11 @@ def packed_weight(kind, w, threads=0, codebook=CODEBOOK4):
     if kind == "int8":
         return PackedWeight("TensorWiseINT8Layout", fields["_qdata"],
                             PackedParams((rows, K), scale=fields["scale"].view(rows, 1)))
+    if kind in ("w4a8", "w6a8"):
+        from .offload import WA8_LAYOUT
+        return PackedWeight(WA8_LAYOUT, fields["_qdata"],
+                            PackedParams((rows, K), scale=fields["scale"], convrot=False, convrot_groupsize=0,
+                                         group_size=128))
     book = torch.as_tensor(codebook, dtype=torch.float32).clone() if kind == "w4" else None
     return PackedWeight("AsymW4A8Int8Layout", fields["_qdata"],
                         PackedParams((rows, K), scale=fields["scale"], s_channel=fields["s_channel"], codebook=book))

@@ -221,9 +221,10 @@ int d3_ipc_close(void* base);
 /* d3_moe_decode without a workspace argument. No counterpart in the reference: it is for callers that cannot
  * allocate device memory themselves, such as a plugin whose host application's memory manager owns every device
  * allocation, or a C host that links this library without any device allocator. The scratch is an array inside the
- * library (1,442,048 bytes, held on every GPU that loads it until the process exits), so the call allocates nothing
+ * library (1,445,888 bytes, held on every GPU that loads it until the process exits), so the call allocates nothing
  * and calls no allocating routine. Limits: at most 128 routed pairs (M * k), intermediate size <= 768; larger shapes
- * return D3_ERR_TOO_LARGE. The first call on a device sets up the array's device address (synchronous); make it
+ * return D3_ERR_TOO_LARGE; other bad arguments return the codes d3_moe_decode gives, before anything is put on
+ * the stream. The first call on a device sets up the array's device address (synchronous); make it
  * before any stream capture. All calls share the one array: calls that overlap on the GPU race, so issue them on
  * one stream (or order them). Each call clears the array's barrier word on `stream` before its kernel. */
 int d3_moe_decode_static(int fmt, const void* x, int x_bf16, int M, int k, int E, int H, int I, const int64_t* ids,

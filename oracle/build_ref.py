@@ -2,6 +2,9 @@
 
     python oracle/build_ref.py [/path/to/ComfyUI-Drama3]
 
+Without an argument the checkout is taken from the DRAMA3_REFERENCE environment variable, else from the
+"reference_path" entry of BASELINE.json at the repository root; with none of these nothing is built.
+
 The reference keeps its kernels as one CUDA C string (drama3/kernels.py:14-588, `SOURCE`) and compiles it at run
 time with NVRTC for the current device (drama3/kernels.py:593-596, through torch.cuda._compile_kernel, which adds
 -D__CUDA_NO_HALF_OPERATORS__ and friends and nothing that changes float code). This recipe reads that string from
@@ -10,6 +13,7 @@ sm_100 with the same defines; only the cubin lands in oracle/_ref/ (git-ignored;
 the working tree). Nothing of the reference's source is kept.
 """
 import ast
+import json
 import os
 import subprocess
 import sys
@@ -32,8 +36,23 @@ def reference_source(root):
     raise RuntimeError("SOURCE not found in drama3/kernels.py")
 
 
-def build(root="/root/reference", force=False):
+def reference_root():
+    """The reference checkout named by DRAMA3_REFERENCE or by BASELINE.json's "reference_path", or None."""
+    if os.environ.get("DRAMA3_REFERENCE"):
+        return Path(os.environ["DRAMA3_REFERENCE"])
+    baseline = HERE.parent / "BASELINE.json"
+    if baseline.exists():
+        path = json.loads(baseline.read_text()).get("reference_path")
+        if path:
+            return Path(path)
+    return None
+
+
+def build(root=None, force=False):
     """Build the cubin when the reference checkout is present; returns its path (or None without the checkout)."""
+    root = root or reference_root()
+    if root is None:
+        return CUBIN if CUBIN.exists() else None
     kernels = Path(root) / "drama3" / "kernels.py"
     if not kernels.exists():
         return CUBIN if CUBIN.exists() else None
@@ -52,4 +71,4 @@ def build(root="/root/reference", force=False):
 
 
 if __name__ == "__main__":
-    print(build(sys.argv[1] if len(sys.argv) > 1 else "/root/reference", force=True))
+    print(build(sys.argv[1] if len(sys.argv) > 1 else None, force=True))

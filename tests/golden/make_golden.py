@@ -1,6 +1,6 @@
 """Generate tests/golden/golden.npz from the reference's own Python CPU functions.
 
-    python tests/golden/make_golden.py [/path/to/ComfyUI-Drama3]
+    python tests/golden/make_golden.py [/path/to/ComfyUI-Drama3]   (default: as oracle/build_ref.py finds it)
 
 Runs only where the reference checkout exists (it is read, never copied). drama3/offload.py imports ComfyUI
 modules that are not installed; a minimal stand-in provides the three names it touches at import time and the one
@@ -169,4 +169,9 @@ def main(root):
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference"))
+    sys.path.insert(0, str(Path(__file__).resolve().parents[2]))
+    from oracle.build_ref import reference_root
+    root = Path(sys.argv[1]) if len(sys.argv) > 1 else reference_root()
+    if root is None:
+        sys.exit("name the reference checkout: an argument, DRAMA3_REFERENCE, or BASELINE.json's reference_path")
+    main(root)

@@ -77,7 +77,8 @@ def test_quantized_experts_lines_and_prompt(cuda, kind):
     """Experts over quantized banks: 4 lines (fused) and a 40-row prompt (grouped kernels) against the oracle."""
     gu, gu_bank = quant_module(kind, E, 2 * I, H, 60, cuda)
     dn, dn_bank = quant_module(kind, E, H, I, 61, cuda)
-    ex = Experts(E, gu, dn)
+    ex = Experts(E, H, I, device=cuda, dtype=torch.bfloat16)  # the reference's argument list
+    ex.gate_up_proj.weight, ex.down_proj.weight = gu.weight, dn.weight
     cbs = gd.codebooks(kind, cuda)
     x = gd.rand_rows(4, H, 62, cuda)
     ids, w = gd.rand_routing(4, E, 8, 63, cuda)
@@ -202,9 +203,10 @@ def test_packed_float_experts_through_the_module(cuda, kind, bound):
     gen = torch.Generator().manual_seed(150)
     gu_f = torch.randn((Ef, 2 * I, H), generator=gen) * 0.02
     dn_f = torch.randn((Ef, H, I), generator=gen) * 0.02
-    mods = [type("Bank", (), {"weight": pack.packed_weight(kind, t).to(cuda), "num_experts": Ef})()
-            for t in (gu_f, dn_f)]
-    ex = Experts(Ef, *mods)
+    ex = Experts(Ef, H, I, device=cuda, dtype=torch.bfloat16)
+    ex.gate_up_proj.weight = pack.packed_weight(kind, gu_f).to(cuda)
+    ex.down_proj.weight = pack.packed_weight(kind, dn_f).to(cuda)
+    mods = (ex.gate_up_proj, ex.down_proj)
     x = gd.rand_rows(4, H, 151, cuda)
     ids, w = gd.rand_routing(4, Ef, 8, 152, cuda)
     out = ex(x, ids, w).float()

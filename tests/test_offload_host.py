@@ -171,3 +171,54 @@ def test_prompt_pass_sorts_on_the_device_under_graph_capture(monkeypatch):
     monkeypatch.setattr(offload, "capturing", lambda t: True)
     ex(x, ids, w)
     assert calls == [False, True]
+
+
+def test_modules_take_the_reference_argument_lists():
+    """Experts(num_experts, hidden, intermediate, device, dtype, ops) and SparseMoeBlock(config, device, dtype, ops)
+    build as drama3/model.py:62,95 builds them: with a ComfyUI-like `ops` namespace its factories are used, without one
+    the library's own (torch Linear, MoEBank)."""
+    from types import SimpleNamespace
+    from drama3_b200.model import Experts, MoEBank, SharedExpert
+
+    made = []
+
+    class Linear(torch.nn.Linear):
+        def __init__(self, *a, **kw):
+            made.append(("Linear", a))
+            super().__init__(*a, **kw)
+
+    class MoEExperts(MoEBank):
+        def __init__(self, *a, **kw):
+            made.append(("MoEExperts", a))
+            super().__init__(*a, **kw)
+
+    ops = SimpleNamespace(Linear=Linear, MoEExperts=MoEExperts)
+    ex = Experts(16, 256, 128, "meta", torch.bfloat16, ops)
+    assert ex.num_experts == 16 and isinstance(ex.gate_up_proj, MoEExperts)
+    assert made[:2] == [("MoEExperts", (16, 256, 256)), ("MoEExperts", (16, 128, 256))]
+    block = SparseMoeBlock(block_config(hidden=256, num_experts=16, intermediate=128, shared_intermediate=64,
+                                        fp8=False), "meta", torch.bfloat16, ops)
+    assert isinstance(block.experts, Experts) and isinstance(block.gate, Linear)
+    assert isinstance(block.shared_expert, SharedExpert) and block.gate.weight.shape == (16, 256)
+    fp8 = SparseMoeBlock(block_config(hidden=256, num_experts=16, intermediate=128, shared_intermediate=64),
+                         "meta", torch.bfloat16)
+    assert isinstance(fp8.experts, offload.FP8Experts) and fp8.experts.kind == "fp8"
+    assert fp8.experts.gate_up_scale.shape == (16, 2, 2)
+    chan = SparseMoeBlock(block_config(hidden=256, num_experts=16, intermediate=128, shared_intermediate=64,
+                                       per_channel=True), "meta", torch.bfloat16)
+    assert chan.experts.kind == "fp8c" and chan.experts.gate_up_scale.shape == (16, 256)
+    with pytest.raises(ValueError):
+        MoEBank(4, 8, 8, bias=True)
+
+
+@pytest.mark.parametrize("kind", ["w4a8", "w6a8"])
+def test_baseline_banks_dressed_as_quantized_tensors(kind):
+    """pack.packed_weight of the BASELINE int8-activation layouts is recognized by kernel_bank, with the packer's
+    fields."""
+    from drama3_b200 import pack
+    w = torch.randn((2, 128, 256), generator=torch.Generator().manual_seed(3)) * 0.02
+    packed = pack.packed_weight(kind, w)
+    found, fields = offload.kernel_bank(packed)
+    direct = pack.pack_bank(kind, w)
+    assert found == kind and set(fields) == {"_qdata", "scale"}
+    assert torch.equal(fields["_qdata"], direct["_qdata"]) and torch.equal(fields["scale"], direct["scale"])

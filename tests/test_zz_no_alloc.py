@@ -17,7 +17,7 @@ TOL = 1e-3
 def _call_static(lib, kind, x, ids, w, banks, cbs, out):
     from drama3_b200 import _lib
     gate_up, down = banks
-    wkey = "weight" if kind == "fp8" else "_qdata"
+    wkey = gd.WKEY[kind]
     ptr = lambda t: None if t is None else t.data_ptr()
     s13 = gate_up["scale"].view(torch.uint8) if kind in ("w4", "w6") else gate_up["scale"]
     s2 = down["scale"].view(torch.uint8) if kind in ("w4", "w6") else down["scale"]
@@ -28,7 +28,9 @@ def _call_static(lib, kind, x, ids, w, banks, cbs, out):
                                     torch.cuda.current_stream().cuda_stream)
 
 
-@pytest.mark.parametrize("kind,M", [("fp8", 16), ("w4", 4)])
+# fp8 and w4 run the mma.sync decode; fp8c and w4a8 the tensor-core decodes, whose per-segment counters live in the
+# same array and are cleared by the kernel at its end (the second call checks they were)
+@pytest.mark.parametrize("kind,M", [("fp8", 16), ("w4", 4), ("fp8c", 16), ("w4a8", 16)])
 def test_static_scratch_decode_matches_workspace_decode(cuda, kind, M):
     from drama3_b200 import _lib, kernels
     lib = _lib.lib()
@@ -52,3 +54,5 @@ def test_static_scratch_rejects_shapes_beyond_its_size(cuda):
     assert lib.d3_moe_decode_static(*args) == _lib.D3_ERR_TOO_LARGE
     args = [0, 16, 1, 1, 8, E, H, 1024] + [16] * 11 + [None]  # intermediate 1024 > 768
     assert lib.d3_moe_decode_static(*args) == _lib.D3_ERR_TOO_LARGE
+    args = [0, 16, 1, 1, 8, E, 1024, I] + [16] * 11 + [None]  # hidden 1024: a bad argument, not a size limit
+    assert lib.d3_moe_decode_static(*args) == _lib.D3_ERR_ARG
