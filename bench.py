@@ -1,5 +1,5 @@
 """Benchmark: MoE decode tokens/s of the routed-expert path on B200 (FP8 experts with
-per-output-channel scales).
+per-output-channel scales, 16 lines, 48 layers as configs[4]).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mine|reference] [--lines 16] [--layers 48]
                     [--kind fp8c] [--no-extras] [--prefill-only]
@@ -11,16 +11,21 @@ e4m3 rows + fp32 per-output-channel scales) and its own see
 larger than L2, so every step streams its experts from HBM (no flush needed). Inputs are resident in HBM; the timed
 region replays one CUDA graph per step and is bracketed by cudaProfilerStart/Stop, so `ncu --profile-from-start off`
 sees exactly its launches; `--layers 4` is the small case for multi-pass captures (the same banks and routing as the
-first 4 layers of the full run). Multi-GPU: independent replicas (each rank decodes its own lines with all experts
-resident; no collective), weak scaling. `value` = tokens/s of all ranks; timing = CUDA events, max over ranks.
+first 4 layers of the full run).
 
-Also reported at N = 1: the 1-line decode; W4A8 at 16 and 1 lines; the reference's fp8 layout
-(128 x 128 block scales) at 16 lines beside the reference's own kernels (compiled from drama3/kernels.py into
-oracle/_ref) on the same GPU; the end-to-end rate through the Python API with host buffers; a prompt-pass leg
-(2048 tokens, Zipf-skewed routing; W6A8, and the reference's W6 and fp8 layouts beside the
-reference's kernels); the reference's CPU path on the host cores. At N > 1: expert parallelism over the N GPUs
-(each holds 128 / N experts of every layer, all decode the same 16 lines, fp32 partials all-gathered and summed in
-rank order per layer). `--impl reference` runs only that CPU path (rank 0) and prints its line.
+One GPU: `value` is that decode. N > 1 GPUs: `value` is expert parallelism, one 16-line job over all N GPUs (strong
+scaling): rank r holds experts expert_range(128, r, N) of every layer, every rank decodes all 16 lines over its own
+experts, and each layer's fp32 partials are exchanged over NVLink by the decode kernel itself (peer stores into every
+rank's exchange area) and summed in rank order. Timing: CUDA events, max over ranks. The replicated layout (each rank
+its own 16 lines, all experts; weak scaling) and the NCCL all-gather exchange are reported beside it.
+
+Extras at N = 1, one per BASELINE configuration (each with its roofline fraction and, where the reference has one,
+its CPU path timed on the host cores): config 1 (int8 ConvRot, 1 line, and the reference's CPU int8 path); config 2
+(fp8 block scales at 1, 4 and 16 lines with the reference's own kernels beside them, fp8c at 1 and 4 lines);
+config 3 (W4A8 and the reference's W4 layout at 1 and 16 lines); config 4 (the 2048-row Zipf-skewed prompt pass);
+config 5's host-offload slot-cache mode (768 slots on one GPU: hit rate, PCIe GB/s, tokens/s); the end-to-end rate
+through the drop-in module (FP8Experts) with host buffers in and out. `--impl reference` runs the reference's CPU
+decode (rank 0) and prints its line.
 """
 import argparse
 import json
@@ -41,14 +46,18 @@ import torch  # noqa: E402
 METRIC = "MoE decode tokens/s (1 & 16 lines), expert GEMV HBM GB/s vs ~8 TB/s, 1-8 B200"
 E, H, I, K_TOP = 128, 2048, 768, 8
 LAYERS = 48
-KINDS = ("fp8c", "fp8", "w4a8", "w6a8", "w6")
+KINDS = ("fp8c", "fp8", "w4a8", "w6a8", "int8", "w4", "w6")
 FORMAT_NAMES = {
     "fp8c": "e4m3 rows + fp32 per-output-channel scales (BASELINE configs[1])",
-    "fp8": "e4m3 rows + fp32 128x128 block scales (the reference's layout)",
+    "fp8": "e4m3 rows + fp32 128x128 block scales (the reference's fp8 layout)",
+    "int8": "int8 rows + fp32 per-row scales in the ConvRot basis (the reference's int8 layout, BASELINE configs[0])",
     "w4a8": "int4 two per byte + bf16 group-128 scales, int8 per-row activations (BASELINE configs[2])",
     "w6a8": "int6 four per three bytes + bf16 group-128 scales, int8 per-row activations (BASELINE configs[3])",
+    "w4": "4-bit codebook codes + e4m3 group-16 scales + s_channel, ConvRot (the reference's W4A8 layout)",
     "w6": "6-bit codes + e4m3 group-16 scales + s_channel, ConvRot (the reference's W6A8 layout)",
 }
+CODEBOOK4 = (-1.0, -0.6962, -0.5251, -0.3949, -0.2844, -0.1848, -0.0911, 0.0, 0.0796, 0.1609, 0.2461, 0.3379, 0.4407,
+             0.5626, 0.7230, 1.0)
 # dram bytes (read + write) per launch over algorithmic bytes per launch, from the ncu capture of the small case
 # (bench.py --layers 4, the first 2 launches of the timed step: 86 and 87 routed experts); the full run's traffic is
 # this ratio x its own bytes
@@ -57,13 +66,17 @@ TRAFFIC_SOURCE = ("ncu capture of the 4-layer small case (bench.py --layers 4, m
                   "DRAM read + write / algorithmic bytes of the same launches")
 
 
-def kernel_of(kind, lines):
-    """(kernel name, arithmetic) of the fused decode for `kind` banks and `lines` rows."""
+def kernel_of(kind):
+    """(kernel name, arithmetic) of the fused decode for `kind` banks."""
     if kind == "fp8c":
         return ("moe_decode_tc_kernel (tcgen05 kind::f8f6f4; one persistent launch per layer: plan, gate_up + "
                 "SwiGLU, down, combine)",
-                "e4m3 x e4m3 tensor-core MMA: e4m3 weights as stored, bf16 activations as two exact e4m3 terms, "
-                "f32 accumulation")
+                "e4m3 weights x e4m3 activation terms on the tensor cores, f32 accumulation: bf16 rows exact as two "
+                "terms, the fp32 SwiGLU rows of the down projection as four terms (16 significant bits)")
+    if kind == "w4a8":
+        return ("moe_decode_tc8_kernel (tcgen05 kind::i8; one persistent launch per layer)",
+                "int4 weights expanded to int8 x int8 per-row activations on the tensor cores, s32 accumulation, "
+                "bf16 group scales folded per 128 columns")
     return (f"moe_decode_kernel<{kind}> (mma.sync; one persistent launch per layer: plan, gate_up + SwiGLU, down, "
             f"combine)", "f16 MMA inputs (exact weight codes), f32 accumulation")
 
@@ -79,20 +92,44 @@ def rand_bank(kind, n, k, gen, device):
         q = torch.randint(0, 256, (E * n, k * int(kind[1]) // 8), generator=gen, device=device, dtype=torch.uint8)
         s = (torch.rand((E * n, k // 128), generator=gen, device=device) * 2e-3 + 1e-3).to(torch.bfloat16)
         return {"_qdata": q, "scale": s}
-    q = torch.randint(0, 256, (E * n, 3 * k // 4), generator=gen, device=device, dtype=torch.uint8)
-    g = torch.randint(0x30, 0x50, (E * n, k // 16), generator=gen, device=device, dtype=torch.uint8)
+    if kind == "int8":
+        q = torch.randint(-127, 128, (E * n, k), generator=gen, device=device, dtype=torch.int8)
+        return {"_qdata": q, "scale": torch.rand((E * n,), generator=gen, device=device) * 2e-4 + 1e-4}
+    bits = int(kind[1])
+    q = torch.randint(0, 256, (E * n, k * bits // 8), generator=gen, device=device, dtype=torch.uint8)
+    lo, hi = (0x50, 0x70) if bits == 4 else (0x30, 0x50)
+    g = torch.randint(lo, hi, (E * n, k // 16), generator=gen, device=device, dtype=torch.uint8)
     c = torch.rand((E * n,), generator=gen, device=device) * 2e-4 + 1e-4
     return {"_qdata": q, "scale": g, "s_channel": c}
+
+
+def codebooks(kind, device):
+    if kind != "w4":
+        return (None, None)
+    cb = torch.tensor(CODEBOOK4, dtype=torch.float32, device=device)
+    return (cb, cb.clone())
 
 
 def expert_bytes(kind):
     """Algorithmic bytes of one expert of the BASELINE shape in `kind`'s layout (weight and scale bytes)."""
     total = 0
     for n, k in ((2 * I, H), (H, I)):
-        total += n * {"fp8": k, "fp8c": k, "w4a8": k // 2, "w6a8": 3 * k // 4, "w6": 3 * k // 4}[kind]
-        total += {"fp8": (n // 128) * (k // 128) * 4, "fp8c": n * 4, "w4a8": n * (k // 128) * 2,
-                  "w6a8": n * (k // 128) * 2, "w6": n * (k // 16 + 4)}[kind]
+        total += n * {"fp8": k, "fp8c": k, "int8": k, "w4a8": k // 2, "w6a8": 3 * k // 4, "w4": k // 2,
+                      "w6": 3 * k // 4}[kind]
+        total += {"fp8": (n // 128) * (k // 128) * 4, "fp8c": n * 4, "int8": n * 4, "w4a8": n * (k // 128) * 2,
+                  "w6a8": n * (k // 128) * 2, "w4": n * (k // 16 + 4), "w6": n * (k // 16 + 4)}[kind]
     return total
+
+
+def make_routing(lines, n_layers, seed, device):
+    """Per-layer seeded routing: distinct top-8 experts per row, renormalized bf16-valued weights."""
+    cpu_gen = torch.Generator().manual_seed(seed)
+    ids, weights = [], []
+    for _ in range(n_layers):
+        w, i = torch.softmax(torch.randn((lines, E), generator=cpu_gen), dim=-1).topk(K_TOP, dim=-1)
+        ids.append(i)
+        weights.append((w / w.sum(-1, keepdim=True)).to(torch.bfloat16).float())
+    return torch.stack(ids).to(device), torch.stack(weights).to(device)
 
 
 def make_layers(device, lines, kind="fp8c", seed=4, n_layers=LAYERS):
@@ -100,13 +137,8 @@ def make_layers(device, lines, kind="fp8c", seed=4, n_layers=LAYERS):
     not depend on n_layers or the format."""
     gen = torch.Generator(device=device).manual_seed(seed)
     layers = [tuple(rand_bank(kind, n, k, gen, device) for n, k in ((2 * I, H), (H, I))) for _ in range(n_layers)]
-    cpu_gen = torch.Generator().manual_seed(seed + 1)
-    ids, weights = [], []
-    for _ in range(n_layers):
-        w, i = torch.softmax(torch.randn((lines, E), generator=cpu_gen), dim=-1).topk(K_TOP, dim=-1)
-        ids.append(i)
-        weights.append((w / w.sum(-1, keepdim=True)).to(torch.bfloat16).float())
-    return layers, torch.stack(ids).to(device), torch.stack(weights).to(device)
+    ids, weights = make_routing(lines, n_layers, seed + 1, device)
+    return layers, ids, weights
 
 
 def peaks():
@@ -159,12 +191,14 @@ class Clocks:
                 "samples": len(self.rows), "reasons": reasons}
 
 
-def unique_bytes(ids, kind):
+def unique_bytes(ids, kind, rows_bytes=True):
     """Algorithmic bytes of one step: each layer's unique experts, plus its rows in and out (bf16)."""
     per, total = expert_bytes(kind), 0
     lines = ids.shape[1]
     for layer in ids.cpu():
-        total += len(set(layer.reshape(-1).tolist())) * per + 2 * lines * H * 2 + lines * K_TOP * 12
+        total += len(set(layer.reshape(-1).tolist())) * per
+        if rows_bytes:
+            total += 2 * lines * H * 2 + lines * K_TOP * 12
     return total
 
 
@@ -181,11 +215,13 @@ def capture(fn, warmup, stream):
     return graph
 
 
-def time_replays(graph, steps, stream):
-    """ms per replay of `graph`, CUDA events on `stream`."""
+def time_replays(graph, steps, stream, before=None):
+    """ms per replay of `graph`, CUDA events on `stream`; `before(i)` runs ahead of replay i (inside the timing)."""
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(stream)
-    for _ in range(steps):
+    for i in range(steps):
+        if before is not None:
+            before(i)
         graph.replay()
     end.record(stream)
     torch.cuda.synchronize()
@@ -204,18 +240,19 @@ def replay_spread(graph, steps, stream):
     return {"steps": steps, "ms_median": t[len(t) // 2], "ms_p90": t[min(len(t) - 1, (9 * len(t)) // 10)]}
 
 
-def decode_leg(kernels, device, kind, lines, steps, warmup, stream, n_layers, layers):
+def decode_leg(kernels, device, kind, lines, steps, warmup, stream, n_layers, layers, cbs=(None, None)):
     """{tokens_per_s, ms_per_step, hbm_gbs, frac, ...} of the fused decode of `lines` rows through n_layers layers;
-    layers = (banks, ids, weights)."""
+    layers = (banks, ids, weights), the first `lines` rows of the routing used."""
     hbm_peak, _ = peaks()
     banks, ids, weights = layers
+    ids, weights = ids[:, :lines].contiguous(), weights[:, :lines].contiguous()
     x = torch.randn((lines, H), generator=torch.Generator().manual_seed(7)).to(torch.bfloat16).to(device)
     ws = kernels.decode_workspace(lines, K_TOP, I, device)
     outs = torch.empty((n_layers, lines, H), dtype=torch.bfloat16, device=device)
 
     def step():
         for l_ in range(n_layers):
-            kernels.moe_decode(kind, x, ids[l_], weights[l_], banks[l_], workspace=ws, out=outs[l_])
+            kernels.moe_decode(kind, x, ids[l_], weights[l_], banks[l_], cbs, workspace=ws, out=outs[l_])
 
     with torch.cuda.stream(stream):
         graph = capture(step, warmup, stream)
@@ -225,7 +262,51 @@ def decode_leg(kernels, device, kind, lines, steps, warmup, stream, n_layers, la
     gbs = b / (ms * 1e-3) / 1e9
     return {"tokens_per_s": lines / (ms * 1e-3), "ms_per_step": ms, "us_per_layer": 1e3 * ms / n_layers,
             "hbm_gbs": gbs, "frac": gbs / hbm_peak, "bytes_per_step": b, "format": FORMAT_NAMES[kind],
-            "lines": lines}
+            "lines": lines, "kernel": kernel_of(kind)[0]}
+
+
+def reference_gpu_leg(device, kind, lines, steps, stream, n_layers, layers, cbs=(None, None)):
+    """The reference's own kernels (drama3/kernels.py compiled into oracle/_ref) on the same banks, rows and routing,
+    driven as drama3/offload.py:108-123 drives them (gemv -> SwiGLU [+ rotation] -> gemv -> weighted_sum), one row at
+    a time as drama3/model.py:111-113 runs lines, one CUDA graph per step."""
+    from oracle import ref_gpu
+    if not ref_gpu.available():
+        return {"unavailable": "reference kernels not built (oracle/_ref)"}
+    banks, ids, weights = layers
+    x = torch.randn((lines, H), generator=torch.Generator().manual_seed(7)).to(torch.bfloat16).to(device)
+
+    def ref_step():
+        for l_ in range(n_layers):
+            ref_gpu.lines_decode(x, ids[l_, :lines], weights[l_, :lines], banks[l_], (2 * I, H), kind, cbs)
+
+    with torch.cuda.stream(stream):
+        graph = capture(ref_step, 2, stream)
+        ms = time_replays(graph, max(3, min(steps, 10)), stream)
+    del graph
+    return {"tokens_per_s": lines / (ms * 1e-3), "ms_per_step": ms, "us_per_layer": 1e3 * ms / n_layers,
+            "what": "reference kernels (drama3/kernels.py, nvcc sm_100) driven as drama3/offload.py:108-123, one "
+                    "row at a time"}
+
+
+def layout_legs(kernels, device, kind, lines_list, args, stream, n_layers, seed, reference=False):
+    """decode_leg at each line count of lines_list on one set of `kind` banks (and the reference's kernels)."""
+    layers = make_layers(device, max(lines_list), kind, seed, n_layers)
+    cbs = codebooks(kind, device)
+    out = {}
+    for lines in lines_list:
+        leg = decode_leg(kernels, device, kind, lines, args.steps, args.warmup, stream, n_layers, layers, cbs)
+        if reference:
+            try:
+                ref = reference_gpu_leg(device, kind, lines, args.steps, stream, n_layers, layers, cbs)
+                leg["reference_gpu"] = ref
+                if "ms_per_step" in ref:
+                    leg["speedup_vs_reference_gpu"] = ref["ms_per_step"] / leg["ms_per_step"]
+            except Exception as exc:  # the comparison must not sink the bench line
+                leg["reference_gpu"] = {"error": repr(exc)[:200]}
+        out[f"lines_{lines}"] = leg
+    del layers
+    torch.cuda.empty_cache()
+    return out
 
 
 def prefill_leg(device, steps, tokens=2048, seed=3):
@@ -308,10 +389,84 @@ def prefill_leg(device, steps, tokens=2048, seed=3):
     return out
 
 
-def cpu_reference(lines, layers_sampled=2, seed=4, n_layers=LAYERS, seconds=10.0):
-    """The reference's CPU decode (oracle/cpu_port.py, the FP8Experts CPU forward with its block-scaled layout) on
-    the host cores: `lines` rows through at least `layers_sampled` layers and about `seconds` of work, scaled to
-    n_layers layers. Returns (tokens/s, seconds, threads, sample description)."""
+def slot_cache_leg(device, args, stream, slots_per_layer=16, n_routings=8, seed=40):
+    """BASELINE configs[4]'s host-offload mode on one GPU: every layer's fp8 experts (the reference's block-scaled
+    layout, 29 GB at 48 layers) in pinned host memory behind one slot cache of 16 slots per layer (768 at 48
+    layers), decoded through the drop-in ExpertStore / OffloadedExperts: per layer and row, resolve (slot lookup and
+    least-used eviction on the GPU), gate_up, SwiGLU, down, weighted sum, with missed experts read from host memory
+    over PCIe by the GEMVs themselves (and filled into their slot). Lines run one row at a time, as the store does
+    for the reference. A step replays one CUDA graph; each step takes its routing from n_routings seeded routings in
+    turn (copied in ahead of the replay, inside the timing). Reports the cache's hit rate, the PCIe bytes of the
+    misses and tokens/s."""
+    from drama3_b200 import offload
+    n_layers, lines = args.layers, args.lines
+    gen = torch.Generator(device=device).manual_seed(seed)
+    per_expert = expert_bytes("fp8")
+    # the cache budget is the configuration's slot count: the pool makes budget // expert bytes slots
+    store = offload.ExpertStore(slots_per_layer * n_layers * per_expert, pin=True)
+    modules = []
+    for _ in range(n_layers):
+        ex = offload.FP8Experts(E, H, I, device="meta")
+        for name, n, k in (("gate_up", 2 * I, H), ("down", H, I)):
+            bank = rand_bank("fp8", n, k, gen, device)
+            w = torch.empty((E, n, k), dtype=torch.uint8, pin_memory=True)
+            s = torch.empty((E, n // 128, k // 128), dtype=torch.float32, pin_memory=True)
+            w.view(-1, k).copy_(bank["weight"])
+            s.view(-1, k // 128).copy_(bank["scale"])
+            setattr(ex, f"{name}_weight", torch.nn.Parameter(w.view(torch.float8_e4m3fn), requires_grad=False))
+            setattr(ex, f"{name}_scale", torch.nn.Parameter(s, requires_grad=False))
+        modules.append(store.add(ex))
+    torch.cuda.synchronize()
+    routings = [make_routing(lines, n_layers, seed + 1 + r, device) for r in range(n_routings)]
+    ids_buf, w_buf = torch.empty_like(routings[0][0]), torch.empty_like(routings[0][1])
+    x = torch.randn((lines, H), generator=torch.Generator().manual_seed(7)).to(torch.bfloat16).to(device)
+    outs = torch.empty((n_layers, lines, H), dtype=torch.bfloat16, device=device)
+
+    def step():
+        for l_ in range(n_layers):
+            for r in range(lines):
+                outs[l_, r:r + 1] = modules[l_](x[r:r + 1], ids_buf[l_, r:r + 1], w_buf[l_, r:r + 1])
+
+    def load(i):
+        ids_buf.copy_(routings[i % n_routings][0], non_blocking=True)
+        w_buf.copy_(routings[i % n_routings][1], non_blocking=True)
+
+    with store.session(device, rows=lines):
+        cache = store.cache
+        with torch.cuda.stream(stream):
+            load(0)
+            step()  # first step eagerly: moves the cache state to the device
+            torch.cuda.synchronize()
+            graph = capture(step, 0, stream)
+            for i in range(args.warmup):
+                load(i)
+                graph.replay()
+            torch.cuda.synchronize()
+            before = cache.reads.clone()
+            n = max(3, min(args.steps, 8))
+            ms = time_replays(graph, n, stream, before=load)
+            reads = (cache.reads - before).tolist()
+        del graph
+        slots = cache.count
+    total = sum(reads[:2])
+    miss_bytes = reads[1] * per_expert / n
+    del modules, store
+    torch.cuda.empty_cache()
+    return {"tokens_per_s": lines / (ms * 1e-3), "ms_per_step": ms, "us_per_layer": 1e3 * ms / n_layers,
+            "slots": slots, "slots_per_layer": slots_per_layer, "layers": n_layers, "lines": lines,
+            "hit_rate": reads[0] / total if total else None, "expert_reads_per_step": total / n,
+            "misses_per_step": reads[1] / n, "pcie_gbs": miss_bytes / (ms * 1e-3) / 1e9,
+            "format": FORMAT_NAMES["fp8"],
+            "routing": f"{n_routings} seeded routings used in turn, one per step",
+            "what": "ExpertStore (pinned host banks, 768-slot GPU cache): resolve + gemv_fp8 (slot or host "
+                    "zero-copy, filling the slot) + SwiGLU + gemv_fp8 + weighted_sum per layer and row, one graph"}
+
+
+# ---- CPU baselines: the reference's CPU paths (oracle/cpu_port.py), bounded samples on the host cores
+def cpu_fp8(lines, n_layers=LAYERS, seed=4, seconds=10.0, min_layers=2):
+    """The reference's CPU decode for fp8 experts (the FP8Experts CPU forward, block-scaled layout: the reference
+    has no per-channel layout) of `lines` rows, one row at a time; at least min_layers layers and about `seconds`.
+    Returns (tokens/s of an n_layers step, seconds timed, threads, layers timed, sample description)."""
     from oracle import cpu_port
     torch.set_num_threads(os.cpu_count() or 1)
     gen = torch.Generator().manual_seed(seed)
@@ -324,7 +479,7 @@ def cpu_reference(lines, layers_sampled=2, seed=4, n_layers=LAYERS, seconds=10.0
         ds = torch.rand((E, H // 128, I // 128), generator=gen) * 1e-4
         banks.append((gu, gs, dn, ds))
     total, done = 0.0, 0
-    while done < n_layers and (done < layers_sampled or total < seconds):
+    while done < n_layers and (done < min_layers or total < seconds):
         gu, gs, dn, ds = banks[done % 2]
         w, ids = torch.softmax(torch.randn((lines, E), generator=gen), -1).topk(K_TOP, dim=-1)
         w = (w / w.sum(-1, keepdim=True)).to(torch.bfloat16)
@@ -332,92 +487,258 @@ def cpu_reference(lines, layers_sampled=2, seed=4, n_layers=LAYERS, seconds=10.0
         cpu_port.fp8_decode_lines(x, ids, w, gu, gs, dn, ds)
         total += time.perf_counter() - started
         done += 1
-    per_step = total / done * n_layers
-    sample = (f"{lines} rows x {done} layers ({total:.1f} s) of the reference CPU path (bf16 dequant + matmuls, one "
-              f"row at a time), scaled to {n_layers} layers")
-    return lines / per_step, total, torch.get_num_threads(), sample
+    sample = (f"{lines} rows x {done} layers timed ({total:.1f} s) of the reference's CPU decode (FP8Experts CPU "
+              f"forward: bf16 dequantization + matmuls, one row at a time), tokens/s of a {n_layers}-layer step")
+    return lines / (total / done * n_layers), total, torch.get_num_threads(), done, sample
 
 
-def ep_leg(kernels, device, kind, args, stream, pg):
-    """Expert-parallel decode of `lines` rows through n_layers layers: rank r holds experts expert_range(E, r, N) of
-    every layer (seeded whole banks, sliced), all ranks see the same rows and routing; per layer one fused decode of
-    the local experts (fp32 partial) and one all-gather + rank-order sum, captured as one CUDA graph per step. Timed
-    with CUDA events, max over ranks."""
+def cpu_int8(n_layers=LAYERS, seed=0, seconds=8.0):
+    """BASELINE configs[0]'s CPU baseline: the reference's own CPU int8 decode of one row (hadamard rotation,
+    experts_on_cpu with torch._weight_int8pack_mm, routing-weighted sum; oracle/cpu_port.int8_decode_row, bit for
+    bit the reference's output on config 1), over layers of random int8 banks."""
+    from oracle import cpu_port
+    torch.set_num_threads(os.cpu_count() or 1)
+    gen = torch.Generator().manual_seed(seed)
+    rot = cpu_port.hadamard()
+    banks = [(torch.randint(-127, 128, (E, 2 * I, H), generator=gen, dtype=torch.int8),
+              torch.rand((E, 2 * I), generator=gen) * 1e-3,
+              torch.randint(-127, 128, (E, H, I), generator=gen, dtype=torch.int8),
+              torch.rand((E, H), generator=gen) * 1e-3) for _ in range(2)]
+    x = torch.randn((1, H), generator=gen).to(torch.bfloat16)
+    total, done = 0.0, 0
+    while done < n_layers and (done < 3 or total < seconds):
+        w, ids = torch.softmax(torch.randn((E,), generator=gen), -1).topk(K_TOP)
+        started = time.perf_counter()
+        cpu_port.int8_decode_row(x, ids, w / w.sum(), *banks[done % 2], rot)
+        total += time.perf_counter() - started
+        done += 1
+    sample = (f"1 row x {done} layers timed ({total:.2f} s) of the reference's CPU int8 decode (experts_on_cpu), "
+              f"tokens/s of a {n_layers}-layer step")
+    return 1 / (total / done * n_layers), total, torch.get_num_threads(), done, sample
+
+
+def cpu_codes(kind, lines, n_layers=LAYERS, seed=2, seconds=8.0):
+    """Configs[2]/[3]'s CPU baseline for the reference's W4 / W6 code layouts: a RESTATEMENT (the reference's CPU
+    matmuls for these layouts live in comfy_kitchen, absent): codes decoded as drama3/kernels.py:466-483 to bf16
+    weights, then the decode's matmuls, one row at a time (oracle/cpu_port.codes_decode_row)."""
+    from oracle import cpu_port
+    torch.set_num_threads(os.cpu_count() or 1)
+    bits = int(kind[1])
+    gen = torch.Generator().manual_seed(seed)
+    rot = cpu_port.hadamard()
+    cbs = (torch.tensor(CODEBOOK4), torch.tensor(CODEBOOK4)) if bits == 4 else (None, None)
+
+    def bank(n, k):
+        return (torch.randint(0, 256, (E, n, k * bits // 8), generator=gen, dtype=torch.uint8),
+                torch.randint(0x30, 0x50, (E, n, k // 16), generator=gen, dtype=torch.uint8),
+                torch.rand((E, n), generator=gen) * 2e-4 + 1e-4)
+
+    b13, b2 = bank(2 * I, H), bank(H, I)
+    x = torch.randn((lines, H), generator=gen).to(torch.bfloat16)
+    total, done = 0.0, 0
+    while done < n_layers and (done < 2 or total < seconds):
+        w, ids = torch.softmax(torch.randn((lines, E), generator=gen), -1).topk(K_TOP, dim=-1)
+        started = time.perf_counter()
+        for t in range(lines):
+            cpu_port.codes_decode_row(x[t:t + 1], ids[t], w[t] / w[t].sum(), b13, b2, bits, cbs, rot)
+        total += time.perf_counter() - started
+        done += 1
+    sample = (f"{lines} rows x {done} layers timed ({total:.1f} s), restatement of the reference's {kind} CPU "
+              f"decode (codes decoded to bf16 weights, matmuls, one row at a time), tokens/s of a {n_layers}-layer "
+              "step")
+    return lines / (total / done * n_layers), total, torch.get_num_threads(), done, sample
+
+
+def cpu_line(result):
+    tps, secs, threads, done, sample = result
+    return {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port", "layers_timed": done,
+            "seconds": secs, "sample": sample}
+
+
+def e2e_leg(device, layers, x, ids, weights, lines, steps):
+    """End to end through the drop-in module: 48 FP8Experts modules (per-channel layout, parameters viewing the
+    bench's banks), host buffers in (rows, routing) and out (the last layer's rows), every step, each copy
+    included in the timing."""
+    from drama3_b200 import offload
+    mods = []
+    for banks in layers:
+        ex = offload.FP8Experts(E, H, I, device="meta", per_channel=True)
+        for name, bank, n, k in (("gate_up", banks[0], 2 * I, H), ("down", banks[1], H, I)):
+            setattr(ex, f"{name}_weight", torch.nn.Parameter(bank["weight"].view(E, n, k).view(torch.float8_e4m3fn),
+                                                             requires_grad=False))
+            setattr(ex, f"{name}_scale", torch.nn.Parameter(bank["scale"].view(E, n), requires_grad=False))
+        mods.append(ex)
+    xh = x.cpu().pin_memory()
+    idh, wh = ids.cpu().pin_memory(), weights.cpu().pin_memory()
+    outh = torch.empty((lines, H), dtype=torch.bfloat16).pin_memory()
+    xd, idd, wd = torch.empty_like(x), torch.empty_like(ids), torch.empty_like(weights)
+    n_e2e = max(3, min(steps, 20))
+    for it in range(n_e2e + 2):
+        if it == 2:
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            es.record()
+        xd.copy_(xh, non_blocking=True)
+        idd.copy_(idh, non_blocking=True)
+        wd.copy_(wh, non_blocking=True)
+        out = xd
+        for l_, mod in enumerate(mods):
+            out = mod(xd, idd[l_], wd[l_])
+        outh.copy_(out, non_blocking=True)
+    ee.record()
+    torch.cuda.synchronize()
+    ms = es.elapsed_time(ee) / n_e2e
+    return {"value": lines / (ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": xh.nbytes + idh.nbytes + wh.nbytes,
+            "d2h_bytes_per_step": outh.nbytes, "ms_per_step": ms,
+            "wall_ms_per_step": 1e3 * (time.perf_counter() - t0) / n_e2e,
+            "through": "drama3_b200.offload.FP8Experts(per_channel=True).forward, 48 modules, eager (no graph)"}
+
+
+def ep_setup(device, kind, args, rank, world):
+    """Rank r's expert-parallel banks (experts expert_range(E, r, N) of every layer, sliced from seeded whole banks),
+    the shared rows and routing."""
     from drama3_b200 import ep
-    rank, world = pg.get_rank(), pg.get_world_size()
     n_layers = args.layers
     gen = torch.Generator(device=device).manual_seed(4)
     layers = []
     for _ in range(n_layers):
         full = tuple(rand_bank(kind, n, k, gen, device) for n, k in ((2 * I, H), (H, I)))
-        layers.append(ep.ExpertParallelDecode(kind, tuple({n: t.clone() for n, t in b.items()}
-                                                          for b in ep.local_banks(full, E, rank, world)), E))
+        layers.append(tuple({n: t.clone() for n, t in b.items()} for b in ep.local_banks(full, E, rank, world)))
         del full
     torch.cuda.empty_cache()
-    cpu_gen = torch.Generator().manual_seed(5)
-    ids, weights = [], []
-    for _ in range(n_layers):
-        w, i = torch.softmax(torch.randn((args.lines, E), generator=cpu_gen), dim=-1).topk(K_TOP, dim=-1)
-        ids.append(i.to(device))
-        weights.append((w / w.sum(-1, keepdim=True)).to(torch.bfloat16).float().to(device))
+    ids, weights = make_routing(args.lines, n_layers, 5, device)
     x = torch.randn((args.lines, H), generator=torch.Generator().manual_seed(7)).to(torch.bfloat16).to(device)
-
-    peer = ep.PeerExchange(args.lines, H, device)
-    peer_layers = [ep.ExpertParallelDecode(kind, lay.banks, E, peer=peer) for lay in layers]
-    outs = [None] * n_layers
-    timed = {}
-    for name, mods in (("local", layers), ("nccl", layers), ("peer", peer_layers)):
-        def step(mods=mods, local=name == "local"):
-            for l_ in range(n_layers):
-                # "local": each rank's decode alone (its fp32 partial, no exchange), the floor of both exchanges
-                outs[l_] = (mods[l_].partial if local else mods[l_])(x, ids[l_], weights[l_])
-
-        with torch.cuda.stream(stream):
-            graph = capture(step, args.warmup, stream)  # the exchanges are captured with the kernels
-            torch.cuda.synchronize()
-            pg.barrier()
-            ms = time_replays(graph, max(3, min(args.steps, 20)), stream)
-        del graph  # released before the process group is destroyed
-        t = torch.tensor([ms], device=device)
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        timed[name] = float(t.item())
-    fault = kernels._lib.take_fault()
-    peer.close()
-    first, count = ep.expert_range(E, rank, world)
-    ms = timed["peer"]
-    return {"tokens_per_s": args.lines / (ms * 1e-3), "ms_per_step": ms, "us_per_layer": 1e3 * ms / n_layers,
-            "experts_per_rank": count, "scaling": "strong (one job of `lines` rows over all ranks)",
-            "exchange": "fused: each rank's decode kernel stores its fp32 partial into every rank's exchange area "
-                        "over NVLink (P2P), flags with system-scope release, a small reduce kernel sums in rank order",
-            "fault_bits": fault,
-            "nccl_all_gather": {"tokens_per_s": args.lines / (timed["nccl"] * 1e-3), "ms_per_step": timed["nccl"],
-                                "us_per_layer": 1e3 * timed["nccl"] / n_layers},
-            "decode_only_us_per_layer": 1e3 * timed["local"] / n_layers,
-            "resident_bytes_per_rank": sum(t.nbytes for lay in layers for b in lay.banks for t in b.values())}
+    return layers, ids, weights, x
 
 
-def config(args):
+def config(args, world):
+    if world > 1:
+        parallelism = (f"expert parallelism over {world} GPUs (experts 128/{world} per rank, one {args.lines}-line "
+                       "job; partials exchanged over NVLink by the decode kernel)")
+    else:
+        parallelism = "1 GPU"
     return {"workload": f"MoE decode, {args.lines} lines x {args.layers} layers per step, {args.kind} experts "
                         f"(BASELINE configs[1] layer shape; 48 layers as configs[4])",
             "layers": args.layers, "lines": args.lines, "experts": E, "top_k": K_TOP, "hidden": H, "intermediate": I,
             "format": FORMAT_NAMES[args.kind],
             "l2": f"inputs larger than L2: {args.layers * E * expert_bytes(args.kind) / 1e9:.1f} GB of expert banks, "
                   f"each layer's routed experts streamed per step",
-            "parallelism": f"replicas x{args.gpus} (lines data-parallel)"}
+            "parallelism": parallelism}
 
 
-def run_reference_arm(args, rank):
-    if rank != 0:
-        return
-    tps, secs, threads, sample = cpu_reference(args.lines, layers_sampled=max(1, min(args.steps, 2)),
-                                               n_layers=args.layers)
+def run_reference_arm(args, world):
+    """The reference's CPU decode on the host cores: each step is a bounded sample of the workload, `lines` rows
+    through ONE MoE layer (about 0.5 s at 16 lines); `value` is tokens/s of a whole `layers`-layer step at that
+    layer rate. The reference's CPU forward reads its only fp8 layout, 128x128 block scales (the per-channel layout
+    of this bench's headline is not in the reference; the bytes differ by under 0.3 %)."""
+    from oracle import cpu_port
+    torch.set_num_threads(os.cpu_count() or 1)
+    gen = torch.Generator().manual_seed(4)
+    x = torch.randn((args.lines, H), generator=gen).to(torch.bfloat16)
+    gu = torch.randint(0, 126, (E, 2 * I, H), generator=gen, dtype=torch.uint8)
+    dn = torch.randint(0, 126, (E, H, I), generator=gen, dtype=torch.uint8)
+    gs = torch.rand((E, 2 * I // 128, H // 128), generator=gen) * 1e-4
+    ds = torch.rand((E, H // 128, I // 128), generator=gen) * 1e-4
+    routes = []
+    for _ in range(4):
+        w, ids = torch.softmax(torch.randn((args.lines, E), generator=gen), -1).topk(K_TOP, dim=-1)
+        routes.append((ids, (w / w.sum(-1, keepdim=True)).to(torch.bfloat16)))
+    for i in range(args.warmup):
+        cpu_port.fp8_decode_lines(x, *routes[i % 4], gu, gs, dn, ds)
+    started = time.perf_counter()
+    for i in range(args.steps):
+        cpu_port.fp8_decode_lines(x, *routes[i % 4], gu, gs, dn, ds)
+    secs = time.perf_counter() - started
+    layer_s = secs / args.steps
+    tps = args.lines / (layer_s * args.layers)
+    cfg = config(args, world)
+    cfg["format"] = FORMAT_NAMES["fp8"] + " (the reference's only fp8 layout)"
+    cfg["sample_layers_per_step"] = 1
+    sample = (f"each step: {args.lines} rows through 1 MoE layer of the reference's CPU decode (FP8Experts CPU "
+              f"forward, one row at a time); {args.steps} steps timed ({secs:.1f} s); value = tokens/s of a "
+              f"{args.layers}-layer step at that layer rate")
     line = {"impl": "reference", "metric": METRIC, "value": tps, "unit": "tokens/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * args.lines / tps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (CPU)",
-            "data": "synthetic", "config": config(args),
-            "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * layer_s, "higher_is_better": True,
+            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+            "dtype": "bf16 (CPU: e4m3 weights dequantized to bf16, bf16 matmuls)", "data": "synthetic",
+            "config": cfg,
+            "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": sample},
             "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def timed_region(graph, args, stream, pg, local):
+    """The timed region: a barrier and syncs on both sides, `steps` replays between CUDA events, clocks sampled;
+    returns (ms per step, max over ranks; clock summary)."""
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clocks:
+        torch.cuda.profiler.start()
+        ms = time_replays(graph, args.steps, stream)
+        torch.cuda.profiler.stop()
+    if pg:
+        t = torch.tensor([ms], device=stream.device)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms, clocks.summary()
+
+
+def ep_extras(kind, args, stream, pg, device, local_layers, mods, ids, weights, x, ms, outs):
+    """Beside the expert-parallel headline: each rank's decode alone (no exchange) and the NCCL all-gather exchange
+    of the same job, and the end-to-end rate through ExpertParallelDecode with host buffers."""
+    from drama3_b200 import ep
+    n_layers = args.layers
+    plain = [ep.ExpertParallelDecode(kind, banks, E) for banks in local_layers]
+    timed = {}
+    for name, fn in (("decode_only", lambda l_: plain[l_].partial(x, ids[l_], weights[l_])),
+                     ("nccl_all_gather", lambda l_: plain[l_](x, ids[l_], weights[l_]))):
+        def alt(fn=fn):
+            for l_ in range(n_layers):
+                outs[l_] = fn(l_)
+
+        with torch.cuda.stream(stream):
+            graph = capture(alt, args.warmup, stream)
+            pg.barrier()
+            t_ms = time_replays(graph, max(3, min(args.steps, 20)), stream)
+        del graph  # released before the process group is destroyed
+        t = torch.tensor([t_ms], device=device)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        timed[name] = {"ms_per_step": float(t.item()), "us_per_layer": 1e3 * float(t.item()) / n_layers,
+                       "tokens_per_s": args.lines / (float(t.item()) * 1e-3)}
+    timed["exchange_us_per_layer"] = 1e3 * (ms - timed["decode_only"]["ms_per_step"]) / n_layers
+    # end to end: host rows and routing in, the last layer's rows out, every step, eager
+    xh, idh, wh = x.cpu().pin_memory(), ids.cpu().pin_memory(), weights.cpu().pin_memory()
+    outh = torch.empty((args.lines, H), dtype=torch.bfloat16).pin_memory()
+    xd, idd, wd = torch.empty_like(x), torch.empty_like(ids), torch.empty_like(weights)
+    n_e2e = max(3, min(args.steps, 10))
+    with torch.cuda.stream(stream):
+        for it in range(n_e2e + 2):
+            if it == 2:
+                torch.cuda.synchronize()
+                pg.barrier()
+                es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                es.record(stream)
+            xd.copy_(xh, non_blocking=True)
+            idd.copy_(idh, non_blocking=True)
+            wd.copy_(wh, non_blocking=True)
+            for l_ in range(n_layers):
+                outs[l_] = mods[l_](xd, idd[l_], wd[l_])
+            outh.copy_(outs[-1], non_blocking=True)
+        ee.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([es.elapsed_time(ee) / n_e2e], device=device)
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    e2e = {"value": args.lines / (float(t.item()) * 1e-3), "unit": "tokens/s",
+           "h2d_bytes_per_step": xh.nbytes + idh.nbytes + wh.nbytes, "d2h_bytes_per_step": outh.nbytes,
+           "ms_per_step": float(t.item()),
+           "through": "drama3_b200.ep.ExpertParallelDecode (peer exchange), eager, every rank"}
+    return timed, e2e
 
 
 def main():
@@ -428,7 +749,8 @@ def main():
     ap.add_argument("--impl", choices=("mine", "reference"), default="mine")
     ap.add_argument("--lines", type=int, default=16)
     ap.add_argument("--layers", type=int, default=LAYERS, help="layers per step (48: the benchmark; 4: small case)")
-    ap.add_argument("--kind", choices=KINDS[:4], default="fp8c", help="expert layout of the headline decode")
+    ap.add_argument("--kind", choices=("fp8c", "fp8", "w4a8", "w6a8"), default="fp8c",
+                    help="expert layout of the headline decode")
     ap.add_argument("--no-extras", action="store_true", help="skip every leg but the headline")
     ap.add_argument("--prefill-only", action="store_true", help="print only the prompt-pass leg (BASELINE configs[3])")
     args = ap.parse_args()
@@ -438,7 +760,8 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        run_reference_arm(args, rank)
+        if rank == 0:
+            run_reference_arm(args, world)
         return
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
@@ -457,136 +780,122 @@ def main():
             print(json.dumps({"prefill": prefill_leg(device, args.steps)}), flush=True)
         return
     n_layers, kind = args.layers, args.kind
-    layers, ids, weights = make_layers(device, args.lines, kind, seed=4 + rank, n_layers=n_layers)
-    x = torch.randn((args.lines, H), generator=torch.Generator().manual_seed(7 + rank)).to(torch.bfloat16).to(device)
-    ws = kernels.decode_workspace(args.lines, K_TOP, I, device)
-    outs = torch.empty((n_layers, args.lines, H), dtype=torch.bfloat16, device=device)
     stream = torch.cuda.Stream(device)
-
-    def step(xin=x, ids_=ids, w_=weights, out_=outs):
-        for l_ in range(n_layers):
-            kernels.moe_decode(kind, xin, ids_[l_], w_[l_], layers[l_], workspace=ws, out=out_[l_])
-
-    with torch.cuda.stream(stream):
-        graph = capture(step, args.warmup, stream)
-        for _ in range(args.warmup):
-            graph.replay()
-        torch.cuda.synchronize()
-        if pg:
-            pg.barrier()
-        torch.cuda.synchronize()
-        with Clocks(local) as clocks:
-            torch.cuda.profiler.start()
-            ms = time_replays(graph, args.steps, stream)
-            torch.cuda.profiler.stop()
-        # the spread of single steps, after the timed region (this rank's)
-        try:
-            spread = replay_spread(graph, max(5, min(args.steps, 50)), stream)
-        except Exception as exc:  # the spread must not sink the bench line
-            spread = {"error": repr(exc)[:200]}
-    if pg:
-        t = torch.tensor([ms], device=device)
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        ms = float(t.item())
-    step_bytes = unique_bytes(ids, kind)
     hbm_peak, peak_kind = peaks()
-    achieved = step_bytes / (ms * 1e-3) / 1e9
-    value = world * args.lines / (ms * 1e-3)
-    del graph
-
     extras = {}
-    if world > 1 and not args.no_extras:
-        # expert parallelism (every rank): each rank holds 128 / N experts of one bank set, all ranks decode the same
-        # 16 lines, partials gathered and summed in rank order (ep.py); strong scaling of one job
-        extras["expert_parallel"] = ep_leg(kernels, device, kind, args, stream, pg)
-    if not args.no_extras and world == 1:
-        # the single-GPU legs (at N > 1 the other ranks would wait on them at the final barrier)
-        # one line decoded at a time (M = 1), same banks
-        extras["lines_1"] = decode_leg(kernels, device, kind, 1, args.steps, args.warmup, stream, n_layers,
-                                       (layers, ids[:, :1].contiguous(), weights[:, :1].contiguous()))
-        # end to end through the Python API: host inputs in, host output back, every step
-        xh = x.cpu().pin_memory()
-        idh, wh = ids.cpu().pin_memory(), weights.cpu().pin_memory()
-        outh = torch.empty((args.lines, H), dtype=torch.bfloat16).pin_memory()
-        xd, idd, wd = torch.empty_like(x), torch.empty_like(ids), torch.empty_like(weights)
-        n_e2e = max(3, min(args.steps, 20))
-        for it in range(n_e2e + 2):
-            if it == 2:
-                torch.cuda.synchronize()
-                t0 = time.perf_counter()
-                es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                es.record()
-            xd.copy_(xh, non_blocking=True)
-            idd.copy_(idh, non_blocking=True)
-            wd.copy_(wh, non_blocking=True)
-            step(xd, idd, wd, outs)
-            outh.copy_(outs[-1], non_blocking=True)
-        ee.record()
-        torch.cuda.synchronize()
-        ms_e2e = es.elapsed_time(ee) / n_e2e
-        extras["e2e"] = {"value": args.lines / (ms_e2e * 1e-3), "unit": "tokens/s",
-                         "h2d_bytes_per_step": xh.nbytes + idh.nbytes + wh.nbytes, "d2h_bytes_per_step": outh.nbytes,
-                         "ms_per_step": ms_e2e, "wall_ms_per_step": 1e3 * (time.perf_counter() - t0) / n_e2e}
+    spread = None
+    if world == 1:
+        layers, ids, weights = make_layers(device, args.lines, kind, seed=4, n_layers=n_layers)
+        x = torch.randn((args.lines, H), generator=torch.Generator().manual_seed(7)).to(torch.bfloat16).to(device)
+        ws = kernels.decode_workspace(args.lines, K_TOP, I, device)
+        outs = torch.empty((n_layers, args.lines, H), dtype=torch.bfloat16, device=device)
+
+        def step():
+            for l_ in range(n_layers):
+                kernels.moe_decode(kind, x, ids[l_], weights[l_], layers[l_], workspace=ws, out=outs[l_])
+
+        with torch.cuda.stream(stream):
+            graph = capture(step, args.warmup, stream)
+            ms, clocks = timed_region(graph, args, stream, pg, local)
+            try:
+                spread = replay_spread(graph, max(5, min(args.steps, 50)), stream)
+            except Exception as exc:  # the spread must not sink the bench line
+                spread = {"error": repr(exc)[:200]}
+        del graph
+        step_bytes = unique_bytes(ids, kind)
+        launches = n_layers * args.steps
+    else:
+        # expert parallelism: the headline at N > 1
+        from drama3_b200 import ep
+        local_layers, ids, weights, x = ep_setup(device, kind, args, rank, world)
+        peer = ep.PeerExchange(args.lines, H, device)
+        mods = [ep.ExpertParallelDecode(kind, banks, E, peer=peer) for banks in local_layers]
+        outs = [None] * n_layers
+
+        def step():
+            for l_ in range(n_layers):
+                outs[l_] = mods[l_](x, ids[l_], weights[l_])
+
+        with torch.cuda.stream(stream):
+            graph = capture(step, args.warmup, stream)
+            ms, clocks = timed_region(graph, args, stream, pg, local)
+        del graph
+        first, count = ep.expert_range(E, rank, world)
+        per, step_bytes = expert_bytes(kind), 0
+        for layer in ids.cpu():
+            step_bytes += len({v for v in layer.reshape(-1).tolist() if first <= v < first + count}) * per
+        launches = 2 * n_layers * args.steps  # the decode kernel and the reduce kernel per layer
+        if not args.no_extras:
+            extras["expert_parallel_detail"], extras["e2e"] = ep_extras(kind, args, stream, pg, device, local_layers,
+                                                                        mods, ids, weights, x, ms, outs)
+        peer.close()
+        del mods, local_layers
+        torch.cuda.empty_cache()
+        if not args.no_extras:
+            # replicas (weak scaling): each rank its own 16 lines, all 128 experts resident, no collective
+            rl = make_layers(device, args.lines, kind, seed=4 + rank, n_layers=n_layers)
+            rleg = decode_leg(kernels, device, kind, args.lines, max(3, min(args.steps, 20)), args.warmup, stream,
+                              n_layers, rl)
+            t = torch.tensor([rleg["ms_per_step"]], device=device)
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+            extras["replicas"] = {"tokens_per_s": world * args.lines / (float(t.item()) * 1e-3),
+                                  "ms_per_step": float(t.item()), "scaling": "weak (each rank its own lines)"}
+            del rl
+            torch.cuda.empty_cache()
+    value = args.lines / (ms * 1e-3)
+    achieved = step_bytes / (ms * 1e-3) / 1e9
+
+    if world == 1 and not args.no_extras:
+        # the headline layout at fewer lines (same banks): 1 and 4 lines (config 2's M)
+        for lines in (1, 4):
+            extras[f"lines_{lines}"] = decode_leg(kernels, device, kind, lines, args.steps, args.warmup, stream,
+                                                  n_layers, (layers, ids, weights))
+        extras["e2e"] = e2e_leg(device, layers, x, ids, weights, args.lines, args.steps)
         del layers
         torch.cuda.empty_cache()
-        # W4A8 at 16 and 1 lines
-        w4 = make_layers(device, args.lines, "w4a8", 5, n_layers)
-        extras["w4a8"] = {
-            "lines_16": decode_leg(kernels, device, "w4a8", args.lines, args.steps, args.warmup, stream, n_layers, w4),
-            "lines_1": decode_leg(kernels, device, "w4a8", 1, args.steps, args.warmup, stream, n_layers,
-                                  (w4[0], w4[1][:, :1].contiguous(), w4[2][:, :1].contiguous()))}
-        del w4
-        torch.cuda.empty_cache()
-        # the reference's fp8 layout, and the reference's own kernels on it, one row at a time
-        # (drama3/model.py:111-113), one CUDA graph per step
-        ref_layers = make_layers(device, args.lines, "fp8", 4, n_layers)
-        leg = decode_leg(kernels, device, "fp8", args.lines, args.steps, args.warmup, stream, n_layers, ref_layers)
+        # config 1: int8 ConvRot (the reference's layout) at 1 line (and 16), the reference's kernels beside
+        c1 = layout_legs(kernels, device, "int8", (1, 16), args, stream, n_layers, 10, reference=True)
+        c1["cpu_baseline"] = cpu_line(cpu_int8(n_layers))
+        extras["config1_int8"] = c1
+        # config 2: the reference's fp8 layout at 1, 4 and 16 lines, the reference's kernels beside
+        c2 = layout_legs(kernels, device, "fp8", (1, 4, 16), args, stream, n_layers, 4, reference=True)
+        c2["cpu_baseline_lines_1"] = cpu_line(cpu_fp8(1, n_layers, seconds=6.0, min_layers=3))
+        extras["config2_fp8_reference_layout"] = c2
+        # config 3: W4A8 (BASELINE layout) and the reference's W4 layout at 1 and 16 lines
+        extras["config3_w4a8"] = layout_legs(kernels, device, "w4a8", (1, 16), args, stream, n_layers, 5)
+        c3 = layout_legs(kernels, device, "w4", (1, 16), args, stream, n_layers, 6, reference=True)
+        c3["cpu_baseline_lines_1"] = cpu_line(cpu_codes("w4", 1, n_layers))
+        extras["config3_w4_reference_layout"] = c3
+        # config 4: the prompt pass on the tensor cores
         try:
-            from oracle import ref_gpu
-            if ref_gpu.available():
-                banks_r, ids_r, w_r = ref_layers
-
-                def ref_step():
-                    for l_ in range(n_layers):
-                        ref_gpu.lines_decode(x, ids_r[l_], w_r[l_], banks_r[l_], (2 * I, H), "fp8", (None, None))
-
-                with torch.cuda.stream(stream):
-                    gr = capture(ref_step, 2, stream)
-                    rms = time_replays(gr, max(3, min(args.steps, 10)), stream)
-                del gr
-                leg["reference_gpu"] = {"tokens_per_s": args.lines / (rms * 1e-3), "ms_per_step": rms,
-                                        "what": "reference kernels (drama3/kernels.py, nvcc sm_100) driven as "
-                                                "drama3/offload.py:108-117, one row at a time"}
-                leg["speedup_vs_reference_gpu"] = rms / leg["ms_per_step"]
-        except Exception as exc:  # the comparison leg must not sink the bench line
-            leg["reference_gpu"] = {"error": repr(exc)[:200]}
-        extras["fp8_reference_layout"] = leg
-        del ref_layers
-        torch.cuda.empty_cache()
-        # a prompt pass on the tensor cores (BASELINE configs[3] shape)
-        try:
-            extras["prefill"] = prefill_leg(device, args.steps)
+            extras["config4_prefill"] = prefill_leg(device, args.steps)
         except Exception as exc:
-            extras["prefill"] = {"error": repr(exc)[:200]}
-        # the reference's CPU path on the host cores (bounded sample)
-        tps, secs, threads, sample = cpu_reference(args.lines, n_layers=n_layers)
-        extras["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
-                                  "sample": sample, "seconds": secs}
+            extras["config4_prefill"] = {"error": repr(exc)[:200]}
+        # config 5's host-offload mode: 768-slot cache on one GPU
+        try:
+            extras["config5_slot_cache"] = slot_cache_leg(device, args, stream)
+        except Exception as exc:
+            extras["config5_slot_cache"] = {"error": repr(exc)[:300]}
+        # the reference's CPU path for the headline (block-scaled fp8: its only fp8 layout), 16 lines
+        extras["cpu_baseline"] = cpu_line(cpu_fp8(args.lines, n_layers))
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": kernel_of(kind, args.lines)[1],
-                "data": "synthetic (seeded random banks)", "config": config(args),
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": kernel_of(kind)[1],
+                "data": "synthetic (seeded random banks)", "config": config(args, world),
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                              "frac": achieved / hbm_peak, "peak_kind": peak_kind,
                              "traffic": TRAFFIC_RATIO * step_bytes / n_layers,
                              "traffic_unit": "bytes per launch", "traffic_source": TRAFFIC_SOURCE,
-                             "kernel": kernel_of(kind, args.lines)[0],
+                             "kernel": kernel_of(kind)[0],
                              "bytes_per_launch": step_bytes / n_layers, "us_per_layer": 1e3 * ms / n_layers,
-                             "launch_time": "step time / layers: the launches run back to back in one graph"},
-                "gpu_launches": n_layers * args.steps, "step_spread": spread,
-                "clocks": clocks.summary()}
+                             "launch_time": "step time / layers: the launches run back to back in one graph",
+                             "bytes_of": "rank 0's experts" if world > 1 else "all routed experts"},
+                "gpu_launches": launches, "step_spread": spread, "clocks": clocks}
+        for key in ("e2e", "cpu_baseline"):
+            if key in extras:
+                line[key] = extras.pop(key)
         line.update(extras)
         print(json.dumps(line), flush=True)
     if pg:

@@ -47,8 +47,8 @@ BASELINE_KINDS = ("fp8c", "w4a8", "w6a8")
 
 def pinned(tensor, pin):
     """tensor in page-locked host memory when `pin` (the kernels read it through its device address), else as is
-    (contiguous) (drama3/offload.py:54-58)."""
-    if not pin:
+    (contiguous) (drama3/offload.py:54-58). A tensor already page-locked and contiguous is kept, not copied."""
+    if not pin or (tensor.is_pinned() and tensor.is_contiguous()):
         return tensor.contiguous()
     return torch.empty(tensor.shape, dtype=tensor.dtype, pin_memory=True).copy_(tensor)
 

@@ -18,6 +18,9 @@ Cases:
   prefill_route  the prompt-routing expression of drama3/model.py:120-121, run through torch
   slotpool     offload.SlotPool host methods (use / free_slots / assign / claim / room) on a fixed call sequence,
                drama3/offload.py:689-722
+  config1      BASELINE config 1 (tests/config_data.py: seed 0, int8 ConvRot, one decode row) through the
+               reference's CPU int8 decode: the row rotated (hadamard) and rounded to bf16, experts_on_cpu over its
+               8 routed experts, the routing-weighted sum, bf16 (drama3/offload.py:170-189, 403-450)
 """
 import sys
 import types
@@ -164,12 +167,38 @@ def main(root):
     g["slot_score"], g["slot_at"] = pool.score.numpy(), pool.at.numpy()
     g["slot_clock"] = pool.clock.numpy()
 
+    # BASELINE config 1 through the reference's CPU int8 decode
+    import config_data as cd
+    d = cd.draw(1)
+    ids, wts = cd.routing(1, d)
+    packed = cd.pack("int8", d)
+
+    class ConfigBank:
+        cpu_linear = offload.QuantHostBank.cpu_linear
+
+        def __init__(self, fields):
+            self.num_experts = cd.E
+            self.fields = {"_qdata": fields["_qdata"], "scale": fields["scale"].view(-1, 1)}
+            self.scale_bf16 = fields["scale"].view(-1).to(torch.bfloat16)
+
+        def rows(self, name):
+            return self.fields[name].shape[0] // self.num_experts
+
+    rot = offload.hadamard(256)
+    row = (d["x"].float().view(1, -1, 256) @ rot).flatten(1).to(torch.bfloat16)
+    k = ids.shape[1]
+    with torch.no_grad():
+        parts = offload.experts_on_cpu((ConfigBank(packed[0]), ConfigBank(packed[1])), ids[0].tolist(), [1] * k,
+                                       row.expand(k, -1), rot)
+        g["c1_ref_cpu_out"] = (torch.from_numpy(wts[0]) @ parts).to(torch.bfloat16).float().numpy().reshape(1, -1)
+
     np.savez_compressed(OUT, **g)
     print(f"{OUT}: {OUT.stat().st_size} bytes, {len(g)} arrays")
 
 
 if __name__ == "__main__":
-    sys.path.insert(0, str(Path(__file__).resolve().parents[2]))
+    for path in ("", "comfyui-drama3_b200", "tests"):
+        sys.path.insert(0, str(Path(__file__).resolve().parents[2] / path))
     from oracle.build_ref import reference_root
     root = Path(sys.argv[1]) if len(sys.argv) > 1 else reference_root()
     if root is None:

@@ -22,3 +22,6 @@ def test_reference_arm_prints_the_contract_line():
     assert cpu["kind"] in ("port", "reference") and cpu["cores"] >= 1 and cpu["sample"] and cpu["value"] == line["value"]
     assert line["e2e"] == {"value": line["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                            "d2h_bytes_per_step": 0}
+    # each step is a bounded sample (one layer) that the line names, so steps x ms_per_step is the time it ran
+    assert line["config"]["sample_layers_per_step"] == 1 and "block scales" in line["config"]["format"]
+    assert abs(line["value"] - 16 / (48 * line["ms_per_step"] * 1e-3)) <= 1e-6 * line["value"]
