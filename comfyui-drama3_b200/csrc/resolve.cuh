@@ -23,10 +23,10 @@
 //      owner leaves the table. A miss finding no candidate reads host memory without a slot (plan slot -1).
 // Design: a claimed slot becomes a non-candidate and no other slot's value changes, so the claims of one call take
 // the m lowest (value, slot) candidates in ascending order. Each slot's (value, slot) pair is packed into one
-// ordered 64-bit key, and the block extracts the m smallest keys by m rounds of "smallest key above the last one"
-// (warp shuffles, one shared atomicMin per warp, one barrier per round); the claims are then committed in parallel
-// (they touch distinct slots and keys). The ranking of step 2 is one warp's: lane e holds expert e and counts the
-// lanes ahead of it.
+// ordered 64-bit key, and the block extracts the m smallest keys by m rounds of "smallest key above the last one":
+// per round a warp minimum, the warps' minima through shared memory, warp 0's minimum of those (two barriers, the
+// same m rounds in every thread, no atomics); the claims are then committed in parallel (they touch distinct slots
+// and keys). The ranking of step 2 is one warp's: lane e holds expert e and counts the lanes ahead of it.
 // plan[2e] = slot, plan[2e+1] = 0 cached, 1 read from host memory (and fill plan slot when >= 0), 2 left to the CPU.
 // Expert ids outside [0, experts) are misses without a slot (code 1, never claiming) and set the fault word.
 #pragma once
@@ -72,6 +72,7 @@ __global__ void __launch_bounds__(RESOLVE_THREADS)
                    float* score, int* at, int* pending, int count, int* clock, int* budget, int* plan, int* reads,
                    int* step, const float* share, double half_life, int cpu, double admit) {
   __shared__ unsigned long long picked[RESOLVE_MAX_K];  // the m smallest candidate keys, ascending
+  __shared__ unsigned long long warp_best[RESOLVE_THREADS / 32];
   __shared__ int now_s, claims_s;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float log2_decay = -1.0f / ((float)half_life * layers);
@@ -117,8 +118,9 @@ __global__ void __launch_bounds__(RESOLVE_THREADS)
     // reservations: the most used CPU experts keep theirs while the step's and the layer's budgets last
     const bool asks = mine && code == 3;
     const int order = use_rank(use, asks, lane);
-    const int allowed = (lane == 0 && cpu) ? min(budget[0], budget[1]) : 0;
-    const bool keeps = asks && order < __shfl_sync(0xffffffffu, allowed, 0);
+    // every lane takes the shuffle (a full-mask shuffle behind a short-circuit would leave lanes out of it)
+    const int allowed = __shfl_sync(0xffffffffu, (lane == 0 && cpu) ? min(budget[0], budget[1]) : 0, 0);
+    const bool keeps = asks && order < allowed;
     if (asks && !keeps) code = 2;
     const int kept = __popc(__ballot_sync(0xffffffffu, keeps));
     const int hits = __popc(__ballot_sync(0xffffffffu, mine && code == 0));
@@ -143,9 +145,9 @@ __global__ void __launch_bounds__(RESOLVE_THREADS)
   // ---- the whole block: the m smallest candidate keys (rule 3)
   const int now = now_s, m = claims_s;
   unsigned long long above = 0;  // every key taken so far is <= above; keys are unique (the slot is in them)
-  for (int r = 0; r < m; r++) {
+  for (int r = 0; r < m; r++) {  // m is the same in every thread (read after a barrier), and so is every round
     unsigned long long best = RESOLVE_NO_SLOT;
-    for (int i = tid; i < count; i += RESOLVE_THREADS) {
+    for (int i = tid; i < count && above != RESOLVE_NO_SLOT; i += RESOLVE_THREADS) {
       const int holder = owner[i];
       float value;
       if (holder < 0) {
@@ -160,10 +162,16 @@ __global__ void __launch_bounds__(RESOLVE_THREADS)
       if ((r == 0 || cand > above) && cand < best) best = cand;
     }
     best = warp_min_u64(best);
-    if (lane == 0 && best != RESOLVE_NO_SLOT) atomicMin(&picked[r], best);
+    if (lane == 0) warp_best[warp] = best;
     __syncthreads();
+    if (warp == 0) {
+      const unsigned long long v = warp_min_u64(warp_best[lane]);
+      if (lane == 0) picked[r] = v;
+    }
+    __syncthreads();
+    // NO_SLOT: no candidates left, and none in the later rounds (their scans are skipped): those claimers go
+    // without a slot
     above = picked[r];
-    if (above == RESOLVE_NO_SLOT) break;  // no candidates left: the remaining claimers go without a slot
   }
   // ---- commit (warp 0): distinct slots, distinct keys
   if (warp == 0 && lane < k) {

@@ -603,10 +603,12 @@ class SlotPool:
 
 
 def _unsort_weighted_sum(sorted_out, order, weights, num_tokens, top_k):
-    """Pair outputs in expert order back in (token, rank) order, each times its routing weight (stored in
-    sorted_out's dtype), summed over a token's k pairs (drama3/offload.py:146-149, 461-466)."""
-    out = torch.empty_like(sorted_out)
-    out[order] = sorted_out * weights.reshape(-1)[order].unsqueeze(1)
+    """Pair outputs in expert order back in (token, rank) order, each times its routing weight, summed over a token's
+    k pairs (drama3/offload.py:146-149, 461-466); in the dtype of the products (bf16 for bf16 outputs and weights,
+    as the reference's model passes them)."""
+    weighted = sorted_out * weights.reshape(-1)[order].unsqueeze(1)
+    out = torch.empty_like(weighted)
+    out[order] = weighted
     return out.view(num_tokens, top_k, -1).sum(dim=1)
 
 
