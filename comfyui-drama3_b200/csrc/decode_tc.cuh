@@ -17,7 +17,9 @@
 // columns; B holds the segment's pairs' a1 rows (N = 16 pairs x 4 terms), two segments' worth. The work of each phase
 // is split across the grid by whole tiles, in proportion, so a CTA's phase-2 segments are mostly its own phase-1 ones.
 // Between the phases no grid-wide wait: a segment's phase-2 staging waits (bounded) for the count of its finished
-// phase-1 tiles. The combine follows a grid barrier, each CTA taking an even share of the columns.
+// phase-1 tiles. With many segments the combine follows a grid barrier, each CTA taking an even share of the columns;
+// with few (one or two lines: DecodeArgs::lastarrive_nseg) each 128-row block is combined by the CTA whose phase-2
+// tile completes it, and no CTA waits for the others.
 //
 // Roles (8 warps): warp 0 lane 0 issues the TMA loads, warp 1 owns TMEM and lane 0 issues the MMAs, warps 2-5 are
 // the TMEM epilogue (one warp per lane quarter), warps 2-7 stage the B operands and run the combine.
@@ -231,6 +233,59 @@ D3_DEV void tc_plan(DecodePlan& pl, int* ecnt, int* ebase, int* esegb, long long
   __syncthreads();
 }
 
+// Raise this rank's flag for the current call on every rank of the exchange (after its partial is pushed).
+D3_DEV void tc_raise_flags(const EpExchange& ex) {
+  const unsigned ep = *(volatile const unsigned*)ex.epoch + 1u;
+  __threadfence_system();
+  for (int r = 0; r < ex.world; ++r) {
+    unsigned* f = ex.flags[r] + (ep & 1u) * EP_MAX_RANKS + ex.rank;
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(ep) : "memory");
+  }
+}
+
+// Combine by last arrival (few segments): once a phase-2 tile's parts rows are written, the epilogue threads (TC_EPI,
+// from TC_HELP0) count the tile for its 128-row block; the tile that completes the block (one per segment) combines
+// those rows, with the same arithmetic as the grid-wide combine, so the output is the same bit for bit. With the
+// peer exchange, the block's rows go to every rank, and the block that completes all H / 128 raises the flags.
+// Counters: a.blocks[rb] (reset by the block's combiner) and a.ep_done (reset by the flag raiser).
+D3_DEV void tc_block_done(const DecodeArgs& a, const unsigned char* c_ok, const float* c_w, int rb, int nseg,
+                          bool ok) {
+  __shared__ int s_last;
+  named_sync(3, TC_EPI);
+  if (threadIdx.x == TC_HELP0) {
+    __threadfence();
+    s_last = atomicAdd(a.blocks + rb, 1u) + 1u == (unsigned)nseg;
+  }
+  named_sync(3, TC_EPI);
+  if (!s_last) return;  // the same value in every participant
+  __threadfence();
+  combine_columns(a, c_ok, c_w, rb * TC_R2, rb * TC_R2 + TC_R2, ok, TC_HELP0, TC_EPI);
+  named_sync(3, TC_EPI);
+  if (threadIdx.x == TC_HELP0) {
+    a.blocks[rb] = 0u;  // every tile of the block has counted: nothing adds to it again in this call
+    if (a.ex && ep_geometry_ok(*a.ex, a.M, DEC_H)) {
+      __threadfence_system();
+      if (atomicAdd(a.ep_done, 1u) + 1u == (unsigned)(DEC_H / TC_R2)) {
+        tc_raise_flags(*a.ex);
+        *a.ep_done = 0u;
+      }
+    }
+  }
+}
+
+// Combine by last arrival: every helper of this CTA is past its staging waits and combines; the last CTA to get
+// here clears the segment counters (a.arrive) and this count (a.depart[0]) for the next call.
+D3_DEV void tc_exit_count(const DecodeArgs& a, int nseg, int G) {
+  named_sync(1, TC_HELPERS);
+  if (threadIdx.x == TC_HELP0) {
+    __threadfence();
+    if (atomicAdd(a.depart, 1u) + 1u == (unsigned)G) {
+      for (int s = 0; s < nseg; ++s) a.arrive[s] = 0u;
+      a.depart[0] = 0u;
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 template <bool XBF, int NKB2>
 __global__ void __launch_bounds__(TC_THREADS, 1)
@@ -391,6 +446,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   // phase-2 segments of this CTA: at most two (its range is at most TPS2 tiles when nseg <= G, which the host checks)
   const int s2a = t2_lo / TPS2, s2n = t2_hi > t2_lo ? (t2_hi - 1) / TPS2 - s2a + 1 : 0;
   bool ok = true;
+  // few segments: each 128-row block is combined by its last-arriving phase-2 tile (no grid barrier)
+  const bool last_arrive = nseg <= a.lastarrive_nseg;
   if (tid == 0) TC_STAMP(1);
 
   if (warp == 0) {
@@ -653,8 +710,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
           }
         }
+        if (last_arrive) tc_block_done(a, c_ok, c_w, rb, nseg, ok);
       }
     }
+    if (last_arrive) {
+      // the row blocks were combined by their last tiles; the last CTA out clears the counters for the next call
+      if (tid == TC_HELP0) TC_STAMP(9);
+      tc_exit_count(a, nseg, G);
+    } else {
     // every CTA's parts are written; each CTA combines an even share of the columns
     if (tid == TC_HELP0) TC_STAMP(9);
     ok = grid_barrier<TC_HELPERS, TC_HELP0>(a.barrier, G) && ok;
@@ -671,17 +734,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (tid == TC_HELP0 && ep_geometry_ok(*a.ex, a.M, H)) {
         __threadfence_system();
         if (atomicAdd(a.ep_done, 1u) + 1u == (unsigned)G) {
-          const EpExchange& ex = *a.ex;
-          const unsigned ep = *(volatile const unsigned*)ex.epoch + 1u;
-          __threadfence_system();
-          for (int r = 0; r < ex.world; ++r) {
-            unsigned* f = ex.flags[r] + (ep & 1u) * EP_MAX_RANKS + ex.rank;
-            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(ep) : "memory");
-          }
+          tc_raise_flags(*a.ex);
           *a.ep_done = 0u;
         }
       }
     }
+    }  // grid-barrier combine
   }
   tc_fence_before();
   __syncthreads();

@@ -212,6 +212,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const int s2a = t2_lo / TPS2, s2n = t2_hi > t2_lo ? (t2_hi - 1) / TPS2 - s2a + 1 : 0;
   const int nkb = (t1_hi - t1_lo) * NKB1 + (t2_hi - t2_lo) * NKB2;  // this CTA's 128-column groups, both phases
   bool ok = true;
+  // few segments: each 128-row block is combined by its last-arriving phase-2 tile (no grid barrier)
+  const bool last_arrive = nseg <= a.lastarrive_nseg;
 
   if (warp == 0) {
     // ---------------- TMA producer: packed rows ----------------
@@ -477,8 +479,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           for (int j = 0; j < TC_CAP; ++j)
             if (j < cnt) __stcg(a.parts + (size_t)spair[bb * TC_CAP + j] * H + r, acc[j] * sinv[bb * TC_CAP + j]);
         }
+        if (last_arrive) tc_block_done(a, c_ok, c_w, rb, nseg, ok);
       }
     }
+    if (last_arrive) {
+      // the row blocks were combined by their last tiles; the last CTA out clears the counters for the next call
+      tc_exit_count(a, nseg, G);
+    } else {
     // every CTA's parts are written; each CTA combines an even share of the columns
     ok = grid_barrier<TC_HELPERS, TC_HELP0>(a.barrier, G) && ok;
     if (blockIdx.x == 0)
@@ -492,17 +499,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (tid == TC_HELP0 && ep_geometry_ok(*a.ex, a.M, H)) {
         __threadfence_system();
         if (atomicAdd(a.ep_done, 1u) + 1u == (unsigned)G) {
-          const EpExchange& ex = *a.ex;
-          const unsigned ep = *(volatile const unsigned*)ex.epoch + 1u;
-          __threadfence_system();
-          for (int r = 0; r < ex.world; ++r) {
-            unsigned* f = ex.flags[r] + (ep & 1u) * EP_MAX_RANKS + ex.rank;
-            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(ep) : "memory");
-          }
+          tc_raise_flags(*a.ex);
           *a.ep_done = 0u;
         }
       }
     }
+    }  // grid-barrier combine
   }
   tc_fence_before();
   __syncthreads();

@@ -463,6 +463,13 @@ static bool decode_tc_enabled() {
   return !(v && v[0] == '0');
 }
 
+// Segment counts up to which the tensor-core decodes combine each 128-row block as soon as its last tile is done;
+// above it they combine after a grid barrier. D3_LASTARRIVE_NSEG sets it (default 0: always the grid barrier).
+static int lastarrive_nseg() {
+  const char* v = getenv("D3_LASTARRIVE_NSEG");
+  return v ? atoi(v) : 0;
+}
+
 static int decode_tc_min_lines() {
   const char* v = getenv("D3_DECODE_TC_MIN");
   return v ? atoi(v) : 1;
@@ -555,7 +562,7 @@ static int decode_common(int fmt, const void* x, int x_bf16, int M, int k, int E
   const int cap = cap_for(M);
   d3::DecodeArgs a = {x, x_bf16, ids, weights, M, k, E, H, I, w13, s13, c13, codebook13, w2, s2, c2, codebook2,
                       out, out_f32, e_first, e_count, (const d3::EpExchange*)exchange, words + 4, a1, parts, barrier,
-                      words + 16, words + 128, words + 384, 0, 0, cap};
+                      words + 16, words + 128, words + 384, 0, 0, cap, lastarrive_nseg()};
   cudaStream_t s = (cudaStream_t)stream;
   // per-channel e4m3: the tensor-core kernel (its phase-2 split needs one CTA per segment at least: at most
   // M * k <= 128 segments)

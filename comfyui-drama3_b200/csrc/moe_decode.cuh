@@ -431,6 +431,8 @@ struct DecodeArgs {
   unsigned* arrive;             // scratch [DEC_MAX_GRID]: group-barrier counters, zero between calls
   unsigned* depart;             // scratch [DEC_MAX_GRID]
   int stages, stage_bytes, cap;
+  int lastarrive_nseg;          // tensor-core decodes: at most this many segments combine per 128-row block by the
+                                // block's last-arriving tile instead of after a grid barrier
 };
 
 constexpr int DEC_CB = 64;          // columns per combine block

@@ -103,3 +103,28 @@ def test_tc_decode_expert_parallel_partials(cuda, monkeypatch, kind):
     kernels.moe_decode_ep(kind, x, ids, w, full, 0, E, exchange=st)
     whole = kernels.moe_decode_ep(kind, x, ids, w, full, 0, E)
     assert torch.equal(kernels.ep_reduce(st, M, H), whole.to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("kind", ["fp8c", "w4a8"])
+def test_last_arrival_combine_equals_grid_combine(cuda, monkeypatch, kind):
+    """With few segments (one or two lines) each 128-row block is combined by the tile that completes it instead of
+    after a grid barrier (D3_LASTARRIVE_NSEG: 0 forces the grid barrier). Same arithmetic, so the outputs agree bit
+    for bit, over repeated calls (the block and exit counters reset themselves), for the plain decode and for an
+    expert-parallel partial."""
+    E = 128
+    banks = (gd.rand_bank(kind, E, 1536, H, 400, cuda), gd.rand_bank(kind, E, H, 768, 401, cuda))
+    _lib.take_fault()
+    for call, M in enumerate((1, 2, 1, 1, 2)):
+        x = gd.rand_rows(M, H, 410 + call, cuda)
+        ids, w = gd.rand_routing(M, E, 8, 420 + call, cuda)
+        monkeypatch.setenv("D3_LASTARRIVE_NSEG", "16")
+        fast = kernels.moe_decode(kind, x, ids, w, banks)
+        part_fast = kernels.moe_decode_ep(kind, x, ids, w, ep.local_banks(banks, E, 0, 2), 0, E)
+        monkeypatch.setenv("D3_LASTARRIVE_NSEG", "0")
+        slow = kernels.moe_decode(kind, x, ids, w, banks)
+        part_slow = kernels.moe_decode_ep(kind, x, ids, w, ep.local_banks(banks, E, 0, 2), 0, E)
+        monkeypatch.delenv("D3_LASTARRIVE_NSEG")
+        torch.cuda.synchronize()
+        assert torch.equal(fast, slow), (kind, call, M)
+        assert torch.equal(part_fast, part_slow), (kind, call, M)
+    assert _lib.take_fault() == 0
