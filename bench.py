@@ -23,7 +23,8 @@ Extras at N = 1, one per BASELINE configuration (each with its roofline fraction
 its CPU path timed on the host cores): config 1 (int8 ConvRot, 1 line, and the reference's CPU int8 path); config 2
 (fp8 block scales at 1, 4 and 16 lines with the reference's own kernels beside them, fp8c at 1 and 4 lines);
 config 3 (W4A8 and the reference's W4 layout at 1 and 16 lines); config 4 (the 2048-row Zipf-skewed prompt pass);
-config 5's host-offload slot-cache mode (768 slots on one GPU: hit rate, PCIe GB/s, tokens/s); the end-to-end rate
+config 5 (the whole 48-layer decoder step: attention over a 4096-token KV cache, router and MoE) and its host-offload
+slot-cache mode (768 slots on one GPU: hit rate, PCIe GB/s, tokens/s); the end-to-end rate
 through the drop-in module (FP8Experts) with host buffers in and out. `--impl reference` runs the reference's CPU
 decode (rank 0) and prints its line.
 """
@@ -462,6 +463,80 @@ def slot_cache_leg(device, args, stream, slots_per_layer=16, n_routings=8, seed=
                     "zero-copy, filling the slot) + SwiGLU + gemv_fp8 + weighted_sum per layer and row, one graph"}
 
 
+def full_stack_leg(kernels, device, args, stream, ctx=4096, q_heads=32, kv_heads=4, head_dim=128, seed=44):
+    """the whole 48-layer decoder step of `lines` lines, each layer RMSNorm -> attention (QKV
+    projection, 32 query / 4 KV heads of 128 over a 4096-token bf16 KV cache per line, the step's K / V written at
+    its position, output projection) -> residual -> RMSNorm -> router (bf16 GEMV, then the route kernel) -> the fused
+    MoE decode (fp8c) -> residual. Random-init weights from seed 44, one CUDA graph per step. The attention, the
+    projections and the norms are torch (cuBLAS / SDPA): library calls around this library's MoE path; RoPE is left
+    out (it moves no bytes that matter). Reports tokens/s and the HBM fraction of the step's bytes (routed experts,
+    KV cache, attention and router weights)."""
+    n_layers, lines = args.layers, args.lines
+    hbm_peak, _ = peaks()
+    gen = torch.Generator(device=device).manual_seed(seed)
+    qkv_rows = (q_heads + 2 * kv_heads) * head_dim
+
+    def randn(*shape, std=0.02):
+        return (torch.randn(shape, generator=gen, device=device) * std).to(torch.bfloat16)
+
+    layers = []
+    for _ in range(n_layers):
+        layers.append({
+            "n1": torch.ones((H,), dtype=torch.bfloat16, device=device), "n2": torch.ones((H,), dtype=torch.bfloat16,
+                                                                                            device=device),
+            "wqkv": randn(qkv_rows, H), "wo": randn(H, q_heads * head_dim), "router": randn(E, H),
+            "k": randn(lines, kv_heads, ctx, head_dim, std=1.0), "v": randn(lines, kv_heads, ctx, head_dim, std=1.0),
+            "banks": tuple(rand_bank("fp8c", n, k, gen, device) for n, k in ((2 * I, H), (H, I)))})
+    x = torch.randn((lines, H), generator=torch.Generator().manual_seed(7)).to(torch.bfloat16).to(device)
+    h = torch.empty_like(x)
+    ws = kernels.decode_workspace(lines, K_TOP, I, device)
+    moe_out = torch.empty((lines, H), dtype=torch.bfloat16, device=device)
+    ids_seen = []
+
+    def rmsnorm(t, w):
+        tf = t.float()
+        return (tf * torch.rsqrt(tf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16) * w
+
+    def step(record=False):
+        h.copy_(x)
+        for lay in layers:
+            a = rmsnorm(h, lay["n1"])
+            qkv = a @ lay["wqkv"].T
+            # query head h reads KV head h // (q_heads / kv_heads): a KV head's query heads act as its query rows
+            q = qkv[:, :q_heads * head_dim].view(lines, kv_heads, q_heads // kv_heads, head_dim)
+            kv = qkv[:, q_heads * head_dim:].view(lines, 2, kv_heads, 1, head_dim)
+            lay["k"][:, :, ctx - 1:ctx].copy_(kv[:, 0])
+            lay["v"][:, :, ctx - 1:ctx].copy_(kv[:, 1])
+            o = torch.nn.functional.scaled_dot_product_attention(q, lay["k"], lay["v"])
+            h.add_(o.reshape(lines, q_heads * head_dim) @ lay["wo"].T)
+            m = rmsnorm(h, lay["n2"])
+            ids, w = kernels.route(m @ lay["router"].T, K_TOP)
+            if record:
+                ids_seen.append(ids)
+            kernels.moe_decode("fp8c", m, ids, w, lay["banks"], workspace=ws, out=moe_out)
+            h.add_(moe_out)
+
+    with torch.cuda.stream(stream):
+        step(record=True)
+        torch.cuda.synchronize()
+        graph = capture(step, 2, stream)
+        ms = time_replays(graph, max(3, min(args.steps, 20)), stream)
+    del graph
+    expert_b = unique_bytes(torch.stack(ids_seen), "fp8c", rows_bytes=False)
+    kv_b = n_layers * 2 * lines * kv_heads * ctx * head_dim * 2
+    weight_b = n_layers * (qkv_rows * H + H * q_heads * head_dim + E * H) * 2
+    step_b = expert_b + kv_b + weight_b
+    gbs = step_b / (ms * 1e-3) / 1e9
+    del layers
+    torch.cuda.empty_cache()
+    return {"tokens_per_s": lines / (ms * 1e-3), "ms_per_step": ms, "us_per_layer": 1e3 * ms / n_layers,
+            "lines": lines, "layers": n_layers, "context": ctx, "bytes_per_step": step_b,
+            "expert_bytes_per_step": expert_b, "kv_bytes_per_step": kv_b, "attention_router_weight_bytes": weight_b,
+            "hbm_gbs": gbs, "frac": gbs / hbm_peak,
+            "what": "RMSNorm, QKV / O projections (cuBLAS bf16), GQA attention over the KV cache (torch SDPA), "
+                    "router GEMV (cuBLAS) + route kernel, fused MoE decode (moe_decode_tc_kernel), one graph"}
+
+
 # ---- CPU baselines: the reference's CPU paths (oracle/cpu_port.py), bounded samples on the host cores
 def cpu_fp8(lines, n_layers=LAYERS, seed=4, seconds=10.0, min_layers=2):
     """The reference's CPU decode for fp8 experts (the FP8Experts CPU forward, block-scaled layout: the reference
@@ -871,6 +946,11 @@ def main():
             extras["config4_prefill"] = prefill_leg(device, args.steps)
         except Exception as exc:
             extras["config4_prefill"] = {"error": repr(exc)[:200]}
+        # config 5: the whole decoder step (attention + MoE), 48 layers
+        try:
+            extras["config5_full_stack"] = full_stack_leg(kernels, device, args, stream)
+        except Exception as exc:
+            extras["config5_full_stack"] = {"error": repr(exc)[:300]}
         # config 5's host-offload mode: 768-slot cache on one GPU
         try:
             extras["config5_slot_cache"] = slot_cache_leg(device, args, stream)
