@@ -83,6 +83,29 @@ D3_DEV void umma_f8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t id
       : "memory");
 }
 
+// Instruction descriptor, kind::i8: s32 accumulator, signed 8-bit A and B, both K-major, M = 128, N = n.
+D3_DEV uint32_t t8_idesc(int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+D3_DEV void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// One MMA of the tensor-core decode: kind::i8 (s32 accumulators) for int8 rows, kind::f8f6f4 (f32) for e4m3 rows.
+template <bool I8>
+D3_DEV void tc_umma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  if constexpr (I8)
+    umma_i8(tmem_d, adesc, bdesc, idesc, accumulate);
+  else
+    umma_f8(tmem_d, adesc, bdesc, idesc, accumulate);
+}
+
 // 2-D tiled TMA load with an L2 cache hint.
 D3_DEV void tma_load_2d_hint(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar, uint64_t policy) {
   asm volatile(
@@ -143,6 +166,78 @@ D3_DEV void tc_write_terms(uint8_t* b, int rows, int n, int tstride, int q, cons
     }
     *reinterpret_cast<uint4*>(b + tc_b_offset(rows, t * tstride + n, q)) = make_uint4(w[0], w[1], w[2], w[3]);
   }
+}
+
+// ConvRot rotation of 256-column groups held 16 contiguous values a lane: lane L (of a 16-lane group, L = lane % 16)
+// holds the group's columns 16 L .. 16 L + 15. H256 = h4 (x) h4 (x) h4 (x) h4 / 16 acts on the four base-4 digits of
+// the column index: the two low ones inside the lane, the two high ones across lanes. One radix-4 stage of h4
+// (rows [1,1,1,-1], [1,1,-1,1], [1,-1,1,1], [-1,1,1,1]) gives output p = (sum of the four inputs) - 2 x input 3 - p.
+// The stages run in the reference's order (digit 0 first); float results agree with it to rounding.
+D3_DEV void tc_h4_regs(float (&v)[16], int base, int stride) {
+  const float a = v[base], b = v[base + stride], c = v[base + 2 * stride], d = v[base + 3 * stride];
+  const float s = (a + b) + (c + d);
+  v[base] = s - 2.0f * d;
+  v[base + stride] = s - 2.0f * c;
+  v[base + 2 * stride] = s - 2.0f * b;
+  v[base + 3 * stride] = s - 2.0f * a;
+}
+
+D3_DEV float tc_h4_lanes(float v, int x1, int x2, int mirror) {
+  float s = v + __shfl_xor_sync(0xffffffffu, v, x1);
+  s += __shfl_xor_sync(0xffffffffu, s, x2);
+  return s - 2.0f * __shfl_xor_sync(0xffffffffu, v, mirror);
+}
+
+// The whole warp calls it (shuffles); each 16-lane half rotates its own group.
+D3_DEV void tc_rotate16(float (&v)[16]) {
+#pragma unroll
+  for (int b = 0; b < 16; b += 4) tc_h4_regs(v, b, 1);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) tc_h4_regs(v, i, 4);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = tc_h4_lanes(v[i], 1, 2, 3);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = 0.0625f * tc_h4_lanes(v[i], 4, 8, 12);
+}
+
+// Power-of-two scale for int8 terms: m * 2^e in [32, 64) (1 for an all-zero row).
+D3_DEV int tc_exponent_i8(float m) {
+  if (!(m > 0.0f) || !(m < 3.0e38f)) return 0;
+  const int ex = (int)((__float_as_uint(m) >> 23) & 0xFF) - 127;
+  return min(100, max(-100, 5 - ex));
+}
+
+// 16 consecutive values of a row as three int8 terms of y = v * scale (|y| < 64): t1 = rint(y), t2 = rint(128 (y -
+// t1)), t3 = rint(128 (128 (y - t1) - t2)), so y = t1 + t2 / 128 + t3 / 16384 to within 2^-15; term t of the row goes
+// to B row t * tstride + n as 16-byte chunks of a K-major, 128-byte-swizzled operand.
+D3_DEV void tc_write_i8_terms(uint8_t* b, int rows, int n, int tstride, int q, const float (&v)[16], float scale) {
+  uint32_t w[3][4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    uint32_t t1w = 0u, t2w = 0u, t3w = 0u;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float y = v[4 * p + i] * scale;
+      const float t1 = rintf(y);
+      const float r1 = (y - t1) * 128.0f;
+      const float t2 = rintf(r1);
+      const float t3 = fminf(127.0f, fmaxf(-127.0f, rintf((r1 - t2) * 128.0f)));
+      t1w |= ((uint32_t)(int)t1 & 0xFFu) << (8 * i);
+      t2w |= ((uint32_t)(int)t2 & 0xFFu) << (8 * i);
+      t3w |= ((uint32_t)(int)t3 & 0xFFu) << (8 * i);
+    }
+    w[0][p] = t1w;
+    w[1][p] = t2w;
+    w[2][p] = t3w;
+  }
+#pragma unroll
+  for (int t = 0; t < 3; ++t)
+    *reinterpret_cast<uint4*>(b + tc_b_offset(rows, t * tstride + n, q)) = make_uint4(w[t][0], w[t][1], w[t][2], w[t][3]);
+}
+
+// The s32 accumulators of three int8 terms as one float: D1 + D2 / 128 + D3 / 16384 (each |D| < 2^24: exact).
+D3_DEV float tc_i8_sum(uint32_t d1, uint32_t d2, uint32_t d3) {
+  return (float)(int)d1 + (float)(int)d2 * 0.0078125f + (float)(int)d3 * 6.103515625e-05f;
 }
 
 D3_DEV void tc_load16(const void* src, bool bf16, size_t i, float (&v)[16]) {
@@ -287,16 +382,21 @@ D3_DEV void tc_exit_count(const DecodeArgs& a, int nseg, int G) {
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-template <bool XBF, int NKB2>
+// FMT: FMT_FP8C (e4m3 rows, kind::f8f6f4, e4m3 activation terms) or FMT_I8 (int8 ConvRot rows, kind::i8: the
+// activation rows rotated while staged and written as three int8 terms, s32 accumulators).
+template <int FMT, bool XBF, int NKB2>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     moe_decode_tc_kernel(const __grid_constant__ CUtensorMap map13, const __grid_constant__ CUtensorMap map2,
                          const DecodeArgs a) {
-  constexpr int T1 = XBF ? 2 : 3;           // phase-1 terms
+  constexpr bool I8 = FMT == FMT_I8;
+  constexpr int T1 = I8 ? 3 : XBF ? 2 : 3;  // phase-1 terms
   constexpr int N1 = TC_LINES * T1;         // 32 / 48
+  constexpr int T2 = I8 ? 3 : TC_TERMS2;    // phase-2 terms
+  constexpr int N2 = TC_CAP * T2;           // 48 / 64
   constexpr int H = DEC_H, NKB1 = H / 128;  // 16 column blocks in phase 1
   constexpr int I = NKB2 * 128;
   constexpr int TPS1 = I / TC_U1, TPS2 = H / TC_R2;
-  constexpr int B2BYTES = TC_N2 * I;        // one phase-2 B buffer
+  constexpr int B2BYTES = N2 * I;           // one phase-2 B buffer
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -413,12 +513,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
           for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(v[u][i]));
         }
+        if constexpr (I8) {
+          // ConvRot: the row in the weights' rotated basis (lanes 16h .. 16h + 15 hold group 2u + h), then its max
+          m = 0.0f;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            tc_rotate16(v[u]);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(v[u][i]));
+          }
+        }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        const int e = tc_exponent(m);
+        const int e = I8 ? tc_exponent_i8(m) : tc_exponent(m);
         const float scale = __uint_as_float((uint32_t)(e + 127) << 23);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) tc_write_terms<T1>(breg, N1, n, TC_LINES, lane + 32 * u, v[u], scale);
+        for (int u = 0; u < 4; ++u) {
+          if constexpr (I8)
+            tc_write_i8_terms(breg, N1, n, TC_LINES, lane + 32 * u, v[u], scale);
+          else
+            tc_write_terms<T1>(breg, N1, n, TC_LINES, lane + 32 * u, v[u], scale);
+        }
         if (lane == 0) linv[n] = __uint_as_float((uint32_t)(127 - e) << 23);
       }
       fence_async_smem();
@@ -494,7 +609,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       const uint32_t ring_s = smem_u32(ring), b_s = smem_u32(breg);
-      const uint32_t id1 = tc_idesc(N1), id2 = tc_idesc(TC_N2);
+      const uint32_t id1 = I8 ? t8_idesc(N1) : tc_idesc(N1), id2 = I8 ? t8_idesc(N2) : tc_idesc(N2);
       int c = 0, tn = 0;
       if (t1_hi > t1_lo) ok = mbar_wait(b1_full, 0);
       TC_STAMP(3);
@@ -516,8 +631,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           tc_fence_after();
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks)
-            umma_f8(d, umma_desc_sw128(ring_s + st * TC_ABYTES + 32 * ks),
-                    umma_desc_sw128(b_s + kb * N1 * 128 + 32 * ks), id1, (kb | ks) != 0 ? 1u : 0u);
+            tc_umma<I8>(d, umma_desc_sw128(ring_s + st * TC_ABYTES + 32 * ks),
+                        umma_desc_sw128(b_s + kb * N1 * 128 + 32 * ks), id1, (kb | ks) != 0 ? 1u : 0u);
           umma_commit(empty + st);
         }
         umma_commit(acc_full + buf);
@@ -554,8 +669,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           tc_fence_after();
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks)
-            umma_f8(d, umma_desc_sw128(ring_s + st * TC_ABYTES + 32 * ks),
-                    umma_desc_sw128(b_s + bb * B2BYTES + kb * TC_N2 * 128 + 32 * ks), id2,
+            tc_umma<I8>(d, umma_desc_sw128(ring_s + st * TC_ABYTES + 32 * ks),
+                    umma_desc_sw128(b_s + bb * B2BYTES + kb * N2 * 128 + 32 * ks), id2,
                     (kb | ks) != 0 ? 1u : 0u);
           umma_commit(empty + st);
         }
@@ -588,8 +703,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
         for (int l = 0; l < TC_LINES; ++l) {
           float sum = v[l];
+          if constexpr (I8) {
+            sum = tc_i8_sum(__float_as_uint(v[l]), __float_as_uint(v[TC_LINES + l]), __float_as_uint(v[2 * TC_LINES + l]));
+          } else {
 #pragma unroll
-          for (int tt = 1; tt < T1; ++tt) sum += v[tt * TC_LINES + l];
+            for (int tt = 1; tt < T1; ++tt) sum += v[tt * TC_LINES + l];
+          }
           xchg[row * TC_XPITCH + l] = ok ? sum : 0.0f;
         }
         named_sync(3, TC_EPI);
@@ -660,14 +779,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
           for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(v[u][i]));
         }
+        if constexpr (I8) {
+          // ConvRot on the SwiGLU rows (as the reference's rotate(swiglu=True)): group u is lane sub's chunk u
+          m = 0.0f;
+#pragma unroll
+          for (int u = 0; u < CPL; ++u) {
+            tc_rotate16(v[u]);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(v[u][i]));
+          }
+        }
 #pragma unroll
         for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        const int e = tc_exponent(m);
+        const int e = I8 ? tc_exponent_i8(m) : tc_exponent(m);
         const float scale = __uint_as_float((uint32_t)(e + 127) << 23);
         if (live)
 #pragma unroll
-          for (int u = 0; u < CPL; ++u)
-            tc_write_terms<TC_TERMS2>(breg + bb * B2BYTES, TC_N2, j, TC_CAP, sub + 16 * u, v[u], scale);
+          for (int u = 0; u < CPL; ++u) {
+            if constexpr (I8)
+              tc_write_i8_terms(breg + bb * B2BYTES, N2, j, TC_CAP, sub + 16 * u, v[u], scale);
+            else
+              tc_write_terms<T2>(breg + bb * B2BYTES, N2, j, TC_CAP, sub + 16 * u, v[u], scale);
+          }
         if (live && sub == 0) {
           spair[bb * TC_CAP + j] = pair;
           sinv[bb * TC_CAP + j] = __uint_as_float((uint32_t)(127 - e) << 23);
@@ -686,10 +819,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (ok) ok = mbar_wait(acc_full + buf, (tn >> 1) & 1);
         ok = __all_sync(0xffffffffu, ok);
         tc_fence_after();
-        float v[TC_N2];
+        float v[N2];
         if (ok) {
 #pragma unroll
-          for (int cb = 0; cb < TC_N2 / 16; ++cb)
+          for (int cb = 0; cb < N2 / 16; ++cb)
             tmem_ld16(tmem + lane_base + buf * 64 + 16 * cb, (float(&)[16])v[16 * cb]);
         }
         tc_fence_before();
@@ -704,8 +837,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           for (int j = 0; j < TC_CAP; ++j) {
             if (j < cnt) {
               float sum = v[j];
+              if constexpr (I8) {
+                sum = tc_i8_sum(__float_as_uint(v[j]), __float_as_uint(v[TC_CAP + j]), __float_as_uint(v[2 * TC_CAP + j]));
+              } else {
 #pragma unroll
-              for (int tt = 1; tt < TC_TERMS2; ++tt) sum += v[tt * TC_CAP + j];
+                for (int tt = 1; tt < T2; ++tt) sum += v[tt * TC_CAP + j];
+              }
               __stcg(a.parts + (size_t)spair[bb * TC_CAP + j] * H + r, sum * (sc * sinv[bb * TC_CAP + j]));
             }
           }

@@ -475,23 +475,27 @@ static int decode_tc_min_lines() {
   return v ? atoi(v) : 1;
 }
 
-template <bool XBF, int NKB2>
+template <int FMT, bool XBF, int NKB2>
 static int decode_tc_launch(const d3::DecodeArgs& a, const CUtensorMap& m13, const CUtensorMap& m2,
                             const DeviceInfo& d, cudaStream_t s) {
-  auto kern = d3::moe_decode_tc_kernel<XBF, NKB2>;
+  auto kern = d3::moe_decode_tc_kernel<FMT, XBF, NKB2>;
   const int smem = d3::TcSmem::launch;
   if (int st = allow_smem(kern, smem)) return st;
   return launch(kern, dim3(d.sms), dim3(d3::TC_THREADS), smem, s, true, m13, m2, a);
 }
 
+// e4m3 (fp8c) or int8 ConvRot rows: one byte a weight either way
+template <int FMT>
 static int decode_tc(const d3::DecodeArgs& a, const DeviceInfo& d, cudaStream_t s) {
   CUtensorMap m13, m2;
   // gate_up rows [e_count * 2I, H] in boxes of 64 rows x 128 bytes; down rows [e_count * H, I] in 128 x 128
   if (!byte_tile_map(&m13, a.w13, (uint64_t)a.H, (uint64_t)a.e_count * 2 * a.I, 128, 64)) return D3_ERR_ARG;
   if (!byte_tile_map(&m2, a.w2, (uint64_t)a.I, (uint64_t)a.e_count * a.H, 128, 128)) return D3_ERR_ARG;
   switch (a.I) {
-    case 512: return a.x_bf16 ? decode_tc_launch<true, 4>(a, m13, m2, d, s) : decode_tc_launch<false, 4>(a, m13, m2, d, s);
-    case 768: return a.x_bf16 ? decode_tc_launch<true, 6>(a, m13, m2, d, s) : decode_tc_launch<false, 6>(a, m13, m2, d, s);
+    case 512:
+      return a.x_bf16 ? decode_tc_launch<FMT, true, 4>(a, m13, m2, d, s) : decode_tc_launch<FMT, false, 4>(a, m13, m2, d, s);
+    case 768:
+      return a.x_bf16 ? decode_tc_launch<FMT, true, 6>(a, m13, m2, d, s) : decode_tc_launch<FMT, false, 6>(a, m13, m2, d, s);
     default: return D3_ERR_ARG;
   }
 }
@@ -568,7 +572,10 @@ static int decode_common(int fmt, const void* x, int x_bf16, int M, int k, int E
   // M * k <= 128 segments)
   if (fmt == d3::FMT_FP8C && M >= decode_tc_min_lines() && d.sms >= d3::DEC_MAX_PAIRS && e_count <= d3::TC_MAX_E &&
       decode_tc_enabled())
-    return decode_tc(a, d, s);
+    return decode_tc<d3::FMT_FP8C>(a, d, s);
+  if (fmt == d3::FMT_I8 && M >= decode_tc_min_lines() && d.sms >= d3::DEC_MAX_PAIRS && e_count <= d3::TC_MAX_E &&
+      decode_tc_enabled())
+    return decode_tc<d3::FMT_I8>(a, d, s);
   if (fmt == d3::FMT_W4A8 && M >= decode_tc_min_lines() && d.sms >= d3::DEC_MAX_PAIRS && e_count <= d3::TC_MAX_E &&
       decode_tc_enabled())
     return decode_tc8(a, d, s);

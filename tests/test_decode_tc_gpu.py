@@ -1,6 +1,7 @@
 """The tensor-core decodes (1-16 lines) against the oracle and against the mma.sync decode on the same inputs
-(D3_DECODE_TC=0 selects it): per-channel e4m3 rows (tcgen05 kind::f8f6f4, the activations as exact e4m3 terms) and
-W4A8 (kind::i8 on int8-expanded int4 codes and int8 activations, group scales folded per 128 columns)."""
+(D3_DECODE_TC=0 selects it): per-channel e4m3 rows (tcgen05 kind::f8f6f4, the activations as exact e4m3 terms),
+int8 ConvRot rows (kind::i8, the activations rotated while staged and written as three int8 terms) and W4A8
+(kind::i8 on int8-expanded int4 codes and int8 activations, group scales folded per 128 columns)."""
 import numpy as np
 import pytest
 import torch
@@ -22,7 +23,13 @@ def both(monkeypatch, kind, x, ids, w, banks, **kw):
     return tc, ref
 
 
-@pytest.mark.parametrize("kind", ["fp8c", "w4a8"])
+def oracle(kind, x, ids, w, banks):
+    if kind == "int8":
+        return gd.oracle_decode(kind, x, ids, w, banks, (None, None), H)
+    return gd.baseline_oracle_decode(kind, x, ids, w, banks)
+
+
+@pytest.mark.parametrize("kind", ["fp8c", "w4a8", "int8"])
 @pytest.mark.parametrize("I", [768, 512])
 @pytest.mark.parametrize("M", [1, 2, 4, 8, 12, 16])
 @pytest.mark.parametrize("bf16", [True, False])
@@ -36,12 +43,12 @@ def test_tc_decode_matches_oracle(cuda, monkeypatch, kind, I, M, bf16):
     _lib.take_fault()
     tc, old = both(monkeypatch, kind, x, ids, w, banks)
     assert _lib.take_fault() == 0
-    ref = gd.baseline_oracle_decode(kind, x, ids, w, banks)
+    ref = oracle(kind, x, ids, w, banks)
     assert gd.rel_l2(tc.float(), ref) <= 1e-3
     assert gd.rel_l2(tc.float(), old.float()) <= 1e-3
 
 
-@pytest.mark.parametrize("kind", ["fp8c", "w4a8"])
+@pytest.mark.parametrize("kind", ["fp8c", "w4a8", "int8"])
 def test_tc_decode_benchmark_shape_and_repeats(cuda, monkeypatch, kind):
     """128 experts, 16 lines (the benchmark's layer): against the mma.sync decode, and bit-identical over repeated
     calls that share one workspace."""
@@ -76,7 +83,7 @@ def test_tc_decode_crowded_and_bad_ids(cuda, monkeypatch):
     assert gd.rel_l2(tc.float(), old.float()) <= 1e-3
 
 
-@pytest.mark.parametrize("kind", ["fp8c", "w4a8"])
+@pytest.mark.parametrize("kind", ["fp8c", "w4a8", "int8"])
 def test_tc_decode_expert_parallel_partials(cuda, monkeypatch, kind):
     """Expert blocks of 3 emulated ranks: each rank's fp32 partial against the mma.sync kernel's, their rank-order sum
     against the whole decode; then the peer exchange of one rank bit for bit against the same partial."""
@@ -105,7 +112,7 @@ def test_tc_decode_expert_parallel_partials(cuda, monkeypatch, kind):
     assert torch.equal(kernels.ep_reduce(st, M, H), whole.to(torch.bfloat16))
 
 
-@pytest.mark.parametrize("kind", ["fp8c", "w4a8"])
+@pytest.mark.parametrize("kind", ["fp8c", "w4a8", "int8"])
 def test_last_arrival_combine_equals_grid_combine(cuda, monkeypatch, kind):
     """With few segments (one or two lines) each 128-row block is combined by the tile that completes it instead of
     after a grid barrier (D3_LASTARRIVE_NSEG: 0 forces the grid barrier). Same arithmetic, so the outputs agree bit
