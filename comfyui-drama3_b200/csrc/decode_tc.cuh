@@ -55,6 +55,8 @@ constexpr int TC_BREGION = 98304;     // phase-1 B (<= 48 rows x 2048) or two ph
 constexpr int TC_XPITCH = 17;         // exchange row pitch (floats)
 constexpr int TC_TMEM_COLS = 128;     // two accumulators of <= 64 columns
 constexpr int TC_MAX_E = 512;         // experts per rank the plan's counting sort holds
+constexpr int TC_I8_TERMS = 3;        // int8 activation terms: about 22 bits of the row maximum (two, 15 bits, measured
+                                      // 1.25e-3 rel-L2 on bf16 outputs at one line)
 
 struct TcSmem {
   static constexpr int ring = 0;
@@ -207,37 +209,38 @@ D3_DEV int tc_exponent_i8(float m) {
   return min(100, max(-100, 5 - ex));
 }
 
-// 16 consecutive values of a row as three int8 terms of y = v * scale (|y| < 64): t1 = rint(y), t2 = rint(128 (y -
-// t1)), t3 = rint(128 (128 (y - t1) - t2)), so y = t1 + t2 / 128 + t3 / 16384 to within 2^-15; term t of the row goes
-// to B row t * tstride + n as 16-byte chunks of a K-major, 128-byte-swizzled operand.
+// 16 consecutive values of a row as TERMS int8 terms of y = v * scale (|y| < 64): t1 = rint(y), t2 = rint(128 (y -
+// t1)), t3 = rint(128 (128 (y - t1) - t2)), so y = t1 + t2 / 128 (+ t3 / 16384) to within 2^-8 (2^-15); term t of
+// the row goes to B row t * tstride + n as 16-byte chunks of a K-major, 128-byte-swizzled operand.
+template <int TERMS>
 D3_DEV void tc_write_i8_terms(uint8_t* b, int rows, int n, int tstride, int q, const float (&v)[16], float scale) {
-  uint32_t w[3][4];
+  uint32_t w[TERMS][4];
 #pragma unroll
   for (int p = 0; p < 4; ++p) {
-    uint32_t t1w = 0u, t2w = 0u, t3w = 0u;
+#pragma unroll
+    for (int t = 0; t < TERMS; ++t) w[t][p] = 0u;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float y = v[4 * p + i] * scale;
-      const float t1 = rintf(y);
-      const float r1 = (y - t1) * 128.0f;
-      const float t2 = rintf(r1);
-      const float t3 = fminf(127.0f, fmaxf(-127.0f, rintf((r1 - t2) * 128.0f)));
-      t1w |= ((uint32_t)(int)t1 & 0xFFu) << (8 * i);
-      t2w |= ((uint32_t)(int)t2 & 0xFFu) << (8 * i);
-      t3w |= ((uint32_t)(int)t3 & 0xFFu) << (8 * i);
+      float r = v[4 * p + i] * scale;
+#pragma unroll
+      for (int t = 0; t < TERMS; ++t) {
+        const float q8 = fminf(127.0f, fmaxf(-127.0f, rintf(r)));
+        w[t][p] |= ((uint32_t)(int)q8 & 0xFFu) << (8 * i);
+        r = (r - q8) * 128.0f;
+      }
     }
-    w[0][p] = t1w;
-    w[1][p] = t2w;
-    w[2][p] = t3w;
   }
 #pragma unroll
-  for (int t = 0; t < 3; ++t)
+  for (int t = 0; t < TERMS; ++t)
     *reinterpret_cast<uint4*>(b + tc_b_offset(rows, t * tstride + n, q)) = make_uint4(w[t][0], w[t][1], w[t][2], w[t][3]);
 }
 
-// The s32 accumulators of three int8 terms as one float: D1 + D2 / 128 + D3 / 16384 (each |D| < 2^24: exact).
-D3_DEV float tc_i8_sum(uint32_t d1, uint32_t d2, uint32_t d3) {
-  return (float)(int)d1 + (float)(int)d2 * 0.0078125f + (float)(int)d3 * 6.103515625e-05f;
+// The s32 accumulators of TERMS int8 terms as one float: D1 + D2 / 128 (+ D3 / 16384); each |D| < 2^24, exact.
+template <int TERMS>
+D3_DEV float tc_i8_sum(const float* v, int stride) {
+  float sum = (float)__float_as_int(v[0]) + (float)__float_as_int(v[stride]) * 0.0078125f;
+  if constexpr (TERMS > 2) sum += (float)__float_as_int(v[2 * stride]) * 6.103515625e-05f;
+  return sum;
 }
 
 D3_DEV void tc_load16(const void* src, bool bf16, size_t i, float (&v)[16]) {
@@ -389,9 +392,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     moe_decode_tc_kernel(const __grid_constant__ CUtensorMap map13, const __grid_constant__ CUtensorMap map2,
                          const DecodeArgs a) {
   constexpr bool I8 = FMT == FMT_I8;
-  constexpr int T1 = I8 ? 3 : XBF ? 2 : 3;  // phase-1 terms
+  constexpr int T1 = I8 ? TC_I8_TERMS : XBF ? 2 : 3;  // phase-1 terms
   constexpr int N1 = TC_LINES * T1;         // 32 / 48
-  constexpr int T2 = I8 ? 3 : TC_TERMS2;    // phase-2 terms
+  constexpr int T2 = I8 ? TC_I8_TERMS : TC_TERMS2;  // phase-2 terms
   constexpr int N2 = TC_CAP * T2;           // 48 / 64
   constexpr int H = DEC_H, NKB1 = H / 128;  // 16 column blocks in phase 1
   constexpr int I = NKB2 * 128;
@@ -530,7 +533,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           if constexpr (I8)
-            tc_write_i8_terms(breg, N1, n, TC_LINES, lane + 32 * u, v[u], scale);
+            tc_write_i8_terms<T1>(breg, N1, n, TC_LINES, lane + 32 * u, v[u], scale);
           else
             tc_write_terms<T1>(breg, N1, n, TC_LINES, lane + 32 * u, v[u], scale);
         }
@@ -704,7 +707,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         for (int l = 0; l < TC_LINES; ++l) {
           float sum = v[l];
           if constexpr (I8) {
-            sum = tc_i8_sum(__float_as_uint(v[l]), __float_as_uint(v[TC_LINES + l]), __float_as_uint(v[2 * TC_LINES + l]));
+            sum = tc_i8_sum<T1>(v + l, TC_LINES);
           } else {
 #pragma unroll
             for (int tt = 1; tt < T1; ++tt) sum += v[tt * TC_LINES + l];
@@ -797,7 +800,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
           for (int u = 0; u < CPL; ++u) {
             if constexpr (I8)
-              tc_write_i8_terms(breg + bb * B2BYTES, N2, j, TC_CAP, sub + 16 * u, v[u], scale);
+              tc_write_i8_terms<T2>(breg + bb * B2BYTES, N2, j, TC_CAP, sub + 16 * u, v[u], scale);
             else
               tc_write_terms<T2>(breg + bb * B2BYTES, N2, j, TC_CAP, sub + 16 * u, v[u], scale);
           }
@@ -838,7 +841,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             if (j < cnt) {
               float sum = v[j];
               if constexpr (I8) {
-                sum = tc_i8_sum(__float_as_uint(v[j]), __float_as_uint(v[TC_CAP + j]), __float_as_uint(v[2 * TC_CAP + j]));
+                sum = tc_i8_sum<T2>(v + j, TC_CAP);
               } else {
 #pragma unroll
                 for (int tt = 1; tt < T2; ++tt) sum += v[tt * TC_CAP + j];

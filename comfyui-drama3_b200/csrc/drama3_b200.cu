@@ -6,6 +6,7 @@
 
 #include <cstdlib>
 #include <cstring>
+#include <algorithm>
 #include <mutex>
 
 #include <cudaTypedefs.h>
@@ -573,8 +574,10 @@ static int decode_common(int fmt, const void* x, int x_bf16, int M, int k, int E
   if (fmt == d3::FMT_FP8C && M >= decode_tc_min_lines() && d.sms >= d3::DEC_MAX_PAIRS && e_count <= d3::TC_MAX_E &&
       decode_tc_enabled())
     return decode_tc<d3::FMT_FP8C>(a, d, s);
-  if (fmt == d3::FMT_I8 && M >= decode_tc_min_lines() && d.sms >= d3::DEC_MAX_PAIRS && e_count <= d3::TC_MAX_E &&
-      decode_tc_enabled())
+  // int8 ConvRot: from 3 lines (each CTA rotates the lines' rows while staging them, which costs more than the
+  // mma.sync decode saves at one or two lines: 27.3 against 24.2 us a layer at one line, 43.9 against 50.1 at four)
+  if (fmt == d3::FMT_I8 && M >= std::max(3, decode_tc_min_lines()) && d.sms >= d3::DEC_MAX_PAIRS &&
+      e_count <= d3::TC_MAX_E && decode_tc_enabled())
     return decode_tc<d3::FMT_I8>(a, d, s);
   if (fmt == d3::FMT_W4A8 && M >= decode_tc_min_lines() && d.sms >= d3::DEC_MAX_PAIRS && e_count <= d3::TC_MAX_E &&
       decode_tc_enabled())
