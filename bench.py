@@ -463,10 +463,56 @@ def slot_cache_leg(device, args, stream, slots_per_layer=16, n_routings=8, seed=
                     "zero-copy, filling the slot) + SwiGLU + gemv_fp8 + weighted_sum per layer and row, one graph"}
 
 
+def block_leg(kernels, device, args, stream, shared_i=512, seed=45):
+    """The whole MoE block per layer (drama3/model.py:92-124) for 16 decode lines, 48 layers: router (bf16 linear
+    2048 -> 128 and the decode routing), the routed experts (fp8c, the fused decode) and the sigmoid-gated shared
+    expert (bf16, intermediate 512), fused (kernels.router: one launch; kernels.shared_expert: two) against the same
+    block on torch's chain (cuBLAS linears, the route kernel, silu / sigmoid / mul / add). One graph per step each."""
+    n_layers, lines = args.layers, args.lines
+    gen = torch.Generator(device=device).manual_seed(seed)
+
+    def randn(*shape):
+        return (torch.randn(shape, generator=gen, device=device) * 0.02).to(torch.bfloat16)
+
+    layers = [{"router": randn(E, H), "gu": randn(2 * shared_i, H), "dn": randn(H, shared_i), "g": randn(1, H),
+               "banks": tuple(rand_bank("fp8c", n, k, gen, device) for n, k in ((2 * I, H), (H, I)))}
+              for _ in range(n_layers)]
+    x = torch.randn((lines, H), generator=torch.Generator().manual_seed(7)).to(torch.bfloat16).to(device)
+    ws = kernels.decode_workspace(lines, K_TOP, I, device)
+    outs = torch.empty((n_layers, lines, H), dtype=torch.bfloat16, device=device)
+
+    def fused():
+        for l_, lay in enumerate(layers):
+            ids, w = kernels.router(x, lay["router"], K_TOP)
+            kernels.moe_decode("fp8c", x, ids, w, lay["banks"], workspace=ws, out=outs[l_])
+            kernels.shared_expert(x, lay["gu"], lay["dn"], lay["g"], outs[l_])
+
+    def eager():
+        for l_, lay in enumerate(layers):
+            ids, w = kernels.route(x @ lay["router"].T, K_TOP)
+            moe = kernels.moe_decode("fp8c", x, ids, w, lay["banks"], workspace=ws, out=outs[l_])
+            h = x @ lay["gu"].T
+            sh = (torch.nn.functional.silu(h[:, :shared_i]) * h[:, shared_i:]) @ lay["dn"].T
+            outs[l_].copy_(moe + torch.sigmoid(x @ lay["g"].T) * sh)
+
+    res = {}
+    for name, fn in (("fused", fused), ("torch_chain", eager)):
+        with torch.cuda.stream(stream):
+            graph = capture(fn, 2, stream)
+            ms = time_replays(graph, max(3, min(args.steps, 20)), stream)
+        del graph
+        res[name] = {"tokens_per_s": lines / (ms * 1e-3), "ms_per_step": ms, "us_per_layer": 1e3 * ms / n_layers}
+    del layers
+    torch.cuda.empty_cache()
+    res["what"] = ("per layer: router 2048 -> 128 bf16 + top-8 routing, fp8c routed experts (fused decode), shared "
+                   "expert 2048 -> 2 x 512 -> 2048 bf16 with its sigmoid gate, 16 lines")
+    return res
+
+
 def full_stack_leg(kernels, device, args, stream, ctx=4096, q_heads=32, kv_heads=4, head_dim=128, seed=44):
     """the whole 48-layer decoder step of `lines` lines, each layer RMSNorm -> attention (QKV
     projection, 32 query / 4 KV heads of 128 over a 4096-token bf16 KV cache per line, the step's K / V written at
-    its position, output projection) -> residual -> RMSNorm -> router (bf16 GEMV, then the route kernel) -> the fused
+    its position, output projection) -> residual -> RMSNorm -> router (linear and routing in one launch) -> the fused
     MoE decode (fp8c) -> residual. Random-init weights from seed 44, one CUDA graph per step. The attention, the
     projections and the norms are torch (cuBLAS / SDPA): library calls around this library's MoE path; RoPE is left
     out (it moves no bytes that matter). Reports tokens/s and the HBM fraction of the step's bytes (routed experts,
@@ -510,7 +556,7 @@ def full_stack_leg(kernels, device, args, stream, ctx=4096, q_heads=32, kv_heads
             o = torch.nn.functional.scaled_dot_product_attention(q, lay["k"], lay["v"])
             h.add_(o.reshape(lines, q_heads * head_dim) @ lay["wo"].T)
             m = rmsnorm(h, lay["n2"])
-            ids, w = kernels.route(m @ lay["router"].T, K_TOP)
+            ids, w = kernels.router(m, lay["router"], K_TOP)
             if record:
                 ids_seen.append(ids)
             kernels.moe_decode("fp8c", m, ids, w, lay["banks"], workspace=ws, out=moe_out)
@@ -534,7 +580,7 @@ def full_stack_leg(kernels, device, args, stream, ctx=4096, q_heads=32, kv_heads
             "expert_bytes_per_step": expert_b, "kv_bytes_per_step": kv_b, "attention_router_weight_bytes": weight_b,
             "hbm_gbs": gbs, "frac": gbs / hbm_peak,
             "what": "RMSNorm, QKV / O projections (cuBLAS bf16), GQA attention over the KV cache (torch SDPA), "
-                    "router GEMV (cuBLAS) + route kernel, fused MoE decode (moe_decode_tc_kernel), one graph"}
+                    "router (router_kernel: linear + routing), fused MoE decode (moe_decode_tc_kernel), one graph"}
 
 
 # ---- CPU baselines: the reference's CPU paths (oracle/cpu_port.py), bounded samples on the host cores
@@ -946,6 +992,11 @@ def main():
             extras["config4_prefill"] = prefill_leg(device, args.steps)
         except Exception as exc:
             extras["config4_prefill"] = {"error": repr(exc)[:200]}
+        # the whole MoE block (router, experts, shared expert), fused against torch's chain
+        try:
+            extras["moe_block"] = block_leg(kernels, device, args, stream)
+        except Exception as exc:
+            extras["moe_block"] = {"error": repr(exc)[:300]}
         # config 5: the whole decoder step (attention + MoE), 48 layers
         try:
             extras["config5_full_stack"] = full_stack_leg(kernels, device, args, stream)

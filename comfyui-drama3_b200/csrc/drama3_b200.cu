@@ -19,6 +19,8 @@
 #include "decode_tc.cuh"
 #include "decode_tc8.cuh"
 #include "resolve.cuh"
+#include "router.cuh"
+#include "shared.cuh"
 #include "rotate.cuh"
 #include "route.cuh"
 
@@ -179,8 +181,8 @@ int d3_route(const uint16_t* logits, int rows, int n, int k, int64_t* ids, float
   if (rows < 0 || n < 1 || n > d3::ROUTE_MAX_N || k < 1 || k > 32 || k > n) return D3_ERR_ARG;
   if (!logits || !ids || !weights) return D3_ERR_ARG;
   if (rows == 0) return D3_OK;
-  dim3 grid((rows + d3::ROUTE_WARPS - 1) / d3::ROUTE_WARPS);
-  d3::route_rows<<<grid, d3::ROUTE_WARPS * 32, 0, (cudaStream_t)stream>>>(logits, rows, n, k, ids, weights);
+  dim3 grid((rows + d3::ROUTE_ROWS - 1) / d3::ROUTE_ROWS);
+  d3::route_rows<<<grid, d3::ROUTE_ROWS * d3::ROUTE_GROUP, 0, (cudaStream_t)stream>>>(logits, rows, n, k, ids, weights);
   return launch_status();
 }
 
@@ -200,6 +202,57 @@ int d3_rotate(const void* x, int mode, int rows, int K, float* out, const int* o
   if (st) return st;
   d3::rotate_rows_kernel<<<rows, 256, smem, (cudaStream_t)stream>>>(x, mode, K, out, only_if);
   return launch_status();
+}
+
+int d3_router(const void* x, int M, int H, const void* w, int E, int k, int64_t* ids, float* weights, void* logits,
+              void* stream) {
+  if (!x || !w || !ids || !weights) return D3_ERR_ARG;
+  if (M < 1 || M > d3::RT_MAX_M || H != d3::RT_H || E < 64 || E > d3::RT_MAX_E || E % 64 || k < 1 || k > 32 ||
+      k > E)
+    return D3_ERR_ARG;
+  if (!aligned(x, 16) || !aligned(w, 16) || !aligned(logits, 2)) return D3_ERR_ALIGN;
+  DeviceInfo d;
+  if (int st = device_info(&d)) return st;
+  const int smem = (E / d3::RT_CTAS + d3::RT_MAX_M) * d3::RT_PITCH * 2;
+  if (int st = allow_smem(d3::router_kernel, smem)) return st;
+  return launch(d3::router_kernel, dim3(d3::RT_CTAS), dim3(d3::RT_WARPS * 32), smem, (cudaStream_t)stream, true,
+                (const uint16_t*)x, M, (const uint16_t*)w, E, k, ids, weights, (uint16_t*)logits);
+}
+
+extern "C++" {
+template <int KS>
+static int shared_down(const void* scratch, int M, const void* w_d, const float* gate, void* out, cudaStream_t s) {
+  const int smem = (d3::SH_DOWN_ROWS + d3::RT_MAX_M) * (KS * 128 + 8) * 2;
+  if (int st = allow_smem(d3::shared_down_kernel<KS>, smem)) return st;
+  return launch(d3::shared_down_kernel<KS>, dim3(d3::SH_H / d3::SH_DOWN_ROWS), dim3(d3::SH_WARPS * 32), smem, s, true,
+                (const uint16_t*)scratch, M, (const uint16_t*)w_d, gate, (uint16_t*)out);
+}
+}
+
+int d3_shared_expert(const void* x, int M, int H, const void* w_gu, const void* w_d, const void* w_g, int I,
+                     void* scratch, void* out, void* stream) {
+  if (!x || !w_gu || !w_d || !w_g || !scratch || !out) return D3_ERR_ARG;
+  if (M < 1 || M > d3::RT_MAX_M || H != d3::SH_H || I < 256 || I > 1024 || I % 256) return D3_ERR_ARG;
+  if (!aligned(x, 16) || !aligned(w_gu, 16) || !aligned(w_d, 16) || !aligned(w_g, 16) || !aligned(scratch, 16) ||
+      !aligned(out, 2))
+    return D3_ERR_ALIGN;
+  DeviceInfo d;
+  if (int st = device_info(&d)) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  // scratch: a [M, I] bf16, then the gate [M] fp32
+  float* gate = reinterpret_cast<float*>((uint16_t*)scratch + (size_t)M * I);
+  const int smem_up = (9 + d3::RT_MAX_M) * d3::SH_UP_PITCH * 2;
+  if (int st = allow_smem(d3::shared_up_kernel, smem_up)) return st;
+  if (int st = launch(d3::shared_up_kernel, dim3(I / d3::SH_UP_CH), dim3(d3::SH_WARPS * 32), smem_up, s, true,
+                      (const uint16_t*)x, M, (const uint16_t*)w_gu, (const uint16_t*)w_g, I, (uint16_t*)scratch,
+                      gate))
+    return st;
+  switch (I / 128) {
+    case 2: return shared_down<2>(scratch, M, w_d, gate, out, s);
+    case 4: return shared_down<4>(scratch, M, w_d, gate, out, s);
+    case 6: return shared_down<6>(scratch, M, w_d, gate, out, s);
+    default: return shared_down<8>(scratch, M, w_d, gate, out, s);
+  }
 }
 
 int d3_resolve(const int64_t* ids, int k, int layer, int layers, int experts, int* table, int* owner, float* score,

@@ -359,11 +359,6 @@ D3_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_
       : "memory");
 }
 
-D3_DEV uint64_t policy_evict_last() {
-  uint64_t p;
-  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
-  return p;
-}
 
 // ---------------------------------------------------------------------------------------------------------------
 struct GmArgs {

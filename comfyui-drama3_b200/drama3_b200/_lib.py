@@ -30,6 +30,8 @@ SIGNATURES = {
     "d3_device_check": (_i, []),
     "d3_take_fault": (_i, [ctypes.POINTER(ctypes.c_uint)]),
     "d3_route": (_i, [_p, _i, _i, _i, _p, _p, _p]),
+    "d3_router": (_i, [_p, _i, _i, _p, _i, _i, _p, _p, _p, _p]),
+    "d3_shared_expert": (_i, [_p, _i, _i, _p, _p, _p, _i, _p, _p, _p]),
     "d3_weighted_sum": (_i, [_p, _p, _i, _i, _i, _p, _p]),
     "d3_rotate": (_i, [_p, _i, _i, _i, _p, _p, _p]),
     "d3_resolve": (_i, [_p, _i, _i, _i, _i, _p, _p, _p, _p, _p, _i, _p, _p, _p, _p, _p, _p, _d, _i, _d, _p]),

@@ -96,6 +96,68 @@ def route(logits, k):
     return ids, weights
 
 
+def _aligned16(t):
+    """t, or a copy of it where its data does not start on a 16-byte boundary (the bulk copies' rule)."""
+    return t if t.data_ptr() % 16 == 0 else t.clone()
+
+
+def router(x, weight, k, logits=False):
+    """(ids [rows, k] int64, weights [rows, k] float32[, logits [rows, E] bfloat16]) of decode rows x [rows, H]
+    (bfloat16, rows <= 16) through a bias-free bf16 router linear `weight` [E, H] and the decode routing, in one launch:
+    route(x @ weight.T, k) with the logits as the bf16 rounding of fp32 sums of the exact products."""
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise TypeError("router takes bfloat16 rows and weight")
+    x, weight = _aligned16(x.contiguous()), _aligned16(weight.contiguous())
+    rows, H = x.shape
+    E = weight.shape[0]
+    ids = torch.empty((rows, k), dtype=torch.int64, device=x.device)
+    w = torch.empty((rows, k), dtype=torch.float32, device=x.device)
+    lg = torch.empty((rows, E), dtype=torch.bfloat16, device=x.device) if logits else None
+    with _on(x.device):
+        check(lib().d3_router(_ptr(x), rows, H, _ptr(weight), E, int(k), _ptr(ids), _ptr(w), _ptr(lg),
+                              _stream(x.device)), "router")
+    return (ids, w, lg) if logits else (ids, w)
+
+
+def router_fits(rows, hidden, experts, k):
+    """Whether `router` takes these shapes."""
+    return 1 <= rows <= 16 and hidden == 2048 and experts % 64 == 0 and 64 <= experts <= 256 and k <= min(32, experts)
+
+
+_SHARED_SCRATCH = {}
+
+
+def shared_expert(x, gate_up, down, gate, out):
+    """out [rows, H] bfloat16 += sigmoid(x @ gate.T) * down(SwiGLU(gate_up(x))) for decode rows x [rows, H] (bfloat16,
+    rows <= 16), in place, in two launches; gate_up [2I, H], down [H, I], gate [1, H] or [H], all bfloat16 (the
+    reference's SharedExpert and shared_expert_gate linears, drama3/model.py:40-47,123). Returns out."""
+    for t in (x, gate_up, down, gate, out):
+        if t.dtype != torch.bfloat16:
+            raise TypeError("shared_expert takes bfloat16 tensors")
+    x, gate_up, down, gate = (_aligned16(t.contiguous()) for t in (x, gate_up, down, gate))
+    if not out.is_contiguous():
+        raise ValueError("out must be contiguous (it is updated in place)")
+    rows, H = x.shape
+    I = down.shape[1]
+    # scratch: the SwiGLU rows [rows, I] bf16, then the gate [rows] fp32
+    key = (x.device, torch.cuda.current_stream(x.device).cuda_stream, rows, I)
+    if torch.cuda.is_current_stream_capturing():
+        scratch = torch.empty(rows * (I + 2), dtype=torch.bfloat16, device=x.device)
+    else:
+        scratch = _SHARED_SCRATCH.get(key)
+        if scratch is None:
+            scratch = _SHARED_SCRATCH[key] = torch.empty(rows * (I + 2), dtype=torch.bfloat16, device=x.device)
+    with _on(x.device):
+        check(lib().d3_shared_expert(_ptr(x), rows, H, _ptr(gate_up), _ptr(down), _ptr(gate), I, _ptr(scratch),
+                                     _ptr(out), _stream(x.device)), "shared_expert")
+    return out
+
+
+def shared_expert_fits(rows, hidden, intermediate):
+    """Whether `shared_expert` takes these shapes."""
+    return 1 <= rows <= 16 and hidden == 2048 and intermediate in (256, 512, 768, 1024)
+
+
 def weighted_sum(parts, weights):
     """[rows, H] bfloat16: parts [rows * k, H] (float32) summed per row by weights [rows, k] or [k] (float32), in
     rank order (drama3/kernels.py:656-661; there rows == 1)."""

@@ -8,10 +8,12 @@ checkpoint's QuantizedTensor or `pack.packed_weight`). The routed experts are FP
 per-channel scales with config.fp8_per_channel), Experts over quantized banks, or any module passed as `experts=`
 (an `OffloadedExperts` of a slot-cache store).
 
-One change on the hot path: the decode rows of lines batched together ([B, 1, H]) are routed together by one
-`kernels.route` launch and run through the experts as one call (one fused decode kernel for up to 16 rows), where
-the reference loops the block row by row (drama3/model.py:111-113). Routing and combine keep the reference's numerics,
-so each row's result is the one the per-row loop gives up to the fused kernel's summation order.
+Changes on the hot path: the decode rows of lines batched together ([B, 1, H]) are routed together and run through
+the experts as one call (one fused decode kernel for up to 16 rows), where the reference loops the block row by row
+(drama3/model.py:111-113); and for decode rows the router linear with its routing is one launch (`kernels.router`)
+and the sigmoid-gated shared expert two (`kernels.shared_expert`, added into the experts' output), where torch runs
+about a dozen. Routing keeps the reference's rule on the router's bf16 logits (whose fp32 sums may differ from
+cuBLAS's in the last bf16 place), and each row's result is the one the per-row loop gives up to summation order.
 """
 import contextlib
 from types import SimpleNamespace
@@ -131,6 +133,9 @@ class SparseMoeBlock(nn.Module):
         self.shared_expert = SharedExpert(hidden, config.shared_expert_intermediate_size, device=device, dtype=dtype,
                                           ops=ops)
         self.shared_expert_gate = ops.Linear(hidden, 1, bias=False, device=device, dtype=dtype)
+        # decode rows: the router (linear + routing) in one launch and the gated shared expert in two, where the
+        # modules are plain bias-free bf16 linears of shapes the kernels take; False keeps torch's chain
+        self.fused = True
 
     def route(self, logits, decode):
         """(ids, weights) of router logits [rows, E]: the route kernel for decode rows (bit-identical to the
@@ -141,21 +146,43 @@ class SparseMoeBlock(nn.Module):
         weights, ids = torch.softmax(logits.float(), dim=-1).topk(self.top_k, dim=-1)
         return ids, (weights / weights.sum(dim=-1, keepdim=True)).to(logits.dtype)
 
+    def _plain(self, *linears):
+        """Whether these modules are bias-free bf16 torch linears on a CUDA device (what the fused kernels read)."""
+        return all(type(m) is nn.Linear and m.bias is None and m.weight.dtype == torch.bfloat16 and m.weight.is_cuda
+                   for m in linears)
+
+    def fused_router(self, flat):
+        return (self.fused and flat.dtype == torch.bfloat16 and self._plain(self.gate)
+                and kernels.router_fits(flat.shape[0], flat.shape[1], self.gate.weight.shape[0], self.top_k))
+
+    def fused_shared(self, flat):
+        se = self.shared_expert
+        return (self.fused and flat.dtype == torch.bfloat16
+                and self._plain(se.gate_up_proj, se.down_proj, self.shared_expert_gate)
+                and kernels.shared_expert_fits(flat.shape[0], flat.shape[1], se.down_proj.weight.shape[1]))
+
     def forward(self, x, norm=None):
         if norm is not None:
             x = norm(x)
         flat = x.reshape(-1, x.shape[-1])
-        logits = self.gate(flat)
         # decode: one row, or the rows of lines decoded together ([B, 1, H]) routed and run at once
         decode = flat.shape[0] == 1 or (x.dim() == 3 and x.shape[1] == 1 and flat.shape[0] <= MAX_DECODE_ROWS)
-        topk_idx, topk_weight = self.route(logits, decode)
+        if decode and self.fused_router(flat):
+            topk_idx, topk_weight = kernels.router(flat, self.gate.weight, self.top_k)
+        else:
+            topk_idx, topk_weight = self.route(self.gate(flat), decode)
         if decode and flat.shape[0] > 1 and not isinstance(self.experts, (FP8Experts, Experts)):
             # a slot-cache store decodes one row at a time
             out = torch.cat([self.experts(flat[r:r + 1], topk_idx[r:r + 1], topk_weight[r:r + 1])
                              for r in range(flat.shape[0])])
         else:
             out = self.experts(flat, topk_idx, topk_weight)
-        out = out + torch.sigmoid(self.shared_expert_gate(flat)) * self.shared_expert(flat)
+        if decode and self.fused_shared(flat) and out.dtype == torch.bfloat16 and out.is_contiguous():
+            se = self.shared_expert
+            out = kernels.shared_expert(flat, se.gate_up_proj.weight, se.down_proj.weight,
+                                        self.shared_expert_gate.weight, out)
+        else:
+            out = out + torch.sigmoid(self.shared_expert_gate(flat)) * self.shared_expert(flat)
         return out.view_as(x)
 
 

@@ -78,6 +78,24 @@ int d3_weighted_sum(const float* parts, const float* weights, int rows, int k, i
  * K % 256 == 0. Replaces drama3/kernels.py:222-258 (rotate_rows) and :636-644 (rotate). */
 int d3_rotate(const void* x, int mode, int rows, int K, float* out, const int* only_if, void* stream);
 
+/* The router of a decode step in one launch: SparseMoeBlock's gate linear (drama3/model.py:115, a bias-free bf16
+ * linear hidden -> experts) and kernels.route (drama3/kernels.py:647-653) on its output. x [M, H] bf16, w [E, H]
+ * bf16 -> ids [M, k] int64, weights [M, k] fp32 (bf16 values, renormalized softmax of the k largest logits), and the
+ * logits [M, E] bf16 when `logits` is not null. The logits are the bf16 rounding of fp32 sums of the exact products;
+ * ids and weights are kernels.route's on them. M <= 16, H == 2048, E % 64 == 0, E <= 256, k <= min(32, E); x and w
+ * 16-byte aligned. */
+int d3_router(const void* x, int M, int H, const void* w, int E, int k, int64_t* ids, float* weights, void* logits,
+              void* stream);
+
+/* The shared expert of a decode step, sigmoid-gated and added to the MoE output, in two launches (drama3/model.py:40-47
+ * and :123: out + sigmoid(shared_expert_gate(x)) * shared_expert(x)). x [M, H] bf16; w_gu [2I, H] bf16 (gate rows,
+ * then up rows), w_d [H, I] bf16, w_g [H] bf16 (the gate linear's one row); scratch: M * I bf16 then M fp32 of the
+ * caller's (the SwiGLU rows and the gate values between the launches); out [M, H] bf16, updated in place. bf16
+ * rounding where the reference's bf16 modules round. M <= 16, H == 2048, I in {256, 512, 768, 1024}; x, the weights
+ * and scratch 16-byte aligned. */
+int d3_shared_expert(const void* x, int M, int H, const void* w_gu, const void* w_d, const void* w_g, int I,
+                     void* scratch, void* out, void* stream);
+
 /* Slot-cache lookup and eviction for one decode row's k experts of `layer`; writes plan [k, 2] (slot, code) and
  * updates the cache state in place. Same state arrays and semantics as drama3/kernels.py:78-191 (resolve_experts),
  * launcher :618-625 (resolve); k <= 32. */
