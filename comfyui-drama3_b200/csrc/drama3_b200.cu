@@ -21,6 +21,7 @@
 #include "resolve.cuh"
 #include "router.cuh"
 #include "shared.cuh"
+#include "plan.cuh"
 #include "rotate.cuh"
 #include "route.cuh"
 
@@ -253,6 +254,14 @@ int d3_shared_expert(const void* x, int M, int H, const void* w_gu, const void* 
     case 6: return shared_down<6>(scratch, M, w_d, gate, out, s);
     default: return shared_down<8>(scratch, M, w_d, gate, out, s);
   }
+}
+
+int d3_prefill_plan(const int64_t* ids, int P, int E, int drop_invalid, int64_t* order, int64_t* pos, int* groups,
+                    void* stream) {
+  if (P < 0 || E < 1 || E > d3::PLAN_MAX_E || !groups || (P > 0 && (!ids || !order || !pos))) return D3_ERR_ARG;
+  d3::prefill_plan_kernel<<<1, d3::PLAN_THREADS, 0, (cudaStream_t)stream>>>(ids, P, E, drop_invalid, order, pos,
+                                                                           groups);
+  return launch_status();
 }
 
 int d3_resolve(const int64_t* ids, int k, int layer, int layers, int experts, int* table, int* owner, float* score,

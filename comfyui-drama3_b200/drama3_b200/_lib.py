@@ -32,6 +32,7 @@ SIGNATURES = {
     "d3_route": (_i, [_p, _i, _i, _i, _p, _p, _p]),
     "d3_router": (_i, [_p, _i, _i, _p, _i, _i, _p, _p, _p, _p]),
     "d3_shared_expert": (_i, [_p, _i, _i, _p, _p, _p, _i, _p, _p, _p]),
+    "d3_prefill_plan": (_i, [_p, _i, _i, _i, _p, _p, _p, _p]),
     "d3_weighted_sum": (_i, [_p, _p, _i, _i, _i, _p, _p]),
     "d3_rotate": (_i, [_p, _i, _i, _i, _p, _p, _p]),
     "d3_resolve": (_i, [_p, _i, _i, _i, _i, _p, _p, _p, _p, _p, _i, _p, _p, _p, _p, _p, _p, _d, _i, _d, _p]),

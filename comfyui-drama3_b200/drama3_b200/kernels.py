@@ -158,6 +158,28 @@ def shared_expert_fits(rows, hidden, intermediate):
     return 1 <= rows <= 16 and hidden == 2048 and intermediate in (256, 512, 768, 1024)
 
 
+def prefill_plan(topk_idx, num_experts, drop_invalid=False):
+    """(order [P] int64, pos [P] int64, groups [E + 1, 5] int32) of a prompt's routing [T, k] sorted by expert on the
+    device in one launch, no host sync: order holds the (token, rank) pairs by expert id, within an expert in index
+    order, ids outside [0, E) last; pos its inverse; groups (expert, slot, 0, first, rows) for every expert and one
+    last group for the out-of-range ids (0 rows when drop_invalid). num_experts <= 256 (drama3/offload.py:141-145
+    sorts on the host)."""
+    flat = topk_idx.reshape(-1).to(torch.int64).contiguous()
+    P = flat.numel()
+    order = torch.empty(P, dtype=torch.int64, device=flat.device)
+    pos = torch.empty(P, dtype=torch.int64, device=flat.device)
+    groups = torch.empty((num_experts + 1, 5), dtype=torch.int32, device=flat.device)
+    with _on(flat.device):
+        check(lib().d3_prefill_plan(_ptr(flat), P, int(num_experts), int(bool(drop_invalid)), _ptr(order), _ptr(pos),
+                                    _ptr(groups), _stream(flat.device)), "prefill_plan")
+    return order, pos, groups
+
+
+def prefill_plan_fits(num_experts):
+    """Whether `prefill_plan` takes this many experts."""
+    return 1 <= num_experts <= 256
+
+
 def weighted_sum(parts, weights):
     """[rows, H] bfloat16: parts [rows * k, H] (float32) summed per row by weights [rows, k] or [k] (float32), in
     rank order (drama3/kernels.py:656-661; there rows == 1)."""

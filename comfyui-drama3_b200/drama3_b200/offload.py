@@ -227,8 +227,8 @@ def capturing(x):
 
 def prefill_plan(topk_idx, num_experts, drop_invalid=False):
     """The prompt's (token, rank) pairs sorted by expert on the device, with no host sync, so that a prompt pass can
-    be captured in a CUDA graph (the host-side sort of drama3/offload.py:141-145 reads the counts back): a counting
-    sort by per-expert prefix sums of the pairs' one-hot rows. Returns (order, pos, groups, tiles):
+    be captured in a CUDA graph (the host-side sort of drama3/offload.py:141-145 reads the counts back). Returns
+    (order, pos, groups, tiles):
       order [P] int64: the pairs in expert order, in (token, rank) order within an expert; pos [P] its inverse;
       groups [E + 1, 5] int32 (expert, slot, 0, first, rows): every expert's group, empty ones included (they get no
         tile), then one group for the pairs whose id is outside [0, E), which sort last (slot E: the grouped kernels
@@ -236,9 +236,15 @@ def prefill_plan(topk_idx, num_experts, drop_invalid=False):
       tiles: a host int from the shapes alone that bounds the row tiles of any routing, (P + (t - 1)(E + 1)) // t for
         t rows per tile (the kernels run the number of tiles the groups need, counted on the device).
     drop_invalid: the last group gets no rows, so the pairs of out-of-range ids are left out (not computed, no fault):
-    for padding rows."""
+    for padding rows.
+    On a GPU with up to 256 experts the sort is one kernel launch (kernels.prefill_plan, a counting sort); otherwise
+    (CPU tensors, more experts) it is the same counting sort in torch ops: per-expert prefix sums of one-hot rows."""
     flat = topk_idx.reshape(-1).to(torch.int64)
     E, P = num_experts, flat.numel()
+    t = kernels.grouped_tile_rows()
+    tiles = (P + (t - 1) * (E + 1)) // t
+    if flat.is_cuda and kernels.prefill_plan_fits(E):
+        return (*kernels.prefill_plan(flat, E, drop_invalid), tiles)
     key = torch.where((flat >= 0) & (flat < E), flat, torch.full_like(flat, E))
     onehot = (key.unsqueeze(1) == torch.arange(E + 1, device=flat.device)).to(torch.int32)
     ranks = torch.cumsum(onehot, dim=0, dtype=torch.int32)
@@ -249,8 +255,7 @@ def prefill_plan(topk_idx, num_experts, drop_invalid=False):
     experts = torch.arange(E + 1, dtype=torch.int32, device=flat.device)
     rows = torch.cat([counts[:E], torch.zeros_like(counts[E:])]) if drop_invalid else counts
     groups = torch.stack([experts, experts, torch.zeros_like(experts), first, rows], dim=1).contiguous()
-    t = kernels.grouped_tile_rows()
-    return order, pos, groups, (P + (t - 1) * (E + 1)) // t
+    return order, pos, groups, tiles
 
 
 def _grouped_resident(kind, x, groups, tiles, bank, rows, codebook):

@@ -78,6 +78,14 @@ int d3_weighted_sum(const float* parts, const float* weights, int rows, int k, i
  * K % 256 == 0. Replaces drama3/kernels.py:222-258 (rotate_rows) and :636-644 (rotate). */
 int d3_rotate(const void* x, int mode, int rows, int K, float* out, const int* only_if, void* stream);
 
+/* The prompt pass's sort of its (token, rank) pairs by expert, on the device, in one launch (replaces the host-side
+ * sort and group list of drama3/offload.py:141-145, which reads the counts back to the host): ids [P] int64 ->
+ * order [P] int64 (pairs by expert id, within an expert in index order; ids outside [0, E) last), pos [P] int64 (the
+ * inverse of order), groups [E + 1][5] int32 (expert, slot = expert, 0, first row, rows; group E holds the
+ * out-of-range ids, with 0 rows when drop_invalid). 1 <= E <= 256. */
+int d3_prefill_plan(const int64_t* ids, int P, int E, int drop_invalid, int64_t* order, int64_t* pos, int* groups,
+                    void* stream);
+
 /* The router of a decode step in one launch: SparseMoeBlock's gate linear (drama3/model.py:115, a bias-free bf16
  * linear hidden -> experts) and kernels.route (drama3/kernels.py:647-653) on its output. x [M, H] bf16, w [E, H]
  * bf16 -> ids [M, k] int64, weights [M, k] fp32 (bf16 values, renormalized softmax of the k largest logits), and the

@@ -98,3 +98,32 @@ def test_fp8_experts_prompt_pass_captured(cuda):
         assert torch.equal(out, eager)
     finally:
         del graph
+
+
+def _ids_cases():
+    g = torch.Generator().manual_seed(91)
+    yield "zipf", torch.multinomial(torch.arange(1, E + 1).float().pow(-1.1), 16384, True, generator=g).view(-1, 8), E
+    yield "ragged", torch.randint(0, E, (333, 7), generator=g), E
+    bad = torch.randint(0, E, (1500, 8), generator=g)
+    bad[::7, 3] = -1
+    bad[::11, 5] = E
+    bad[::13, 0] = 10 ** 6
+    yield "out_of_range", bad, E
+    yield "one_expert", torch.full((2048, 8), 5, dtype=torch.int64), E
+    yield "empty", torch.zeros((0, 8), dtype=torch.int64), E
+    yield "e256", torch.randint(0, 256, (4096, 8), generator=g), 256
+    yield "e1", torch.randint(0, 2, (100, 3), generator=g), 1
+
+
+@pytest.mark.parametrize("drop_invalid", [False, True])
+def test_native_plan_equals_the_torch_counting_sort(cuda, drop_invalid):
+    """kernels.prefill_plan (one block, counting sort) against the torch restatement of the same sort run on the CPU:
+    order, inverse and groups identical, for skewed, ragged, out-of-range, one-expert, empty and 256-expert
+    routings."""
+    from drama3_b200 import kernels
+    for name, ids, n_exp in _ids_cases():
+        order, pos, groups = kernels.prefill_plan(ids.to(cuda), n_exp, drop_invalid)
+        want = offload.prefill_plan(ids, n_exp, drop_invalid)
+        assert torch.equal(order.cpu(), want[0]), name
+        assert torch.equal(pos.cpu(), want[1]), name
+        assert torch.equal(groups.cpu(), want[2]), name
