@@ -67,8 +67,13 @@ TRAFFIC_SOURCE = ("ncu capture of the 4-layer small case (bench.py --layers 4, m
                   "DRAM read + write / algorithmic bytes of the same launches")
 
 
-def kernel_of(kind):
-    """(kernel name, arithmetic) of the fused decode for `kind` banks."""
+def kernel_of(kind, lines=16):
+    """(kernel name, arithmetic) of the fused decode for `kind` banks at `lines` lines."""
+    if kind == "fp8c" and lines == 1:
+        return ("moe_decode_gv_kernel (mma.sync e4m3; one launch per layer: gate_up rows streamed by bulk copies, "
+                "SwiGLU, per-pair counters, down by (pair, row block), rank-order combine by last arrival)",
+                "e4m3 weights x e4m3 activation terms (two groups of three, the second scaled by 2^12: bf16 rows "
+                "exact, fp32 rows ~24 significant bits), f32 accumulation")
     if kind == "fp8c":
         return ("moe_decode_tc_kernel (tcgen05 kind::f8f6f4; one persistent launch per layer: plan, gate_up + "
                 "SwiGLU, down, combine)",
@@ -263,7 +268,7 @@ def decode_leg(kernels, device, kind, lines, steps, warmup, stream, n_layers, la
     gbs = b / (ms * 1e-3) / 1e9
     return {"tokens_per_s": lines / (ms * 1e-3), "ms_per_step": ms, "us_per_layer": 1e3 * ms / n_layers,
             "hbm_gbs": gbs, "frac": gbs / hbm_peak, "bytes_per_step": b, "format": FORMAT_NAMES[kind],
-            "lines": lines, "kernel": kernel_of(kind)[0]}
+            "lines": lines, "kernel": kernel_of(kind, lines)[0]}
 
 
 def reference_gpu_leg(device, kind, lines, steps, stream, n_layers, layers, cbs=(None, None)):

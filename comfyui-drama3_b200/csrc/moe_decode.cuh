@@ -52,10 +52,14 @@ __shared__ unsigned long long s_trace[32];
   if (threadIdx.x == 0) s_trace[slot] += (v)
 #define D3_ADD_EPI(slot, v) \
   if (threadIdx.x == DEC_WARPS * 32) s_trace[slot] += (v)
+// globaltimer at a milestone of a short kernel, straight into this CTA's row of the table
+#define D3_GSTAMP(slot) \
+  if (threadIdx.x == 0) g_trace[blockIdx.x][slot] = globaltimer()
 #else
 #define D3_STAMP(slot)
 #define D3_ADD(slot, v)
 #define D3_ADD_EPI(slot, v)
+#define D3_GSTAMP(slot)
 #endif
 
 constexpr int DEC_WARPS = 8;                       // consumer warps

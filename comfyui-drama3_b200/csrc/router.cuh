@@ -13,17 +13,10 @@
 
 #include <cooperative_groups.h>
 
+#include "moe_decode.cuh"
 #include "route.cuh"
 
 namespace d3 {
-
-#ifdef D3_TRACE
-// trace builds: globaltimer at a milestone, per CTA, into the trace table's given slot
-#define D3_GSTAMP(slot) \
-  if (threadIdx.x == 0) g_trace[blockIdx.x][slot] = globaltimer()
-#else
-#define D3_GSTAMP(slot)
-#endif
 
 constexpr int RT_CTAS = 8;     // the cluster: experts split over its CTAs
 constexpr int RT_WARPS = 8;    // the hidden dimension split over a CTA's warps
