@@ -1,5 +1,5 @@
-// One-line decode of per-channel e4m3 experts (fp8c): drama3/offload.py:108-123 (resident_decode) for one row, as a
-// streaming kernel shaped for that case. At one line every byte of the pairs' weights is used once by one column, so
+// One-line decode of e4m3 experts, per-channel (fp8c) or in the reference's 128 x 128 blocks (fp8):
+// drama3/offload.py:108-123 (resident_decode) for one row, as a streaming kernel shaped for that case. At one line every byte of the pairs' weights is used once by one column, so
 // the layer is bound by how early the bytes start to stream and how little waiting follows them; the tensor-core
 // decodes (built for 16 lines) spend more on their phase changes than on the bytes at one line.
 //
@@ -24,7 +24,9 @@
 // largest magnitude in [2^7, 2^8); terms 1-3 are successive roundings to 3 mantissa bits (subnormal steps of 2^-9
 // below 2^-6) with exact fp32 residuals; the residual after them is scaled by 2^12 and split the same way into terms
 // 4-6, whose columns are scaled back by 2^-12 after the MMA. A bf16 row is exact, an fp32 row keeps ~24 significant
-// bits; only magnitudes below 2^-29 of the row's largest are lost. The per-channel scale multiplies the fp32 dot.
+// bits; only magnitudes below 2^-29 of the row's largest are lost. The per-channel scale multiplies the fp32 dot; a
+// block scale multiplies the fp32 partial dot of its 128 columns (a warp's phase-1 columns are two blocks, a down row's
+// are I / 128), as the reference's block dequantization does before its fp32 sum.
 #pragma once
 
 #include "moe_decode.cuh"
@@ -163,8 +165,9 @@ D3_DEV bool gv_wait_at_least(const unsigned* p, unsigned target) {
 
 // Synchronization words (zero between calls; every call leaves them zero): a.depart[32 q] counts pair q's finished
 // units, a.depart[32 q + 16] its consumers that have passed the wait; a.arrive[rb] counts row block rb's pairs done.
-template <int I>
+template <int FMT, int I>
 __global__ void __launch_bounds__(GV_THREADS, 1) moe_decode_gv_kernel(const DecodeArgs a) {
+  constexpr bool BLK = FMT == FMT_FP8;  // scales per 128 x 128 block, else per output channel
   constexpr int UPP = I / GV_UNIT_CH;  // units per pair
   constexpr int P2P = gv_p2_pitch(I);
   constexpr int HPT = (I + GV_MMA_THREADS - 1) / GV_MMA_THREADS;
@@ -309,19 +312,39 @@ __global__ void __launch_bounds__(GV_THREADS, 1) moe_decode_gv_kernel(const Deco
     // the SwiGLU threads' scales (thread t < 16: unit t / 4, channel t % 4), loaded while the stage lands
     const int su = u_lo + GV_STAGE_UNITS * i + (tid >> 2);
     const bool swi = tid < 4 * units;
-    float sg = 0.0f, sup = 0.0f;
+    float sg = 1.0f, sup = 1.0f;
     int sv = 0, sch = 0;
     if (swi) {
       sv = su / UPP;
       sch = (su - sv * UPP) * GV_UNIT_CH + (tid & 3);
-      const float* sc = (const float*)a.s13 + (size_t)e_of[sv] * 2 * I;
-      sg = __ldg(sc + sch);
-      sup = __ldg(sc + I + sch);
+      if (!BLK) {
+        const float* sc = (const float*)a.s13 + (size_t)e_of[sv] * 2 * I;
+        sg = __ldg(sc + sch);
+        sup = __ldg(sc + I + sch);
+      }
+    }
+    // block scales: this lane's rows (g of units 2 tl, 2 tl + 1) over the warp's two column blocks
+    float bs[2][2][2] = {};  // [tile][row g / g + 8][block]
+    if (BLK) {
+      const int g = lane >> 2;
+#pragma unroll
+      for (int tl = 0; tl < 2; ++tl)
+#pragma unroll
+        for (int hr = 0; hr < 2; ++hr) {
+          const int uu = GV_STAGE_UNITS * i + 2 * tl + hr;
+          if (uu < n1) {
+            const int u = u_lo + uu, v = u / UPP, ch = (u - v * UPP) * GV_UNIT_CH + (g & 3);
+            const int row = e_of[v] * 2 * I + (g < 4 ? ch : I + ch);
+            const float* sc = (const float*)a.s13 + (size_t)(row / 128) * (GV_K / 128) + kw / 128;
+            bs[tl][hr][0] = __ldg(sc);
+            bs[tl][hr][1] = __ldg(sc + 1);
+          }
+        }
     }
     ok = mbar_wait(full + s, (i / GV_STAGES) & 1) && ok;
     if (i == 0) D3_GSTAMP(2);
     const uint8_t* st = ring + s * GV_STAGE_BYTES;
-    float acc[2][2][4] = {};  // [tile][chain]
+    float acc[2][2][2][4] = {};  // [tile][column block][chain]
     if (ok) {
 #pragma unroll
       for (int kb = 0; kb < GV_K / GV_WARPS; kb += 64) {
@@ -329,8 +352,8 @@ __global__ void __launch_bounds__(GV_THREADS, 1) moe_decode_gv_kernel(const Deco
         for (int tl = 0; tl < 2; ++tl) {
           if (tl == 0 || units > 2) {
             const uint8_t* lo = st + 16 * tl * GV_P1_PITCH;
-            gv_mma32(acc[tl][0], lo, lo + 8 * GV_P1_PITCH, GV_P1_PITCH, xt, GV_XPITCH, kw + kb);
-            gv_mma32(acc[tl][1], lo, lo + 8 * GV_P1_PITCH, GV_P1_PITCH, xt, GV_XPITCH, kw + kb + 32);
+            gv_mma32(acc[tl][kb >> 7][0], lo, lo + 8 * GV_P1_PITCH, GV_P1_PITCH, xt, GV_XPITCH, kw + kb);
+            gv_mma32(acc[tl][kb >> 7][1], lo, lo + 8 * GV_P1_PITCH, GV_P1_PITCH, xt, GV_XPITCH, kw + kb + 32);
           }
         }
       }
@@ -340,14 +363,27 @@ __global__ void __launch_bounds__(GV_THREADS, 1) moe_decode_gv_kernel(const Deco
     float* rbuf = red + (i & 1) * GV_WARPS * 32;
 #pragma unroll
     for (int tl = 0; tl < 2; ++tl) {
-      float t4[4];
+      float r_lo = 0.0f, r_hi = 0.0f;
+      if constexpr (BLK) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) t4[e] = acc[tl][0][e] + acc[tl][1][e];
-      float d_lo, d_hi;
-      gv_term_sums(t4, d_lo, d_hi);
+        for (int blk = 0; blk < 2; ++blk) {
+          float t4[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) t4[e] = acc[tl][blk][0][e] + acc[tl][blk][1][e];
+          float d_lo, d_hi;
+          gv_term_sums(t4, d_lo, d_hi);
+          r_lo += d_lo * bs[tl][0][blk];
+          r_hi += d_hi * bs[tl][1][blk];
+        }
+      } else {
+        float t4[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) t4[e] = (acc[tl][0][0][e] + acc[tl][0][1][e]) + (acc[tl][1][0][e] + acc[tl][1][1][e]);
+        gv_term_sums(t4, r_lo, r_hi);
+      }
       if ((lane & 3) == 0) {
-        rbuf[warp * 32 + 16 * tl + (lane >> 2)] = d_lo;
-        rbuf[warp * 32 + 16 * tl + (lane >> 2) + 8] = d_hi;
+        rbuf[warp * 32 + 16 * tl + (lane >> 2)] = r_lo;
+        rbuf[warp * 32 + 16 * tl + (lane >> 2) + 8] = r_hi;
       }
     }
     named_sync(1, GV_MMA_THREADS);
@@ -410,11 +446,24 @@ __global__ void __launch_bounds__(GV_THREADS, 1) moe_decode_gv_kernel(const Deco
     hv[i] = col < I ? __ldcg(a.a1 + (size_t)q2 * I + col) : 0.0f;
     m = fmaxf(m, fabsf(hv[i]));
   }
-  // this thread's down scales for its tile rows, loaded while the row lands
+  // this thread's down scales for its tile rows (per channel, or per 128-column block), loaded while the row lands
+  constexpr int NKB2 = I / 128;
   const int row_lo = r0 + 16 * warp + (lane >> 2), row_hi = row_lo + 8;
   const bool live_lo = 16 * warp + (lane >> 2) < rows2, live_hi = 16 * warp + (lane >> 2) + 8 < rows2;
-  const float* s2 = (const float*)a.s2 + (size_t)e_of[q2] * GV_K;
-  const float sc_lo = live_lo ? __ldg(s2 + row_lo) : 0.0f, sc_hi = live_hi ? __ldg(s2 + row_hi) : 0.0f;
+  float sc_lo[BLK ? NKB2 : 1], sc_hi[BLK ? NKB2 : 1];
+  if (BLK) {
+    const float* s2b = (const float*)a.s2;
+    const size_t blo = ((size_t)e_of[q2] * GV_K + row_lo) / 128 * NKB2, bhi = ((size_t)e_of[q2] * GV_K + row_hi) / 128 * NKB2;
+#pragma unroll
+    for (int kb = 0; kb < (BLK ? NKB2 : 1); ++kb) {
+      sc_lo[kb] = live_lo ? __ldg(s2b + blo + kb) : 0.0f;
+      sc_hi[kb] = live_hi ? __ldg(s2b + bhi + kb) : 0.0f;
+    }
+  } else {
+    const float* s2 = (const float*)a.s2 + (size_t)e_of[q2] * GV_K;
+    sc_lo[0] = live_lo ? __ldg(s2 + row_lo) : 0.0f;
+    sc_hi[0] = live_hi ? __ldg(s2 + row_hi) : 0.0f;
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   if (lane == 0) s_max[warp] = m;  // s_max's phase-1 readers all passed the barriers since
@@ -435,24 +484,38 @@ __global__ void __launch_bounds__(GV_THREADS, 1) moe_decode_gv_kernel(const Deco
   if (warp < nt2) {
     const int item = n1s + warp / (GV_P2_ROWS / 16), s = item % GV_STAGES;
     ok = mbar_wait(full + s, (item / GV_STAGES) & 1) && ok;
+    // four chains over the row's columns; with block scales, their term sums fold per column block (128)
+    float r_lo = 0.0f, r_hi = 0.0f;
+    const uint8_t* rows = ring + s * GV_STAGE_BYTES + (warp % (GV_P2_ROWS / 16)) * 16 * P2P;
     float acc[4][4] = {};
-    if (ok) {
-      const uint8_t* rows = ring + s * GV_STAGE_BYTES + (warp % (GV_P2_ROWS / 16)) * 16 * P2P;
 #pragma unroll
-      for (int kb = 0; kb < I; kb += 128) {
+    for (int kb = 0; kb < I; kb += 128) {
+      if (ok) {
 #pragma unroll
         for (int c4 = 0; c4 < 4; ++c4) gv_mma32(acc[c4], rows, rows + 8 * P2P, P2P, ht, P2P, kb + 32 * c4);
       }
-    }
-    float t4[4];
+      if constexpr (BLK) {
+        float t4[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) t4[i] = (acc[0][i] + acc[1][i]) + (acc[2][i] + acc[3][i]);
-    float d_lo, d_hi;
-    gv_term_sums(t4, d_lo, d_hi);
+        for (int e = 0; e < 4; ++e) t4[e] = (acc[0][e] + acc[1][e]) + (acc[2][e] + acc[3][e]);
+        float d_lo, d_hi;
+        gv_term_sums(t4, d_lo, d_hi);
+        r_lo += d_lo * sc_lo[kb / 128];
+        r_hi += d_hi * sc_hi[kb / 128];
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) acc[c4][0] = acc[c4][1] = acc[c4][2] = acc[c4][3] = 0.0f;
+      }
+    }
+    if constexpr (!BLK) {
+      float t4[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) t4[e] = (acc[0][e] + acc[1][e]) + (acc[2][e] + acc[3][e]);
+      gv_term_sums(t4, r_lo, r_hi);
+    }
     if ((lane & 3) == 0) {
       float* part = a.parts + (size_t)q2 * GV_K;
-      if (live_lo) part[row_lo] = d_lo * h_inv * sc_lo;
-      if (live_hi) part[row_hi] = d_hi * h_inv * sc_hi;
+      if (live_lo) part[row_lo] = r_lo * h_inv * (BLK ? 1.0f : sc_lo[0]);
+      if (live_hi) part[row_hi] = r_hi * h_inv * (BLK ? 1.0f : sc_hi[0]);
     }
   }
   named_sync(1, GV_MMA_THREADS);

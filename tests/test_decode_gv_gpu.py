@@ -97,3 +97,25 @@ def test_gv_decode_bad_id_zero_row_and_repeats(cuda):
     for _ in range(5):
         assert torch.equal(kernels.moe_decode("fp8c", x, ids, w, banks, workspace=ws), first)
     assert _lib.take_fault() == 0
+
+
+@pytest.mark.parametrize("I", [768, 512])
+@pytest.mark.parametrize("bf16", [True, False])
+def test_gv_decode_block_scaled_fp8(cuda, monkeypatch, I, bf16):
+    """The reference's fp8 layout (128 x 128 block scales) through the streaming kernel: against the oracle of the
+    reference's chain and against the mma.sync decode (D3_DECODE_GV=0) of the same call."""
+    banks = (gd.rand_bank("fp8", E, 2 * I, H, 130, cuda), gd.rand_bank("fp8", E, H, I, 131, cuda))
+    x = gd.rand_rows(1, H, 132, cuda)
+    if not bf16:
+        x = torch.randn((1, H), generator=torch.Generator().manual_seed(133)).to(cuda)
+    ids, w = gd.rand_routing(1, E, 8, 134, cuda)
+    _lib.take_fault()
+    monkeypatch.delenv("D3_DECODE_GV", raising=False)
+    gv = kernels.moe_decode("fp8", x, ids, w, banks)
+    monkeypatch.setenv("D3_DECODE_GV", "0")
+    old = kernels.moe_decode("fp8", x, ids, w, banks)
+    monkeypatch.delenv("D3_DECODE_GV")
+    torch.cuda.synchronize()
+    assert _lib.take_fault() == 0
+    assert close_to_oracle(gv, gd.oracle_decode("fp8", x, ids, w, banks, (None, None), H))
+    assert gd.rel_l2(gv.float(), old.float()) <= 1e-3
