@@ -79,6 +79,14 @@ def kernel_of(kind, lines=16):
                 "SwiGLU, down, combine)",
                 "e4m3 weights x e4m3 activation terms on the tensor cores, f32 accumulation: bf16 rows exact as two "
                 "terms, the fp32 SwiGLU rows of the down projection as four terms (16 significant bits)")
+    if kind == "w4a8" and lines == 1:
+        return ("moe_decode_gv_kernel (mma.sync s8; one launch per layer: int4 rows streamed by bulk copies and "
+                "expanded in registers, per-pair counters, down by (pair, row block), rank-order combine by last "
+                "arrival)", "int4 weights expanded to int8 x int8 per-row activations, s32 accumulation, bf16 group "
+                "scales folded per 128 columns")
+    if kind == "fp8" and lines == 1:
+        return ("moe_decode_gv_kernel (mma.sync e4m3; one launch per layer, block scales folded per 128 columns)",
+                "e4m3 weights x e4m3 activation terms (two groups of three), f32 accumulation")
     if kind == "w4a8":
         return ("moe_decode_tc8_kernel (tcgen05 kind::i8; one persistent launch per layer)",
                 "int4 weights expanded to int8 x int8 per-row activations on the tensor cores, s32 accumulation, "

@@ -536,7 +536,7 @@ static bool decode_gv_enabled() {
 template <int FMT, int I>
 static int decode_gv_launch(const d3::DecodeArgs& a, const DeviceInfo& d, cudaStream_t s) {
   auto kern = d3::moe_decode_gv_kernel<FMT, I>;
-  const int smem = d3::GvSmem::total(I);
+  const int smem = d3::GvSmem<FMT>::total(I);
   if (int st = allow_smem(kern, smem)) return st;
   return launch(kern, dim3(d.sms), dim3(d3::GV_THREADS), smem, s, true, a);
 }
@@ -646,12 +646,15 @@ static int decode_common(int fmt, const void* x, int x_bf16, int M, int k, int E
                       out, out_f32, e_first, e_count, (const d3::EpExchange*)exchange, words + 4, a1, parts, barrier,
                       words + 16, words + 128, words + 384, 0, 0, cap, lastarrive_nseg()};
   cudaStream_t s = (cudaStream_t)stream;
-  // e4m3 rows (per channel or in 128 x 128 blocks) at one line: the streaming kernel (its row blocks of
+  // e4m3 rows (per channel or in 128 x 128 blocks) and W4A8 at one line: the streaming kernel (its row blocks of
   // 2048 / (G / pairs) rows fit 8 tiles of 16 from 128 CTAs; its counters cover 256)
-  if ((fmt == d3::FMT_FP8C || fmt == d3::FMT_FP8) && M == 1 && k <= d3::GV_MAX_PAIRS && out && !out_f32 && !exchange &&
-      e_first == 0 && d.sms >= d3::GV_MIN_GRID && d.sms <= d3::DEC_MAX_GRID && decode_gv_enabled()) {
+  if ((fmt == d3::FMT_FP8C || fmt == d3::FMT_FP8 || fmt == d3::FMT_W4A8) && M == 1 && k <= d3::GV_MAX_PAIRS && out &&
+      !out_f32 && !exchange && e_first == 0 && d.sms >= d3::GV_MIN_GRID && d.sms <= d3::DEC_MAX_GRID &&
+      decode_gv_enabled()) {
     if (fmt == d3::FMT_FP8)
       return a.I == 768 ? decode_gv_launch<d3::FMT_FP8, 768>(a, d, s) : decode_gv_launch<d3::FMT_FP8, 512>(a, d, s);
+    if (fmt == d3::FMT_W4A8)
+      return a.I == 768 ? decode_gv_launch<d3::FMT_W4A8, 768>(a, d, s) : decode_gv_launch<d3::FMT_W4A8, 512>(a, d, s);
     return a.I == 768 ? decode_gv_launch<d3::FMT_FP8C, 768>(a, d, s) : decode_gv_launch<d3::FMT_FP8C, 512>(a, d, s);
   }
   // per-channel e4m3: the tensor-core kernel (its phase-2 split needs one CTA per segment at least: at most

@@ -119,3 +119,27 @@ def test_gv_decode_block_scaled_fp8(cuda, monkeypatch, I, bf16):
     assert _lib.take_fault() == 0
     assert close_to_oracle(gv, gd.oracle_decode("fp8", x, ids, w, banks, (None, None), H))
     assert gd.rel_l2(gv.float(), old.float()) <= 1e-3
+
+
+@pytest.mark.parametrize("I", [768, 512])
+@pytest.mark.parametrize("bf16", [True, False])
+@pytest.mark.parametrize("k", [8, 5])
+def test_gv_decode_w4a8(cuda, monkeypatch, I, bf16, k):
+    """W4A8 (int4 codes, bf16 group scales, int8 per-row activations) through the streaming kernel: against the oracle
+    of the format's definition (exact integer dots, so only the fp32 sums of the group partials and the output's bf16
+    rounding can differ) and against the tensor-core decode (D3_DECODE_GV=0)."""
+    banks = (gd.rand_bank("w4a8", E, 2 * I, H, 140 + k, cuda), gd.rand_bank("w4a8", E, H, I, 141 + k, cuda))
+    x = gd.rand_rows(1, H, 142 + k, cuda)
+    if not bf16:
+        x = torch.randn((1, H), generator=torch.Generator().manual_seed(143 + k)).to(cuda)
+    ids, w = gd.rand_routing(1, E, k, 144 + k, cuda)
+    _lib.take_fault()
+    monkeypatch.delenv("D3_DECODE_GV", raising=False)
+    gv = kernels.moe_decode("w4a8", x, ids, w, banks)
+    monkeypatch.setenv("D3_DECODE_GV", "0")
+    tc = kernels.moe_decode("w4a8", x, ids, w, banks)
+    monkeypatch.delenv("D3_DECODE_GV")
+    torch.cuda.synchronize()
+    assert _lib.take_fault() == 0
+    assert close_to_oracle(gv, gd.baseline_oracle_decode("w4a8", x, ids, w, banks))
+    assert gd.rel_l2(gv.float(), tc.float()) <= 1e-3
