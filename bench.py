@@ -84,6 +84,10 @@ def kernel_of(kind, lines=16):
                 "expanded in registers, per-pair counters, down by (pair, row block), rank-order combine by last "
                 "arrival)", "int4 weights expanded to int8 x int8 per-row activations, s32 accumulation, bf16 group "
                 "scales folded per 128 columns")
+    if kind == "int8" and lines == 1:
+        return ("moe_decode_gv_kernel (mma.sync s8; one launch per layer: ConvRot in registers, int8 rows streamed by "
+                "bulk copies, per-pair counters, rank-order combine by last arrival)",
+                "int8 weights x the rotated rows as three int8 terms (~21 significant bits), s32 accumulation")
     if kind == "fp8" and lines == 1:
         return ("moe_decode_gv_kernel (mma.sync e4m3; one launch per layer, block scales folded per 128 columns)",
                 "e4m3 weights x e4m3 activation terms (two groups of three), f32 accumulation")

@@ -1,6 +1,6 @@
 // One-line decode: drama3/offload.py:108-123 (resident_decode) for one row, as a streaming kernel shaped for that
-// case, for e4m3 experts per channel (fp8c) or in the reference's 128 x 128 blocks (fp8), and for W4A8 (int4 codes
-// two per byte, bf16 scales per 128 columns, int8 per-row activations). At one line every byte of the pairs' weights
+// case, for e4m3 experts per channel (fp8c) or in the reference's 128 x 128 blocks (fp8), for the reference's int8
+// ConvRot rows, and for W4A8 (int4 codes two per byte, bf16 scales per 128 columns, int8 per-row activations). At one line every byte of the pairs' weights
 // is used once by one column, so the layer is bound by how early the bytes start to stream and how little waiting
 // follows them; the tensor-core decodes (built for 16 lines) spend more on their phase changes than on the bytes.
 //
@@ -28,6 +28,12 @@
 // block scale multiplies the fp32 partial dot of its 128 columns (a warp's phase-1 columns are two blocks, a down
 // row's are I / 128), as the reference's block dequantization does before its fp32 sum.
 //
+// int8 ConvRot arithmetic (the reference's chain: rotate, gemv, rotate(SwiGLU), gemv): the row, and each pair's SwiGLU
+// row, rotated per 256 columns in registers (the radix-4 butterfly of the tensor-core int8 decode, tc_rotate16) and
+// written as three int8 terms of the rotated row scaled by a power of two that puts its largest magnitude in [32, 64)
+// (t1 = rint(y), t2 = rint(128 (y - t1)), t3 = rint(128 (128 (y - t1) - t2)): ~21 significant bits) in B's columns;
+// mma.sync m16n8k32 s8 x s8 -> s32 on the int8 rows as stored; D1 + D2 / 128 + D3 / 16384, then the row scale.
+//
 // W4A8 arithmetic (the format's definition, oracle.moe.gemm_wa8): the row, and each pair's SwiGLU row, quantized to
 // int8 by its own max (s = max / 127, q = rint(x / s) clipped, quant_i8_n); mma.sync m16n8k32 s8 x s8 -> s32, exact,
 // on the codes expanded in registers: packed byte b (columns 2j, 2j + 1) gives (b << 4) & 0xF0 and b & 0xF0, 16 x
@@ -36,7 +42,7 @@
 // group scale into an fp32 sum; the row's s / 16 multiplies the total.
 #pragma once
 
-#include "moe_decode.cuh"
+#include "decode_tc.cuh"
 
 namespace d3 {
 
@@ -61,6 +67,7 @@ __host__ __device__ constexpr int gv_pitch(int bytes) { return bytes + 16; }
 template <int FMT>
 struct GvFmt {
   static constexpr bool INT4 = false;
+  static constexpr bool ROT = false;
   static constexpr bool BLK = FMT == FMT_FP8;  // scales per 128 x 128 block, else per output channel
   static constexpr int ROW1 = GV_K;
   static constexpr int UNITS = 4;
@@ -68,7 +75,18 @@ struct GvFmt {
   __host__ __device__ static constexpr int row2(int I) { return I; }
 };
 template <>
+struct GvFmt<FMT_I8> {
+  static constexpr bool INT4 = false;
+  static constexpr bool BLK = false;
+  static constexpr bool ROT = true;  // ConvRot rows: the activations are rotated and split into int8 terms
+  static constexpr int ROW1 = GV_K;
+  static constexpr int UNITS = 4;
+  static constexpr int TERMS = 3;
+  __host__ __device__ static constexpr int row2(int I) { return I; }
+};
+template <>
 struct GvFmt<FMT_W4A8> {
+  static constexpr bool ROT = false;
   static constexpr bool INT4 = true;
   static constexpr bool BLK = false;
   static constexpr int ROW1 = GV_K / 2;
@@ -145,6 +163,58 @@ D3_DEV void gv_mma64_i4(int (&acc)[4], const uint8_t* lo, const uint8_t* hi, int
                b[0], b[1]);
   mma_s8_16832(acc, (w[2] << 4) & 0xF0F0F0F0u, (w[3] << 4) & 0xF0F0F0F0u, w[2] & 0xF0F0F0F0u, w[3] & 0xF0F0F0F0u,
                b[2], b[3]);
+}
+
+// acc += 16 int8 rows (rows 0-7 at `lo`, 8-15 at `hi`, pitch `pitch` bytes) x the three int8 activation terms at
+// `xt` (term t at xt + t * xpitch in B column t), over 32 columns from kb.
+D3_DEV void gv_mma32_i8(int (&acc)[4], const uint8_t* lo, const uint8_t* hi, int pitch, const uint8_t* xt, int xpitch,
+                        int kb) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+  uint32_t w[4];
+  ldsm_x4(w, ((lane >> 3) & 1 ? hi : lo) + (lane & 7) * pitch + kb + 16 * (lane >> 4));
+  uint32_t b0 = 0u, b1 = 0u;
+  if (g < 3) {
+    const uint8_t* xr = xt + g * xpitch + kb + 4 * c;
+    b0 = *reinterpret_cast<const uint32_t*>(xr);
+    b1 = *reinterpret_cast<const uint32_t*>(xr + 16);
+  }
+  mma_s8_16832(acc, w[0], w[1], w[2], w[3], b0, b1);
+}
+
+// The rows g and g + 8 of the three-term int8 sums (this lane's quad): D1 + D2 / 128 + D3 / 16384, every lane of the
+// quad gets the same values.
+D3_DEV void gv_i8_term_sums(const int (&acc)[4], float& r_lo, float& r_hi) {
+  const int c = threadIdx.x & 3;
+  // lane c holds columns 2c, 2c + 1: c = 0 has D1, D2; c = 1 has D3
+  float a = c == 0 ? (float)acc[0] + (float)acc[1] * 0.0078125f : c == 1 ? (float)acc[0] * 6.103515625e-05f : 0.0f;
+  float b = c == 0 ? (float)acc[2] + (float)acc[3] * 0.0078125f : c == 1 ? (float)acc[2] * 6.103515625e-05f : 0.0f;
+  a += __shfl_xor_sync(0xffffffffu, a, 1);
+  b += __shfl_xor_sync(0xffffffffu, b, 1);
+  a += __shfl_xor_sync(0xffffffffu, a, 2);
+  b += __shfl_xor_sync(0xffffffffu, b, 2);
+  r_lo = a;
+  r_hi = b;
+}
+
+// 16 values of a row (rotated, |v * scale| < 64) as three int8 terms, 16 bytes each into dst[t * pitch].
+D3_DEV void gv_i8_terms16(const float (&v)[16], float scale, uint8_t* dst, int pitch) {
+  uint32_t w[3][4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    w[0][p] = w[1][p] = w[2][p] = 0u;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float r = v[4 * p + i] * scale;
+#pragma unroll
+      for (int t = 0; t < 3; ++t) {
+        const float q8 = fminf(127.0f, fmaxf(-127.0f, rintf(r)));
+        w[t][p] |= ((uint32_t)(int)q8 & 0xFFu) << (8 * i);
+        r = (r - q8) * 128.0f;
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < 3; ++t) *reinterpret_cast<uint4*>(dst + t * pitch) = make_uint4(w[t][0], w[t][1], w[t][2], w[t][3]);
 }
 
 // Byte position of column j (0..31) of a 32-column chunk in the W4A8 activation order: even columns first.
@@ -249,7 +319,7 @@ D3_DEV float gv_group_scale(const void* scale, size_t row, int groups, int grp) 
 template <int FMT, int I>
 __global__ void __launch_bounds__(GV_THREADS, 1) moe_decode_gv_kernel(const DecodeArgs a) {
   using F = GvFmt<FMT>;
-  constexpr bool INT4 = F::INT4, GRP = F::INT4 || F::BLK;  // GRP: scales per 128-column group
+  constexpr bool INT4 = F::INT4, ROT = F::ROT, GRP = F::INT4 || F::BLK;  // GRP: scales per 128-column group
   using S = GvSmem<FMT>;
   constexpr int UNITS = F::UNITS, TPS = UNITS / 2;       // units and 16-row tiles per stage
   constexpr int STAGE = S::stage, RED = S::red_rows;
@@ -357,9 +427,27 @@ __global__ void __launch_bounds__(GV_THREADS, 1) moe_decode_gv_kernel(const Deco
     return;
   }
 
-  // ---- MMA warps: the row as terms (e4m3) or int8 codes (W4A8); xmul undoes the row's scaling after the sum
+  // ---- MMA warps: the row as terms (e4m3, rotated int8) or int8 codes (W4A8); xmul undoes the row's scaling
   float xmul;
-  {
+  if constexpr (ROT) {
+    // warps 0-3 rotate the row's 8 groups of 256 (a 16-lane half each, 16 contiguous columns a lane)
+    float v16[16];
+    const int col0 = 256 * (2 * warp + (lane >> 4)) + 16 * (lane & 15);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v16[i] = 0.0f;
+    if (warp < 4) {
+      tc_load16(a.x, a.x_bf16 != 0, col0, v16);
+      tc_rotate16(v16);
+    }
+    float m = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(v16[i]));
+    m = gv_block_max(m, s_max);
+    const int e = tc_exponent_i8(m);
+    xmul = gv_pow2(-e);
+    if (warp < 4) gv_i8_terms16(v16, gv_pow2(e), xt + col0, GV_XPITCH);
+    named_sync(1, GV_MMA_THREADS);
+  } else {
     float v[8];
     const int c0 = 8 * tid;
     if (a.x_bf16) {
@@ -465,6 +553,28 @@ __global__ void __launch_bounds__(GV_THREADS, 1) moe_decode_gv_kernel(const Deco
         r_lo[tl] = (float)acc[tl][0][0] * gs[tl][0][0] + (float)acc[tl][1][0] * gs[tl][0][1];
         r_hi[tl] = (float)acc[tl][0][2] * gs[tl][1][0] + (float)acc[tl][1][2] * gs[tl][1][1];
       }
+    } else if constexpr (ROT) {
+      int acc[TPS][2][4] = {};  // [tile][chain]
+      if (ok) {
+#pragma unroll
+        for (int kb = 0; kb < GV_K / GV_WARPS; kb += 64)
+#pragma unroll
+          for (int tl = 0; tl < TPS; ++tl)
+            if (2 * tl < units) {
+              const uint8_t* lo = st + 16 * tl * P1;
+              gv_mma32_i8(acc[tl][0], lo, lo + 8 * P1, P1, xt, GV_XPITCH, kw + kb);
+              gv_mma32_i8(acc[tl][1], lo, lo + 8 * P1, P1, xt, GV_XPITCH, kw + kb + 32);
+            }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty + s);  // the stage's bytes are in registers: hand it back before the sums
+#pragma unroll
+      for (int tl = 0; tl < TPS; ++tl) {
+        int t4[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) t4[e] = acc[tl][0][e] + acc[tl][1][e];
+        gv_i8_term_sums(t4, r_lo[tl], r_hi[tl]);
+      }
     } else {
       float acc[TPS][2][2][4] = {};  // [tile][column group][chain]
       if (ok) {
@@ -562,13 +672,27 @@ __global__ void __launch_bounds__(GV_THREADS, 1) moe_decode_gv_kernel(const Deco
   named_sync(1, GV_MMA_THREADS);
   ok = ok && s_flag != 0;
   D3_GSTAMP(4);
-  float hv[HPT];
+  // the pair's SwiGLU row: HPT strided values a thread, or (rotated int8) 16 contiguous values a lane of the warps
+  // holding its groups of 256
+  float hv[ROT ? 16 : HPT];
   float m = 0.0f;
+  const int hcol0 = 256 * (2 * warp + (lane >> 4)) + 16 * (lane & 15);
+  if constexpr (ROT) {
 #pragma unroll
-  for (int i = 0; i < HPT; ++i) {
-    const int col = tid + i * GV_MMA_THREADS;
-    hv[i] = col < I ? __ldcg(a.a1 + (size_t)q2 * I + col) : 0.0f;
-    m = fmaxf(m, fabsf(hv[i]));
+    for (int i = 0; i < 16; ++i) hv[i] = 0.0f;
+    if (2 * warp < I / 256) {  // warp-uniform: whole warps rotate (a half past the row's groups holds zeros)
+      if (hcol0 < I) tc_load16(a.a1 + (size_t)q2 * I, false, hcol0, (float(&)[16])hv);
+      tc_rotate16((float(&)[16])hv);
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(hv[i]));
+  } else {
+#pragma unroll
+    for (int i = 0; i < HPT; ++i) {
+      const int col = tid + i * GV_MMA_THREADS;
+      hv[i] = col < I ? __ldcg(a.a1 + (size_t)q2 * I + col) : 0.0f;
+      m = fmaxf(m, fabsf(hv[i]));
+    }
   }
   // this thread's down scales for its tile rows (per channel, or per 128-column group), loaded while the row lands
   const int row_lo = r0 + 16 * warp + (lane >> 2), row_hi = row_lo + 8;
@@ -589,7 +713,11 @@ __global__ void __launch_bounds__(GV_THREADS, 1) moe_decode_gv_kernel(const Deco
   }
   m = gv_block_max(m, s_max);  // s_max's phase-1 readers all passed the barriers since
   float hmul;
-  if constexpr (INT4) {
+  if constexpr (ROT) {
+    const int e = tc_exponent_i8(m);
+    hmul = gv_pow2(-e);
+    if (2 * warp < I / 256 && hcol0 < I) gv_i8_terms16((float(&)[16])hv, gv_pow2(e), ht + hcol0, HTP);
+  } else if constexpr (INT4) {
     const float sq = m / 127.0f;
     float q[HPT];
     quant_i8_n<HPT>(hv, sq, __frcp_rn(sq), q);
@@ -629,6 +757,20 @@ __global__ void __launch_bounds__(GV_THREADS, 1) moe_decode_gv_kernel(const Deco
         r_lo += (float)acc[0] * sc_lo[kb / 128];
         r_hi += (float)acc[2] * sc_hi[kb / 128];
       }
+    } else if constexpr (ROT) {
+      int acc[4][4] = {};
+      if (ok) {
+#pragma unroll
+        for (int kb = 0; kb < I; kb += 128)
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) gv_mma32_i8(acc[c4], rows, rows + 8 * P2, P2, ht, HTP, kb + 32 * c4);
+      }
+      int t4[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) t4[e] = (acc[0][e] + acc[1][e]) + (acc[2][e] + acc[3][e]);
+      gv_i8_term_sums(t4, r_lo, r_hi);
+      r_lo *= sc_lo[0];
+      r_hi *= sc_hi[0];
     } else {
       // four chains over the row's columns; with block scales, their term sums fold per column block (128)
       float acc[4][4] = {};

@@ -646,11 +646,13 @@ static int decode_common(int fmt, const void* x, int x_bf16, int M, int k, int E
                       out, out_f32, e_first, e_count, (const d3::EpExchange*)exchange, words + 4, a1, parts, barrier,
                       words + 16, words + 128, words + 384, 0, 0, cap, lastarrive_nseg()};
   cudaStream_t s = (cudaStream_t)stream;
-  // e4m3 rows (per channel or in 128 x 128 blocks) and W4A8 at one line: the streaming kernel (its row blocks of
+  // e4m3 rows (per channel or in 128 x 128 blocks), int8 ConvRot rows and W4A8 at one line: the streaming kernel (its row blocks of
   // 2048 / (G / pairs) rows fit 8 tiles of 16 from 128 CTAs; its counters cover 256)
-  if ((fmt == d3::FMT_FP8C || fmt == d3::FMT_FP8 || fmt == d3::FMT_W4A8) && M == 1 && k <= d3::GV_MAX_PAIRS && out &&
-      !out_f32 && !exchange && e_first == 0 && d.sms >= d3::GV_MIN_GRID && d.sms <= d3::DEC_MAX_GRID &&
-      decode_gv_enabled()) {
+  if ((fmt == d3::FMT_FP8C || fmt == d3::FMT_FP8 || fmt == d3::FMT_W4A8 || fmt == d3::FMT_I8) && M == 1 &&
+      k <= d3::GV_MAX_PAIRS && out && !out_f32 && !exchange && e_first == 0 && d.sms >= d3::GV_MIN_GRID &&
+      d.sms <= d3::DEC_MAX_GRID && decode_gv_enabled()) {
+    if (fmt == d3::FMT_I8)
+      return a.I == 768 ? decode_gv_launch<d3::FMT_I8, 768>(a, d, s) : decode_gv_launch<d3::FMT_I8, 512>(a, d, s);
     if (fmt == d3::FMT_FP8)
       return a.I == 768 ? decode_gv_launch<d3::FMT_FP8, 768>(a, d, s) : decode_gv_launch<d3::FMT_FP8, 512>(a, d, s);
     if (fmt == d3::FMT_W4A8)

@@ -143,3 +143,27 @@ def test_gv_decode_w4a8(cuda, monkeypatch, I, bf16, k):
     assert _lib.take_fault() == 0
     assert close_to_oracle(gv, gd.baseline_oracle_decode("w4a8", x, ids, w, banks))
     assert gd.rel_l2(gv.float(), tc.float()) <= 1e-3
+
+
+@pytest.mark.parametrize("I", [768, 512])
+@pytest.mark.parametrize("bf16", [True, False])
+def test_gv_decode_int8_convrot(cuda, monkeypatch, I, bf16):
+    """The reference's int8 ConvRot layout through the streaming kernel: the row and each pair's
+    SwiGLU row rotated in registers and written as three int8 terms; against the oracle of the reference's chain
+    (rotate, gemv, rotate(SwiGLU), gemv, weighted sum) and against the mma.sync decode (D3_DECODE_GV=0)."""
+    banks = (gd.rand_bank("int8", E, 2 * I, H, 150, cuda), gd.rand_bank("int8", E, H, I, 151, cuda))
+    x = gd.rand_rows(1, H, 152, cuda)
+    if not bf16:
+        x = torch.randn((1, H), generator=torch.Generator().manual_seed(153)).to(cuda)
+    ids, w = gd.rand_routing(1, E, 8, 154, cuda)
+    _lib.take_fault()
+    monkeypatch.delenv("D3_DECODE_GV", raising=False)
+    gv = kernels.moe_decode("int8", x, ids, w, banks)
+    monkeypatch.setenv("D3_DECODE_GV", "0")
+    old = kernels.moe_decode("int8", x, ids, w, banks)
+    monkeypatch.delenv("D3_DECODE_GV")
+    torch.cuda.synchronize()
+    assert _lib.take_fault() == 0
+    ref = gd.oracle_decode("int8", x, ids, w, banks, (None, None), H)
+    assert gd.rel_l2(gv.float(), ref) <= 1e-3
+    assert gd.rel_l2(gv.float(), old.float()) <= 1e-3
