@@ -65,6 +65,10 @@ CODEBOOK4 = (-1.0, -0.6962, -0.5251, -0.3949, -0.2844, -0.1848, -0.0911, 0.0, 0.
 TRAFFIC_RATIO = (407.196928 + 5.279488 + 411.930368 + 4.855552) / (407.164416 + 411.897344)
 TRAFFIC_SOURCE = ("ncu capture of the 4-layer small case (bench.py --layers 4, moe_decode_tc_kernel, 2 launches): "
                   "DRAM read + write / algorithmic bytes of the same launches")
+# the same for the one-line decode (bench.py --layers 4 --lines 1, moe_decode_gv_kernel, 2 launches of 37.87 MB)
+TRAFFIC_RATIO_1 = (37.934848 + 0.035840 + 37.934592 + 0.027392) / (2 * 37.871712)
+TRAFFIC_SOURCE_1 = ("ncu capture of the 4-layer one-line case (bench.py --layers 4 --lines 1, moe_decode_gv_kernel, "
+                    "2 launches): DRAM read + write / algorithmic bytes of the same launches")
 
 
 def kernel_of(kind, lines=16):
@@ -1030,13 +1034,14 @@ def main():
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-                "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": kernel_of(kind)[1],
+                "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": kernel_of(kind, args.lines)[1],
                 "data": "synthetic (seeded random banks)", "config": config(args, world),
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                              "frac": achieved / hbm_peak, "peak_kind": peak_kind,
-                             "traffic": TRAFFIC_RATIO * step_bytes / n_layers,
-                             "traffic_unit": "bytes per launch", "traffic_source": TRAFFIC_SOURCE,
-                             "kernel": kernel_of(kind)[0],
+                             "traffic": (TRAFFIC_RATIO_1 if args.lines == 1 else TRAFFIC_RATIO) * step_bytes
+                             / n_layers, "traffic_unit": "bytes per launch",
+                             "traffic_source": TRAFFIC_SOURCE_1 if args.lines == 1 else TRAFFIC_SOURCE,
+                             "kernel": kernel_of(kind, args.lines)[0],
                              "bytes_per_launch": step_bytes / n_layers, "us_per_layer": 1e3 * ms / n_layers,
                              "launch_time": "step time / layers: the launches run back to back in one graph",
                              "bytes_of": "rank 0's experts" if world > 1 else "all routed experts"},
