@@ -58,9 +58,11 @@ def local_exchanges(world, m_max, device):
 
 
 @pytest.mark.parametrize("kind", ["fp8c", "w4a8"])
-def test_exchange_one_rank_equals_moe_decode(cuda, kind):
-    """World 1: the partial pushed into the area and reduced is moe_decode's output bit for bit, over calls of both
-    parities and fewer lines than the area holds."""
+def test_exchange_one_rank_equals_moe_decode(cuda, monkeypatch, kind):
+    """World 1: the partial pushed into the area and reduced is the tensor-core decode's output bit for bit (the
+    exchanged decode runs that kernel at every line count; D3_DECODE_GV=0 makes moe_decode run it at one line too),
+    over calls of both parities and fewer lines than the area holds."""
+    monkeypatch.setenv("D3_DECODE_GV", "0")
     banks = (gd.rand_bank(kind, E, 2 * I, H, 200, cuda), gd.rand_bank(kind, E, H, I, 201, cuda))
     areas, (st,) = local_exchanges(1, 16, cuda)  # the areas stay referenced while the structs point at them
     _lib.take_fault()
