@@ -85,20 +85,6 @@ D3_DEV void umma_f8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t id
       : "memory");
 }
 
-// Instruction descriptor, kind::i8: s32 accumulator, signed 8-bit A and B, both K-major, M = 128, N = n.
-D3_DEV uint32_t t8_idesc(int n) {
-  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-}
-
-D3_DEV void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
 // One MMA of the tensor-core decode: kind::i8 (s32 accumulators) for int8 rows, kind::f8f6f4 (f32) for e4m3 rows.
 template <bool I8>
 D3_DEV void tc_umma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {

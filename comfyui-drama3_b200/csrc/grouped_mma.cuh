@@ -66,7 +66,7 @@ struct GroupedTile {
   int group;  // index into groups[]
   int row0;   // first sorted row of the tile
   int rows;   // rows in the tile (1..128)
-  int pad;
+  int slot;   // the group's slot (its expert's index in the bank): groups[5 group + 1]
 };
 
 // Byte offset of 16-byte chunk c (columns 8c..8c+7 of a 64-column chunk) of row r in a K-major, 128-byte-swizzled
@@ -85,8 +85,9 @@ __host__ __device__ constexpr size_t gm_workspace_bytes(int tiles, int K) {
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// Staging: one block (8 warps) per tile slot. Block t finds its (group, tile of the group) from the groups' row
-// counts, writes the tile table entry, and converts the tile's rows (zeros past the group's end, up to the MMA width)
+// Staging: one block (8 warps) per (tile slot, 16-row slice of the tile), so a full tile's rows are spread over 8 SMs'
+// blocks. Block (t, s) finds its (group, tile of the group) from the groups' row counts, slice 0 writes the tile table
+// entry, and the block converts its slice of the tile's rows (zeros past the group's end, up to the MMA width)
 // to the hi / lo f16 operand blocks plus inv[row] = 2^-e (times 1/16 after a rotation; 0 for padding rows). Block 0
 // also writes the number of tiles. A warp owns a row: its K values sit in registers (lane l holds columns
 // 256 q + 8 l .. + 7), so the row's bound is exact.
@@ -97,8 +98,9 @@ __host__ __device__ constexpr size_t gm_workspace_bytes(int tiles, int K) {
 //        drama3/kernels.py:240-256), the 1/16 folded into inv
 // Needs K % 256 == 0, K <= 2048.
 //   mode bit GM_INT8 (W4A8 / W6A8): the row is quantized to int8 by its exact max (s = max / 127, q = rint(x / s)
-//        clamped, IEEE division) and staged as one exact f16 term; inv = s
+//        clamped, IEEE division) and staged as int8 operand blocks of 128 columns for kind::i8; inv = s
 enum { GM_ROTATE = 1, GM_SWIGLU = 2, GM_INT8 = 4 };
+constexpr int GM_STAGE_ROWS = 16;  // rows of a tile per staging block (grid: tile slots x GM_NT / GM_STAGE_ROWS)
 
 D3_DEV float gm_load(const void* x, bool bf16, size_t i) {
   return bf16 ? bf16_to_f32(((const uint16_t*)x)[i]) : ((const float*)x)[i];
@@ -129,7 +131,7 @@ __global__ void __launch_bounds__(256) gm_stage_kernel(const void* __restrict__ 
   __shared__ int s_group, s_local, s_total;
   __shared__ float scratch[8][256];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x;
+  const int t = blockIdx.x, slice = blockIdx.y;
   if (warp == 0) {
     int base = 0, found_g = -1, found_l = 0;
     for (int c0 = 0; c0 < G; c0 += 32) {
@@ -156,7 +158,7 @@ __global__ void __launch_bounds__(256) gm_stage_kernel(const void* __restrict__ 
       s_group = found_g;
       s_local = found_l;
       s_total = base;
-      if (t == 0) {
+      if (t == 0 && slice == 0) {
         *ntiles = min(base, max_tiles);
         if (base > max_tiles) record_fault(FAULT_TILES);
       }
@@ -167,15 +169,16 @@ __global__ void __launch_bounds__(256) gm_stage_kernel(const void* __restrict__ 
   const int g = s_group;
   const int first = groups[5 * g + 3], count = groups[5 * g + 4];
   const int row0 = first + s_local * GM_NT, rows = min(GM_NT, count - s_local * GM_NT);
-  if (threadIdx.x == 0) table[t] = GroupedTile{g, row0, rows, 0};
+  if (threadIdx.x == 0 && slice == 0) table[t] = GroupedTile{g, row0, rows, groups[5 * g + 1]};
   const bool bf16 = src_bf16 != 0, rotate = (mode & GM_ROTATE) != 0, swiglu = (mode & GM_SWIGLU) != 0;
   const bool int8q = (mode & GM_INT8) != 0;
   const int nkc = K / GM_KC, nq = K / 256;
   const size_t pitch = swiglu ? 2 * (size_t)K : (size_t)K;
   uint8_t* tile_base = staged + (size_t)t * nkc * 2 * GM_B_BYTES;
   const int width = (rows + 15) & ~15;  // rows the GEMM reads (its MMA N)
+  const int j_end = min(width, GM_STAGE_ROWS * (slice + 1));
   float* row = scratch[warp];
-  for (int j = warp; j < width; j += 8) {
+  for (int j = GM_STAGE_ROWS * slice + warp; j < j_end; j += 8) {
     const bool live = j < rows;
     const size_t src_row = live ? (size_t)(row_index ? row_index[row0 + j] : row0 + j) : 0;
     float v[8][8];
@@ -228,19 +231,19 @@ __global__ void __launch_bounds__(256) gm_stage_kernel(const void* __restrict__ 
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       if (q >= nq) break;
-      uint32_t hw[4], lw[4];
       if (int8q) {
+        // int8 operand blocks of 128 columns (one per kind::i8 MMA chunk, GM_B_BYTES apart): columns 256q + 8 lane
+        // .. + 7 are chunk 2q + lane / 16, the (lane & 1) half of 16-byte piece (lane % 16) / 2
         float qv[8];
         quant_i8_n<8>(v[q], qs, __frcp_rn(qs), qv);
+        uint32_t b[2] = {0u, 0u};
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float q0 = qv[2 * u];
-          const float q1 = qv[2 * u + 1];
-          hw[u] = (uint32_t)__half_as_ushort(__float2half_rn(q0)) |
-                  ((uint32_t)__half_as_ushort(__float2half_rn(q1)) << 16);
-          lw[u] = 0u;
-        }
-      } else {
+        for (int u = 0; u < 8; ++u) b[u >> 2] |= ((uint32_t)(int)qv[u] & 0xFFu) << (8 * (u & 3));
+        uint8_t* blk = tile_base + (size_t)(2 * q + (lane >> 4)) * GM_B_BYTES;
+        *(uint2*)(blk + sw128_offset(j, (lane & 15) >> 1) + 8 * (lane & 1)) = make_uint2(b[0], b[1]);
+        continue;
+      }
+      uint32_t hw[4], lw[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const float s0 = v[q][2 * u] * scale, s1 = v[q][2 * u + 1] * scale;
@@ -248,7 +251,6 @@ __global__ void __launch_bounds__(256) gm_stage_kernel(const void* __restrict__ 
         hw[u] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
         const __half l0 = __float2half_rn(s0 - __half2float(h0)), l1 = __float2half_rn(s1 - __half2float(h1));
         lw[u] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
-      }
       }
       // columns 256q + 8 lane .. + 7: chunk kc = 4q + lane / 8, 16-byte piece c = lane % 8
       const int kc = 4 * q + (lane >> 3), c = lane & 7;
@@ -315,6 +317,20 @@ D3_DEV void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t i
       : "memory");
 }
 
+// Instruction descriptor, kind::i8: s32 accumulator, signed 8-bit A and B, both K-major, M = 128, N = n.
+D3_DEV uint32_t t8_idesc(int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+D3_DEV void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive on `bar` once every tcgen05.mma this thread issued so far has completed.
 D3_DEV void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -375,6 +391,14 @@ struct GmArgs {
   int bank_rows;           // rows in the bank (E*N): slot indices beyond it are skipped
 };
 
+constexpr int GM_UNIT_CAP = 64;  // units per CTA whose description is cached in shared memory
+
+// One unit as every role needs it: the weight rows' first bank row (wrow < 0: skipped; -1 also records a bad slot),
+// the tile, its rows and its first sorted row.
+struct GmUnit {
+  int wrow, tile, rows, row0;
+};
+
 struct GmSmem {
   static constexpr int a = 0;
   static constexpr int b = a + GM_MMA_ST * GM_A_BYTES;
@@ -384,7 +408,8 @@ struct GmSmem {
   static constexpr int nbars = 2 * GM_RAW_ST + 3 * GM_MMA_ST + 4;
   static constexpr int tmem = bars + nbars * 8;
   static constexpr int lut = tmem + 16;
-  static constexpr int total = lut + 64;
+  static constexpr int units = lut + 64;  // GmUnit [GM_UNIT_CAP]: this CTA's first units
+  static constexpr int total = units + GM_UNIT_CAP * 16;
   static constexpr int launch = total + 1024;  // slack to align the base to 1024 bytes
 };
 
@@ -406,6 +431,27 @@ D3_DEV bool gm_unit(const GmArgs& a, int ntiles, int u, int& tile, int& rb) {
   if (u >= ntiles * RB || u >= a.max_units) return false;
   tile = u / RB;
   rb = u - tile * RB;
+  return true;
+}
+
+// Unit u's description, read from the tile table.
+D3_DEV GmUnit gm_unit_read(const GmArgs& a, int tile, int rb) {
+  const GroupedTile tl = a.table[tile];
+  const int wrow = tl.slot * a.N + rb * GM_M;
+  GmUnit g;
+  g.wrow = tl.slot < 0 || wrow >= a.bank_rows ? -1 : wrow + GM_M > a.bank_rows ? -2 : wrow;
+  g.tile = tile;
+  g.rows = tl.rows;
+  g.row0 = tl.row0;
+  return g;
+}
+
+// The CTA's i-th unit (u = blockIdx.x + i * gridDim.x): from the shared-memory cache for the first GM_UNIT_CAP,
+// read from the table past them; false past the end.
+D3_DEV bool gm_unit_at(const GmArgs& a, const GmUnit* cache, int ntiles, int i, GmUnit& out) {
+  int tile, rb;
+  if (!gm_unit(a, ntiles, blockIdx.x + i * gridDim.x, tile, rb)) return false;
+  out = i < GM_UNIT_CAP ? cache[i] : gm_unit_read(a, tile, rb);
   return true;
 }
 
@@ -493,6 +539,57 @@ D3_DEV void gm_convert(const uint8_t* raw, int h, uint8_t* astage, int r, uint32
   }
 }
 
+// W4A8 / W6A8 on kind::i8: a raw stage's weight row r (128 columns) as int8 into the A stage, K-major with the
+// 128-byte swizzle, 16 columns per 16-byte piece. Each code becomes an exact int8 multiple of itself placed in the
+// byte's high bits (int4: 16 x code, int6: 4 x code); gm_i8_unscale undoes the factor in the fold.
+template <int FMT>
+D3_DEV void gm_convert_i8(const uint8_t* raw, uint8_t* astage, int r) {
+  if (FMT == FMT_W6A8) {
+    // 96-byte rows, no swizzle: 16-column group g is 12 bytes (three words) at 12 g; four 6-bit codes per 24 bits
+    const uint4* row = (const uint4*)(raw + r * 96);
+    uint32_t w[24];
+#pragma unroll
+    for (int i = 0; i < 6; ++i) {
+      const uint4 q = row[i];
+      w[4 * i] = q.x; w[4 * i + 1] = q.y; w[4 * i + 2] = q.z; w[4 * i + 3] = q.w;
+    }
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      const uint32_t w0 = w[3 * g], w1 = w[3 * g + 1], w2 = w[3 * g + 2];
+      const uint32_t t[4] = {w0, __funnelshift_r(w0, w1, 24), __funnelshift_r(w1, w2, 16), w2 >> 8};
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        o[i] = ((t[i] << 2) & 0xFCu) | ((t[i] << 4) & 0xFC00u) | ((t[i] << 6) & 0xFC0000u) |
+               ((t[i] << 8) & 0xFC000000u);
+      *(uint4*)(astage + sw128_offset(r, g)) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  } else {
+    // 64-byte rows with the hardware swizzle of their width (16-byte chunk c of row r at c ^ ((r / 2) % 4)):
+    // group g is 8 bytes, byte i holding columns 2i (low nibble) and 2i + 1
+    const uint8_t* low = raw + r * 64;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      const uint2 lw = *(const uint2*)(low + (((g >> 1) ^ ((r >> 1) & 3)) << 4) + 8 * (g & 1));
+      const uint32_t wv[2] = {lw.x, lw.y};
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const uint32_t lo = (wv[i] << 4) & 0xF0F0F0F0u, hi = wv[i] & 0xF0F0F0F0u;
+        o[2 * i] = __byte_perm(lo, hi, 0x5140);
+        o[2 * i + 1] = __byte_perm(lo, hi, 0x7362);
+      }
+      *(uint4*)(astage + sw128_offset(r, g)) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+// The factor gm_convert_i8 put on every code, undone: 1/4 (int6), 1/16 (int4). Powers of two, so exact.
+template <int FMT>
+__host__ __device__ constexpr float gm_i8_unscale() {
+  return FMT == FMT_W6A8 ? 0.25f : 0.0625f;
+}
+
 template <int FMT>
 __global__ void __launch_bounds__(GM_THREADS, 1)
     grouped_mma_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap pmap, GmArgs a) {
@@ -533,12 +630,25 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
   }
   if (FMT == FMT_W4 && threadIdx.x < 16) lut[threadIdx.x] = a.codebook[threadIdx.x];
   if (warp == 2) tmem_alloc(tmem_slot, GM_TMEM_COLS);
+  const int ntiles = *a.ntiles;
+  // the CTA's first units, described once for every role (one table read each, all in flight together)
+  GmUnit* units = (GmUnit*)(smem + GmSmem::units);
+  if (threadIdx.x < GM_UNIT_CAP) {
+    int tile, rb;
+    if (gm_unit(a, ntiles, blockIdx.x + threadIdx.x * gridDim.x, tile, rb))
+      units[threadIdx.x] = gm_unit_read(a, tile, rb);
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int ntiles = *a.ntiles;
-  const int nkc = a.K / GM_KC;
+  // W4A8 / W6A8 (int8 activations) run kind::i8: int8 A and B, 128 columns (128 bytes of a row) per MMA chunk, one
+  // raw stage each; the other formats run kind::f16 with 64 columns per chunk, two chunks per raw stage
+  constexpr bool I8 = fmt_a8(FMT);
+  constexpr int KC = I8 ? 128 : GM_KC;
+  const int nkc = a.K / KC;
+  const size_t tile_bytes = (size_t)(a.K / GM_KC) * 2 * GM_B_BYTES;  // staged bytes per tile (the f16 layout's)
+  constexpr int chunk_bytes = I8 ? GM_B_BYTES : 2 * GM_B_BYTES;      // staged bytes per chunk
   const int G = gridDim.x;
   bool ok = true;
 
@@ -547,11 +657,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     if (lane == 0) {
       int rs = 0;
       uint32_t rph = 0;
-      int tile, rb;
-      for (int u = blockIdx.x; ok && gm_unit(a, ntiles, u, tile, rb); u += G) {
-        const int slot = a.groups[5 * a.table[tile].group + 1];
-        const int wrow = slot * a.N + rb * GM_M;
-        if (slot < 0 || wrow + GM_M > a.bank_rows) continue;
+      GmUnit un;
+      for (int i = 0; ok && gm_unit_at(a, units, ntiles, i, un); ++i) {
+        const int wrow = un.wrow;
+        if (wrow < 0) continue;
         for (int kr = 0; kr < a.K / GM_RKC && ok; ++kr) {
           {
             GM_T0();
@@ -584,12 +693,11 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       const uint64_t keep = policy_evict_last();
       int ms = 0;
       uint32_t mph = 0;
-      int tile, rb;
-      for (int u = blockIdx.x; ok && gm_unit(a, ntiles, u, tile, rb); u += G) {
-        const int slot = a.groups[5 * a.table[tile].group + 1];
-        if (slot < 0 || slot * a.N + rb * GM_M + GM_M > a.bank_rows) continue;
-        const uint8_t* src = a.staged + (size_t)tile * nkc * 2 * GM_B_BYTES;
-        const uint32_t bytes = (uint32_t)gm_width(a.table[tile].rows) * 128u;  // rows x 64 f16 per term
+      GmUnit un;
+      for (int i = 0; ok && gm_unit_at(a, units, ntiles, i, un); ++i) {
+        if (un.wrow < 0) continue;
+        const uint8_t* src = a.staged + (size_t)un.tile * tile_bytes;
+        const uint32_t bytes = (uint32_t)gm_width(un.rows) * 128u;  // rows x 128 bytes per term
         for (int kc = 0; kc < nkc && ok; ++kc) {
           {
             GM_T0();
@@ -598,7 +706,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
           }
           if (!ok) break;
           uint8_t* dst = smem + GmSmem::b + ms * 2 * GM_B_BYTES;
-          const uint8_t* blk = src + (size_t)kc * 2 * GM_B_BYTES;
+          const uint8_t* blk = src + (size_t)kc * chunk_bytes;
           mbar_arrive_expect_tx(b_full + ms, fmt_a8(FMT) ? bytes : 2 * bytes);
           bulk_g2s(dst, blk, bytes, b_full + ms, keep);
           if (!fmt_a8(FMT)) bulk_g2s(dst + GM_B_BYTES, blk + GM_B_BYTES, bytes, b_full + ms, keep);
@@ -614,13 +722,12 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     if (lane == 0) {
       int ms = 0, folds = 0;
       uint32_t mph = 0;
-      const int kbc = gm_folds<FMT>() ? 128 / GM_KC : nkc;  // chunks per fold
-      int tile, rb;
-      for (int u = blockIdx.x; ok && gm_unit(a, ntiles, u, tile, rb); u += G) {
-        const int slot = a.groups[5 * a.table[tile].group + 1];
-        if (slot < 0 || slot * a.N + rb * GM_M + GM_M > a.bank_rows) continue;
+      const int kbc = gm_folds<FMT>() ? 128 / KC : nkc;  // chunks per fold
+      GmUnit un;
+      for (int i = 0; ok && gm_unit_at(a, units, ntiles, i, un); ++i) {
+        if (un.wrow < 0) continue;
         uint32_t acc = 0;
-        const uint32_t idesc = gm_idesc(gm_width(a.table[tile].rows));
+        const uint32_t idesc = I8 ? t8_idesc(gm_width(un.rows)) : gm_idesc(gm_width(un.rows));
         for (int kc = 0; kc < nkc && ok; ++kc) {
           if (kc % kbc == 0) {
             const int region = folds & 1;
@@ -648,10 +755,15 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
           const uint32_t as = smem_u32(smem + GmSmem::a + ms * GM_A_BYTES);
           const uint32_t bs = smem_u32(smem + GmSmem::b + ms * 2 * GM_B_BYTES);
 #pragma unroll
-          for (int ks = 0; ks < GM_KC / 16; ++ks) {
+          for (int ks = 0; ks < 4; ++ks) {  // K steps of 32 bytes: 16 f16 or 32 int8 columns
             const uint64_t ad = umma_desc_sw128(as + 32 * ks);
-            umma_f16(acc, ad, umma_desc_sw128(bs + 32 * ks), idesc, (kc % kbc != 0 || ks != 0) ? 1u : 0u);
-            if (!fmt_a8(FMT)) umma_f16(acc, ad, umma_desc_sw128(bs + GM_B_BYTES + 32 * ks), idesc, 1u);
+            const uint32_t accumulate = (kc % kbc != 0 || ks != 0) ? 1u : 0u;
+            if (I8) {
+              umma_i8(acc, ad, umma_desc_sw128(bs + 32 * ks), idesc, accumulate);
+            } else {
+              umma_f16(acc, ad, umma_desc_sw128(bs + 32 * ks), idesc, accumulate);
+              if (!fmt_a8(FMT)) umma_f16(acc, ad, umma_desc_sw128(bs + GM_B_BYTES + 32 * ks), idesc, 1u);
+            }
           }
           umma_commit(mma_empty + ms);
           if (kc % kbc == kbc - 1) {
@@ -670,20 +782,23 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     const int r = threadIdx.x - GM_CONV0 * 32;
     int rs = 0, ms = 0;
     uint32_t rph = 0, mph = 0;
-    int tile, rb;
-    for (int u = blockIdx.x; ok && gm_unit(a, ntiles, u, tile, rb); u += G) {
-      const int slot = a.groups[5 * a.table[tile].group + 1];
-      const int wrow = slot * a.N + rb * GM_M;
-      if (slot < 0 || wrow + GM_M > a.bank_rows) continue;
+    GmUnit un;
+    for (int i = 0; ok && gm_unit_at(a, units, ntiles, i, un); ++i) {
+      const int wrow = un.wrow;
+      if (wrow < 0) continue;
       const uint8_t* srow = FMT == FMT_W4 || FMT == FMT_W6
                                 ? (const uint8_t*)a.scale + (size_t)(wrow + r) * (a.K / 16)
                                 : nullptr;
+      // W4 / W6 group scales: four bytes a chunk, loaded one chunk ahead of their use
+      uint32_t snext = srow ? __ldg((const uint32_t*)srow) : 0u;
       for (int kc = 0; kc < nkc && ok; ++kc) {
         const int h = kc & 1;
-        const uint32_t sbytes = srow ? __ldg((const uint32_t*)(srow + 4 * kc)) : 0u;
+        const bool first = I8 || h == 0, last = I8 || h == 1;  // this chunk's raw stage: first / last use
+        const uint32_t sbytes = snext;
+        if (srow && kc + 1 < nkc) snext = __ldg((const uint32_t*)(srow + 4 * (kc + 1)));
         {
           GM_T0();
-          ok = (h == 1 || mbar_wait(raw_full + rs, rph));
+          ok = (!first || mbar_wait(raw_full + rs, rph));
           if (r == 0) GM_TADD(5);
         }
         {
@@ -694,17 +809,20 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         if (!ok) break;
         {
           GM_T0();
-          gm_convert<FMT>(smem + GmSmem::raw + rs * GM_RAW_BYTES, h, smem + GmSmem::a + ms * GM_A_BYTES, r, sbytes,
-                          lut);
+          if constexpr (I8)
+            gm_convert_i8<FMT>(smem + GmSmem::raw + rs * GM_RAW_BYTES, smem + GmSmem::a + ms * GM_A_BYTES, r);
+          else
+            gm_convert<FMT>(smem + GmSmem::raw + rs * GM_RAW_BYTES, h, smem + GmSmem::a + ms * GM_A_BYTES, r,
+                            sbytes, lut);
           if (r == 0) GM_TADD(10);
         }
         fence_async_smem();
         __syncwarp();
         if (lane == 0) {
-          if (h == 1) mbar_arrive(raw_empty + rs);
+          if (last) mbar_arrive(raw_empty + rs);
           mbar_arrive(a_full + ms);
         }
-        if (h == 1 && ++rs == GM_RAW_ST) {
+        if (last && ++rs == GM_RAW_ST) {
           rs = 0;
           rph ^= 1;
         }
@@ -719,28 +837,68 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     const int quarter = warp & 3;
     const int r = 32 * quarter + lane;
     const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
-    const int kbc = gm_folds<FMT>() ? 128 / GM_KC : nkc;
-    const int nfold = nkc / kbc;
+    const int kbc = gm_folds<FMT>() ? 128 / KC : nkc;
+    const int nfold = nkc / kbc;  // at most 16 (K <= 2048)
+    // fold f's scale of the unit whose weight rows start at wrow: the 128 x 128 block's (fp8), or this row's bf16
+    // group scale times the int8 expansion's 1/4 or 1/16 (W4A8 / W6A8); loaded one fold ahead of its use
+    auto fold_scale = [&](int wrow, int f) -> float {
+      if (FMT == FMT_FP8) return __ldg((const float*)a.scale + (size_t)(wrow / 128) * (a.K / 128) + f);
+      return bf16_to_f32(__ldg((const uint16_t*)a.scale + (size_t)(wrow + r) * (a.K / 128) + f)) *
+             gm_i8_unscale<FMT>();
+    };
     int folds = 0;
-    int tile, rb;
-    for (int u = blockIdx.x; ok && gm_unit(a, ntiles, u, tile, rb); u += G) {
-      const GroupedTile tl = a.table[tile];
-      const int slot = a.groups[5 * tl.group + 1];
-      const int wrow = slot * a.N + rb * GM_M;
-      if (slot < 0 || wrow + GM_M > a.bank_rows) {
-        if (slot < 0 || wrow >= a.bank_rows) record_fault(FAULT_BAD_SLOT);
-        continue;
-      }
-      const float* inv = a.inv + (size_t)tile * GM_NT;
-      float* dst = a.out + (size_t)tl.row0 * a.N + rb * GM_M + r;
-      if (gm_folds<FMT>()) {
-        // one fold per 128 columns: acc += scale x partial (fp8: the 128 x 128 block's; W4A8 / W6A8: the row's
-        // bf16 group scale)
-        float acc[GM_NT];
+    GmUnit un;
+    for (int i = 0; ok && gm_unit_at(a, units, ntiles, i, un); ++i) {
+      if (un.wrow < 0) {
+        if (un.wrow == -1) record_fault(FAULT_BAD_SLOT);
+      } else {
+        const float* inv = a.inv + (size_t)un.tile * GM_NT;
+        float* dst = a.out + (size_t)un.row0 * a.N + (un.wrow % a.N) + r;
+        if (gm_folds<FMT>()) {
+          // one fold per 128 columns: acc += scale x partial (fp8: the 128 x 128 block's; W4A8 / W6A8: the row's
+          // bf16 group scale)
+          float acc[GM_NT];
 #pragma unroll
-        for (int j = 0; j < GM_NT; ++j) acc[j] = 0.0f;
-        for (int f = 0; f < nfold && ok; ++f) {
+          for (int j = 0; j < GM_NT; ++j) acc[j] = 0.0f;
+          float s_cur = fold_scale(un.wrow, 0), s_nxt = 0.0f;
+          for (int f = 0; f < nfold && ok; ++f) {
+            const int region = folds & 1;
+            if (f + 1 < nfold) s_nxt = fold_scale(un.wrow, f + 1);  // in flight while this fold's MMAs finish
+            {
+              GM_T0();
+              ok = mbar_wait(acc_full + region, (folds >> 1) & 1);
+              if (r == 0) GM_TADD(7);
+            }
+            if (!ok) break;
+            tc_fence_after();
+            const float s = s_cur;
+            s_cur = s_nxt;
+#pragma unroll
+            for (int c = 0; c < GM_NT / 16; ++c) {
+              if (16 * c >= un.rows) break;
+              float v[16];
+              tmem_ld16(tmem + lane_base + region * GM_NT + 16 * c, v);
+              if (I8) {  // s32 partials of one 128-column group: |sum| < 2^24, exact as floats
+#pragma unroll
+                for (int q = 0; q < 16; ++q) v[q] = (float)(int)__float_as_uint(v[q]);
+              }
+#pragma unroll
+              for (int q = 0; q < 16; ++q) acc[16 * c + q] = fmaf(s, v[q], acc[16 * c + q]);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty + region);
+            ++folds;
+          }
+          if (!ok) break;
+#pragma unroll
+          for (int j = 0; j < GM_NT; ++j)
+            if (j < un.rows) dst[(size_t)j * a.N] = acc[j] * __ldg(inv + j);
+        } else {
+          // one fold per unit: the row scale (int8 scale, W4/W6 s_channel) and each row's 2^-e, straight to out
           const int region = folds & 1;
+          const float rs = fmt_row_scale(FMT) ? __ldg((const float*)a.scale + un.wrow + r)
+                                              : __ldg(a.s_channel + un.wrow + r);
           {
             GM_T0();
             ok = mbar_wait(acc_full + region, (folds >> 1) & 1);
@@ -748,51 +906,21 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
           }
           if (!ok) break;
           tc_fence_after();
-          const float s = FMT == FMT_FP8
-                              ? __ldg((const float*)a.scale + (size_t)(wrow / 128) * (a.K / 128) + f)
-                              : bf16_to_f32(__ldg((const uint16_t*)a.scale + (size_t)(wrow + r) * (a.K / 128) + f));
-#pragma unroll
-          for (int c = 0; c < GM_NT / 16; ++c) {
-            if (16 * c >= tl.rows) break;
+#pragma unroll 1
+          for (int c = 0; 16 * c < un.rows; ++c) {
             float v[16];
             tmem_ld16(tmem + lane_base + region * GM_NT + 16 * c, v);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) acc[16 * c + i] = fmaf(s, v[i], acc[16 * c + i]);
+            for (int q = 0; q < 16; ++q) {
+              const int j = 16 * c + q;
+              if (j < un.rows) dst[(size_t)j * a.N] = v[q] * __ldg(inv + j) * rs;
+            }
           }
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(acc_empty + region);
           ++folds;
         }
-        if (!ok) break;
-#pragma unroll
-        for (int j = 0; j < GM_NT; ++j)
-          if (j < tl.rows) dst[(size_t)j * a.N] = acc[j] * __ldg(inv + j);
-      } else {
-        // one fold per unit: the row scale (int8 scale, W4/W6 s_channel) and each row's 2^-e, straight to out
-        const int region = folds & 1;
-        {
-          GM_T0();
-          ok = mbar_wait(acc_full + region, (folds >> 1) & 1);
-          if (r == 0) GM_TADD(7);
-        }
-        if (!ok) break;
-        tc_fence_after();
-        const float rs = fmt_row_scale(FMT) ? __ldg((const float*)a.scale + wrow + r) : __ldg(a.s_channel + wrow + r);
-#pragma unroll 1
-        for (int c = 0; 16 * c < tl.rows; ++c) {
-          float v[16];
-          tmem_ld16(tmem + lane_base + region * GM_NT + 16 * c, v);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int j = 16 * c + i;
-            if (j < tl.rows) dst[(size_t)j * a.N] = v[i] * __ldg(inv + j) * rs;
-          }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(acc_empty + region);
-        ++folds;
       }
     }
   }
