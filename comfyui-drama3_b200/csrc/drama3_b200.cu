@@ -162,7 +162,7 @@ int d3_device_check(void) {
 #ifdef D3_TRACE
 // Trace builds only: copy the per-CTA phase timestamps (uint64 [1024][24]) to host memory.
 int d3_trace_read(void* dst) { return cuda_status(cudaMemcpyFromSymbol(dst, d3::g_trace, sizeof(d3::g_trace))); }
-// Trace builds only: the grouped GEMM's per-CTA wait counters (uint64 [1024][12]).
+// Trace builds only: the grouped GEMM's per-CTA wait counters (uint64 [1024][16]).
 int d3_gm_trace_read(void* dst) {
   return cuda_status(cudaMemcpyFromSymbol(dst, d3::g_gm_trace, sizeof(d3::g_gm_trace)));
 }

@@ -20,7 +20,7 @@
 //   1     activation producer: two bulk copies (hi, lo) per 64-column chunk into a 3-stage ring; a tile of R rows
 //         copies and multiplies only its first round_up(R, 16) rows (MMA N = that), which matters for the many
 //         small groups of a skewed routing
-//   2     MMA issuer (one elected thread) and owner of the 256 tensor-memory columns
+//   2     MMA issuer (one elected thread) and owner of the 512 tensor-memory columns (4 accumulator regions)
 //   3-6   converters: thread = weight row, raw bytes -> f16, written swizzled into the A stage
 //   7-10  fold + epilogue: tcgen05.ld of their 32-lane quarter, scale, accumulate, write fp32 rows
 // Every wait is bounded (2 s) and records FAULT_WAIT_TIMEOUT instead of hanging.
@@ -38,8 +38,9 @@ namespace d3 {
 // Trace builds only: per CTA, cycles each role spent waiting at each barrier (clock64), and counters.
 //   0 raw producer / raw_empty   1 B producer / mma_empty   2 MMA / acc_empty   3 MMA / a_full   4 MMA / b_full
 //   5 converters / raw_full      6 converters / mma_empty   7 fold / acc_full   8 units   9 total cycles
-//   10 converter busy cycles     11 fold busy cycles
-__device__ unsigned long long g_gm_trace[1024][12];
+//   10 converter busy cycles     11 MMA issue cycles     12 fold tmem-load + fma cycles     13 fold epilogue cycles
+//   14 converter fence + arrive cycles
+__device__ unsigned long long g_gm_trace[1024][16];
 #define GM_T0() const long long _t0 = clock64()
 #define GM_TADD(slot) \
   if (blockIdx.x < 1024) atomicAdd(&g_gm_trace[blockIdx.x][slot], (unsigned long long)(clock64() - _t0))
@@ -60,7 +61,8 @@ constexpr int GM_B_BYTES = GM_NT * GM_KC * 2;     // 16 KB per term
 constexpr int GM_WARPS = 11;
 constexpr int GM_THREADS = GM_WARPS * 32;
 constexpr int GM_CONV0 = 3, GM_FOLD0 = 7;         // first converter / fold warp
-constexpr int GM_TMEM_COLS = 256;  // two accumulator regions of GM_NT columns
+constexpr int GM_REGIONS = 4;                      // accumulator regions of GM_NT columns: the MMAs run up to three
+constexpr int GM_TMEM_COLS = GM_REGIONS * GM_NT;   // folds ahead of the fold warps (one CTA per SM: all 512 columns)
 
 struct GroupedTile {
   int group;  // index into groups[]
@@ -404,12 +406,13 @@ struct GmSmem {
   static constexpr int b = a + GM_MMA_ST * GM_A_BYTES;
   static constexpr int raw = b + GM_MMA_ST * 2 * GM_B_BYTES;
   static constexpr int bars = raw + GM_RAW_ST * GM_RAW_BYTES;
-  // raw_full, raw_empty [GM_RAW_ST]; a_full, b_full, mma_empty [GM_MMA_ST]; acc_full, acc_empty [2]
-  static constexpr int nbars = 2 * GM_RAW_ST + 3 * GM_MMA_ST + 4;
+  // raw_full, raw_empty [GM_RAW_ST]; a_full, b_full, mma_empty [GM_MMA_ST]; acc_full, acc_empty [GM_REGIONS]
+  static constexpr int nbars = 2 * GM_RAW_ST + 3 * GM_MMA_ST + 2 * GM_REGIONS;
   static constexpr int tmem = bars + nbars * 8;
   static constexpr int lut = tmem + 16;
   static constexpr int units = lut + 64;  // GmUnit [GM_UNIT_CAP]: this CTA's first units
-  static constexpr int total = units + GM_UNIT_CAP * 16;
+  static constexpr int inv = units + GM_UNIT_CAP * 16;  // float [4][GM_NT]: the tile rows' 2^-e, a copy per fold warp
+  static constexpr int total = inv + 4 * GM_NT * 4;
   static constexpr int launch = total + 1024;  // slack to align the base to 1024 bytes
 };
 
@@ -602,7 +605,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
   uint64_t* b_full = a_full + GM_MMA_ST;
   uint64_t* mma_empty = b_full + GM_MMA_ST;
   uint64_t* acc_full = mma_empty + GM_MMA_ST;
-  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* acc_empty = acc_full + GM_REGIONS;
   uint32_t* tmem_slot = (uint32_t*)(smem + GmSmem::tmem);
   float* lut = (float*)(smem + GmSmem::lut);
 
@@ -610,7 +613,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
 #ifdef D3_TRACE
   const long long t_kernel = clock64();
   if (threadIdx.x == 0 && blockIdx.x < 1024)
-    for (int i = 0; i < 12; ++i) g_gm_trace[blockIdx.x][i] = 0;
+    for (int i = 0; i < 16; ++i) g_gm_trace[blockIdx.x][i] = 0;
 #endif
   if (threadIdx.x == 0) {
     for (int i = 0; i < GM_RAW_ST; ++i) {
@@ -622,7 +625,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       mbar_init(b_full + i, 1);
       mbar_init(mma_empty + i, 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < GM_REGIONS; ++i) {
       mbar_init(acc_full + i, 1);
       mbar_init(acc_empty + i, 4);
     }
@@ -730,10 +733,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         const uint32_t idesc = I8 ? t8_idesc(gm_width(un.rows)) : gm_idesc(gm_width(un.rows));
         for (int kc = 0; kc < nkc && ok; ++kc) {
           if (kc % kbc == 0) {
-            const int region = folds & 1;
+            const int region = folds % GM_REGIONS;
             {
               GM_T0();
-              ok = mbar_wait(acc_empty + region, ((folds >> 1) & 1) ^ 1);
+              ok = mbar_wait(acc_empty + region, ((folds / GM_REGIONS) & 1) ^ 1);
               GM_TADD(2);
             }
             if (!ok) break;
@@ -751,6 +754,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
             GM_TADD(4);
           }
           if (!ok) break;
+          GM_T0();
           tc_fence_after();
           const uint32_t as = smem_u32(smem + GmSmem::a + ms * GM_A_BYTES);
           const uint32_t bs = smem_u32(smem + GmSmem::b + ms * 2 * GM_B_BYTES);
@@ -767,9 +771,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
           }
           umma_commit(mma_empty + ms);
           if (kc % kbc == kbc - 1) {
-            umma_commit(acc_full + (folds & 1));
+            umma_commit(acc_full + folds % GM_REGIONS);
             ++folds;
           }
+          GM_TADD(11);
           if (++ms == GM_MMA_ST) {
             ms = 0;
             mph ^= 1;
@@ -816,11 +821,15 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                             sbytes, lut);
           if (r == 0) GM_TADD(10);
         }
-        fence_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          if (last) mbar_arrive(raw_empty + rs);
-          mbar_arrive(a_full + ms);
+        {
+          GM_T0();
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (last) mbar_arrive(raw_empty + rs);
+            mbar_arrive(a_full + ms);
+          }
+          if (r == 0) GM_TADD(14);
         }
         if (last && ++rs == GM_RAW_ST) {
           rs = 0;
@@ -852,7 +861,12 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       if (un.wrow < 0) {
         if (un.wrow == -1) record_fault(FAULT_BAD_SLOT);
       } else {
-        const float* inv = a.inv + (size_t)un.tile * GM_NT;
+        // the tile rows' factors, copied into this warp's own shared-memory row while the unit's MMAs run, so the
+        // epilogue's stores do not wait on global loads (the warp's previous epilogue has read the row already)
+        float* inv = (float*)(smem + GmSmem::inv) + quarter * GM_NT;
+#pragma unroll
+        for (int m = 0; m < GM_NT / 32; ++m)
+          inv[lane + 32 * m] = __ldg(a.inv + (size_t)un.tile * GM_NT + lane + 32 * m);
         float* dst = a.out + (size_t)un.row0 * a.N + (un.wrow % a.N) + r;
         if (gm_folds<FMT>()) {
           // one fold per 128 columns: acc += scale x partial (fp8: the 128 x 128 block's; W4A8 / W6A8: the row's
@@ -862,15 +876,16 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
           for (int j = 0; j < GM_NT; ++j) acc[j] = 0.0f;
           float s_cur = fold_scale(un.wrow, 0), s_nxt = 0.0f;
           for (int f = 0; f < nfold && ok; ++f) {
-            const int region = folds & 1;
+            const int region = folds % GM_REGIONS;
             if (f + 1 < nfold) s_nxt = fold_scale(un.wrow, f + 1);  // in flight while this fold's MMAs finish
             {
               GM_T0();
-              ok = mbar_wait(acc_full + region, (folds >> 1) & 1);
+              ok = mbar_wait(acc_full + region, (folds / GM_REGIONS) & 1);
               if (r == 0) GM_TADD(7);
             }
             if (!ok) break;
             tc_fence_after();
+            GM_T0();
             const float s = s_cur;
             s_cur = s_nxt;
 #pragma unroll
@@ -885,27 +900,32 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
 #pragma unroll
               for (int q = 0; q < 16; ++q) acc[16 * c + q] = fmaf(s, v[q], acc[16 * c + q]);
             }
+            if (r == 0) GM_TADD(12);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(acc_empty + region);
             ++folds;
           }
           if (!ok) break;
+          GM_T0();
+          __syncwarp();
 #pragma unroll
           for (int j = 0; j < GM_NT; ++j)
-            if (j < un.rows) dst[(size_t)j * a.N] = acc[j] * __ldg(inv + j);
+            if (j < un.rows) dst[(size_t)j * a.N] = acc[j] * inv[j];
+          if (r == 0) GM_TADD(13);
         } else {
           // one fold per unit: the row scale (int8 scale, W4/W6 s_channel) and each row's 2^-e, straight to out
-          const int region = folds & 1;
+          const int region = folds % GM_REGIONS;
           const float rs = fmt_row_scale(FMT) ? __ldg((const float*)a.scale + un.wrow + r)
                                               : __ldg(a.s_channel + un.wrow + r);
           {
             GM_T0();
-            ok = mbar_wait(acc_full + region, (folds >> 1) & 1);
+            ok = mbar_wait(acc_full + region, (folds / GM_REGIONS) & 1);
             if (r == 0) GM_TADD(7);
           }
           if (!ok) break;
           tc_fence_after();
+          __syncwarp();
 #pragma unroll 1
           for (int c = 0; 16 * c < un.rows; ++c) {
             float v[16];
@@ -913,7 +933,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
 #pragma unroll
             for (int q = 0; q < 16; ++q) {
               const int j = 16 * c + q;
-              if (j < un.rows) dst[(size_t)j * a.N] = v[q] * __ldg(inv + j) * rs;
+              if (j < un.rows) dst[(size_t)j * a.N] = v[q] * inv[j] * rs;
             }
           }
           tc_fence_before();
