@@ -442,8 +442,9 @@ int d3_grouped_mma(int fmt, const void* x, int x_bf16, const int64_t* row_index,
   if (!byte_tile_map(&wmap, weight, row_bytes, (uint64_t)bank_rows, box)) return D3_ERR_ARG;
   pmap = wmap;
   if (fmt == d3::FMT_W6 && !byte_tile_map(&pmap, weight, row_bytes, (uint64_t)bank_rows, 32)) return D3_ERR_ARG;
-  if (int st = launch(d3::gm_stage_kernel, dim3(tiles, d3::GM_NT / d3::GM_STAGE_ROWS), dim3(256), 0, s, false, x,
-                      x_bf16, row_index, mode, groups, n_groups, K, tiles, staged, inv, table, ntiles))
+  if (int st = launch((mode & d3::GM_ROTATE) ? d3::gm_stage_kernel<true> : d3::gm_stage_kernel<false>,
+                      dim3(tiles, d3::GM_NT / d3::GM_STAGE_ROWS), dim3(256), 0, s, false, x, x_bf16, row_index, mode,
+                      groups, n_groups, K, tiles, staged, inv, table, ntiles))
     return st;
   const int units = tiles * (N / d3::GM_M);
   d3::GmArgs a = {staged, inv, table, ntiles, groups, scale, s_channel, codebook, out, N, K, units, bank_rows};

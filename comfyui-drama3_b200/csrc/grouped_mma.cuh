@@ -87,8 +87,9 @@ __host__ __device__ constexpr size_t gm_workspace_bytes(int tiles, int K) {
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// Staging: one block (8 warps) per (tile slot, 16-row slice of the tile), so a full tile's rows are spread over 8 SMs'
-// blocks. Block (t, s) finds its (group, tile of the group) from the groups' row counts, slice 0 writes the tile table
+// Staging: one block (8 warps) per (tile slot, 16-row slice of the tile), so a full tile's rows are spread over 8
+// blocks. Without a rotation a warp reads its row twice (the row's bound, then the conversion), which keeps few values
+// in registers and many warps resident. Block (t, s) finds its (group, tile of the group) from the groups' row counts, slice 0 writes the tile table
 // entry, and the block converts its slice of the tile's rows (zeros past the group's end, up to the MMA width)
 // to the hi / lo f16 operand blocks plus inv[row] = 2^-e (times 1/16 after a rotation; 0 for padding rows). Block 0
 // also writes the number of tiles. A warp owns a row: its K values sit in registers (lane l holds columns
@@ -103,12 +104,13 @@ __host__ __device__ constexpr size_t gm_workspace_bytes(int tiles, int K) {
 //        clamped, IEEE division) and staged as int8 operand blocks of 128 columns for kind::i8; inv = s
 enum { GM_ROTATE = 1, GM_SWIGLU = 2, GM_INT8 = 4 };
 constexpr int GM_STAGE_ROWS = 16;  // rows of a tile per staging block (grid: tile slots x GM_NT / GM_STAGE_ROWS)
+constexpr int GM_STAGE_PREFETCH = 9;  // chunks of 32 group counts a staging block loads up front (257 groups)
 
 D3_DEV float gm_load(const void* x, bool bf16, size_t i) {
   return bf16 ? bf16_to_f32(((const uint16_t*)x)[i]) : ((const float*)x)[i];
 }
 
-D3_DEV void gm_load8(const void* x, bool bf16, size_t base, float (&v)[8]) {
+D3_DEV void gm_load8(const void* x, bool bf16, size_t base, float* v) {
   if (bf16) {
     const uint4 b = __ldg((const uint4*)((const uint16_t*)x + base));
     const uint32_t w[4] = {b.x, b.y, b.z, b.w};
@@ -125,7 +127,8 @@ D3_DEV void gm_load8(const void* x, bool bf16, size_t base, float (&v)[8]) {
   }
 }
 
-__global__ void __launch_bounds__(256) gm_stage_kernel(const void* __restrict__ x, int src_bf16,
+template <bool ROT>
+__global__ void __launch_bounds__(256, ROT ? 2 : 3) gm_stage_kernel(const void* __restrict__ x, int src_bf16,
                                                        const int64_t* __restrict__ row_index, int mode,
                                                        const int* __restrict__ groups, int G, int K, int max_tiles,
                                                        uint8_t* __restrict__ staged, float* __restrict__ inv,
@@ -135,11 +138,18 @@ __global__ void __launch_bounds__(256) gm_stage_kernel(const void* __restrict__ 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x, slice = blockIdx.y;
   if (warp == 0) {
+    // the row counts of the first GM_STAGE_PREFETCH x 32 groups, loaded together (one memory latency, not one per
+    // 32 groups); groups past them are read in the loop
+    int pre[GM_STAGE_PREFETCH];
+#pragma unroll
+    for (int m = 0; m < GM_STAGE_PREFETCH; ++m) {
+      const int g = 32 * m + lane;
+      pre[m] = g < G ? groups[5 * g + 4] : 0;
+    }
     int base = 0, found_g = -1, found_l = 0;
-    for (int c0 = 0; c0 < G; c0 += 32) {
-      const int g = c0 + lane;
-      const int n = g < G ? max(0, groups[5 * g + 4]) : 0;
-      const int tiles = (n + GM_NT - 1) / GM_NT;
+    // one chunk of 32 groups (g = c0 + lane holds n rows): find tile slot t among the chunk's tiles
+    auto chunk = [&](int c0, int n) {
+      const int tiles = (max(0, n) + GM_NT - 1) / GM_NT;
       int incl = tiles;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -155,7 +165,12 @@ __global__ void __launch_bounds__(256) gm_stage_kernel(const void* __restrict__ 
         found_l = t - base - src_excl;
       }
       base += __shfl_sync(0xffffffffu, incl, 31);
-    }
+    };
+#pragma unroll
+    for (int m = 0; m < GM_STAGE_PREFETCH; ++m)
+      if (32 * m < G) chunk(32 * m, pre[m]);
+    for (int c0 = 32 * GM_STAGE_PREFETCH; c0 < G; c0 += 32)
+      chunk(c0, c0 + lane < G ? groups[5 * (c0 + lane) + 4] : 0);
     if (lane == 0) {
       s_group = found_g;
       s_local = found_l;
@@ -172,7 +187,7 @@ __global__ void __launch_bounds__(256) gm_stage_kernel(const void* __restrict__ 
   const int first = groups[5 * g + 3], count = groups[5 * g + 4];
   const int row0 = first + s_local * GM_NT, rows = min(GM_NT, count - s_local * GM_NT);
   if (threadIdx.x == 0 && slice == 0) table[t] = GroupedTile{g, row0, rows, groups[5 * g + 1]};
-  const bool bf16 = src_bf16 != 0, rotate = (mode & GM_ROTATE) != 0, swiglu = (mode & GM_SWIGLU) != 0;
+  const bool bf16 = src_bf16 != 0, swiglu = (mode & GM_SWIGLU) != 0;  // GM_ROTATE: the ROT instance
   const bool int8q = (mode & GM_INT8) != 0;
   const int nkc = K / GM_KC, nq = K / 256;
   const size_t pitch = swiglu ? 2 * (size_t)K : (size_t)K;
@@ -180,29 +195,63 @@ __global__ void __launch_bounds__(256) gm_stage_kernel(const void* __restrict__ 
   const int width = (rows + 15) & ~15;  // rows the GEMM reads (its MMA N)
   const int j_end = min(width, GM_STAGE_ROWS * (slice + 1));
   float* row = scratch[warp];
+  // columns 256 q + 8 lane .. + 7 of a source row (through SwiGLU when asked; zeros for padding rows)
+  auto load_q = [&](int q, size_t src_row, bool live, float* v) {
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = 0.0f;
+    if (live) {
+      const size_t base = src_row * pitch + 256 * q + 8 * lane;
+      gm_load8(x, bf16, base, v);
+      if (swiglu) {
+        float up[8];
+        gm_load8(x, bf16, base + K, up);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = swiglu_fast(v[u], up[u]);
+      }
+    }
+  };
+  // the same columns of staged row j: int8 codes (GM_INT8), or the hi / lo f16 terms of v * scale
+  auto store_q = [&](int q, int j, const float* v, float scale, float qs) {
+    if (int8q) {
+      // int8 operand blocks of 128 columns (one per kind::i8 MMA chunk, GM_B_BYTES apart): columns 256q + 8 lane
+      // .. + 7 are chunk 2q + lane / 16, the (lane & 1) half of 16-byte piece (lane % 16) / 2
+      float qv[8];
+      quant_i8_n<8>(v, qs, __frcp_rn(qs), qv);
+      uint32_t b[2] = {0u, 0u};
+#pragma unroll
+      for (int u = 0; u < 8; ++u) b[u >> 2] |= ((uint32_t)(int)qv[u] & 0xFFu) << (8 * (u & 3));
+      uint8_t* blk = tile_base + (size_t)(2 * q + (lane >> 4)) * GM_B_BYTES;
+      *(uint2*)(blk + sw128_offset(j, (lane & 15) >> 1) + 8 * (lane & 1)) = make_uint2(b[0], b[1]);
+      return;
+    }
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float s0 = v[2 * u] * scale, s1 = v[2 * u + 1] * scale;
+      const __half h0 = __float2half_rn(s0), h1 = __float2half_rn(s1);
+      hw[u] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+      const __half l0 = __float2half_rn(s0 - __half2float(h0)), l1 = __float2half_rn(s1 - __half2float(h1));
+      lw[u] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+    }
+    // columns 256q + 8 lane .. + 7: chunk kc = 4q + lane / 8, 16-byte piece c = lane % 8
+    const int kc = 4 * q + (lane >> 3), c = lane & 7;
+    uint8_t* blk = tile_base + (size_t)kc * 2 * GM_B_BYTES;
+    *(uint4*)(blk + sw128_offset(j, c)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *(uint4*)(blk + GM_B_BYTES + sw128_offset(j, c)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+  };
   for (int j = GM_STAGE_ROWS * slice + warp; j < j_end; j += 8) {
     const bool live = j < rows;
     const size_t src_row = live ? (size_t)(row_index ? row_index[row0 + j] : row0 + j) : 0;
-    float v[8][8];
     float m = 0.0f;
+    float v[ROT ? 8 : 1][8];  // ROT: the whole rotated row; otherwise one 256-column group at a time
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       if (q >= nq) break;
+      float* vq = v[ROT ? q : 0];
+      load_q(q, src_row, live, vq);
+      if (ROT) {
 #pragma unroll
-      for (int u = 0; u < 8; ++u) v[q][u] = 0.0f;
-      if (live) {
-        const size_t base = src_row * pitch + 256 * q + 8 * lane;
-        gm_load8(x, bf16, base, v[q]);
-        if (swiglu) {
-          float up[8];
-          gm_load8(x, bf16, base + K, up);
-#pragma unroll
-          for (int u = 0; u < 8; ++u) v[q][u] = swiglu_fast(v[q][u], up[u]);
-        }
-      }
-      if (rotate) {
-#pragma unroll
-        for (int u = 0; u < 8; ++u) row[8 * lane + u] = v[q][u];
+        for (int u = 0; u < 8; ++u) row[8 * lane + u] = vq[u];
         __syncwarp();
 #pragma unroll
         for (int stride = 1; stride < 256; stride *= 4) {
@@ -219,11 +268,11 @@ __global__ void __launch_bounds__(256) gm_stage_kernel(const void* __restrict__ 
           __syncwarp();
         }
 #pragma unroll
-        for (int u = 0; u < 8; ++u) v[q][u] = row[8 * lane + u];
+        for (int u = 0; u < 8; ++u) vq[u] = row[8 * lane + u];
         __syncwarp();
       }
 #pragma unroll
-      for (int u = 0; u < 8; ++u) m = fmaxf(m, fabsf(v[q][u]));
+      for (int u = 0; u < 8; ++u) m = fmaxf(m, fabsf(vq[u]));
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -233,36 +282,12 @@ __global__ void __launch_bounds__(256) gm_stage_kernel(const void* __restrict__ 
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       if (q >= nq) break;
-      if (int8q) {
-        // int8 operand blocks of 128 columns (one per kind::i8 MMA chunk, GM_B_BYTES apart): columns 256q + 8 lane
-        // .. + 7 are chunk 2q + lane / 16, the (lane & 1) half of 16-byte piece (lane % 16) / 2
-        float qv[8];
-        quant_i8_n<8>(v[q], qs, __frcp_rn(qs), qv);
-        uint32_t b[2] = {0u, 0u};
-#pragma unroll
-        for (int u = 0; u < 8; ++u) b[u >> 2] |= ((uint32_t)(int)qv[u] & 0xFFu) << (8 * (u & 3));
-        uint8_t* blk = tile_base + (size_t)(2 * q + (lane >> 4)) * GM_B_BYTES;
-        *(uint2*)(blk + sw128_offset(j, (lane & 15) >> 1) + 8 * (lane & 1)) = make_uint2(b[0], b[1]);
-        continue;
-      }
-      uint32_t hw[4], lw[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float s0 = v[q][2 * u] * scale, s1 = v[q][2 * u + 1] * scale;
-        const __half h0 = __float2half_rn(s0), h1 = __float2half_rn(s1);
-        hw[u] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
-        const __half l0 = __float2half_rn(s0 - __half2float(h0)), l1 = __float2half_rn(s1 - __half2float(h1));
-        lw[u] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
-      }
-      // columns 256q + 8 lane .. + 7: chunk kc = 4q + lane / 8, 16-byte piece c = lane % 8
-      const int kc = 4 * q + (lane >> 3), c = lane & 7;
-      uint8_t* blk = tile_base + (size_t)kc * 2 * GM_B_BYTES;
-      *(uint4*)(blk + sw128_offset(j, c)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-      *(uint4*)(blk + GM_B_BYTES + sw128_offset(j, c)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+      if (!ROT) load_q(q, src_row, live, v[0]);  // the second pass reads the row again (from L1 / L2)
+      store_q(q, j, v[ROT ? q : 0], scale, qs);
     }
     if (lane == 0)
       inv[(size_t)t * GM_NT + j] =
-          !live ? 0.0f : int8q ? qs : (rotate ? 0.0625f : 1.0f) * __uint_as_float((uint32_t)(127 - e) << 23);
+          !live ? 0.0f : int8q ? qs : (ROT ? 0.0625f : 1.0f) * __uint_as_float((uint32_t)(127 - e) << 23);
   }
 }
 
