@@ -354,8 +354,9 @@ def prefill_leg(device, steps, tokens=2048, seed=3):
     dgen = torch.Generator(device=device).manual_seed(seed)
     out = {"tokens": tokens, "top_k": K_TOP, "largest_group": int(counts.max()), "median_group": int(counts.median()),
            "flops_per_layer": flops, "peak_tflops": bf16_peak,
-           "note": "f16 MMAs with f32 accumulation; fp32 activations enter as two f16 terms (hi + lo), int8-quantized "
-                   "ones (W6A8) as one exact term; frac = algorithmic flops / time / measured dense bf16 peak"}
+           "note": "W6A8: tcgen05 kind::i8 (int6 codes expanded to int8, int8 activations, exact s32 sums per "
+                   "128-column group); fp8 / W6: kind::f16 with f32 accumulation, activations as two f16 terms "
+                   "(hi + lo); frac = algorithmic flops / time / measured dense bf16 peak (the int8 rate is twice it)"}
     for kind in ("w6a8", "w6", "fp8"):
         banks = (rand_bank(kind, 2 * I, H, dgen, device), rand_bank(kind, H, I, dgen, device))
 
