@@ -78,3 +78,47 @@ def test_plan_of_int32_ids_equals_int64():
     a = offload.prefill_plan(ids, 32)
     b = offload.prefill_plan(ids.to(torch.int32), 32)
     assert all(torch.equal(u, v) for u, v in zip(a[:3], b[:3])) and a[3] == b[3]
+
+
+# ---- the native plan kernel's own scheme (csrc/plan.cuh, prefill_plan_kernel), restated in integers: 32 warps, each
+# owning a contiguous segment of S pairs (S = ceil(P / 32) rounded up to 32), counting and then placing its pairs 32
+# a round; the rank of a pair among the equal keys of its round is what __match_any_sync gives (its position among
+# the lanes holding the same key)
+
+def warp_segment_plan(ids, E):
+    P = ids.size
+    keys = E + 1
+    S = ((P + 31) // 32 + 31) & ~31
+    key = np.where((ids >= 0) & (ids < E), ids, E)
+    start = np.zeros((32, keys), np.int64)
+    for w in range(32):  # pass 1: each warp's own row of counts
+        for i in range(w * S, min(P, w * S + S)):
+            start[w, key[i]] += 1
+    total = start.sum(axis=0)
+    start = (np.cumsum(start, axis=0) - start) + (np.cumsum(total) - total)  # per key over warps, then over keys
+    order, pos = np.zeros(P, np.int64), np.zeros(P, np.int64)
+    for w in range(32):  # pass 2: place, a round at a time
+        seg1 = min(P, w * S + S)
+        for i0 in range(w * S, seg1, 32):
+            lanes = list(range(i0, min(i0 + 32, seg1)))
+            for i in lanes:
+                before = sum(1 for j in lanes if j < i and key[j] == key[i])
+                pos[i] = start[w, key[i]] + before
+                order[pos[i]] = i
+            for k in set(key[lanes].tolist()):
+                start[w, k] += int((key[lanes] == k).sum())
+    return order, pos, total
+
+
+@pytest.mark.parametrize("P, E, seed", [(16384, 128, 0), (1, 4, 1), (33, 3, 2), (1000, 256, 3), (0, 8, 4),
+                                         (5000, 1, 5), (1025, 16, 6)])
+def test_warp_segment_scheme_is_a_stable_sort(P, E, seed):
+    rng = np.random.default_rng(seed)
+    ids = rng.integers(-2, E + 2, P)
+    if P > 8:
+        ids[: P // 2] = rng.zipf(1.5, P // 2) % E  # skew, ties in every round
+    order, pos, total = warp_segment_plan(ids, E)
+    key = np.where((ids >= 0) & (ids < E), ids, E)
+    assert np.array_equal(order, np.argsort(key, kind="stable"))
+    assert np.array_equal(pos[order], np.arange(P))
+    assert np.array_equal(total, np.bincount(key, minlength=E + 1))
