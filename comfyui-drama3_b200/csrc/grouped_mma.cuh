@@ -3,25 +3,29 @@
 // (drama3/kernels.py:365-464, 538-587: fp8 block-scaled, int8 ConvRot, W4A8 / W6A8 codes), for banks held whole on
 // the GPU.
 //
-// Work unit = (token tile of up to 128 rows of one group, block of 128 weight rows). Per unit, D[128 x 128] (weight
-// rows x tokens) accumulates in tensor memory (tcgen05.mma kind::f16, M = 128, N <= 128, K = 16, f32 accumulate):
-//   A = 128 weight rows, converted exactly to f16 in shared memory (every e4m3 value, every int8 and every int8-grid
-//       code is an f16), K-major with the 128-byte swizzle;
-//   B = the tile's rows as two f16 terms, hi = f16(x * 2^e) and lo = f16(x * 2^e - hi) (e per row puts its max in
-//       [2^14, 2^15)), laid out by the staging kernel in global memory exactly as the MMA reads them from shared
-//       memory, so one 1-D bulk copy moves a 16 KB operand block. The products are exact; two MMAs per K step.
-// fp8 block scales vary every 128 columns: the accumulator is folded every 128 columns (two alternating regions of
-// 128 tensor-memory columns) by the fold warps, which add scale x partial into registers; the other formats fold
-// once per unit and apply the row scale (int8 scale, W4/W6 s_channel).
+// Work unit = (token tile of up to 128 rows of one group, block of 128 weight rows). Per unit, D[128 x N] (weight
+// rows x the tile's rows rounded up to 16) accumulates in tensor memory, in one of two MMA forms:
+//   kind::f16 (fp8 blocks, int8 ConvRot, W4 / W6 codes; f32 accumulators, K = 16, 64 columns a chunk):
+//     A = 128 weight rows, converted exactly to f16 in shared memory (every e4m3 value, every int8 and every
+//         int8-grid code is an f16), K-major with the 128-byte swizzle;
+//     B = the tile's rows as two f16 terms, hi = f16(x * 2^e) and lo = f16(x * 2^e - hi) (e per row puts its max in
+//         [2^14, 2^15)); the products are exact; two MMAs per K step.
+//   kind::i8 (W4A8 / W6A8; s32 accumulators, K = 32, 128 columns a chunk):
+//     A = the int4 / int6 codes expanded to int8 (16 x code, 4 x code), B = the rows' int8 codes; the sums are exact.
+// B is laid out by the staging kernel in global memory exactly as the MMA reads it from shared memory, so one 1-D
+// bulk copy per term moves a chunk's operand block.
+// Scales that vary every 128 columns (fp8 blocks, W4A8 / W6A8 groups) are folded every 128 columns: the MMA thread
+// cycles through four regions of 128 tensor-memory columns and the fold warps add scale x partial into registers;
+// the other formats fold once per unit and apply the row scale (int8 scale, W4/W6 s_channel).
 //
 // Warps (352 threads, one CTA per SM, persistent over units):
 //   0     raw-weight producer: 2-D TMA tile loads (128 columns x 128 rows, hardware-swizzled so the converters'
 //         row reads hit distinct banks) into a 4-stage ring of 16 KB
-//   1     activation producer: two bulk copies (hi, lo) per 64-column chunk into a 3-stage ring; a tile of R rows
-//         copies and multiplies only its first round_up(R, 16) rows (MMA N = that), which matters for the many
-//         small groups of a skewed routing
+//   1     activation producer: one bulk copy per term and chunk into a 3-stage ring; a tile of R rows copies and
+//         multiplies only its first round_up(R, 16) rows (MMA N = that), which matters for the many small groups of
+//         a skewed routing
 //   2     MMA issuer (one elected thread) and owner of the 512 tensor-memory columns (4 accumulator regions)
-//   3-6   converters: thread = weight row, raw bytes -> f16, written swizzled into the A stage
+//   3-6   converters: thread = weight row, raw bytes -> f16 or int8, written swizzled into the A stage
 //   7-10  fold + epilogue: tcgen05.ld of their 32-lane quarter, scale, accumulate, write fp32 rows
 // Every wait is bounded (2 s) and records FAULT_WAIT_TIMEOUT instead of hanging.
 #pragma once
@@ -88,12 +92,12 @@ __host__ __device__ constexpr size_t gm_workspace_bytes(int tiles, int K) {
 
 // ---------------------------------------------------------------------------------------------------------------
 // Staging: one block (8 warps) per (tile slot, 16-row slice of the tile), so a full tile's rows are spread over 8
-// blocks. Without a rotation a warp reads its row twice (the row's bound, then the conversion), which keeps few values
-// in registers and many warps resident. Block (t, s) finds its (group, tile of the group) from the groups' row counts, slice 0 writes the tile table
-// entry, and the block converts its slice of the tile's rows (zeros past the group's end, up to the MMA width)
-// to the hi / lo f16 operand blocks plus inv[row] = 2^-e (times 1/16 after a rotation; 0 for padding rows). Block 0
-// also writes the number of tiles. A warp owns a row: its K values sit in registers (lane l holds columns
-// 256 q + 8 l .. + 7), so the row's bound is exact.
+// blocks. Block (t, s) finds its (group, tile of the group) from the groups' row counts, slice 0 writes the tile table
+// entry, and the block converts its slice of the tile's rows (zeros past the group's end, up to the MMA width) to
+// the hi / lo f16 operand blocks (or int8 codes) plus inv[row] = 2^-e (times 1/16 after a rotation; 0 for padding
+// rows). Block (0, 0) also writes the number of tiles. A warp owns a row (lane l: columns 256 q + 8 l .. + 7), so
+// the row's bound is exact: with a rotation the rotated row stays in registers; without one the warp reads the row
+// twice (its bound, then the conversion), which keeps few values in registers and many warps resident.
 //   source row of sorted row s: x[row_index ? row_index[s] : s], fp32 or bf16 (src_bf16)
 //   mode bit GM_SWIGLU: the source row holds 2K columns, gate then up; the staged value is SiLU(gate) * up in the
 //        fast-exp form of the reference's rotate kernel (drama3/kernels.py:233-236)
@@ -716,7 +720,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       }
     }
   } else if (warp == 1) {
-    // staged activations: hi and lo operand blocks of each chunk
+    // staged activations: the operand blocks of each chunk (hi and lo for kind::f16, the int8 block for kind::i8)
     if (lane == 0) {
       const uint64_t keep = policy_evict_last();
       int ms = 0;
