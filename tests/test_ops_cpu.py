@@ -90,3 +90,19 @@ def test_ops_have_no_fallback_off_the_gpu():
     """On CPU tensors an op is refused before the library is called (no CPU or torch path exists)."""
     with pytest.raises(ValueError, match="cuda device"):
         torch.ops.drama3_b200.route(torch.zeros((2, 128), dtype=torch.bfloat16), 8)
+
+
+def test_ops_trace_into_an_exported_program():
+    """torch.export traces a module that calls the ops through their fake implementations (nothing runs), and the
+    exported graph holds the ops themselves."""
+
+    class Block(torch.nn.Module):
+        def forward(self, logits, parts):
+            ids, w = torch.ops.drama3_b200.route(logits, 8)
+            return ids, torch.ops.drama3_b200.weighted_sum(parts, w)
+
+    ep = torch.export.export(Block(), (torch.zeros((4, 128), dtype=torch.bfloat16), torch.zeros((32, 2048))))
+    targets = {str(n.target) for n in ep.graph.nodes if n.op == "call_function"}
+    assert {"drama3_b200.route.default", "drama3_b200.weighted_sum.default"} <= targets
+    out = [n for n in ep.graph.nodes if n.op == "output"][0].args[0]
+    assert tuple(out[1].meta["val"].shape) == (4, 2048) and out[1].meta["val"].dtype == torch.bfloat16
