@@ -6,7 +6,7 @@ import pytest
 import torch
 
 import gpu_data as gd
-from drama3_b200 import kernels
+from drama3_b200 import _lib, kernels
 from oracle import moe
 
 pytestmark = pytest.mark.gpu
@@ -171,3 +171,24 @@ def test_grouped_mma_too_few_tiles_records_fault(cuda):
     assert _lib.take_fault() & 8
     kernels.grouped_mma("fp8", x, groups, bank, None, N, kernels.grouped_tiles(COUNTS))
     assert _lib.take_fault() == 0
+
+
+def test_grouped_mma_many_units_per_cta(cuda):
+    """A prompt large enough that each CTA takes more units than its shared-memory unit table holds (128 experts x
+    800 rows: 10752 units over at most 148 CTAs, 64 cached): the last experts' units come from the tile table, and
+    their rows equal those of a call holding only those experts, bit for bit (tiles are computed independently)."""
+    E, N, K, per = 128, 1536, 2048, 800
+    kind = "w6a8"
+    bank = gd.rand_bank(kind, E, N, K, 400, cuda)
+    x = gd.rand_rows(E * per, K, 401, cuda)
+    groups = torch.tensor([(e, e, 0, e * per, per) for e in range(E)], dtype=torch.int32, device=cuda)
+    tiles = kernels.grouped_tiles([per] * E)
+    assert tiles * (N // 128) > 64 * 148
+    _lib.take_fault()
+    big = kernels.grouped_mma(kind, x, groups, bank, None, N, tiles)
+    last = torch.tensor([(e, e, 0, (e - E + 2) * per, per) for e in (E - 2, E - 1)], dtype=torch.int32, device=cuda)
+    small = kernels.grouped_mma(kind, x[(E - 2) * per:].contiguous(), last, bank, None, N,
+                                kernels.grouped_tiles([per, per]))
+    torch.cuda.synchronize()
+    assert _lib.take_fault() == 0
+    assert torch.equal(big[(E - 2) * per:], small)
